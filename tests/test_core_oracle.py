@@ -1,0 +1,154 @@
+"""CPU parity of the numerical core against the reference implementation (FP64)."""
+
+import numpy as np
+import pytest
+import torch
+
+from tornado_gcm_b200.core import legendre, fourier, spherical_harmonic as sh
+from tornado_gcm_b200.core import sigma_coordinates as sc, primitive_equations as pe
+from tornado_gcm_b200.core import coordinate_systems as cs, time_integration as ti
+from tornado_gcm_b200.utils.units import SimUnits
+
+pytestmark = pytest.mark.oracle
+
+
+def _ref_grid_fp64(ref, name):
+    """Reference grid forced to FP64 transforms (its with_einsum is overridden
+    by the resolution-adaptive choice, so the cached property is pre-filled)."""
+    rg = getattr(ref.spherical_harmonic.Grid, name)()
+    rsh = ref.spherical_harmonic.RealSphericalHarmonics(
+        longitude_wavenumbers=rg.longitude_wavenumbers, total_wavenumbers=rg.total_wavenumbers,
+        longitude_nodes=rg.longitude_nodes, latitude_nodes=rg.latitude_nodes,
+        latitude_spacing=rg.latitude_spacing, einsum_fn=ref.spherical_harmonic.einsum_highest)
+    rg.__dict__["spherical_harmonics"] = rsh
+    return rg
+
+
+def _band_limited_modal(grid, layers, rng, batch=()):
+    m, l = grid.modal_mesh
+    amp = np.where(grid.mask, (1.0 + l) ** -1.5, 0.0)
+    x = rng.standard_normal(batch + (layers,) + grid.modal_shape) * amp
+    x[..., -1] = 0.0
+    return torch.tensor(x, dtype=torch.float64)
+
+
+def test_legendre_matches(ref):
+    x, _ = legendre.gauss_legendre_nodes(24)
+    a = legendre.evaluate(11, 13, x)
+    b = ref.associated_legendre.evaluate(11, 13, x)
+    np.testing.assert_allclose(a, b, atol=1e-13)
+    xg, wg = ref.associated_legendre.gauss_legendre_nodes(24)
+    np.testing.assert_allclose(x, xg, atol=1e-14)
+    xe, we = legendre.equiangular_nodes(16)
+    xr, wr = ref.associated_legendre.equiangular_nodes(16)
+    np.testing.assert_allclose(we, wr, atol=1e-12)
+
+
+def test_fourier_matches(ref):
+    np.testing.assert_allclose(fourier.real_basis(7, 16), ref.fourier.real_basis(7, 16), atol=1e-13)
+    u = torch.randn(3, 13, dtype=torch.float64)
+    torch.testing.assert_close(fourier.real_basis_derivative(u, axis=-1),
+                               ref.fourier.real_basis_derivative(u, axis=-1))
+    u2 = torch.randn(3, 12, dtype=torch.float64)
+    torch.testing.assert_close(fourier.real_basis_derivative_with_zero_imag(u2, axis=-1),
+                               ref.fourier.real_basis_derivative_with_zero_imag(u2, axis=-1))
+
+
+@pytest.mark.parametrize("factory", ["T21", "TL31"])
+def test_sht_and_operators_match(ref, rng, factory):
+    g = getattr(sh.Grid, factory)(precision="highest")
+    rg = _ref_grid_fp64(ref, factory)
+    x = _band_limited_modal(g, 3, rng)
+    torch.testing.assert_close(g.to_nodal(x), rg.to_nodal(x), rtol=1e-11, atol=1e-12)
+    nod = g.to_nodal(x)
+    torch.testing.assert_close(g.to_modal(nod), rg.to_modal(nod), rtol=1e-11, atol=1e-12)
+    torch.testing.assert_close(g.to_modal(nod), x, rtol=1e-9, atol=1e-11)
+    for op in ["cos_lat_d_dlat", "sec_lat_d_dlat_cos2", "d_dlon", "laplacian", "inverse_laplacian"]:
+        torch.testing.assert_close(getattr(g, op)(x), getattr(rg, op)(x), rtol=1e-12, atol=1e-13)
+    torch.testing.assert_close(g.div_cos_lat((x, 2 * x)), rg.div_cos_lat((x, 2 * x)))
+    torch.testing.assert_close(g.curl_cos_lat((x, 2 * x)), rg.curl_cos_lat((x, 2 * x)))
+    u, v = sh.vor_div_to_uv_nodal(g, x, 0.5 * x)
+    ru, rv = ref.spherical_harmonic.vor_div_to_uv_nodal(rg, x, 0.5 * x)
+    torch.testing.assert_close(u, ru)
+    torch.testing.assert_close(v, rv)
+
+
+def test_sigma_ops_match(ref, rng):
+    s = sc.SigmaCoordinates.equidistant(8)
+    rs = ref.sigma_coordinates.SigmaCoordinates.equidistant(8)
+    x = torch.tensor(rng.standard_normal((2, 8, 5, 4)))
+    w = torch.tensor(rng.standard_normal((2, 7, 5, 4)))
+    torch.testing.assert_close(sc.cumulative_sigma_integral(x, s), ref.sigma_coordinates.cumulative_sigma_integral(x, rs))
+    torch.testing.assert_close(sc.cumulative_sigma_integral(x, s, downward=False),
+                               ref.sigma_coordinates.cumulative_sigma_integral(x, rs, downward=False))
+    torch.testing.assert_close(sc.sigma_integral(x, s), ref.sigma_coordinates.sigma_integral(x, rs))
+    torch.testing.assert_close(sc.centered_vertical_advection(w, x, s),
+                               ref.sigma_coordinates.centered_vertical_advection(w, x, rs))
+    torch.testing.assert_close(sc.upwind_vertical_advection(w, x, s),
+                               ref.sigma_coordinates.upwind_vertical_advection(w, x, rs))
+    torch.testing.assert_close(sc.cumulative_log_sigma_integral(x, s),
+                               ref.sigma_coordinates.cumulative_log_sigma_integral(x, rs))
+    np.testing.assert_allclose(pe.get_temperature_implicit_weights_sigma(s, np.linspace(220, 290, 8), 2 / 7),
+                               ref.primitive_equations.get_temperature_implicit_weights_sigma(rs, np.linspace(220, 290, 8), 2 / 7))
+    np.testing.assert_allclose(pe.get_geopotential_weights_sigma(s, 0.3),
+                               ref.primitive_equations.get_geopotential_weights_sigma(rs, 0.3))
+    sf = sc.SigmaCoordinates.from_centers(s.centers)
+    np.testing.assert_allclose(sf.boundaries, s.boundaries, atol=1e-12)
+
+
+def _make_pair(ref, grid_name, layers, humidity, clouds, rng, batch=()):
+    units = SimUnits.from_si()
+    g = getattr(sh.Grid, grid_name)(precision="highest")
+    rg = _ref_grid_fp64(ref, grid_name)
+    s = sc.SigmaCoordinates.equidistant(layers)
+    rs = ref.sigma_coordinates.SigmaCoordinates.equidistant(layers)
+    coords = cs.CoordinateSystem(g, s)
+    rcoords = ref.coordinate_systems.CoordinateSystem(rg, rs)
+    t_ref = np.linspace(210.0, 290.0, layers)
+    oro = _band_limited_modal(g, 1, rng)[0] * 1e-3
+    hk = "specific_humidity" if humidity else None
+    ck = ("specific_cloud_ice_water_content", "specific_cloud_liquid_water_content") if clouds else None
+    eq = pe.PrimitiveEquationsSigma(t_ref, oro, coords, units, humidity_key=hk, cloud_keys=ck)
+    req = ref.primitive_equations.PrimitiveEquationsSigma(t_ref, oro, rcoords, units, humidity_key=hk, cloud_keys=ck)
+    tr = {}
+    if humidity:
+        tr["specific_humidity"] = _band_limited_modal(g, layers, rng, batch) * 1e-3
+    if clouds:
+        tr["specific_cloud_ice_water_content"] = _band_limited_modal(g, layers, rng, batch) * 1e-5
+        tr["specific_cloud_liquid_water_content"] = _band_limited_modal(g, layers, rng, batch) * 1e-5
+    st = pe.State(_band_limited_modal(g, layers, rng, batch) * 1e-1, _band_limited_modal(g, layers, rng, batch) * 1e-2,
+                  _band_limited_modal(g, layers, rng, batch), _band_limited_modal(g, 1, rng, batch) * 1e-2, tr, 0.0)
+    rst = ref.primitive_equations.State(st.vorticity, st.divergence, st.temperature_variation,
+                                        st.log_surface_pressure, dict(tr), 0.0)
+    return eq, req, st, rst
+
+
+def _assert_state_close(a, b, rtol=1e-9, atol=1e-12):
+    for name in ("vorticity", "divergence", "temperature_variation", "log_surface_pressure"):
+        torch.testing.assert_close(getattr(a, name), getattr(b, name), rtol=rtol, atol=atol, msg=name)
+    for k in a.tracers:
+        torch.testing.assert_close(a.tracers[k], b.tracers[k], rtol=rtol, atol=atol, msg=k)
+
+
+@pytest.mark.parametrize("humidity,clouds", [(False, False), (True, False), (True, True)])
+def test_explicit_implicit_match(ref, rng, humidity, clouds):
+    eq, req, st, rst = _make_pair(ref, "T42", 6, humidity, clouds, rng)
+    _assert_state_close(eq.explicit_terms(st), req.explicit_terms(rst), rtol=1e-8, atol=1e-10)
+    _assert_state_close(eq.implicit_terms(st), req.implicit_terms(rst))
+    _assert_state_close(eq.implicit_inverse(st, 0.07), req.implicit_inverse(rst, 0.07))
+
+
+def test_batched_explicit_terms(ref, rng):
+    eq, req, st, rst = _make_pair(ref, "T21", 5, True, False, rng, batch=(3,))
+    out = eq.explicit_terms(st)
+    for b in range(3):
+        sb = st.tree_map(lambda t: t[b])
+        ob = eq.explicit_terms(sb)
+        _assert_state_close(out.tree_map(lambda t: t[b]), ob, rtol=1e-10, atol=1e-13)
+
+
+def test_sil3_step_matches(ref, rng):
+    eq, req, st, rst = _make_pair(ref, "T42", 5, True, False, rng)
+    step = ti.imex_rk_sil3(eq, 0.01)
+    rstep = ref.time_integration.imex_rk_sil3(req.as_imex_ode(), 0.01)
+    _assert_state_close(step(st), rstep(rst), rtol=1e-8, atol=1e-10)
