@@ -536,10 +536,26 @@ class PrimitiveEquationsSigma(time_integration.ImplicitExplicitODE):
             return dycore_ops.explicit_terms(self, state)
         return self.explicit_terms_reference(state)
 
-    def nodal_inputs(self, state: State, grid=None) -> dict:
-        """Spectral pre-processing + stacked inverse transform."""
+    def input_names(self, tracer_keys) -> tuple[list, list]:
+        """Stacked-slice order of the nodal inputs: (n-level names, 1-level names)."""
+        full = ["vort", "div", "temp", "u", "v"] + ["tr:" + k for k in tracer_keys]
+        single = ["gx", "gy"]
+        if self.humidity:
+            full += ["qx", "qy"]
+            single += ["lap_lnps"]
+        return full, single
+
+    def output_names(self, tracer_keys) -> tuple[list, list]:
+        names = ["flux_u", "flux_v", "ke", "temp", "temp_u", "temp_v"]
+        for k in tracer_keys:
+            names += ["tr:" + k, "tr_u:" + k, "tr_v:" + k]
+        if self.humidity:
+            names += ["tdiff", "hum_div", "hum_vort"]
+        return names, ["lnps"]
+
+    def modal_pre_stack(self, state: State, grid=None) -> torch.Tensor:
+        """Modal fields whose nodal values the column tendency needs, stacked on axis -3."""
         grid = grid or self.grid
-        n = state.vorticity.shape[-3]
         tr_keys = sorted(state.tracers)
         uc, vc = spherical_harmonic.get_cos_lat_vector(state.vorticity, state.divergence, grid, clip=False)
         gx, gy = grid.cos_lat_grad(state.log_surface_pressure, clip=False)
@@ -551,35 +567,39 @@ class PrimitiveEquationsSigma(time_integration.ImplicitExplicitODE):
             qgx, qgy = grid.cos_lat_grad(q, clip=False)
             full += [qgx, qgy]
             single += [grid.laplacian(state.log_surface_pressure)]
-        nodal = grid.to_nodal(torch.cat(full + single, dim=-3))
+        return torch.cat(full + single, dim=-3)
+
+    def split_nodal_inputs(self, nodal: torch.Tensor, tracer_keys) -> dict:
+        n = self.vertical.layers
+        full, single = self.input_names(tracer_keys)
         parts = torch.split(nodal, [n] * len(full) + [1] * len(single), dim=-3)
-        inp = {"vort": parts[0], "div": parts[1], "temp": parts[2], "u": parts[3], "v": parts[4]}
-        inp["tracers"] = dict(zip(tr_keys, parts[5:5 + len(tr_keys)]))
-        i = 5 + len(tr_keys)
+        named = dict(zip(full + single, parts))
+        inp = {k: named[k] for k in ("vort", "div", "temp", "u", "v", "gx", "gy")}
+        inp["tracers"] = {k: named["tr:" + k] for k in tracer_keys}
         if self.humidity:
-            inp["qx"], inp["qy"] = parts[i], parts[i + 1]
-            i += 2
+            inp["qx"], inp["qy"], inp["lap_lnps"] = named["qx"], named["qy"], named["lap_lnps"]
             if self.humidity_key not in inp["tracers"]:
                 inp["q"] = torch.zeros_like(inp["temp"])
-        inp["gx"], inp["gy"] = parts[i], parts[i + 1]
-        if self.humidity:
-            inp["lap_lnps"] = parts[i + 2]
         return inp
 
-    def modal_outputs(self, out: dict, state: State, grid=None) -> State:
-        """Stacked forward transform + spectral post-processing."""
+    def stack_nodal_outputs(self, out: dict, tracer_keys) -> torch.Tensor:
+        names, single = self.output_names(tracer_keys)
+        return torch.cat([out[k] for k in names] + [out[k] for k in single], dim=-3)
+
+    def nodal_inputs(self, state: State, grid=None) -> dict:
+        """Spectral pre-processing + stacked inverse transform."""
         grid = grid or self.grid
-        n = state.vorticity.shape[-3]
+        nodal = grid.to_nodal(self.modal_pre_stack(state, grid))
+        return self.split_nodal_inputs(nodal, sorted(state.tracers))
+
+    def modal_post(self, modal: torch.Tensor, state: State, grid=None) -> State:
+        """Spectral post-processing of the stacked forward-transformed outputs."""
+        grid = grid or self.grid
+        n = self.vertical.layers
         tr_keys = sorted(state.tracers)
-        names = ["flux_u", "flux_v", "ke", "temp", "temp_u", "temp_v"]
-        for k in tr_keys:
-            names += ["tr:" + k, "tr_u:" + k, "tr_v:" + k]
-        if self.humidity:
-            names += ["tdiff", "hum_div", "hum_vort"]
-        names_single = ["lnps"]
-        modal = grid.to_modal(torch.cat([out[k] for k in names] + [out[k] for k in names_single], dim=-3))
+        names, single = self.output_names(tr_keys)
         parts = torch.split(modal, [n] * len(names) + [1], dim=-3)
-        m = dict(zip(names + names_single, parts))
+        m = dict(zip(names + single, parts))
         fu, fv = m["flux_u"], m["flux_v"]
         vort_t = -grid.curl_cos_lat((fu, fv), clip=False)
         div_t = -grid.div_cos_lat((fu, fv), clip=False)
@@ -595,8 +615,13 @@ class PrimitiveEquationsSigma(time_integration.ImplicitExplicitODE):
         return State(clip(vort_t), clip(div_t), clip(temp_t), clip(m["lnps"]),
                      {k: clip(v) for k, v in tracers_t.items()}, state.sim_time)
 
+    def modal_outputs(self, out: dict, state: State, grid=None) -> State:
+        grid = grid or self.grid
+        stacked = self.stack_nodal_outputs(out, sorted(state.tracers))
+        return self.modal_post(grid.to_modal(stacked), state, grid)
+
     def explicit_terms_reference(self, state: State, grid=None) -> State:
-        """Torch implementation; FP64 diagnostics when the grid precision is 'highest'."""
+        """Torch implementation; FP64 transforms when the grid precision is 'highest'."""
         grid = grid or self.grid
         inp = self.nodal_inputs(state, grid)
         out = nodal_explicit_tendencies(inp, self.column_constants, self.humidity_key, self.cloud_keys or ())

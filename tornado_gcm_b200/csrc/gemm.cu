@@ -1,0 +1,330 @@
+// Host side of the tcgen05 GEMM engine: tensor-map encoding (cached), the
+// template dispatch table, and the two users built on it:
+//   * spherical-harmonic transforms (TF32): Legendre synthesis/analysis as
+//     per-wavenumber grouped GEMMs in "pair" addressing, real DFT synthesis/
+//     analysis as batched GEMMs against a resident Fourier basis;
+//   * BF16 linear layers: forward with fused bias + activation (+ saved
+//     pre-activation), data-gradient with the activation derivative fused,
+//     weight-gradient with split-K fp32 accumulation.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/library.h>
+
+#include <mutex>
+#include <stdexcept>
+#include <unordered_map>
+
+#include "gemm_sm100.cuh"
+
+namespace tgcm {
+
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeFn get_encode_fn() {
+  static EncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || ptr == nullptr)
+      throw std::runtime_error("tgcm: cuTensorMapEncodeTiled entry point unavailable");
+    fn = reinterpret_cast<EncodeFn>(ptr);
+  });
+  return fn;
+}
+
+struct TmapKey {
+  uint64_t ptr;
+  int dtype;
+  uint64_t d0, d1, d2, s1, s2;
+  uint32_t b0, b1, b2;
+  bool operator==(const TmapKey& o) const {
+    return ptr == o.ptr && dtype == o.dtype && d0 == o.d0 && d1 == o.d1 && d2 == o.d2 && s1 == o.s1 &&
+           s2 == o.s2 && b0 == o.b0 && b1 == o.b1 && b2 == o.b2;
+  }
+};
+struct TmapKeyHash {
+  size_t operator()(const TmapKey& k) const {
+    size_t h = std::hash<uint64_t>()(k.ptr);
+    auto mix = [&h](uint64_t v) { h ^= std::hash<uint64_t>()(v) + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2); };
+    mix(k.dtype); mix(k.d0); mix(k.d1); mix(k.d2); mix(k.s1); mix(k.s2); mix(k.b0); mix(k.b1); mix(k.b2);
+    return h;
+  }
+};
+
+// dtype: 1 = bf16, 2 = fp32.  dims innermost first; strides in bytes for dims 1, 2.
+static CUtensorMap make_tmap(const void* ptr, int dtype, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1,
+                             uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2) {
+  static std::mutex mu;
+  static std::unordered_map<TmapKey, CUtensorMap, TmapKeyHash> cache;
+  TmapKey key{reinterpret_cast<uint64_t>(ptr), dtype, d0, d1, d2, s1, s2, b0, b1, b2};
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  const int esize = dtype == 1 ? 2 : 4;
+  if (reinterpret_cast<uint64_t>(ptr) % 16 != 0) throw std::runtime_error("tgcm: TMA base address not 16B aligned");
+  if (s1 % 16 != 0 || s2 % 16 != 0) throw std::runtime_error("tgcm: TMA strides must be multiples of 16 bytes");
+  if (b0 * esize != 128) throw std::runtime_error("tgcm: TMA box inner extent must be 128 bytes");
+  CUtensorMap map;
+  cuuint64_t dims[3] = {d0, d1, d2 == 0 ? 1 : d2};
+  cuuint64_t strides[2] = {s1, s2 == 0 ? s1 * d1 : s2};
+  if (strides[1] % 16 != 0) strides[1] = ((strides[1] + 15) / 16) * 16;
+  cuuint32_t box[3] = {b0, b1, b2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = get_encode_fn()(&map, dtype == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                               3, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("tgcm: cuTensorMapEncodeTiled failed with code " + std::to_string(int(r)));
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache.size() > 4096) cache.clear();
+  cache.emplace(key, map);
+  return map;
+}
+
+template <int BN>
+struct StagesFor {
+  static constexpr int value = BN <= 80 ? 4 : BN <= 144 ? 3 : 2;
+};
+
+template <int FMT, int BN, bool A_MN, bool B_MN>
+static void launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream) {
+  constexpr int ST = StagesFor<BN>::value;
+  using S = GemmSmem<FMT, BN, ST>;
+  auto kern = gemm_sm100_kernel<FMT, BN, ST, A_MN, B_MN>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
+    attr_set = true;
+  }
+  dim3 grid(p.tiles_n, p.tiles_m * p.groups, p.k_splits);
+  kern<<<grid, 192, S::kTotal, stream>>>(ta, tb, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string("tgcm gemm launch: ") + cudaGetErrorString(e));
+}
+
+// Runtime dispatch over the instantiated configurations.
+static void gemm_dispatch(int fmt, int bn, bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
+                          const GemmParams& p, cudaStream_t st) {
+#define TGCM_CASE(F, B, AM, BM)                                  \
+  if (fmt == F && bn == B && a_mn == AM && b_mn == BM) {         \
+    launch_cfg<F, B, AM, BM>(ta, tb, p, st);                     \
+    return;                                                      \
+  }
+  TGCM_CASE(2, 64, false, false)
+  TGCM_CASE(2, 128, false, false)
+  TGCM_CASE(2, 256, false, false)
+  TGCM_CASE(2, 80, false, false)
+  TGCM_CASE(2, 144, false, false)
+  TGCM_CASE(2, 64, false, true)
+  TGCM_CASE(2, 128, false, true)
+  TGCM_CASE(2, 256, false, true)
+  TGCM_CASE(1, 64, false, false)
+  TGCM_CASE(1, 128, false, false)
+  TGCM_CASE(1, 64, false, true)
+  TGCM_CASE(1, 128, false, true)
+  TGCM_CASE(1, 64, true, true)
+  TGCM_CASE(1, 128, true, true)
+#undef TGCM_CASE
+  throw std::runtime_error("tgcm: no GEMM configuration for fmt=" + std::to_string(fmt) + " bn=" + std::to_string(bn));
+}
+
+static GemmParams default_params() {
+  GemmParams p;
+  memset(&p, 0, sizeof(p));
+  p.k_splits = 1;
+  p.alpha = 1.f;
+  p.a_group_div = 1;
+  p.b_group_div = 1;
+  return p;
+}
+
+static int* err_ptr(const c10::optional<at::Tensor>& err) {
+  if (err.has_value() && err->defined()) return err->data_ptr<int>();
+  return nullptr;
+}
+
+static int pick_bn_j(int64_t j) { return j <= 64 ? 64 : (j <= 128 ? 128 : 256); }
+static int pick_bn_l(int64_t l) { return l <= 80 ? 80 : 144; }
+static int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// ── spherical-harmonic transforms ───────────────────────────────────────────
+// x: (S, M2, Lp) fp32 modal, logical L;  P: (Mw, J, Lp);  F: (I, M2p).
+// Returns nodal (S, I, J) fp32.  ws: (S, J, M2p) workspace.
+at::Tensor sht_synth(const at::Tensor& x, int64_t L, const at::Tensor& P, const at::Tensor& F, const at::Tensor& ws,
+                     const c10::optional<at::Tensor>& col_scale, const c10::optional<at::Tensor>& err) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kFloat && x.is_contiguous(), "x must be contiguous fp32 CUDA");
+  TORCH_CHECK(x.dim() == 3, "x must be (S, M2, Lp)");
+  c10::cuda::CUDAGuard guard(x.device());
+  const int64_t S = x.size(0), M2 = x.size(1), Lp = x.size(2);
+  const int64_t Mw = P.size(0), J = P.size(1);
+  const int64_t I = F.size(0), M2p = F.size(1);
+  TORCH_CHECK(Lp % 4 == 0 && P.size(2) == Lp, "modal rows must be padded to a multiple of 4");
+  TORCH_CHECK(M2 == 2 * Mw - 1 && M2p % 4 == 0 && M2p >= M2, "basis shape mismatch");
+  TORCH_CHECK(ws.numel() >= S * J * M2p, "workspace too small");
+  auto out = at::empty({S, I, J}, x.options());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const int bnj = pick_bn_j(J);
+  // 1) Legendre synthesis, grouped per zonal wavenumber, pair rows (slice, cos/sin)
+  {
+    CUtensorMap ta = make_tmap(x.data_ptr(), 2, L, M2, S, Lp * 4, M2 * Lp * 4, 32, 2, 64);
+    CUtensorMap tb = make_tmap(P.data_ptr(), 2, L, J, Mw, Lp * 4, J * Lp * 4, 32, bnj, 1);
+    GemmParams p = default_params();
+    p.M = 2 * S; p.N = J; p.K = L; p.groups = Mw;
+    p.tiles_m = cdiv(S, 64); p.tiles_n = cdiv(J, bnj);
+    p.a_pair = 1; p.k_tri = 1;
+    p.C = ws.data_ptr(); p.c_pair = 1; p.c_ps = J * M2p; p.c_pmr = 1; p.c_sc = M2p;
+    p.err = err_ptr(err);
+    gemm_dispatch(2, bnj, false, false, ta, tb, p, st);
+  }
+  // 2) real DFT synthesis: out[s] (I x J) = F (I x M2) . Y[s]^T
+  {
+    CUtensorMap ta = make_tmap(F.data_ptr(), 2, M2, I, 1, M2p * 4, I * M2p * 4, 32, 128, 1);
+    CUtensorMap tb = make_tmap(ws.data_ptr(), 2, M2, J, S, M2p * 4, J * M2p * 4, 32, bnj, 1);
+    GemmParams p = default_params();
+    p.M = I; p.N = J; p.K = M2; p.groups = S;
+    p.tiles_m = cdiv(I, 128); p.tiles_n = cdiv(J, bnj);
+    p.a_group_div = 0; p.b_group_div = 1;
+    p.C = out.data_ptr(); p.c_sg = I * J; p.c_sr = J; p.c_sc = 1;
+    if (col_scale.has_value() && col_scale->defined()) p.col_scale = col_scale->data_ptr<float>();
+    p.err = err_ptr(err);
+    gemm_dispatch(2, bnj, false, false, ta, tb, p, st);
+  }
+  return out;
+}
+
+// N: (S, I, J) fp32 nodal;  Ft: (M2, I);  Pt: (Mw, L, J);  returns (S, M2, Lo) with Lo >= L.
+at::Tensor sht_anal(const at::Tensor& N, const at::Tensor& Ft, const at::Tensor& Pt, int64_t Lo,
+                    const at::Tensor& ws, const c10::optional<at::Tensor>& col_scale,
+                    const c10::optional<at::Tensor>& err) {
+  TORCH_CHECK(N.is_cuda() && N.scalar_type() == at::kFloat && N.is_contiguous(), "N must be contiguous fp32 CUDA");
+  c10::cuda::CUDAGuard guard(N.device());
+  const int64_t S = N.size(0), I = N.size(1), J = N.size(2);
+  const int64_t M2 = Ft.size(0);
+  const int64_t Mw = Pt.size(0), L = Pt.size(1);
+  TORCH_CHECK(Ft.size(1) == I && Pt.size(2) == J && J % 4 == 0 && I % 4 == 0, "basis shape mismatch");
+  TORCH_CHECK(ws.numel() >= S * M2 * J, "workspace too small");
+  TORCH_CHECK(Lo >= L, "output row length too small");
+  auto out = at::zeros({S, M2, Lo}, N.options());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const int bnj = pick_bn_j(J);
+  // 1) real DFT analysis: Z[s] (M2 x J) = Ft (M2 x I) . N[s] (I x J) [B operand N-major], times w_j
+  {
+    CUtensorMap ta = make_tmap(Ft.data_ptr(), 2, I, M2, 1, I * 4, M2 * I * 4, 32, 128, 1);
+    CUtensorMap tb = make_tmap(N.data_ptr(), 2, J, I, S, J * 4, I * J * 4, 32, 32, 1);
+    GemmParams p = default_params();
+    p.M = M2; p.N = J; p.K = I; p.groups = S;
+    p.tiles_m = cdiv(M2, 128); p.tiles_n = cdiv(J, bnj);
+    p.a_group_div = 0; p.b_group_div = 1;
+    p.C = ws.data_ptr(); p.c_sg = M2 * J; p.c_sr = J; p.c_sc = 1;
+    if (col_scale.has_value() && col_scale->defined()) p.col_scale = col_scale->data_ptr<float>();
+    p.err = err_ptr(err);
+    gemm_dispatch(2, bnj, false, true, ta, tb, p, st);
+  }
+  // 2) Legendre analysis per zonal wavenumber: out rows (slice, cos/sin), cols l
+  {
+    const int bnl = pick_bn_l(L);
+    CUtensorMap ta = make_tmap(ws.data_ptr(), 2, J, M2, S, J * 4, M2 * J * 4, 32, 2, 64);
+    CUtensorMap tb = make_tmap(Pt.data_ptr(), 2, J, L, Mw, J * 4, L * J * 4, 32, bnl, 1);
+    GemmParams p = default_params();
+    p.M = 2 * S; p.N = L; p.K = J; p.groups = Mw;
+    p.tiles_m = cdiv(S, 64); p.tiles_n = cdiv(L, bnl);
+    p.a_pair = 1;
+    p.C = out.data_ptr(); p.c_pair = 1; p.c_ps = M2 * Lo; p.c_pmr = Lo; p.c_sc = 1;
+    p.err = err_ptr(err);
+    gemm_dispatch(2, bnl, false, false, ta, tb, p, st);
+  }
+  return out;
+}
+
+// ── BF16 linear layers ──────────────────────────────────────────────────────
+// X: (T, Kp) bf16;  W: (O, Kp) bf16;  bias (O) fp32.  out (T, O) bf16 or fp32.
+void linear_fwd(const at::Tensor& X, const at::Tensor& W, const c10::optional<at::Tensor>& bias, int64_t act,
+                at::Tensor& out, const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& err) {
+  TORCH_CHECK(X.scalar_type() == at::kBFloat16 && W.scalar_type() == at::kBFloat16, "bf16 operands expected");
+  TORCH_CHECK(X.is_contiguous() && W.is_contiguous() && out.is_contiguous(), "contiguous operands expected");
+  c10::cuda::CUDAGuard guard(X.device());
+  const int64_t T = X.size(0), Kp = X.size(1), O = W.size(0);
+  TORCH_CHECK(W.size(1) == Kp && Kp % 8 == 0, "feature dim must be padded to a multiple of 8");
+  const int bn = O <= 64 ? 64 : 128;
+  CUtensorMap ta = make_tmap(X.data_ptr(), 1, Kp, T, 1, Kp * 2, T * Kp * 2, 64, 128, 1);
+  CUtensorMap tb = make_tmap(W.data_ptr(), 1, Kp, O, 1, Kp * 2, O * Kp * 2, 64, bn, 1);
+  GemmParams p = default_params();
+  p.M = T; p.N = O; p.K = Kp; p.groups = 1;
+  p.tiles_m = cdiv(T, 128); p.tiles_n = cdiv(O, bn);
+  p.C = out.data_ptr(); p.c_sr = O; p.c_sc = 1; p.c_sg = 0;
+  p.out_bf16 = out.scalar_type() == at::kBFloat16 ? 1 : 0;
+  if (bias.has_value() && bias->defined()) p.bias = bias->data_ptr<float>();
+  p.act = static_cast<int>(act);
+  if (aux.has_value() && aux->defined()) p.aux = reinterpret_cast<__nv_bfloat16*>(aux->data_ptr());
+  p.err = err_ptr(err);
+  gemm_dispatch(1, bn, false, false, ta, tb, p, at::cuda::getCurrentCUDAStream());
+}
+
+// dX (T, Kp) = dY (T, O) . W (O, Kp), optionally times act'(pre) of the layer input.
+void linear_dgrad(const at::Tensor& dY, const at::Tensor& W, at::Tensor& dX,
+                  const c10::optional<at::Tensor>& pre, int64_t pre_act, const c10::optional<at::Tensor>& err) {
+  c10::cuda::CUDAGuard guard(dY.device());
+  const int64_t T = dY.size(0), O = dY.size(1), Kp = W.size(1);
+  TORCH_CHECK(O % 8 == 0, "output features must be a multiple of 8");
+  const int bn = Kp <= 64 ? 64 : 128;
+  CUtensorMap ta = make_tmap(dY.data_ptr(), 1, O, T, 1, O * 2, T * O * 2, 64, 128, 1);
+  CUtensorMap tb = make_tmap(W.data_ptr(), 1, Kp, O, 1, Kp * 2, O * Kp * 2, 64, 64, 1);
+  GemmParams p = default_params();
+  p.M = T; p.N = Kp; p.K = O; p.groups = 1;
+  p.tiles_m = cdiv(T, 128); p.tiles_n = cdiv(Kp, bn);
+  p.C = dX.data_ptr(); p.c_sr = Kp; p.c_sc = 1;
+  p.out_bf16 = dX.scalar_type() == at::kBFloat16 ? 1 : 0;
+  if (pre.has_value() && pre->defined()) {
+    p.grad_pre = reinterpret_cast<const __nv_bfloat16*>(pre->data_ptr());
+    p.grad_act = static_cast<int>(pre_act);
+  }
+  p.err = err_ptr(err);
+  gemm_dispatch(1, bn, false, true, ta, tb, p, at::cuda::getCurrentCUDAStream());
+}
+
+// dW (O, Kp) fp32 += dY^T (O x T) . X (T x Kp)   [split-K, atomics]
+void linear_wgrad(const at::Tensor& dY, const at::Tensor& X, at::Tensor& dW, int64_t splits,
+                  const c10::optional<at::Tensor>& err) {
+  c10::cuda::CUDAGuard guard(dY.device());
+  const int64_t T = dY.size(0), O = dY.size(1), Kp = X.size(1);
+  TORCH_CHECK(dW.scalar_type() == at::kFloat && dW.size(0) == O && dW.size(1) == Kp, "dW shape");
+  const int bn = Kp <= 64 ? 64 : 128;
+  CUtensorMap ta = make_tmap(dY.data_ptr(), 1, O, T, 1, O * 2, T * O * 2, 64, 64, 1);
+  CUtensorMap tb = make_tmap(X.data_ptr(), 1, Kp, T, 1, Kp * 2, T * Kp * 2, 64, 64, 1);
+  GemmParams p = default_params();
+  p.M = O; p.N = Kp; p.K = T; p.groups = 1;
+  p.tiles_m = cdiv(O, 128); p.tiles_n = cdiv(Kp, bn);
+  const int64_t kblocks = cdiv(T, 64);
+  int64_t sp = splits > 0 ? splits : std::max<int64_t>(1, 296 / (p.tiles_m * p.tiles_n));
+  sp = std::min<int64_t>(sp, kblocks);
+  p.k_splits = static_cast<int>(sp);
+  p.beta = 1.f;
+  p.C = dW.data_ptr(); p.c_sr = Kp; p.c_sc = 1;
+  p.err = err_ptr(err);
+  gemm_dispatch(1, bn, true, true, ta, tb, p, at::cuda::getCurrentCUDAStream());
+}
+
+}  // namespace tgcm
+
+TORCH_LIBRARY_FRAGMENT(tgcm, m) {
+  m.def("sht_synth(Tensor x, int L, Tensor P, Tensor F, Tensor ws, Tensor? col_scale, Tensor? err) -> Tensor");
+  m.def("sht_anal(Tensor N, Tensor Ft, Tensor Pt, int Lo, Tensor ws, Tensor? col_scale, Tensor? err) -> Tensor");
+  m.def("linear_fwd(Tensor X, Tensor W, Tensor? bias, int act, Tensor(a!) out, Tensor? aux, Tensor? err) -> ()");
+  m.def("linear_dgrad(Tensor dY, Tensor W, Tensor(a!) dX, Tensor? pre, int pre_act, Tensor? err) -> ()");
+  m.def("linear_wgrad(Tensor dY, Tensor X, Tensor(a!) dW, int splits, Tensor? err) -> ()");
+}
+
+TORCH_LIBRARY_IMPL(tgcm, CUDA, m) {
+  m.impl("sht_synth", &tgcm::sht_synth);
+  m.impl("sht_anal", &tgcm::sht_anal);
+  m.impl("linear_fwd", &tgcm::linear_fwd);
+  m.impl("linear_dgrad", &tgcm::linear_dgrad);
+  m.impl("linear_wgrad", &tgcm::linear_wgrad);
+}

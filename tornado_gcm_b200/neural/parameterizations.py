@@ -1,0 +1,208 @@
+"""Neural physics parameterizations (Z3) — reference ``neural/parameterizations.py``.
+
+* :class:`SimpleParameterization` / :class:`ModalNeuralDivCurlParameterization`
+  keep the reference constructor signatures and state-dict keys; both accept
+  leading batch dimensions.
+* :class:`NodalColumnParameterization` is the per-column physics tower of the
+  NeuralGCM design: nodal (u, v, T', tracers, ln ps) plus forcings →
+  column network → nodal tendencies → modal (u, v mapped to ζ, δ by curl /
+  divergence).  On CUDA the column network runs on the tcgen05 BF16 GEMMs.
+"""
+
+from __future__ import annotations
+
+from typing import Callable, Optional, Sequence
+
+import torch
+import torch.nn as nn
+
+from tornado_gcm_b200.core import primitive_equations, spherical_harmonic
+from tornado_gcm_b200.core.spherical_harmonic import Grid
+
+State = primitive_equations.State
+
+
+def _forcing_channels(forcings: Optional[dict], like: torch.Tensor, lead: tuple, keys=None) -> list:
+    """Nodal forcing fields as (…, 1, lon, lat) channels, sorted by key."""
+    if not forcings:
+        return []
+    out = []
+    for k in (keys if keys is not None else sorted(forcings)):
+        if k not in forcings:
+            continue
+        v = forcings[k]
+        if not isinstance(v, torch.Tensor):
+            continue
+        v = v.to(like.dtype)
+        if v.shape[-2:] != like.shape[-2:]:
+            continue
+        while v.ndim < len(lead) + 3:
+            v = v.unsqueeze(-3) if v.ndim == len(lead) + 2 else v.unsqueeze(0)
+        out.append(v.expand(*lead, v.shape[-3], *like.shape[-2:]))
+    return out
+
+
+class SimpleParameterization(nn.Module):
+    """MLP on the flattened modal state (test/debug parameterization)."""
+
+    def __init__(self, modal_shape: tuple[int, int], n_levels: int, hidden_size: int = 64):
+        super().__init__()
+        self.modal_shape = tuple(modal_shape)
+        self.n_levels = n_levels
+        self.input_size = (3 * n_levels + 1) * modal_shape[0] * modal_shape[1]
+        self.output_size = self.input_size
+        self.net = nn.Sequential(
+            nn.Linear(self.input_size, hidden_size), nn.GELU(),
+            nn.Linear(hidden_size, hidden_size), nn.GELU(),
+            nn.Linear(hidden_size, self.output_size),
+        )
+        nn.init.zeros_(self.net[-1].weight)
+        nn.init.zeros_(self.net[-1].bias)
+
+    def forward(self, state: State, forcings=None, memory=None) -> State:
+        M, L = self.modal_shape
+        nz = self.n_levels
+        lead = state.vorticity.shape[:-3]
+        flat = lambda t: t.reshape(*lead, -1)
+        parts = [flat(state.vorticity), flat(state.divergence), flat(state.temperature_variation),
+                 flat(state.log_surface_pressure)]
+        if forcings:
+            for k in sorted(forcings):
+                f = forcings[k].to(parts[0].dtype)
+                parts.append(f.reshape(*lead, -1) if f.shape[:len(lead)] == lead else
+                             f.reshape(-1).expand(*lead, -1))
+        x = torch.cat(parts, dim=-1)
+        n_in = x.shape[-1]
+        if n_in < self.input_size:
+            x = torch.nn.functional.pad(x, (0, self.input_size - n_in))
+        elif n_in > self.input_size:
+            x = x[..., : self.input_size]
+        y = self.net(x.to(self.net[0].weight.dtype))
+        vol = nz * M * L
+        vor = y[..., :vol].reshape(*lead, nz, M, L)
+        div = y[..., vol:2 * vol].reshape(*lead, nz, M, L)
+        tmp = y[..., 2 * vol:3 * vol].reshape(*lead, nz, M, L)
+        lsp = y[..., 3 * vol:3 * vol + M * L].reshape(*lead, 1, M, L)
+        return State(vor, div, tmp, lsp, {k: torch.zeros_like(v) for k, v in state.tracers.items()}, state.sim_time)
+
+
+class ModalNeuralDivCurlParameterization(nn.Module):
+    """Nodal features (ζ, δ, T', ln ps) → tower → nodal tendencies → modal (+filter)."""
+
+    def __init__(self, grid: Grid, neural_net: nn.Module, n_levels: int,
+                 filter_fn: Optional[Callable[[torch.Tensor], torch.Tensor]] = None,
+                 use_mixed_precision_backward: bool = False, fwd_dtype: torch.dtype = torch.bfloat16):
+        super().__init__()
+        self.grid = grid
+        self.neural_net = neural_net
+        self.n_levels = n_levels
+        self.filter_fn = filter_fn
+        self.use_mixed_precision_backward = use_mixed_precision_backward
+        self.fwd_dtype = fwd_dtype
+
+    def _state_to_nodal_features(self, state: State) -> torch.Tensor:
+        stacked = torch.cat([state.vorticity, state.divergence, state.temperature_variation,
+                             state.log_surface_pressure], dim=-3)
+        return self.grid.to_nodal(stacked)
+
+    def _nodal_output_to_state(self, y: torch.Tensor, state: State) -> State:
+        nz = self.n_levels
+        modal = self.grid.to_modal(y[..., : 3 * nz + 1, :, :])
+        vor, div, tmp, sp = torch.split(modal, [nz, nz, nz, 1], dim=-3)
+        if self.filter_fn is not None:
+            vor, div, tmp, sp = (self.filter_fn(t) for t in (vor, div, tmp, sp))
+        return State(vor, div, tmp, sp, {k: torch.zeros_like(v) for k, v in state.tracers.items()}, state.sim_time)
+
+    def forward(self, state: State, forcings=None, memory=None) -> State:
+        x = self._state_to_nodal_features(state)
+        extra = _forcing_channels(forcings, x, tuple(x.shape[:-3]))
+        if extra:
+            x = torch.cat([x] + extra, dim=-3)
+        if self.use_mixed_precision_backward and self.training:
+            from tornado_gcm_b200.training.optimization import MixedPrecisionBackward
+
+            y = MixedPrecisionBackward.apply(self.neural_net, x, self.fwd_dtype)
+        else:
+            y = self.neural_net(x)
+        return self._nodal_output_to_state(y.to(state.vorticity.dtype), state)
+
+
+class NodalColumnParameterization(nn.Module):
+    """Column physics: nodal (u, v, T', tracers, ln ps, forcings) → nodal tendencies.
+
+    Input channels per column: ``2n (u, v) + n (T') + n·len(tracers) + 1
+    (ln ps) + len(forcing_keys)``.  Output channels: the same prognostic
+    set (without forcings).  Velocity tendencies are converted to vorticity
+    / divergence tendencies with the spectral curl / divergence of
+    ``(u, v)/cosθ`` as in NeuralGCM's div-curl parameterizations.
+    """
+
+    def __init__(self, grid: Grid, n_levels: int, tracer_keys: Sequence[str], neural_net: nn.Module,
+                 forcing_keys: Sequence[str] = (), output_scale: float = 1.0,
+                 filter_fn: Optional[Callable[[torch.Tensor], torch.Tensor]] = None,
+                 compute_dtype: torch.dtype = torch.bfloat16):
+        super().__init__()
+        self.grid = grid
+        self.n_levels = n_levels
+        self.tracer_keys = tuple(tracer_keys)
+        self.forcing_keys = tuple(forcing_keys)
+        self.tower = neural_net
+        self.output_scale = output_scale
+        self.filter_fn = filter_fn
+        self.compute_dtype = compute_dtype
+
+    @property
+    def n_inputs(self) -> int:
+        return self.n_levels * (3 + len(self.tracer_keys)) + 1 + len(self.forcing_keys)
+
+    @property
+    def n_outputs(self) -> int:
+        return self.n_levels * (3 + len(self.tracer_keys)) + 1
+
+    def nodal_prognostics(self, state: State) -> torch.Tensor:
+        """(…, C, lon, lat) with channels [u, v, T', tracers…, ln ps] (u, v physical)."""
+        g = self.grid
+        uc, vc = spherical_harmonic.get_cos_lat_vector(state.vorticity, state.divergence, g, clip=False)
+        tr = [state.tracers[k] if k in state.tracers else torch.zeros_like(state.temperature_variation)
+              for k in self.tracer_keys]
+        nodal = g.to_nodal(torch.cat([uc, vc, state.temperature_variation] + tr + [state.log_surface_pressure],
+                                     dim=-3))
+        n = self.n_levels
+        sec = 1.0 / g.const("cos_lat", nodal.device, nodal.dtype)
+        u = nodal[..., :n, :, :] * sec
+        v = nodal[..., n:2 * n, :, :] * sec
+        return torch.cat([u, v, nodal[..., 2 * n:, :, :]], dim=-3)
+
+    def forward(self, state: State, forcings=None, memory=None) -> State:
+        x = self.nodal_prognostics(state)
+        lead = tuple(x.shape[:-3])
+        extra = _forcing_channels(forcings, x, lead, self.forcing_keys)
+        if extra:
+            x = torch.cat([x] + extra, dim=-3)
+        elif self.forcing_keys:
+            x = torch.cat([x, x.new_zeros(*lead, len(self.forcing_keys), *x.shape[-2:])], dim=-3)
+        y = self.tower(x.to(self.compute_dtype)).to(state.vorticity.dtype) * self.output_scale
+        return self.nodal_tendency_to_modal(y, state)
+
+    def nodal_tendency_to_modal(self, y: torch.Tensor, state: State) -> State:
+        g = self.grid
+        n = self.n_levels
+        cos = g.const("cos_lat", y.device, y.dtype)
+        # u, v tendencies → divide by cosθ before the transform (curl/div of v·cosθ / cos²θ)
+        uv = y[..., : 2 * n, :, :] / cos
+        modal = g.to_modal(torch.cat([uv, y[..., 2 * n:, :, :]], dim=-3))
+        um, vm = modal[..., :n, :, :], modal[..., n:2 * n, :, :]
+        vort = g.curl_cos_lat((um, vm), clip=True)
+        div = g.div_cos_lat((um, vm), clip=True)
+        temp = modal[..., 2 * n:3 * n, :, :]
+        tr = {}
+        off = 3 * n
+        for k in self.tracer_keys:
+            tr[k] = modal[..., off:off + n, :, :]
+            off += n
+        lsp = modal[..., off:off + 1, :, :]
+        out = State(vort, div, temp, lsp, {k: tr.get(k, torch.zeros_like(v)) for k, v in state.tracers.items()},
+                    state.sim_time)
+        if self.filter_fn is not None:
+            out = out.tree_map(self.filter_fn)
+        return out

@@ -1,0 +1,69 @@
+"""Loader for the in-tree sm_100a extension (``tornado_gcm_b200/_C*.so``).
+
+The CUDA code paths require it: when a CUDA tensor reaches an op and the
+extension did not load, :func:`require` raises instead of silently falling
+back to eager torch.
+"""
+
+from __future__ import annotations
+
+import glob
+import os
+
+import torch
+
+_LOADED = None
+_ERROR = None
+
+
+def load() -> bool:
+    global _LOADED, _ERROR
+    if _LOADED is not None:
+        return _LOADED
+    try:
+        from tornado_gcm_b200 import _C  # noqa: F401  (registers torch.ops.tgcm.*)
+
+        _LOADED = hasattr(torch.ops.tgcm, "sht_synth")
+    except Exception as exc:  # pragma: no cover - depends on the build
+        _ERROR = exc
+        _LOADED = False
+    return _LOADED
+
+
+def available() -> bool:
+    return load()
+
+
+def require(what: str = "kernel"):
+    if not load():
+        here = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        found = glob.glob(os.path.join(here, "_C*.so"))
+        raise RuntimeError(
+            f"tornado_gcm_b200 CUDA extension required for {what} but not loaded "
+            f"(found {found}; error: {_ERROR}). Build it with `python setup.py build_ext --inplace`.")
+    return torch.ops.tgcm
+
+
+def error_flag(device) -> torch.Tensor:
+    """Per-device int32 flag that kernels set on a bounded-wait timeout."""
+    key = str(device)
+    t = _FLAGS.get(key)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=device)
+        _FLAGS[key] = t
+    return t
+
+
+_FLAGS: dict = {}
+
+
+def check_error_flag(device) -> int:
+    """Read (and clear) the device error flag; raises on a recorded timeout."""
+    f = _FLAGS.get(str(device))
+    if f is None:
+        return 0
+    code = int(f.item())
+    if code:
+        f.zero_()
+        raise RuntimeError(f"tornado_gcm_b200 kernel reported error code {code} (bounded wait expired)")
+    return 0

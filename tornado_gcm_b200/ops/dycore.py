@@ -1,0 +1,321 @@
+"""Fused dycore path on sm_100a.
+
+* :class:`ColumnSpec` — slice layout and constants of the per-column
+  nonlinear tendency kernel (``csrc/dycore_column.h``).
+* :class:`ColumnFn` — autograd op: forward kernel, backward = the
+  hand-written VJP kernel (both also have CPU twins used as oracles).
+* :class:`ImplicitSolveFn` / :class:`ImplicitTermsFn` — per-wavenumber
+  vertical operators; backward = their transposes (same kernel, modes 1/3).
+* :func:`explicit_terms` — spectral pre-processing → stacked TF32 synthesis
+  → column kernel → stacked TF32 analysis → spectral post-processing.
+* :class:`FusedSIL3` — one IMEX-SIL3 substep (Whitaker & Kar 2013 tableau,
+  same as ``core.time_integration.SIL3_TABLEAU``) with the constant physics
+  tendency, the combined spectral filter and the inner-state sanitiser.
+  The last stage is returned directly: SIL3 is stiffly accurate (its final
+  implicit weight row equals b_im), so y_out = y_3 exactly in exact
+  arithmetic and one implicit-terms evaluation is saved.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+from typing import Sequence
+
+import numpy as np
+import torch
+
+from tornado_gcm_b200.core import primitive_equations as pe
+from tornado_gcm_b200.ops import _ext
+
+State = pe.State
+
+
+@dataclasses.dataclass
+class ColumnSpec:
+    n: int
+    tracer_keys: tuple
+    hum: int
+    hum_terms: int
+    clouds: list
+    vadv: int
+    R: float
+    kappa: float
+    rv: float
+    cpv: float
+    level_consts: torch.Tensor  # (5, n) fp32 on CPU
+    sec2: np.ndarray
+    cor: np.ndarray
+    eq: object = None
+    _dev: dict = dataclasses.field(default_factory=dict)
+
+    @classmethod
+    def from_equation(cls, eq: pe.PrimitiveEquationsSigma, tracer_keys: Sequence[str]) -> "ColumnSpec":
+        c = eq.column_constants
+        keys = tuple(tracer_keys)
+        n = eq.vertical.layers
+        hum = keys.index(eq.humidity_key) if (eq.humidity_key is not None and eq.humidity_key in keys) else -1
+        clouds = [keys.index(k) for k in (eq.cloud_keys or ()) if k in keys]
+        idc = np.zeros(n)
+        idc[: n - 1] = c.inv_dcenter
+        lc = torch.tensor(np.stack([c.dsigma, c.alpha, c.t_ref, idc, c.cum_dsigma]), dtype=torch.float32)
+        return cls(n, keys, hum, 1 if eq.humidity_key is not None else 0, clouds, 1 if c.vertical_advection else 0,
+                   c.R, c.kappa, c.rv_ratio, c.cpv_ratio, lc, c.sec2, c.coriolis, eq)
+
+    @property
+    def n_in(self) -> int:
+        h = self.hum_terms
+        return (5 + len(self.tracer_keys) + 2 * h) * self.n + 2 + h
+
+    @property
+    def n_out(self) -> int:
+        return (6 + 3 * len(self.tracer_keys) + 3 * self.hum_terms) * self.n + 1
+
+    def device_consts(self, device):
+        key = str(device)
+        d = self._dev.get(key)
+        if d is None:
+            d = (torch.as_tensor(self.sec2, dtype=torch.float32, device=device),
+                 torch.as_tensor(self.cor, dtype=torch.float32, device=device))
+            self._dev[key] = d
+        return d
+
+    def args(self):
+        return (self.level_consts, self.n, len(self.tracer_keys), self.hum, self.hum_terms, list(self.clouds),
+                self.vadv, self.R, self.kappa, self.rv, self.cpv)
+
+    # helpers for tests: dict <-> stacked (B*S, I, J)
+    def stack_inputs(self, inp: dict) -> torch.Tensor:
+        parts = [inp["vort"], inp["div"], inp["temp"], inp["u"], inp["v"]]
+        parts += [inp["tracers"][k] for k in self.tracer_keys]
+        if self.hum_terms:
+            parts += [inp["qx"], inp["qy"]]
+        parts += [inp["gx"], inp["gy"]]
+        if self.hum_terms:
+            parts += [inp["lap_lnps"]]
+        x = torch.cat(parts, dim=-3)
+        return x.reshape(-1, *x.shape[-2:])
+
+    def stack_outputs(self, out: dict) -> torch.Tensor:
+        parts = [out[k] for k in ("flux_u", "flux_v", "ke", "temp", "temp_u", "temp_v")]
+        for k in self.tracer_keys:
+            parts += [out["tr:" + k], out["tr_u:" + k], out["tr_v:" + k]]
+        if self.hum_terms:
+            parts += [out["tdiff"], out["hum_div"], out["hum_vort"]]
+        parts += [out["lnps"]]
+        x = torch.cat(parts, dim=-3)
+        return x.reshape(-1, *x.shape[-2:])
+
+
+def column_forward_raw(spec: ColumnSpec, nin: torch.Tensor, batch: int) -> torch.Tensor:
+    ops = _ext.require("column tendency")
+    s2, co = spec.device_consts(nin.device)
+    return ops.column_fwd(nin.contiguous(), s2, co, *_args_with_batch(spec, batch))
+
+
+def column_vjp_raw(spec: ColumnSpec, nin: torch.Tensor, gout: torch.Tensor, batch: int) -> torch.Tensor:
+    ops = _ext.require("column tendency VJP")
+    s2, co = spec.device_consts(nin.device)
+    return ops.column_vjp(nin.contiguous(), gout.contiguous(), s2, co, *_args_with_batch(spec, batch))
+
+
+def _args_with_batch(spec, batch):
+    a = spec.args()
+    return (a[0], batch) + a[1:]
+
+
+class ColumnFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, nin, spec, batch):
+        ctx.spec, ctx.batch = spec, batch
+        ctx.save_for_backward(nin)
+        return column_forward_raw(spec, nin, batch)
+
+    @staticmethod
+    def backward(ctx, gout):
+        (nin,) = ctx.saved_tensors
+        return column_vjp_raw(ctx.spec, nin, gout, ctx.batch), None, None
+
+
+# ── implicit operators ─────────────────────────────────────────────────────
+class _ImplicitConsts:
+    def __init__(self, eq: pe.PrimitiveEquationsSigma):
+        self.eq = eq
+        self.G = torch.tensor(eq._G_matrix, dtype=torch.float32)
+        self.H = torch.tensor(eq._H_matrix, dtype=torch.float32)
+        self.lam = torch.tensor(np.asarray(eq.grid.laplacian_eigenvalues, np.float64), dtype=torch.float32)
+        self.tref = torch.tensor(eq.T_ref, dtype=torch.float32)
+        self.dsig = torch.tensor(eq._dsigma, dtype=torch.float32)
+        self._dev: dict = {}
+        self._minv: dict = {}
+
+    def on(self, device):
+        key = str(device)
+        d = self._dev.get(key)
+        if d is None:
+            d = tuple(t.to(device) for t in (self.G, self.H, self.lam, self.tref, self.dsig))
+            self._dev[key] = d
+        return d
+
+    def minv(self, eta: float, device):
+        key = (round(float(eta), 15), str(device))
+        m = self._minv.get(key)
+        if m is None:
+            eq = self.eq
+            g, h = eq._G_matrix, eq._H_matrix
+            lam = np.asarray(eq.grid.laplacian_eigenvalues, np.float64)
+            n = g.shape[0]
+            core = g @ h + eq.R * np.outer(eq.T_ref, eq._dsigma)
+            mats = np.eye(n)[None] - (eta * eta) * lam[:, None, None] * core[None]
+            m = torch.tensor(np.linalg.inv(mats), dtype=torch.float32, device=device)
+            self._minv[key] = m
+        return m
+
+
+def _consts(eq) -> _ImplicitConsts:
+    c = getattr(eq, "_fused_implicit_consts", None)
+    if c is None:
+        c = _ImplicitConsts(eq)
+        eq._fused_implicit_consts = c
+    return c
+
+
+def implicit_apply(eq, d, t, p, eta: float, mode: int):
+    ops = _ext.require("implicit solve")
+    c = _consts(eq)
+    G, H, lam, tref, dsig = c.on(d.device)
+    minv = c.minv(eta, d.device) if mode <= 1 else None
+    squeeze = d.dim() == 3
+    if squeeze:
+        d, t, p = d.unsqueeze(0), t.unsqueeze(0), p.unsqueeze(0)
+    out = ops.implicit_apply(d, t, p, G, H, minv, lam, tref, dsig, float(eq.R), float(eta), int(mode))
+    if squeeze:
+        out = [o.squeeze(0) for o in out]
+    return out
+
+
+class ImplicitSolveFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, d, t, p, eq, eta):
+        ctx.eq, ctx.eta = eq, eta
+        return tuple(implicit_apply(eq, d, t, p, eta, 0))
+
+    @staticmethod
+    def backward(ctx, gd, gt, gp):
+        od, ot, op = implicit_apply(ctx.eq, gd.contiguous(), gt.contiguous(), gp.contiguous(), ctx.eta, 1)
+        return od, ot, op, None, None
+
+
+class ImplicitTermsFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, d, t, p, eq):
+        ctx.eq = eq
+        return tuple(implicit_apply(eq, d, t, p, 0.0, 2))
+
+    @staticmethod
+    def backward(ctx, gd, gt, gp):
+        od, ot, op = implicit_apply(ctx.eq, gd.contiguous(), gt.contiguous(), gp.contiguous(), 0.0, 3)
+        return od, ot, op, None
+
+
+# ── explicit terms ─────────────────────────────────────────────────────────
+def explicit_terms(eq: pe.PrimitiveEquationsSigma, state: State) -> State:
+    """Fused GPU explicit tendency (TF32 transforms + column kernel)."""
+    grid = eq.grid
+    if grid.resolved_precision == "highest":
+        return eq.explicit_terms_reference(state)
+    keys = tuple(sorted(state.tracers))
+    spec = _spec_for(eq, keys)
+    lead = state.vorticity.shape[:-3]
+    batch = int(np.prod(lead)) if len(lead) else 1
+    dtype = state.vorticity.dtype
+    st = state.tree_map(lambda x: x.float()) if dtype != torch.float32 else state
+    modal_in = eq.modal_pre_stack(st, grid)
+    nodal_in = grid.to_nodal(modal_in).reshape(batch * spec.n_in, *grid.nodal_shape)
+    nodal_out = ColumnFn.apply(nodal_in, spec, batch)
+    modal_out = grid.to_modal(nodal_out).reshape(*lead, spec.n_out, *grid.modal_shape)
+    out = eq.modal_post(modal_out, st, grid)
+    return out.tree_map(lambda x: x.to(dtype)) if dtype != torch.float32 else out
+
+
+def _spec_for(eq, keys) -> ColumnSpec:
+    cache = getattr(eq, "_column_specs", None)
+    if cache is None:
+        cache = {}
+        eq._column_specs = cache
+    s = cache.get(keys)
+    if s is None:
+        s = ColumnSpec.from_equation(eq, keys)
+        cache[keys] = s
+    return s
+
+
+def implicit_terms(eq, state: State) -> State:
+    d, t, p = ImplicitTermsFn.apply(state.divergence, state.temperature_variation, state.log_surface_pressure, eq)
+    return State(torch.zeros_like(state.vorticity), d, t, p, {k: torch.zeros_like(v) for k, v in state.tracers.items()},
+                 state.sim_time)
+
+
+def implicit_inverse(eq, state: State, eta: float) -> State:
+    d, t, p = ImplicitSolveFn.apply(state.divergence, state.temperature_variation, state.log_surface_pressure, eq,
+                                    float(eta))
+    return State(state.vorticity, d, t, p, state.tracers, state.sim_time)
+
+
+# ── SIL3 substep ───────────────────────────────────────────────────────────
+def _lin(terms):
+    """Σ c_i · x_i over (coefficient, State) pairs (coefficients may be 0)."""
+    out = None
+    for c, x in terms:
+        if c == 0:
+            continue
+        out = x * c if out is None else out + x * c
+    return out
+
+
+class FusedSIL3:
+    """One SIL3 substep of dycore + constant physics, then filter + sanitise."""
+
+    A_EX = [[1 / 3], [1 / 6, 1 / 2], [1 / 2, -1 / 2, 1]]
+    A_IM = [[1 / 6, 1 / 6], [1 / 3, 0, 1 / 3], [3 / 8, 0, 3 / 8, 1 / 4]]
+
+    def __init__(self, eq: pe.PrimitiveEquationsSigma, dt: float, filter_scaling: np.ndarray,
+                 clamp_abs: float = 1.0e12, sanitize: bool = True):
+        self.eq = eq
+        self.dt = float(dt)
+        self.filter_scaling = np.asarray(filter_scaling, dtype=np.float64)
+        self.clamp_abs = clamp_abs
+        self.sanitize = sanitize
+        self._filt: dict = {}
+
+    def _filter(self, device):
+        key = str(device)
+        f = self._filt.get(key)
+        if f is None:
+            f = torch.as_tensor(self.filter_scaling, dtype=torch.float32, device=device)
+            self._filt[key] = f
+        return f
+
+    def step(self, y0: State, phys: State) -> State:
+        eq, dt = self.eq, self.dt
+        E = []
+        ys = [y0]
+        G0 = implicit_terms(eq, y0)
+        Gs = {0: G0}
+        for i in range(1, 4):
+            E.append(explicit_terms(eq, ys[-1]) + phys)
+            a_ex = self.A_EX[i - 1]
+            a_im = self.A_IM[i - 1]
+            terms = [(1.0, y0)] + [(dt * a_ex[j], E[j]) for j in range(i)]
+            terms += [(dt * a_im[j], Gs[j]) for j in range(i) if a_im[j] != 0]
+            y_star = _lin(terms)
+            yi = implicit_inverse(eq, y_star, dt * a_im[i])
+            ys.append(yi)
+            if i == 2:
+                Gs[2] = implicit_terms(eq, yi)
+        out = ys[-1]
+        f = self._filter(out.vorticity.device)
+        out = out.tree_map(lambda x: x * f)
+        if self.sanitize:
+            c = self.clamp_abs
+            out = out.tree_map(lambda x: torch.clamp(torch.nan_to_num(x, nan=0.0, posinf=c, neginf=-c), -c, c))
+        return dataclasses.replace(out, sim_time=y0.sim_time)

@@ -1,0 +1,138 @@
+"""Spherical-harmonic transforms on sm_100a (tcgen05 TF32 GEMMs).
+
+``to_nodal`` = Legendre synthesis (grouped per zonal wavenumber m, cos/sin
+rows paired so one tile row-block serves both) followed by the real-DFT
+synthesis against a resident Fourier basis; ``to_modal`` = quadrature-
+weighted DFT analysis followed by Legendre analysis.  Both are
+``torch.autograd.Function`` s whose adjoints are the opposite transforms:
+
+* adjoint of synthesis  = analysis without quadrature weights;
+* adjoint of analysis   = w_j ⊙ synthesis.
+
+Bases are built once per grid in FP64, cast to fp32 and kept on the device:
+``P (Mw, J, Lp)``, ``Pt (Mw, L, J)``, ``F (I, M2p)``, ``Ft (M2, I)``, ``w (J)``.
+The "highest" precision setting runs FP64 torch contractions instead (the
+numerical oracle mode).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from tornado_gcm_b200.ops import _ext
+
+
+def _round_up(x: int, m: int) -> int:
+    return (x + m - 1) // m * m
+
+
+class _Bases:
+    def __init__(self, sh, device):
+        Mw = sh.longitude_wavenumbers
+        L = sh.total_wavenumbers
+        I = sh.longitude_nodes
+        J = sh.latitude_nodes
+        M2 = 2 * Mw - 1
+        self.L, self.Lp, self.I, self.J, self.M2 = L, _round_up(L, 4), I, J, M2
+        self.M2p = _round_up(M2, 4)
+        p = sh.legendre_table  # (Mw, J, L)
+        pp = np.zeros((Mw, J, self.Lp))
+        pp[:, :, :L] = p
+        f = sh.basis.f  # (I, M2)
+        fp = np.zeros((I, self.M2p))
+        fp[:, :M2] = f
+        dev = torch.device(device)
+        t = lambda a: torch.as_tensor(np.ascontiguousarray(a), dtype=torch.float32, device=dev)
+        self.P = t(pp)
+        self.Pt = t(np.transpose(p, (0, 2, 1)))
+        self.F = t(fp)
+        self.Ft = t(f.T)
+        self.w = t(sh.basis.w)
+        if I % 4 or J % 4:
+            raise ValueError("GPU transforms need lon/lat node counts divisible by 4")
+
+
+_BASES: dict = {}
+
+
+def bases(sh, device) -> _Bases:
+    key = (id(sh), str(device))
+    entry = _BASES.get(key)
+    if entry is None:
+        entry = (_Bases(sh, device), sh)  # keep sh alive so id() stays unique
+        _BASES[key] = entry
+    return entry[0]
+
+
+def _synth(x3: torch.Tensor, b: _Bases, col_scale=None) -> torch.Tensor:
+    ops = _ext.require("spherical-harmonic synthesis")
+    S = x3.shape[0]
+    x3 = x3.float()
+    if b.Lp != b.L:
+        x3 = torch.nn.functional.pad(x3, (0, b.Lp - b.L))
+    x3 = x3.contiguous()
+    ws = torch.empty(S * b.J * b.M2p, dtype=torch.float32, device=x3.device)
+    return ops.sht_synth(x3, b.L, b.P, b.F, ws, col_scale, _ext.error_flag(x3.device))
+
+
+def _anal(n3: torch.Tensor, b: _Bases, col_scale=None) -> torch.Tensor:
+    ops = _ext.require("spherical-harmonic analysis")
+    S = n3.shape[0]
+    n3 = n3.float().contiguous()
+    ws = torch.empty(S * b.M2 * b.J, dtype=torch.float32, device=n3.device)
+    return ops.sht_anal(n3, b.Ft, b.Pt, b.L, ws, col_scale, _ext.error_flag(n3.device))
+
+
+class ToNodalFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x3, b):
+        ctx.b = b
+        return _synth(x3, b)
+
+    @staticmethod
+    def backward(ctx, g):
+        return _anal(g, ctx.b), None
+
+
+class ToModalFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, n3, b):
+        ctx.b = b
+        return _anal(n3, b, b.w)
+
+    @staticmethod
+    def backward(ctx, g):
+        return _synth(g, ctx.b, ctx.b.w), None
+
+
+def to_nodal(x: torch.Tensor, sh) -> torch.Tensor:
+    """Modal (…, 2M-1, L) → nodal (…, I, J) on the GPU."""
+    if sh.precision == "highest":
+        return _highest(x, sh, inverse=True)
+    b = bases(sh, x.device)
+    lead = x.shape[:-2]
+    out = ToNodalFn.apply(x.reshape(-1, b.M2, b.L).float(), b)
+    return out.reshape(*lead, b.I, b.J).to(x.dtype)
+
+
+def to_modal(x: torch.Tensor, sh) -> torch.Tensor:
+    """Nodal (…, I, J) → modal (…, 2M-1, L) on the GPU."""
+    if sh.precision == "highest":
+        return _highest(x, sh, inverse=False)
+    b = bases(sh, x.device)
+    lead = x.shape[:-2]
+    out = ToModalFn.apply(x.reshape(-1, b.I, b.J).float(), b)
+    return out.reshape(*lead, b.M2, b.L).to(x.dtype)
+
+
+def _highest(x, sh, inverse: bool):
+    p = sh.device_basis("p", x.device, torch.float64)
+    f = sh.device_basis("f", x.device, torch.float64)
+    x64 = x.to(torch.float64)
+    if inverse:
+        out = torch.einsum("im,...mj->...ij", f, torch.einsum("mjl,...ml->...mj", p, x64))
+    else:
+        w = sh.device_basis("w", x.device, torch.float64)
+        out = torch.einsum("mjl,...mj->...ml", p, torch.einsum("im,...ij->...mj", f, x64 * w))
+    return out.to(x.dtype)
