@@ -1,0 +1,461 @@
+#!/usr/bin/env python
+"""Training-throughput benchmark of the hybrid GCM (6-h model steps per second).
+
+Workload (per GPU): 2.8° model (TL63, 128×64 Gaussian grid, 32 σ levels),
+batch 4, backpropagation through a 4 × 6-h rollout (72 physics steps of
+20 min, neural tendency every physics step), column encoder 3×256 from 7
+fields × 37 pressure levels, column tower 5×384, column decoder 3×256, Z2
+fixer every step, MSE loss on the decoded fields, AdamW (lr 1e-4), grad
+clipping and EMA.  Synthetic reanalysis-shaped data, random-init weights.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+For N > 1 launch one process per GPU with torch.distributed.run; data
+parallel over ranks (weak scaling, batch 4 per GPU).  Device time of the K
+timed steps is taken with CUDA events between barrier + synchronize and
+reduced as the max over ranks.  Rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+PUBLISHED_STEPS_PER_S = 4.1  # reference README, 2.8° on 1× A100
+METRIC = "model steps/s (train & 6h-forecast) at 2.8°/1.4°/0.7°, 1/2/4/8 B200, vs ref NCCL"
+MY_KERNELS = ("gemm_sm100_kernel", "column_fwd_kernel", "column_vjp_kernel", "implicit_kernel",
+              "fused_allreduce", "fixer_", "tgcm_")
+
+
+# ── helpers ─────────────────────────────────────────────────────────────────
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    p.add_argument("--resolution", default="2.8deg")
+    p.add_argument("--batch", type=int, default=4, help="per-GPU batch")
+    p.add_argument("--rollout", type=int, default=4, help="6-h steps per training example")
+    p.add_argument("--no-graph", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str | None):
+        self.uuid = uuid
+        self.proc = None
+        self.lines: list[str] = []
+        self._thr = None
+
+    def start(self):
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+        if self.uuid:
+            cmd += ["-i", self.uuid]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self._thr = threading.Thread(target=self._read, daemon=True)
+        self._thr.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self._thr is not None:
+            self._thr.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 10:
+                continue
+            try:
+                sm.append(float(parts[2]))
+                smax.append(float(parts[3]))
+            except ValueError:
+                continue
+            for nm, flag in zip(names, parts[6:10]):
+                if flag.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world <= 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def device_uuid() -> str | None:
+    try:
+        u = torch.cuda.get_device_properties(torch.cuda.current_device()).uuid
+        s = str(u)
+        return s if s.startswith("GPU-") else "GPU-" + s
+    except Exception:
+        return None
+
+
+def timed_region(step_fn, steps: int, world: int, sampler: ClockSampler | None):
+    barrier(world)
+    torch.cuda.synchronize()
+    if sampler is not None:
+        sampler.start()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(steps):
+        step_fn(i)
+    end.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = sampler.stop() if sampler is not None else None
+    ms = start.elapsed_time(end)
+    return max_over_ranks(ms, world), clocks
+
+
+# ── this framework ──────────────────────────────────────────────────────────
+def run_b200(args, rank, world):
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    from tornado_gcm_b200.models.builders import RESOLUTIONS, build_hybrid_gcm
+    from tornado_gcm_b200.ops import _ext
+    from tornado_gcm_b200.training.trainer import GCMTrainer
+
+    _ext.require("benchmark")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    gcm, data = build_hybrid_gcm(args.resolution, dev, seed=0)
+    spec = RESOLUTIONS[args.resolution]
+    trainer = GCMTrainer(gcm, lr=1e-4, graph=not args.no_graph, data_parallel=world > 1)
+    B, K = args.batch, args.rollout
+    enc = gcm.encoder
+
+    def norm(d):
+        return {k: ((v.to(dev) - getattr(enc, f"mean_{k}")) / getattr(enc, f"std_{k}")).cpu() for k, v in d.items()}
+
+    # pinned host pool of a few batches (cycled); distinct per rank
+    pool = []
+    for j in range(2):
+        s = 100 * rank + 10 * j
+        x0 = norm(data.sample(B, s))
+        tg = [norm(data.sample(B, s + i + 1)) for i in range(K)]
+        pool.append(({k: v.pin_memory() for k, v in x0.items()},
+                     [{k: v.pin_memory() for k, v in t.items()} for t in tg]))
+    forc_host = {k: v.pin_memory() for k, v in data.forcings(B).items()}
+    to_dev = lambda d: {k: v.to(dev, non_blocking=True) for k, v in d.items()}
+    dev_pool = [(to_dev(a), [to_dev(t) for t in b]) for a, b in pool]
+    forc_dev = to_dev(forc_host)
+    h2d_bytes = sum(v.numel() * v.element_size() for v in pool[0][0].values())
+    h2d_bytes += sum(v.numel() * v.element_size() for t in pool[0][1] for v in t.values())
+    h2d_bytes += sum(v.numel() * v.element_size() for v in forc_host.values())
+
+    losses = []
+
+    def step_dev(i):
+        x0, tg = dev_pool[i % len(dev_pool)]
+        losses.append(trainer.train_step(x0, tg, forc_dev))
+
+    for i in range(args.warmup):
+        step_dev(i)
+    torch.cuda.synchronize()
+    _ext.check_error_flag(dev)
+    sampler = ClockSampler(device_uuid()) if rank == 0 else None
+    ms, clocks = timed_region(step_dev, args.steps, world, sampler)
+    _ext.check_error_flag(dev)
+    ms_per_step = ms / args.steps
+    loss_last = float(losses[-1].item()) if losses else float("nan")
+
+    e2e = None
+    if not args.no_e2e:
+        host_loss = []
+
+        def step_e2e(i):
+            x0h, tgh = pool[i % len(pool)]
+            x0 = to_dev(x0h)
+            tg = [to_dev(t) for t in tgh]
+            f = to_dev(forc_host)
+            loss = trainer.train_step(x0, tg, f)
+            host_loss.append(float(loss.item()))  # D2H read of the step's result
+
+        ms_e2e, _ = timed_region(step_e2e, args.steps, world, None)
+        e2e = {"value": world * B * K / (ms_e2e / args.steps / 1000.0),
+               "unit": "6h model-steps/s (samples x 6-h steps, all GPUs), end to end",
+               "h2d_bytes_per_step": int(h2d_bytes), "d2h_bytes_per_step": 4,
+               "ms_per_step": ms_e2e / args.steps}
+
+    # count this framework's kernels in one (eager) step, outside the timed region
+    launches = None
+    try:
+        from torch.profiler import ProfilerActivity, profile
+
+        x0, tg = dev_pool[0]
+        use_graph = trainer.use_graph
+        trainer.use_graph = False
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            trainer._zero()
+            trainer._step_body(x0, tg, forc_dev)
+            torch.cuda.synchronize()
+        trainer.use_graph = use_graph
+        n_mine = 0
+        n_all = 0
+        for ev in prof.events():
+            if ev.device_type == torch.autograd.DeviceType.CUDA:
+                n_all += 1
+                if any(k in ev.name for k in MY_KERNELS):
+                    n_mine += 1
+        launches = {"per_step_mine": n_mine, "per_step_all": n_all}
+    except Exception as exc:  # pragma: no cover
+        launches = {"error": str(exc)}
+
+    value = world * B * K / (ms_per_step / 1000.0)
+    if rank == 0:
+        out = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "6h model-steps/s (samples x 6-h steps, all GPUs)",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_per_step,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": value / PUBLISHED_STEPS_PER_S,
+            "dtype": "bf16",
+            "data": "synthetic reanalysis-shaped fields, random-init weights",
+            "config": {
+                "model": f"{args.resolution} {spec.grid} L{spec.layers} hybrid GCM (encoder 3x256, tower 5x"
+                         f"{spec.tower_width}, decoder 3x256, IMEX-SIL3 dt={spec.dt_minutes:g} min, "
+                         f"{spec.physics_steps_per_output} physics steps per 6 h)",
+                "global_batch": world * B,
+                "seq_len": K,
+                "seq_len_meaning": "6-h rollout steps per example (backprop through the whole rollout)",
+                "parallelism": f"dp{world}",
+                "zones": "Z1 TF32 tcgen05 transforms, Z3 BF16 tcgen05 towers, Z2 FP64-accumulated fixer",
+                "cuda_graph": trainer.use_graph,
+                "l2": "working set per step (activations of 72 physics steps) far exceeds the 126 MB L2",
+                "loss": loss_last,
+            },
+            "clocks": clocks,
+            "e2e": e2e,
+            "gpu_launches": (launches or {}).get("per_step_mine", 0) * args.steps,
+            "launch_detail": launches,
+            "impl": "b200",
+        }
+        print(json.dumps(out), flush=True)
+    trainer.release_graph()
+
+
+# ── reference arm (unmodified reference from baseline/_ref) ─────────────────
+def run_reference(args, rank, world):
+    here = os.path.dirname(os.path.abspath(__file__))
+    ref_root = os.path.join(here, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_root, "tornado_gcm")):
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref/tornado_gcm not installed"}))
+        return
+    sys.path.insert(0, ref_root)
+    from types import SimpleNamespace
+
+    import numpy as np
+    import torch.nn.functional as F
+
+    from tornado_gcm.core import coordinate_systems, sigma_coordinates, spherical_harmonic
+    from tornado_gcm.model.api import ModelConfig, NeuralGCMModel
+    from tornado_gcm.neural.fixers import LiteConservationFixer
+    from tornado_gcm.neural.parameterizations import ModalNeuralDivCurlParameterization
+    from tornado_gcm.neural.standard_layers import Mlp
+    from tornado_gcm.neural.towers import ForwardTower
+    from tornado_gcm.precision.policy import PrecisionPolicy
+
+    if args.resolution != "2.8deg":
+        raise SystemExit("reference arm implemented for the 2.8deg configuration")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    torch.manual_seed(0)
+    # physical constants in the reference's non-dimensional units (pint is not installed)
+    L0, T0 = 6.37122e6, 1.0 / (2 * 7.292e-5)
+    nd = lambda si, e_len, e_time: si * (T0 ** (-e_time)) / (L0 ** e_len)
+    R = nd(1004.0 * 2 / 7, 2, -2)
+    specs = SimpleNamespace(R=R, R_vapor=nd(461.0, 2, -2), g=nd(9.80616, 1, -2), Cp=R / (2 / 7),
+                            Cp_vapor=nd(1859.0, 2, -2), kappa=2 / 7, angular_velocity=7.292e-5 * T0, radius=1.0)
+    grid = spherical_harmonic.Grid.TL63()
+    vertical = sigma_coordinates.SigmaCoordinates.equidistant(32)
+    coords = coordinate_systems.CoordinateSystem(grid, vertical)
+    n = 32
+    t_ref = np.maximum(200.0, 288.0 * vertical.centers ** 0.19)
+    dt = 20 * 60 / T0
+    cfg = ModelConfig(coords=coords, dt=dt, inner_steps=18, dycore_substeps=1, physics_specs=specs,
+                      reference_temperature=t_ref, orography=torch.zeros(grid.modal_shape),
+                      precision_policy=PrecisionPolicy(), filter_attenuation=dt / (120 * 60 / T0), filter_order=3,
+                      filter_cutoff=0.0, stability_filter_attenuation=dt / (4 * 60 / T0),
+                      stability_filter_order=10, stability_filter_cutoff=0.4, humidity_key="specific_humidity",
+                      cloud_keys=("specific_cloud_ice_water_content", "specific_cloud_liquid_water_content"))
+    tower = ForwardTower(Mlp.uniform(3 * n + 1 + 4, 3 * n + 1, hidden_size=384, hidden_layers=5,
+                                     activation=F.gelu))
+    param = ModalNeuralDivCurlParameterization(grid, tower, n)
+    model = NeuralGCMModel(cfg, parameterization=param, conservation_fixer=LiteConservationFixer()).to(dev)
+    encoder = ForwardTower(Mlp.uniform(7 * 37 + 4, 6 * n + 1, hidden_size=256, hidden_layers=3,
+                                       activation=F.gelu)).to(dev)
+    decoder = ForwardTower(Mlp.uniform(6 * n + 1, 7 * 37, hidden_size=256, hidden_layers=3,
+                                       activation=F.gelu)).to(dev)
+    params = list(model.parameters()) + list(encoder.parameters()) + list(decoder.parameters())
+    with torch.no_grad():
+        for m in (tower, encoder, decoder):
+            m.neural_net.layers[-1].weight.mul_(0.01)
+    opt = torch.optim.AdamW(params, lr=1e-4, betas=(0.9, 0.95), eps=1e-6)
+    ema = [p.detach().clone() for p in params]
+    B, K = args.batch, args.rollout
+    I, J = grid.nodal_shape
+    g = torch.Generator(device="cpu").manual_seed(rank)
+    mk = lambda *s: torch.randn(*s, generator=g)
+    pool = [(mk(B, 7 * 37, I, J).pin_memory(), mk(B, K, 7 * 37, I, J).pin_memory()) for _ in range(2)]
+    forc = mk(4, I, J).to(dev)
+    t_ref_t = torch.tensor(t_ref, dtype=torch.float32, device=dev).reshape(-1, 1, 1)
+    tr_keys = ("specific_humidity", "specific_cloud_liquid_water_content", "specific_cloud_ice_water_content")
+
+    def encode(x):  # x: (7*37, I, J) → reference State
+        h = encoder(torch.cat([x, forc], 0))
+        u, v, T = h[:n] * 1e-3, h[n:2 * n] * 1e-3, h[2 * n:3 * n] + t_ref_t
+        trs = [h[3 * n + i * n:3 * n + (i + 1) * n] * 1e-6 for i in range(3)]
+        lnps = h[6 * n:] * 1e-3
+        vort, div = spherical_harmonic.uv_nodal_to_vor_div_modal(grid, u, v)
+        temp = grid.to_modal(T - t_ref_t)
+        from tornado_gcm.core.primitive_equations import State
+
+        return State(vort, div, temp, grid.to_modal(lnps),
+                     {k: grid.to_modal(t) for k, t in zip(tr_keys, trs)}, sim_time=0.0)
+
+    def decode(s):
+        u, v = spherical_harmonic.vor_div_to_uv_nodal(grid, s.vorticity, s.divergence)
+        parts = [u * 1e3, v * 1e3, grid.to_nodal(s.temperature_variation)]
+        parts += [grid.to_nodal(s.tracers[k]) * 1e6 for k in tr_keys] + [grid.to_nodal(s.log_surface_pressure)]
+        return decoder(torch.cat(parts, 0))
+
+    def step_fn(i):
+        xh, th = pool[i % 2]
+        x = xh.to(dev, non_blocking=True)
+        tgt = th.to(dev, non_blocking=True)
+        opt.zero_grad(set_to_none=True)
+        for b in range(B):
+            state = encode(x[b])
+            loss = 0.0
+            for k in range(K):
+                for _ in range(cfg.inner_steps):
+                    state = model.step(state, forcings={"f": forc})
+                loss = loss + ((decode(state) - tgt[b, k]) ** 2).mean()
+            (loss / (K * B)).backward()
+        if world > 1:
+            import torch.distributed as dist
+
+            flat = torch.cat([p.grad.reshape(-1) for p in params if p.grad is not None])
+            dist.all_reduce(flat)
+            flat /= world
+            off = 0
+            for p in params:
+                if p.grad is not None:
+                    nn_ = p.grad.numel()
+                    p.grad.copy_(flat[off:off + nn_].view_as(p.grad))
+                    off += nn_
+        torch.nn.utils.clip_grad_norm_(params, 1.0)
+        opt.step()
+        with torch.no_grad():
+            for e, p in zip(ema, params):
+                e.lerp_(p, 2.0 / 2000)
+
+    for i in range(args.warmup):
+        step_fn(i)
+    sampler = ClockSampler(device_uuid()) if rank == 0 else None
+    ms, clocks = timed_region(step_fn, args.steps, world, sampler)
+    ms_per_step = ms / args.steps
+    value = world * B * K / (ms_per_step / 1000.0)
+    if rank == 0:
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": value,
+            "unit": "6h model-steps/s (samples x 6-h steps, all GPUs)", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": value / PUBLISHED_STEPS_PER_S, "dtype": "fp32 (reference default path: FP64 SHT at TL63)",
+            "data": "synthetic, random-init weights",
+            "config": {"model": "2.8deg TL63 L32 (reference NeuralGCMModel + ModalNeuralDivCurlParameterization "
+                                "tower 5x384, encoder/decoder 3x256 built from reference modules)",
+                       "global_batch": world * B, "seq_len": K, "parallelism": f"dp{world}",
+                       "batching": "per-sample loop (reference modules are single-sample)",
+                       "l2": "working set far exceeds L2"},
+            "clocks": clocks, "e2e": {"value": value, "unit": "same loop includes H2D of inputs each step",
+                                       "h2d_bytes_per_step": int(pool[0][0].numel() * 4 + pool[0][1].numel() * 4),
+                                       "d2h_bytes_per_step": 0},
+            "gpu_launches": 0,
+        }), flush=True)
+
+
+def main():
+    args = parse_args()
+    rank, world, local = dist_setup(args.gpus)
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+        else:
+            run_b200(args, rank, world)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,181 @@
+"""sm_100a kernels against fp32/fp64 torch references of the same ops (needs a B200)."""
+
+import numpy as np
+import pytest
+import torch
+
+from tornado_gcm_b200.ops import _ext
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not torch.cuda.is_available(), reason="needs CUDA")]
+
+DEV = "cuda"
+
+
+def _require():
+    _ext.require("GPU tests")
+
+
+def _grid(name, precision="tf32"):
+    from tornado_gcm_b200.core import spherical_harmonic as sh
+
+    return getattr(sh.Grid, name)(precision=precision)
+
+
+def _modal(grid, S, seed=0):
+    rng = np.random.default_rng(seed)
+    m, l = grid.modal_mesh
+    amp = np.where(grid.mask, (1.0 + l) ** -1.5, 0.0)
+    return torch.tensor(rng.standard_normal((S,) + grid.modal_shape) * amp)
+
+
+def _rel(a, b):
+    return float((a.double() - b.double()).norm() / (b.double().norm() + 1e-30))
+
+
+def _eq(name="T21", n=8):
+    from tornado_gcm_b200.core import coordinate_systems as cs, primitive_equations as pe
+    from tornado_gcm_b200.core import sigma_coordinates as sc
+    from tornado_gcm_b200.utils.units import SimUnits
+
+    g = _grid(name, "float32")
+    coords = cs.CoordinateSystem(g, sc.SigmaCoordinates.equidistant(n))
+    return pe.PrimitiveEquationsSigma(np.linspace(210, 290, n), torch.zeros(g.modal_shape), coords,
+                                      SimUnits.from_si(), humidity_key="specific_humidity",
+                                      cloud_keys=("specific_cloud_ice_water_content",
+                                                  "specific_cloud_liquid_water_content"))
+
+
+def test_column_kernel_gpu_matches_cpu_twin():
+    _require()
+    from tornado_gcm_b200.ops import dycore as dyops
+
+    eq = _eq("TL63", 32)
+    keys = ("specific_cloud_ice_water_content", "specific_cloud_liquid_water_content", "specific_humidity")
+    spec = dyops.ColumnSpec.from_equation(eq, keys)
+    B = 2
+    I, J = eq.grid.nodal_shape
+    torch.manual_seed(0)
+    nin = torch.randn(B * spec.n_in, I, J) * 0.01
+    out_cpu = dyops.column_forward_raw(spec, nin, B)
+    out_gpu = dyops.column_forward_raw(spec, nin.to(DEV), B).cpu()
+    torch.testing.assert_close(out_gpu, out_cpu, rtol=1e-4, atol=1e-6)
+    gout = torch.randn_like(out_cpu)
+    g_cpu = dyops.column_vjp_raw(spec, nin, gout, B)
+    g_gpu = dyops.column_vjp_raw(spec, nin.to(DEV), gout.to(DEV), B).cpu()
+    torch.testing.assert_close(g_gpu, g_cpu, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2, 3])
+def test_implicit_kernel_gpu_matches_cpu(mode):
+    _require()
+    from tornado_gcm_b200.ops import dycore as dyops
+
+    eq = _eq("TL63", 32)
+    M2, L = eq.grid.modal_shape
+    torch.manual_seed(1)
+    d, t, p = torch.randn(3, 32, M2, L), torch.randn(3, 32, M2, L), torch.randn(3, 1, M2, L)
+    cpu = dyops.implicit_apply(eq, d, t, p, 0.05, mode)
+    gpu = dyops.implicit_apply(eq, d.to(DEV), t.to(DEV), p.to(DEV), 0.05, mode)
+    for a, b in zip(gpu, cpu):
+        torch.testing.assert_close(a.cpu(), b, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("name,S", [("T21", 5), ("TL63", 70), ("TL127", 9)])
+def test_sht_roundtrip_vs_fp64(name, S):
+    _require()
+    g = _grid(name)
+    g64 = g.with_precision("highest")
+    x = _modal(g, S)
+    nod_ref = g64.to_nodal(x)  # CPU fp64 oracle
+    nod = g.to_nodal(x.float().to(DEV))
+    assert _rel(nod.cpu(), nod_ref) < 3e-3
+    mod_ref = g64.to_modal(nod_ref)
+    mod = g.to_modal(nod_ref.float().to(DEV))
+    assert _rel(mod.cpu(), mod_ref) < 3e-3
+    assert _ext.check_error_flag(torch.device(DEV)) == 0
+
+
+def test_sht_adjoints():
+    _require()
+    g = _grid("TL63")
+    x = _modal(g, 6).float().to(DEV).requires_grad_(True)
+    y = torch.randn(6, *g.nodal_shape, device=DEV)
+    (g.to_nodal(x) * y).sum().backward()
+    # <synth x, y> = <x, synth^T y>: compare with fp64 CPU autograd
+    x64 = x.detach().cpu().double().requires_grad_(True)
+    (g.with_precision("highest").to_nodal(x64) * y.cpu().double()).sum().backward()
+    assert _rel(x.grad.cpu(), x64.grad) < 3e-3
+    n = torch.randn(6, *g.nodal_shape, device=DEV, requires_grad=True)
+    ym = torch.randn(6, *g.modal_shape, device=DEV)
+    (g.to_modal(n) * ym).sum().backward()
+    n64 = n.detach().cpu().double().requires_grad_(True)
+    (g.with_precision("highest").to_modal(n64) * ym.cpu().double()).sum().backward()
+    assert _rel(n.grad.cpu(), n64.grad) < 3e-3
+
+
+@pytest.mark.parametrize("T,K,O,act", [(300, 200, 72, "gelu_tanh"), (4096, 197, 384, "relu"), (1000, 384, 193, "none")])
+def test_linear_kernels_vs_fp32(T, K, O, act):
+    _require()
+    from tornado_gcm_b200.neural.standard_layers import apply_activation
+    from tornado_gcm_b200.ops import linear as lops
+
+    torch.manual_seed(2)
+    l1 = torch.nn.Linear(K, O).to(DEV)
+    l2 = torch.nn.Linear(O, 40).to(DEV)
+    x = torch.randn(T, K, device=DEV, requires_grad=True)
+    y = lops.mlp_forward(x, [l1, l2], [act, "none"])
+    xr = x.detach().clone().requires_grad_(True)
+    bf = lambda t: t.to(torch.bfloat16).float()
+    h = apply_activation(act, bf(xr) @ bf(l1.weight).t() + l1.bias)
+    yr = bf(h) @ bf(l2.weight).t() + l2.bias
+    assert _rel(y.detach(), yr.detach()) < 2e-2
+    gy = torch.randn_like(y)
+    grads = torch.autograd.grad(y, [x, l1.weight, l1.bias, l2.weight], gy)
+    grads_r = torch.autograd.grad(yr, [xr, l1.weight, l1.bias, l2.weight], gy)
+    for a, b in zip(grads, grads_r):
+        assert _rel(a, b) < 3e-2
+
+
+def test_fused_sil3_gpu_matches_cpu():
+    _require()
+    from tornado_gcm_b200.core import filtering, primitive_equations as pe
+    from tornado_gcm_b200.ops import dycore as dyops
+
+    eq = _eq("TL63", 32)
+    g = eq.grid
+    rng = np.random.default_rng(4)
+    m, l = g.modal_mesh
+    amp = np.where(g.mask, (1.0 + l) ** -1.5, 0.0)
+    mk = lambda lv, s: torch.tensor(rng.standard_normal((2, lv) + g.modal_shape) * amp * s, dtype=torch.float32)
+    keys = ("specific_cloud_ice_water_content", "specific_cloud_liquid_water_content", "specific_humidity")
+    st = pe.State(mk(32, 1e-1), mk(32, 1e-2), mk(32, 1.0), mk(1, 1e-2), {k: mk(32, 1e-4) for k in keys}, 0.0)
+    phys = st.tree_map(lambda x: 1e-4 * torch.randn_like(x))
+    f = filtering.exponential_filter(g, 0.1, 3, 0.0)
+    stepper = dyops.FusedSIL3(eq, 0.1, f.scaling)
+    out_cpu = stepper.step(st, phys)
+    to = lambda s: s.tree_map(lambda x: x.to(DEV))
+    out_gpu = stepper.step(to(st), to(phys))
+    for a, b in zip(out_gpu.tensors(), out_cpu.tensors()):
+        assert _rel(a.cpu(), b) < 1e-2
+    assert _ext.check_error_flag(torch.device(DEV)) == 0
+
+
+def test_model_train_step_finite():
+    _require()
+    from tornado_gcm_b200.models.builders import build_hybrid_gcm
+    from tornado_gcm_b200.training.trainer import GCMTrainer
+
+    dev = torch.device(DEV)
+    gcm, data = build_hybrid_gcm("2.8deg", dev)
+    gcm.physics_steps_per_output = 2
+    enc = gcm.encoder
+    norm = lambda d: {k: ((v.to(dev) - getattr(enc, f"mean_{k}")) / getattr(enc, f"std_{k}")) for k, v in d.items()}
+    tr = GCMTrainer(gcm, graph=False)
+    x0 = norm(data.sample(2, 0))
+    tg = [norm(data.sample(2, 1)), norm(data.sample(2, 2))]
+    forc = {k: v.to(dev) for k, v in data.forcings(2).items()}
+    l1 = tr.train_step(x0, tg, forc)
+    l2 = tr.train_step(x0, tg, forc)
+    assert torch.isfinite(l1) and torch.isfinite(l2)
+    assert _ext.check_error_flag(dev) == 0

@@ -138,7 +138,7 @@ class NodalColumnParameterization(nn.Module):
     """
 
     def __init__(self, grid: Grid, n_levels: int, tracer_keys: Sequence[str], neural_net: nn.Module,
-                 forcing_keys: Sequence[str] = (), output_scale: float = 1.0,
+                 forcing_keys: Sequence[str] = (), output_scale=1.0, input_scale=None,
                  filter_fn: Optional[Callable[[torch.Tensor], torch.Tensor]] = None,
                  compute_dtype: torch.dtype = torch.bfloat16):
         super().__init__()
@@ -147,9 +147,14 @@ class NodalColumnParameterization(nn.Module):
         self.tracer_keys = tuple(tracer_keys)
         self.forcing_keys = tuple(forcing_keys)
         self.tower = neural_net
-        self.output_scale = output_scale
         self.filter_fn = filter_fn
         self.compute_dtype = compute_dtype
+        osc = torch.as_tensor(output_scale, dtype=torch.float32).reshape(-1)
+        if osc.numel() == 1:
+            osc = osc.expand(self.n_outputs).clone()
+        self.register_buffer("output_scale", osc.reshape(-1, 1, 1))
+        isc = torch.ones(self.n_inputs) if input_scale is None else torch.as_tensor(input_scale, dtype=torch.float32)
+        self.register_buffer("input_scale", isc.reshape(-1, 1, 1))
 
     @property
     def n_inputs(self) -> int:
@@ -181,7 +186,7 @@ class NodalColumnParameterization(nn.Module):
             x = torch.cat([x] + extra, dim=-3)
         elif self.forcing_keys:
             x = torch.cat([x, x.new_zeros(*lead, len(self.forcing_keys), *x.shape[-2:])], dim=-3)
-        y = self.tower(x.to(self.compute_dtype)).to(state.vorticity.dtype) * self.output_scale
+        y = self.tower((x * self.input_scale).to(self.compute_dtype)).to(state.vorticity.dtype) * self.output_scale
         return self.nodal_tendency_to_modal(y, state)
 
     def nodal_tendency_to_modal(self, y: torch.Tensor, state: State) -> State:

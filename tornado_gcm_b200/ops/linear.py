@@ -1,0 +1,151 @@
+"""Column MLPs on sm_100a: BF16 tcgen05 GEMMs with fused epilogues.
+
+Forward per layer: ``H = act(X Wᵀ + b)`` in one GEMM (bias, activation and
+the saved pre-activation written by the epilogue).  Backward per layer:
+weight gradient ``dW += dYᵀ X`` (split-K, fp32 atomics), bias gradient as a
+column sum, and data gradient ``dX = dY W`` with the previous layer's
+activation derivative fused into the epilogue.  Master weights stay fp32;
+BF16 copies are refreshed when a parameter's version changes.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from tornado_gcm_b200.ops import _ext
+
+ACT_CODES = {"none": 0, "relu": 1, "gelu": 2, "gelu_tanh": 3, "silu": 4, "tanh": 5}
+
+
+def _pad8(n: int) -> int:
+    return (n + 7) // 8 * 8
+
+
+def supports(x: torch.Tensor, layers) -> bool:
+    if not x.is_cuda or not _ext.available():
+        return False
+    for lyr in layers:
+        if not isinstance(lyr, nn.Linear) or lyr.weight.dtype not in (torch.float32, torch.bfloat16):
+            return False
+    return True
+
+
+class _WeightCache:
+    """Persistent BF16 zero-padded copies of Linear weights.
+
+    A copy is refreshed on the first use after :func:`begin_step` (the
+    trainer calls it once per optimizer step, also inside CUDA-graph
+    capture so the refresh is part of the replayed graph) or when the
+    master weight's version counter changed.
+    """
+
+    def __init__(self):
+        self.store = {}
+        self.token = 0
+
+    def get(self, lin: nn.Linear):
+        w = lin.weight
+        key = id(lin)
+        ver = (w._version, w.data_ptr(), str(w.device))
+        ent = self.store.get(key)
+        if ent is not None and ent[0] == ver and ent[1] == self.token:
+            return ent[2]
+        if ent is None or ent[2].device != w.device:
+            O, K = w.shape
+            buf = torch.zeros(_pad8(O), _pad8(K), dtype=torch.bfloat16, device=w.device)
+        else:
+            buf = ent[2]
+        buf[: w.shape[0], : w.shape[1]].copy_(w.detach())
+        self.store[key] = (ver, self.token, buf)
+        return buf
+
+
+_CACHE = _WeightCache()
+
+
+def begin_step() -> None:
+    """Mark a new optimizer step: BF16 weight copies refresh on next use."""
+    _CACHE.token += 1
+
+
+class MlpFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x2d, acts, layers, *params):
+        ops = _ext.require("column MLP")
+        err = _ext.error_flag(x2d.device)
+        T, K0 = x2d.shape
+        h = torch.zeros(T, _pad8(K0), dtype=torch.bfloat16, device=x2d.device)
+        h[:, :K0] = x2d
+        hs, zs, ws = [h], [], []
+        n = len(layers)
+        for i, lin in enumerate(layers):
+            wp = _CACHE.get(lin)
+            ws.append(wp)
+            Op = wp.shape[0]
+            bias = None
+            if lin.bias is not None:
+                bias = torch.zeros(Op, dtype=torch.float32, device=x2d.device)
+                bias[: lin.bias.shape[0]] = lin.bias.detach().float()
+            last = i == n - 1
+            out = torch.empty(T, Op, dtype=torch.float32 if last else torch.bfloat16, device=x2d.device)
+            code = ACT_CODES[acts[i]]
+            aux = torch.empty(T, Op, dtype=torch.bfloat16, device=x2d.device) if (code and not last) else None
+            ops.linear_fwd(hs[-1], wp, bias, code, out, aux, err)
+            zs.append(aux)
+            hs.append(out)
+        ctx.acts, ctx.layers, ctx.K0, ctx.x_dtype = acts, layers, K0, x2d.dtype
+        ctx.save_for_backward(*(hs[:-1] + [z if z is not None else torch.empty(0) for z in zs] + ws))
+        ctx.n = n
+        O_last = layers[-1].weight.shape[0]
+        return hs[-1][:, :O_last]
+
+    @staticmethod
+    def backward(ctx, g):
+        ops = _ext.require("column MLP backward")
+        n = ctx.n
+        saved = ctx.saved_tensors
+        hs, zs, ws = saved[:n], saved[n:2 * n], saved[2 * n:]
+        err = _ext.error_flag(g.device)
+        T = g.shape[0]
+        O_last = ctx.layers[-1].weight.shape[0]
+        dy = torch.zeros(T, ws[-1].shape[0], dtype=torch.bfloat16, device=g.device)
+        dy[:, :O_last] = g
+        grads = []
+        dx_out = None
+        for i in range(n - 1, -1, -1):
+            lin = ctx.layers[i]
+            wp = ws[i]
+            dw = torch.zeros(wp.shape, dtype=torch.float32, device=g.device)
+            ops.linear_wgrad(dy, hs[i], dw, 0, err)
+            O, K = lin.weight.shape
+            gb = dy[:, :O].float().sum(0) if lin.bias is not None else None
+            grads.append((dw[:O, :K].to(lin.weight.dtype), gb))
+            if i > 0:
+                prev = zs[i - 1]
+                code = ACT_CODES[ctx.acts[i - 1]]
+                dprev = torch.empty(T, wp.shape[1], dtype=torch.bfloat16, device=g.device)
+                ops.linear_dgrad(dy, wp, dprev, prev if prev.numel() else None, code, err)
+                dy = dprev
+            else:
+                dx = torch.empty(T, wp.shape[1], dtype=torch.float32, device=g.device)
+                ops.linear_dgrad(dy, wp, dx, None, 0, err)
+                dx_out = dx[:, : ctx.K0].to(ctx.x_dtype)
+        grads.reverse()
+        flat = []
+        for lin, (gw, gb) in zip(ctx.layers, grads):
+            flat.append(gw)
+            if lin.bias is not None:
+                flat.append(gb)
+        return (dx_out, None, None) + tuple(flat)
+
+
+def mlp_forward(x: torch.Tensor, layers, acts) -> torch.Tensor:
+    lead = x.shape[:-1]
+    params = []
+    for lin in layers:
+        params.append(lin.weight)
+        if lin.bias is not None:
+            params.append(lin.bias)
+    out = MlpFn.apply(x.reshape(-1, x.shape[-1]), tuple(acts), tuple(layers), *params)
+    return out.reshape(*lead, out.shape[-1])
