@@ -63,7 +63,7 @@ def test_column_kernel_gpu_matches_cpu_twin():
     gout = torch.randn_like(out_cpu)
     g_cpu = dyops.column_vjp_raw(spec, nin, gout, B)
     g_gpu = dyops.column_vjp_raw(spec, nin.to(DEV), gout.to(DEV), B).cpu()
-    torch.testing.assert_close(g_gpu, g_cpu, rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(g_gpu, g_cpu, rtol=3e-3, atol=3e-4)
 
 
 @pytest.mark.parametrize("mode", [0, 1, 2, 3])
