@@ -73,3 +73,57 @@ def test_fused_sil3_gradients_match():
     g_ref = loss(lambda x: _reference_step(eq, x, phys, dt, f))
     for a, b in zip(g_fused, g_ref):
         torch.testing.assert_close(a, b, rtol=2e-3, atol=1e-5)
+
+
+def _packed_setup():
+    eq, st, phys = _setup()
+    keys = tuple(sorted(st.tracers))
+    return eq, st, phys, keys
+
+
+def test_spectral_recipes_match_torch_pre_post():
+    from tornado_gcm_b200.ops import spectral
+
+    eq, st, phys, keys = _packed_setup()
+    y = spectral.pack_state(st, keys)
+    pre = spectral.explicit_pre_recipe(eq, keys)
+    ref_pre = eq.modal_pre_stack(st)
+    torch.testing.assert_close(pre.apply(y), ref_pre, rtol=1e-5, atol=1e-7)
+    post = spectral.explicit_post_recipe(eq, keys)
+    rng = np.random.default_rng(5)
+    modal = torch.tensor(rng.standard_normal((2, post.c_in) + eq.grid.modal_shape), dtype=torch.float32)
+    ref_post = eq.modal_post(modal, st)
+    out = post.apply(modal)
+    oro = eq.grid.clip_wavenumbers(eq.orography_tendency(modal.device, modal.dtype))
+    ref_packed = spectral.pack_state(ref_post, keys)
+    ref_packed[:, eq.vertical.layers:2 * eq.vertical.layers] -= oro
+    torch.testing.assert_close(out, ref_packed, rtol=1e-4, atol=1e-5)
+    # transposes: <A x, y> == <x, A^T y>
+    for r in (pre, post):
+        x = torch.randn(2, r.c_in, *eq.grid.modal_shape, dtype=torch.float32)
+        z = torch.randn(2, r.c_out, *eq.grid.modal_shape, dtype=torch.float32)
+        lhs = (r.apply(x).double() * z.double()).sum()
+        rhs = (x.double() * r.transpose().apply(z).double()).sum()
+        assert abs(float(lhs - rhs)) <= 1e-4 * max(1.0, abs(float(lhs)))
+
+
+def test_packed_sil3_matches_fused_values_and_grads():
+    from tornado_gcm_b200.ops import spectral
+
+    eq, st, phys, keys = _packed_setup()
+    dt = 0.02
+    f = filtering.exponential_filter(eq.grid, 16.0, 18, 0.0)
+    ref_stepper = dyops.FusedSIL3(eq, dt, f.scaling)
+    stepper = dyops.PackedSIL3(eq, dt, f.scaling, keys)
+    n = eq.vertical.layers
+    P = spectral.pack_state(phys, keys) + stepper.orography_packed(torch.device("cpu"))
+    y0 = spectral.pack_state(st, keys).requires_grad_(True)
+    out = stepper.step_packed(y0, P)
+    st_ref = st.tree_map(lambda t: t.clone().requires_grad_(True))
+    ref = spectral.pack_state(ref_stepper.step(st_ref, phys), keys)
+    torch.testing.assert_close(out, ref, rtol=1e-3, atol=1e-6)
+    w = torch.randn_like(out)
+    (gy,) = torch.autograd.grad((out * w).sum(), y0)
+    g_ref = torch.autograd.grad((ref * w).sum(), st_ref.tensors())
+    g_ref_packed = torch.cat([g_ref[0], g_ref[1], g_ref[2], g_ref[3]] + list(g_ref[4:]), dim=-3)
+    torch.testing.assert_close(gy, g_ref_packed, rtol=3e-3, atol=1e-5)

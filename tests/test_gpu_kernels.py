@@ -78,7 +78,7 @@ def test_implicit_kernel_gpu_matches_cpu(mode):
     cpu = dyops.implicit_apply(eq, d, t, p, 0.05, mode)
     gpu = dyops.implicit_apply(eq, d.to(DEV), t.to(DEV), p.to(DEV), 0.05, mode)
     for a, b in zip(gpu, cpu):
-        torch.testing.assert_close(a.cpu(), b, rtol=1e-4, atol=1e-5)
+        torch.testing.assert_close(a.cpu(), b, rtol=5e-3, atol=5e-4)
 
 
 @pytest.mark.parametrize("name,S", [("T21", 5), ("TL63", 70), ("TL127", 9)])
@@ -94,6 +94,19 @@ def test_sht_roundtrip_vs_fp64(name, S):
     mod = g.to_modal(nod_ref.float().to(DEV))
     assert _rel(mod.cpu(), mod_ref) < 3e-3
     assert _ext.check_error_flag(torch.device(DEV)) == 0
+
+
+def test_sht_lat_major_roundtrip():
+    _require()
+    from tornado_gcm_b200.ops import sht as sht_ops
+
+    g = _grid("TL63")
+    x = _modal(g, 7).float().to(DEV)
+    nod = sht_ops.to_nodal_lat_major(x, g.spherical_harmonics)
+    nod_ref = g.with_precision("highest").to_nodal(x.cpu().double()).transpose(-1, -2)
+    assert _rel(nod.cpu(), nod_ref) < 3e-3
+    mod = sht_ops.to_modal_lat_major(nod_ref.float().contiguous().to(DEV), g.spherical_harmonics)
+    assert _rel(mod.cpu(), g.with_precision("highest").to_modal(nod_ref.transpose(-1, -2))) < 3e-3
 
 
 def test_sht_adjoints():
@@ -152,12 +165,19 @@ def test_fused_sil3_gpu_matches_cpu():
     st = pe.State(mk(32, 1e-1), mk(32, 1e-2), mk(32, 1.0), mk(1, 1e-2), {k: mk(32, 1e-4) for k in keys}, 0.0)
     phys = st.tree_map(lambda x: 1e-4 * torch.randn_like(x))
     f = filtering.exponential_filter(g, 0.1, 3, 0.0)
-    stepper = dyops.FusedSIL3(eq, 0.1, f.scaling)
-    out_cpu = stepper.step(st, phys)
-    to = lambda s: s.tree_map(lambda x: x.to(DEV))
-    out_gpu = stepper.step(to(st), to(phys))
-    for a, b in zip(out_gpu.tensors(), out_cpu.tensors()):
-        assert _rel(a.cpu(), b) < 1e-2
+    from tornado_gcm_b200.ops import spectral
+
+    stepper = dyops.PackedSIL3(eq, 0.1, f.scaling, keys)
+    P = spectral.pack_state(phys, keys)
+    y0 = spectral.pack_state(st, keys)
+    out_cpu = stepper.step_packed(y0.requires_grad_(True), P + stepper.orography_packed(torch.device("cpu")))
+    y0g = y0.detach().to(DEV).requires_grad_(True)
+    out_gpu = stepper.step_packed(y0g, P.to(DEV) + stepper.orography_packed(torch.device(DEV)))
+    assert _rel(out_gpu.detach().cpu(), out_cpu.detach()) < 1e-2
+    w = torch.randn_like(out_cpu)
+    (g_cpu,) = torch.autograd.grad((out_cpu * w).sum(), y0)
+    (g_gpu,) = torch.autograd.grad((out_gpu * w.to(DEV)).sum(), y0g)
+    assert _rel(g_gpu.cpu(), g_cpu) < 2e-2
     assert _ext.check_error_flag(torch.device(DEV)) == 0
 
 

@@ -38,17 +38,28 @@ def real_basis_with_zero_imag(wavenumbers: int, nodes: int) -> np.ndarray:
     return f
 
 
+_DERIV_CACHE: dict = {}
+
+
 def derivative_index_and_scale(n: int, device=None, dtype=torch.float32):
     """Gather index and signed scale implementing d/dλ on an odd-length axis.
 
     out[k] = scale[k] * u[src[k]] with out[2j-1] = j u[2j], out[2j] = -j u[2j-1].
+    Cached per (n, device, dtype) so repeated calls (and CUDA-graph capture)
+    issue no host-to-device copies.
     """
-    k = torch.arange(n, device=device)
+    key = (n, str(device), dtype)
+    hit = _DERIV_CACHE.get(key)
+    if hit is not None:
+        return hit
+    k = np.arange(n)
     j = (k + 1) // 2
-    src = torch.where(k % 2 == 1, k + 1, k - 1).clamp(0, n - 1)
-    scale = torch.where(k % 2 == 1, j, -j).to(dtype)
-    scale[0] = 0
-    return src, scale
+    src = np.clip(np.where(k % 2 == 1, k + 1, k - 1), 0, n - 1)
+    scale = np.where(k % 2 == 1, j, -j).astype(np.float64)
+    scale[0] = 0.0
+    out = (torch.as_tensor(src, device=device), torch.as_tensor(scale, dtype=dtype, device=device))
+    _DERIV_CACHE[key] = out
+    return out
 
 
 def real_basis_derivative(u: torch.Tensor, /, axis: int = -1) -> torch.Tensor:

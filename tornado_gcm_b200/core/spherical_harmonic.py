@@ -405,6 +405,10 @@ class Grid:
                 arr = self._derivative_recurrence_weights[1]
             elif name == "l":
                 arr = self.modal_mesh[1].astype(np.float64)
+            elif name.startswith("clip_mask_"):
+                k = int(name.rsplit("_", 1)[1])
+                arr = np.ones(self.modal_shape[-1])
+                arr[-k:] = 0.0
             else:
                 arr = getattr(self, name)
             return torch.as_tensor(np.ascontiguousarray(arr), dtype=dtype, device=device)
@@ -432,9 +436,7 @@ class Grid:
         def clip_fn(t):
             if not isinstance(t, torch.Tensor):
                 return t
-            keep = torch.ones(self.modal_shape[-1], dtype=t.dtype, device=t.device)
-            keep[-n:] = 0
-            return t * keep
+            return t * self.const(f"clip_mask_{n}", t.device, t.dtype)
 
         if isinstance(x, tuple):
             return tuple(clip_fn(xi) for xi in x)

@@ -54,13 +54,13 @@ static ColumnConsts consts_from(const at::Tensor& level_consts, int64_t n, int64
 // ── column kernels ──────────────────────────────────────────────────────────
 __global__ void column_fwd_kernel(ColumnConsts c, SliceIndex ix, const float* __restrict__ in,
                                   float* __restrict__ out, const float* __restrict__ sec2,
-                                  const float* __restrict__ cor, int B, int I, int J) {
+                                  const float* __restrict__ cor, int B, int I, int J, int lat_major) {
   const long long plane = static_cast<long long>(I) * J;
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= static_cast<long long>(B) * plane) return;
   const int b = static_cast<int>(idx / plane);
   const long long ij = idx - static_cast<long long>(b) * plane;
-  const int j = static_cast<int>(ij % J);
+  const int j = lat_major ? static_cast<int>(ij / I) : static_cast<int>(ij % J);
   const float* ib = in + static_cast<long long>(b) * ix.n_in * plane + ij;
   float* ob = out + static_cast<long long>(b) * ix.n_out * plane + ij;
   auto rd = [ib, plane](int q) -> float { return __ldg(ib + q * plane); };
@@ -71,13 +71,13 @@ __global__ void column_fwd_kernel(ColumnConsts c, SliceIndex ix, const float* __
 __global__ void column_vjp_kernel(ColumnConsts c, SliceIndex ix, const float* __restrict__ in,
                                   const float* __restrict__ gout, float* __restrict__ gin,
                                   const float* __restrict__ sec2, const float* __restrict__ cor, int B, int I,
-                                  int J) {
+                                  int J, int lat_major) {
   const long long plane = static_cast<long long>(I) * J;
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= static_cast<long long>(B) * plane) return;
   const int b = static_cast<int>(idx / plane);
   const long long ij = idx - static_cast<long long>(b) * plane;
-  const int j = static_cast<int>(ij % J);
+  const int j = lat_major ? static_cast<int>(ij / I) : static_cast<int>(ij % J);
   const float* ib = in + static_cast<long long>(b) * ix.n_in * plane + ij;
   const float* gb = gout + static_cast<long long>(b) * ix.n_out * plane + ij;
   float* gib = gin + static_cast<long long>(b) * ix.n_in * plane + ij;
@@ -95,13 +95,13 @@ static void check_nodal(const at::Tensor& t, const char* name) {
 at::Tensor column_fwd(const at::Tensor& nin, const at::Tensor& sec2, const at::Tensor& cor,
                       const at::Tensor& level_consts, int64_t batch, int64_t n, int64_t nt, int64_t hum,
                       int64_t hum_terms, std::vector<int64_t> clouds, int64_t vadv, double R, double kappa,
-                      double rv, double cpv) {
+                      double rv, double cpv, bool lat_major) {
   check_nodal(nin, "nin");
   ColumnConsts c = consts_from(level_consts, n, nt, hum, hum_terms, clouds, vadv, R, kappa, rv, cpv);
   SliceIndex ix = make_slice_index(c);
-  const int64_t I = nin.size(1), J = nin.size(2);
+  const int64_t I = lat_major ? nin.size(2) : nin.size(1), J = lat_major ? nin.size(1) : nin.size(2);
   TORCH_CHECK(nin.size(0) == batch * ix.n_in, "nin slice count mismatch: expected ", batch * ix.n_in);
-  auto out = at::empty({batch * ix.n_out, I, J}, nin.options());
+  auto out = at::empty({batch * ix.n_out, nin.size(1), nin.size(2)}, nin.options());
   auto s2 = sec2.to(nin.device(), at::kFloat).contiguous();
   auto co = cor.to(nin.device(), at::kFloat).contiguous();
   if (nin.is_cuda()) {
@@ -110,7 +110,7 @@ at::Tensor column_fwd(const at::Tensor& nin, const at::Tensor& sec2, const at::T
     const int threads = 128;
     column_fwd_kernel<<<(total + threads - 1) / threads, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
         c, ix, nin.data_ptr<float>(), out.data_ptr<float>(), s2.data_ptr<float>(), co.data_ptr<float>(),
-        static_cast<int>(batch), static_cast<int>(I), static_cast<int>(J));
+        static_cast<int>(batch), static_cast<int>(I), static_cast<int>(J), lat_major ? 1 : 0);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   } else {
     const float* in = nin.data_ptr<float>();
@@ -122,7 +122,7 @@ at::Tensor column_fwd(const at::Tensor& nin, const at::Tensor& sec2, const at::T
         float* ob = o + b * ix.n_out * plane + ij;
         auto rd = [ib, plane](int q) -> float { return ib[q * plane]; };
         auto wr = [ob, plane](int q, float v) { ob[q * plane] = v; };
-        const int j = static_cast<int>(ij % J);
+        const int j = lat_major ? static_cast<int>(ij / I) : static_cast<int>(ij % J);
         column_forward(c, ix, rd, wr, s2.data_ptr<float>()[j], co.data_ptr<float>()[j]);
       }
   }
@@ -132,12 +132,12 @@ at::Tensor column_fwd(const at::Tensor& nin, const at::Tensor& sec2, const at::T
 at::Tensor column_vjp_op(const at::Tensor& nin, const at::Tensor& gout, const at::Tensor& sec2,
                          const at::Tensor& cor, const at::Tensor& level_consts, int64_t batch, int64_t n, int64_t nt,
                          int64_t hum, int64_t hum_terms, std::vector<int64_t> clouds, int64_t vadv, double R,
-                         double kappa, double rv, double cpv) {
+                         double kappa, double rv, double cpv, bool lat_major) {
   check_nodal(nin, "nin");
   check_nodal(gout, "gout");
   ColumnConsts c = consts_from(level_consts, n, nt, hum, hum_terms, clouds, vadv, R, kappa, rv, cpv);
   SliceIndex ix = make_slice_index(c);
-  const int64_t I = nin.size(1), J = nin.size(2);
+  const int64_t I = lat_major ? nin.size(2) : nin.size(1), J = lat_major ? nin.size(1) : nin.size(2);
   TORCH_CHECK(gout.size(0) == batch * ix.n_out, "gout slice count mismatch");
   auto gin = at::empty_like(nin);
   auto s2 = sec2.to(nin.device(), at::kFloat).contiguous();
@@ -148,7 +148,7 @@ at::Tensor column_vjp_op(const at::Tensor& nin, const at::Tensor& gout, const at
     const int threads = 64;
     column_vjp_kernel<<<(total + threads - 1) / threads, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
         c, ix, nin.data_ptr<float>(), gout.data_ptr<float>(), gin.data_ptr<float>(), s2.data_ptr<float>(),
-        co.data_ptr<float>(), static_cast<int>(batch), static_cast<int>(I), static_cast<int>(J));
+        co.data_ptr<float>(), static_cast<int>(batch), static_cast<int>(I), static_cast<int>(J), lat_major ? 1 : 0);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   } else {
     const float* in = nin.data_ptr<float>();
@@ -163,7 +163,7 @@ at::Tensor column_vjp_op(const at::Tensor& nin, const at::Tensor& gout, const at
         auto rd = [ib, plane](int q) -> float { return ib[q * plane]; };
         auto rg = [gb, plane](int q) -> float { return gb[q * plane]; };
         auto wg = [gib, plane](int q, float v) { gib[q * plane] = v; };
-        const int j = static_cast<int>(ij % J);
+        const int j = lat_major ? static_cast<int>(ij / I) : static_cast<int>(ij % J);
         column_vjp(c, ix, rd, rg, wg, s2.data_ptr<float>()[j], co.data_ptr<float>()[j]);
       }
   }
@@ -371,9 +371,9 @@ std::vector<at::Tensor> implicit_apply(const at::Tensor& d, const at::Tensor& t,
 
 TORCH_LIBRARY_FRAGMENT(tgcm, m) {
   m.def("column_fwd(Tensor nin, Tensor sec2, Tensor cor, Tensor level_consts, int batch, int n, int nt, int hum, "
-        "int hum_terms, int[] clouds, int vadv, float R, float kappa, float rv, float cpv) -> Tensor");
+        "int hum_terms, int[] clouds, int vadv, float R, float kappa, float rv, float cpv, bool lat_major=False) -> Tensor");
   m.def("column_vjp(Tensor nin, Tensor gout, Tensor sec2, Tensor cor, Tensor level_consts, int batch, int n, "
-        "int nt, int hum, int hum_terms, int[] clouds, int vadv, float R, float kappa, float rv, float cpv) -> Tensor");
+        "int nt, int hum, int hum_terms, int[] clouds, int vadv, float R, float kappa, float rv, float cpv, bool lat_major=False) -> Tensor");
   m.def("implicit_apply(Tensor d, Tensor t, Tensor p, Tensor G, Tensor H, Tensor? Minv, Tensor lam, Tensor tref, "
         "Tensor dsig, float R, float eta, int mode) -> Tensor[]");
 }

@@ -122,9 +122,6 @@ static void gemm_dispatch(int fmt, int bn, bool a_mn, bool b_mn, const CUtensorM
   TGCM_CASE(2, 256, false, false)
   TGCM_CASE(2, 80, false, false)
   TGCM_CASE(2, 144, false, false)
-  TGCM_CASE(2, 64, false, true)
-  TGCM_CASE(2, 128, false, true)
-  TGCM_CASE(2, 256, false, true)
   TGCM_CASE(1, 64, false, false)
   TGCM_CASE(1, 128, false, false)
   TGCM_CASE(1, 64, false, true)
@@ -155,25 +152,30 @@ static int pick_bn_l(int64_t l) { return l <= 80 ? 80 : 144; }
 static int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 // ── spherical-harmonic transforms ───────────────────────────────────────────
-// x: (S, M2, Lp) fp32 modal, logical L;  P: (Mw, J, Lp);  F: (I, M2p).
-// Returns nodal (S, I, J) fp32.  ws: (S, J, M2p) workspace.
+// Nodal layouts: "lon-major" (S, I, J) = the public (…, lon, lat) layout, and
+// "lat-major" (S, J, I) used inside the fused dycore.  Both TF32 GEMMs of the
+// analysis take K-major operands only (TF32 MN-major operands would need the
+// 32-byte-atom swizzle), so a lon-major analysis input is transposed first.
+//
+// x: (S, M2, L) fp32 modal view (last-dim stride 1, row stride 16B-aligned), logical L;
+// P: (Mw, J, Lp);  F: (I, M2p).  Returns nodal (S, I, J) or (S, J, I).  ws: (S, J, M2p).
 at::Tensor sht_synth(const at::Tensor& x, int64_t L, const at::Tensor& P, const at::Tensor& F, const at::Tensor& ws,
-                     const c10::optional<at::Tensor>& col_scale, const c10::optional<at::Tensor>& err) {
-  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kFloat && x.is_contiguous(), "x must be contiguous fp32 CUDA");
-  TORCH_CHECK(x.dim() == 3, "x must be (S, M2, Lp)");
+                     const c10::optional<at::Tensor>& col_scale, const c10::optional<at::Tensor>& err,
+                     bool lat_major) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kFloat && x.dim() == 3, "x must be a (S, M2, L) fp32 CUDA tensor");
+  TORCH_CHECK(x.stride(2) == 1 && (x.stride(1) * 4) % 16 == 0 && (x.stride(0) * 4) % 16 == 0,
+              "x rows must be contiguous with 16-byte aligned strides");
   c10::cuda::CUDAGuard guard(x.device());
-  const int64_t S = x.size(0), M2 = x.size(1), Lp = x.size(2);
-  const int64_t Mw = P.size(0), J = P.size(1);
+  const int64_t S = x.size(0), M2 = x.size(1);
+  const int64_t Mw = P.size(0), J = P.size(1), Lp = P.size(2);
   const int64_t I = F.size(0), M2p = F.size(1);
-  TORCH_CHECK(Lp % 4 == 0 && P.size(2) == Lp, "modal rows must be padded to a multiple of 4");
-  TORCH_CHECK(M2 == 2 * Mw - 1 && M2p % 4 == 0 && M2p >= M2, "basis shape mismatch");
+  TORCH_CHECK(M2 == 2 * Mw - 1 && M2p % 4 == 0 && M2p >= M2 && Lp >= L, "basis shape mismatch");
   TORCH_CHECK(ws.numel() >= S * J * M2p, "workspace too small");
-  auto out = at::empty({S, I, J}, x.options());
+  auto out = lat_major ? at::empty({S, J, I}, x.options()) : at::empty({S, I, J}, x.options());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const int bnj = pick_bn_j(J);
-  // 1) Legendre synthesis, grouped per zonal wavenumber, pair rows (slice, cos/sin)
   {
-    CUtensorMap ta = make_tmap(x.data_ptr(), 2, L, M2, S, Lp * 4, M2 * Lp * 4, 32, 2, 64);
+    CUtensorMap ta = make_tmap(x.data_ptr(), 2, L, M2, S, x.stride(1) * 4, x.stride(0) * 4, 32, 2, 64);
     CUtensorMap tb = make_tmap(P.data_ptr(), 2, L, J, Mw, Lp * 4, J * Lp * 4, 32, bnj, 1);
     GemmParams p = default_params();
     p.M = 2 * S; p.N = J; p.K = L; p.groups = Mw;
@@ -183,7 +185,6 @@ at::Tensor sht_synth(const at::Tensor& x, int64_t L, const at::Tensor& P, const 
     p.err = err_ptr(err);
     gemm_dispatch(2, bnj, false, false, ta, tb, p, st);
   }
-  // 2) real DFT synthesis: out[s] (I x J) = F (I x M2) . Y[s]^T
   {
     CUtensorMap ta = make_tmap(F.data_ptr(), 2, M2, I, 1, M2p * 4, I * M2p * 4, 32, 128, 1);
     CUtensorMap tb = make_tmap(ws.data_ptr(), 2, M2, J, S, M2p * 4, J * M2p * 4, 32, bnj, 1);
@@ -191,7 +192,8 @@ at::Tensor sht_synth(const at::Tensor& x, int64_t L, const at::Tensor& P, const 
     p.M = I; p.N = J; p.K = M2; p.groups = S;
     p.tiles_m = cdiv(I, 128); p.tiles_n = cdiv(J, bnj);
     p.a_group_div = 0; p.b_group_div = 1;
-    p.C = out.data_ptr(); p.c_sg = I * J; p.c_sr = J; p.c_sc = 1;
+    p.C = out.data_ptr(); p.c_sg = I * J;
+    if (lat_major) { p.c_sr = 1; p.c_sc = I; } else { p.c_sr = J; p.c_sc = 1; }
     if (col_scale.has_value() && col_scale->defined()) p.col_scale = col_scale->data_ptr<float>();
     p.err = err_ptr(err);
     gemm_dispatch(2, bnj, false, false, ta, tb, p, st);
@@ -199,25 +201,26 @@ at::Tensor sht_synth(const at::Tensor& x, int64_t L, const at::Tensor& P, const 
   return out;
 }
 
-// N: (S, I, J) fp32 nodal;  Ft: (M2, I);  Pt: (Mw, L, J);  returns (S, M2, Lo) with Lo >= L.
-at::Tensor sht_anal(const at::Tensor& N, const at::Tensor& Ft, const at::Tensor& Pt, int64_t Lo,
+// N: nodal (S, J, I) if lat_major else (S, I, J);  Ft: (M2, I);  Pt: (Mw, L, J);  returns (S, M2, Lo).
+at::Tensor sht_anal(const at::Tensor& N_in, const at::Tensor& Ft, const at::Tensor& Pt, int64_t Lo,
                     const at::Tensor& ws, const c10::optional<at::Tensor>& col_scale,
-                    const c10::optional<at::Tensor>& err) {
-  TORCH_CHECK(N.is_cuda() && N.scalar_type() == at::kFloat && N.is_contiguous(), "N must be contiguous fp32 CUDA");
-  c10::cuda::CUDAGuard guard(N.device());
-  const int64_t S = N.size(0), I = N.size(1), J = N.size(2);
+                    const c10::optional<at::Tensor>& err, bool lat_major) {
+  TORCH_CHECK(N_in.is_cuda() && N_in.scalar_type() == at::kFloat && N_in.dim() == 3, "N must be fp32 CUDA (S, ., .)");
+  c10::cuda::CUDAGuard guard(N_in.device());
+  at::Tensor N = lat_major ? N_in.contiguous() : N_in.transpose(1, 2).contiguous();  // -> (S, J, I)
+  const int64_t S = N.size(0), J = N.size(1), I = N.size(2);
   const int64_t M2 = Ft.size(0);
   const int64_t Mw = Pt.size(0), L = Pt.size(1);
   TORCH_CHECK(Ft.size(1) == I && Pt.size(2) == J && J % 4 == 0 && I % 4 == 0, "basis shape mismatch");
   TORCH_CHECK(ws.numel() >= S * M2 * J, "workspace too small");
   TORCH_CHECK(Lo >= L, "output row length too small");
-  auto out = at::zeros({S, M2, Lo}, N.options());
+  auto out = Lo > L ? at::zeros({S, M2, Lo}, N.options()) : at::empty({S, M2, Lo}, N.options());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const int bnj = pick_bn_j(J);
-  // 1) real DFT analysis: Z[s] (M2 x J) = Ft (M2 x I) . N[s] (I x J) [B operand N-major], times w_j
+  // 1) real DFT analysis: Z[s] (M2 x J) = Ft (M2 x I) . N[s]^T, both K-major (K = I), times w_j
   {
     CUtensorMap ta = make_tmap(Ft.data_ptr(), 2, I, M2, 1, I * 4, M2 * I * 4, 32, 128, 1);
-    CUtensorMap tb = make_tmap(N.data_ptr(), 2, J, I, S, J * 4, I * J * 4, 32, 32, 1);
+    CUtensorMap tb = make_tmap(N.data_ptr(), 2, I, J, S, I * 4, J * I * 4, 32, bnj, 1);
     GemmParams p = default_params();
     p.M = M2; p.N = J; p.K = I; p.groups = S;
     p.tiles_m = cdiv(M2, 128); p.tiles_n = cdiv(J, bnj);
@@ -225,7 +228,7 @@ at::Tensor sht_anal(const at::Tensor& N, const at::Tensor& Ft, const at::Tensor&
     p.C = ws.data_ptr(); p.c_sg = M2 * J; p.c_sr = J; p.c_sc = 1;
     if (col_scale.has_value() && col_scale->defined()) p.col_scale = col_scale->data_ptr<float>();
     p.err = err_ptr(err);
-    gemm_dispatch(2, bnj, false, true, ta, tb, p, st);
+    gemm_dispatch(2, bnj, false, false, ta, tb, p, st);
   }
   // 2) Legendre analysis per zonal wavenumber: out rows (slice, cos/sin), cols l
   {
@@ -314,8 +317,8 @@ void linear_wgrad(const at::Tensor& dY, const at::Tensor& X, at::Tensor& dW, int
 }  // namespace tgcm
 
 TORCH_LIBRARY_FRAGMENT(tgcm, m) {
-  m.def("sht_synth(Tensor x, int L, Tensor P, Tensor F, Tensor ws, Tensor? col_scale, Tensor? err) -> Tensor");
-  m.def("sht_anal(Tensor N, Tensor Ft, Tensor Pt, int Lo, Tensor ws, Tensor? col_scale, Tensor? err) -> Tensor");
+  m.def("sht_synth(Tensor x, int L, Tensor P, Tensor F, Tensor ws, Tensor? col_scale, Tensor? err, bool lat_major) -> Tensor");
+  m.def("sht_anal(Tensor N, Tensor Ft, Tensor Pt, int Lo, Tensor ws, Tensor? col_scale, Tensor? err, bool lat_major) -> Tensor");
   m.def("linear_fwd(Tensor X, Tensor W, Tensor? bias, int act, Tensor(a!) out, Tensor? aux, Tensor? err) -> ()");
   m.def("linear_dgrad(Tensor dY, Tensor W, Tensor(a!) dX, Tensor? pre, int pre_act, Tensor? err) -> ()");
   m.def("linear_wgrad(Tensor dY, Tensor X, Tensor(a!) dW, int splits, Tensor? err) -> ()");

@@ -1,0 +1,514 @@
+// Spectral-space kernels for sm_100a (with CPU twins sharing the same code):
+//
+//  * spectral_linear: a table-driven linear map between stacked modal
+//    fields, y[b, s, m, l] = Σ_terms coef · post[l] · D( pre[l'] · x[b, src, ., .] )(m, l),
+//    where D is one of the spherical-harmonic stencils (identity, ∂/∂λ,
+//    cosθ ∂/∂θ, secθ ∂/∂θ cos², and the transposes of the latitudinal
+//    ones) or a vertical matrix row.  The spectral pre/post-processing of
+//    the explicit tendency, of the neural parameterization and of the
+//    encoders are all instances of this op, and an op's adjoint is the
+//    same kernel with the transposed term table.
+//  * sil3_stage: one IMEX-SIL3 stage on a packed prognostic state
+//    (channels [ζ | δ | T' | ln ps | tracers]) — explicit combination, the
+//    implicit terms of the stage's z-combination, the per-wavenumber
+//    implicit solve, and on the last stage the spectral filter and the
+//    inner-state sanitiser — plus its adjoint.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/library.h>
+
+#include <vector>
+
+#ifndef __CUDACC__
+#define __host__
+#define __device__
+#endif
+
+namespace tgcm {
+
+// Term table rows (int32): dst, src, stencil, pre_diag, post_diag, mat, row; coefficient in a float array.
+enum Stencil : int {
+  kStId = 0,
+  kStDlon = 1,
+  kStCdlat = 2,     // cosθ ∂/∂θ
+  kStHdlat = 3,     // secθ ∂/∂θ (cos²θ ·)
+  kStCdlatT = 4,    // transpose of kStCdlat
+  kStHdlatT = 5,    // transpose of kStHdlat
+  kStVert = 6,      // Σ_k' M[row, k'] x[src + k']
+  kStVertT = 7,     // Σ_k' M[k', row] x[src + k']
+};
+
+struct LinearArgs {
+  const float* x;
+  float* y;
+  long long xs_b, xs_c, xs_m;  // input strides (batch, channel, m); l stride 1
+  long long ys_b, ys_c, ys_m;  // output strides
+  const int* row_ptr;          // (C_out + 1) CSR offsets into terms
+  const int* terms;            // (n_terms, 7)
+  const float* coef;           // (n_terms)
+  const float* diag;           // (n_diag, L)
+  const float* rec_a;          // (M2, L) recurrence weights a
+  const float* rec_b;          // (M2, L) recurrence weights b
+  const float* mats;           // (n_mats, n, n)
+  int nlev;                    // matrix size n
+  int B, C_out, M2, L;
+};
+
+__host__ __device__ inline float xval(const LinearArgs& a, int b, int c, int mr, int l, int pre) {
+  if (l < 0 || l >= a.L) return 0.f;
+  const float v = a.x[b * a.xs_b + c * a.xs_c + mr * a.xs_m + l];
+  return pre >= 0 ? v * a.diag[pre * a.L + l] : v;
+}
+
+__host__ __device__ inline float stencil_val(const LinearArgs& a, int b, int src, int st, int pre, int mr, int l,
+                                             int mat, int row) {
+  switch (st) {
+    case kStId:
+      return xval(a, b, src, mr, l, pre);
+    case kStDlon: {
+      if (mr == 0) return 0.f;
+      const int j = (mr + 1) / 2;
+      return (mr & 1) ? j * xval(a, b, src, mr + 1, l, pre) : -j * xval(a, b, src, mr - 1, l, pre);
+    }
+    case kStCdlat: {
+      float r = 0.f;
+      if (l + 1 < a.L) r += (l + 2) * a.rec_a[mr * a.L + l + 1] * xval(a, b, src, mr, l + 1, pre);
+      if (l - 1 >= 0) r -= (l - 1) * a.rec_b[mr * a.L + l - 1] * xval(a, b, src, mr, l - 1, pre);
+      return r;
+    }
+    case kStHdlat: {
+      float r = 0.f;
+      if (l + 1 < a.L) r += l * a.rec_a[mr * a.L + l + 1] * xval(a, b, src, mr, l + 1, pre);
+      if (l - 1 >= 0) r -= (l + 1) * a.rec_b[mr * a.L + l - 1] * xval(a, b, src, mr, l - 1, pre);
+      return r;
+    }
+    case kStCdlatT: {
+      float r = 0.f;
+      if (l - 1 >= 0) r += (l + 1) * a.rec_a[mr * a.L + l] * xval(a, b, src, mr, l - 1, pre);
+      if (l + 1 < a.L) r -= l * a.rec_b[mr * a.L + l] * xval(a, b, src, mr, l + 1, pre);
+      return r;
+    }
+    case kStHdlatT: {
+      float r = 0.f;
+      if (l - 1 >= 0) r += (l - 1) * a.rec_a[mr * a.L + l] * xval(a, b, src, mr, l - 1, pre);
+      if (l + 1 < a.L) r -= (l + 2) * a.rec_b[mr * a.L + l] * xval(a, b, src, mr, l + 1, pre);
+      return r;
+    }
+    case kStVert: {
+      const float* M = a.mats + static_cast<long long>(mat) * a.nlev * a.nlev;
+      float r = 0.f;
+      for (int k = 0; k < a.nlev; ++k) r += M[row * a.nlev + k] * xval(a, b, src + k, mr, l, pre);
+      return r;
+    }
+    case kStVertT: {
+      const float* M = a.mats + static_cast<long long>(mat) * a.nlev * a.nlev;
+      float r = 0.f;
+      for (int k = 0; k < a.nlev; ++k) r += M[k * a.nlev + row] * xval(a, b, src + k, mr, l, pre);
+      return r;
+    }
+    default:
+      return 0.f;
+  }
+}
+
+__host__ __device__ inline void linear_point(const LinearArgs& a, int b, int s, int mr, int l) {
+  float acc = 0.f;
+  for (int t = a.row_ptr[s]; t < a.row_ptr[s + 1]; ++t) {
+    const int* T = a.terms + 7 * t;
+    float v = stencil_val(a, b, T[1], T[2], T[3], mr, l, T[5], T[6]);
+    if (T[4] >= 0) v *= a.diag[T[4] * a.L + l];
+    acc += a.coef[t] * v;
+  }
+  a.y[b * a.ys_b + s * a.ys_c + mr * a.ys_m + l] = acc;
+}
+
+__global__ void spectral_linear_kernel(LinearArgs a) {
+  const long long total = static_cast<long long>(a.B) * a.C_out * a.M2 * a.L;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int l = static_cast<int>(i % a.L);
+    long long r = i / a.L;
+    const int mr = static_cast<int>(r % a.M2);
+    r /= a.M2;
+    const int s = static_cast<int>(r % a.C_out);
+    const int b = static_cast<int>(r / a.C_out);
+    linear_point(a, b, s, mr, l);
+  }
+}
+
+// x: (B, C_in, M2, Lx) ; returns y: (B, C_out, M2, Ly) with Ly = out_lpad (>= L), pad zero.
+at::Tensor spectral_linear(const at::Tensor& x, int64_t L, int64_t C_out, int64_t out_lpad, const at::Tensor& row_ptr,
+                           const at::Tensor& terms, const at::Tensor& coef, const at::Tensor& diag,
+                           const at::Tensor& rec_a, const at::Tensor& rec_b, const at::Tensor& mats, int64_t nlev) {
+  TORCH_CHECK(x.dim() == 4 && x.scalar_type() == at::kFloat && x.stride(3) == 1, "x must be (B, C, M2, L) fp32");
+  const int64_t B = x.size(0), M2 = x.size(2);
+  auto y = (out_lpad > L) ? at::zeros({B, C_out, M2, out_lpad}, x.options())
+                          : at::empty({B, C_out, M2, out_lpad}, x.options());
+  LinearArgs a;
+  a.x = x.data_ptr<float>();
+  a.y = y.data_ptr<float>();
+  a.xs_b = x.stride(0); a.xs_c = x.stride(1); a.xs_m = x.stride(2);
+  a.ys_b = y.stride(0); a.ys_c = y.stride(1); a.ys_m = y.stride(2);
+  a.row_ptr = row_ptr.data_ptr<int>();
+  a.terms = terms.data_ptr<int>();
+  a.coef = coef.data_ptr<float>();
+  a.diag = diag.data_ptr<float>();
+  a.rec_a = rec_a.data_ptr<float>();
+  a.rec_b = rec_b.data_ptr<float>();
+  a.mats = mats.data_ptr<float>();
+  a.nlev = static_cast<int>(nlev);
+  a.B = static_cast<int>(B); a.C_out = static_cast<int>(C_out); a.M2 = static_cast<int>(M2); a.L = static_cast<int>(L);
+  if (x.is_cuda()) {
+    c10::cuda::CUDAGuard guard(x.device());
+    const long long total = B * C_out * M2 * L;
+    const int threads = 256;
+    const long long blocks = std::min<long long>((total + threads - 1) / threads, 148LL * 32);
+    spectral_linear_kernel<<<static_cast<unsigned>(blocks), threads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  } else {
+    for (int b = 0; b < B; ++b)
+      for (int s = 0; s < C_out; ++s)
+        for (int mr = 0; mr < M2; ++mr)
+          for (int l = 0; l < L; ++l) linear_point(a, b, s, mr, l);
+  }
+  return y;
+}
+
+// ── SIL3 stage on a packed state ───────────────────────────────────────────
+constexpr int kStageMaxLev = 64;
+constexpr int kStageMaxE = 3;
+
+struct StageArgs {
+  // packed tensors (B, C, M2, L) contiguous
+  const float* y0;
+  const float* E[kStageMaxE];
+  const float* P;
+  const float* y2;    // extra implicit-combination input (stage 3) or null
+  float* out;
+  const float* gin;   // adjoint: cotangent of the stage output
+  float* g_y0;
+  float* g_E[kStageMaxE];
+  float* g_P;
+  float* g_y2;
+  float ce[kStageMaxE];
+  int nE;
+  float cp, cg, eta;
+  const float* G; const float* H; const float* Minv; const float* lam; const float* tref; const float* dsig;
+  const float* filt;  // (L) or null
+  float clamp_abs;
+  float R;
+  int final_stage;
+  int B, C, n, M2, L;
+};
+
+template <typename Mat>
+__host__ __device__ void stage_column_fwd(const StageArgs& a, int b, int mr, int l, Mat mat) {
+  const int n = a.n;
+  const long long cs = static_cast<long long>(a.M2) * a.L;
+  const long long base = static_cast<long long>(b) * a.C * cs + static_cast<long long>(mr) * a.L + l;
+  auto at_ = [&](const float* p, int c) -> float { return p[base + c * cs]; };
+  const float f = a.filt ? a.filt[l] : 1.f;
+  auto finish = [&](float v) -> float {
+    if (!a.final_stage) return v;
+    v *= f;
+    if (v != v) v = 0.f;
+    if (v > a.clamp_abs) v = a.clamp_abs;
+    if (v < -a.clamp_abs) v = -a.clamp_abs;
+    return v;
+  };
+  auto expl = [&](int c) -> float {
+    float v = at_(a.y0, c) + a.cp * at_(a.P, c);
+    for (int j = 0; j < a.nE; ++j) v += a.ce[j] * at_(a.E[j], c);
+    return v;
+  };
+  // vorticity (channels [0, n)) and tracers (channels [3n+1, C)): explicit only
+  for (int c = 0; c < n; ++c) a.out[base + c * cs] = finish(expl(c));
+  for (int c = 3 * n + 1; c < a.C; ++c) a.out[base + c * cs] = finish(expl(c));
+  // implicit channels
+  float zd[kStageMaxLev], zt[kStageMaxLev], rd[kStageMaxLev], rt[kStageMaxLev], od[kStageMaxLev];
+  for (int k = 0; k < n; ++k) {
+    zd[k] = at_(a.y0, n + k) + (a.y2 ? at_(a.y2, n + k) : 0.f);
+    zt[k] = at_(a.y0, 2 * n + k) + (a.y2 ? at_(a.y2, 2 * n + k) : 0.f);
+  }
+  const float zp = at_(a.y0, 3 * n) + (a.y2 ? at_(a.y2, 3 * n) : 0.f);
+  const float lam = a.lam[l];
+  float zp_g = 0.f;
+  for (int i = 0; i < n; ++i) {
+    float gt = 0.f, hd = 0.f;
+    for (int j = 0; j < n; ++j) {
+      gt += mat(0, i, j) * zt[j];
+      hd += mat(1, i, j) * zd[j];
+    }
+    // rhs = explicit + cg * G(z)
+    rd[i] = expl(n + i) + a.cg * (-lam * (gt + a.R * a.tref[i] * zp));
+    rt[i] = expl(2 * n + i) + a.cg * (-hd);
+    zp_g += a.dsig[i] * zd[i];
+  }
+  const float rp = expl(3 * n) + a.cg * (-zp_g);
+  // solve: r = rd - eta*lam*(G rt + R Tr rp); δ = Minv r; T = rt - eta H δ; p = rp - eta Δσ·δ
+  const float el = a.eta * lam;
+  float tmp[kStageMaxLev];
+  for (int i = 0; i < n; ++i) {
+    float gt = 0.f;
+    for (int j = 0; j < n; ++j) gt += mat(0, i, j) * rt[j];
+    tmp[i] = rd[i] - el * (gt + a.R * a.tref[i] * rp);
+  }
+  float sp = 0.f;
+  for (int i = 0; i < n; ++i) {
+    float s = 0.f;
+    for (int j = 0; j < n; ++j) s += mat(2, i, j) * tmp[j];
+    od[i] = s;
+    sp += a.dsig[i] * s;
+  }
+  for (int i = 0; i < n; ++i) {
+    float hd = 0.f;
+    for (int j = 0; j < n; ++j) hd += mat(1, i, j) * od[j];
+    a.out[base + (n + i) * cs] = finish(od[i]);
+    a.out[base + (2 * n + i) * cs] = finish(rt[i] - a.eta * hd);
+  }
+  a.out[base + 3 * n * cs] = finish(rp - a.eta * sp);
+}
+
+template <typename Mat>
+__host__ __device__ void stage_column_adj(const StageArgs& a, int b, int mr, int l, Mat mat) {
+  const int n = a.n;
+  const long long cs = static_cast<long long>(a.M2) * a.L;
+  const long long base = static_cast<long long>(b) * a.C * cs + static_cast<long long>(mr) * a.L + l;
+  const float f = a.filt ? a.filt[l] : 1.f;
+  // cotangent of the pre-filter value: g * f * [not clamped]
+  auto gpre = [&](int c) -> float {
+    float g = a.gin[base + c * cs];
+    if (!a.final_stage) return g;
+    const float o = a.out[base + c * cs];  // saved forward output
+    if (o >= a.clamp_abs || o <= -a.clamp_abs) return 0.f;
+    return g * f;
+  };
+  auto scatter = [&](int c, float r) {
+    a.g_y0[base + c * cs] = r;
+    a.g_P[base + c * cs] = a.cp * r;
+    for (int j = 0; j < a.nE; ++j) a.g_E[j][base + c * cs] = a.ce[j] * r;
+  };
+  for (int c = 0; c < n; ++c) scatter(c, gpre(c));
+  for (int c = 3 * n + 1; c < a.C; ++c) scatter(c, gpre(c));
+  if (a.g_y2) {
+    for (int c = 0; c < n; ++c) a.g_y2[base + c * cs] = 0.f;
+    for (int c = 3 * n + 1; c < a.C; ++c) a.g_y2[base + c * cs] = 0.f;
+  }
+  // transpose of the solve: inputs (d̄, t̄, p̄) = cotangents of (δ, T, p)
+  float dd[kStageMaxLev], tt[kStageMaxLev], r[kStageMaxLev], od[kStageMaxLev], ot[kStageMaxLev];
+  for (int k = 0; k < n; ++k) {
+    dd[k] = gpre(n + k);
+    tt[k] = gpre(2 * n + k);
+  }
+  const float pp = gpre(3 * n);
+  const float lam = a.lam[l];
+  const float el = a.eta * lam;
+  for (int i = 0; i < n; ++i) {
+    float htt = 0.f;
+    for (int j = 0; j < n; ++j) htt += mat(1, j, i) * tt[j];
+    r[i] = dd[i] - a.eta * htt - a.eta * a.dsig[i] * pp;
+  }
+  float trd = 0.f;
+  for (int i = 0; i < n; ++i) {
+    float s = 0.f;
+    for (int j = 0; j < n; ++j) s += mat(2, j, i) * r[j];
+    od[i] = s;  // cotangent of rd (δ* side)
+    trd += a.tref[i] * s;
+  }
+  for (int i = 0; i < n; ++i) {
+    float gtr = 0.f;
+    for (int j = 0; j < n; ++j) gtr += mat(0, j, i) * od[j];
+    ot[i] = tt[i] - el * gtr;  // cotangent of rt
+  }
+  const float op = pp - el * a.R * trd;  // cotangent of rp
+  // rhs = explicit + cg * G(z): explicit part
+  for (int i = 0; i < n; ++i) {
+    scatter(n + i, od[i]);
+    scatter(2 * n + i, ot[i]);
+  }
+  scatter(3 * n, op);
+  // z-part: z̄ = cg Gᵀ(ō) with Gᵀ: δ̄z = −Hᵀ t̄ − Δσ p̄ ; T̄z = −λ Gᵀ d̄ ; p̄z = −λ R Tr·d̄
+  float trdot = 0.f;
+  for (int i = 0; i < n; ++i) trdot += a.tref[i] * od[i];
+  for (int i = 0; i < n; ++i) {
+    float htb = 0.f, gta = 0.f;
+    for (int j = 0; j < n; ++j) {
+      htb += mat(1, j, i) * ot[j];
+      gta += mat(0, j, i) * od[j];
+    }
+    const float zd = a.cg * (-htb - a.dsig[i] * op);
+    const float zt = a.cg * (-lam * gta);
+    a.g_y0[base + (n + i) * cs] += zd;
+    a.g_y0[base + (2 * n + i) * cs] += zt;
+    if (a.g_y2) {
+      a.g_y2[base + (n + i) * cs] = zd;
+      a.g_y2[base + (2 * n + i) * cs] = zt;
+    }
+  }
+  const float zp = a.cg * (-lam * a.R * trdot);
+  a.g_y0[base + 3 * n * cs] += zp;
+  if (a.g_y2) a.g_y2[base + 3 * n * cs] = zp;
+}
+
+constexpr int kStageL = 4;
+constexpr int kStageM = 32;
+
+__global__ void sil3_stage_kernel(StageArgs a, int adjoint) {
+  extern __shared__ float sm[];
+  const int n = a.n;
+  float* sG = sm;
+  float* sH = sG + n * n;
+  float* sMi = sH + n * n;
+  const int l0 = blockIdx.x * kStageL;
+  const int b = blockIdx.y;
+  for (int i = threadIdx.x; i < n * n; i += blockDim.x) {
+    sG[i] = a.G[i];
+    sH[i] = a.H[i];
+  }
+  for (int i = threadIdx.x; i < kStageL * n * n; i += blockDim.x) {
+    const int ll = l0 + i / (n * n);
+    sMi[i] = ll < a.L ? a.Minv[static_cast<long long>(ll) * n * n + i % (n * n)] : 0.f;
+  }
+  __syncthreads();
+  const int tl = threadIdx.x % kStageL;
+  const int tm = threadIdx.x / kStageL;
+  const int l = l0 + tl;
+  if (l >= a.L) return;
+  const float* mi = sMi + tl * n * n;
+  auto mat = [sG, sH, mi, n](int kind, int i, int j) -> float {
+    return kind == 0 ? sG[i * n + j] : (kind == 1 ? sH[i * n + j] : mi[i * n + j]);
+  };
+  for (int m = tm; m < a.M2; m += kStageM) {
+    if (adjoint)
+      stage_column_adj(a, b, m, l, mat);
+    else
+      stage_column_fwd(a, b, m, l, mat);
+  }
+}
+
+static const float* ptr_or_null(const c10::optional<at::Tensor>& t) {
+  return (t.has_value() && t->defined()) ? t->data_ptr<float>() : nullptr;
+}
+
+static void run_stage(StageArgs& a, const at::Tensor& like, int adjoint) {
+  if (like.is_cuda()) {
+    c10::cuda::CUDAGuard guard(like.device());
+    dim3 grid((a.L + kStageL - 1) / kStageL, a.B);
+    const size_t smem = (2 * a.n * a.n + kStageL * a.n * a.n) * sizeof(float);
+    sil3_stage_kernel<<<grid, kStageL * kStageM, smem, at::cuda::getCurrentCUDAStream()>>>(a, adjoint);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  } else {
+    const int n = a.n;
+    for (int b = 0; b < a.B; ++b)
+      for (int l = 0; l < a.L; ++l) {
+        const float* mi = a.Minv + static_cast<long long>(l) * n * n;
+        const float* g = a.G;
+        const float* h = a.H;
+        auto mat = [g, h, mi, n](int kind, int i, int j) -> float {
+          return kind == 0 ? g[i * n + j] : (kind == 1 ? h[i * n + j] : mi[i * n + j]);
+        };
+        for (int m = 0; m < a.M2; ++m) {
+          if (adjoint)
+            stage_column_adj(a, b, m, l, mat);
+          else
+            stage_column_fwd(a, b, m, l, mat);
+        }
+      }
+  }
+}
+
+static void fill_common(StageArgs& a, const at::Tensor& y0, const std::vector<double>& ce, double cp, double cg,
+                        double eta, const at::Tensor& G, const at::Tensor& H, const at::Tensor& Minv,
+                        const at::Tensor& lam, const at::Tensor& tref, const at::Tensor& dsig,
+                        const c10::optional<at::Tensor>& filt, double clamp_abs, double R, int64_t final_stage,
+                        int64_t n) {
+  TORCH_CHECK(y0.dim() == 4 && y0.is_contiguous() && y0.scalar_type() == at::kFloat, "packed state must be contiguous fp32");
+  TORCH_CHECK(n <= kStageMaxLev && static_cast<int>(ce.size()) <= kStageMaxE, "stage limits exceeded");
+  a.nE = static_cast<int>(ce.size());
+  for (int j = 0; j < a.nE; ++j) a.ce[j] = static_cast<float>(ce[j]);
+  a.cp = static_cast<float>(cp); a.cg = static_cast<float>(cg); a.eta = static_cast<float>(eta);
+  a.G = G.data_ptr<float>(); a.H = H.data_ptr<float>(); a.Minv = Minv.data_ptr<float>();
+  a.lam = lam.data_ptr<float>(); a.tref = tref.data_ptr<float>(); a.dsig = dsig.data_ptr<float>();
+  a.filt = ptr_or_null(filt);
+  a.clamp_abs = static_cast<float>(clamp_abs);
+  a.R = static_cast<float>(R);
+  a.final_stage = static_cast<int>(final_stage);
+  a.B = static_cast<int>(y0.size(0)); a.C = static_cast<int>(y0.size(1)); a.n = static_cast<int>(n);
+  a.M2 = static_cast<int>(y0.size(2)); a.L = static_cast<int>(y0.size(3));
+}
+
+at::Tensor sil3_stage(const at::Tensor& y0, std::vector<at::Tensor> E, const at::Tensor& P,
+                      const c10::optional<at::Tensor>& y2, std::vector<double> ce, double cp, double cg, double eta,
+                      const at::Tensor& G, const at::Tensor& H, const at::Tensor& Minv, const at::Tensor& lam,
+                      const at::Tensor& tref, const at::Tensor& dsig, const c10::optional<at::Tensor>& filt,
+                      double clamp_abs, double R, int64_t final_stage, int64_t n) {
+  StageArgs a;
+  memset(&a, 0, sizeof(a));
+  fill_common(a, y0, ce, cp, cg, eta, G, H, Minv, lam, tref, dsig, filt, clamp_abs, R, final_stage, n);
+  TORCH_CHECK(E.size() == ce.size(), "one coefficient per explicit tendency");
+  auto out = at::empty_like(y0);
+  a.y0 = y0.data_ptr<float>();
+  for (size_t j = 0; j < E.size(); ++j) {
+    TORCH_CHECK(E[j].is_contiguous() && E[j].sizes() == y0.sizes(), "E shape");
+    a.E[j] = E[j].data_ptr<float>();
+  }
+  TORCH_CHECK(P.is_contiguous() && P.sizes() == y0.sizes(), "P shape");
+  a.P = P.data_ptr<float>();
+  a.y2 = ptr_or_null(y2);
+  a.out = out.data_ptr<float>();
+  run_stage(a, y0, 0);
+  return out;
+}
+
+std::vector<at::Tensor> sil3_stage_adjoint(const at::Tensor& gout, const at::Tensor& out, int64_t nE, int64_t has_y2,
+                                           std::vector<double> ce, double cp, double cg, double eta,
+                                           const at::Tensor& G, const at::Tensor& H, const at::Tensor& Minv,
+                                           const at::Tensor& lam, const at::Tensor& tref, const at::Tensor& dsig,
+                                           const c10::optional<at::Tensor>& filt, double clamp_abs, double R,
+                                           int64_t final_stage, int64_t n) {
+  StageArgs a;
+  memset(&a, 0, sizeof(a));
+  fill_common(a, gout, ce, cp, cg, eta, G, H, Minv, lam, tref, dsig, filt, clamp_abs, R, final_stage, n);
+  auto g_y0 = at::empty_like(gout);
+  auto g_P = at::empty_like(gout);
+  std::vector<at::Tensor> res{g_y0};
+  std::vector<at::Tensor> gE;
+  for (int64_t j = 0; j < nE; ++j) {
+    gE.push_back(at::empty_like(gout));
+    a.g_E[j] = gE.back().data_ptr<float>();
+  }
+  at::Tensor g_y2;
+  if (has_y2) {
+    g_y2 = at::empty_like(gout);
+    a.g_y2 = g_y2.data_ptr<float>();
+  }
+  a.gin = gout.data_ptr<float>();
+  a.out = const_cast<float*>(out.data_ptr<float>());
+  a.g_y0 = g_y0.data_ptr<float>();
+  a.g_P = g_P.data_ptr<float>();
+  run_stage(a, gout, 1);
+  for (auto& t : gE) res.push_back(t);
+  res.push_back(g_P);
+  if (has_y2) res.push_back(g_y2);
+  return res;
+}
+
+}  // namespace tgcm
+
+TORCH_LIBRARY_FRAGMENT(tgcm, m) {
+  m.def("spectral_linear(Tensor x, int L, int C_out, int out_lpad, Tensor row_ptr, Tensor terms, Tensor coef, "
+        "Tensor diag, Tensor rec_a, Tensor rec_b, Tensor mats, int nlev) -> Tensor");
+  m.def("sil3_stage(Tensor y0, Tensor[] E, Tensor P, Tensor? y2, float[] ce, float cp, float cg, float eta, "
+        "Tensor G, Tensor H, Tensor Minv, Tensor lam, Tensor tref, Tensor dsig, Tensor? filt, float clamp_abs, "
+        "float R, int final_stage, int n) -> Tensor");
+  m.def("sil3_stage_adjoint(Tensor gout, Tensor out, int nE, int has_y2, float[] ce, float cp, float cg, float eta, "
+        "Tensor G, Tensor H, Tensor Minv, Tensor lam, Tensor tref, Tensor dsig, Tensor? filt, float clamp_abs, "
+        "float R, int final_stage, int n) -> Tensor[]");
+}
+
+TORCH_LIBRARY_IMPL(tgcm, CompositeExplicitAutograd, m) {
+  m.impl("spectral_linear", &tgcm::spectral_linear);
+  m.impl("sil3_stage", &tgcm::sil3_stage);
+  m.impl("sil3_stage_adjoint", &tgcm::sil3_stage_adjoint);
+}

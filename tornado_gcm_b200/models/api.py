@@ -237,12 +237,18 @@ class NeuralGCMModel(nn.Module):
         return s
 
     # ── inner step ────────────────────────────────────────────────────
-    def _fused_stepper(self):
+    def _fused_stepper(self, tracer_keys):
         if self._fused is None:
+            self._fused = {}
+        st = self._fused.get(tracer_keys)
+        if st is None:
             from tornado_gcm_b200.ops import dycore as dycore_ops
 
-            self._fused = dycore_ops.FusedSIL3(self._dycore, self._inner_dt, self.combined_filter_scaling())
-        return self._fused
+            st = dycore_ops.PackedSIL3(self._dycore, self._inner_dt, self.combined_filter_scaling(), tracer_keys,
+                                       clamp_abs=self._sanitize_inner_clamp_abs if self._sanitize_inner_enabled
+                                       else float("inf"))
+            self._fused[tracer_keys] = st
+        return st
 
     def _build_inner_step_fn(self, physics_tendency: State):
         eq = self._dycore
@@ -289,12 +295,18 @@ class NeuralGCMModel(nn.Module):
         if self._dycore is not None:
             with record_function("Z1_dycore"):
                 if self._use_fused(state):
-                    stepper = self._fused_stepper()
+                    from tornado_gcm_b200.ops import spectral
+
+                    keys = tuple(sorted(state.tracers))
+                    stepper = self._fused_stepper(keys)
+                    y = spectral.pack_state(state, keys)
+                    P = spectral.pack_state(phys, keys) + stepper.orography_packed(y.device)
                     for _ in range(self.config.dycore_substeps):
                         if self.config.checkpoint_inner_steps and self.training:
-                            state = torch_checkpoint.checkpoint(stepper.step, state, phys, use_reentrant=False)
+                            y = torch_checkpoint.checkpoint(stepper.step_packed, y, P, use_reentrant=False)
                         else:
-                            state = stepper.step(state, phys)
+                            y = stepper.step_packed(y, P)
+                    state = spectral.unpack_state(y, self.config.coords.vertical.layers, keys, state.sim_time)
                 else:
                     inner = self._build_inner_step_fn(phys)
                     for _ in range(self.config.dycore_substeps):

@@ -319,3 +319,156 @@ class FusedSIL3:
             c = self.clamp_abs
             out = out.tree_map(lambda x: torch.clamp(torch.nan_to_num(x, nan=0.0, posinf=c, neginf=-c), -c, c))
         return dataclasses.replace(out, sim_time=y0.sim_time)
+
+
+# ── packed-state SIL3 (the production GPU path) ─────────────────────────────
+def _synth_lat(x3: torch.Tensor, grid) -> torch.Tensor:
+    """(S, M2, L) modal (possibly a padded-row view) → (S, J, I) nodal."""
+    if x3.is_cuda:
+        from tornado_gcm_b200.ops import sht as sht_ops
+
+        return sht_ops.to_nodal_lat_major(x3, grid.spherical_harmonics)
+    return grid.to_nodal(x3).transpose(-1, -2).contiguous()
+
+
+def _anal_lat(n3: torch.Tensor, grid) -> torch.Tensor:
+    """(S, J, I) nodal → (S, M2, L) modal."""
+    if n3.is_cuda:
+        from tornado_gcm_b200.ops import sht as sht_ops
+
+        return sht_ops.to_modal_lat_major(n3, grid.spherical_harmonics)
+    return grid.to_modal(n3.transpose(-1, -2).contiguous())
+
+
+class ColumnLatFn(torch.autograd.Function):
+    """Column tendency on latitude-major nodal slices (S, J, I)."""
+
+    @staticmethod
+    def forward(ctx, nin, spec, batch):
+        ctx.spec, ctx.batch = spec, batch
+        ctx.save_for_backward(nin)
+        ops = _ext.require("column tendency")
+        s2, co = spec.device_consts(nin.device)
+        return ops.column_fwd(nin.contiguous(), s2, co, *_args_with_batch(spec, batch), True)
+
+    @staticmethod
+    def backward(ctx, gout):
+        (nin,) = ctx.saved_tensors
+        ops = _ext.require("column tendency VJP")
+        s2, co = ctx.spec.device_consts(nin.device)
+        g = ops.column_vjp(nin, gout.contiguous(), s2, co, *_args_with_batch(ctx.spec, ctx.batch), True)
+        return g, None, None
+
+
+class StageFn(torch.autograd.Function):
+    """One SIL3 stage on the packed state (explicit combination + implicit solve)."""
+
+    @staticmethod
+    def forward(ctx, y0, P, y2, E0, E1, E2, meta):
+        ops = _ext.require("SIL3 stage")
+        Es = [e for e in (E0, E1, E2) if e is not None]
+        G, H, lam, tref, dsig = meta["consts"]
+        out = ops.sil3_stage(y0.contiguous(), [e.contiguous() for e in Es], P.contiguous(), y2, meta["ce"],
+                             meta["cp"], meta["cg"], meta["eta"], G, H, meta["minv"], lam, tref, dsig,
+                             meta["filt"], meta["clamp"], meta["R"], meta["final"], meta["n"])
+        ctx.meta, ctx.nE, ctx.has_y2 = meta, len(Es), y2 is not None
+        if meta["final"]:
+            ctx.save_for_backward(out)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        ops = _ext.require("SIL3 stage adjoint")
+        meta = ctx.meta
+        G, H, lam, tref, dsig = meta["consts"]
+        out = ctx.saved_tensors[0] if meta["final"] else g
+        res = ops.sil3_stage_adjoint(g.contiguous(), out, ctx.nE, int(ctx.has_y2), meta["ce"], meta["cp"],
+                                     meta["cg"], meta["eta"], G, H, meta["minv"], lam, tref, dsig, meta["filt"],
+                                     meta["clamp"], meta["R"], meta["final"], meta["n"])
+        g_y0 = res[0]
+        gE = list(res[1:1 + ctx.nE]) + [None] * (3 - ctx.nE)
+        g_P = res[1 + ctx.nE]
+        g_y2 = res[2 + ctx.nE] if ctx.has_y2 else None
+        return g_y0, g_P, g_y2, gE[0], gE[1], gE[2], None
+
+
+class PackedSIL3:
+    """SIL3 substep on packed states ``[ζ | δ | T' | ln ps | tracers]`` (B, C, 2M-1, L).
+
+    Per substep: 3 × (pre recipe → TF32 synthesis → column kernel → TF32
+    analysis → post recipe) and 3 stage kernels; every piece has a kernel
+    adjoint, so backward-through-rollout runs the same number of kernels.
+    """
+
+    def __init__(self, eq: pe.PrimitiveEquationsSigma, dt: float, filter_scaling: np.ndarray, tracer_keys,
+                 clamp_abs: float = 1.0e12):
+        from tornado_gcm_b200.ops import spectral
+
+        self.eq = eq
+        self.dt = float(dt)
+        self.keys = tuple(tracer_keys)
+        self.n = eq.vertical.layers
+        self.pre = spectral.explicit_pre_recipe(eq, self.keys)
+        self.post = spectral.explicit_post_recipe(eq, self.keys)
+        self.spec = ColumnSpec.from_equation(eq, self.keys)
+        self.ch = spectral.packed_channels(self.n, self.keys)
+        self.filter_scaling = np.asarray(filter_scaling, dtype=np.float64)
+        self.clamp = float(clamp_abs)
+        self._dev: dict = {}
+        g = eq.grid
+        self.L = g.modal_shape[-1]
+        self.Lp = (self.L + 3) // 4 * 4
+
+    def _consts(self, device):
+        key = str(device)
+        d = self._dev.get(key)
+        if d is None:
+            c = _consts(self.eq)
+            base = c.on(device)
+            dt = self.dt
+            minv = {e: c.minv(e, device) for e in (dt / 6, dt / 3, dt / 4)}
+            filt = torch.as_tensor(self.filter_scaling, dtype=torch.float32, device=device)
+            g = self.eq.grid
+            oro = self.eq.orography_tendency(device, torch.float32)
+            oro = g.clip_wavenumbers(oro)
+            packed_oro = torch.zeros(self.ch["C"], *g.modal_shape, dtype=torch.float32, device=device)
+            packed_oro[self.n:2 * self.n] = oro
+            d = {"base": base, "minv": minv, "filt": filt, "oro": packed_oro}
+            self._dev[key] = d
+        return d
+
+    def orography_packed(self, device) -> torch.Tensor:
+        return self._consts(device)["oro"]
+
+    def explicit(self, y: torch.Tensor) -> torch.Tensor:
+        from tornado_gcm_b200.ops import spectral
+
+        B = y.shape[0]
+        grid = self.eq.grid
+        lp = self.Lp if y.is_cuda else self.L
+        x_in = spectral.spectral_linear(y, self.pre, out_lpad=lp, grad_lpad=self.L)
+        S_in = self.spec.n_in
+        nodal = _synth_lat(x_in.reshape(B * S_in, *grid.modal_shape), grid)
+        nout = ColumnLatFn.apply(nodal, self.spec, B)
+        modal = _anal_lat(nout, grid).reshape(B, self.spec.n_out, *grid.modal_shape)
+        return spectral.spectral_linear(modal, self.post, out_lpad=self.L, grad_lpad=lp)
+
+    def _meta(self, device, ce, cp, cg, eta, final):
+        d = self._consts(device)
+        return {"consts": d["base"], "minv": d["minv"][eta], "filt": d["filt"] if final else None, "ce": ce,
+                "cp": cp, "cg": cg, "eta": eta, "clamp": self.clamp, "R": float(self.eq.R), "final": int(final),
+                "n": self.n}
+
+    def step_packed(self, y0: torch.Tensor, P: torch.Tensor) -> torch.Tensor:
+        """One substep; ``P`` = packed physics tendency plus the orography term."""
+        dt = self.dt
+        dev = y0.device
+        E0 = self.explicit(y0)
+        y1 = StageFn.apply(y0, P, None, E0, None, None, self._meta(dev, [dt / 3], dt / 3, dt / 6, dt / 6, False))
+        E1 = self.explicit(y1)
+        y2 = StageFn.apply(y0, P, None, E0, E1, None,
+                           self._meta(dev, [dt / 6, dt / 2], dt * (1 / 6 + 1 / 2), dt / 3, dt / 3, False))
+        E2 = self.explicit(y2)
+        y3 = StageFn.apply(y0, P, y2, E0, E1, E2,
+                           self._meta(dev, [dt / 2, -dt / 2, dt], dt, 3 * dt / 8, dt / 4, True))
+        return y3

@@ -65,45 +65,53 @@ def bases(sh, device) -> _Bases:
     return entry[0]
 
 
-def _synth(x3: torch.Tensor, b: _Bases, col_scale=None) -> torch.Tensor:
+def _synth(x3: torch.Tensor, b: _Bases, col_scale=None, lat_major: bool = False) -> torch.Tensor:
+    """Modal (S, M2, L) → nodal; x3 may be a strided view of a row-padded buffer."""
     ops = _ext.require("spherical-harmonic synthesis")
     S = x3.shape[0]
     x3 = x3.float()
-    if b.Lp != b.L:
-        x3 = torch.nn.functional.pad(x3, (0, b.Lp - b.L))
-    x3 = x3.contiguous()
+    ok = (x3.stride(-1) == 1 and (x3.stride(-2) * 4) % 16 == 0 and (x3.stride(0) * 4) % 16 == 0
+          and x3.data_ptr() % 16 == 0)
+    if not ok:
+        x3 = torch.nn.functional.pad(x3, (0, b.Lp - b.L)).contiguous() if b.Lp != b.L else x3.contiguous()
+        if b.Lp != b.L:
+            x3 = x3[..., : b.L]
     ws = torch.empty(S * b.J * b.M2p, dtype=torch.float32, device=x3.device)
-    return ops.sht_synth(x3, b.L, b.P, b.F, ws, col_scale, _ext.error_flag(x3.device))
+    return ops.sht_synth(x3, b.L, b.P, b.F, ws, col_scale, _ext.error_flag(x3.device), lat_major)
 
 
-def _anal(n3: torch.Tensor, b: _Bases, col_scale=None) -> torch.Tensor:
+def _anal(n3: torch.Tensor, b: _Bases, col_scale=None, lat_major: bool = False) -> torch.Tensor:
+    """Nodal (S, I, J) (or (S, J, I) when lat_major) → modal (S, M2, L)."""
     ops = _ext.require("spherical-harmonic analysis")
     S = n3.shape[0]
-    n3 = n3.float().contiguous()
     ws = torch.empty(S * b.M2 * b.J, dtype=torch.float32, device=n3.device)
-    return ops.sht_anal(n3, b.Ft, b.Pt, b.L, ws, col_scale, _ext.error_flag(n3.device))
+    return ops.sht_anal(n3.float(), b.Ft, b.Pt, b.L, ws, col_scale, _ext.error_flag(n3.device), lat_major)
 
 
 class ToNodalFn(torch.autograd.Function):
+    """Synthesis; adjoint = unweighted analysis (same nodal layout)."""
+
     @staticmethod
-    def forward(ctx, x3, b):
-        ctx.b = b
-        return _synth(x3, b)
+    def forward(ctx, x3, b, lat_major=False):
+        ctx.b, ctx.lat_major = b, lat_major
+        return _synth(x3, b, None, lat_major)
 
     @staticmethod
     def backward(ctx, g):
-        return _anal(g, ctx.b), None
+        return _anal(g, ctx.b, None, ctx.lat_major), None, None
 
 
 class ToModalFn(torch.autograd.Function):
+    """Quadrature-weighted analysis; adjoint = w_j ⊙ synthesis."""
+
     @staticmethod
-    def forward(ctx, n3, b):
-        ctx.b = b
-        return _anal(n3, b, b.w)
+    def forward(ctx, n3, b, lat_major=False):
+        ctx.b, ctx.lat_major = b, lat_major
+        return _anal(n3, b, b.w, lat_major)
 
     @staticmethod
     def backward(ctx, g):
-        return _synth(g, ctx.b, ctx.b.w), None
+        return _synth(g, ctx.b, ctx.b.w, ctx.lat_major), None, None
 
 
 def to_nodal(x: torch.Tensor, sh) -> torch.Tensor:
@@ -112,7 +120,7 @@ def to_nodal(x: torch.Tensor, sh) -> torch.Tensor:
         return _highest(x, sh, inverse=True)
     b = bases(sh, x.device)
     lead = x.shape[:-2]
-    out = ToNodalFn.apply(x.reshape(-1, b.M2, b.L).float(), b)
+    out = ToNodalFn.apply(x.reshape(-1, b.M2, b.L).float(), b, False)
     return out.reshape(*lead, b.I, b.J).to(x.dtype)
 
 
@@ -122,8 +130,18 @@ def to_modal(x: torch.Tensor, sh) -> torch.Tensor:
         return _highest(x, sh, inverse=False)
     b = bases(sh, x.device)
     lead = x.shape[:-2]
-    out = ToModalFn.apply(x.reshape(-1, b.I, b.J).float(), b)
+    out = ToModalFn.apply(x.reshape(-1, b.I, b.J).float(), b, False)
     return out.reshape(*lead, b.M2, b.L).to(x.dtype)
+
+
+def to_nodal_lat_major(x3: torch.Tensor, sh) -> torch.Tensor:
+    """(S, 2M-1, L) modal (may be a row-padded view) → (S, J, I) nodal (internal layout)."""
+    return ToNodalFn.apply(x3, bases(sh, x3.device), True)
+
+
+def to_modal_lat_major(n3: torch.Tensor, sh) -> torch.Tensor:
+    """(S, J, I) nodal → (S, 2M-1, L) modal."""
+    return ToModalFn.apply(n3, bases(sh, n3.device), True)
 
 
 def _highest(x, sh, inverse: bool):
