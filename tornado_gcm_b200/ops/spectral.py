@@ -121,11 +121,16 @@ class SpectralLinearFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, recipe: SpectralRecipe, out_lpad: int, grad_lpad: int):
         ctx.recipe, ctx.grad_lpad = recipe, grad_lpad
-        return recipe.apply(x, out_lpad)
+        L = recipe.grid.modal_shape[-1]
+        y = recipe.apply(x, out_lpad)
+        # rows padded to out_lpad (16-byte aligned for TMA); expose the logical L view
+        return y[..., :L] if out_lpad > L else y
 
     @staticmethod
     def backward(ctx, gy):
-        return ctx.recipe.transpose().apply(gy.contiguous(), ctx.grad_lpad), None, None, None
+        L = ctx.recipe.grid.modal_shape[-1]
+        g = ctx.recipe.transpose().apply(gy if gy.stride(-1) == 1 else gy.contiguous(), ctx.grad_lpad)
+        return (g[..., :L] if ctx.grad_lpad > L else g), None, None, None
 
 
 def spectral_linear(x: torch.Tensor, recipe: SpectralRecipe, out_lpad: Optional[int] = None,
