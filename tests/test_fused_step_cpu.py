@@ -127,3 +127,40 @@ def test_packed_sil3_matches_fused_values_and_grads():
     g_ref = torch.autograd.grad((ref * w).sum(), st_ref.tensors())
     g_ref_packed = torch.cat([g_ref[0], g_ref[1], g_ref[2], g_ref[3]] + list(g_ref[4:]), dim=-3)
     torch.testing.assert_close(gy, g_ref_packed, rtol=3e-3, atol=1e-5)
+
+
+def test_packed_parameterization_matches_state_path():
+    from tornado_gcm_b200.neural.parameterizations import NodalColumnParameterization
+    from tornado_gcm_b200.neural.standard_layers import MlpUniform
+    from tornado_gcm_b200.neural.towers import ForwardTower
+    from tornado_gcm_b200.ops import spectral
+
+    eq, st, _ = _setup()
+    g, n = eq.grid, 5
+    st.tracers["specific_cloud_ice_water_content"] = st.tracers["specific_humidity"] * 0.1
+    keys = tuple(sorted(st.tracers))
+    pkeys = ("specific_humidity",)  # the network sees a subset of the state tracers
+    fk = ("orography", "sea_surface_temperature")
+    torch.manual_seed(0)
+    n_in = n * (3 + len(pkeys)) + 1 + len(fk)
+    n_out = n * (3 + len(pkeys)) + 1
+    tower = ForwardTower(MlpUniform(n_in, n_out, hidden_size=16, n_hidden_layers=2))
+    p = NodalColumnParameterization(g, n, pkeys, tower, forcing_keys=fk, output_scale=torch.rand(n_out),
+                                    input_scale=torch.rand(n_in), compute_dtype=torch.float32)
+    forc = {k: torch.randn(2, *g.nodal_shape) for k in fk}
+    ref = spectral.pack_state(p(st, forcings=forc), keys)
+    y = spectral.pack_state(st, keys).requires_grad_(True)
+    out = p.forward_packed(y, keys, forc)
+    torch.testing.assert_close(out, ref, rtol=2e-4, atol=1e-7)
+    w = torch.randn_like(out)
+    (gy,) = torch.autograd.grad((out * w).sum(), y)
+    st_leaves = [t.detach().clone().requires_grad_(True) for t in (st.vorticity, st.divergence,
+                                                                    st.temperature_variation,
+                                                                    st.log_surface_pressure)]
+    trs = {k: st.tracers[k].detach().clone().requires_grad_(True) for k in keys}
+    st2 = pe.State(*st_leaves, trs, 0.0)
+    ref2 = spectral.pack_state(p(st2, forcings=forc), keys)
+    gref = torch.autograd.grad((ref2 * w).sum(), st_leaves + [trs[k] for k in keys], allow_unused=True)
+    gref = torch.cat([x if x is not None else torch.zeros_like(t)
+                      for x, t in zip(gref, st_leaves + [trs[k] for k in keys])], dim=-3)
+    torch.testing.assert_close(gy, gref, rtol=2e-3, atol=1e-6)

@@ -195,6 +195,20 @@ class NeuralGCMModel(nn.Module):
             self.monitor.audit_zone_transfer("Z3_to_Z1", tend.vorticity, out.vorticity)
         return out
 
+    def _packed_parameterization(self, state: State, y: torch.Tensor, keys: tuple, forcings, memory):
+        """Physics tendency in the packed layout of ``y``.
+
+        Parameterizations with a ``forward_packed`` method stay in the packed
+        layout end to end; others run on the :class:`State` and are packed.
+        """
+        p = self.parameterization
+        z1 = self.policy.compute_dtype(PrecisionZone.Z1_DYNAMICS_CORE)
+        if p is not None and hasattr(p, "forward_packed") and self.monitor is None and y.ndim == 4:
+            return p.forward_packed(y, keys, forcings).to(z1)
+        from tornado_gcm_b200.ops import spectral
+
+        return spectral.pack_state(self._apply_parameterization(state, forcings=forcings, memory=memory), keys)
+
     def _apply_conservation_fix(self, state: State, before: State) -> State:
         if self.conservation_fixer is None:
             return state
@@ -290,17 +304,22 @@ class NeuralGCMModel(nn.Module):
         before = state
         if self.forcing_fn is not None and forcings is not None:
             forcings = self.forcing_fn(forcings, state.sim_time if state.sim_time is not None else 0.0)
-        with record_function("Z3_neural_net"):
-            phys = self._apply_parameterization(state, forcings=forcings, memory=memory)
+        fused = self._dycore is not None and self._use_fused(state)
+        if fused:
+            from tornado_gcm_b200.ops import spectral
+
+            keys = tuple(sorted(state.tracers))
+            stepper = self._fused_stepper(keys)
+            y = spectral.pack_state(state, keys)
+            with record_function("Z3_neural_net"):
+                P = self._packed_parameterization(state, y, keys, forcings, memory)
+        else:
+            with record_function("Z3_neural_net"):
+                phys = self._apply_parameterization(state, forcings=forcings, memory=memory)
         if self._dycore is not None:
             with record_function("Z1_dycore"):
-                if self._use_fused(state):
-                    from tornado_gcm_b200.ops import spectral
-
-                    keys = tuple(sorted(state.tracers))
-                    stepper = self._fused_stepper(keys)
-                    y = spectral.pack_state(state, keys)
-                    P = spectral.pack_state(phys, keys) + stepper.orography_packed(y.device)
+                if fused:
+                    P = P + stepper.orography_packed(y.device)
                     for _ in range(self.config.dycore_substeps):
                         if self.config.checkpoint_inner_steps and self.training:
                             y = torch_checkpoint.checkpoint(stepper.step_packed, y, P, use_reentrant=False)

@@ -189,6 +189,67 @@ class NodalColumnParameterization(nn.Module):
         y = self.tower((x * self.input_scale).to(self.compute_dtype)).to(state.vorticity.dtype) * self.output_scale
         return self.nodal_tendency_to_modal(y, state)
 
+    # ── packed path (lat-major nodal, table-driven spectral operators) ──────
+    def _packed_recipes(self, state_keys: tuple):
+        cache = self.__dict__.setdefault("_recipes", {})
+        r = cache.get(state_keys)
+        if r is None:
+            from tornado_gcm_b200.ops import spectral
+
+            r = (spectral.param_pre_recipe(self.grid, self.n_levels, state_keys, self.tracer_keys),
+                 spectral.param_post_recipe(self.grid, self.n_levels, state_keys, self.tracer_keys))
+            cache[state_keys] = r
+        return r
+
+    def _lat_factors(self, device, dtype):
+        """Per-channel × per-latitude input and output factors, (C, J, 1) each."""
+        n = self.n_levels
+        sec = (1.0 / self.grid.const("cos_lat", device, dtype)).reshape(-1, 1)  # (J, 1)
+        cin = self.n_outputs
+        fin = self.input_scale[:cin].to(device, dtype).expand(cin, sec.shape[0], 1).clone()
+        fin[: 2 * n] = fin[: 2 * n] * sec
+        fout = self.output_scale.to(device, dtype).expand(cin, sec.shape[0], 1).clone()
+        fout[: 2 * n] = fout[: 2 * n] * sec
+        return fin, fout
+
+    def forward_packed(self, y: torch.Tensor, state_keys, forcings=None) -> torch.Tensor:
+        """Packed state ``(B, C, 2M-1, L)`` → packed tendency of the same layout.
+
+        Same mathematics as :meth:`forward` with the spectral pre/post work in
+        two table-driven kernels and the nodal fields kept latitude-major
+        ``(B, C, J, I)`` between the transforms (the column network is
+        pointwise, so its layout does not matter).
+        """
+        from tornado_gcm_b200.ops import dycore as dyops, spectral
+
+        state_keys = tuple(state_keys)
+        g = self.grid
+        M2, L = g.modal_shape
+        I, J = g.nodal_shape
+        B = y.shape[0]
+        pre, post = self._packed_recipes(state_keys)
+        lp = (L + 3) // 4 * 4 if y.is_cuda else L
+        xm = spectral.spectral_linear(y, pre, out_lpad=lp, grad_lpad=L)
+        C = self.n_outputs
+        nod = dyops._synth_lat(xm.reshape(B * C, M2, L), g).reshape(B, C, J, I)
+        fin, fout = self._lat_factors(y.device, nod.dtype)
+        x = nod * fin
+        if self.forcing_keys:
+            like = y.new_empty((1, 1, I, J))
+            extra = _forcing_channels(forcings, like, (B,), self.forcing_keys)
+            nf = len(self.forcing_keys)
+            if extra:
+                f = torch.cat(extra, dim=-3).transpose(-1, -2)
+                x = torch.cat([x, f * self.input_scale[C:].to(f.dtype)], dim=-3)
+            else:
+                x = torch.cat([x, x.new_zeros(B, nf, J, I)], dim=-3)
+        out = self.tower(x.to(self.compute_dtype)).to(nod.dtype) * fout
+        modal = dyops._anal_lat(out.reshape(B * C, J, I), g).reshape(B, C, M2, L)
+        res = spectral.spectral_linear(modal, post, out_lpad=L, grad_lpad=lp)
+        if self.filter_fn is not None:
+            res = self.filter_fn(res)
+        return res
+
     def nodal_tendency_to_modal(self, y: torch.Tensor, state: State) -> State:
         g = self.grid
         n = self.n_levels

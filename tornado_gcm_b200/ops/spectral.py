@@ -275,3 +275,58 @@ def unpack_state(packed: torch.Tensor, n: int, tracer_keys, sim_time=None, extra
     if extra_tracers:
         tr.update(extra_tracers)
     return State(vort, div, temp, lnps, tr, sim_time)
+
+
+def param_pre_recipe(grid, n: int, state_keys, param_keys) -> SpectralRecipe:
+    """Packed state → modal column-physics inputs ``[cosθ·u | cosθ·v | T' | tracers | ln ps]``.
+
+    ``param_keys`` is the parameterization's tracer order; a tracer missing
+    from ``state_keys`` stays zero (no terms).  The velocity rows are the
+    unclipped cosθ-weighted wind of reference
+    ``core/spherical_harmonic.py`` ``get_cos_lat_vector`` (ψ, χ by inverse
+    Laplacian, then ∂λ and cosθ∂θ).
+    """
+    inv_r = 1.0 / grid.radius
+    b = _Builder(grid, n)
+    ch = packed_channels(n, state_keys)
+    for k in range(n):
+        b.add(k, ch["div"] + k, DLON, pre=b.ILAP, coef=inv_r)
+        b.add(k, ch["vort"] + k, CDLAT, pre=b.ILAP, coef=-inv_r)
+        b.add(n + k, ch["div"] + k, CDLAT, pre=b.ILAP, coef=inv_r)
+        b.add(n + k, ch["vort"] + k, DLON, pre=b.ILAP, coef=inv_r)
+        b.add(2 * n + k, ch["temp"] + k)
+    s = 3 * n
+    for key in param_keys:
+        if ("tr:" + key) in ch:
+            for k in range(n):
+                b.add(s + k, ch["tr:" + key] + k)
+        s += n
+    b.add(s, ch["lnps"])
+    return b.recipe(ch["C"], s + 1)
+
+
+def param_post_recipe(grid, n: int, state_keys, param_keys) -> SpectralRecipe:
+    """Modal column-physics outputs ``[u/cosθ | v/cosθ | T' | tracers | ln ps]`` → packed tendency.
+
+    ζ and δ tendencies are the clipped curl / divergence of the cosθ-weighted
+    velocity tendency (reference ``neural/parameterizations.py``
+    ``ModalNeuralDivCurlParameterization``); state tracers that the network
+    does not predict get a zero tendency.
+    """
+    inv_r = 1.0 / grid.radius
+    b = _Builder(grid, n)
+    ch = packed_channels(n, state_keys)
+    for k in range(n):
+        b.add(ch["vort"] + k, n + k, DLON, post=b.CLIP, coef=inv_r)
+        b.add(ch["vort"] + k, k, HDLAT, post=b.CLIP, coef=-inv_r)
+        b.add(ch["div"] + k, k, DLON, post=b.CLIP, coef=inv_r)
+        b.add(ch["div"] + k, n + k, HDLAT, post=b.CLIP, coef=inv_r)
+        b.add(ch["temp"] + k, 2 * n + k)
+    s = 3 * n
+    for key in param_keys:
+        if ("tr:" + key) in ch:
+            for k in range(n):
+                b.add(ch["tr:" + key] + k, s + k)
+        s += n
+    b.add(ch["lnps"], s)
+    return b.recipe(s + 1, ch["C"])
