@@ -32,10 +32,29 @@ import torch
 PUBLISHED_STEPS_PER_S = 4.1  # reference README, 2.8° on 1× A100
 METRIC = "model steps/s (train & 6h-forecast) at 2.8°/1.4°/0.7°, 1/2/4/8 B200, vs ref NCCL"
 MY_KERNELS = ("gemm_sm100_kernel", "column_fwd_kernel", "column_vjp_kernel", "implicit_kernel",
-              "fused_allreduce", "fixer_", "tgcm_")
+              "sil3_stage_kernel", "spectral_linear_kernel", "fix_partial_kernel", "fix_apply_kernel",
+              "fix_adjoint_kernel", "fused_allreduce", "tgcm_")
 
 
 # ── helpers ─────────────────────────────────────────────────────────────────
+def write_kernel_table(prof, path: str) -> None:
+    """Per-kernel count and summed device time of one profiled step, largest first."""
+    agg: dict = {}
+    for ev in prof.events():
+        if ev.device_type != torch.autograd.DeviceType.CUDA:
+            continue
+        name = ev.name if len(ev.name) < 110 else ev.name[:107] + "..."
+        c, t = agg.get(name, (0, 0.0))
+        agg[name] = (c + 1, t + ev.device_time_total)
+    total = sum(t for _, t in agg.values()) or 1.0
+    rows = sorted(agg.items(), key=lambda kv: -kv[1][1])
+    with open(path, "w") as fh:
+        fh.write(f"# one eager training step; total device time {total / 1000.0:.2f} ms\n")
+        fh.write("share%  time_ms  count  kernel\n")
+        for name, (c, t) in rows:
+            fh.write(f"{100.0 * t / total:6.2f} {t / 1000.0:8.3f} {c:6d}  {name}\n")
+
+
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
@@ -47,6 +66,9 @@ def parse_args():
     p.add_argument("--rollout", type=int, default=4, help="6-h steps per training example")
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--kernel-table", default=None,
+                   help="write a per-kernel device-time table of one eager step (torch profiler, "
+                        "outside the timed region) to this path")
     return p.parse_args()
 
 
@@ -259,6 +281,8 @@ def run_b200(args, rank, world):
                 if any(k in ev.name for k in MY_KERNELS):
                     n_mine += 1
         launches = {"per_step_mine": n_mine, "per_step_all": n_all}
+        if args.kernel_table and rank == 0:
+            write_kernel_table(prof, args.kernel_table)
     except Exception as exc:  # pragma: no cover
         launches = {"error": str(exc)}
 

@@ -47,6 +47,7 @@ def ref():
 
     r = _Ref()
     r.__dict__.update(mods)
+    r.import_module = importlib.import_module
     return r
 
 

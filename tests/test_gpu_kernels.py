@@ -199,3 +199,24 @@ def test_model_train_step_finite():
     l2 = tr.train_step(x0, tg, forc)
     assert torch.isfinite(l1) and torch.isfinite(l2)
     assert _ext.check_error_flag(dev) == 0
+
+
+def test_packed_fixer_gpu_matches_cpu():
+    _require()
+    from tornado_gcm_b200.ops import fixers as fops
+
+    torch.manual_seed(5)
+    n, C = 8, 8 * 4 + 1
+    y = torch.randn(3, C, 43, 23) * 0.1
+    y[:, 2 * n:3 * n, 0, 0] += 40.0
+    yb = y * 1.001 + 1e-3 * torch.randn_like(y)
+    out_c = fops.packed_fix(y.requires_grad_(True), yb.requires_grad_(True), n)
+    yg = y.detach().to(DEV).requires_grad_(True)
+    ybg = yb.detach().to(DEV).requires_grad_(True)
+    out_g = fops.packed_fix(yg, ybg, n)
+    torch.testing.assert_close(out_g.detach().cpu(), out_c.detach(), rtol=1e-6, atol=1e-6)
+    w = torch.randn_like(out_c)
+    gc = torch.autograd.grad((out_c * w).sum(), [y, yb])
+    gg = torch.autograd.grad((out_g * w.to(DEV)).sum(), [yg, ybg])
+    for a, b in zip(gg, gc):
+        torch.testing.assert_close(a.cpu(), b, rtol=1e-5, atol=1e-6)

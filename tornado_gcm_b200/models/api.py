@@ -305,12 +305,14 @@ class NeuralGCMModel(nn.Module):
         if self.forcing_fn is not None and forcings is not None:
             forcings = self.forcing_fn(forcings, state.sim_time if state.sim_time is not None else 0.0)
         fused = self._dycore is not None and self._use_fused(state)
+        fixed_in_packed = False
         if fused:
             from tornado_gcm_b200.ops import spectral
 
             keys = tuple(sorted(state.tracers))
             stepper = self._fused_stepper(keys)
             y = spectral.pack_state(state, keys)
+            y_start = y
             with record_function("Z3_neural_net"):
                 P = self._packed_parameterization(state, y, keys, forcings, memory)
         else:
@@ -325,6 +327,13 @@ class NeuralGCMModel(nn.Module):
                             y = torch_checkpoint.checkpoint(stepper.step_packed, y, P, use_reentrant=False)
                         else:
                             y = stepper.step_packed(y, P)
+                    self._step_count += 1
+                    fixer = self.conservation_fixer
+                    if (self._step_count % self._fixer_cadence == 0 and fixer is not None
+                            and hasattr(fixer, "forward_packed") and not self._diagnostics_enabled):
+                        with record_function("Z2_physics_bridge"):
+                            y = fixer.forward_packed(y, y_start, self.config.coords.vertical.layers)
+                        fixed_in_packed = True
                     state = spectral.unpack_state(y, self.config.coords.vertical.layers, keys, state.sim_time)
                 else:
                     inner = self._build_inner_step_fn(phys)
@@ -339,8 +348,9 @@ class NeuralGCMModel(nn.Module):
                 state = state + self.config.dt * phys
             with record_function("Z0_spectral"):
                 state = self._filter_state(state)
-        self._step_count += 1
-        if self._step_count % self._fixer_cadence == 0:
+        if not fused:
+            self._step_count += 1
+        if self._step_count % self._fixer_cadence == 0 and not fixed_in_packed:
             with record_function("Z2_physics_bridge"):
                 state = self._apply_conservation_fix(state, before)
         if state.sim_time is not None:

@@ -160,10 +160,11 @@ def build_hybrid_gcm(resolution: str = "2.8deg", device: str | torch.device = "c
                                         output_scale=out_scale, input_scale=in_scale)
     model = NeuralGCMModel(cfg, parameterization=param, conservation_fixer=LiteConservationFixer())
     stats = data.stats()
+    forcing_scale = {"sea_surface_temperature": (288.0, 0.1), "orography": (0.0, 1e-3)}
     enc = ColumnEncoder(coords, t_ref, data.levels, stats, FORCING_FIELDS, hidden=spec.encoder_width,
-                        depth=spec.encoder_hidden_layers)
+                        depth=spec.encoder_hidden_layers, orography_key="orography",
+                        orography_unit_m=1.0 / forcing_scale["orography"][1])
     dec = ColumnDecoder(coords, t_ref, data.levels, stats, hidden=spec.encoder_width,
                         depth=spec.encoder_hidden_layers)
-    forcing_scale = {"sea_surface_temperature": (288.0, 0.1), "orography": (0.0, 1e-3)}
     gcm = HybridGCM(model, enc, dec, spec.physics_steps_per_output, FORCING_FIELDS, forcing_scale)
     return gcm.to(device), data

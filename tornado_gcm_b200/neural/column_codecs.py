@@ -30,6 +30,8 @@ from tornado_gcm_b200.training.synthetic import (DATA_FIELDS, pressure_to_sigma_
                                                  sigma_to_pressure_matrix)
 
 VELOCITY_SCALE = 6.37122e6 * 2 * 7.292e-5  # m/s per model velocity unit (radius · 2Ω)
+_G_SI = 9.80616
+_RD_SI = 1004.0 * 2.0 / 7.0
 TRACERS = ("specific_cloud_ice_water_content", "specific_cloud_liquid_water_content", "specific_humidity")
 _TRACER_OF_FIELD = {"q": "specific_humidity", "clwc": "specific_cloud_liquid_water_content",
                     "ciwc": "specific_cloud_ice_water_content"}
@@ -43,9 +45,12 @@ def _scale_last_layer(mlp: Mlp, factor: float):
 class ColumnEncoder(nn.Module):
     def __init__(self, coords, reference_temperature: np.ndarray, pressure_levels: np.ndarray,
                  data_stats: dict, forcing_keys: Sequence[str], hidden: int = 256, depth: int = 3,
-                 correction_scale: float = 0.1):
+                 correction_scale: float = 0.1, orography_key: str | None = None,
+                 orography_unit_m: float = 1.0):
         super().__init__()
         self.coords = coords
+        self.orography_key = orography_key
+        self.orography_unit_m = float(orography_unit_m)
         self.grid = coords.horizontal
         n = coords.vertical.layers
         npl = len(pressure_levels)
@@ -92,6 +97,12 @@ class ColumnEncoder(nn.Module):
         cl = torch.clamp(interp(self._phys(data, "clwc")) + corr[..., 4 * n:5 * n, :, :], min=0.0)
         ci = torch.clamp(interp(self._phys(data, "ciwc")) + corr[..., 5 * n:6 * n, :, :], min=0.0)
         lnps = corr[..., 6 * n:, :, :]
+        if self.orography_key is not None and forcings is not None and self.orography_key in forcings:
+            # hypsometric prior: ln(ps / p0) = −g z_s / (R_d T_s) with T_s the lowest-level temperature
+            zs = forcings[self.orography_key].to(T.dtype) * self.orography_unit_m
+            while zs.dim() < T.dim():
+                zs = zs.unsqueeze(-3)
+            lnps = lnps - _G_SI * zs / (_RD_SI * T[..., -1:, :, :])
         g = self.grid
         vort, div = sh.uv_nodal_to_vor_div_modal(g, u / VELOCITY_SCALE, v / VELOCITY_SCALE)
         modal = g.to_modal(torch.cat([T - self.t_ref, q, cl, ci, lnps], dim=-3))

@@ -143,12 +143,17 @@ class LiteConservationFixer(nn.Module):
     def bypass_upcast(self) -> bool:
         return True
 
+    def forward_packed(self, y: torch.Tensor, y_before: torch.Tensor, n: int) -> torch.Tensor:
+        """Fix a packed ``[ζ | δ | T' | ln ps | …]`` state (differentiable kernel pair)."""
+        from tornado_gcm_b200.ops import fixers as fixer_ops
+
+        return fixer_ops.packed_fix(y, y_before, n, self.fix_mass, self.fix_energy)
+
     def forward(self, state: State, state_before: State) -> State:
-        if state.vorticity.is_cuda and not torch.is_grad_enabled():
+        if state.vorticity.is_cuda:
             from tornado_gcm_b200.ops import fixers as fixer_ops
 
-            if fixer_ops.available():
-                return fixer_ops.lite_fix(state, state_before, self.fix_mass, self.fix_energy)
+            return fixer_ops.lite_fix(state, state_before, self.fix_mass, self.fix_energy)
         if self.fix_mass:
             state = _mass_fix(state, state_before)
         if self.fix_energy:

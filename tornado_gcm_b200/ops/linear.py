@@ -10,6 +10,8 @@ BF16 copies are refreshed when a parameter's version changes.
 
 from __future__ import annotations
 
+import weakref
+
 import torch
 import torch.nn as nn
 
@@ -49,15 +51,17 @@ class _WeightCache:
         key = id(lin)
         ver = (w._version, w.data_ptr(), str(w.device))
         ent = self.store.get(key)
+        if ent is not None and ent[3]() is not lin:
+            ent = None  # the id belonged to a module that no longer exists
         if ent is not None and ent[0] == ver and ent[1] == self.token:
             return ent[2]
-        if ent is None or ent[2].device != w.device:
-            O, K = w.shape
+        O, K = w.shape
+        if ent is None or ent[2].device != w.device or ent[2].shape != (_pad8(O), _pad8(K)):
             buf = torch.zeros(_pad8(O), _pad8(K), dtype=torch.bfloat16, device=w.device)
         else:
             buf = ent[2]
-        buf[: w.shape[0], : w.shape[1]].copy_(w.detach())
-        self.store[key] = (ver, self.token, buf)
+        buf[:O, :K].copy_(w.detach())
+        self.store[key] = (ver, self.token, buf, weakref.ref(lin))
         return buf
 
 

@@ -4,11 +4,12 @@ Fields follow the benchmark specification: each field is a level-mean
 profile plus noise band-limited to total wavenumber ≤ 21 (generated in
 spectral space and synthesised on the grid):
 
-* T: 200–300 K profile, noise σ = 5 K;  u, v: N(0, 10 m/s);
+* T: 200–300 K profile, noise σ = 5 K;  u, v: 10 m/s rms, mostly rotational
+  (divergence 10 % of vorticity in spectral amplitude);
 * q: lognormal in (0, 0.02] kg/kg;  z: hydrostatic 0–4.8e5 m²/s²;
 * cloud liquid / ice: lognormal ≤ 1e-4;
-* forcings: SST 271–305 K, sea ice U[0, 1], smooth orography 0–5 km,
-  binary land mask.
+* forcings: SST 271–305 K, sea ice U[0, 1], orography 0–5 km rising from
+  0 at the coast of the binary land mask.
 
 Everything is deterministic given the seed.  Fields are returned in
 physical units on ``(..., levels, lon, lat)`` nodal grids, plus
@@ -44,6 +45,32 @@ def band_limited_noise(grid: Grid, n_fields: int, lmax: int, rng: np.random.Gene
     return nodal / std
 
 
+def rotational_winds(grid: Grid, n_fields: int, lmax: int, rng: np.random.Generator, batch: int = 1,
+                     speed: float = 10.0, divergent_fraction: float = 0.1) -> tuple[np.ndarray, np.ndarray]:
+    """Band-limited (u, v) that are mostly rotational, like the real atmosphere.
+
+    Vorticity and divergence are drawn in spectral space (support
+    ``1 ≤ l ≤ lmax``, divergence ``divergent_fraction`` as large), turned into
+    winds through the stream function and velocity potential, and scaled so
+    each level's wind components have standard deviation ``speed``.
+    Independent u and v noise would carry as much divergence as vorticity,
+    which excites gravity waves far beyond observed amplitudes.
+    """
+    from tornado_gcm_b200.core.spherical_harmonic import get_cos_lat_vector
+
+    g = grid.with_precision("highest")
+    m, l = g.modal_mesh
+    amp = np.where(g.mask & (l <= lmax) & (l > 0), 1.0, 0.0)
+    zeta = torch.as_tensor(rng.standard_normal((batch, n_fields) + g.modal_shape) * amp)
+    delta = torch.as_tensor(rng.standard_normal((batch, n_fields) + g.modal_shape) * amp * divergent_fraction)
+    uc, vc = get_cos_lat_vector(zeta, delta, g, clip=False)
+    cos = torch.as_tensor(np.cos(g.latitudes))
+    u = (g.to_nodal(uc) / cos).numpy()
+    v = (g.to_nodal(vc) / cos).numpy()
+    rms = np.sqrt(0.5 * (u ** 2 + v ** 2).mean(axis=(-2, -1), keepdims=True)) + 1e-12
+    return speed * u / rms, speed * v / rms
+
+
 @dataclasses.dataclass
 class SyntheticReanalysis:
     """Generator of pressure-level data and forcings on a grid."""
@@ -68,9 +95,10 @@ class SyntheticReanalysis:
         t_mean, q_mean, z_mean, cl_mean, ci_mean = self._profiles()
         noise = lambda: band_limited_noise(self.grid, nl, self.lmax, rng, batch)
         sh = (1, nl, 1, 1)
+        u, v = rotational_winds(self.grid, nl, self.lmax, rng, batch, speed=10.0, divergent_fraction=0.1)
         out = {
-            "u": 10.0 * noise(),
-            "v": 10.0 * noise(),
+            "u": u,
+            "v": v,
             "t": np.clip(t_mean.reshape(sh) + 5.0 * noise(), 180.0, 320.0),
             "q": np.minimum(q_mean.reshape(sh) * np.exp(0.3 * noise()), 0.02),
             "z": z_mean.reshape(sh) + 2.0e3 * noise(),
@@ -85,8 +113,10 @@ class SyntheticReanalysis:
         n1 = lambda: band_limited_noise(self.grid, 1, 10, rng, 1)[:, 0]
         sst = 271.0 + 34.0 * np.cos(lat)[None, None, :] ** 2 + 0.0 * n1()
         ice = np.clip(0.5 + 0.5 * n1(), 0.0, 1.0)
-        oro = np.clip(5.0e3 * (0.5 + 0.3 * n1()), 0.0, 5.0e3)
-        land = (n1() > 0.3).astype(np.float64)
+        relief = n1()
+        # continents where the relief field exceeds 0.3; height grows from 0 at the coast, ≤ 5 km
+        oro = np.clip(2.5e3 * (relief - 0.3), 0.0, 5.0e3)
+        land = (relief > 0.3).astype(np.float64)
         f = {"sea_surface_temperature": sst, "sea_ice_cover": ice, "orography": oro, "land_sea_mask": land}
         return {k: torch.as_tensor(np.broadcast_to(v, (batch,) + self.grid.nodal_shape).copy(), dtype=torch.float32)
                 for k, v in f.items()}
