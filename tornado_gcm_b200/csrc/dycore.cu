@@ -68,6 +68,7 @@ __global__ void column_fwd_kernel(ColumnConsts c, SliceIndex ix, const float* __
   column_forward(c, ix, rd, wr, sec2[j], cor[j]);
 }
 
+template <int MAXL, int MAXT>
 __global__ void column_vjp_kernel(ColumnConsts c, SliceIndex ix, const float* __restrict__ in,
                                   const float* __restrict__ gout, float* __restrict__ gin,
                                   const float* __restrict__ sec2, const float* __restrict__ cor, int B, int I,
@@ -84,7 +85,7 @@ __global__ void column_vjp_kernel(ColumnConsts c, SliceIndex ix, const float* __
   auto rd = [ib, plane](int q) -> float { return __ldg(ib + q * plane); };
   auto rg = [gb, plane](int q) -> float { return __ldg(gb + q * plane); };
   auto wg = [gib, plane](int q, float v) { gib[q * plane] = v; };
-  column_vjp(c, ix, rd, rg, wg, sec2[j], cor[j]);
+  column_vjp<MAXL, MAXT>(c, ix, rd, rg, wg, sec2[j], cor[j]);
 }
 
 static void check_nodal(const at::Tensor& t, const char* name) {
@@ -146,9 +147,17 @@ at::Tensor column_vjp_op(const at::Tensor& nin, const at::Tensor& gout, const at
     c10::cuda::CUDAGuard guard(nin.device());
     const long long total = batch * I * J;
     const int threads = 64;
-    column_vjp_kernel<<<(total + threads - 1) / threads, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
-        c, ix, nin.data_ptr<float>(), gout.data_ptr<float>(), gin.data_ptr<float>(), s2.data_ptr<float>(),
-        co.data_ptr<float>(), static_cast<int>(batch), static_cast<int>(I), static_cast<int>(J), lat_major ? 1 : 0);
+    const unsigned blocks = static_cast<unsigned>((total + threads - 1) / threads);
+    auto st = at::cuda::getCurrentCUDAStream();
+    const int bi = static_cast<int>(batch), ii = static_cast<int>(I), jj = static_cast<int>(J), lm = lat_major ? 1 : 0;
+    if (n <= 32 && nt <= 4)
+      column_vjp_kernel<32, 4><<<blocks, threads, 0, st>>>(c, ix, nin.data_ptr<float>(), gout.data_ptr<float>(),
+                                                             gin.data_ptr<float>(), s2.data_ptr<float>(),
+                                                             co.data_ptr<float>(), bi, ii, jj, lm);
+    else
+      column_vjp_kernel<kMaxLevels, kMaxTracers><<<blocks, threads, 0, st>>>(
+          c, ix, nin.data_ptr<float>(), gout.data_ptr<float>(), gin.data_ptr<float>(), s2.data_ptr<float>(),
+          co.data_ptr<float>(), bi, ii, jj, lm);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   } else {
     const float* in = nin.data_ptr<float>();

@@ -156,7 +156,10 @@ __host__ __device__ void column_forward(const ColumnConsts& c, const SliceIndex&
 // `gin(q, v)` accumulates v into the cotangent of input slice q (each input
 // slice of the column is written exactly once at the end: the function
 // keeps the accumulators in local arrays and calls gin once per slice).
-template <typename In, typename GOut, typename GIn>
+// MAXL / MAXT bound the per-column scratch arrays (levels / tracers); the GPU
+// launches the smallest instantiation that fits, which keeps the thread's
+// local-memory footprint proportional to the actual column.
+template <int MAXL = kMaxLevels, int MAXT = kMaxTracers, typename In, typename GOut, typename GIn>
 __host__ __device__ void column_vjp(const ColumnConsts& c, const SliceIndex& ix, In in, GOut gout, GIn gin,
                                     float s2, float fcor) {
   const int n = c.n;
@@ -169,7 +172,7 @@ __host__ __device__ void column_vjp(const ColumnConsts& c, const SliceIndex& ix,
     FF += (in(ix.div + k) + A) * c.dsig[k];
   }
   // forward-sweep quantities needed in reverse: prefix sums and sigma-dot
-  float fe[kMaxLevels], ff[kMaxLevels], sf[kMaxLevels], se[kMaxLevels];
+  float fe[MAXL], ff[MAXL], sf[MAXL], se[MAXL];
   {
     float a = 0.f, b = 0.f;
     for (int k = 0; k < n; ++k) {
@@ -183,10 +186,10 @@ __host__ __device__ void column_vjp(const ColumnConsts& c, const SliceIndex& ix,
     }
   }
   // cotangent accumulators
-  float g_u[kMaxLevels], g_v[kMaxLevels], g_T[kMaxLevels], g_div[kMaxLevels], g_vort[kMaxLevels];
-  float g_A[kMaxLevels], g_fe[kMaxLevels], g_ff[kMaxLevels], g_sf[kMaxLevels], g_se[kMaxLevels];
-  float g_tr[kMaxTracers][kMaxLevels];
-  float g_qx[kMaxLevels], g_qy[kMaxLevels];
+  float g_u[MAXL], g_v[MAXL], g_T[MAXL], g_div[MAXL], g_vort[MAXL];
+  float g_A[MAXL], g_fe[MAXL], g_ff[MAXL], g_sf[MAXL], g_se[MAXL];
+  float g_tr[MAXT][MAXL];
+  float g_qx[MAXL], g_qy[MAXL];
   for (int k = 0; k < n; ++k) {
     g_u[k] = g_v[k] = g_T[k] = g_div[k] = g_vort[k] = 0.f;
     g_A[k] = g_fe[k] = g_ff[k] = g_sf[k] = g_se[k] = 0.f;

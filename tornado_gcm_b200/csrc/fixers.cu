@@ -286,9 +286,93 @@ std::vector<at::Tensor> packed_fix_adjoint(const at::Tensor& gout, const at::Ten
   return {g_y, g_yb};
 }
 
+// ── FP64 reductions (one block per row, fixed order: deterministic) ─────────
+// sphere_integrate: out[b] = Σ_{i,j} w[j] · z[b, i, j]   (z (B, I, J), w (J))
+// sum_squares:      out[b] = Σ_k x[b, k]²                 (x (B, N))
+namespace {
+
+constexpr int kRedThreads = 512;
+
+template <typename T>
+__global__ void __launch_bounds__(kRedThreads) row_reduce_kernel(const T* __restrict__ x, const double* __restrict__ w,
+                                                               long long n, long long inner, double* out) {
+  __shared__ double sh[kRedThreads / 32];
+  const int b = blockIdx.x;
+  const T* row = x + b * n;
+  double s = 0.0;
+  for (long long i = threadIdx.x; i < n; i += kRedThreads) {
+    const double v = static_cast<double>(row[i]);
+    s += w ? w[i % inner] * v : v * v;
+  }
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_down_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double r = 0.0;
+    for (int i = 0; i < kRedThreads / 32; ++i) r += sh[i];
+    out[b] = r;
+  }
+}
+
+at::Tensor row_reduce(const at::Tensor& x2, const c10::optional<at::Tensor>& w, int64_t inner) {
+  TORCH_CHECK(x2.dim() == 2 && x2.is_contiguous(), "row_reduce: contiguous (B, N) input");
+  TORCH_CHECK(x2.scalar_type() == at::kFloat || x2.scalar_type() == at::kDouble, "row_reduce: fp32/fp64 input");
+  const int64_t B = x2.size(0), N = x2.size(1);
+  auto out = at::empty({B}, x2.options().dtype(at::kDouble));
+  at::Tensor wd;
+  if (w.has_value() && w->defined()) {
+    wd = w->to(x2.device(), at::kDouble).contiguous();
+    TORCH_CHECK(wd.numel() == inner && N % inner == 0, "row_reduce: weight length must divide the row");
+  }
+  if (B == 0) return out;
+  if (x2.is_cuda()) {
+    c10::cuda::CUDAGuard guard(x2.device());
+    auto st = at::cuda::getCurrentCUDAStream();
+    const double* wp = wd.defined() ? wd.data_ptr<double>() : nullptr;
+    if (x2.scalar_type() == at::kFloat)
+      row_reduce_kernel<float><<<B, kRedThreads, 0, st>>>(x2.data_ptr<float>(), wp, N, inner, out.data_ptr<double>());
+    else
+      row_reduce_kernel<double><<<B, kRedThreads, 0, st>>>(x2.data_ptr<double>(), wp, N, inner, out.data_ptr<double>());
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  } else {
+    auto xd = x2.to(at::kDouble);
+    const double* xp = xd.data_ptr<double>();
+    const double* wp = wd.defined() ? wd.data_ptr<double>() : nullptr;
+    for (int64_t b = 0; b < B; ++b) {
+      double s = 0.0;
+      for (int64_t i = 0; i < N; ++i) {
+        const double v = xp[b * N + i];
+        s += wp ? wp[i % inner] * v : v * v;
+      }
+      out.data_ptr<double>()[b] = s;
+    }
+  }
+  return out;
+}
+
+}  // namespace
+
+at::Tensor sphere_integrate(const at::Tensor& z, const at::Tensor& w) {
+  TORCH_CHECK(z.dim() >= 2 && w.dim() == 1 && w.size(0) == z.size(-1), "sphere_integrate: z (..., I, J), w (J)");
+  auto lead = z.sizes().slice(0, z.dim() - 2).vec();
+  auto x2 = z.reshape({-1, z.size(-2) * z.size(-1)}).contiguous();
+  return row_reduce(x2, w, z.size(-1)).reshape(lead);
+}
+
+at::Tensor sum_squares(const at::Tensor& x, int64_t n_trailing) {
+  TORCH_CHECK(n_trailing >= 1 && n_trailing <= x.dim(), "sum_squares: bad trailing dim count");
+  auto lead = x.sizes().slice(0, x.dim() - n_trailing).vec();
+  int64_t n = 1;
+  for (int64_t d = x.dim() - n_trailing; d < x.dim(); ++d) n *= x.size(d);
+  auto x2 = x.reshape({-1, n}).contiguous();
+  return row_reduce(x2, c10::nullopt, 1).reshape(lead);
+}
+
 }  // namespace tgcm
 
 TORCH_LIBRARY_FRAGMENT(tgcm, m) {
+  m.def("sphere_integrate(Tensor z, Tensor w) -> Tensor");
+  m.def("sum_squares(Tensor x, int n_trailing) -> Tensor");
   m.def("packed_fix(Tensor y, Tensor y_before, int n, bool fix_mass, bool fix_energy) -> Tensor[]");
   m.def("packed_fix_adjoint(Tensor gout, Tensor y, Tensor y_before, Tensor part, int n, bool fix_mass, "
         "bool fix_energy, bool need_before) -> Tensor[]");
@@ -297,4 +381,6 @@ TORCH_LIBRARY_FRAGMENT(tgcm, m) {
 TORCH_LIBRARY_IMPL(tgcm, CompositeExplicitAutograd, m) {
   m.impl("packed_fix", &tgcm::packed_fix);
   m.impl("packed_fix_adjoint", &tgcm::packed_fix_adjoint);
+  m.impl("sphere_integrate", &tgcm::sphere_integrate);
+  m.impl("sum_squares", &tgcm::sum_squares);
 }

@@ -98,13 +98,23 @@ static void launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmP
   constexpr int ST = StagesFor<BN>::value;
   using S = GemmSmem<FMT, BN, ST>;
   auto kern = gemm_sm100_kernel<FMT, BN, ST, A_MN, B_MN>;
-  static bool attr_set = false;
-  if (!attr_set) {
+  static bool attr_set[64] = {false};
+  int cur = 0;
+  cudaGetDevice(&cur);
+  if (cur >= 64 || !attr_set[cur]) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
-    attr_set = true;
+    if (cur < 64) attr_set[cur] = true;
   }
-  dim3 grid(p.tiles_n, p.tiles_m * p.groups, p.k_splits);
-  kern<<<grid, 192, S::kTotal, stream>>>(ta, tb, p);
+  // persistent launch: at most one CTA per SM, each walking tiles with stride gridDim.x
+  static int sms[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && sms[dev] == 0) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  const int n_sm = (dev < 64 && sms[dev] > 0) ? sms[dev] : 148;
+  const int tiles = gemm_total_tiles(p);
+  if (tiles == 0) return;
+  dim3 grid(tiles < n_sm ? tiles : n_sm);
+  kern<<<grid, kGemmThreads, S::kTotal, stream>>>(ta, tb, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("tgcm gemm launch: ") + cudaGetErrorString(e));
 }
@@ -314,9 +324,40 @@ void linear_wgrad(const at::Tensor& dY, const at::Tensor& X, at::Tensor& dW, int
   gemm_dispatch(1, bn, true, true, ta, tb, p, at::cuda::getCurrentCUDAStream());
 }
 
+// ── batched TF32 GEMM ───────────────────────────────────────────────────────
+// C[g] (M x N) = alpha * A[g] (M x K) . B[g] (N x K)^T, fp32 data read as TF32.
+// A (G, M, K) and B (G, N, K) may be strided views: last dim contiguous, the
+// other two strides multiples of 4 elements, base 16-byte aligned.  C is any
+// (G, M, N) fp32 view (the epilogue stores through its strides).
+void bgemm_tf32(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, double alpha,
+                const c10::optional<at::Tensor>& err) {
+  TORCH_CHECK(A.dim() == 3 && B.dim() == 3 && C.dim() == 3, "bgemm_tf32 expects 3-D operands");
+  TORCH_CHECK(A.scalar_type() == at::kFloat && B.scalar_type() == at::kFloat && C.scalar_type() == at::kFloat,
+              "bgemm_tf32 expects fp32 operands");
+  const int64_t G = A.size(0), M = A.size(1), K = A.size(2), N = B.size(1);
+  TORCH_CHECK(B.size(0) == G && B.size(2) == K && C.size(0) == G && C.size(1) == M && C.size(2) == N,
+              "bgemm_tf32 shape mismatch");
+  TORCH_CHECK(A.stride(2) == 1 && B.stride(2) == 1, "bgemm_tf32: K must be the contiguous dim");
+  TORCH_CHECK(A.stride(1) % 4 == 0 && A.stride(0) % 4 == 0 && B.stride(1) % 4 == 0 && B.stride(0) % 4 == 0,
+              "bgemm_tf32: operand strides must be multiples of 4 elements");
+  c10::cuda::CUDAGuard guard(A.device());
+  const int bn = N <= 64 ? 64 : (N <= 128 ? 128 : 256);
+  CUtensorMap ta = make_tmap(A.data_ptr(), 2, K, M, G, A.stride(1) * 4, A.stride(0) * 4, 32, 128, 1);
+  CUtensorMap tb = make_tmap(B.data_ptr(), 2, K, N, G, B.stride(1) * 4, B.stride(0) * 4, 32, bn, 1);
+  GemmParams p = default_params();
+  p.M = static_cast<int>(M); p.N = static_cast<int>(N); p.K = static_cast<int>(K);
+  p.groups = static_cast<int>(G);
+  p.tiles_m = static_cast<int>(cdiv(M, 128)); p.tiles_n = static_cast<int>(cdiv(N, bn));
+  p.alpha = static_cast<float>(alpha);
+  p.C = C.data_ptr(); p.c_sg = C.stride(0); p.c_sr = C.stride(1); p.c_sc = C.stride(2);
+  p.err = err_ptr(err);
+  gemm_dispatch(2, bn, false, false, ta, tb, p, at::cuda::getCurrentCUDAStream());
+}
+
 }  // namespace tgcm
 
 TORCH_LIBRARY_FRAGMENT(tgcm, m) {
+  m.def("bgemm_tf32(Tensor A, Tensor B, Tensor(a!) C, float alpha, Tensor? err) -> ()");
   m.def("sht_synth(Tensor x, int L, Tensor P, Tensor F, Tensor ws, Tensor? col_scale, Tensor? err, bool lat_major) -> Tensor");
   m.def("sht_anal(Tensor N, Tensor Ft, Tensor Pt, int Lo, Tensor ws, Tensor? col_scale, Tensor? err, bool lat_major) -> Tensor");
   m.def("linear_fwd(Tensor X, Tensor W, Tensor? bias, int act, Tensor(a!) out, Tensor? aux, Tensor? err) -> ()");
@@ -330,4 +371,5 @@ TORCH_LIBRARY_IMPL(tgcm, CUDA, m) {
   m.impl("linear_fwd", &tgcm::linear_fwd);
   m.impl("linear_dgrad", &tgcm::linear_dgrad);
   m.impl("linear_wgrad", &tgcm::linear_wgrad);
+  m.impl("bgemm_tf32", &tgcm::bgemm_tf32);
 }

@@ -73,8 +73,9 @@ struct GemmSmem {
   static constexpr int kA = 128 * 128;        // bytes per A stage
   static constexpr int kB = BN * 128;         // bytes per B stage
   static constexpr int kStage = kA + kB;
+  static constexpr int kStaging = 8 * 32 * 33 * 4;  // epilogue transpose tiles (8 warps x 32 x 33 fp32)
   static constexpr int kBars = 1024;          // barrier / bookkeeping area
-  static constexpr int kTotal = STAGES * kStage + kBars + 1024;  // + alignment slack
+  static constexpr int kTotal = STAGES * kStage + kStaging + kBars + 1024;  // + alignment slack
 };
 
 __device__ __forceinline__ void store_out(const GemmParams& p, long long off, float v) {
@@ -93,50 +94,90 @@ __device__ __forceinline__ void store_out(const GemmParams& p, long long off, fl
   }
 }
 
+// 2 control warps (TMA producer, MMA issuer) + 8 epilogue warps.
+constexpr int kGemmThreads = 320;
+constexpr int kEpiWarps = 8;
+
+// Tile t of the launch → (tn, tm, g, split); tn fastest.
+struct TileCoord {
+  int tn, tm, g, split;
+};
+
+__device__ __forceinline__ TileCoord tile_coord(const GemmParams& p, int t) {
+  TileCoord c;
+  c.tn = t % p.tiles_n;
+  int r = t / p.tiles_n;
+  const int mg = p.tiles_m * p.groups;
+  const int y = r % mg;
+  c.split = r / mg;
+  c.tm = y % p.tiles_m;
+  c.g = y / p.tiles_m;
+  return c;
+}
+
+template <int BK>
+__device__ __forceinline__ int tile_kblocks(const GemmParams& p, int g, int split, int* kb0_out, int* kbegin_out) {
+  const int k_begin = p.k_tri ? (g / BK) * BK : 0;
+  int total = (p.K - k_begin + BK - 1) / BK;
+  if (total < 0) total = 0;
+  const int per = (total + p.k_splits - 1) / p.k_splits;
+  const int kb0 = split * per;
+  int kb1 = kb0 + per;
+  if (kb1 > total) kb1 = total;
+  *kb0_out = kb0;
+  *kbegin_out = k_begin;
+  return kb1 > kb0 ? kb1 - kb0 : 0;
+}
+
+__host__ __device__ inline int gemm_total_tiles(const GemmParams& p) {
+  return p.tiles_n * p.tiles_m * p.groups * p.k_splits;
+}
+
+// Persistent kernel: each CTA walks tiles t = blockIdx.x, +gridDim.x, ….
+//   warp 0     TMA producer; runs ahead across tiles through the STAGES ring
+//   warp 1     TMEM owner + MMA issuer; accumulates tile i into TMEM buffer i % 2
+//   warps 2-9  epilogue; drains buffer i % 2 while the MMA fills the other one
+//              (warp % 4 selects the TMEM lane quarter, (warp - 2) / 4 the
+//              half of the column chunks it handles)
+// Barriers: full/empty per ring stage (phase from a CTA-wide k-block
+// counter), tmem_full/tmem_empty per accumulator buffer (phase from the
+// CTA's count of non-empty tiles).
 template <int FMT, int BN, int STAGES, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                       const GemmParams p) {
   using T = FmtTraits<FMT>;
   using S = GemmSmem<FMT, BN, STAGES>;
   constexpr int BK = T::kBK;
   constexpr int CH = 128 / T::kElem;  // elements per 128-byte MN chunk
-  constexpr uint32_t kTmemCols = TmemCols<BN>::value;
+  constexpr uint32_t kAccCols = TmemCols<BN>::value;
+  constexpr uint32_t kTmemCols = 2 * kAccCols;
   constexpr uint32_t kIdesc = make_idesc(FMT, A_MN ? 1 : 0, B_MN ? 1 : 0, 128, BN);
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* bar_area = smem + STAGES * S::kStage;
+  float* staging = reinterpret_cast<float*>(smem + STAGES * S::kStage);
+  uint8_t* bar_area = smem + STAGES * S::kStage + S::kStaging;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(bar_area);
   uint64_t* empty_bar = full_bar + STAGES;
-  uint64_t* tmem_full_bar = empty_bar + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_full_bar + 1);
+  uint64_t* tmem_full_bar = empty_bar + STAGES;   // [2]
+  uint64_t* tmem_empty_bar = tmem_full_bar + 2;   // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-
-  // tile coordinates
-  const int tn = blockIdx.x;
-  const int tm = blockIdx.y % p.tiles_m;
-  const int g = blockIdx.y / p.tiles_m;
-  const int split = blockIdx.z;
-
-  int k_begin = p.k_tri ? (g / BK) * BK : 0;
-  int k_total_blocks = (p.K - k_begin + BK - 1) / BK;
-  if (k_total_blocks < 0) k_total_blocks = 0;
-  const int kb_per_split = (k_total_blocks + p.k_splits - 1) / p.k_splits;
-  const int kb0 = split * kb_per_split;
-  int kb1 = kb0 + kb_per_split;
-  if (kb1 > k_total_blocks) kb1 = k_total_blocks;
-  const int num_kb = kb1 > kb0 ? kb1 - kb0 : 0;
+  const int n_tiles = gemm_total_tiles(p);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(tmem_full_bar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tmem_full_bar[b], 1);
+      mbar_init(&tmem_empty_bar[b], kEpiWarps * 32);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -153,132 +194,220 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (num_kb == 0) {
-    // nothing to accumulate for this split: leave C untouched
-  } else if (warp == 0) {
+  if (warp == 0) {
     if (lane == 0) {
-      const int a_batch = p.a_group_div > 0 ? g / p.a_group_div : 0;
-      const int b_batch = p.b_group_div > 0 ? g / p.b_group_div : 0;
-      const int a_mr = (g == 0) ? 0 : 2 * g - 1;
-      int issued = 0;
-      for (int i = 0; i < num_kb; ++i) {
-        const int s = i % STAGES;
-        const uint32_t ph = (i / STAGES) & 1;
-        if (!mbar_wait(&empty_bar[s], ph ^ 1, p.err, kErrTimeoutEmpty)) {
-          *abort_flag = 1;
-          break;
-        }
-        if (*abort_flag) break;
-        uint8_t* sa = smem + s * S::kStage;
-        uint8_t* sb = sa + S::kA;
-        const int k0 = k_begin + (kb0 + i) * BK;
-        mbar_arrive_expect_tx(&full_bar[s], S::kStage);
-        if (!A_MN) {
-          if (p.a_pair)
-            tma_load_3d(sa, &tmap_a, &full_bar[s], k0, a_mr, tm * 64);
-          else
-            tma_load_3d(sa, &tmap_a, &full_bar[s], k0, tm * 128, a_batch);
-        } else {
+      int kb_global = 0;
+      for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x) {
+        const TileCoord tc = tile_coord(p, t);
+        int kb0, k_begin;
+        const int num_kb = tile_kblocks<BK>(p, tc.g, tc.split, &kb0, &k_begin);
+        const int a_batch = p.a_group_div > 0 ? tc.g / p.a_group_div : 0;
+        const int b_batch = p.b_group_div > 0 ? tc.g / p.b_group_div : 0;
+        const int a_mr = (tc.g == 0) ? 0 : 2 * tc.g - 1;
+        for (int i = 0; i < num_kb; ++i, ++kb_global) {
+          const int s = kb_global % STAGES;
+          const uint32_t ph = (kb_global / STAGES) & 1;
+          if (!mbar_wait(&empty_bar[s], ph ^ 1, p.err, kErrTimeoutEmpty)) {
+            *abort_flag = 1;
+            break;
+          }
+          if (*abort_flag) break;
+          uint8_t* sa = smem + s * S::kStage;
+          uint8_t* sb = sa + S::kA;
+          const int k0 = k_begin + (kb0 + i) * BK;
+          mbar_arrive_expect_tx(&full_bar[s], S::kStage);
+          if (!A_MN) {
+            if (p.a_pair)
+              tma_load_3d(sa, &tmap_a, &full_bar[s], k0, a_mr, tc.tm * 64);
+            else
+              tma_load_3d(sa, &tmap_a, &full_bar[s], k0, tc.tm * 128, a_batch);
+          } else {
 #pragma unroll
-          for (int q = 0; q < 128 / CH; ++q)
-            tma_load_3d(sa + q * BK * 128, &tmap_a, &full_bar[s], tm * 128 + q * CH, k0, a_batch);
-        }
-        if (!B_MN) {
-          tma_load_3d(sb, &tmap_b, &full_bar[s], k0, tn * BN, b_batch);
-        } else {
+            for (int q = 0; q < 128 / CH; ++q)
+              tma_load_3d(sa + q * BK * 128, &tmap_a, &full_bar[s], tc.tm * 128 + q * CH, k0, a_batch);
+          }
+          if (!B_MN) {
+            tma_load_3d(sb, &tmap_b, &full_bar[s], k0, tc.tn * BN, b_batch);
+          } else {
 #pragma unroll
-          for (int q = 0; q < BN / CH; ++q)
-            tma_load_3d(sb + q * BK * 128, &tmap_b, &full_bar[s], tn * BN + q * CH, k0, b_batch);
+            for (int q = 0; q < BN / CH; ++q)
+              tma_load_3d(sb + q * BK * 128, &tmap_b, &full_bar[s], tc.tn * BN + q * CH, k0, b_batch);
+          }
         }
-        ++issued;
       }
-      // drain: make sure every TMA this thread issued has landed before exit
-      for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; ++i) {
+      // drain: every load this thread issued has landed before the CTA exits
+      for (int i = (kb_global > STAGES ? kb_global - STAGES : 0); i < kb_global; ++i)
         mbar_wait(&full_bar[i % STAGES], (i / STAGES) & 1, p.err, kErrTimeoutDrain);
-      }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      bool ok = true;
-      for (int i = 0; i < num_kb; ++i) {
-        const int s = i % STAGES;
-        const uint32_t ph = (i / STAGES) & 1;
-        if (!mbar_wait(&full_bar[s], ph, p.err, kErrTimeoutFull)) {
+      int kb_global = 0, tile_i = 0;
+      for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x) {
+        const TileCoord tc = tile_coord(p, t);
+        int kb0, k_begin;
+        const int num_kb = tile_kblocks<BK>(p, tc.g, tc.split, &kb0, &k_begin);
+        if (num_kb == 0) continue;
+        const int acc = tile_i & 1;
+        const uint32_t use = static_cast<uint32_t>(tile_i >> 1);
+        if (!mbar_wait(&tmem_empty_bar[acc], (use & 1) ^ 1, p.err, kErrTimeoutEmpty)) {
           *abort_flag = 1;
-          ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t sa = smem_u32(smem + s * S::kStage);
-        const uint32_t sb = sa + S::kA;
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc) * kAccCols;
+        for (int i = 0; i < num_kb; ++i, ++kb_global) {
+          const int s = kb_global % STAGES;
+          const uint32_t ph = (kb_global / STAGES) & 1;
+          if (!mbar_wait(&full_bar[s], ph, p.err, kErrTimeoutFull)) {
+            *abort_flag = 1;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * S::kStage);
+          const uint32_t sb = sa + S::kA;
 #pragma unroll
-        for (int k = 0; k < BK / T::kUK; ++k) {
-          uint64_t adesc, bdesc;
-          if (!A_MN)
-            adesc = make_sw128_desc(sa + k * 32, 16, 1024);
-          else
-            adesc = make_sw128_desc(sa + k * T::kUK * 128, BK * 128, 1024);
-          if (!B_MN)
-            bdesc = make_sw128_desc(sb + k * 32, 16, 1024);
-          else
-            bdesc = make_sw128_desc(sb + k * T::kUK * 128, BK * 128, 1024);
-          const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
-          if (FMT == 2)
-            umma_tf32(tmem_base, adesc, bdesc, kIdesc, acc);
-          else
-            umma_bf16(tmem_base, adesc, bdesc, kIdesc, acc);
+          for (int k = 0; k < BK / T::kUK; ++k) {
+            uint64_t adesc, bdesc;
+            if (!A_MN)
+              adesc = make_sw128_desc(sa + k * 32, 16, 1024);
+            else
+              adesc = make_sw128_desc(sa + k * T::kUK * 128, BK * 128, 1024);
+            if (!B_MN)
+              bdesc = make_sw128_desc(sb + k * 32, 16, 1024);
+            else
+              bdesc = make_sw128_desc(sb + k * T::kUK * 128, BK * 128, 1024);
+            const uint32_t accum = (i > 0 || k > 0) ? 1u : 0u;
+            if (FMT == 2)
+              umma_tf32(d_tmem, adesc, bdesc, kIdesc, accum);
+            else
+              umma_bf16(d_tmem, adesc, bdesc, kIdesc, accum);
+          }
+          tc_commit(&empty_bar[s]);
         }
-        tc_commit(&empty_bar[s]);
+        // signal the epilogue (also on abort, so it does not wait for nothing)
+        tc_commit(&tmem_full_bar[acc]);
+        ++tile_i;
       }
-      // signal the epilogue (also on abort, so it does not wait forever)
-      tc_commit(tmem_full_bar);
-      (void)ok;
     }
   } else {
-    // epilogue warps 2..5
+    // epilogue warps 2..9
     const int q = warp & 3;
-    const bool have = mbar_wait(tmem_full_bar, 0, p.err, kErrTimeoutTmemFull);
-    tc_fence_after();
-    if (have && !*abort_flag) {
-      const int r = q * 32 + lane;
-      const uint32_t taddr_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
-      long long row_off = 0;
-      bool row_ok;
-      if (p.c_pair) {
-        const int s_idx = tm * 64 + (r >> 1);
-        const int pm = r & 1;
-        const int mr = (g == 0) ? 0 : 2 * g - 1 + pm;
-        row_ok = (s_idx < p.M / 2) && !(g == 0 && pm == 1);
-        row_off = static_cast<long long>(s_idx) * p.c_ps + static_cast<long long>(mr) * p.c_pmr;
-      } else {
-        const int row = tm * 128 + r;
-        row_ok = row < p.M;
-        row_off = static_cast<long long>(g) * p.c_sg + static_cast<long long>(row) * p.c_sr;
-      }
+    const int half = (warp - 2) >> 2;
+    int tile_i = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+      const TileCoord tc = tile_coord(p, t);
+      int kb0, k_begin;
+      if (tile_kblocks<BK>(p, tc.g, tc.split, &kb0, &k_begin) == 0) continue;
+      const int acc = tile_i & 1;
+      const uint32_t use = static_cast<uint32_t>(tile_i >> 1);
+      ++tile_i;
+      const bool have = mbar_wait(&tmem_full_bar[acc], use & 1, p.err, kErrTimeoutTmemFull);
+      tc_fence_after();
+      if (!have || *abort_flag) break;
+      const int tm = tc.tm, tn = tc.tn, g = tc.g, split = tc.split;
+      const uint32_t taddr_row = tmem_base + static_cast<uint32_t>(acc) * kAccCols +
+                                 (static_cast<uint32_t>(q * 32) << 16);
+      const bool plain = !p.bias && !p.col_scale && !p.aux && !p.grad_pre && p.act == 0 && !p.out_bf16 &&
+                         p.k_splits == 1 && p.beta == 0.f;
+      if (!p.c_pair && p.c_sc == 1 && p.c_sr != 1) {
+        // Row-major C: stage each 32-row x 32-column block through shared
+        // memory so that lanes walk along a row and every store instruction
+        // writes one contiguous row segment.
+        float* stage = staging + (warp - 2) * (32 * 33);
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        uint32_t v[16];
-        tmem_ld_32x32b_x16(taddr_row + c0, v);
-        tmem_ld_wait();
-        if (!row_ok) continue;
+        for (int c0 = half * 32; c0 < BN; c0 += 64) {
+          const int ncol = (BN - c0) >= 32 ? 32 : (BN - c0);
+          uint32_t v0[16], v1[16];
+          tmem_ld_32x32b_x16(taddr_row + c0, v0);
+          if (ncol == 32) tmem_ld_32x32b_x16(taddr_row + c0 + 16, v1);
+          tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int col = tn * BN + c0 + j;
-          if (col >= p.N) break;
-          float x = __uint_as_float(v[j]) * p.alpha;
-          if (p.col_scale) x *= p.col_scale[col];
-          if (p.bias && split == 0) x += p.bias[col];
-          const long long off = row_off + static_cast<long long>(col) * p.c_sc;
-          if (p.aux) p.aux[off] = __float2bfloat16(x);
-          if (p.grad_pre) x *= act_grad(p.grad_act, __bfloat162float(p.grad_pre[off]));
-          x = apply_act(p.act, x);
-          store_out(p, off, x);
+          for (int j = 0; j < 16; ++j) stage[lane * 33 + j] = __uint_as_float(v0[j]);
+          if (ncol == 32) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) stage[lane * 33 + 16 + j] = __uint_as_float(v1[j]);
+          }
+          __syncwarp();
+          const int col = tn * BN + c0 + lane;
+          const bool col_ok = lane < ncol && col < p.N;
+          const int row0 = tm * 128 + q * 32;
+          if (plain) {
+            float* cbase = reinterpret_cast<float*>(p.C) + static_cast<long long>(g) * p.c_sg + col;
+#pragma unroll 8
+            for (int rr = 0; rr < 32; ++rr)
+              if (col_ok && row0 + rr < p.M)
+                cbase[static_cast<long long>(row0 + rr) * p.c_sr] = stage[rr * 33 + lane] * p.alpha;
+          } else {
+            const float cs = (col_ok && p.col_scale) ? p.col_scale[col] : 1.f;
+            const float bs = (col_ok && p.bias && split == 0) ? p.bias[col] : 0.f;
+#pragma unroll 4
+            for (int rr = 0; rr < 32; ++rr) {
+              const int row = row0 + rr;
+              if (!col_ok || row >= p.M) continue;
+              float x = stage[rr * 33 + lane] * p.alpha * cs + bs;
+              const long long off =
+                  static_cast<long long>(g) * p.c_sg + static_cast<long long>(row) * p.c_sr + col;
+              if (p.aux) p.aux[off] = __float2bfloat16(x);
+              if (p.grad_pre) x *= act_grad(p.grad_act, __bfloat162float(p.grad_pre[off]));
+              x = apply_act(p.act, x);
+              store_out(p, off, x);
+            }
+          }
+          __syncwarp();
+        }
+      } else {
+        // Column-strided C (lat-major transforms, pair layout): one lane per
+        // row keeps consecutive lanes on consecutive addresses where the
+        // layout allows it.
+        const int r = q * 32 + lane;
+        long long row_off = 0;
+        bool row_ok;
+        if (p.c_pair) {
+          const int s_idx = tm * 64 + (r >> 1);
+          const int pm = r & 1;
+          const int mr = (g == 0) ? 0 : 2 * g - 1 + pm;
+          row_ok = (s_idx < p.M / 2) && !(g == 0 && pm == 1);
+          row_off = static_cast<long long>(s_idx) * p.c_ps + static_cast<long long>(mr) * p.c_pmr;
+        } else {
+          const int row = tm * 128 + r;
+          row_ok = row < p.M;
+          row_off = static_cast<long long>(g) * p.c_sg + static_cast<long long>(row) * p.c_sr;
+        }
+#pragma unroll 1
+        for (int c0 = half * 16; c0 < BN; c0 += 32) {
+          uint32_t v[16];
+          tmem_ld_32x32b_x16(taddr_row + c0, v);
+          tmem_ld_wait();
+          if (!row_ok) continue;
+          const int colb = tn * BN + c0;
+          if (plain && colb + 16 <= p.N) {
+            float* cp = reinterpret_cast<float*>(p.C) + row_off + static_cast<long long>(colb) * p.c_sc;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) cp[j * p.c_sc] = __uint_as_float(v[j]) * p.alpha;
+            continue;
+          }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int col = colb + j;
+            if (col >= p.N) break;
+            float x = __uint_as_float(v[j]) * p.alpha;
+            if (p.col_scale) x *= p.col_scale[col];
+            if (p.bias && split == 0) x += p.bias[col];
+            const long long off = row_off + static_cast<long long>(col) * p.c_sc;
+            if (p.aux) p.aux[off] = __float2bfloat16(x);
+            if (p.grad_pre) x *= act_grad(p.grad_act, __bfloat162float(p.grad_pre[off]));
+            x = apply_act(p.act, x);
+            store_out(p, off, x);
+          }
         }
       }
+      // this thread has finished reading the accumulator: release the buffer
+      tc_fence_before();
+      mbar_arrive(&tmem_empty_bar[acc]);
     }
-    tc_fence_before();
   }
 
+  tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();

@@ -37,6 +37,8 @@ std::mutex g_setup_mu;
 EncodeFn g_encode = nullptr;
 // Device address of the scratch array per device ordinal; null until set up.
 float* g_scratch_addr[kMaxDevices] = {};
+// Multiprocessor count per device ordinal (persistent grid size).
+int g_num_sms[kMaxDevices] = {};
 
 template <int BN>
 struct Stages {
@@ -94,6 +96,10 @@ int setup_device(int dev, float** scratch) {
       (e = cudaFuncSetAttribute(kernel_for<256>(), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 smem_bytes<256>())) != cudaSuccess)
     return cuda_fail("cudaFuncSetAttribute(max dynamic shared memory)", e);
+  int sms = 0;
+  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+    return cuda_fail("cudaDeviceGetAttribute(multiprocessor count)", e);
+  g_num_sms[dev] = sms > 0 ? sms : 1;
   g_scratch_addr[dev] = static_cast<float*>(addr);
   *scratch = g_scratch_addr[dev];
   return TGCM_SHT_NOALLOC_OK;
@@ -125,18 +131,22 @@ tgcm::GemmParams base_params(int* err) {
   return p;
 }
 
+// Persistent launch: at most one CTA per SM (the kernels walk their tiles).
 template <int BN>
-cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const tgcm::GemmParams& p, cudaStream_t st) {
-  dim3 grid(p.tiles_n, p.tiles_m * p.groups, 1);
-  kernel_for<BN>()<<<grid, 192, smem_bytes<BN>(), st>>>(ta, tb, p);
+cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const tgcm::GemmParams& p, int n_sm,
+                   cudaStream_t st) {
+  const int tiles = tgcm::gemm_total_tiles(p);
+  if (tiles == 0) return cudaSuccess;
+  dim3 grid(tiles < n_sm ? tiles : n_sm);
+  kernel_for<BN>()<<<grid, tgcm::kGemmThreads, smem_bytes<BN>(), st>>>(ta, tb, p);
   return cudaGetLastError();
 }
 
-cudaError_t launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const tgcm::GemmParams& p,
+cudaError_t launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const tgcm::GemmParams& p, int n_sm,
                       cudaStream_t st) {
-  if (bn == 64) return launch<64>(ta, tb, p, st);
-  if (bn == 128) return launch<128>(ta, tb, p, st);
-  return launch<256>(ta, tb, p, st);
+  if (bn == 64) return launch<64>(ta, tb, p, n_sm, st);
+  if (bn == 128) return launch<128>(ta, tb, p, n_sm, st);
+  return launch<256>(ta, tb, p, n_sm, st);
 }
 
 long long cdiv(long long a, long long b) { return (a + b - 1) / b; }
@@ -207,7 +217,8 @@ extern "C" __attribute__((visibility("default"))) int tgcm_sht_synth_noalloc(
   p1.c_ps = J * M2p;
   p1.c_pmr = 1;
   p1.c_sc = M2p;
-  if ((e = launch_bn(bnj, ta1, tb1, p1, stream)) != cudaSuccess) return cuda_fail("Legendre GEMM launch", e);
+  const int n_sm = g_num_sms[dev];
+  if ((e = launch_bn(bnj, ta1, tb1, p1, n_sm, stream)) != cudaSuccess) return cuda_fail("Legendre GEMM launch", e);
 
   // 2) Fourier: out from F and W, one group per slice.
   tgcm::GemmParams p2 = base_params(err);
@@ -228,6 +239,6 @@ extern "C" __attribute__((visibility("default"))) int tgcm_sht_synth_noalloc(
     p2.c_sr = J;
     p2.c_sc = 1;
   }
-  if ((e = launch_bn(bnj, ta2, tb2, p2, stream)) != cudaSuccess) return cuda_fail("Fourier GEMM launch", e);
+  if ((e = launch_bn(bnj, ta2, tb2, p2, n_sm, stream)) != cudaSuccess) return cuda_fail("Fourier GEMM launch", e);
   return TGCM_SHT_NOALLOC_OK;
 }

@@ -123,18 +123,17 @@ __host__ __device__ inline void linear_point(const LinearArgs& a, int b, int s, 
   a.y[b * a.ys_b + s * a.ys_c + mr * a.ys_m + l] = acc;
 }
 
-__global__ void spectral_linear_kernel(LinearArgs a) {
-  const long long total = static_cast<long long>(a.B) * a.C_out * a.M2 * a.L;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int l = static_cast<int>(i % a.L);
-    long long r = i / a.L;
-    const int mr = static_cast<int>(r % a.M2);
-    r /= a.M2;
-    const int s = static_cast<int>(r % a.C_out);
-    const int b = static_cast<int>(r / a.C_out);
-    linear_point(a, b, s, mr, l);
-  }
+// grid: x over the (m, l) plane of one output channel, y over (b, channel);
+// 32-bit index arithmetic only.
+__global__ void __launch_bounds__(256) spectral_linear_kernel(LinearArgs a) {
+  const int plane = a.M2 * a.L;
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= plane) return;
+  const int s = blockIdx.y % a.C_out;
+  const int b = blockIdx.y / a.C_out;
+  const int mr = idx / a.L;
+  const int l = idx - mr * a.L;
+  linear_point(a, b, s, mr, l);
 }
 
 // x: (B, C_in, M2, Lx) ; returns y: (B, C_out, M2, Ly) with Ly = out_lpad (>= L), pad zero.
@@ -161,10 +160,9 @@ at::Tensor spectral_linear(const at::Tensor& x, int64_t L, int64_t C_out, int64_
   a.B = static_cast<int>(B); a.C_out = static_cast<int>(C_out); a.M2 = static_cast<int>(M2); a.L = static_cast<int>(L);
   if (x.is_cuda()) {
     c10::cuda::CUDAGuard guard(x.device());
-    const long long total = B * C_out * M2 * L;
-    const int threads = 256;
-    const long long blocks = std::min<long long>((total + threads - 1) / threads, 148LL * 32);
-    spectral_linear_kernel<<<static_cast<unsigned>(blocks), threads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+    TORCH_CHECK(B * C_out <= 65535 && M2 * L < (1LL << 31), "spectral_linear: launch grid too large");
+    dim3 grid(static_cast<unsigned>((M2 * L + 255) / 256), static_cast<unsigned>(B * C_out));
+    spectral_linear_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   } else {
     for (int b = 0; b < B; ++b)
@@ -195,6 +193,7 @@ struct StageArgs {
   int nE;
   float cp, cg, eta;
   const float* G; const float* H; const float* Minv; const float* lam; const float* tref; const float* dsig;
+  const float* MinvT;  // (n*n, L): MinvT[(i*n + j)*L + l] = Minv[l][i][j], or null
   const float* filt;  // (L) or null
   float clamp_abs;
   float R;
@@ -387,12 +386,180 @@ __global__ void sil3_stage_kernel(StageArgs a, int adjoint) {
   }
 }
 
+// Column-parallel stage kernel for a compile-time level count N: one thread
+// per (b, m, l) column with consecutive threads on consecutive l, so every
+// channel load/store of a warp is one contiguous row segment; G, H and the
+// level vectors sit in shared memory (broadcast reads) and the per-l Schur
+// inverse is read from its l-fastest transposed copy (coalesced).  Same
+// arithmetic as stage_column_fwd / stage_column_adj.
+template <int N>
+__global__ void __launch_bounds__(256) sil3_stage_cols_kernel(StageArgs a, int adjoint) {
+  __shared__ float sG[N * N], sH[N * N], sTr[N], sDs[N];
+  for (int i = threadIdx.x; i < N * N; i += blockDim.x) {
+    sG[i] = a.G[i];
+    sH[i] = a.H[i];
+  }
+  for (int i = threadIdx.x; i < N; i += blockDim.x) {
+    sTr[i] = a.tref[i];
+    sDs[i] = a.dsig[i];
+  }
+  __syncthreads();
+  const int total = a.B * a.M2 * a.L;
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= total) return;
+  const int bm = t / a.L;
+  const int l = t - bm * a.L;
+  const int b = bm / a.M2;
+  const int mr = bm - b * a.M2;
+  const long long cs = static_cast<long long>(a.M2) * a.L;
+  const long long base = static_cast<long long>(b) * a.C * cs + static_cast<long long>(mr) * a.L + l;
+  const float* mi = a.MinvT + l;
+  const long long ms = a.L;  // stride between consecutive (i, j) entries of MinvT
+  const float f = a.filt ? a.filt[l] : 1.f;
+  const float lam = a.lam[l];
+  const float el = a.eta * lam;
+  if (!adjoint) {
+    auto finish = [&](float v) -> float {
+      if (!a.final_stage) return v;
+      v *= f;
+      if (v != v) v = 0.f;
+      return fminf(fmaxf(v, -a.clamp_abs), a.clamp_abs);
+    };
+    auto expl = [&](int c) -> float {
+      float v = a.y0[base + c * cs] + a.cp * a.P[base + c * cs];
+      for (int j = 0; j < a.nE; ++j) v += a.ce[j] * a.E[j][base + c * cs];
+      return v;
+    };
+    for (int c = 0; c < N; ++c) a.out[base + c * cs] = finish(expl(c));
+    for (int c = 3 * N + 1; c < a.C; ++c) a.out[base + c * cs] = finish(expl(c));
+    float x[N], y[N], z[N];
+    float zp = a.y0[base + 3 * N * cs] + (a.y2 ? a.y2[base + 3 * N * cs] : 0.f);
+#pragma unroll
+    for (int k = 0; k < N; ++k) {  // x = z_δ, y = z_T
+      x[k] = a.y0[base + (N + k) * cs] + (a.y2 ? a.y2[base + (N + k) * cs] : 0.f);
+      y[k] = a.y0[base + (2 * N + k) * cs] + (a.y2 ? a.y2[base + (2 * N + k) * cs] : 0.f);
+    }
+    float zpg = 0.f;
+#pragma unroll
+    for (int k = 0; k < N; ++k) zpg += sDs[k] * x[k];
+    // z ← rd = expl_δ + cg·(−λ(G z_T + R Tr z_p));  x ← rt = expl_T − cg·H z_δ
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      float gt = 0.f;
+#pragma unroll
+      for (int j = 0; j < N; ++j) gt += sG[i * N + j] * y[j];
+      z[i] = expl(N + i) + a.cg * (-lam * (gt + a.R * sTr[i] * zp));
+    }
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      float hd = 0.f;
+#pragma unroll
+      for (int j = 0; j < N; ++j) hd += sH[i * N + j] * x[j];
+      y[i] = expl(2 * N + i) - a.cg * hd;
+    }
+    const float rp = expl(3 * N) - a.cg * zpg;
+    // z ← rd − el·(G rt + R Tr rp)   (rt in y)
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      float gt = 0.f;
+#pragma unroll
+      for (int j = 0; j < N; ++j) gt += sG[i * N + j] * y[j];
+      z[i] = z[i] - el * (gt + a.R * sTr[i] * rp);
+    }
+    // x ← δ = Minv z
+    float sp = 0.f;
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      float acc = 0.f;
+#pragma unroll
+      for (int j = 0; j < N; ++j) acc += mi[(i * N + j) * ms] * z[j];
+      x[i] = acc;
+      sp += sDs[i] * acc;
+    }
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      float hd = 0.f;
+#pragma unroll
+      for (int j = 0; j < N; ++j) hd += sH[i * N + j] * x[j];
+      a.out[base + (N + i) * cs] = finish(x[i]);
+      a.out[base + (2 * N + i) * cs] = finish(y[i] - a.eta * hd);
+    }
+    a.out[base + 3 * N * cs] = finish(rp - a.eta * sp);
+    return;
+  }
+  // adjoint
+  auto gpre = [&](int c) -> float {
+    const float g = a.gin[base + c * cs];
+    if (!a.final_stage) return g;
+    const float o = a.out[base + c * cs];
+    if (o >= a.clamp_abs || o <= -a.clamp_abs) return 0.f;
+    return g * f;
+  };
+  auto scatter = [&](int c, float r, float zextra, bool has_z) {
+    a.g_y0[base + c * cs] = r + zextra;
+    a.g_P[base + c * cs] = a.cp * r;
+    for (int j = 0; j < a.nE; ++j) a.g_E[j][base + c * cs] = a.ce[j] * r;
+    if (a.g_y2) a.g_y2[base + c * cs] = has_z ? zextra : 0.f;
+  };
+  for (int c = 0; c < N; ++c) scatter(c, gpre(c), 0.f, false);
+  for (int c = 3 * N + 1; c < a.C; ++c) scatter(c, gpre(c), 0.f, false);
+  float x[N], y[N];
+  const float pp = gpre(3 * N);
+#pragma unroll
+  for (int k = 0; k < N; ++k) y[k] = gpre(2 * N + k);  // t̄
+  float r[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    float htt = 0.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) htt += sH[j * N + i] * y[j];
+    r[i] = gpre(N + i) - a.eta * htt - a.eta * sDs[i] * pp;
+  }
+  float trd = 0.f;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {  // x = od = Minvᵀ r
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) acc += mi[(j * N + i) * ms] * r[j];
+    x[i] = acc;
+    trd += sTr[i] * acc;
+  }
+#pragma unroll
+  for (int i = 0; i < N; ++i) {  // y = ot = t̄ − el Gᵀ od
+    float gtr = 0.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) gtr += sG[j * N + i] * x[j];
+    y[i] = y[i] - el * gtr;
+  }
+  const float op = pp - el * a.R * trd;
+  float dsop = 0.f;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    float htb = 0.f, gta = 0.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      htb += sH[j * N + i] * y[j];
+      gta += sG[j * N + i] * x[j];
+    }
+    scatter(N + i, x[i], a.cg * (-htb - sDs[i] * op), true);
+    scatter(2 * N + i, y[i], a.cg * (-lam * gta), true);
+  }
+  (void)dsop;
+  scatter(3 * N, op, a.cg * (-lam * a.R * trd), true);
+}
+
 static const float* ptr_or_null(const c10::optional<at::Tensor>& t) {
   return (t.has_value() && t->defined()) ? t->data_ptr<float>() : nullptr;
 }
 
 static void run_stage(StageArgs& a, const at::Tensor& like, int adjoint) {
-  if (like.is_cuda()) {
+  if (like.is_cuda() && a.n == 32 && a.MinvT != nullptr) {
+    c10::cuda::CUDAGuard guard(like.device());
+    const long long total = static_cast<long long>(a.B) * a.M2 * a.L;
+    sil3_stage_cols_kernel<32><<<static_cast<unsigned>((total + 255) / 256), 256, 0,
+                                 at::cuda::getCurrentCUDAStream()>>>(a, adjoint);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  } else if (like.is_cuda()) {
     c10::cuda::CUDAGuard guard(like.device());
     dim3 grid((a.L + kStageL - 1) / kStageL, a.B);
     const size_t smem = (2 * a.n * a.n + kStageL * a.n * a.n) * sizeof(float);
@@ -442,10 +609,12 @@ at::Tensor sil3_stage(const at::Tensor& y0, std::vector<at::Tensor> E, const at:
                       const c10::optional<at::Tensor>& y2, std::vector<double> ce, double cp, double cg, double eta,
                       const at::Tensor& G, const at::Tensor& H, const at::Tensor& Minv, const at::Tensor& lam,
                       const at::Tensor& tref, const at::Tensor& dsig, const c10::optional<at::Tensor>& filt,
-                      double clamp_abs, double R, int64_t final_stage, int64_t n) {
+                      double clamp_abs, double R, int64_t final_stage, int64_t n,
+                      const c10::optional<at::Tensor>& minv_t) {
   StageArgs a;
   memset(&a, 0, sizeof(a));
   fill_common(a, y0, ce, cp, cg, eta, G, H, Minv, lam, tref, dsig, filt, clamp_abs, R, final_stage, n);
+  a.MinvT = ptr_or_null(minv_t);
   TORCH_CHECK(E.size() == ce.size(), "one coefficient per explicit tendency");
   auto out = at::empty_like(y0);
   a.y0 = y0.data_ptr<float>();
@@ -466,10 +635,11 @@ std::vector<at::Tensor> sil3_stage_adjoint(const at::Tensor& gout, const at::Ten
                                            const at::Tensor& G, const at::Tensor& H, const at::Tensor& Minv,
                                            const at::Tensor& lam, const at::Tensor& tref, const at::Tensor& dsig,
                                            const c10::optional<at::Tensor>& filt, double clamp_abs, double R,
-                                           int64_t final_stage, int64_t n) {
+                                           int64_t final_stage, int64_t n, const c10::optional<at::Tensor>& minv_t) {
   StageArgs a;
   memset(&a, 0, sizeof(a));
   fill_common(a, gout, ce, cp, cg, eta, G, H, Minv, lam, tref, dsig, filt, clamp_abs, R, final_stage, n);
+  a.MinvT = ptr_or_null(minv_t);
   auto g_y0 = at::empty_like(gout);
   auto g_P = at::empty_like(gout);
   std::vector<at::Tensor> res{g_y0};
@@ -501,10 +671,10 @@ TORCH_LIBRARY_FRAGMENT(tgcm, m) {
         "Tensor diag, Tensor rec_a, Tensor rec_b, Tensor mats, int nlev) -> Tensor");
   m.def("sil3_stage(Tensor y0, Tensor[] E, Tensor P, Tensor? y2, float[] ce, float cp, float cg, float eta, "
         "Tensor G, Tensor H, Tensor Minv, Tensor lam, Tensor tref, Tensor dsig, Tensor? filt, float clamp_abs, "
-        "float R, int final_stage, int n) -> Tensor");
+        "float R, int final_stage, int n, Tensor? minv_t=None) -> Tensor");
   m.def("sil3_stage_adjoint(Tensor gout, Tensor out, int nE, int has_y2, float[] ce, float cp, float cg, float eta, "
         "Tensor G, Tensor H, Tensor Minv, Tensor lam, Tensor tref, Tensor dsig, Tensor? filt, float clamp_abs, "
-        "float R, int final_stage, int n) -> Tensor[]");
+        "float R, int final_stage, int n, Tensor? minv_t=None) -> Tensor[]");
 }
 
 TORCH_LIBRARY_IMPL(tgcm, CompositeExplicitAutograd, m) {

@@ -370,7 +370,7 @@ class StageFn(torch.autograd.Function):
         G, H, lam, tref, dsig = meta["consts"]
         out = ops.sil3_stage(y0.contiguous(), [e.contiguous() for e in Es], P.contiguous(), y2, meta["ce"],
                              meta["cp"], meta["cg"], meta["eta"], G, H, meta["minv"], lam, tref, dsig,
-                             meta["filt"], meta["clamp"], meta["R"], meta["final"], meta["n"])
+                             meta["filt"], meta["clamp"], meta["R"], meta["final"], meta["n"], meta.get("minv_t"))
         ctx.meta, ctx.nE, ctx.has_y2 = meta, len(Es), y2 is not None
         if meta["final"]:
             ctx.save_for_backward(out)
@@ -384,7 +384,7 @@ class StageFn(torch.autograd.Function):
         out = ctx.saved_tensors[0] if meta["final"] else g
         res = ops.sil3_stage_adjoint(g.contiguous(), out, ctx.nE, int(ctx.has_y2), meta["ce"], meta["cp"],
                                      meta["cg"], meta["eta"], G, H, meta["minv"], lam, tref, dsig, meta["filt"],
-                                     meta["clamp"], meta["R"], meta["final"], meta["n"])
+                                     meta["clamp"], meta["R"], meta["final"], meta["n"], meta.get("minv_t"))
         g_y0 = res[0]
         gE = list(res[1:1 + ctx.nE]) + [None] * (3 - ctx.nE)
         g_P = res[1 + ctx.nE]
@@ -427,13 +427,15 @@ class PackedSIL3:
             base = c.on(device)
             dt = self.dt
             minv = {e: c.minv(e, device) for e in (dt / 6, dt / 3, dt / 4)}
+            # l-fastest copies (n*n, L) for the column-parallel stage kernel
+            minv_t = {e: m.reshape(m.shape[0], -1).t().contiguous() for e, m in minv.items()}
             filt = torch.as_tensor(self.filter_scaling, dtype=torch.float32, device=device)
             g = self.eq.grid
             oro = self.eq.orography_tendency(device, torch.float32)
             oro = g.clip_wavenumbers(oro)
             packed_oro = torch.zeros(self.ch["C"], *g.modal_shape, dtype=torch.float32, device=device)
             packed_oro[self.n:2 * self.n] = oro
-            d = {"base": base, "minv": minv, "filt": filt, "oro": packed_oro}
+            d = {"base": base, "minv": minv, "minv_t": minv_t, "filt": filt, "oro": packed_oro}
             self._dev[key] = d
         return d
 
@@ -455,7 +457,8 @@ class PackedSIL3:
 
     def _meta(self, device, ce, cp, cg, eta, final):
         d = self._consts(device)
-        return {"consts": d["base"], "minv": d["minv"][eta], "filt": d["filt"] if final else None, "ce": ce,
+        return {"consts": d["base"], "minv": d["minv"][eta], "minv_t": d["minv_t"][eta],
+                "filt": d["filt"] if final else None, "ce": ce,
                 "cp": cp, "cg": cg, "eta": eta, "clamp": self.clamp, "R": float(self.eq.R), "final": int(final),
                 "n": self.n}
 
