@@ -208,6 +208,50 @@ __device__ __forceinline__ float gelu_erf_grad_f(float x) {
 
 enum Activation : int { kActNone = 0, kActRelu = 1, kActGelu = 2, kActGeluTanh = 3, kActSilu = 4, kActTanh = 5 };
 
+// Hardware tanh (MUFU, relative error about 2^-11): used by the BF16 GEMM
+// epilogues, whose outputs are rounded to BF16 (8-bit mantissa) anyway.
+__device__ __forceinline__ float tanh_hw(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float gelu_tanh_hw(float x) {
+  const float u = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
+  return 0.5f * x * (1.f + tanh_hw(u));
+}
+
+__device__ __forceinline__ float gelu_tanh_grad_hw(float x) {
+  const float x2 = x * x;
+  const float u = 0.7978845608028654f * fmaf(0.044715f * x, x2, x);
+  const float t = tanh_hw(u);
+  return 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * 0.7978845608028654f * fmaf(3.f * 0.044715f, x2, 1.f);
+}
+
+template <int ACT>
+__device__ __forceinline__ float act_fast(float x) {
+  if constexpr (ACT == kActRelu) return x > 0.f ? x : 0.f;
+  else if constexpr (ACT == kActGelu) return gelu_erf_f(x);
+  else if constexpr (ACT == kActGeluTanh) return gelu_tanh_hw(x);
+  else if constexpr (ACT == kActSilu) return x / (1.f + __expf(-x));
+  else if constexpr (ACT == kActTanh) return tanh_hw(x);
+  else return x;
+}
+
+template <int ACT>
+__device__ __forceinline__ float act_grad_fast(float x) {
+  if constexpr (ACT == kActRelu) return x > 0.f ? 1.f : 0.f;
+  else if constexpr (ACT == kActGelu) return gelu_erf_grad_f(x);
+  else if constexpr (ACT == kActGeluTanh) return gelu_tanh_grad_hw(x);
+  else if constexpr (ACT == kActSilu) {
+    const float sg = 1.f / (1.f + __expf(-x));
+    return sg * (1.f + x * (1.f - sg));
+  } else if constexpr (ACT == kActTanh) {
+    const float t = tanh_hw(x);
+    return 1.f - t * t;
+  } else return 1.f;
+}
+
 __device__ __forceinline__ float apply_act(int act, float x) {
   switch (act) {
     case kActRelu: return x > 0.f ? x : 0.f;

@@ -93,6 +93,10 @@ struct StagesFor {
   static constexpr int value = BN <= 80 ? 4 : BN <= 144 ? 3 : 2;
 };
 
+// Optional per-CTA cycle-counter buffer (diagnostics; see GemmParams::prof).
+static unsigned long long* g_prof_buf = nullptr;
+static int64_t g_prof_ctas = 0;
+
 template <int FMT, int BN, bool A_MN, bool B_MN>
 static void launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream) {
   constexpr int ST = StagesFor<BN>::value;
@@ -114,7 +118,9 @@ static void launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmP
   const int tiles = gemm_total_tiles(p);
   if (tiles == 0) return;
   dim3 grid(tiles < n_sm ? tiles : n_sm);
-  kern<<<grid, kGemmThreads, S::kTotal, stream>>>(ta, tb, p);
+  GemmParams q = p;
+  q.prof = (g_prof_buf != nullptr && grid.x <= g_prof_ctas) ? g_prof_buf : nullptr;
+  kern<<<grid, kGemmThreads, S::kTotal, stream>>>(ta, tb, q);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("tgcm gemm launch: ") + cudaGetErrorString(e));
 }
@@ -354,9 +360,25 @@ void bgemm_tf32(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, double 
   gemm_dispatch(2, bn, false, false, ta, tb, p, at::cuda::getCurrentCUDAStream());
 }
 
+// Route the GEMM kernels' per-CTA cycle counters into `buf` ((ctas, 8) int64 on
+// the device), or stop recording when `buf` is absent.
+void gemm_profile_buffer(const c10::optional<at::Tensor>& buf) {
+  if (buf.has_value() && buf->defined()) {
+    TORCH_CHECK(buf->is_cuda() && buf->scalar_type() == at::kLong && buf->dim() == 2 && buf->size(1) == 8 &&
+                    buf->is_contiguous(),
+                "profile buffer must be a contiguous (ctas, 8) int64 CUDA tensor");
+    g_prof_buf = reinterpret_cast<unsigned long long*>(buf->data_ptr<int64_t>());
+    g_prof_ctas = buf->size(0);
+  } else {
+    g_prof_buf = nullptr;
+    g_prof_ctas = 0;
+  }
+}
+
 }  // namespace tgcm
 
 TORCH_LIBRARY_FRAGMENT(tgcm, m) {
+  m.def("gemm_profile_buffer(Tensor? buf) -> ()");
   m.def("bgemm_tf32(Tensor A, Tensor B, Tensor(a!) C, float alpha, Tensor? err) -> ()");
   m.def("sht_synth(Tensor x, int L, Tensor P, Tensor F, Tensor ws, Tensor? col_scale, Tensor? err, bool lat_major) -> Tensor");
   m.def("sht_anal(Tensor N, Tensor Ft, Tensor Pt, int Lo, Tensor ws, Tensor? col_scale, Tensor? err, bool lat_major) -> Tensor");
@@ -372,4 +394,8 @@ TORCH_LIBRARY_IMPL(tgcm, CUDA, m) {
   m.impl("linear_dgrad", &tgcm::linear_dgrad);
   m.impl("linear_wgrad", &tgcm::linear_wgrad);
   m.impl("bgemm_tf32", &tgcm::bgemm_tf32);
+}
+
+TORCH_LIBRARY_IMPL(tgcm, CompositeExplicitAutograd, m) {
+  m.impl("gemm_profile_buffer", &tgcm::gemm_profile_buffer);
 }

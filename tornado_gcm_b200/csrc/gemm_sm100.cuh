@@ -46,6 +46,10 @@ struct GemmParams {
   const __nv_bfloat16* grad_pre; // multiply by act'(grad_pre) (plain layout) or null
   int grad_act;
   int* err;
+  // optional per-CTA cycle counters (diagnostics): [cta][0..7] =
+  // producer wait, producer issue, mma wait-empty-acc, mma wait-full, mma issue,
+  // epilogue wait, epilogue work, tiles
+  unsigned long long* prof;
 };
 
 template <int FMT>
@@ -73,7 +77,7 @@ struct GemmSmem {
   static constexpr int kA = 128 * 128;        // bytes per A stage
   static constexpr int kB = BN * 128;         // bytes per B stage
   static constexpr int kStage = kA + kB;
-  static constexpr int kStaging = 8 * 32 * 33 * 4;  // epilogue transpose tiles (8 warps x 32 x 33 fp32)
+  static constexpr int kStaging = 8 * 32 * 144;  // epilogue staging tiles (8 warps x 32 rows x 144 B)
   static constexpr int kBars = 1024;          // barrier / bookkeeping area
   static constexpr int kTotal = STAGES * kStage + kStaging + kBars + 1024;  // + alignment slack
 };
@@ -131,6 +135,151 @@ __device__ __forceinline__ int tile_kblocks(const GemmParams& p, int g, int spli
 
 __host__ __device__ inline int gemm_total_tiles(const GemmParams& p) {
   return p.tiles_n * p.tiles_m * p.groups * p.k_splits;
+}
+
+// ── vectorised row-major epilogue ──────────────────────────────────────────
+// One warp handles 32 rows (its TMEM lane quarter) x 32 columns per chunk.
+// Lane r holds row r's 32 accumulator values (tcgen05.ld); bias, column
+// scale, activation and its derivative are applied in registers; the chunk
+// goes through a padded shared-memory tile and leaves (or, for the
+// pre-activation operand of dgrad, arrives) as 16-byte vectors, so every
+// global access of the warp is a run of whole 16-byte sectors.
+constexpr int kStageRowBf16 = 80;   // 32 bf16 + 16 B pad (conflict-free v4 accesses)
+constexpr int kStageRowF32 = 144;   // 32 fp32 + 16 B pad
+
+// Copy a 32 x 32 bf16 chunk between the staging tile and global memory.
+// dir = 0: staging → global, dir = 1: global → staging.  Rows ≥ nrows and
+// columns ≥ ncols are skipped; partial 8-column vectors fall back to scalars.
+__device__ __forceinline__ void chunk_copy_bf16(uint8_t* stage, __nv_bfloat16* g, long long ld, int nrows, int ncols,
+                                                int lane, int dir) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int v = lane + 32 * i;
+    const int row = v >> 2, seg = v & 3;
+    if (row >= nrows) continue;
+    uint8_t* sp = stage + row * kStageRowBf16 + seg * 16;
+    __nv_bfloat16* gp = g + row * ld + seg * 8;
+    if (seg * 8 + 8 <= ncols) {
+      if (dir == 0)
+        *reinterpret_cast<uint4*>(gp) = *reinterpret_cast<const uint4*>(sp);
+      else
+        *reinterpret_cast<uint4*>(sp) = __ldg(reinterpret_cast<const uint4*>(gp));
+    } else {
+      __nv_bfloat16* se = reinterpret_cast<__nv_bfloat16*>(sp);
+      for (int e = 0; e < 8 && seg * 8 + e < ncols; ++e) {
+        if (dir == 0)
+          gp[e] = se[e];
+        else
+          se[e] = gp[e];
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void chunk_store_f32(const uint8_t* stage, float* g, long long ld, int nrows, int ncols,
+                                                int lane) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int v = lane + 32 * i;
+    const int row = v >> 3, seg = v & 7;
+    if (row >= nrows) continue;
+    const uint8_t* sp = stage + row * kStageRowF32 + seg * 16;
+    float* gp = g + row * ld + seg * 4;
+    if (seg * 4 + 4 <= ncols) {
+      *reinterpret_cast<float4*>(gp) = *reinterpret_cast<const float4*>(sp);
+    } else {
+      const float* se = reinterpret_cast<const float*>(sp);
+      for (int e = 0; e < 4 && seg * 4 + e < ncols; ++e) gp[e] = se[e];
+    }
+  }
+}
+
+// Epilogue of one 32-row x BN tile slice for row-major C with 16-byte aligned
+// rows.  ACT is the forward activation (or, with grad_pre, the activation
+// whose derivative multiplies the result).
+template <int ACT, int BN>
+__device__ __forceinline__ void epilogue_rowmajor_vec(const GemmParams& p, uint32_t taddr_row, uint8_t* stage,
+                                                      int tm, int tn, int g, int q, int half, int lane) {
+  const int row0 = tm * 128 + q * 32;
+  const int nrows = p.M - row0 < 32 ? p.M - row0 : 32;
+#pragma unroll 1
+  for (int c0 = half * 32; c0 < BN; c0 += 64) {
+    const int ncolc = (BN - c0) >= 32 ? 32 : (BN - c0);
+    const int col0 = tn * BN + c0;
+    int ncols = p.N - col0;
+    if (ncols > ncolc) ncols = ncolc;
+    uint32_t v0[16], v1[16];
+    tmem_ld_32x32b_x16(taddr_row + c0, v0);
+    if (ncolc == 32) tmem_ld_32x32b_x16(taddr_row + c0 + 16, v1);
+    tmem_ld_wait();
+    if (ncols <= 0 || nrows <= 0) continue;
+    const long long base = static_cast<long long>(g) * p.c_sg + static_cast<long long>(row0) * p.c_sr + col0;
+    float x[32];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) x[j] = __uint_as_float(v0[j]) * p.alpha;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) x[16 + j] = (ncolc == 32) ? __uint_as_float(v1[j]) * p.alpha : 0.f;
+    if (p.col_scale) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) x[j] *= (j < ncols) ? __ldg(p.col_scale + col0 + j) : 0.f;
+    }
+    if (p.bias) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) x[j] += (j < ncols) ? __ldg(p.bias + col0 + j) : 0.f;
+    }
+    uint8_t* my = stage + lane * kStageRowBf16;
+    if (p.aux) {  // pre-activation copy (bf16)
+#pragma unroll
+      for (int j = 0; j < 32; j += 2)
+        *reinterpret_cast<__nv_bfloat162*>(my + 2 * j) = __floats2bfloat162_rn(x[j], x[j + 1]);
+      __syncwarp();
+      chunk_copy_bf16(stage, p.aux + base, p.c_sr, nrows, ncols, lane, 0);
+      __syncwarp();
+    }
+    if (p.grad_pre) {  // x *= act'(pre)
+      chunk_copy_bf16(stage, const_cast<__nv_bfloat16*>(p.grad_pre) + base, p.c_sr, nrows, ncols, lane, 1);
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) {
+        const float2 pr = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(my + 2 * j));
+        x[j] *= act_grad_fast<ACT>(pr.x);
+        x[j + 1] *= act_grad_fast<ACT>(pr.y);
+      }
+      __syncwarp();
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) x[j] = act_fast<ACT>(x[j]);
+    }
+    if (p.out_bf16) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 2)
+        *reinterpret_cast<__nv_bfloat162*>(my + 2 * j) = __floats2bfloat162_rn(x[j], x[j + 1]);
+      __syncwarp();
+      chunk_copy_bf16(stage, reinterpret_cast<__nv_bfloat16*>(p.C) + base, p.c_sr, nrows, ncols, lane, 0);
+    } else {
+      uint8_t* myf = stage + lane * kStageRowF32;
+#pragma unroll
+      for (int j = 0; j < 32; j += 4)
+        *reinterpret_cast<float4*>(myf + 4 * j) = make_float4(x[j], x[j + 1], x[j + 2], x[j + 3]);
+      __syncwarp();
+      chunk_store_f32(stage, reinterpret_cast<float*>(p.C) + base, p.c_sr, nrows, ncols, lane);
+    }
+    __syncwarp();
+  }
+}
+
+template <int BN>
+__device__ __forceinline__ void epilogue_rowmajor_dispatch(const GemmParams& p, int act, uint32_t taddr_row,
+                                                           uint8_t* stage, int tm, int tn, int g, int q, int half,
+                                                           int lane) {
+  switch (act) {
+    case kActRelu: epilogue_rowmajor_vec<kActRelu, BN>(p, taddr_row, stage, tm, tn, g, q, half, lane); break;
+    case kActGelu: epilogue_rowmajor_vec<kActGelu, BN>(p, taddr_row, stage, tm, tn, g, q, half, lane); break;
+    case kActGeluTanh: epilogue_rowmajor_vec<kActGeluTanh, BN>(p, taddr_row, stage, tm, tn, g, q, half, lane); break;
+    case kActSilu: epilogue_rowmajor_vec<kActSilu, BN>(p, taddr_row, stage, tm, tn, g, q, half, lane); break;
+    case kActTanh: epilogue_rowmajor_vec<kActTanh, BN>(p, taddr_row, stage, tm, tn, g, q, half, lane); break;
+    default: epilogue_rowmajor_vec<kActNone, BN>(p, taddr_row, stage, tm, tn, g, q, half, lane); break;
+  }
 }
 
 // Persistent kernel: each CTA walks tiles t = blockIdx.x, +gridDim.x, ….
@@ -197,6 +346,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       int kb_global = 0;
+      unsigned long long t_wait = 0, t_issue = 0;
       for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x) {
         const TileCoord tc = tile_coord(p, t);
         int kb0, k_begin;
@@ -207,10 +357,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int i = 0; i < num_kb; ++i, ++kb_global) {
           const int s = kb_global % STAGES;
           const uint32_t ph = (kb_global / STAGES) & 1;
+          const unsigned long long c0 = p.prof ? clock64() : 0ull;
           if (!mbar_wait(&empty_bar[s], ph ^ 1, p.err, kErrTimeoutEmpty)) {
             *abort_flag = 1;
             break;
           }
+          if (p.prof) t_wait += clock64() - c0;
           if (*abort_flag) break;
           uint8_t* sa = smem + s * S::kStage;
           uint8_t* sb = sa + S::kA;
@@ -238,10 +390,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // drain: every load this thread issued has landed before the CTA exits
       for (int i = (kb_global > STAGES ? kb_global - STAGES : 0); i < kb_global; ++i)
         mbar_wait(&full_bar[i % STAGES], (i / STAGES) & 1, p.err, kErrTimeoutDrain);
+      if (p.prof) {
+        p.prof[blockIdx.x * 8 + 0] = t_wait;
+        p.prof[blockIdx.x * 8 + 1] = t_issue;
+      }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       int kb_global = 0, tile_i = 0;
+      unsigned long long t_acc = 0, t_full = 0;
       for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x) {
         const TileCoord tc = tile_coord(p, t);
         int kb0, k_begin;
@@ -249,19 +406,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (num_kb == 0) continue;
         const int acc = tile_i & 1;
         const uint32_t use = static_cast<uint32_t>(tile_i >> 1);
+        unsigned long long c0 = p.prof ? clock64() : 0ull;
         if (!mbar_wait(&tmem_empty_bar[acc], (use & 1) ^ 1, p.err, kErrTimeoutEmpty)) {
           *abort_flag = 1;
           break;
         }
+        if (p.prof) t_acc += clock64() - c0;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc) * kAccCols;
         for (int i = 0; i < num_kb; ++i, ++kb_global) {
           const int s = kb_global % STAGES;
           const uint32_t ph = (kb_global / STAGES) & 1;
+          c0 = p.prof ? clock64() : 0ull;
           if (!mbar_wait(&full_bar[s], ph, p.err, kErrTimeoutFull)) {
             *abort_flag = 1;
             break;
           }
+          if (p.prof) t_full += clock64() - c0;
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + s * S::kStage);
           const uint32_t sb = sa + S::kA;
@@ -288,12 +449,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_commit(&tmem_full_bar[acc]);
         ++tile_i;
       }
+      if (p.prof) {
+        p.prof[blockIdx.x * 8 + 2] = t_acc;
+        p.prof[blockIdx.x * 8 + 3] = t_full;
+        p.prof[blockIdx.x * 8 + 7] = tile_i;
+      }
     }
   } else {
     // epilogue warps 2..9
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
     int tile_i = 0;
+    unsigned long long t_ew = 0, t_work = 0;
     for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
       const TileCoord tc = tile_coord(p, t);
       int kb0, k_begin;
@@ -301,15 +468,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int acc = tile_i & 1;
       const uint32_t use = static_cast<uint32_t>(tile_i >> 1);
       ++tile_i;
+      const unsigned long long c0 = p.prof ? clock64() : 0ull;
       const bool have = mbar_wait(&tmem_full_bar[acc], use & 1, p.err, kErrTimeoutTmemFull);
       tc_fence_after();
+      const unsigned long long c1 = p.prof ? clock64() : 0ull;
+      if (p.prof) t_ew += c1 - c0;
       if (!have || *abort_flag) break;
       const int tm = tc.tm, tn = tc.tn, g = tc.g, split = tc.split;
       const uint32_t taddr_row = tmem_base + static_cast<uint32_t>(acc) * kAccCols +
                                  (static_cast<uint32_t>(q * 32) << 16);
       const bool plain = !p.bias && !p.col_scale && !p.aux && !p.grad_pre && p.act == 0 && !p.out_bf16 &&
                          p.k_splits == 1 && p.beta == 0.f;
-      if (!p.c_pair && p.c_sc == 1 && p.c_sr != 1) {
+      const int esz = p.out_bf16 ? 2 : 4;
+      const bool vec_ok = !p.c_pair && p.c_sc == 1 && p.c_sr != 1 && p.k_splits == 1 && p.beta == 0.f &&
+                          (reinterpret_cast<uintptr_t>(p.C) % 16 == 0) && ((p.c_sr * esz) % 16 == 0) &&
+                          ((p.c_sg * esz) % 16 == 0) && (BN % 8 == 0) &&
+                          (!p.aux || (reinterpret_cast<uintptr_t>(p.aux) % 16 == 0 && (p.c_sr * 2) % 16 == 0 &&
+                                      (p.c_sg * 2) % 16 == 0)) &&
+                          (!p.grad_pre || (reinterpret_cast<uintptr_t>(p.grad_pre) % 16 == 0 &&
+                                           (p.c_sr * 2) % 16 == 0 && (p.c_sg * 2) % 16 == 0));
+      if (vec_ok) {
+        uint8_t* stage = reinterpret_cast<uint8_t*>(staging) + (warp - 2) * (32 * kStageRowF32);
+        epilogue_rowmajor_dispatch<BN>(p, p.grad_pre ? p.grad_act : p.act, taddr_row, stage, tm, tn, g, q, half,
+                                       lane);
+      } else if (!p.c_pair && p.c_sc == 1 && p.c_sr != 1) {
         // Row-major C: stage each 32-row x 32-column block through shared
         // memory so that lanes walk along a row and every store instruction
         // writes one contiguous row segment.
@@ -404,6 +586,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // this thread has finished reading the accumulator: release the buffer
       tc_fence_before();
       mbar_arrive(&tmem_empty_bar[acc]);
+      if (p.prof) t_work += clock64() - c1;
+    }
+    if (p.prof && warp == 2 && lane == 0) {
+      p.prof[blockIdx.x * 8 + 5] = t_ew;
+      p.prof[blockIdx.x * 8 + 6] = t_work;
     }
   }
 

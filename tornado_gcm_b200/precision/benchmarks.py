@@ -14,6 +14,8 @@ Kernel micro-benchmarks (used for profiler captures on small cases)::
     python -m tornado_gcm_b200.precision.benchmarks mlp --tokens 32768 --width 384
     python -m tornado_gcm_b200.precision.benchmarks sht --grid TL63 --slices 1292
     python -m tornado_gcm_b200.precision.benchmarks stage --grid TL63 --batch 4
+    python -m tornado_gcm_b200.precision.benchmarks linear --mode dgrad --tokens 32768 --width 384 --cycles
+    python -m tornado_gcm_b200.precision.benchmarks bgemm --groups 1292 --m 128 --n 64 --k 128 --cycles
 """
 
 from __future__ import annotations
@@ -219,7 +221,7 @@ def _mlp_case(args):
 
     def step():
         y = lops.mlp_forward(x, layers, acts)
-        y.backward(torch.ones_like(y))
+        torch.autograd.grad(y.sum(), [x] + [p for lyr in layers for p in lyr.parameters()])
 
     flops = 6.0 * args.tokens * sum(a * b for a, b in zip(dims[:-1], dims[1:]))
     return step, flops
@@ -266,14 +268,80 @@ def _stage_case(args):
 
     def step():
         out = st.step_packed(y, P)
-        out.backward(torch.ones_like(out))
+        torch.autograd.grad(out.sum(), [y])
 
     return step, 0.0
 
 
+def _linear_case(args):
+    from tornado_gcm_b200.ops import _ext
+
+    ops = _ext.require("linear micro-benchmark")
+    dev = torch.device("cuda")
+    T, K, O = args.tokens, args.width, args.width
+    X = torch.randn(T, K, device=dev).bfloat16()
+    W = torch.randn(O, K, device=dev).bfloat16() * 0.05
+    bias = torch.zeros(O, device=dev)
+    out = torch.empty(T, O, device=dev, dtype=torch.bfloat16)
+    aux = torch.empty(T, O, device=dev, dtype=torch.bfloat16)
+    dY = torch.randn(T, O, device=dev).bfloat16()
+    dX = torch.empty(T, K, device=dev, dtype=torch.bfloat16)
+    dW = torch.zeros(O, K, device=dev)
+    err = _ext.error_flag(dev)
+    if args.mode == "fwd":
+        fn = lambda: ops.linear_fwd(X, W, bias, 3, out, aux, err)
+    elif args.mode == "dgrad":
+        fn = lambda: ops.linear_dgrad(dY, W, dX, X, 3, err)
+    else:
+        fn = lambda: ops.linear_wgrad(dY, X, dW, 0, err)
+    return fn, 2.0 * T * K * O
+
+
+def _bgemm_case(args):
+    from tornado_gcm_b200.ops import _ext
+
+    ops = _ext.require("batched GEMM micro-benchmark")
+    dev = torch.device("cuda")
+    A = torch.randn(args.groups, args.m, args.k, device=dev)
+    B = torch.randn(args.groups, args.n, args.k, device=dev)
+    C = torch.empty(args.groups, args.m, args.n, device=dev)
+    err = _ext.error_flag(dev)
+    return (lambda: ops.bgemm_tf32(A, B, C, 1.0, err)), 2.0 * args.groups * args.m * args.n * args.k
+
+
+def gemm_cycle_breakdown(fn) -> list:
+    """Run ``fn`` once per GEMM launch recorded and return per-CTA-averaged cycle counters.
+
+    Counters (cycles, averaged over the CTAs of the last GEMM launch in ``fn``):
+    producer waiting for a free ring stage, MMA waiting for a free accumulator,
+    MMA waiting for operands, epilogue waiting for an accumulator, epilogue work.
+    """
+    from tornado_gcm_b200.ops import _ext
+
+    ops = _ext.require("GEMM profile")
+    buf = torch.zeros(1024, 8, dtype=torch.int64, device="cuda")
+    ops.gemm_profile_buffer(buf)
+    try:
+        fn()
+        torch.cuda.synchronize()
+    finally:
+        ops.gemm_profile_buffer(None)
+    b = buf[buf[:, 7] > 0].double()
+    if b.numel() == 0:
+        return []
+    m = b.mean(0).tolist()
+    return [{"producer_wait": m[0], "mma_wait_acc": m[2], "mma_wait_full": m[3], "epi_wait": m[5],
+             "epi_work": m[6], "tiles_per_cta": m[7], "ctas": int(b.shape[0])}]
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description="kernel micro-benchmarks (CUDA events)")
-    ap.add_argument("case", choices=["mlp", "sht", "stage"])
+    ap.add_argument("case", choices=["mlp", "sht", "stage", "linear", "bgemm"])
+    ap.add_argument("--mode", default="fwd", choices=["fwd", "dgrad", "wgrad"])
+    ap.add_argument("--groups", type=int, default=1292)
+    ap.add_argument("--m", type=int, default=128)
+    ap.add_argument("--n", type=int, default=64)
+    ap.add_argument("--k", type=int, default=128)
     ap.add_argument("--tokens", type=int, default=32768)
     ap.add_argument("--width", type=int, default=384)
     ap.add_argument("--width-in", type=int, default=197)
@@ -284,13 +352,17 @@ def main(argv=None) -> None:
     ap.add_argument("--batch", type=int, default=4)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--cycles", action="store_true", help="print the GEMM cycle breakdown of one call")
     args = ap.parse_args(argv)
-    fn, flops = {"mlp": _mlp_case, "sht": _sht_case, "stage": _stage_case}[args.case](args)
+    fn, flops = {"mlp": _mlp_case, "sht": _sht_case, "stage": _stage_case, "linear": _linear_case,
+                 "bgemm": _bgemm_case}[args.case](args)
     tb = TimingBenchmark(warmup=args.warmup, iterations=args.iters)
     r = tb.time_fn(args.case, fn)
     out = {"case": args.case, "mean_ms": r.mean_ms, "min_ms": r.min_ms}
     if flops:
         out["tflops"] = round(flops / (r.min_ms * 1e-3) / 1e12, 2)
+    if args.cycles:
+        out["gemm_cycles_last_launch"] = gemm_cycle_breakdown(fn)
     print(json.dumps(out))
 
 
