@@ -51,7 +51,20 @@ static ColumnConsts consts_from(const at::Tensor& level_consts, int64_t n, int64
   return c;
 }
 
+// Optional fused geopotential matrix: a (n, n) fp32 copy on the data's device;
+// the returned tensor keeps it alive for the duration of the call.
+static at::Tensor attach_gmat(ColumnConsts& c, const c10::optional<at::Tensor>& gmat, const at::Tensor& like,
+                              int64_t n) {
+  c.gmat = nullptr;
+  if (!gmat.has_value() || !gmat->defined()) return at::Tensor();
+  TORCH_CHECK(gmat->dim() == 2 && gmat->size(0) == n && gmat->size(1) == n, "gmat must be (n, n)");
+  at::Tensor g = gmat->to(like.device(), at::kFloat).contiguous();
+  c.gmat = g.data_ptr<float>();
+  return g;
+}
+
 // ── column kernels ──────────────────────────────────────────────────────────
+template <int MAXL>
 __global__ void column_fwd_kernel(ColumnConsts c, SliceIndex ix, const float* __restrict__ in,
                                   float* __restrict__ out, const float* __restrict__ sec2,
                                   const float* __restrict__ cor, int B, int I, int J, int lat_major) {
@@ -65,7 +78,7 @@ __global__ void column_fwd_kernel(ColumnConsts c, SliceIndex ix, const float* __
   float* ob = out + static_cast<long long>(b) * ix.n_out * plane + ij;
   auto rd = [ib, plane](int q) -> float { return __ldg(ib + q * plane); };
   auto wr = [ob, plane](int q, float v) { ob[q * plane] = v; };
-  column_forward(c, ix, rd, wr, sec2[j], cor[j]);
+  column_forward<MAXL>(c, ix, rd, wr, sec2[j], cor[j]);
 }
 
 template <int MAXL, int MAXT>
@@ -96,9 +109,10 @@ static void check_nodal(const at::Tensor& t, const char* name) {
 at::Tensor column_fwd(const at::Tensor& nin, const at::Tensor& sec2, const at::Tensor& cor,
                       const at::Tensor& level_consts, int64_t batch, int64_t n, int64_t nt, int64_t hum,
                       int64_t hum_terms, std::vector<int64_t> clouds, int64_t vadv, double R, double kappa,
-                      double rv, double cpv, bool lat_major) {
+                      double rv, double cpv, bool lat_major, const c10::optional<at::Tensor>& gmat) {
   check_nodal(nin, "nin");
   ColumnConsts c = consts_from(level_consts, n, nt, hum, hum_terms, clouds, vadv, R, kappa, rv, cpv);
+  at::Tensor gm = attach_gmat(c, gmat, nin, n);
   SliceIndex ix = make_slice_index(c);
   const int64_t I = lat_major ? nin.size(2) : nin.size(1), J = lat_major ? nin.size(1) : nin.size(2);
   TORCH_CHECK(nin.size(0) == batch * ix.n_in, "nin slice count mismatch: expected ", batch * ix.n_in);
@@ -109,9 +123,18 @@ at::Tensor column_fwd(const at::Tensor& nin, const at::Tensor& sec2, const at::T
     c10::cuda::CUDAGuard guard(nin.device());
     const long long total = batch * I * J;
     const int threads = 128;
-    column_fwd_kernel<<<(total + threads - 1) / threads, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
-        c, ix, nin.data_ptr<float>(), out.data_ptr<float>(), s2.data_ptr<float>(), co.data_ptr<float>(),
-        static_cast<int>(batch), static_cast<int>(I), static_cast<int>(J), lat_major ? 1 : 0);
+    const unsigned blocks = static_cast<unsigned>((total + threads - 1) / threads);
+    auto st = at::cuda::getCurrentCUDAStream();
+    if (n <= 32)
+      column_fwd_kernel<32><<<blocks, threads, 0, st>>>(c, ix, nin.data_ptr<float>(), out.data_ptr<float>(),
+                                                        s2.data_ptr<float>(), co.data_ptr<float>(),
+                                                        static_cast<int>(batch), static_cast<int>(I),
+                                                        static_cast<int>(J), lat_major ? 1 : 0);
+    else
+      column_fwd_kernel<kMaxLevels><<<blocks, threads, 0, st>>>(c, ix, nin.data_ptr<float>(), out.data_ptr<float>(),
+                                                                s2.data_ptr<float>(), co.data_ptr<float>(),
+                                                                static_cast<int>(batch), static_cast<int>(I),
+                                                                static_cast<int>(J), lat_major ? 1 : 0);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   } else {
     const float* in = nin.data_ptr<float>();
@@ -133,10 +156,11 @@ at::Tensor column_fwd(const at::Tensor& nin, const at::Tensor& sec2, const at::T
 at::Tensor column_vjp_op(const at::Tensor& nin, const at::Tensor& gout, const at::Tensor& sec2,
                          const at::Tensor& cor, const at::Tensor& level_consts, int64_t batch, int64_t n, int64_t nt,
                          int64_t hum, int64_t hum_terms, std::vector<int64_t> clouds, int64_t vadv, double R,
-                         double kappa, double rv, double cpv, bool lat_major) {
+                         double kappa, double rv, double cpv, bool lat_major, const c10::optional<at::Tensor>& gmat) {
   check_nodal(nin, "nin");
   check_nodal(gout, "gout");
   ColumnConsts c = consts_from(level_consts, n, nt, hum, hum_terms, clouds, vadv, R, kappa, rv, cpv);
+  at::Tensor gm = attach_gmat(c, gmat, nin, n);
   SliceIndex ix = make_slice_index(c);
   const int64_t I = lat_major ? nin.size(2) : nin.size(1), J = lat_major ? nin.size(1) : nin.size(2);
   TORCH_CHECK(gout.size(0) == batch * ix.n_out, "gout slice count mismatch");
@@ -380,9 +404,11 @@ std::vector<at::Tensor> implicit_apply(const at::Tensor& d, const at::Tensor& t,
 
 TORCH_LIBRARY_FRAGMENT(tgcm, m) {
   m.def("column_fwd(Tensor nin, Tensor sec2, Tensor cor, Tensor level_consts, int batch, int n, int nt, int hum, "
-        "int hum_terms, int[] clouds, int vadv, float R, float kappa, float rv, float cpv, bool lat_major=False) -> Tensor");
+        "int hum_terms, int[] clouds, int vadv, float R, float kappa, float rv, float cpv, bool lat_major=False, "
+        "Tensor? gmat=None) -> Tensor");
   m.def("column_vjp(Tensor nin, Tensor gout, Tensor sec2, Tensor cor, Tensor level_consts, int batch, int n, "
-        "int nt, int hum, int hum_terms, int[] clouds, int vadv, float R, float kappa, float rv, float cpv, bool lat_major=False) -> Tensor");
+        "int nt, int hum, int hum_terms, int[] clouds, int vadv, float R, float kappa, float rv, float cpv, bool lat_major=False, "
+        "Tensor? gmat=None) -> Tensor");
   m.def("implicit_apply(Tensor d, Tensor t, Tensor p, Tensor G, Tensor H, Tensor? Minv, Tensor lam, Tensor tref, "
         "Tensor dsig, float R, float eta, int mode) -> Tensor[]");
 }

@@ -41,6 +41,10 @@ struct ColumnConsts {
   float tref[kMaxLevels];
   float idc[kMaxLevels];
   float cs[kMaxLevels];
+  // When set (n x n, row-major): the humidity temperature-difference output
+  // tdiff_k is replaced by Σ_k' gmat[k][k'] tdiff_k' (the geopotential
+  // operator applied in the column instead of on the spectral side).
+  const float* gmat;
 };
 
 struct SliceIndex {
@@ -64,10 +68,11 @@ __host__ __device__ __forceinline__ SliceIndex make_slice_index(const ColumnCons
 }
 
 // ── forward ─────────────────────────────────────────────────────────────────
-template <typename In, typename Out>
+template <int MAXL = kMaxLevels, typename In, typename Out>
 __host__ __device__ void column_forward(const ColumnConsts& c, const SliceIndex& ix, In in, Out out, float s2,
                                         float fcor) {
   const int n = c.n;
+  float td[MAXL];
   const float gx = in(ix.gx), gy = in(ix.gy);
   const float lap = c.hum_terms ? in(ix.lap) : 0.f;
   // pass 1: column totals of the two sigma-flux integrands
@@ -141,7 +146,11 @@ __host__ __device__ void column_forward(const ColumnConsts& c, const SliceIndex&
     if (c.hum_terms) {
       const float rd = c.R * (c.rv - 1.f);
       const float qx = in(ix.qx + k), qy = in(ix.qy + k);
-      out(ix.tdiff + k, q_hum * (T + c.tref[k]) * (c.rv - 1.f));
+      const float tdk = q_hum * (T + c.tref[k]) * (c.rv - 1.f);
+      if (c.gmat)
+        td[k] = tdk;
+      else
+        out(ix.tdiff + k, tdk);
       out(ix.hdiv + k, rd * c.tref[k] * s2 * (qx * gx + qy * gy) + q_hum * lap * c.tref[k] * rd);
       out(ix.hvort + k, rd * c.tref[k] * s2 * (gx * qy - gy * qx));
     }
@@ -149,6 +158,13 @@ __host__ __device__ void column_forward(const ColumnConsts& c, const SliceIndex&
     ff_prev = ff;
     sf_prev = sf;
     se_prev = se;
+  }
+  if (c.hum_terms && c.gmat) {
+    for (int k = 0; k < n; ++k) {
+      float acc = 0.f;
+      for (int j = 0; j < n; ++j) acc += c.gmat[k * n + j] * td[j];
+      out(ix.tdiff + k, acc);
+    }
   }
 }
 
@@ -197,6 +213,19 @@ __host__ __device__ void column_vjp(const ColumnConsts& c, const SliceIndex& ix,
     for (int t = 0; t < c.nt; ++t) g_tr[t][k] = 0.f;
   }
   float g_gx = 0.f, g_gy = 0.f, g_lap = 0.f, g_FE = 0.f, g_FF = 0.f;
+  // cotangent of the per-level tdiff values (through gmat when it is fused)
+  float g_td[MAXL];
+  if (c.hum_terms) {
+    for (int k = 0; k < n; ++k) {
+      if (c.gmat) {
+        float acc = 0.f;
+        for (int j = 0; j < n; ++j) acc += c.gmat[j * n + k] * gout(ix.tdiff + j);
+        g_td[k] = acc;
+      } else {
+        g_td[k] = gout(ix.tdiff + k);
+      }
+    }
+  }
   g_FE -= gout(ix.lnps);
 
   // vertical-advection adjoint: out_k = -1/2 (w_k dx_k + w_{k-1} dx_{k-1});
@@ -320,7 +349,7 @@ __host__ __device__ void column_vjp(const ColumnConsts& c, const SliceIndex& ix,
     if (c.hum_terms) {
       const float rd = c.R * (c.rv - 1.f);
       const float qx = in(ix.qx + k), qy = in(ix.qy + k);
-      const float Gtd = gout(ix.tdiff + k);
+      const float Gtd = g_td[k];
       g_q += Gtd * (T + c.tref[k]) * (c.rv - 1.f);
       g_T[k] += Gtd * q_hum * (c.rv - 1.f);
       const float Ghd = gout(ix.hdiv + k);

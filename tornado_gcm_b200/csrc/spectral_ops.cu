@@ -123,17 +123,188 @@ __host__ __device__ inline void linear_point(const LinearArgs& a, int b, int s, 
   a.y[b * a.ys_b + s * a.ys_c + mr * a.ys_m + l] = acc;
 }
 
-// grid: x over the (m, l) plane of one output channel, y over (b, channel);
-// 32-bit index arithmetic only.
-__global__ void __launch_bounds__(256) spectral_linear_kernel(LinearArgs a) {
+// grid: x over the (m, l) plane of one output channel (one point per thread),
+// y over (b, channel); the channel's terms are warp-uniform read-only loads
+// and addressing inside one batch sample uses 32-bit offsets.
+constexpr int kLinThreads = 256;
+
+struct LinSample {  // one batch sample's input with 32-bit strides
+  const float* x;
+  int sc, sm, L;
+  __device__ __forceinline__ float at(int c, int mr, int l, const float* diag, int pre) const {
+    if (l < 0 || l >= L) return 0.f;
+    const float v = __ldg(x + c * sc + mr * sm + l);
+    return pre >= 0 ? v * __ldg(diag + pre * L + l) : v;
+  }
+};
+
+__device__ __forceinline__ float stencil_fast(const LinearArgs& a, const LinSample& xs, int src, int st, int pre,
+                                              int mr, int l, int mat, int row) {
+  const int L = a.L;
+  switch (st) {
+    case kStId:
+      return xs.at(src, mr, l, a.diag, pre);
+    case kStDlon: {
+      if (mr == 0) return 0.f;
+      const int j = (mr + 1) >> 1;
+      return (mr & 1) ? j * xs.at(src, mr + 1, l, a.diag, pre) : -j * xs.at(src, mr - 1, l, a.diag, pre);
+    }
+    case kStCdlat:
+      return (l + 1 < L ? (l + 2) * __ldg(a.rec_a + mr * L + l + 1) * xs.at(src, mr, l + 1, a.diag, pre) : 0.f) -
+             (l >= 1 ? (l - 1) * __ldg(a.rec_b + mr * L + l - 1) * xs.at(src, mr, l - 1, a.diag, pre) : 0.f);
+    case kStHdlat:
+      return (l + 1 < L ? l * __ldg(a.rec_a + mr * L + l + 1) * xs.at(src, mr, l + 1, a.diag, pre) : 0.f) -
+             (l >= 1 ? (l + 1) * __ldg(a.rec_b + mr * L + l - 1) * xs.at(src, mr, l - 1, a.diag, pre) : 0.f);
+    case kStCdlatT:
+      return (l >= 1 ? (l + 1) * __ldg(a.rec_a + mr * L + l) * xs.at(src, mr, l - 1, a.diag, pre) : 0.f) -
+             (l + 1 < L ? l * __ldg(a.rec_b + mr * L + l) * xs.at(src, mr, l + 1, a.diag, pre) : 0.f);
+    case kStHdlatT:
+      return (l >= 1 ? (l - 1) * __ldg(a.rec_a + mr * L + l) * xs.at(src, mr, l - 1, a.diag, pre) : 0.f) -
+             (l + 1 < L ? (l + 2) * __ldg(a.rec_b + mr * L + l) * xs.at(src, mr, l + 1, a.diag, pre) : 0.f);
+    default:
+      return stencil_val(a, 0, src, st, pre, mr, l, mat, row);  // vertical terms: generic path
+  }
+}
+
+__global__ void __launch_bounds__(kLinThreads) spectral_linear_kernel(LinearArgs a) {
   const int plane = a.M2 * a.L;
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  const int idx = blockIdx.x * kLinThreads + threadIdx.x;
   if (idx >= plane) return;
   const int s = blockIdx.y % a.C_out;
   const int b = blockIdx.y / a.C_out;
   const int mr = idx / a.L;
   const int l = idx - mr * a.L;
-  linear_point(a, b, s, mr, l);
+  LinearArgs ab = a;  // vertical stencils use the generic path on the shifted sample
+  ab.x = a.x + b * a.xs_b;
+  const LinSample xs{ab.x, static_cast<int>(a.xs_c), static_cast<int>(a.xs_m), a.L};
+  const int t0 = __ldg(a.row_ptr + s), t1 = __ldg(a.row_ptr + s + 1);
+  float acc = 0.f;
+  for (int t = t0; t < t1; ++t) {
+    const int* T = a.terms + 7 * t;
+    float v = stencil_fast(ab, xs, __ldg(T + 1), __ldg(T + 2), __ldg(T + 3), mr, l, __ldg(T + 5), __ldg(T + 6));
+    const int post = __ldg(T + 4);
+    if (post >= 0) v *= __ldg(a.diag + post * a.L + l);
+    acc = fmaf(__ldg(a.coef + t), v, acc);
+  }
+  float* yrow = a.y + b * a.ys_b + s * a.ys_c + mr * a.ys_m;
+  yrow[l] = acc;
+  if (l == a.L - 1)
+    for (long long z = a.L; z < a.ys_m; ++z) yrow[z] = 0.f;  // zero the 16-byte row padding
+}
+
+// Row kernel: one warp per (b, output channel, m-row); lane handles
+// l = lane + 32 j (j < NL).  For each term the warp reads the source row once
+// (coalesced, pre-diagonal applied) into a per-warp shared buffer, from which
+// the ±1-in-l neighbours of the latitudinal stencils are taken; ∂/∂λ switches
+// the source row to the paired ±m row.  Vertical terms use the per-point path.
+constexpr int kRowWarps = 8;
+
+template <int NL>
+__global__ void __launch_bounds__(32 * kRowWarps) spectral_linear_rows_kernel(LinearArgs a) {
+  __shared__ float sbuf[kRowWarps][32 * NL + 2];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mr = blockIdx.x * kRowWarps + warp;
+  if (mr >= a.M2) return;
+  const int s = blockIdx.y % a.C_out;
+  const int b = blockIdx.y / a.C_out;
+  const int L = a.L;
+  const float* xb = a.x + b * a.xs_b;
+  float* buf = sbuf[warp] + 1;  // buf[l] for l in [-1, 32*NL]
+  float acc[NL];
+#pragma unroll
+  for (int j = 0; j < NL; ++j) acc[j] = 0.f;
+  const int t0 = __ldg(a.row_ptr + s), t1 = __ldg(a.row_ptr + s + 1);
+  for (int t = t0; t < t1; ++t) {
+    const int* T = a.terms + 7 * t;
+    const int src = __ldg(T + 1), st = __ldg(T + 2), pre = __ldg(T + 3), post = __ldg(T + 4);
+    const float cf = __ldg(a.coef + t);
+    if (st == kStVert || st == kStVertT) {
+      LinearArgs ab = a;
+      ab.x = xb;
+      const int mat = __ldg(T + 5), row = __ldg(T + 6);
+#pragma unroll
+      for (int j = 0; j < NL; ++j) {
+        const int l = lane + 32 * j;
+        if (l < L) {
+          float v = stencil_val(ab, 0, src, st, pre, mr, l, mat, row);
+          if (post >= 0) v *= __ldg(a.diag + post * L + l);
+          acc[j] = fmaf(cf, v, acc[j]);
+        }
+      }
+      continue;
+    }
+    int srow = mr;
+    float fac = 1.f;
+    if (st == kStDlon) {
+      if (mr == 0) continue;
+      const int jm = (mr + 1) >> 1;
+      srow = (mr & 1) ? mr + 1 : mr - 1;
+      fac = (mr & 1) ? static_cast<float>(jm) : -static_cast<float>(jm);
+    }
+    const float* xr = xb + src * a.xs_c + srow * a.xs_m;
+    float xv[NL];
+#pragma unroll
+    for (int j = 0; j < NL; ++j) {
+      const int l = lane + 32 * j;
+      float v = 0.f;
+      if (l < L) {
+        v = __ldg(xr + l);
+        if (pre >= 0) v *= __ldg(a.diag + pre * L + l);
+      }
+      xv[j] = v;
+    }
+    const bool lat = st == kStCdlat || st == kStHdlat || st == kStCdlatT || st == kStHdlatT;
+    if (lat) {
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < NL; ++j) buf[lane + 32 * j] = xv[j];
+      if (lane == 0) {
+        buf[-1] = 0.f;
+        buf[32 * NL] = 0.f;
+      }
+      __syncwarp();
+    }
+#pragma unroll
+    for (int j = 0; j < NL; ++j) {
+      const int l = lane + 32 * j;
+      if (l >= L) continue;
+      float v;
+      if (!lat) {
+        v = fac * xv[j];
+      } else {
+        const float xp = (l + 1 < L) ? buf[l + 1] : 0.f;
+        const float xm = (l >= 1) ? buf[l - 1] : 0.f;
+        const float* ra = a.rec_a + mr * L;
+        const float* rb = a.rec_b + mr * L;
+        if (st == kStCdlat)
+          v = (l + 1 < L ? (l + 2) * __ldg(ra + l + 1) * xp : 0.f) - (l >= 1 ? (l - 1) * __ldg(rb + l - 1) * xm : 0.f);
+        else if (st == kStHdlat)
+          v = (l + 1 < L ? l * __ldg(ra + l + 1) * xp : 0.f) - (l >= 1 ? (l + 1) * __ldg(rb + l - 1) * xm : 0.f);
+        else if (st == kStCdlatT)
+          v = (l >= 1 ? (l + 1) * __ldg(ra + l) * xm : 0.f) - (l + 1 < L ? l * __ldg(rb + l) * xp : 0.f);
+        else
+          v = (l >= 1 ? (l - 1) * __ldg(ra + l) * xm : 0.f) - (l + 1 < L ? (l + 2) * __ldg(rb + l) * xp : 0.f);
+      }
+      if (post >= 0) v *= __ldg(a.diag + post * L + l);
+      acc[j] = fmaf(cf, v, acc[j]);
+    }
+  }
+  float* yrow = a.y + b * a.ys_b + s * a.ys_c + mr * a.ys_m;
+#pragma unroll
+  for (int j = 0; j < NL; ++j) {
+    const int l = lane + 32 * j;
+    if (l < L)
+      yrow[l] = acc[j];
+    else if (l < a.ys_m)
+      yrow[l] = 0.f;  // 16-byte row padding
+  }
+  for (long long z = 32 * NL + lane; z < a.ys_m; z += 32) yrow[z] = 0.f;
+}
+
+template <int NL>
+static void launch_rows(const LinearArgs& a, cudaStream_t st) {
+  dim3 grid(static_cast<unsigned>((a.M2 + kRowWarps - 1) / kRowWarps), static_cast<unsigned>(a.B * a.C_out));
+  spectral_linear_rows_kernel<NL><<<grid, 32 * kRowWarps, 0, st>>>(a);
 }
 
 // x: (B, C_in, M2, Lx) ; returns y: (B, C_out, M2, Ly) with Ly = out_lpad (>= L), pad zero.
@@ -142,8 +313,9 @@ at::Tensor spectral_linear(const at::Tensor& x, int64_t L, int64_t C_out, int64_
                            const at::Tensor& rec_a, const at::Tensor& rec_b, const at::Tensor& mats, int64_t nlev) {
   TORCH_CHECK(x.dim() == 4 && x.scalar_type() == at::kFloat && x.stride(3) == 1, "x must be (B, C, M2, L) fp32");
   const int64_t B = x.size(0), M2 = x.size(2);
-  auto y = (out_lpad > L) ? at::zeros({B, C_out, M2, out_lpad}, x.options())
-                          : at::empty({B, C_out, M2, out_lpad}, x.options());
+  // the CUDA kernel writes the padding columns itself; the CPU loop does not
+  auto y = (out_lpad > L && !x.is_cuda()) ? at::zeros({B, C_out, M2, out_lpad}, x.options())
+                                          : at::empty({B, C_out, M2, out_lpad}, x.options());
   LinearArgs a;
   a.x = x.data_ptr<float>();
   a.y = y.data_ptr<float>();
@@ -161,8 +333,18 @@ at::Tensor spectral_linear(const at::Tensor& x, int64_t L, int64_t C_out, int64_
   if (x.is_cuda()) {
     c10::cuda::CUDAGuard guard(x.device());
     TORCH_CHECK(B * C_out <= 65535 && M2 * L < (1LL << 31), "spectral_linear: launch grid too large");
-    dim3 grid(static_cast<unsigned>((M2 * L + 255) / 256), static_cast<unsigned>(B * C_out));
-    spectral_linear_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+    TORCH_CHECK(x.stride(1) < (1LL << 31) && x.size(1) * x.stride(1) < (1LL << 31),
+                "spectral_linear: one batch sample must fit 32-bit offsets");
+    auto st = at::cuda::getCurrentCUDAStream();
+    if (L <= 32) launch_rows<1>(a, st);
+    else if (L <= 64) launch_rows<2>(a, st);
+    else if (L <= 96) launch_rows<3>(a, st);
+    else if (L <= 160) launch_rows<5>(a, st);
+    else if (L <= 288) launch_rows<9>(a, st);
+    else {
+      dim3 grid(static_cast<unsigned>((M2 * L + kLinThreads - 1) / kLinThreads), static_cast<unsigned>(B * C_out));
+      spectral_linear_kernel<<<grid, kLinThreads, 0, st>>>(a);
+    }
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   } else {
     for (int b = 0; b < B; ++b)
@@ -386,38 +568,93 @@ __global__ void sil3_stage_kernel(StageArgs a, int adjoint) {
   }
 }
 
-// Column-parallel stage kernel for a compile-time level count N: one thread
-// per (b, m, l) column with consecutive threads on consecutive l, so every
-// channel load/store of a warp is one contiguous row segment; G, H and the
-// level vectors sit in shared memory (broadcast reads) and the per-l Schur
-// inverse is read from its l-fastest transposed copy (coalesced).  Same
-// arithmetic as stage_column_fwd / stage_column_adj.
+template <bool TRANS>
+struct SMat {  // n x n matrix in shared memory with padded row stride
+  const float* m;
+  int ld;
+  __device__ __forceinline__ float operator()(int i, int j) const { return TRANS ? m[j * ld + i] : m[i * ld + j]; }
+};
+
+template <bool TRANS>
+struct GMat {  // per-l matrix from its l-fastest global copy
+  const float* m;
+  long long ms;
+  int n;
+  __device__ __forceinline__ float operator()(int i, int j) const {
+    return TRANS ? m[(j * n + i) * ms] : m[(i * n + j) * ms];
+  }
+};
+
+// yo[kk] = Σ_j M(q*P + kk, j) x_j; x is spread over the Q lanes of the group
+// (lane gl + qq owns x[qq*P .. qq*P + P-1]) and gathered with shuffles.
+template <int P, int Q, typename Mat>
+__device__ __forceinline__ void mv_group(const Mat& M, const float (&xo)[P], float (&yo)[P], int q, int gl) {
+#pragma unroll
+  for (int kk = 0; kk < P; ++kk) yo[kk] = 0.f;
+#pragma unroll 1
+  for (int qq = 0; qq < Q; ++qq) {
+#pragma unroll
+    for (int jj = 0; jj < P; ++jj) {
+      const float xv = __shfl_sync(0xffffffffu, xo[jj], gl + qq);
+#pragma unroll
+      for (int kk = 0; kk < P; ++kk) yo[kk] = fmaf(M(q * P + kk, qq * P + jj), xv, yo[kk]);
+    }
+  }
+}
+
+// Quarter-split stage kernel: Q = 4 threads share one (b, m, l) column, each
+// owning N / 4 consecutive levels; vectors are exchanged with warp shuffles
+// inside the 4-lane group, so a thread keeps 3 x N/4 values in registers
+// instead of 3 x N (occupancy) while the arithmetic is that of
+// stage_column_fwd / stage_column_adj.  A warp covers 8 consecutive l of one
+// (b, m) row: every channel access is a 32-byte run per quarter.
 template <int N>
-__global__ void __launch_bounds__(256) sil3_stage_cols_kernel(StageArgs a, int adjoint) {
-  __shared__ float sG[N * N], sH[N * N], sTr[N], sDs[N];
+__global__ void __launch_bounds__(256) sil3_stage_q4_kernel(StageArgs a, int adjoint) {
+  constexpr int Q = 4;
+  constexpr int P = N / Q;
+  constexpr int LD = N + 1;  // padded row stride of G, H in shared memory (conflict-free)
+  __shared__ float sG[N * LD], sH[N * LD], sTr[N], sDs[N];
   for (int i = threadIdx.x; i < N * N; i += blockDim.x) {
-    sG[i] = a.G[i];
-    sH[i] = a.H[i];
+    sG[(i / N) * LD + i % N] = a.G[i];
+    sH[(i / N) * LD + i % N] = a.H[i];
   }
   for (int i = threadIdx.x; i < N; i += blockDim.x) {
     sTr[i] = a.tref[i];
     sDs[i] = a.dsig[i];
   }
   __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int q = lane & (Q - 1);
+  const int gl = lane & ~(Q - 1);
   const int total = a.B * a.M2 * a.L;
-  const int t = blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= total) return;
-  const int bm = t / a.L;
-  const int l = t - bm * a.L;
+  const int t = blockIdx.x * (blockDim.x / Q) + threadIdx.x / Q;
+  const bool valid = t < total;
+  const int tt = valid ? t : 0;
+  const int bm = tt / a.L;
+  const int l = tt - bm * a.L;
   const int b = bm / a.M2;
   const int mr = bm - b * a.M2;
   const long long cs = static_cast<long long>(a.M2) * a.L;
   const long long base = static_cast<long long>(b) * a.C * cs + static_cast<long long>(mr) * a.L + l;
   const float* mi = a.MinvT + l;
-  const long long ms = a.L;  // stride between consecutive (i, j) entries of MinvT
+  const long long ms = a.L;
   const float f = a.filt ? a.filt[l] : 1.f;
   const float lam = a.lam[l];
   const float el = a.eta * lam;
+  const unsigned full = 0xffffffffu;
+
+  auto group_sum = [&](float v) -> float {
+    v += __shfl_xor_sync(full, v, 1);
+    v += __shfl_xor_sync(full, v, 2);
+    return v;
+  };
+  const SMat<false> G_{sG, LD};
+  const SMat<false> H_{sH, LD};
+  const SMat<true> Gt{sG, LD};
+  const SMat<true> Ht{sH, LD};
+  const GMat<false> Mi{mi, ms, N};
+  const GMat<true> Mit{mi, ms, N};
+
   if (!adjoint) {
     auto finish = [&](float v) -> float {
       if (!a.final_stage) return v;
@@ -427,64 +664,54 @@ __global__ void __launch_bounds__(256) sil3_stage_cols_kernel(StageArgs a, int a
     };
     auto expl = [&](int c) -> float {
       float v = a.y0[base + c * cs] + a.cp * a.P[base + c * cs];
-      for (int j = 0; j < a.nE; ++j) v += a.ce[j] * a.E[j][base + c * cs];
+#pragma unroll
+      for (int j = 0; j < kStageMaxE; ++j)
+        if (j < a.nE) v += a.ce[j] * a.E[j][base + c * cs];
       return v;
     };
-    for (int c = 0; c < N; ++c) a.out[base + c * cs] = finish(expl(c));
-    for (int c = 3 * N + 1; c < a.C; ++c) a.out[base + c * cs] = finish(expl(c));
-    float x[N], y[N], z[N];
-    float zp = a.y0[base + 3 * N * cs] + (a.y2 ? a.y2[base + 3 * N * cs] : 0.f);
-#pragma unroll
-    for (int k = 0; k < N; ++k) {  // x = z_δ, y = z_T
-      x[k] = a.y0[base + (N + k) * cs] + (a.y2 ? a.y2[base + (N + k) * cs] : 0.f);
-      y[k] = a.y0[base + (2 * N + k) * cs] + (a.y2 ? a.y2[base + (2 * N + k) * cs] : 0.f);
+    if (valid) {
+      for (int c = q; c < N; c += Q) a.out[base + c * cs] = finish(expl(c));
+      for (int c = 3 * N + 1 + q; c < a.C; c += Q) a.out[base + c * cs] = finish(expl(c));
     }
+    float x[P], y[P], z[P], tmp[P];
+    const float zp = valid ? a.y0[base + 3 * N * cs] + (a.y2 ? a.y2[base + 3 * N * cs] : 0.f) : 0.f;
     float zpg = 0.f;
 #pragma unroll
-    for (int k = 0; k < N; ++k) zpg += sDs[k] * x[k];
-    // z ← rd = expl_δ + cg·(−λ(G z_T + R Tr z_p));  x ← rt = expl_T − cg·H z_δ
-#pragma unroll
-    for (int i = 0; i < N; ++i) {
-      float gt = 0.f;
-#pragma unroll
-      for (int j = 0; j < N; ++j) gt += sG[i * N + j] * y[j];
-      z[i] = expl(N + i) + a.cg * (-lam * (gt + a.R * sTr[i] * zp));
+    for (int kk = 0; kk < P; ++kk) {
+      const int k = q * P + kk;
+      x[kk] = valid ? a.y0[base + (N + k) * cs] + (a.y2 ? a.y2[base + (N + k) * cs] : 0.f) : 0.f;
+      y[kk] = valid ? a.y0[base + (2 * N + k) * cs] + (a.y2 ? a.y2[base + (2 * N + k) * cs] : 0.f) : 0.f;
+      zpg += sDs[k] * x[kk];
     }
+    zpg = group_sum(zpg);
+    mv_group<P, Q>(G_, y, tmp, q, gl);  // G z_T
 #pragma unroll
-    for (int i = 0; i < N; ++i) {
-      float hd = 0.f;
-#pragma unroll
-      for (int j = 0; j < N; ++j) hd += sH[i * N + j] * x[j];
-      y[i] = expl(2 * N + i) - a.cg * hd;
+    for (int kk = 0; kk < P; ++kk) {
+      const int i = q * P + kk;
+      z[kk] = (valid ? expl(N + i) : 0.f) + a.cg * (-lam * (tmp[kk] + a.R * sTr[i] * zp));
     }
-    const float rp = expl(3 * N) - a.cg * zpg;
-    // z ← rd − el·(G rt + R Tr rp)   (rt in y)
+    mv_group<P, Q>(H_, x, tmp, q, gl);  // H z_δ
 #pragma unroll
-    for (int i = 0; i < N; ++i) {
-      float gt = 0.f;
+    for (int kk = 0; kk < P; ++kk) y[kk] = (valid ? expl(2 * N + q * P + kk) : 0.f) - a.cg * tmp[kk];
+    const float rp = (valid ? expl(3 * N) : 0.f) - a.cg * zpg;
+    mv_group<P, Q>(G_, y, tmp, q, gl);  // G rt
 #pragma unroll
-      for (int j = 0; j < N; ++j) gt += sG[i * N + j] * y[j];
-      z[i] = z[i] - el * (gt + a.R * sTr[i] * rp);
-    }
-    // x ← δ = Minv z
+    for (int kk = 0; kk < P; ++kk) z[kk] -= el * (tmp[kk] + a.R * sTr[q * P + kk] * rp);
+    mv_group<P, Q>(Mi, z, x, q, gl);  // δ = Minv z
     float sp = 0.f;
 #pragma unroll
-    for (int i = 0; i < N; ++i) {
-      float acc = 0.f;
+    for (int kk = 0; kk < P; ++kk) sp += sDs[q * P + kk] * x[kk];
+    sp = group_sum(sp);
+    mv_group<P, Q>(H_, x, tmp, q, gl);  // H δ
+    if (valid) {
 #pragma unroll
-      for (int j = 0; j < N; ++j) acc += mi[(i * N + j) * ms] * z[j];
-      x[i] = acc;
-      sp += sDs[i] * acc;
+      for (int kk = 0; kk < P; ++kk) {
+        const int i = q * P + kk;
+        a.out[base + (N + i) * cs] = finish(x[kk]);
+        a.out[base + (2 * N + i) * cs] = finish(y[kk] - a.eta * tmp[kk]);
+      }
+      if (q == 0) a.out[base + 3 * N * cs] = finish(rp - a.eta * sp);
     }
-#pragma unroll
-    for (int i = 0; i < N; ++i) {
-      float hd = 0.f;
-#pragma unroll
-      for (int j = 0; j < N; ++j) hd += sH[i * N + j] * x[j];
-      a.out[base + (N + i) * cs] = finish(x[i]);
-      a.out[base + (2 * N + i) * cs] = finish(y[i] - a.eta * hd);
-    }
-    a.out[base + 3 * N * cs] = finish(rp - a.eta * sp);
     return;
   }
   // adjoint
@@ -498,54 +725,46 @@ __global__ void __launch_bounds__(256) sil3_stage_cols_kernel(StageArgs a, int a
   auto scatter = [&](int c, float r, float zextra, bool has_z) {
     a.g_y0[base + c * cs] = r + zextra;
     a.g_P[base + c * cs] = a.cp * r;
-    for (int j = 0; j < a.nE; ++j) a.g_E[j][base + c * cs] = a.ce[j] * r;
+#pragma unroll
+    for (int j = 0; j < kStageMaxE; ++j)
+      if (j < a.nE) a.g_E[j][base + c * cs] = a.ce[j] * r;
     if (a.g_y2) a.g_y2[base + c * cs] = has_z ? zextra : 0.f;
   };
-  for (int c = 0; c < N; ++c) scatter(c, gpre(c), 0.f, false);
-  for (int c = 3 * N + 1; c < a.C; ++c) scatter(c, gpre(c), 0.f, false);
-  float x[N], y[N];
-  const float pp = gpre(3 * N);
-#pragma unroll
-  for (int k = 0; k < N; ++k) y[k] = gpre(2 * N + k);  // t̄
-  float r[N];
-#pragma unroll
-  for (int i = 0; i < N; ++i) {
-    float htt = 0.f;
-#pragma unroll
-    for (int j = 0; j < N; ++j) htt += sH[j * N + i] * y[j];
-    r[i] = gpre(N + i) - a.eta * htt - a.eta * sDs[i] * pp;
+  if (valid) {
+    for (int c = q; c < N; c += Q) scatter(c, gpre(c), 0.f, false);
+    for (int c = 3 * N + 1 + q; c < a.C; c += Q) scatter(c, gpre(c), 0.f, false);
   }
+  float x[P], y[P], r[P], tmp[P];
+  const float pp = valid ? gpre(3 * N) : 0.f;
+#pragma unroll
+  for (int kk = 0; kk < P; ++kk) y[kk] = valid ? gpre(2 * N + q * P + kk) : 0.f;  // t̄
+  mv_group<P, Q>(Ht, y, tmp, q, gl);  // Hᵀ t̄
+#pragma unroll
+  for (int kk = 0; kk < P; ++kk) {
+    const int i = q * P + kk;
+    r[kk] = (valid ? gpre(N + i) : 0.f) - a.eta * tmp[kk] - a.eta * sDs[i] * pp;
+  }
+  mv_group<P, Q>(Mit, r, x, q, gl);  // od = Minvᵀ r
   float trd = 0.f;
 #pragma unroll
-  for (int i = 0; i < N; ++i) {  // x = od = Minvᵀ r
-    float acc = 0.f;
+  for (int kk = 0; kk < P; ++kk) trd += sTr[q * P + kk] * x[kk];
+  trd = group_sum(trd);
+  mv_group<P, Q>(Gt, x, tmp, q, gl);  // Gᵀ od
 #pragma unroll
-    for (int j = 0; j < N; ++j) acc += mi[(j * N + i) * ms] * r[j];
-    x[i] = acc;
-    trd += sTr[i] * acc;
-  }
-#pragma unroll
-  for (int i = 0; i < N; ++i) {  // y = ot = t̄ − el Gᵀ od
-    float gtr = 0.f;
-#pragma unroll
-    for (int j = 0; j < N; ++j) gtr += sG[j * N + i] * x[j];
-    y[i] = y[i] - el * gtr;
-  }
+  for (int kk = 0; kk < P; ++kk) y[kk] -= el * tmp[kk];  // ot
   const float op = pp - el * a.R * trd;
-  float dsop = 0.f;
+  mv_group<P, Q>(Ht, y, tmp, q, gl);  // Hᵀ ot
+  float gta[P];
+  mv_group<P, Q>(Gt, x, gta, q, gl);  // Gᵀ od
+  if (valid) {
 #pragma unroll
-  for (int i = 0; i < N; ++i) {
-    float htb = 0.f, gta = 0.f;
-#pragma unroll
-    for (int j = 0; j < N; ++j) {
-      htb += sH[j * N + i] * y[j];
-      gta += sG[j * N + i] * x[j];
+    for (int kk = 0; kk < P; ++kk) {
+      const int i = q * P + kk;
+      scatter(N + i, x[kk], a.cg * (-tmp[kk] - sDs[i] * op), true);
+      scatter(2 * N + i, y[kk], a.cg * (-lam * gta[kk]), true);
     }
-    scatter(N + i, x[i], a.cg * (-htb - sDs[i] * op), true);
-    scatter(2 * N + i, y[i], a.cg * (-lam * gta), true);
+    if (q == 0) scatter(3 * N, op, a.cg * (-lam * a.R * trd), true);
   }
-  (void)dsop;
-  scatter(3 * N, op, a.cg * (-lam * a.R * trd), true);
 }
 
 static const float* ptr_or_null(const c10::optional<at::Tensor>& t) {
@@ -556,8 +775,8 @@ static void run_stage(StageArgs& a, const at::Tensor& like, int adjoint) {
   if (like.is_cuda() && a.n == 32 && a.MinvT != nullptr) {
     c10::cuda::CUDAGuard guard(like.device());
     const long long total = static_cast<long long>(a.B) * a.M2 * a.L;
-    sil3_stage_cols_kernel<32><<<static_cast<unsigned>((total + 255) / 256), 256, 0,
-                                 at::cuda::getCurrentCUDAStream()>>>(a, adjoint);
+    sil3_stage_q4_kernel<32><<<static_cast<unsigned>((total + 63) / 64), 256, 0,
+                               at::cuda::getCurrentCUDAStream()>>>(a, adjoint);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   } else if (like.is_cuda()) {
     c10::cuda::CUDAGuard guard(like.device());

@@ -19,7 +19,7 @@
 from __future__ import annotations
 
 import dataclasses
-from typing import Sequence
+from typing import Optional, Sequence
 
 import numpy as np
 import torch
@@ -47,6 +47,9 @@ class ColumnSpec:
     cor: np.ndarray
     eq: object = None
     _dev: dict = dataclasses.field(default_factory=dict)
+    # (n, n) geopotential matrix applied to the humidity tdiff outputs inside the
+    # column kernel (the spectral post-processing then skips its vertical term)
+    gmat: Optional[torch.Tensor] = None
 
     @classmethod
     def from_equation(cls, eq: pe.PrimitiveEquationsSigma, tracer_keys: Sequence[str]) -> "ColumnSpec":
@@ -78,6 +81,21 @@ class ColumnSpec:
                  torch.as_tensor(self.cor, dtype=torch.float32, device=device))
             self._dev[key] = d
         return d
+
+    def device_gmat(self, device):
+        if self.gmat is None:
+            return None
+        key = "gmat:" + str(device)
+        g = self._dev.get(key)
+        if g is None:
+            g = self.gmat.to(device=device, dtype=torch.float32).contiguous()
+            self._dev[key] = g
+        return g
+
+    def with_fused_g(self) -> "ColumnSpec":
+        """A copy whose column kernel applies the geopotential matrix G to tdiff."""
+        g = torch.as_tensor(np.asarray(self.eq._G_matrix), dtype=torch.float32) if self.hum_terms else None
+        return dataclasses.replace(self, gmat=g, _dev={})
 
     def args(self):
         return (self.level_consts, self.n, len(self.tracer_keys), self.hum, self.hum_terms, list(self.clouds),
@@ -349,14 +367,16 @@ class ColumnLatFn(torch.autograd.Function):
         ctx.save_for_backward(nin)
         ops = _ext.require("column tendency")
         s2, co = spec.device_consts(nin.device)
-        return ops.column_fwd(nin.contiguous(), s2, co, *_args_with_batch(spec, batch), True)
+        return ops.column_fwd(nin.contiguous(), s2, co, *_args_with_batch(spec, batch), True,
+                              spec.device_gmat(nin.device))
 
     @staticmethod
     def backward(ctx, gout):
         (nin,) = ctx.saved_tensors
         ops = _ext.require("column tendency VJP")
         s2, co = ctx.spec.device_consts(nin.device)
-        g = ops.column_vjp(nin, gout.contiguous(), s2, co, *_args_with_batch(ctx.spec, ctx.batch), True)
+        g = ops.column_vjp(nin, gout.contiguous(), s2, co, *_args_with_batch(ctx.spec, ctx.batch), True,
+                           ctx.spec.device_gmat(nin.device))
         return g, None, None
 
 
@@ -409,8 +429,9 @@ class PackedSIL3:
         self.keys = tuple(tracer_keys)
         self.n = eq.vertical.layers
         self.pre = spectral.explicit_pre_recipe(eq, self.keys)
-        self.post = spectral.explicit_post_recipe(eq, self.keys)
-        self.spec = ColumnSpec.from_equation(eq, self.keys)
+        # the column kernel applies G to the moist tdiff term; the post recipe keeps only ∇²
+        self.post = spectral.explicit_post_recipe(eq, self.keys, g_fused=True)
+        self.spec = ColumnSpec.from_equation(eq, self.keys).with_fused_g()
         self.ch = spectral.packed_channels(self.n, self.keys)
         self.filter_scaling = np.asarray(filter_scaling, dtype=np.float64)
         self.clamp = float(clamp_abs)

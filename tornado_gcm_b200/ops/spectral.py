@@ -217,7 +217,8 @@ def explicit_pre_recipe(eq, tracer_keys) -> SpectralRecipe:
     return b.recipe(ch["C"], s)
 
 
-def explicit_post_recipe(eq, tracer_keys) -> SpectralRecipe:
+def explicit_post_recipe(eq, tracer_keys, g_fused: bool = False) -> SpectralRecipe:
+    """``g_fused``: the column kernel already applied G to the tdiff outputs."""
     grid = eq.grid
     n = eq.vertical.layers
     inv_r = 1.0 / grid.radius
@@ -231,7 +232,7 @@ def explicit_post_recipe(eq, tracer_keys) -> SpectralRecipe:
     o_hd, o_hv = o_td + n, o_td + 2 * n
     o_lnps = (6 + 3 * nt + 3 * h) * n
     C, CL, LC = b.CLIP, b.CLIP, b.LAPCLIP
-    if h:
+    if h and not g_fused:
         b.mats.append(np.asarray(eq._G_matrix, dtype=np.float64))
     for k in range(n):
         # vorticity: −(∂λ Fv − H Fu) + hum_vort
@@ -253,7 +254,10 @@ def explicit_post_recipe(eq, tracer_keys) -> SpectralRecipe:
         if h:
             b.add(ch["vort"] + k, o_hv + k, ID, post=CL)
             b.add(ch["div"] + k, o_hd + k, ID, post=CL, coef=-1.0)
-            b.add(ch["div"] + k, o_td, VERT, post=LC, coef=-1.0, mat=0, row=k)
+            if g_fused:
+                b.add(ch["div"] + k, o_td + k, ID, post=LC, coef=-1.0)
+            else:
+                b.add(ch["div"] + k, o_td, VERT, post=LC, coef=-1.0, mat=0, row=k)
     b.add(ch["lnps"], o_lnps, ID, post=CL)
     return b.recipe(o_lnps + 1, ch["C"])
 

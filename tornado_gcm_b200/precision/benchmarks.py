@@ -273,6 +273,29 @@ def _stage_case(args):
     return step, 0.0
 
 
+def _recipe_case(args):
+    import numpy as np
+
+    from tornado_gcm_b200.core import coordinate_systems as cs, primitive_equations as pe
+    from tornado_gcm_b200.core import sigma_coordinates as sc, spherical_harmonic as sh
+    from tornado_gcm_b200.ops import spectral
+    from tornado_gcm_b200.utils.units import SimUnits
+
+    g = getattr(sh.Grid, args.grid)(precision="tf32")
+    n = 32
+    coords = cs.CoordinateSystem(g, sc.SigmaCoordinates.equidistant(n))
+    keys = ("specific_cloud_ice_water_content", "specific_cloud_liquid_water_content", "specific_humidity")
+    eq = pe.PrimitiveEquationsSigma(np.linspace(210, 290, n), torch.zeros(g.modal_shape), coords,
+                                    SimUnits.from_si(), humidity_key="specific_humidity", cloud_keys=keys[:2])
+    rec = {"pre": spectral.explicit_pre_recipe(eq, keys), "post": spectral.explicit_post_recipe(eq, keys)}[args.recipe]
+    if args.transpose:
+        rec = rec.transpose()
+    L = g.modal_shape[-1]
+    x = torch.randn(args.batch, rec.c_in, *g.modal_shape, device="cuda")
+    lp = (L + 3) // 4 * 4
+    return (lambda: rec.apply(x, lp)), 0.0
+
+
 def _linear_case(args):
     from tornado_gcm_b200.ops import _ext
 
@@ -336,7 +359,9 @@ def gemm_cycle_breakdown(fn) -> list:
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description="kernel micro-benchmarks (CUDA events)")
-    ap.add_argument("case", choices=["mlp", "sht", "stage", "linear", "bgemm"])
+    ap.add_argument("case", choices=["mlp", "sht", "stage", "linear", "bgemm", "recipe"])
+    ap.add_argument("--recipe", default="pre", choices=["pre", "post"])
+    ap.add_argument("--transpose", action="store_true")
     ap.add_argument("--mode", default="fwd", choices=["fwd", "dgrad", "wgrad"])
     ap.add_argument("--groups", type=int, default=1292)
     ap.add_argument("--m", type=int, default=128)
@@ -355,7 +380,7 @@ def main(argv=None) -> None:
     ap.add_argument("--cycles", action="store_true", help="print the GEMM cycle breakdown of one call")
     args = ap.parse_args(argv)
     fn, flops = {"mlp": _mlp_case, "sht": _sht_case, "stage": _stage_case, "linear": _linear_case,
-                 "bgemm": _bgemm_case}[args.case](args)
+                 "bgemm": _bgemm_case, "recipe": _recipe_case}[args.case](args)
     tb = TimingBenchmark(warmup=args.warmup, iterations=args.iters)
     r = tb.time_fn(args.case, fn)
     out = {"case": args.case, "mean_ms": r.mean_ms, "min_ms": r.min_ms}
