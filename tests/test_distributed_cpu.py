@@ -1,0 +1,110 @@
+"""Multi-process host logic on CPU ranks (gloo): gradient averaging, the packed
+metric all-reduce, and failure detection by host-side injection (a rank that
+raises before a collective; the survivors' collective ends with an error
+instead of hanging)."""
+
+import datetime
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _init(rank, world, port, timeout_s=30.0):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=timeout_s))
+
+
+def _worker_reduce(rank, world, port, q):
+    try:
+        _init(rank, world, port)
+        from tornado_gcm_b200.parallel.ddp import GradientAllReducer
+        from tornado_gcm_b200.parallel.metrics import all_reduce_metrics
+
+        torch.manual_seed(0)
+        model = torch.nn.Sequential(torch.nn.Linear(5, 7), torch.nn.Linear(7, 3))
+        red = GradientAllReducer(list(model.parameters()), bucket_mb=0.0001)
+        red.broadcast_parameters()
+        red.zero()
+        x = torch.full((4, 5), float(rank + 1))
+        model(x).sum().backward()
+        local = [p.grad.clone() for p in model.parameters()]
+        red.reduce()
+        gathered = [torch.zeros_like(t) for t in local for _ in range(1)]
+        sums = []
+        for t in local:
+            tt = t.clone()
+            dist.all_reduce(tt)
+            sums.append(tt / world)
+        ok_grads = all(torch.allclose(p.grad, s, atol=1e-6) for p, s in zip(model.parameters(), sums))
+        m = all_reduce_metrics({"loss": torch.tensor(float(rank)), "n": 2.0})
+        q.put((rank, ok_grads, m["loss"], m["n"], len(gathered)))
+        dist.destroy_process_group()
+    except Exception:  # pragma: no cover - reported to the parent
+        q.put((rank, traceback.format_exc()))
+
+
+def test_gradient_allreducer_and_metrics_gloo():
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker_reduce, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for r in res:
+        assert len(r) == 5, r[1]
+        _, ok, loss, n, _ = r
+        assert ok
+        assert loss == pytest.approx(0.5)
+        assert n == pytest.approx(2.0)
+
+
+def _worker_failure(rank, world, port, q):
+    try:
+        _init(rank, world, port, timeout_s=5.0)
+        t = torch.ones(3)
+        dist.all_reduce(t)  # both ranks healthy here
+        if rank == 1:
+            raise RuntimeError("injected failure on rank 1")
+        try:
+            dist.all_reduce(t)  # rank 1 never joins: must end with an error, not hang
+            q.put((rank, "completed"))
+        except Exception as exc:
+            q.put((rank, "error:" + type(exc).__name__))
+    except RuntimeError as exc:
+        q.put((rank, "raised:" + str(exc)))
+
+
+def test_peer_failure_surfaces_as_error_not_hang():
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker_failure, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():  # pragma: no cover
+            p.kill()
+    assert res[1].startswith("raised:")
+    assert res[0].startswith("error:")

@@ -1,0 +1,170 @@
+// Fused gradient all-reduce over NVLink peer memory (sm_100a).
+//
+// Every rank's fp32 gradient buffer lives in symmetric memory, so each rank
+// holds device pointers to all peers' buffers and signal pads.  One kernel
+// does the whole mean all-reduce ("two-shot" in one launch):
+//
+//   phase 0  per-block barrier: block b of every rank announces, in every
+//            peer's signal pad, that its gradients are ready (the kernel runs
+//            after backward on the rank's stream);
+//   phase 1  reduce-scatter + all-gather: rank r owns chunk r; block b of
+//            rank r reads its slice of chunk r from all W peers (16-byte P2P
+//            loads), sums, multiplies by 1/W (the averaging, fused) and writes
+//            the result into chunk r of every peer (P2P stores);
+//   phase 2  per-block barrier, so that no rank uses its buffer before every
+//            peer's pushes into it have landed.
+//
+// Signals are epoch counters (uint32) in the pads: pad[phase][src_rank][block]
+// (2 x 8 x blocks words per rank, zeroed once at set-up).
+// A block's epoch is one more than the value it last wrote, so no host value
+// is baked into a captured CUDA graph.  Every wait is bounded (1 s of
+// %globaltimer): on expiry the kernel records an error code in `err` and the
+// block returns; the host reads the flag.  No TMA and no multicast is used:
+// peer memory is touched only with plain loads and stores.
+
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/library.h>
+
+#include <cstdint>
+
+namespace tgcm {
+namespace {
+
+constexpr int kArThreads = 512;
+constexpr int kArMaxRanks = 8;
+constexpr uint64_t kArWaitNs = 1000000000ull;
+constexpr int kErrArTimeout = 20;
+
+__device__ __forceinline__ uint64_t ar_now() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+struct ArArgs {
+  float* bufs[kArMaxRanks];        // peers' gradient buffers (index = rank)
+  uint32_t* pads[kArMaxRanks];     // peers' signal pads
+  long long n;                     // elements per buffer
+  int world, rank, blocks;
+  float scale;
+  int* err;
+};
+
+// Block-level barrier on `phase`: announce `epoch` to every peer, then wait
+// until every peer announced it to us.  Returns false on timeout.
+__device__ bool ar_barrier(const ArArgs& a, int phase, uint32_t epoch) {
+  __syncthreads();
+  if (threadIdx.x < a.world) {
+    const int p = threadIdx.x;
+    __threadfence_system();
+    st_release_sys(a.pads[p] + (phase * kArMaxRanks + a.rank) * a.blocks + blockIdx.x, epoch);
+  }
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = 1;
+  __syncthreads();
+  if (threadIdx.x < a.world) {
+    const uint32_t* slot = a.pads[a.rank] + (phase * kArMaxRanks + threadIdx.x) * a.blocks + blockIdx.x;
+    const uint64_t t0 = ar_now();
+    while (static_cast<int32_t>(ld_acquire_sys(slot) - epoch) < 0) {
+      if (ar_now() - t0 > kArWaitNs) {
+        if (a.err) atomicCAS(a.err, 0, kErrArTimeout);
+        ok = 0;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+__global__ void __launch_bounds__(kArThreads) fused_allreduce_kernel(ArArgs a) {
+  // epoch: one more than what this block last announced for phase 0 on its own pad
+  __shared__ uint32_t s_epoch;
+  if (threadIdx.x == 0)
+    s_epoch = *(volatile uint32_t*)(a.pads[a.rank] + (0 * kArMaxRanks + a.rank) * a.blocks + blockIdx.x) + 1u;
+  __syncthreads();
+  const uint32_t epoch = s_epoch;
+  if (!ar_barrier(a, 0, epoch)) return;
+
+  // this rank's chunk, split over the blocks in 16-byte vectors
+  const long long chunk = (a.n + a.world - 1) / a.world;
+  const long long c0 = static_cast<long long>(a.rank) * chunk;
+  long long c1 = c0 + chunk;
+  if (c1 > a.n) c1 = a.n;
+  const long long per = ((c1 - c0 + a.blocks - 1) / a.blocks + 3) / 4 * 4;
+  const long long b0 = c0 + per * blockIdx.x;
+  long long b1 = b0 + per;
+  if (b1 > c1) b1 = c1;
+  if (b0 < b1) {
+    const bool vec = (b0 % 4 == 0);
+    const long long nv = vec ? (b1 - b0) / 4 : 0;
+    for (long long i = threadIdx.x; i < nv; i += blockDim.x) {
+      const long long e = b0 + 4 * i;
+      float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int p = 0; p < a.world; ++p) {
+        const float4 v = __ldcv(reinterpret_cast<const float4*>(a.bufs[p] + e));
+        s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+      }
+      s.x *= a.scale; s.y *= a.scale; s.z *= a.scale; s.w *= a.scale;
+      for (int p = 0; p < a.world; ++p) *reinterpret_cast<float4*>(a.bufs[p] + e) = s;
+    }
+    for (long long e = b0 + 4 * nv + threadIdx.x; e < b1; e += blockDim.x) {
+      float s = 0.f;
+      for (int p = 0; p < a.world; ++p) s += __ldcv(a.bufs[p] + e);
+      s *= a.scale;
+      for (int p = 0; p < a.world; ++p) a.bufs[p][e] = s;
+    }
+  }
+  ar_barrier(a, 1, epoch);
+}
+
+}  // namespace
+
+// buf: this rank's symmetric fp32 buffer; buf_ptrs / pad_ptrs: int64 (world)
+// host tensors of the peers' buffer and signal-pad addresses.
+void fused_allreduce_mean(at::Tensor& buf, const at::Tensor& buf_ptrs, const at::Tensor& pad_ptrs, int64_t rank,
+                          int64_t blocks, const c10::optional<at::Tensor>& err) {
+  TORCH_CHECK(buf.is_cuda() && buf.scalar_type() == at::kFloat && buf.is_contiguous(), "fp32 CUDA buffer expected");
+  TORCH_CHECK(buf_ptrs.scalar_type() == at::kLong && pad_ptrs.scalar_type() == at::kLong && !buf_ptrs.is_cuda() &&
+                  !pad_ptrs.is_cuda(),
+              "pointer tables must be int64 CPU tensors");
+  const int64_t world = buf_ptrs.numel();
+  TORCH_CHECK(world >= 1 && world <= kArMaxRanks && pad_ptrs.numel() == world, "1..8 ranks supported");
+  TORCH_CHECK(blocks >= 1 && blocks <= 1024, "blocks out of range");
+  c10::cuda::CUDAGuard guard(buf.device());
+  ArArgs a;
+  memset(&a, 0, sizeof(a));
+  for (int64_t p = 0; p < world; ++p) {
+    a.bufs[p] = reinterpret_cast<float*>(buf_ptrs.data_ptr<int64_t>()[p]);
+    a.pads[p] = reinterpret_cast<uint32_t*>(pad_ptrs.data_ptr<int64_t>()[p]);
+  }
+  TORCH_CHECK(a.bufs[rank] == buf.data_ptr<float>(), "buffer is not this rank's symmetric allocation");
+  a.n = buf.numel();
+  a.world = static_cast<int>(world);
+  a.rank = static_cast<int>(rank);
+  a.blocks = static_cast<int>(blocks);
+  a.scale = 1.f / static_cast<float>(world);
+  a.err = (err.has_value() && err->defined()) ? err->data_ptr<int>() : nullptr;
+  fused_allreduce_kernel<<<static_cast<unsigned>(blocks), kArThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace tgcm
+
+TORCH_LIBRARY_FRAGMENT(tgcm, m) {
+  m.def("fused_allreduce_mean(Tensor(a!) buf, Tensor buf_ptrs, Tensor pad_ptrs, int rank, int blocks, Tensor? err) -> ()");
+}
+
+TORCH_LIBRARY_IMPL(tgcm, CUDA, m) { m.impl("fused_allreduce_mean", &tgcm::fused_allreduce_mean); }

@@ -90,12 +90,14 @@ static CUtensorMap make_tmap(const void* ptr, int dtype, uint64_t d0, uint64_t d
 
 template <int BN>
 struct StagesFor {
-  static constexpr int value = BN <= 80 ? 4 : BN <= 144 ? 3 : 2;
+  static constexpr int value = BN <= 80 ? 4 : 3;
 };
 
 // Optional per-CTA cycle-counter buffer (diagnostics; see GemmParams::prof).
 static unsigned long long* g_prof_buf = nullptr;
 static int64_t g_prof_ctas = 0;
+static int64_t g_prof_target = -1;  // record only this launch index (-1: every launch)
+static int64_t g_prof_count = 0;
 
 template <int FMT, int BN, bool A_MN, bool B_MN>
 static void launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream) {
@@ -119,7 +121,11 @@ static void launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmP
   if (tiles == 0) return;
   dim3 grid(tiles < n_sm ? tiles : n_sm);
   GemmParams q = p;
-  q.prof = (g_prof_buf != nullptr && grid.x <= g_prof_ctas) ? g_prof_buf : nullptr;
+  q.prof = nullptr;
+  if (g_prof_buf != nullptr && grid.x <= g_prof_ctas) {
+    if (g_prof_target < 0 || g_prof_count == g_prof_target) q.prof = g_prof_buf;
+    ++g_prof_count;
+  }
   kern<<<grid, kGemmThreads, S::kTotal, stream>>>(ta, tb, q);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("tgcm gemm launch: ") + cudaGetErrorString(e));
@@ -201,7 +207,19 @@ at::Tensor sht_synth(const at::Tensor& x, int64_t L, const at::Tensor& P, const 
     p.err = err_ptr(err);
     gemm_dispatch(2, bnj, false, false, ta, tb, p, st);
   }
-  {
+  const bool one_gemm = lat_major && !(col_scale.has_value() && col_scale->defined());
+  if (one_gemm) {
+    // lat-major output: out[s, j, i] = Σ_k F[i, k] W[(s, j), k] is ONE GEMM with
+    // N = S·J (the (s, j) rows of W are contiguous) and a linear output map n·I + i.
+    CUtensorMap ta = make_tmap(F.data_ptr(), 2, M2, I, 1, M2p * 4, I * M2p * 4, 32, 128, 1);
+    CUtensorMap tb = make_tmap(ws.data_ptr(), 2, M2, S * J, 1, M2p * 4, S * J * M2p * 4, 32, 256, 1);
+    GemmParams p = default_params();
+    p.M = I; p.N = S * J; p.K = M2; p.groups = 1;
+    p.tiles_m = cdiv(I, 128); p.tiles_n = cdiv(S * J, 256);
+    p.C = out.data_ptr(); p.c_sg = 0; p.c_sr = 1; p.c_sc = I;
+    p.err = err_ptr(err);
+    gemm_dispatch(2, 256, false, false, ta, tb, p, st);
+  } else {
     CUtensorMap ta = make_tmap(F.data_ptr(), 2, M2, I, 1, M2p * 4, I * M2p * 4, 32, 128, 1);
     CUtensorMap tb = make_tmap(ws.data_ptr(), 2, M2, J, S, M2p * 4, J * M2p * 4, 32, bnj, 1);
     GemmParams p = default_params();
@@ -233,8 +251,20 @@ at::Tensor sht_anal(const at::Tensor& N_in, const at::Tensor& Ft, const at::Tens
   auto out = Lo > L ? at::zeros({S, M2, Lo}, N.options()) : at::empty({S, M2, Lo}, N.options());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const int bnj = pick_bn_j(J);
-  // 1) real DFT analysis: Z[s] (M2 x J) = Ft (M2 x I) . N[s]^T, both K-major (K = I), times w_j
-  {
+  // 1) real DFT analysis.  Without a column scale it is ONE GEMM over all (s, j):
+  //    Z (M2 x S·J) = Ft (M2 x I) . N^T, stored m-major (M2, S, J); with a column
+  //    scale (w_j) it is S grouped GEMMs storing (S, M2, J).
+  const bool one_gemm = !(col_scale.has_value() && col_scale->defined());
+  if (one_gemm) {
+    CUtensorMap ta = make_tmap(Ft.data_ptr(), 2, I, M2, 1, I * 4, M2 * I * 4, 32, 128, 1);
+    CUtensorMap tb = make_tmap(N.data_ptr(), 2, I, S * J, 1, I * 4, S * J * I * 4, 32, 256, 1);
+    GemmParams p = default_params();
+    p.M = M2; p.N = S * J; p.K = I; p.groups = 1;
+    p.tiles_m = cdiv(M2, 128); p.tiles_n = cdiv(S * J, 256);
+    p.C = ws.data_ptr(); p.c_sg = 0; p.c_sr = S * J; p.c_sc = 1;
+    p.err = err_ptr(err);
+    gemm_dispatch(2, 256, false, false, ta, tb, p, st);
+  } else {
     CUtensorMap ta = make_tmap(Ft.data_ptr(), 2, I, M2, 1, I * 4, M2 * I * 4, 32, 128, 1);
     CUtensorMap tb = make_tmap(N.data_ptr(), 2, I, J, S, I * 4, J * I * 4, 32, bnj, 1);
     GemmParams p = default_params();
@@ -249,7 +279,9 @@ at::Tensor sht_anal(const at::Tensor& N_in, const at::Tensor& Ft, const at::Tens
   // 2) Legendre analysis per zonal wavenumber: out rows (slice, cos/sin), cols l
   {
     const int bnl = pick_bn_l(L);
-    CUtensorMap ta = make_tmap(ws.data_ptr(), 2, J, M2, S, J * 4, M2 * J * 4, 32, 2, 64);
+    // A rows (m-row, slice): ws is (M2, S, J) after the one-GEMM DFT, else (S, M2, J)
+    CUtensorMap ta = one_gemm ? make_tmap(ws.data_ptr(), 2, J, M2, S, S * J * 4, J * 4, 32, 2, 64)
+                              : make_tmap(ws.data_ptr(), 2, J, M2, S, J * 4, M2 * J * 4, 32, 2, 64);
     CUtensorMap tb = make_tmap(Pt.data_ptr(), 2, J, L, Mw, J * 4, L * J * 4, 32, bnl, 1);
     GemmParams p = default_params();
     p.M = 2 * S; p.N = L; p.K = J; p.groups = Mw;
@@ -362,7 +394,9 @@ void bgemm_tf32(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, double 
 
 // Route the GEMM kernels' per-CTA cycle counters into `buf` ((ctas, 8) int64 on
 // the device), or stop recording when `buf` is absent.
-void gemm_profile_buffer(const c10::optional<at::Tensor>& buf) {
+void gemm_profile_buffer(const c10::optional<at::Tensor>& buf, int64_t launch_index) {
+  g_prof_target = launch_index;
+  g_prof_count = 0;
   if (buf.has_value() && buf->defined()) {
     TORCH_CHECK(buf->is_cuda() && buf->scalar_type() == at::kLong && buf->dim() == 2 && buf->size(1) == 8 &&
                     buf->is_contiguous(),
@@ -378,7 +412,7 @@ void gemm_profile_buffer(const c10::optional<at::Tensor>& buf) {
 }  // namespace tgcm
 
 TORCH_LIBRARY_FRAGMENT(tgcm, m) {
-  m.def("gemm_profile_buffer(Tensor? buf) -> ()");
+  m.def("gemm_profile_buffer(Tensor? buf, int launch_index=-1) -> ()");
   m.def("bgemm_tf32(Tensor A, Tensor B, Tensor(a!) C, float alpha, Tensor? err) -> ()");
   m.def("sht_synth(Tensor x, int L, Tensor P, Tensor F, Tensor ws, Tensor? col_scale, Tensor? err, bool lat_major) -> Tensor");
   m.def("sht_anal(Tensor N, Tensor Ft, Tensor Pt, int Lo, Tensor ws, Tensor? col_scale, Tensor? err, bool lat_major) -> Tensor");

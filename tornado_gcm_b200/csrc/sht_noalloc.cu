@@ -41,8 +41,8 @@ float* g_scratch_addr[kMaxDevices] = {};
 int g_num_sms[kMaxDevices] = {};
 
 template <int BN>
-struct Stages {
-  static constexpr int value = BN == 128 ? 2 : 3;
+struct Stages {  // pipeline depths chosen to differ from the regular op's instantiations
+  static constexpr int value = BN == 64 ? 3 : 2;
 };
 
 template <int BN>

@@ -46,6 +46,11 @@ class _Bases:
         t = lambda a: torch.as_tensor(np.ascontiguousarray(a), dtype=torch.float32, device=dev)
         self.P = t(pp)
         self.Pt = t(np.transpose(p, (0, 2, 1)))
+        # quadrature weights folded into the Legendre bases: the weighted
+        # analysis and its adjoint then run the one-GEMM Fourier steps
+        wj = np.asarray(sh.basis.w, dtype=np.float64)
+        self.Pw = t(pp * wj[None, :, None])
+        self.Ptw = t(np.transpose(p, (0, 2, 1)) * wj[None, None, :])
         self.F = t(fp)
         self.Ft = t(f.T)
         self.w = t(sh.basis.w)
@@ -65,7 +70,8 @@ def bases(sh, device) -> _Bases:
     return entry[0]
 
 
-def _synth(x3: torch.Tensor, b: _Bases, col_scale=None, lat_major: bool = False) -> torch.Tensor:
+def _synth(x3: torch.Tensor, b: _Bases, col_scale=None, lat_major: bool = False,
+           weighted: bool = False) -> torch.Tensor:
     """Modal (S, M2, L) → nodal; x3 may be a strided view of a row-padded buffer."""
     ops = _ext.require("spherical-harmonic synthesis")
     S = x3.shape[0]
@@ -77,15 +83,18 @@ def _synth(x3: torch.Tensor, b: _Bases, col_scale=None, lat_major: bool = False)
         if b.Lp != b.L:
             x3 = x3[..., : b.L]
     ws = torch.empty(S * b.J * b.M2p, dtype=torch.float32, device=x3.device)
-    return ops.sht_synth(x3, b.L, b.P, b.F, ws, col_scale, _ext.error_flag(x3.device), lat_major)
+    return ops.sht_synth(x3, b.L, b.Pw if weighted else b.P, b.F, ws, col_scale, _ext.error_flag(x3.device),
+                         lat_major)
 
 
-def _anal(n3: torch.Tensor, b: _Bases, col_scale=None, lat_major: bool = False) -> torch.Tensor:
+def _anal(n3: torch.Tensor, b: _Bases, col_scale=None, lat_major: bool = False,
+          weighted: bool = False) -> torch.Tensor:
     """Nodal (S, I, J) (or (S, J, I) when lat_major) → modal (S, M2, L)."""
     ops = _ext.require("spherical-harmonic analysis")
     S = n3.shape[0]
     ws = torch.empty(S * b.M2 * b.J, dtype=torch.float32, device=n3.device)
-    return ops.sht_anal(n3.float(), b.Ft, b.Pt, b.L, ws, col_scale, _ext.error_flag(n3.device), lat_major)
+    return ops.sht_anal(n3.float(), b.Ft, b.Ptw if weighted else b.Pt, b.L, ws, col_scale,
+                        _ext.error_flag(n3.device), lat_major)
 
 
 class ToNodalFn(torch.autograd.Function):
@@ -107,11 +116,11 @@ class ToModalFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, n3, b, lat_major=False):
         ctx.b, ctx.lat_major = b, lat_major
-        return _anal(n3, b, b.w, lat_major)
+        return _anal(n3, b, None, lat_major, weighted=True)
 
     @staticmethod
     def backward(ctx, g):
-        return _synth(g, ctx.b, ctx.b.w, ctx.lat_major), None, None
+        return _synth(g, ctx.b, None, ctx.lat_major, weighted=True), None, None
 
 
 def to_nodal(x: torch.Tensor, sh) -> torch.Tensor:

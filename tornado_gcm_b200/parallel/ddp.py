@@ -189,23 +189,25 @@ class GradientAllReducer:
         dev = self.params[0].device
         sizes = [p.numel() for p in self.params]
         self.numel = sum(sizes)
-        self.flat = torch.zeros(self.numel, dtype=torch.float32, device=dev)
+        self.world = get_world_size()
+        self.bucket_elems = int(bucket_mb * 1e6 / 4) if bucket_mb > 0 else self.numel
+        self.fused = None
+        if use_fused and self.world > 1 and dev.type == "cuda" and os.environ.get("TGCM_FUSED_ALLREDUCE", "1") != "0":
+            try:
+                from tornado_gcm_b200.parallel import fused_allreduce
+
+                self.fused = fused_allreduce.make_reducer(self.numel, dev)
+            except Exception as exc:  # pragma: no cover - depends on platform
+                logger.warning("fused all-reduce unavailable (%s); using NCCL", exc)
+                self.fused = None
+        # the flat buffer is the reducer's symmetric allocation when fused
+        self.flat = self.fused.flat if self.fused is not None else torch.zeros(self.numel, dtype=torch.float32,
+                                                                               device=dev)
         self.views = []
         off = 0
         for p, n in zip(self.params, sizes):
             self.views.append(self.flat[off:off + n].view_as(p))
             off += n
-        self.world = get_world_size()
-        self.bucket_elems = int(bucket_mb * 1e6 / 4) if bucket_mb > 0 else self.numel
-        self.fused = None
-        if use_fused and self.world > 1 and dev.type == "cuda":
-            try:
-                from tornado_gcm_b200.parallel import fused_allreduce
-
-                self.fused = fused_allreduce.make_reducer(self.flat)
-            except Exception as exc:  # pragma: no cover - depends on platform
-                logger.warning("fused all-reduce unavailable (%s); using NCCL", exc)
-                self.fused = None
 
     def attach(self) -> None:
         """Point each parameter's .grad at its view of the flat buffer."""

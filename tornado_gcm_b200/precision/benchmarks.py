@@ -235,9 +235,13 @@ def _sht_case(args):
     x = torch.randn(args.slices, *g.modal_shape, device="cuda")
     b = sht_ops.bases(g.spherical_harmonics, x.device)
 
+    nod = sht_ops.to_nodal_lat_major(x, g.spherical_harmonics)
+
     def step():
-        n = sht_ops.to_nodal_lat_major(x, g.spherical_harmonics)
-        sht_ops.to_modal_lat_major(n, g.spherical_harmonics)
+        if args.mode in ("fwd", "both"):
+            n = sht_ops.to_nodal_lat_major(x, g.spherical_harmonics)
+        if args.mode in ("dgrad", "both", "wgrad"):
+            sht_ops.to_modal_lat_major(nod, g.spherical_harmonics)
 
     M2, L = g.modal_shape
     I, J = g.nodal_shape
@@ -332,7 +336,7 @@ def _bgemm_case(args):
     return (lambda: ops.bgemm_tf32(A, B, C, 1.0, err)), 2.0 * args.groups * args.m * args.n * args.k
 
 
-def gemm_cycle_breakdown(fn) -> list:
+def gemm_cycle_breakdown(fn, launch_index: int = -1) -> list:
     """Run ``fn`` once per GEMM launch recorded and return per-CTA-averaged cycle counters.
 
     Counters (cycles, averaged over the CTAs of the last GEMM launch in ``fn``):
@@ -343,7 +347,7 @@ def gemm_cycle_breakdown(fn) -> list:
 
     ops = _ext.require("GEMM profile")
     buf = torch.zeros(1024, 8, dtype=torch.int64, device="cuda")
-    ops.gemm_profile_buffer(buf)
+    ops.gemm_profile_buffer(buf, launch_index)
     try:
         fn()
         torch.cuda.synchronize()
@@ -362,7 +366,8 @@ def main(argv=None) -> None:
     ap.add_argument("case", choices=["mlp", "sht", "stage", "linear", "bgemm", "recipe"])
     ap.add_argument("--recipe", default="pre", choices=["pre", "post"])
     ap.add_argument("--transpose", action="store_true")
-    ap.add_argument("--mode", default="fwd", choices=["fwd", "dgrad", "wgrad"])
+    ap.add_argument("--mode", default="fwd", choices=["fwd", "dgrad", "wgrad", "both"],
+                    help="linear: which GEMM; sht: fwd = synthesis, dgrad = analysis, both")
     ap.add_argument("--groups", type=int, default=1292)
     ap.add_argument("--m", type=int, default=128)
     ap.add_argument("--n", type=int, default=64)
@@ -378,6 +383,7 @@ def main(argv=None) -> None:
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--cycles", action="store_true", help="print the GEMM cycle breakdown of one call")
+    ap.add_argument("--launch", type=int, default=-1, help="which GEMM launch of the call to break down (-1: last)")
     args = ap.parse_args(argv)
     fn, flops = {"mlp": _mlp_case, "sht": _sht_case, "stage": _stage_case, "linear": _linear_case,
                  "bgemm": _bgemm_case, "recipe": _recipe_case}[args.case](args)
@@ -387,7 +393,7 @@ def main(argv=None) -> None:
     if flops:
         out["tflops"] = round(flops / (r.min_ms * 1e-3) / 1e12, 2)
     if args.cycles:
-        out["gemm_cycles_last_launch"] = gemm_cycle_breakdown(fn)
+        out["gemm_cycles"] = gemm_cycle_breakdown(fn, args.launch)
     print(json.dumps(out))
 
 
