@@ -1,0 +1,191 @@
+"""Model facade, JAX checkpoint mapping, dynamic forcing, inference engines and
+the CLI on the CPU (T21-sized cases where a model is stepped)."""
+
+import pickle
+
+import numpy as np
+import pytest
+import torch
+
+from tornado_gcm_b200.model import jax_checkpoint_loader as jl
+
+
+def _haiku_dict(comps: jl.JaxNeuralComponents, rng) -> dict:
+    """Nested Haiku-style params for every tower of the components (test fixture)."""
+    root = {}
+
+    def put(path, arr):
+        d = root
+        parts = path.split("/")
+        for p in parts[:-1]:
+            d = d.setdefault(p, {})
+        d[parts[-1]] = arr
+
+    def epd(prefix, epd_mod, surface=False):
+        s = "surface_model_" if surface else ""
+        for part in ("encode", "decode"):
+            for i, lin in enumerate(getattr(epd_mod, part).layers):
+                put(f"{prefix}/{s}{part}_tower/~/mlp_uniform/~/linear_{i}/w",
+                    rng.standard_normal(tuple(lin.weight.shape[::-1])).astype(np.float32))
+                if lin.bias is not None:
+                    put(f"{prefix}/{s}{part}_tower/~/mlp_uniform/~/linear_{i}/b",
+                        rng.standard_normal(lin.bias.shape).astype(np.float32))
+        for bidx, blk in enumerate(epd_mod.process_blocks):
+            suffix = "" if bidx == 0 else f"_{bidx}"
+            for i, lin in enumerate(blk.layers):
+                put(f"{prefix}/{s}process_tower{suffix}/~/mlp_uniform/~/linear_{i}/w",
+                    rng.standard_normal(tuple(lin.weight.shape[::-1])).astype(np.float32))
+                put(f"{prefix}/{s}process_tower{suffix}/~/mlp_uniform/~/linear_{i}/b",
+                    rng.standard_normal(lin.bias.shape).astype(np.float32))
+
+    r = "params/stochastic_modular_step_model/~/"
+    epd(r + "dimensional_learned_weatherbench_to_primitive_with_memory_encoder/~/a_nodal_mapping/~/epd_tower",
+        comps.encoder_epd[0])
+    epd(r + "dimensional_learned_weatherbench_to_primitive_with_memory_encoder/~/b_nodal_mapping/~/epd_tower",
+        comps.encoder_epd[1])
+    epd(r + "dimensional_learned_primitive_to_weatherbench_decoder/nodal_mapping/~/epd_tower", comps.decoder_epd)
+    epd(r + "stochastic_physics_parameterization_step/~/physics/~/epd_tower", comps.physics_epd)
+    for k, name in enumerate(("land", "sea", "ice")):
+        epd(r + f"stochastic_physics_parameterization_step/~/{name}_surface", comps.surface_epd[k], surface=True)
+    for i, layer in enumerate(comps.volume_conv.layers):
+        suffix = "" if i == 0 else f"_{i}"
+        w = layer.conv.weight
+        put(r + f"stochastic_physics_parameterization_step/~/volume/~/conv_level{suffix}/w",
+            rng.standard_normal((w.shape[2], w.shape[1], w.shape[0])).astype(np.float32))
+        put(r + f"stochastic_physics_parameterization_step/~/volume/~/conv_level{suffix}/b",
+            rng.standard_normal((w.shape[0], 1)).astype(np.float32))
+    return root
+
+
+def test_jax_checkpoint_roundtrip(tmp_path):
+    comps = jl.JaxNeuralComponents()
+    rng = np.random.default_rng(0)
+    nested = _haiku_dict(comps, rng)
+    path = tmp_path / "ckpt.pkl"
+    with open(path, "wb") as fh:
+        pickle.dump(nested, fh)
+    flat = jl.load_jax_checkpoint(path)
+    target = jl.JaxNeuralComponents()
+    rep = jl.load_jax_weights(target, flat)
+    assert not rep["skipped"] and not rep["unmatched"]
+    mapping = jl.build_weight_mapping(flat)
+    sd = target.state_dict()
+    for p, (key, kind) in mapping.items():
+        ref = torch.as_tensor(flat[p])
+        if kind == "linear_w":
+            ref = ref.t()
+        elif kind == "conv_w":
+            ref = ref.permute(2, 1, 0)
+        torch.testing.assert_close(sd[key], ref.reshape(sd[key].shape))
+    loaded = set(rep["loaded"])
+    assert all(k in loaded for k in sd if "positional" not in k)
+
+
+def test_dynamic_forcing_nearest_row_and_nan():
+    from tornado_gcm_b200.model.dynamic_data_forcing import build_dynamic_data_forcing_torch
+
+    data = {"sim_time": np.array([0.0, 1.0, 2.0]), "sst": np.arange(3 * 4, dtype=np.float32).reshape(3, 2, 2)}
+    fn = build_dynamic_data_forcing_torch(data, dt_tolerance=0.25, device="cpu")
+    out = fn({}, 1.1)
+    torch.testing.assert_close(out["sst"], torch.tensor(data["sst"][1]))
+    assert torch.isnan(fn({}, 1.5)["sst"]).all()
+
+
+def _small():
+    from tornado_gcm_b200.models.builders import build_hybrid_gcm
+
+    gcm, data = build_hybrid_gcm("5.6deg", "cpu")
+    enc = gcm.encoder
+    norm = lambda d: {k: (v - getattr(enc, f"mean_{k}")) / getattr(enc, f"std_{k}") for k, v in d.items()}
+    return gcm, data, norm
+
+
+def test_mp_inference_rollout_and_streaming():
+    from tornado_gcm_b200.inference import InferenceConfig, InferenceRunner, MPInference, NumpyWriter
+
+    gcm, data, norm = _small()
+    eng = MPInference(gcm, use_graph=False)
+    x0 = norm(data.sample(1, 0))
+    forc = data.forcings(1)
+    out = eng.rollout(x0, steps=2, forcings=forc)
+    assert len(out) == 2 and set(out[0]) >= {"u", "t"}
+    assert all(torch.isfinite(v).all() for v in out[-1].values())
+    s0 = gcm.encoder(x0, gcm.normalize_forcings(forc))
+    final, saved = eng.run_streaming(s0, 3, inner_steps=1, forcings=forc, keep_steps={1, 3}, nan_guard=True,
+                                     checkpoint_interval=1)
+    assert [s for s, _ in saved] == [1, 3]
+    ref = eng.run(s0, 3, inner_steps=1, forcings=forc)
+    torch.testing.assert_close(saved[-1][1].vorticity, ref[-1].vorticity)
+    runner = InferenceRunner(eng, InferenceConfig(outer_steps=3, inner_steps=1, chunk_size=2))
+    w = NumpyWriter()
+    traj = runner.run(s0, writer=w)
+    assert len(traj) == 3 and w.finalize()["vorticity"].shape[0] == 3
+
+
+def test_inference_checkpoint_roundtrip(tmp_path):
+    from tornado_gcm_b200.inference import MPInference
+    from tornado_gcm_b200.training.checkpointing import export_inference_checkpoint
+
+    gcm, _, _ = _small()
+    path = tmp_path / "m.pt"
+    export_inference_checkpoint(gcm, path, meta={"resolution": "5.6deg"})
+    eng = MPInference.from_state_dict(torch.load(path, weights_only=True), device="cpu", use_graph=False)
+    a = dict(gcm.named_parameters())
+    for k, v in eng.hybrid.named_parameters():
+        torch.testing.assert_close(v, a[k].to(torch.bfloat16).float())
+    for k, v in eng.hybrid.named_buffers():
+        torch.testing.assert_close(v, dict(gcm.named_buffers())[k])
+
+
+def test_sda_inference_adaptive_and_sparse():
+    from tornado_gcm_b200.inference import SDAInference
+    from tornado_gcm_b200.precision.sda import SDAConfig
+
+    gcm, data, norm = _small()
+    cfg = SDAConfig()
+    cfg.profiler.spectral_audit = True
+    eng = SDAInference(gcm, cfg, use_graph=False)
+    s0 = gcm.encoder(norm(data.sample(1, 0)), gcm.normalize_forcings(data.forcings(1)))
+    f = data.forcings(1)
+    traj = eng.run_adaptive(s0, 2, inner_steps=1, quality_threshold=0.0, forcings=f)
+    assert eng.escalated and len(traj) == 2
+    traj, stats = eng.run_sparse(s0, 2, inner_steps=1, forcings=f)
+    assert 0.0 < stats["memory_savings"] < 1.0
+
+
+def test_sda_trainer_and_cli(tmp_path):
+    from click.testing import CliRunner
+
+    from tornado_gcm_b200.cli import main
+    from tornado_gcm_b200.precision.sda import SDAConfig
+    from tornado_gcm_b200.training.sda_trainer import SDATrainer
+
+    gcm, _, _ = _small()
+    cfg = SDAConfig()
+    cfg.training.rollout_steps = 1
+    cfg.training.batch_size = 1
+    tr = SDATrainer(gcm, cfg, total_steps=2)
+    hist = tr.fit(log_every=1)
+    assert len(hist) == 2 and np.isfinite(hist[-1]["loss"])
+    ck = tmp_path / "c.pt"
+    tr.save_checkpoint(ck)
+    tr.load_checkpoint(ck)
+    yaml_path = tmp_path / "cfg.yaml"
+    yaml_path.write_text("model:\n  resolution: '5.6deg'\ntraining:\n  total_steps: 1\n  batch_size: 1\n"
+                         "  rollout_steps: 1\n")
+    res = CliRunner().invoke(main, ["train", "-c", str(yaml_path), "-k", str(tmp_path / "k.pt"), "-d", "cpu"])
+    assert res.exit_code == 0, res.output
+    from tornado_gcm_b200.training.checkpointing import export_inference_checkpoint
+    from tornado_gcm_b200.training.synthetic import SyntheticReanalysis
+
+    export_inference_checkpoint(gcm, tmp_path / "inf.pt", meta={"resolution": "5.6deg"})
+    src = SyntheticReanalysis(gcm.model.config.coords.horizontal)
+    enc = gcm.encoder
+    ic = {k: (v - getattr(enc, f"mean_{k}")) / getattr(enc, f"std_{k}") for k, v in src.sample(1, 0).items()}
+    ic["forcings"] = src.forcings(1)
+    torch.save(ic, tmp_path / "ic.pt")
+    res = CliRunner().invoke(main, ["infer", "-c", str(yaml_path), "-k", str(tmp_path / "inf.pt"), "-i",
+                                    str(tmp_path / "ic.pt"), "-o", str(tmp_path / "fc.npz"), "-s", "2", "-d", "cpu",
+                                    "--no-sda"])
+    assert res.exit_code == 0, res.output
+    assert np.load(tmp_path / "fc.npz")["t"].shape[0] == 2

@@ -173,6 +173,27 @@ class NeuralGCMModel(nn.Module):
         self._cached_diagnostics.clear()
         return d
 
+    def set_transform_precision(self, precision: str) -> None:
+        """Switch the spherical-harmonic transforms of the step to ``precision``
+        ("tf32" kernels, "float32", or "highest" = FP64 torch contractions).
+
+        The dycore equation is rebuilt on the re-precisioned grid; the fused
+        packed path (TF32 kernels) is used only for "tf32".
+        """
+        cfg = self.config
+        grid = cfg.coords.horizontal.with_precision(precision)
+        cfg.coords = dataclasses.replace(cfg.coords, horizontal=grid)
+        if self._dycore is not None:
+            old = self._dycore
+            self._dycore = primitive_equations.PrimitiveEquationsSigma(
+                old.reference_temperature, old.orography, cfg.coords, cfg.physics_specs,
+                humidity_key=cfg.humidity_key, cloud_keys=cfg.cloud_keys)
+            self._dycore_equation = self._dycore
+        self._fused = None
+        self.use_fused_dycore = precision == "tf32"
+        if self.parameterization is not None and hasattr(self.parameterization, "grid"):
+            self.parameterization.grid = grid
+
     def set_inner_state_safeguard(self, enabled: bool, clamp_abs: float = 1.0e12) -> None:
         self._sanitize_inner_enabled = bool(enabled)
         self._sanitize_inner_clamp_abs = float(clamp_abs)

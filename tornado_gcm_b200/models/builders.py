@@ -60,6 +60,9 @@ RESOLUTIONS = {
     "2.8deg": ResolutionSpec("2.8deg", "TL63", 20.0, 384),
     "1.4deg": ResolutionSpec("1.4deg", "TL127", 10.0, 512),
     "0.7deg": ResolutionSpec("0.7deg", "TL255", 5.0, 768),
+    # small configuration for tests and CPU demonstrations: T21 (64 x 32 grid), 8 levels, dt 2 h
+    "5.6deg": ResolutionSpec("5.6deg", "T21", 120.0, 32, tower_hidden_layers=2, layers=8, encoder_width=32,
+                             encoder_hidden_layers=1),
 }
 
 
@@ -108,11 +111,20 @@ class HybridGCM(nn.Module):
         return self.rollout(data0, forcings, outer_steps)[1]
 
 
+def resolve_resolution(name) -> str:
+    """``2.8`` / ``"2.8"`` / ``"2.8deg"`` / ``"TL63"`` → the key of :data:`RESOLUTIONS`."""
+    s = str(name).strip().lower().replace("°", "").replace("degrees", "").replace("deg", "")
+    for key, spec in RESOLUTIONS.items():
+        if s == key.replace("deg", "") or s == spec.grid.lower():
+            return key
+    raise KeyError(f"unknown resolution {name!r}; known: {sorted(RESOLUTIONS)}")
+
+
 def build_hybrid_gcm(resolution: str = "2.8deg", device: str | torch.device = "cpu",
                      policy: Optional[PrecisionPolicy] = None, seed: int = 0,
                      sht_precision: Optional[str] = None) -> tuple[HybridGCM, SyntheticReanalysis]:
     """Random-init hybrid model of the given resolution plus its synthetic data source."""
-    spec = RESOLUTIONS[resolution]
+    spec = RESOLUTIONS[resolve_resolution(resolution)]
     policy = policy or PrecisionPolicy.pzha_b200()
     torch.manual_seed(seed)
     grid0 = getattr(spherical_harmonic.Grid, spec.grid)()

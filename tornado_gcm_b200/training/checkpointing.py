@@ -25,7 +25,7 @@ class TrainingState:
 
 def _atomic_save(obj, path: pathlib.Path) -> None:
     path.parent.mkdir(parents=True, exist_ok=True)
-    fd, tmp = tempfile.mkstemp(dir=str(path.parent), prefix=".tmp_ckpt_")
+    fd, tmp = tempfile.mkstemp(dir=str(path.parent), prefix="ckpt_tmp_", suffix=".pt")
     os.close(fd)
     try:
         torch.save(obj, tmp)
@@ -64,10 +64,19 @@ def load_ema(path) -> dict | None:
 
 
 def export_inference_checkpoint(model: nn.Module, path, ema_params: dict | None = None,
-                                nn_dtype: torch.dtype = torch.bfloat16) -> None:
-    sd = dict(ema_params) if ema_params is not None else _unwrap(model).state_dict()
-    conv = {k: (v.to(nn_dtype) if v.is_floating_point() else v).detach().cpu() for k, v in sd.items()}
-    _atomic_save({"model_state_dict": conv, "format": "inference"}, pathlib.Path(path))
+                                nn_dtype: torch.dtype = torch.bfloat16, meta: dict | None = None) -> None:
+    """Parameters (EMA copies when given) in ``nn_dtype``; buffers (normalisation
+    statistics, reference profiles, interpolation matrices) keep their dtype."""
+    raw = _unwrap(model)
+    sd = {k: v for k, v in raw.state_dict().items()}
+    params = dict(raw.named_parameters())
+    if ema_params is not None:
+        sd.update({k: v for k, v in ema_params.items() if k in sd})
+    conv = {}
+    for k, v in sd.items():
+        v = v.detach().cpu()
+        conv[k] = v.to(nn_dtype) if (k in params and v.is_floating_point()) else v
+    _atomic_save({"model_state_dict": conv, "format": "inference", "meta": dict(meta or {})}, pathlib.Path(path))
 
 
 def load_inference_checkpoint(path, model: nn.Module, strict: bool = False) -> None:
