@@ -133,9 +133,10 @@ __global__ void __launch_bounds__(kArThreads) fused_allreduce_kernel(ArArgs a) {
 }  // namespace
 
 // buf: this rank's symmetric fp32 buffer; buf_ptrs / pad_ptrs: int64 (world)
-// host tensors of the peers' buffer and signal-pad addresses.
+// host tensors of the peers' buffer and signal-pad addresses.  The sum is
+// multiplied by `scale`; 0 selects 1/world (the mean).
 void fused_allreduce_mean(at::Tensor& buf, const at::Tensor& buf_ptrs, const at::Tensor& pad_ptrs, int64_t rank,
-                          int64_t blocks, const c10::optional<at::Tensor>& err) {
+                          int64_t blocks, const c10::optional<at::Tensor>& err, double scale) {
   TORCH_CHECK(buf.is_cuda() && buf.scalar_type() == at::kFloat && buf.is_contiguous(), "fp32 CUDA buffer expected");
   TORCH_CHECK(buf_ptrs.scalar_type() == at::kLong && pad_ptrs.scalar_type() == at::kLong && !buf_ptrs.is_cuda() &&
                   !pad_ptrs.is_cuda(),
@@ -155,7 +156,7 @@ void fused_allreduce_mean(at::Tensor& buf, const at::Tensor& buf_ptrs, const at:
   a.world = static_cast<int>(world);
   a.rank = static_cast<int>(rank);
   a.blocks = static_cast<int>(blocks);
-  a.scale = 1.f / static_cast<float>(world);
+  a.scale = scale == 0.0 ? 1.f / static_cast<float>(world) : static_cast<float>(scale);
   a.err = (err.has_value() && err->defined()) ? err->data_ptr<int>() : nullptr;
   fused_allreduce_kernel<<<static_cast<unsigned>(blocks), kArThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -164,7 +165,7 @@ void fused_allreduce_mean(at::Tensor& buf, const at::Tensor& buf_ptrs, const at:
 }  // namespace tgcm
 
 TORCH_LIBRARY_FRAGMENT(tgcm, m) {
-  m.def("fused_allreduce_mean(Tensor(a!) buf, Tensor buf_ptrs, Tensor pad_ptrs, int rank, int blocks, Tensor? err) -> ()");
+  m.def("fused_allreduce_mean(Tensor(a!) buf, Tensor buf_ptrs, Tensor pad_ptrs, int rank, int blocks, Tensor? err, float scale=0.0) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(tgcm, CUDA, m) { m.impl("fused_allreduce_mean", &tgcm::fused_allreduce_mean); }

@@ -64,6 +64,14 @@ class FusedMeanAllReducer:
         ops.fused_allreduce_mean(self.flat, self.buf_ptrs, self.pad_ptrs, self.rank, self.blocks,
                                  _ext.error_flag(self.flat.device))
 
+    def all_reduce_sum(self, flat: torch.Tensor) -> None:
+        """Same kernel with the scale set to 1 (plain sum over ranks)."""
+        if flat.data_ptr() != self.flat.data_ptr():
+            raise ValueError("all_reduce_sum works on the reducer's own symmetric buffer")
+        ops = _ext.require("fused all-reduce")
+        ops.fused_allreduce_mean(self.flat, self.buf_ptrs, self.pad_ptrs, self.rank, self.blocks,
+                                 _ext.error_flag(self.flat.device), 1.0)
+
 
 def make_reducer(numel: int, device: torch.device, group=None) -> FusedMeanAllReducer:
     """Symmetric-memory reducer for a flat buffer of ``numel`` fp32 elements."""
