@@ -56,7 +56,9 @@ def _column_interp(target: torch.Tensor, source: torch.Tensor, values: torch.Ten
     idx = torch.searchsorted(source.contiguous(), target.contiguous()).clamp(1, n_src - 1)
     x0, x1 = source.gather(-1, idx - 1), source.gather(-1, idx)
     f0, f1 = values.gather(-1, idx - 1), values.gather(-1, idx)
-    out = f0 + (target - x0) / (x1 - x0 + 1e-30) * (f1 - f0)
+    den = x1 - x0
+    safe = torch.where(den == 0, torch.ones_like(den), den)
+    out = torch.where(den == 0, f0, f0 + (target - x0) / safe * (f1 - f0))
     if extrapolate == "constant":
         out = torch.where(target <= source[..., :1], values[..., :1].expand_as(out), out)
         out = torch.where(target >= source[..., -1:], values[..., -1:].expand_as(out), out)

@@ -272,3 +272,102 @@ class NodalColumnParameterization(nn.Module):
         if self.filter_fn is not None:
             out = out.tree_map(self.filter_fn)
         return out
+
+
+class JaxAlignedDivCurlParameterization(nn.Module):
+    """NeuralGCM's divergence/curl physics parameterization on the full feature set
+    — reference ``neural/parameterizations.py:240-504``.
+
+    ``feature_extractor`` (a :class:`~tornado_gcm_b200.neural.features.CombinedFeatures`
+    with memory features) → ``feature_transform`` (normalise / level-scale /
+    soft-clip) → features packed in sorted-key order → ``neural_net`` →
+    output split by ``output_keys``/``output_sizes`` → optional
+    ``tendency_transform`` → modal tendencies: nodal (u, v) become (ζ, δ)
+    tendencies through ``u·secφ``, ``v·secφ`` and the cos-lat curl /
+    divergence, everything in one batched analysis
+    (:class:`~tornado_gcm_b200.neural.transforms.ToModalWithDivCurl`).
+    Absent cloud tracers enter the features as zeros, so the packed width is
+    fixed by the checkpoint, and the memory features fall back to the current
+    state when no complete memory is supplied.
+    """
+
+    DEFAULT_OUTPUT_KEYS = ["specific_cloud_ice_water_content", "specific_cloud_liquid_water_content",
+                           "specific_humidity", "temperature_variation", "u", "v"]
+    _EPD_TRACER_KEYS = ("specific_humidity", "specific_cloud_liquid_water_content",
+                        "specific_cloud_ice_water_content")
+
+    def __init__(self, grid: Grid, neural_net: nn.Module, feature_extractor: nn.Module, feature_transform: nn.Module,
+                 tendency_transform: Optional[nn.Module] = None, n_levels: int = 32,
+                 filter_fn: Optional[Callable] = None, output_keys: Optional[list] = None,
+                 output_sizes: Optional[list] = None):
+        super().__init__()
+        from tornado_gcm_b200.neural.transforms import ToModalWithDivCurl
+
+        self.grid = grid
+        self.neural_net = neural_net
+        self.feature_extractor = feature_extractor
+        self.feature_transform = feature_transform
+        self.tendency_transform = tendency_transform
+        self.n_levels = n_levels
+        self.filter_fn = filter_fn
+        self.output_keys = list(output_keys or self.DEFAULT_OUTPUT_KEYS)
+        self.output_sizes = list(output_sizes or [n_levels] * len(self.output_keys))
+        self._to_modal = ToModalWithDivCurl(grid, "u", "v")
+
+    def _state_to_dict(self, state: State) -> dict:
+        tracers = dict(state.tracers or {})
+        for k in self._EPD_TRACER_KEYS:
+            tracers.setdefault(k, torch.zeros_like(state.temperature_variation))
+        d = {"vorticity": state.vorticity, "divergence": state.divergence,
+             "temperature_variation": state.temperature_variation,
+             "log_surface_pressure": state.log_surface_pressure, "tracers": tracers}
+        if state.sim_time is not None:
+            d["sim_time"] = torch.as_tensor(state.sim_time, dtype=torch.float32,
+                                            device=state.vorticity.device).reshape(1)
+        return d
+
+    def _memory_to_dict(self, memory) -> Optional[dict]:
+        if memory is None or isinstance(memory, dict):
+            return memory
+        if hasattr(memory, "vorticity") and hasattr(memory, "divergence"):
+            return self._state_to_dict(State(memory.vorticity, memory.divergence, memory.temperature_variation,
+                                             memory.log_surface_pressure, dict(getattr(memory, "tracers", {}) or {}),
+                                             getattr(memory, "sim_time", None)))
+        return None
+
+    @staticmethod
+    def _memory_dict_matches_inputs(mem: Optional[dict], ref: dict) -> bool:
+        if not mem or any(k not in mem for k in ("vorticity", "divergence", "temperature_variation",
+                                                  "log_surface_pressure")):
+            return False
+        rt, mt = ref.get("tracers"), mem.get("tracers")
+        return not rt or (isinstance(mt, dict) and set(rt) <= set(mt))
+
+    def _unpack_output(self, y: torch.Tensor) -> dict:
+        return dict(zip(self.output_keys, torch.split(y, self.output_sizes, dim=-3)))
+
+    def _nodal_tendencies_to_modal_state(self, tend: dict, state: State) -> State:
+        nodal = {k: v for k, v in tend.items() if k in ("u", "v", "temperature_variation") or k in state.tracers}
+        if ("u" in nodal) != ("v" in nodal):
+            nodal.pop("u", None), nodal.pop("v", None)
+        modal = self._to_modal(nodal)
+        if self.filter_fn is not None:
+            modal = {k: self.filter_fn(v) for k, v in modal.items()}
+        z = torch.zeros_like
+        return State(modal.get("vorticity", z(state.vorticity)), modal.get("divergence", z(state.divergence)),
+                     modal.get("temperature_variation", z(state.temperature_variation)),
+                     z(state.log_surface_pressure),
+                     {k: modal.get(k, z(v)) for k, v in state.tracers.items()}, state.sim_time)
+
+    def forward(self, state: State, forcings: Optional[dict] = None, memory=None) -> State:
+        from tornado_gcm_b200.neural.features import pack_features
+
+        inputs = self._state_to_dict(state)
+        mem = self._memory_to_dict(memory)
+        if not self._memory_dict_matches_inputs(mem, inputs):
+            mem = inputs
+        feats = self.feature_transform(self.feature_extractor(inputs, memory=mem, forcing=forcings))
+        tend = self._unpack_output(self.neural_net(pack_features(feats)))
+        if self.tendency_transform is not None:
+            tend = self.tendency_transform(tend)
+        return self._nodal_tendencies_to_modal_state(tend, state)

@@ -162,3 +162,40 @@ class Perturbation(nn.Module):
         fac = 1.0 + self.epsilon * noise
         f = lambda t: g.to_modal(g.to_nodal(t) * fac)
         return tendency.tree_map(f)
+
+
+class StochasticPhysicsParameterizationStep(nn.Module):
+    """Sub-stepped stochastic physics — reference ``neural/stochastic.py:314-391``.
+
+    Each of ``num_substeps``: tendency of ``physics_parameterization``,
+    perturbed by ``perturbation`` with the current random field, a
+    :class:`Corrector` Euler step, then the AR(1) random field advances.
+    """
+
+    def __init__(self, physics_parameterization: nn.Module, corrector: Corrector,
+                 random_field: Optional[GaussianRandomField] = None, perturbation: Optional[Perturbation] = None,
+                 num_substeps: int = 1):
+        super().__init__()
+        self.physics_param = physics_parameterization
+        self.corrector = corrector
+        self.random_field = random_field
+        self.perturbation = perturbation
+        self.num_substeps = int(num_substeps)
+
+    def forward(self, state: pe.State, forcing=None, randomness: Optional[RandomnessState] = None,
+                generator: Optional[torch.Generator] = None):
+        rand = randomness
+        for _ in range(self.num_substeps):
+            tend = self.physics_param(state)
+            if self.perturbation is not None and rand is not None:
+                tend = self.perturbation(tend, rand)
+            state = self.corrector(state, tend, forcing)
+            if self.random_field is not None and rand is not None:
+                rand = self.random_field.advance(rand, generator=generator)
+        return state, rand
+
+    def initialize_randomness(self, device=torch.device("cpu"), dtype: torch.dtype = torch.float32,
+                              generator: Optional[torch.Generator] = None) -> Optional[RandomnessState]:
+        if self.random_field is None:
+            return None
+        return self.random_field.unconditional_sample(device=device, dtype=dtype, generator=generator)

@@ -102,9 +102,12 @@ class NondimensionalizeTransform(nn.Module):
 class ToModalWithDivCurl(nn.Module):
     """Nodal ``(u, v, …)`` → modal ``(divergence, vorticity, …)``.
 
-    ``u·sec²φ`` and ``v·sec²φ`` are transformed (in the same batched call as
+    ``u·secφ`` and ``v·secφ`` are transformed (in the same batched call as
     every other field) and turned into δ, ζ with the cos-lat divergence and
-    curl operators.
+    curl operators, the inverse of
+    :func:`~tornado_gcm_b200.core.spherical_harmonic.vor_div_to_uv_nodal`.
+    (The reference scales by ``sec²φ`` here, ``neural/transforms.py:180-185``,
+    which does not invert its own ``u, v`` construction.)
     """
 
     def __init__(self, grid, u_key: str = "u_component_of_wind", v_key: str = "v_component_of_wind"):
@@ -121,8 +124,8 @@ class ToModalWithDivCurl(nn.Module):
                  if isinstance(t, torch.Tensor) and tuple(t.shape[-2:]) == tuple(self.grid.nodal_shape)}
         other = {k: t for k, t in rest.items() if k not in nodal}
         if u is not None and v is not None:
-            sec2 = torch.as_tensor(self.grid.sec2_lat, dtype=u.dtype, device=u.device)
-            nodal["__u"], nodal["__v"] = u * sec2, v * sec2
+            sec = torch.as_tensor(1.0 / self.grid.cos_lat, dtype=u.dtype, device=u.device)
+            nodal["__u"], nodal["__v"] = u * sec, v * sec
         modal = batched_to_modal(self.grid, nodal)
         if u is not None and v is not None:
             um, vm = modal.pop("__u"), modal.pop("__v")
