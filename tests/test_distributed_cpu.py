@@ -108,3 +108,54 @@ def test_peer_failure_surfaces_as_error_not_hang():
             p.kill()
     assert res[1].startswith("raised:")
     assert res[0].startswith("error:")
+
+
+def _worker_elastic(rank, world, port, ckpt_dir, q):
+    try:
+        import torch.distributed as dist
+
+        from tornado_gcm_b200.parallel.elastic import maybe_inject_fault, run_with_recovery
+
+        def train(hb, r, w, attempt):
+            path = os.path.join(ckpt_dir, "state.pt")
+            start, acc = 0, torch.zeros(1)
+            if os.path.exists(path):
+                ck = torch.load(path)
+                start, acc = ck["step"] + 1, ck["acc"]
+            for step in range(start, 6):
+                if attempt == 0:
+                    maybe_inject_fault(rank, step, "2:3:exit")   # original rank 2 dies before step 3
+                hb.beat(step)
+                hb.check(step)                                   # host-side detection before the collective
+                t = torch.ones(1)
+                dist.all_reduce(t)
+                acc = acc + t
+                if r == 0:
+                    torch.save({"step": step, "acc": acc}, path + ".tmp")
+                    os.replace(path + ".tmp", path)
+                dist.barrier()
+            return float(acc)
+
+        out = run_with_recovery(train, rank, world, "127.0.0.1", port, heartbeat_timeout_s=3.0)
+        q.put((rank, out))
+    except Exception:  # pragma: no cover
+        q.put((rank, traceback.format_exc()))
+
+
+def test_rank_failure_detected_and_survivors_resume(tmp_path):
+    world = 3
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_elastic, args=(r, world, port, str(tmp_path), q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=180) for _ in range(world - 1)]
+    for p in procs:
+        p.join(timeout=60)
+    assert procs[2].exitcode == 17
+    for rank, out in res:
+        assert isinstance(out, dict), out
+        assert out["attempts"] == 2 and out["world"] == 2
+        # steps 0-2 summed over 3 ranks, steps 3-5 over the 2 survivors
+        assert out["result"] == 3 * 3 + 3 * 2

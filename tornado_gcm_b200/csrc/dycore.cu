@@ -8,6 +8,7 @@
 //    the implicit solve (I − ηG)⁻¹ by block elimination with a cached
 //    per-l Schur-complement inverse — plus their transposes (adjoints).
 //    One thread per (sample, m, l) column; matrices staged in shared memory.
+#include "alloc.h"
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -116,7 +117,7 @@ at::Tensor column_fwd(const at::Tensor& nin, const at::Tensor& sec2, const at::T
   SliceIndex ix = make_slice_index(c);
   const int64_t I = lat_major ? nin.size(2) : nin.size(1), J = lat_major ? nin.size(1) : nin.size(2);
   TORCH_CHECK(nin.size(0) == batch * ix.n_in, "nin slice count mismatch: expected ", batch * ix.n_in);
-  auto out = at::empty({batch * ix.n_out, nin.size(1), nin.size(2)}, nin.options());
+  auto out = out_empty({batch * ix.n_out, nin.size(1), nin.size(2)}, nin.options());
   auto s2 = sec2.to(nin.device(), at::kFloat).contiguous();
   auto co = cor.to(nin.device(), at::kFloat).contiguous();
   if (nin.is_cuda()) {
@@ -164,7 +165,7 @@ at::Tensor column_vjp_op(const at::Tensor& nin, const at::Tensor& gout, const at
   SliceIndex ix = make_slice_index(c);
   const int64_t I = lat_major ? nin.size(2) : nin.size(1), J = lat_major ? nin.size(1) : nin.size(2);
   TORCH_CHECK(gout.size(0) == batch * ix.n_out, "gout slice count mismatch");
-  auto gin = at::empty_like(nin);
+  auto gin = out_empty_like(nin);
   auto s2 = sec2.to(nin.device(), at::kFloat).contiguous();
   auto co = cor.to(nin.device(), at::kFloat).contiguous();
   if (nin.is_cuda()) {
@@ -356,9 +357,9 @@ std::vector<at::Tensor> implicit_apply(const at::Tensor& d, const at::Tensor& t,
     TORCH_CHECK(x->stride(3) == 1 && x->stride(2) == x->size(3), "(m, l) planes must be contiguous");
   const int64_t B = d.size(0), n = d.size(1), M2 = d.size(2), L = d.size(3);
   TORCH_CHECK(n <= kMaxLevels, "too many levels");
-  auto od = at::empty({B, n, M2, L}, d.options());
-  auto ot = at::empty({B, n, M2, L}, d.options());
-  auto opp = at::empty({B, 1, M2, L}, d.options());
+  auto od = out_empty({B, n, M2, L}, d.options());
+  auto ot = out_empty({B, n, M2, L}, d.options());
+  auto opp = out_empty({B, 1, M2, L}, d.options());
   auto dev = d.device();
   auto Gc = G.to(dev, at::kFloat).contiguous(), Hc = H.to(dev, at::kFloat).contiguous();
   auto lc = lam.to(dev, at::kFloat).contiguous(), trc = tref.to(dev, at::kFloat).contiguous();

@@ -17,6 +17,7 @@
 // reduced in a fixed order inside every consumer block, so results are
 // deterministic (no atomics).
 
+#include "alloc.h"
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -238,9 +239,9 @@ std::vector<at::Tensor> packed_fix(const at::Tensor& y, const at::Tensor& yb, in
                                    bool fix_energy) {
   c10::OptionalDeviceGuard guard(y.device());
   FixArgs a = make_args(y, yb, n, fix_mass, fix_energy);
-  auto part = at::empty({a.B, kFixBlocks, 2}, y.options().dtype(at::kDouble));
+  auto part = out_empty({a.B, kFixBlocks, 2}, y.options().dtype(at::kDouble));
   partial_sums(a, part, y);
-  auto out = at::empty_like(y);
+  auto out = out_empty_like(y);
   a.out = out.data_ptr<float>();
   if (y.is_cuda()) {
     fix_apply_kernel<<<dim3(apply_blocks(a), a.B), kFixThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
@@ -266,8 +267,8 @@ std::vector<at::Tensor> packed_fix_adjoint(const at::Tensor& gout, const at::Ten
               "partial sums shape");
   a.part = part.data_ptr<double>();
   a.gout = gout.data_ptr<float>();
-  auto g_y = at::empty_like(y);
-  at::Tensor g_yb = need_before ? at::empty_like(y) : at::Tensor();
+  auto g_y = out_empty_like(y);
+  at::Tensor g_yb = need_before ? out_empty_like(y) : at::Tensor();
   a.g_y = g_y.data_ptr<float>();
   a.g_yb = need_before ? g_yb.data_ptr<float>() : nullptr;
   if (y.is_cuda()) {
@@ -318,7 +319,7 @@ at::Tensor row_reduce(const at::Tensor& x2, const c10::optional<at::Tensor>& w, 
   TORCH_CHECK(x2.dim() == 2 && x2.is_contiguous(), "row_reduce: contiguous (B, N) input");
   TORCH_CHECK(x2.scalar_type() == at::kFloat || x2.scalar_type() == at::kDouble, "row_reduce: fp32/fp64 input");
   const int64_t B = x2.size(0), N = x2.size(1);
-  auto out = at::empty({B}, x2.options().dtype(at::kDouble));
+  auto out = out_empty({B}, x2.options().dtype(at::kDouble));
   at::Tensor wd;
   if (w.has_value() && w->defined()) {
     wd = w->to(x2.device(), at::kDouble).contiguous();

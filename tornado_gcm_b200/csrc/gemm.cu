@@ -6,6 +6,7 @@
 //   * BF16 linear layers: forward with fused bias + activation (+ saved
 //     pre-activation), data-gradient with the activation derivative fused,
 //     weight-gradient with split-K fp32 accumulation.
+#include "alloc.h"
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -193,7 +194,7 @@ at::Tensor sht_synth(const at::Tensor& x, int64_t L, const at::Tensor& P, const 
   const int64_t I = F.size(0), M2p = F.size(1);
   TORCH_CHECK(M2 == 2 * Mw - 1 && M2p % 4 == 0 && M2p >= M2 && Lp >= L, "basis shape mismatch");
   TORCH_CHECK(ws.numel() >= S * J * M2p, "workspace too small");
-  auto out = lat_major ? at::empty({S, J, I}, x.options()) : at::empty({S, I, J}, x.options());
+  auto out = lat_major ? out_empty({S, J, I}, x.options()) : out_empty({S, I, J}, x.options());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const int bnj = pick_bn_j(J);
   {
@@ -248,7 +249,7 @@ at::Tensor sht_anal(const at::Tensor& N_in, const at::Tensor& Ft, const at::Tens
   TORCH_CHECK(Ft.size(1) == I && Pt.size(2) == J && J % 4 == 0 && I % 4 == 0, "basis shape mismatch");
   TORCH_CHECK(ws.numel() >= S * M2 * J, "workspace too small");
   TORCH_CHECK(Lo >= L, "output row length too small");
-  auto out = Lo > L ? at::zeros({S, M2, Lo}, N.options()) : at::empty({S, M2, Lo}, N.options());
+  auto out = Lo > L ? at::zeros({S, M2, Lo}, N.options()) : out_empty({S, M2, Lo}, N.options());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const int bnj = pick_bn_j(J);
   // 1) real DFT analysis.  Without a column scale it is ONE GEMM over all (s, j):

@@ -13,6 +13,7 @@
 //    implicit terms of the stage's z-combination, the per-wavenumber
 //    implicit solve, and on the last stage the spectral filter and the
 //    inner-state sanitiser — plus its adjoint.
+#include "alloc.h"
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -315,7 +316,7 @@ at::Tensor spectral_linear(const at::Tensor& x, int64_t L, int64_t C_out, int64_
   const int64_t B = x.size(0), M2 = x.size(2);
   // the CUDA kernel writes the padding columns itself; the CPU loop does not
   auto y = (out_lpad > L && !x.is_cuda()) ? at::zeros({B, C_out, M2, out_lpad}, x.options())
-                                          : at::empty({B, C_out, M2, out_lpad}, x.options());
+                                          : out_empty({B, C_out, M2, out_lpad}, x.options());
   LinearArgs a;
   a.x = x.data_ptr<float>();
   a.y = y.data_ptr<float>();
@@ -835,7 +836,7 @@ at::Tensor sil3_stage(const at::Tensor& y0, std::vector<at::Tensor> E, const at:
   fill_common(a, y0, ce, cp, cg, eta, G, H, Minv, lam, tref, dsig, filt, clamp_abs, R, final_stage, n);
   a.MinvT = ptr_or_null(minv_t);
   TORCH_CHECK(E.size() == ce.size(), "one coefficient per explicit tendency");
-  auto out = at::empty_like(y0);
+  auto out = out_empty_like(y0);
   a.y0 = y0.data_ptr<float>();
   for (size_t j = 0; j < E.size(); ++j) {
     TORCH_CHECK(E[j].is_contiguous() && E[j].sizes() == y0.sizes(), "E shape");
@@ -859,17 +860,17 @@ std::vector<at::Tensor> sil3_stage_adjoint(const at::Tensor& gout, const at::Ten
   memset(&a, 0, sizeof(a));
   fill_common(a, gout, ce, cp, cg, eta, G, H, Minv, lam, tref, dsig, filt, clamp_abs, R, final_stage, n);
   a.MinvT = ptr_or_null(minv_t);
-  auto g_y0 = at::empty_like(gout);
-  auto g_P = at::empty_like(gout);
+  auto g_y0 = out_empty_like(gout);
+  auto g_P = out_empty_like(gout);
   std::vector<at::Tensor> res{g_y0};
   std::vector<at::Tensor> gE;
   for (int64_t j = 0; j < nE; ++j) {
-    gE.push_back(at::empty_like(gout));
+    gE.push_back(out_empty_like(gout));
     a.g_E[j] = gE.back().data_ptr<float>();
   }
   at::Tensor g_y2;
   if (has_y2) {
-    g_y2 = at::empty_like(gout);
+    g_y2 = out_empty_like(gout);
     a.g_y2 = g_y2.data_ptr<float>();
   }
   a.gin = gout.data_ptr<float>();

@@ -29,7 +29,7 @@ import numpy as np
 import torch
 import torch.nn as nn
 import torch.utils.checkpoint as torch_checkpoint
-from torch.profiler import record_function
+from tornado_gcm_b200.utils.tracing import zone_range as record_function
 
 from tornado_gcm_b200.core import coordinate_systems, filtering, primitive_equations, time_integration
 from tornado_gcm_b200.precision.monitor import PrecisionMonitor

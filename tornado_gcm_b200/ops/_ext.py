@@ -44,6 +44,30 @@ def require(what: str = "kernel"):
     return torch.ops.tgcm
 
 
+_POISON = os.environ.get("TGCM_POISON", "0") not in ("", "0")
+
+
+def poison_enabled() -> bool:
+    """Poison mode: op outputs and scratch start as NaN (see ``csrc/alloc.h``)."""
+    return _POISON
+
+
+def set_poison_mode(on: bool) -> None:
+    """Switch poison mode for both the Python wrappers and the native allocations."""
+    global _POISON
+    _POISON = bool(on)
+    if load():
+        torch.ops.tgcm.set_poison_mode(_POISON)
+
+
+def empty(*shape, dtype, device) -> torch.Tensor:
+    """``torch.empty`` that honours poison mode (NaN / all-ones fill)."""
+    t = torch.empty(*shape, dtype=dtype, device=device)
+    if poison_enabled():
+        t.fill_(float("nan") if t.is_floating_point() else -1)
+    return t
+
+
 def error_flag(device) -> torch.Tensor:
     """Per-device int32 flag that kernels set on a bounded-wait timeout."""
     key = str(device)

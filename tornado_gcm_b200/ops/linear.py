@@ -92,9 +92,9 @@ class MlpFn(torch.autograd.Function):
                 bias = torch.zeros(Op, dtype=torch.float32, device=x2d.device)
                 bias[: lin.bias.shape[0]] = lin.bias.detach().float()
             last = i == n - 1
-            out = torch.empty(T, Op, dtype=torch.float32 if last else torch.bfloat16, device=x2d.device)
+            out = _ext.empty(T, Op, dtype=torch.float32 if last else torch.bfloat16, device=x2d.device)
             code = ACT_CODES[acts[i]]
-            aux = torch.empty(T, Op, dtype=torch.bfloat16, device=x2d.device) if (code and not last) else None
+            aux = _ext.empty(T, Op, dtype=torch.bfloat16, device=x2d.device) if (code and not last) else None
             ops.linear_fwd(hs[-1], wp, bias, code, out, aux, err)
             zs.append(aux)
             hs.append(out)
@@ -128,11 +128,11 @@ class MlpFn(torch.autograd.Function):
             if i > 0:
                 prev = zs[i - 1]
                 code = ACT_CODES[ctx.acts[i - 1]]
-                dprev = torch.empty(T, wp.shape[1], dtype=torch.bfloat16, device=g.device)
+                dprev = _ext.empty(T, wp.shape[1], dtype=torch.bfloat16, device=g.device)
                 ops.linear_dgrad(dy, wp, dprev, prev if prev.numel() else None, code, err)
                 dy = dprev
             else:
-                dx = torch.empty(T, wp.shape[1], dtype=torch.float32, device=g.device)
+                dx = _ext.empty(T, wp.shape[1], dtype=torch.float32, device=g.device)
                 ops.linear_dgrad(dy, wp, dx, None, 0, err)
                 dx_out = dx[:, : ctx.K0].to(ctx.x_dtype)
         grads.reverse()

@@ -82,7 +82,7 @@ def _synth(x3: torch.Tensor, b: _Bases, col_scale=None, lat_major: bool = False,
         x3 = torch.nn.functional.pad(x3, (0, b.Lp - b.L)).contiguous() if b.Lp != b.L else x3.contiguous()
         if b.Lp != b.L:
             x3 = x3[..., : b.L]
-    ws = torch.empty(S * b.J * b.M2p, dtype=torch.float32, device=x3.device)
+    ws = _ext.empty(S * b.J * b.M2p, dtype=torch.float32, device=x3.device)
     return ops.sht_synth(x3, b.L, b.Pw if weighted else b.P, b.F, ws, col_scale, _ext.error_flag(x3.device),
                          lat_major)
 
@@ -92,7 +92,7 @@ def _anal(n3: torch.Tensor, b: _Bases, col_scale=None, lat_major: bool = False,
     """Nodal (S, I, J) (or (S, J, I) when lat_major) → modal (S, M2, L)."""
     ops = _ext.require("spherical-harmonic analysis")
     S = n3.shape[0]
-    ws = torch.empty(S * b.M2 * b.J, dtype=torch.float32, device=n3.device)
+    ws = _ext.empty(S * b.M2 * b.J, dtype=torch.float32, device=n3.device)
     return ops.sht_anal(n3.float(), b.Ft, b.Ptw if weighted else b.Pt, b.L, ws, col_scale,
                         _ext.error_flag(n3.device), lat_major)
 

@@ -17,6 +17,7 @@ from __future__ import annotations
 
 import dataclasses
 import logging
+import os
 import math
 from typing import Any, Callable, Optional, Sequence
 
@@ -240,6 +241,23 @@ class GCMTrainer:
         self._static = None
         self._static_loss = None
         self.step_count = 0
+        # host-side liveness check and fault injection between steps (see parallel/elastic.py)
+        self.heartbeat = None
+        self._fault_spec = os.environ.get("TGCM_FAULT_INJECT") or None
+
+    def attach_heartbeat(self, heartbeat) -> None:
+        """Beat and check peers before every step; a dead peer raises before any launch."""
+        self.heartbeat = heartbeat
+
+    def _pre_step(self) -> None:
+        if self._fault_spec is not None:
+            from tornado_gcm_b200.parallel.elastic import maybe_inject_fault
+            from tornado_gcm_b200.parallel.ddp import get_rank
+
+            maybe_inject_fault(get_rank(), self.step_count, self._fault_spec)
+        if self.heartbeat is not None:
+            self.heartbeat.beat(self.step_count)
+            self.heartbeat.check(self.step_count)
 
     def _step_body(self, data0, targets, forcings):
         from tornado_gcm_b200.ops import linear as linear_ops
@@ -266,6 +284,7 @@ class GCMTrainer:
     def train_step(self, data0: dict, targets: list, forcings: dict) -> torch.Tensor:
         """One optimizer step; returns the loss as a 0-d device tensor."""
         self.gcm.train()
+        self._pre_step()
         if not self.use_graph:
             self._zero()
             loss = self._step_body(data0, targets, forcings)
