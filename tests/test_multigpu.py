@@ -1,0 +1,108 @@
+"""Peer-memory collectives on 2+ B200s (skipped with fewer GPUs).
+
+Ranks are child processes with NCCL for bootstrap (NVLS off) and the
+framework's own kernels on plain peer loads/stores:
+* fused mean / sum all-reduce against NCCL;
+* latitude-sharded transforms (partial quadratures reduced by the fused
+  kernel) against the single-GPU transform;
+* the bounded wait: one rank launches the reduction alone, its barrier gives
+  up after ~1 s and the kernel reports error code 20 instead of hanging.
+"""
+
+import datetime
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                                 reason="needs 2 GPUs")]
+
+
+def _port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=torch.device("cuda", rank))
+        from tornado_gcm_b200.core import spherical_harmonic as shm
+        from tornado_gcm_b200.ops import _ext
+        from tornado_gcm_b200.parallel.fused_allreduce import make_reducer
+        from tornado_gcm_b200.parallel.sharded_sht import LatitudeShardedSHT
+
+        dev = torch.device("cuda", rank)
+        res = {}
+        red = make_reducer(1 << 20, dev)
+        gen = torch.Generator(device=dev).manual_seed(100 + rank)
+        x = torch.randn(1 << 20, device=dev, generator=gen)
+        ref = x.clone()
+        dist.all_reduce(ref)
+        red.flat.copy_(x)
+        red.all_reduce_mean(red.flat)
+        res["mean"] = float((red.flat - ref / world).abs().max())
+        red.flat.copy_(x)
+        red.all_reduce_sum(red.flat)
+        res["sum"] = float((red.flat - ref).abs().max())
+        # latitude-sharded TL63 analysis with the fused reduction
+        g = shm.Grid.TL63(precision="float32")
+        torch.manual_seed(0)
+        modal = (torch.randn(8, *g.modal_shape) * torch.as_tensor(g.mask)).to(dev)
+        nodal = g.to_nodal(modal.cpu().double()).float().to(dev)
+        sht = LatitudeShardedSHT(g, scheme="mirrored", reducer=red)
+        local = sht.scatter(nodal)
+        out = sht.to_modal(local)
+        full = g.to_modal(nodal.cpu().double()).float().to(dev)
+        res["sht"] = float((out - full).abs().max() / full.abs().max())
+        res["nodal"] = float((sht.to_nodal(modal) - local).abs().max() / local.abs().max())
+        torch.cuda.synchronize(dev)
+        res["flag"] = _ext.check_error_flag(dev)
+        # bounded wait: rank 0 reduces alone on a fresh reducer
+        lonely = make_reducer(4096, dev)
+        dist.barrier()
+        if rank == 0:
+            lonely.all_reduce_sum(lonely.flat)
+            torch.cuda.synchronize(dev)
+            code = int(_ext.error_flag(dev).item())
+            _ext.error_flag(dev).zero_()
+            res["timeout_code"] = code
+        dist.barrier()
+        del red, lonely
+        dist.destroy_process_group()
+        q.put((rank, res))
+    except Exception:  # pragma: no cover
+        q.put((rank, traceback.format_exc()))
+
+
+def test_fused_collectives_two_gpus():
+    import torch.multiprocessing as mp
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+    for rank, res in out:
+        assert isinstance(res, dict), res
+        assert res["mean"] < 1e-5 and res["sum"] < 1e-5
+        assert res["sht"] < 1e-4 and res["nodal"] < 1e-4
+        assert res["flag"] == 0
+        if rank == 0:
+            assert res["timeout_code"] == 20

@@ -200,36 +200,45 @@ __global__ void __launch_bounds__(kLinThreads) spectral_linear_kernel(LinearArgs
 // the source row to the paired ±m row.  Vertical terms use the per-point path.
 constexpr int kRowWarps = 8;
 
-template <int NL>
+// NB batch samples per warp: the recipe tables are identical for every sample,
+// so each term's metadata, coefficient, diagonal and recurrence weights are
+// read once and applied to NB rows (the kernel is instruction-bound on that
+// per-term work).  grid = (m-row blocks, C_out, ceil(B / NB)).
+template <int NL, int NB>
 __global__ void __launch_bounds__(32 * kRowWarps) spectral_linear_rows_kernel(LinearArgs a) {
-  __shared__ float sbuf[kRowWarps][32 * NL + 2];
+  __shared__ float sbuf[kRowWarps][NB][32 * NL + 2];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int mr = blockIdx.x * kRowWarps + warp;
   if (mr >= a.M2) return;
-  const int s = blockIdx.y % a.C_out;
-  const int b = blockIdx.y / a.C_out;
+  const int s = blockIdx.y;
+  const int b0 = blockIdx.z * NB;
+  const int nb = min(NB, a.B - b0);
   const int L = a.L;
-  const float* xb = a.x + b * a.xs_b;
-  float* buf = sbuf[warp] + 1;  // buf[l] for l in [-1, 32*NL]
-  float acc[NL];
+  float acc[NB][NL];
 #pragma unroll
-  for (int j = 0; j < NL; ++j) acc[j] = 0.f;
+  for (int q = 0; q < NB; ++q)
+#pragma unroll
+    for (int j = 0; j < NL; ++j) acc[q][j] = 0.f;
   const int t0 = __ldg(a.row_ptr + s), t1 = __ldg(a.row_ptr + s + 1);
   for (int t = t0; t < t1; ++t) {
     const int* T = a.terms + 7 * t;
     const int src = __ldg(T + 1), st = __ldg(T + 2), pre = __ldg(T + 3), post = __ldg(T + 4);
     const float cf = __ldg(a.coef + t);
     if (st == kStVert || st == kStVertT) {
-      LinearArgs ab = a;
-      ab.x = xb;
       const int mat = __ldg(T + 5), row = __ldg(T + 6);
 #pragma unroll
-      for (int j = 0; j < NL; ++j) {
-        const int l = lane + 32 * j;
-        if (l < L) {
-          float v = stencil_val(ab, 0, src, st, pre, mr, l, mat, row);
-          if (post >= 0) v *= __ldg(a.diag + post * L + l);
-          acc[j] = fmaf(cf, v, acc[j]);
+      for (int q = 0; q < NB; ++q) {
+        if (q >= nb) break;
+        LinearArgs ab = a;
+        ab.x = a.x + (b0 + q) * a.xs_b;
+#pragma unroll
+        for (int j = 0; j < NL; ++j) {
+          const int l = lane + 32 * j;
+          if (l < L) {
+            float v = stencil_val(ab, 0, src, st, pre, mr, l, mat, row);
+            if (post >= 0) v *= __ldg(a.diag + post * L + l);
+            acc[q][j] = fmaf(cf, v, acc[q][j]);
+          }
         }
       }
       continue;
@@ -242,70 +251,106 @@ __global__ void __launch_bounds__(32 * kRowWarps) spectral_linear_rows_kernel(Li
       srow = (mr & 1) ? mr + 1 : mr - 1;
       fac = (mr & 1) ? static_cast<float>(jm) : -static_cast<float>(jm);
     }
-    const float* xr = xb + src * a.xs_c + srow * a.xs_m;
-    float xv[NL];
+    // per-l factors shared by all samples
+    float pdiag[NL], qdiag[NL];
 #pragma unroll
     for (int j = 0; j < NL; ++j) {
       const int l = lane + 32 * j;
-      float v = 0.f;
-      if (l < L) {
-        v = __ldg(xr + l);
-        if (pre >= 0) v *= __ldg(a.diag + pre * L + l);
-      }
-      xv[j] = v;
+      pdiag[j] = (pre >= 0 && l < L) ? __ldg(a.diag + pre * L + l) : 1.f;
+      qdiag[j] = (post >= 0 && l < L) ? cf * __ldg(a.diag + post * L + l) : cf;
     }
-    const bool lat = st == kStCdlat || st == kStHdlat || st == kStCdlatT || st == kStHdlatT;
-    if (lat) {
-      __syncwarp();
+    const float* xr0 = a.x + src * a.xs_c + srow * a.xs_m;
+    float xv[NB][NL];
 #pragma unroll
-      for (int j = 0; j < NL; ++j) buf[lane + 32 * j] = xv[j];
+    for (int q = 0; q < NB; ++q)
+#pragma unroll
+      for (int j = 0; j < NL; ++j) {
+        const int l = lane + 32 * j;
+        xv[q][j] = (q < nb && l < L) ? __ldg(xr0 + (b0 + q) * a.xs_b + l) * pdiag[j] : 0.f;
+      }
+    const bool lat = st == kStCdlat || st == kStHdlat || st == kStCdlatT || st == kStHdlatT;
+    if (!lat) {
+#pragma unroll
+      for (int q = 0; q < NB; ++q)
+#pragma unroll
+        for (int j = 0; j < NL; ++j) acc[q][j] = fmaf(qdiag[j] * fac, xv[q][j], acc[q][j]);
+      continue;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < NB; ++q) {
+      float* buf = sbuf[warp][q] + 1;  // buf[l] for l in [-1, 32*NL]
+#pragma unroll
+      for (int j = 0; j < NL; ++j) buf[lane + 32 * j] = xv[q][j];
       if (lane == 0) {
         buf[-1] = 0.f;
         buf[32 * NL] = 0.f;
       }
-      __syncwarp();
     }
+    __syncwarp();
+    const float* ra = a.rec_a + mr * L;
+    const float* rb = a.rec_b + mr * L;
 #pragma unroll
     for (int j = 0; j < NL; ++j) {
       const int l = lane + 32 * j;
       if (l >= L) continue;
-      float v;
-      if (!lat) {
-        v = fac * xv[j];
+      // v = cp * x[l+1] + cm * x[l-1]
+      float cp, cm;
+      if (st == kStCdlat) {
+        cp = (l + 1 < L) ? (l + 2) * __ldg(ra + l + 1) : 0.f;
+        cm = (l >= 1) ? -(l - 1) * __ldg(rb + l - 1) : 0.f;
+      } else if (st == kStHdlat) {
+        cp = (l + 1 < L) ? l * __ldg(ra + l + 1) : 0.f;
+        cm = (l >= 1) ? -(l + 1) * __ldg(rb + l - 1) : 0.f;
+      } else if (st == kStCdlatT) {
+        cm = (l >= 1) ? (l + 1) * __ldg(ra + l) : 0.f;
+        cp = (l + 1 < L) ? -l * __ldg(rb + l) : 0.f;
       } else {
+        cm = (l >= 1) ? (l - 1) * __ldg(ra + l) : 0.f;
+        cp = (l + 1 < L) ? -(l + 2) * __ldg(rb + l) : 0.f;
+      }
+      cp *= qdiag[j];
+      cm *= qdiag[j];
+#pragma unroll
+      for (int q = 0; q < NB; ++q) {
+        const float* buf = sbuf[warp][q] + 1;
         const float xp = (l + 1 < L) ? buf[l + 1] : 0.f;
         const float xm = (l >= 1) ? buf[l - 1] : 0.f;
-        const float* ra = a.rec_a + mr * L;
-        const float* rb = a.rec_b + mr * L;
-        if (st == kStCdlat)
-          v = (l + 1 < L ? (l + 2) * __ldg(ra + l + 1) * xp : 0.f) - (l >= 1 ? (l - 1) * __ldg(rb + l - 1) * xm : 0.f);
-        else if (st == kStHdlat)
-          v = (l + 1 < L ? l * __ldg(ra + l + 1) * xp : 0.f) - (l >= 1 ? (l + 1) * __ldg(rb + l - 1) * xm : 0.f);
-        else if (st == kStCdlatT)
-          v = (l >= 1 ? (l + 1) * __ldg(ra + l) * xm : 0.f) - (l + 1 < L ? l * __ldg(rb + l) * xp : 0.f);
-        else
-          v = (l >= 1 ? (l - 1) * __ldg(ra + l) * xm : 0.f) - (l + 1 < L ? (l + 2) * __ldg(rb + l) * xp : 0.f);
+        acc[q][j] = fmaf(cp, xp, fmaf(cm, xm, acc[q][j]));
       }
-      if (post >= 0) v *= __ldg(a.diag + post * L + l);
-      acc[j] = fmaf(cf, v, acc[j]);
     }
   }
-  float* yrow = a.y + b * a.ys_b + s * a.ys_c + mr * a.ys_m;
 #pragma unroll
-  for (int j = 0; j < NL; ++j) {
-    const int l = lane + 32 * j;
-    if (l < L)
-      yrow[l] = acc[j];
-    else if (l < a.ys_m)
-      yrow[l] = 0.f;  // 16-byte row padding
+  for (int q = 0; q < NB; ++q) {
+    if (q >= nb) break;
+    float* yrow = a.y + (b0 + q) * a.ys_b + s * a.ys_c + mr * a.ys_m;
+#pragma unroll
+    for (int j = 0; j < NL; ++j) {
+      const int l = lane + 32 * j;
+      if (l < L)
+        yrow[l] = acc[q][j];
+      else if (l < a.ys_m)
+        yrow[l] = 0.f;  // 16-byte row padding
+    }
+    for (long long z = 32 * NL + lane; z < a.ys_m; z += 32) yrow[z] = 0.f;
   }
-  for (long long z = 32 * NL + lane; z < a.ys_m; z += 32) yrow[z] = 0.f;
+}
+
+template <int NL, int NB>
+static void launch_rows_nb(const LinearArgs& a, cudaStream_t st) {
+  dim3 grid(static_cast<unsigned>((a.M2 + kRowWarps - 1) / kRowWarps), static_cast<unsigned>(a.C_out),
+            static_cast<unsigned>((a.B + NB - 1) / NB));
+  spectral_linear_rows_kernel<NL, NB><<<grid, 32 * kRowWarps, 0, st>>>(a);
 }
 
 template <int NL>
 static void launch_rows(const LinearArgs& a, cudaStream_t st) {
-  dim3 grid(static_cast<unsigned>((a.M2 + kRowWarps - 1) / kRowWarps), static_cast<unsigned>(a.B * a.C_out));
-  spectral_linear_rows_kernel<NL><<<grid, 32 * kRowWarps, 0, st>>>(a);
+  if (a.B >= 4 && NL <= 5)
+    launch_rows_nb<NL, 4>(a, st);
+  else if (a.B >= 2)
+    launch_rows_nb<NL, 2>(a, st);
+  else
+    launch_rows_nb<NL, 1>(a, st);
 }
 
 // x: (B, C_in, M2, Lx) ; returns y: (B, C_out, M2, Ly) with Ly = out_lpad (>= L), pad zero.
@@ -333,7 +378,7 @@ at::Tensor spectral_linear(const at::Tensor& x, int64_t L, int64_t C_out, int64_
   a.B = static_cast<int>(B); a.C_out = static_cast<int>(C_out); a.M2 = static_cast<int>(M2); a.L = static_cast<int>(L);
   if (x.is_cuda()) {
     c10::cuda::CUDAGuard guard(x.device());
-    TORCH_CHECK(B * C_out <= 65535 && M2 * L < (1LL << 31), "spectral_linear: launch grid too large");
+    TORCH_CHECK(C_out <= 65535 && B <= 65535 && M2 * L < (1LL << 31), "spectral_linear: launch grid too large");
     TORCH_CHECK(x.stride(1) < (1LL << 31) && x.size(1) * x.stride(1) < (1LL << 31),
                 "spectral_linear: one batch sample must fit 32-bit offsets");
     auto st = at::cuda::getCurrentCUDAStream();
