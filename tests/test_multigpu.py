@@ -106,3 +106,59 @@ def test_fused_collectives_two_gpus():
         assert res["flag"] == 0
         if rank == 0:
             assert res["timeout_code"] == 20
+
+
+def _worker_fused_sht(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=torch.device("cuda", rank))
+        from tornado_gcm_b200.core import spherical_harmonic as shm
+        from tornado_gcm_b200.ops import _ext
+        from tornado_gcm_b200.parallel.sharded_sht import LatitudeShardedSHT
+
+        dev = torch.device("cuda", rank)
+        g = shm.Grid.TL63(precision="tf32")
+        torch.manual_seed(0)
+        l = torch.arange(g.modal_shape[1], dtype=torch.float64)
+        modal = (torch.randn(12, *g.modal_shape, dtype=torch.float64) * torch.as_tensor(g.mask)
+                 * (1.0 + l) ** -1.5)
+        nodal = g.with_precision("highest").to_nodal(modal)
+        sht = LatitudeShardedSHT(g, scheme="mirrored")
+        sht.enable_fused(16, dev)
+        res = {}
+        with torch.no_grad():
+            loc = sht.to_nodal_gpu(modal.float().to(dev))
+            res["nodal"] = float((loc.double().cpu() - sht.scatter(nodal)).norm() / sht.scatter(nodal).norm())
+            outs = [sht.to_modal(sht.scatter(nodal).float().to(dev)) for _ in range(3)]  # alternating buffers
+        ref = g.with_precision("highest").to_modal(nodal)
+        res["modal"] = max(float((o.double().cpu() - ref).norm() / ref.norm()) for o in outs)
+        torch.cuda.synchronize(dev)
+        res["flag"] = _ext.check_error_flag(dev)
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, res))
+    except Exception:  # pragma: no cover
+        q.put((rank, traceback.format_exc()))
+
+
+def test_fused_sharded_transform_two_gpus():
+    import torch.multiprocessing as mp
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker_fused_sht, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+    for rank, res in out:
+        assert isinstance(res, dict), res
+        assert res["nodal"] < 2e-3 and res["modal"] < 2e-3     # TF32 transforms
+        assert res["flag"] == 0

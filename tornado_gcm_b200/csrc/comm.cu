@@ -130,7 +130,35 @@ __global__ void __launch_bounds__(kArThreads) fused_allreduce_kernel(ArArgs a) {
   ar_barrier(a, 1, epoch);
 }
 
+// Stand-alone cross-rank barrier on a signal pad (one block): every rank
+// announces the next epoch in every peer's pad and waits (bounded) for all
+// peers' announcements.  Orders the peer reductions of a preceding kernel
+// (fused Legendre analysis) before the ranks read their buffers.
+__global__ void __launch_bounds__(32) peer_barrier_kernel(ArArgs a) {
+  __shared__ uint32_t s_epoch;
+  if (threadIdx.x == 0) s_epoch = *(volatile uint32_t*)(a.pads[a.rank] + a.rank) + 1u;
+  __syncthreads();
+  ar_barrier(a, 0, s_epoch);
+}
+
 }  // namespace
+
+// pad_ptrs: int64 (world) CPU tensor of the peers' signal pads (>= 2 * 8 words each, zeroed once)
+void peer_barrier(const at::Tensor& pad_ptrs, int64_t rank, const c10::optional<at::Tensor>& err, int64_t device) {
+  TORCH_CHECK(pad_ptrs.scalar_type() == at::kLong && !pad_ptrs.is_cuda(), "pad_ptrs must be an int64 CPU tensor");
+  const int64_t world = pad_ptrs.numel();
+  TORCH_CHECK(world >= 1 && world <= kArMaxRanks && rank >= 0 && rank < world, "1..8 ranks supported");
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  ArArgs a;
+  memset(&a, 0, sizeof(a));
+  for (int64_t p = 0; p < world; ++p) a.pads[p] = reinterpret_cast<uint32_t*>(pad_ptrs.data_ptr<int64_t>()[p]);
+  a.world = static_cast<int>(world);
+  a.rank = static_cast<int>(rank);
+  a.blocks = 1;
+  a.err = (err.has_value() && err->defined()) ? err->data_ptr<int>() : nullptr;
+  peer_barrier_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
 
 // buf: this rank's symmetric fp32 buffer; buf_ptrs / pad_ptrs: int64 (world)
 // host tensors of the peers' buffer and signal-pad addresses.  The sum is
@@ -166,6 +194,7 @@ void fused_allreduce_mean(at::Tensor& buf, const at::Tensor& buf_ptrs, const at:
 
 TORCH_LIBRARY_FRAGMENT(tgcm, m) {
   m.def("fused_allreduce_mean(Tensor(a!) buf, Tensor buf_ptrs, Tensor pad_ptrs, int rank, int blocks, Tensor? err, float scale=0.0) -> ()");
+  m.def("peer_barrier(Tensor pad_ptrs, int rank, Tensor? err, int device) -> ()", &tgcm::peer_barrier);
 }
 
 TORCH_LIBRARY_IMPL(tgcm, CUDA, m) { m.impl("fused_allreduce_mean", &tgcm::fused_allreduce_mean); }

@@ -14,10 +14,12 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
 
+#include <algorithm>
 #include <stdexcept>
 #include <vector>
 
 #include "dycore_column.h"
+#include "dycore_column_warp.cuh"
 
 namespace tgcm {
 
@@ -62,6 +64,18 @@ static at::Tensor attach_gmat(ColumnConsts& c, const c10::optional<at::Tensor>& 
   at::Tensor g = gmat->to(like.device(), at::kFloat).contiguous();
   c.gmat = g.data_ptr<float>();
   return g;
+}
+
+// Raise a column kernel's dynamic shared-memory limit once per (kernel, device).
+static void set_col_smem(const void* fn, size_t bytes) {
+  static std::vector<std::pair<const void*, int>> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  for (auto& d : done)
+    if (d.first == fn && d.second == dev) return;
+  cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+  done.emplace_back(fn, dev);
+  TORCH_CHECK(bytes <= 64 * 1024, "column kernel staging exceeds 64 KB");
 }
 
 // ── column kernels ──────────────────────────────────────────────────────────
@@ -126,7 +140,16 @@ at::Tensor column_fwd(const at::Tensor& nin, const at::Tensor& sec2, const at::T
     const int threads = 128;
     const unsigned blocks = static_cast<unsigned>((total + threads - 1) / threads);
     auto st = at::cuda::getCurrentCUDAStream();
-    if (n <= 32)
+    if (n <= 32) {
+      const unsigned wblocks = static_cast<unsigned>((total + kColWarps - 1) / kColWarps);
+      const int h = hum_terms ? 1 : 0;
+      const int slots = std::max(col_in_fields(static_cast<int>(nt), h), col_out_fields(static_cast<int>(nt), h));
+      const size_t smem = static_cast<size_t>(slots) * kSlotFloats * sizeof(float);
+      set_col_smem(reinterpret_cast<const void*>(column_fwd_warp_kernel), smem);
+      column_fwd_warp_kernel<<<wblocks, 32 * kColWarps, smem, st>>>(
+          c, ix, nin.data_ptr<float>(), out.data_ptr<float>(), s2.data_ptr<float>(), co.data_ptr<float>(),
+          static_cast<int>(batch), static_cast<int>(I), static_cast<int>(J), lat_major ? 1 : 0);
+    } else if (n <= 32)
       column_fwd_kernel<32><<<blocks, threads, 0, st>>>(c, ix, nin.data_ptr<float>(), out.data_ptr<float>(),
                                                         s2.data_ptr<float>(), co.data_ptr<float>(),
                                                         static_cast<int>(batch), static_cast<int>(I),
@@ -175,7 +198,16 @@ at::Tensor column_vjp_op(const at::Tensor& nin, const at::Tensor& gout, const at
     const unsigned blocks = static_cast<unsigned>((total + threads - 1) / threads);
     auto st = at::cuda::getCurrentCUDAStream();
     const int bi = static_cast<int>(batch), ii = static_cast<int>(I), jj = static_cast<int>(J), lm = lat_major ? 1 : 0;
-    if (n <= 32 && nt <= 4)
+    if (n <= 32) {
+      const unsigned wblocks = static_cast<unsigned>((total + kColWarps - 1) / kColWarps);
+      const int h = hum_terms ? 1 : 0;
+      const int slots = col_in_fields(static_cast<int>(nt), h) + col_out_fields(static_cast<int>(nt), h);
+      const size_t smem = static_cast<size_t>(slots) * kSlotFloats * sizeof(float);
+      set_col_smem(reinterpret_cast<const void*>(column_vjp_warp_kernel), smem);
+      column_vjp_warp_kernel<<<wblocks, 32 * kColWarps, smem, st>>>(c, ix, nin.data_ptr<float>(), gout.data_ptr<float>(),
+                                                                gin.data_ptr<float>(), s2.data_ptr<float>(),
+                                                                co.data_ptr<float>(), bi, ii, jj, lm);
+    } else if (n <= 32 && nt <= 4)
       column_vjp_kernel<32, 4><<<blocks, threads, 0, st>>>(c, ix, nin.data_ptr<float>(), gout.data_ptr<float>(),
                                                              gin.data_ptr<float>(), s2.data_ptr<float>(),
                                                              co.data_ptr<float>(), bi, ii, jj, lm);

@@ -237,9 +237,14 @@ at::Tensor sht_synth(const at::Tensor& x, int64_t L, const at::Tensor& P, const 
 }
 
 // N: nodal (S, J, I) if lat_major else (S, I, J);  Ft: (M2, I);  Pt: (Mw, L, J);  returns (S, M2, Lo).
+// peer_ptrs (optional, int64 CPU): the Legendre step adds its (S, M2, Lo) result
+// into every listed fp32 buffer (the ranks' symmetric output buffers, this one
+// included) with system-scope reductions instead of writing `out`; the caller
+// zeroes those buffers beforehand and synchronises the ranks afterwards.
 at::Tensor sht_anal(const at::Tensor& N_in, const at::Tensor& Ft, const at::Tensor& Pt, int64_t Lo,
                     const at::Tensor& ws, const c10::optional<at::Tensor>& col_scale,
-                    const c10::optional<at::Tensor>& err, bool lat_major) {
+                    const c10::optional<at::Tensor>& err, bool lat_major,
+                    const c10::optional<at::Tensor>& peer_ptrs) {
   TORCH_CHECK(N_in.is_cuda() && N_in.scalar_type() == at::kFloat && N_in.dim() == 3, "N must be fp32 CUDA (S, ., .)");
   c10::cuda::CUDAGuard guard(N_in.device());
   at::Tensor N = lat_major ? N_in.contiguous() : N_in.transpose(1, 2).contiguous();  // -> (S, J, I)
@@ -290,6 +295,13 @@ at::Tensor sht_anal(const at::Tensor& N_in, const at::Tensor& Ft, const at::Tens
     p.a_pair = 1;
     p.C = out.data_ptr(); p.c_pair = 1; p.c_ps = M2 * Lo; p.c_pmr = Lo; p.c_sc = 1;
     p.err = err_ptr(err);
+    if (peer_ptrs.has_value() && peer_ptrs->defined()) {
+      TORCH_CHECK(!peer_ptrs->is_cuda() && peer_ptrs->scalar_type() == at::kLong && peer_ptrs->numel() >= 1 &&
+                      peer_ptrs->numel() <= 8,
+                  "peer_ptrs must be 1..8 int64 addresses on the CPU");
+      p.n_peers = static_cast<int>(peer_ptrs->numel());
+      for (int i = 0; i < p.n_peers; ++i) p.peer_C[i] = reinterpret_cast<float*>(peer_ptrs->data_ptr<int64_t>()[i]);
+    }
     gemm_dispatch(2, bnl, false, false, ta, tb, p, st);
   }
   return out;
@@ -416,7 +428,8 @@ TORCH_LIBRARY_FRAGMENT(tgcm, m) {
   m.def("gemm_profile_buffer(Tensor? buf, int launch_index=-1) -> ()");
   m.def("bgemm_tf32(Tensor A, Tensor B, Tensor(a!) C, float alpha, Tensor? err) -> ()");
   m.def("sht_synth(Tensor x, int L, Tensor P, Tensor F, Tensor ws, Tensor? col_scale, Tensor? err, bool lat_major) -> Tensor");
-  m.def("sht_anal(Tensor N, Tensor Ft, Tensor Pt, int Lo, Tensor ws, Tensor? col_scale, Tensor? err, bool lat_major) -> Tensor");
+  m.def("sht_anal(Tensor N, Tensor Ft, Tensor Pt, int Lo, Tensor ws, Tensor? col_scale, Tensor? err, bool lat_major, "
+        "Tensor? peer_ptrs=None) -> Tensor");
   m.def("linear_fwd(Tensor X, Tensor W, Tensor? bias, int act, Tensor(a!) out, Tensor? aux, Tensor? err) -> ()");
   m.def("linear_dgrad(Tensor dY, Tensor W, Tensor(a!) dX, Tensor? pre, int pre_act, Tensor? err) -> ()");
   m.def("linear_wgrad(Tensor dY, Tensor X, Tensor(a!) dW, int splits, Tensor? err) -> ()");

@@ -46,6 +46,12 @@ struct GemmParams {
   const __nv_bfloat16* grad_pre; // multiply by act'(grad_pre) (plain layout) or null
   int grad_act;
   int* err;
+  // Peer reduction (fused cross-GPU sum): when n_peers > 0 every output value
+  // is added with a system-scope reduction into the same offset of each
+  // peer's fp32 buffer peer_C[i] (this GPU's own buffer included) instead of
+  // being stored to C.  Plain red.add over NVLink, no TMA, no multicast.
+  int n_peers;
+  float* peer_C[8];
   // optional per-CTA cycle counters (diagnostics): [cta][0..7] =
   // producer wait, producer issue, mma wait-empty-acc, mma wait-full, mma issue,
   // epilogue wait, epilogue work, tiles
@@ -82,7 +88,15 @@ struct GemmSmem {
   static constexpr int kTotal = STAGES * kStage + kStaging + kBars + 1024;  // + alignment slack
 };
 
+__device__ __forceinline__ void red_add_sys(float* addr, float v) {
+  asm volatile("red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(addr), "f"(v) : "memory");
+}
+
 __device__ __forceinline__ void store_out(const GemmParams& p, long long off, float v) {
+  if (p.n_peers > 0) {
+    for (int i = 0; i < p.n_peers; ++i) red_add_sys(p.peer_C[i] + off, v);
+    return;
+  }
   if (p.out_bf16) {
     __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(p.C) + off;
     if (p.beta != 0.f) v += p.beta * __bfloat162float(*c);
@@ -478,9 +492,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t taddr_row = tmem_base + static_cast<uint32_t>(acc) * kAccCols +
                                  (static_cast<uint32_t>(q * 32) << 16);
       const bool plain = !p.bias && !p.col_scale && !p.aux && !p.grad_pre && p.act == 0 && !p.out_bf16 &&
-                         p.k_splits == 1 && p.beta == 0.f;
+                         p.k_splits == 1 && p.beta == 0.f && p.n_peers == 0;
       const int esz = p.out_bf16 ? 2 : 4;
       const bool vec_ok = !p.c_pair && p.c_sc == 1 && p.c_sr != 1 && p.k_splits == 1 && p.beta == 0.f &&
+                          p.n_peers == 0 &&
                           (reinterpret_cast<uintptr_t>(p.C) % 16 == 0) && ((p.c_sr * esz) % 16 == 0) &&
                           ((p.c_sg * esz) % 16 == 0) && (BN % 8 == 0) &&
                           (!p.aux || (reinterpret_cast<uintptr_t>(p.aux) % 16 == 0 && (p.c_sr * 2) % 16 == 0 &&
@@ -588,6 +603,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_arrive(&tmem_empty_bar[acc]);
       if (p.prof) t_work += clock64() - c1;
     }
+    if (p.n_peers > 0) __threadfence_system();  // peer reductions performed before the kernel ends
     if (p.prof && warp == 2 && lane == 0) {
       p.prof[blockIdx.x * 8 + 5] = t_ew;
       p.prof[blockIdx.x * 8 + 6] = t_work;

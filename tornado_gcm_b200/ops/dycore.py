@@ -124,16 +124,19 @@ class ColumnSpec:
         return x.reshape(-1, *x.shape[-2:])
 
 
-def column_forward_raw(spec: ColumnSpec, nin: torch.Tensor, batch: int) -> torch.Tensor:
+def column_forward_raw(spec: ColumnSpec, nin: torch.Tensor, batch: int, lat_major: bool = False) -> torch.Tensor:
     ops = _ext.require("column tendency")
     s2, co = spec.device_consts(nin.device)
-    return ops.column_fwd(nin.contiguous(), s2, co, *_args_with_batch(spec, batch))
+    return ops.column_fwd(nin.contiguous(), s2, co, *_args_with_batch(spec, batch), lat_major,
+                          spec.device_gmat(nin.device))
 
 
-def column_vjp_raw(spec: ColumnSpec, nin: torch.Tensor, gout: torch.Tensor, batch: int) -> torch.Tensor:
+def column_vjp_raw(spec: ColumnSpec, nin: torch.Tensor, gout: torch.Tensor, batch: int,
+                   lat_major: bool = False) -> torch.Tensor:
     ops = _ext.require("column tendency VJP")
     s2, co = spec.device_consts(nin.device)
-    return ops.column_vjp(nin.contiguous(), gout.contiguous(), s2, co, *_args_with_batch(spec, batch))
+    return ops.column_vjp(nin.contiguous(), gout.contiguous(), s2, co, *_args_with_batch(spec, batch), lat_major,
+                          spec.device_gmat(nin.device))
 
 
 def _args_with_batch(spec, batch):

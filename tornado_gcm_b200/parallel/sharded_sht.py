@@ -20,9 +20,20 @@ northern rows only, on even and odd ``l+|m|`` separately, which halves its
 flops.  The ``"contiguous"`` partition matches ``torch.chunk`` along the
 latitude axis (the DTensor ``Shard`` layout) and uses the plain sums.
 
-On CUDA with a symmetric-memory reducer the partial sums are reduced by the
-NVLink peer-memory kernel of :mod:`tornado_gcm_b200.parallel.fused_allreduce`
-(``scale=1``); otherwise by ``torch.distributed.all_reduce``.
+Execution paths for ``to_modal`` with several ranks:
+
+* ``fused`` (CUDA, :meth:`enable_fused`): the local transform runs on the
+  tcgen05 kernels and the Legendre GEMM's epilogue adds every output value
+  straight into all ranks' symmetric output buffers with system-scope
+  reductions over NVLink — the cross-GPU sum is fused into the GEMM — followed
+  by one peer barrier kernel.  Two output buffers alternate, so a single
+  barrier per call orders both the reductions and the re-zeroing.
+* ``reducer``: local partial sums, then the peer-memory all-reduce kernel of
+  :mod:`tornado_gcm_b200.parallel.fused_allreduce` (``scale=1``);
+* otherwise ``torch.distributed.all_reduce`` (the NCCL baseline).
+
+The fused path is forward-only (inference, benchmarks); autograd goes through
+the other two.
 """
 
 from __future__ import annotations
@@ -117,6 +128,7 @@ class LatitudeShardedSHT:
             self._p = p[:, self.lat_index, :]
         self._cache: dict = {}
         self.reducer = reducer
+        self.fused = False
 
     # ── constants on the device ──
     def _t(self, name: str, device, dtype):
@@ -184,6 +196,8 @@ class LatitudeShardedSHT:
 
     def to_modal(self, nodal_local: torch.Tensor) -> torch.Tensor:
         """``(…, I, J_local)`` on every rank → replicated ``(…, 2M-1, L)``."""
+        if self.fused and nodal_local.is_cuda and self.world > 1 and not torch.is_grad_enabled():
+            return self.to_modal_fused(nodal_local)
         part = self.partial_to_modal(nodal_local)
         if self.world > 1:
             part = self._all_reduce_sum(part)
@@ -229,3 +243,92 @@ class LatitudeShardedSHT:
         M2, L = self.modal_shape
         rows = self.local_latitudes / 2 if self._mirrored else self.local_latitudes
         return int(2 * fields * M2 * rows * (math.ceil(L / 2) * 2 if self._mirrored else L))
+
+    # ── fused GPU path ──
+    def enable_fused(self, max_fields: int, device) -> None:
+        """Allocate the symmetric output buffers and the barrier pad (collective call)."""
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from tornado_gcm_b200.ops import _ext
+        from tornado_gcm_b200.ops import sht as sht_ops
+
+        _ext.require("fused sharded transform")
+        device = torch.device(device)
+        sh = self.grid.spherical_harmonics
+        M2, L = self.modal_shape
+        if self.local_latitudes % 4:
+            raise ValueError("the fused path needs a multiple of 4 latitude rows per rank")
+        self._numel = int(max_fields) * M2 * L
+        group = self.group or dist.group.WORLD
+        gname = group.group_name
+        self._bufs, self._peer_tabs = [], []
+        for _ in range(2):
+            b = symm_mem.empty(self._numel, dtype=torch.float32, device=device)
+            b.zero_()
+            h = symm_mem.rendezvous(b, gname)
+            self._bufs.append((b, h))
+            self._peer_tabs.append(torch.tensor([int(x) for x in h.buffer_ptrs], dtype=torch.int64))
+        pad = symm_mem.empty(2 * 8, dtype=torch.int32, device=device)
+        pad.zero_()
+        hp = symm_mem.rendezvous(pad, gname)
+        self._pad = (pad, hp)
+        self._pad_tab = torch.tensor([int(x) for x in hp.buffer_ptrs], dtype=torch.int64)
+        self._call = 0
+        # bases restricted to this rank's latitude rows
+        full = sht_ops.bases(sh, device)
+        idx = torch.as_tensor(self.lat_index, device=device)
+        self._lb = _LocalBases(full, idx)
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group)
+        self.fused = True
+
+    def to_modal_fused(self, nodal_local: torch.Tensor) -> torch.Tensor:
+        """``(…, I, J_local)`` → replicated ``(…, 2M-1, L)`` with the cross-GPU sum in the GEMM epilogue."""
+        from tornado_gcm_b200.ops import _ext
+
+        ops = _ext.require("fused sharded transform")
+        lead = nodal_local.shape[:-2]
+        n3 = nodal_local.reshape((-1,) + tuple(nodal_local.shape[-2:])).float()
+        S = n3.shape[0]
+        M2, L = self.modal_shape
+        if S * M2 * L > self._numel:
+            raise ValueError(f"{S} fields exceed the {self._numel // (M2 * L)} reserved by enable_fused")
+        k = self._call % 2
+        self._call += 1
+        buf = self._bufs[k][0]
+        lb = self._lb
+        ws = _ext.empty(S * lb.M2 * lb.J, dtype=torch.float32, device=n3.device)
+        flag = _ext.error_flag(n3.device)
+        ops.sht_anal(n3, lb.Ft, lb.Ptw, L, ws, None, flag, False, self._peer_tabs[k])
+        ops.peer_barrier(self._pad_tab, self.rank, flag, n3.device.index)
+        view = buf[: S * M2 * L].view(S, M2, L)
+        out = view.clone()
+        view.zero_()
+        return out.reshape(lead + (M2, L)).to(nodal_local.dtype)
+
+    def to_nodal_gpu(self, x: torch.Tensor) -> torch.Tensor:
+        """Synthesis on this rank's rows with the tcgen05 kernels (no communication)."""
+        from tornado_gcm_b200.ops import _ext
+
+        ops = _ext.require("sharded synthesis")
+        lead = x.shape[:-2]
+        x3 = x.reshape((-1,) + tuple(x.shape[-2:])).float().contiguous()
+        lb = self._lb
+        if lb.Lp != lb.L:
+            x3 = torch.nn.functional.pad(x3, (0, lb.Lp - lb.L))[..., : lb.L]
+        ws = _ext.empty(x3.shape[0] * lb.J * lb.M2p, dtype=torch.float32, device=x3.device)
+        out = ops.sht_synth(x3, lb.L, lb.P, lb.F, ws, None, _ext.error_flag(x3.device), False)
+        return out.reshape(lead + tuple(out.shape[-2:])).to(x.dtype)
+
+
+class _LocalBases:
+    """The device bases of a grid restricted to a subset of latitude rows."""
+
+    def __init__(self, full, lat_idx: torch.Tensor):
+        self.L, self.Lp, self.I, self.M2, self.M2p = full.L, full.Lp, full.I, full.M2, full.M2p
+        self.J = int(lat_idx.numel())
+        self.P = full.P[:, lat_idx, :].contiguous()
+        self.Pt = full.Pt[:, :, lat_idx].contiguous()
+        self.Ptw = full.Ptw[:, :, lat_idx].contiguous()
+        self.F, self.Ft = full.F, full.Ft
+
