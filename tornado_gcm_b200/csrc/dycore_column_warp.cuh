@@ -156,21 +156,43 @@ __device__ __forceinline__ float pick(const float (&a)[kMaxTracers], int idx) {
   return r;
 }
 
+// Per-block copies of the level constants and of the fused geopotential
+// matrix.  The kernel parameters hold them, but a lane-dependent index into
+// parameter space is serialised by the constant cache, and a row of G read
+// across lanes is a 32-line strided global access; both are staged once per
+// block instead (rows padded to 33 floats: conflict-free row and column reads).
+struct ColShared {
+  float dsig[32], alpha[32], tref[32], idc[32], cs[32];
+  float g[32][33];
+};
+
+__device__ __forceinline__ void col_shared_fill(ColShared& sh, const ColumnConsts& c) {
+  const int t = threadIdx.x, n = c.n;
+  if (t < n) {
+    sh.dsig[t] = c.dsig[t];
+    sh.alpha[t] = c.alpha[t];
+    sh.tref[t] = c.tref[t];
+    sh.idc[t] = c.idc[t];
+    sh.cs[t] = c.cs[t];
+  }
+  if (c.gmat != nullptr)
+    for (int i = t; i < n * n; i += blockDim.x) sh.g[i / n][i % n] = __ldg(c.gmat + i);
+}
+
 // per-level constants of lane k (zeros beyond n)
 struct LevelConsts {
   float dsig, alpha, alpha_m, tref, tref_p, tref_m, idc, idc_m, cs;
-  __device__ void load(const ColumnConsts& c, int k) {
-    const int n = c.n;
+  __device__ void load(const ColShared& sh, int n, int k) {
     const bool in = k < n;
-    dsig = in ? c.dsig[k] : 1.f;
-    alpha = in ? c.alpha[k] : 0.f;
-    alpha_m = (in && k > 0) ? c.alpha[k - 1] : 0.f;
-    tref = in ? c.tref[k] : 0.f;
-    tref_p = (k + 1 < n) ? c.tref[k + 1] : 0.f;
-    tref_m = (in && k > 0) ? c.tref[k - 1] : 0.f;
-    idc = (k + 1 < n) ? c.idc[k] : 0.f;
-    idc_m = (in && k > 0) ? c.idc[k - 1] : 0.f;
-    cs = (k + 1 < n) ? c.cs[k] : 0.f;
+    dsig = in ? sh.dsig[k] : 1.f;
+    alpha = in ? sh.alpha[k] : 0.f;
+    alpha_m = (in && k > 0) ? sh.alpha[k - 1] : 0.f;
+    tref = in ? sh.tref[k] : 0.f;
+    tref_p = (k + 1 < n) ? sh.tref[k + 1] : 0.f;
+    tref_m = (in && k > 0) ? sh.tref[k - 1] : 0.f;
+    idc = (k + 1 < n) ? sh.idc[k] : 0.f;
+    idc_m = (in && k > 0) ? sh.idc[k - 1] : 0.f;
+    cs = (k + 1 < n) ? sh.cs[k] : 0.f;
   }
 };
 
@@ -180,6 +202,8 @@ __global__ void __launch_bounds__(32 * kColWarps) column_fwd_warp_kernel(
     ColumnConsts c, SliceIndex ix, const float* __restrict__ in, float* __restrict__ out,
     const float* __restrict__ sec2, const float* __restrict__ cor, int B, int I, int J, int lat_major) {
   extern __shared__ float smem_cols[];
+  __shared__ ColShared csh;
+  col_shared_fill(csh, c);
   const long long plane = static_cast<long long>(I) * J, total = static_cast<long long>(B) * plane;
   ColBlock cb;
   cb.init(smem_cols);
@@ -192,9 +216,9 @@ __global__ void __launch_bounds__(32 * kColWarps) column_fwd_warp_kernel(
   const float lap = c.hum_terms ? cb.scalar(in, false, ix.lap) : 0.f;
   const float s2 = cb.valid_w ? sec2[j_w] : 0.f, fcor = cb.valid_w ? cor[j_w] : 0.f;
   const bool lv = k < n;
-  LevelConsts L;
-  L.load(c, k);
   __syncthreads();
+  LevelConsts L;
+  L.load(csh, n, k);
   const float vort = cb.get(0), dv = cb.get(1), T = cb.get(2), u = cb.get(3), v = cb.get(4);
   float trv[kMaxTracers];
 #pragma unroll
@@ -257,7 +281,7 @@ __global__ void __launch_bounds__(32 * kColWarps) column_fwd_warp_kernel(
       float acc = 0.f;
       for (int jj = 0; jj < n; ++jj) {
         const float tj = __shfl_sync(kFull, tdk, jj);
-        if (lv) acc = fmaf(c.gmat[k * n + jj], tj, acc);
+        if (lv) acc = fmaf(csh.g[k][jj], tj, acc);
       }
       o_td = acc;
     }
@@ -296,6 +320,8 @@ __global__ void __launch_bounds__(32 * kColWarps) column_vjp_warp_kernel(
     float* __restrict__ gin, const float* __restrict__ sec2, const float* __restrict__ cor, int B, int I, int J,
     int lat_major) {
   extern __shared__ float smem_cols[];
+  __shared__ ColShared csh;
+  col_shared_fill(csh, c);
   const long long plane = static_cast<long long>(I) * J, total = static_cast<long long>(B) * plane;
   ColBlock cb;
   cb.init(smem_cols);
@@ -311,9 +337,9 @@ __global__ void __launch_bounds__(32 * kColWarps) column_vjp_warp_kernel(
   const float s2 = cb.valid_w ? sec2[j_w] : 0.f, fcor = cb.valid_w ? cor[j_w] : 0.f;
   const bool lv = k < n;
   const bool last = k >= n - 1;
-  LevelConsts L;
-  L.load(c, k);
   __syncthreads();
+  LevelConsts L;
+  L.load(csh, n, k);
   const float vort = cb.get(0), dv = cb.get(1), T = cb.get(2), u = cb.get(3), v = cb.get(4);
   float trv[kMaxTracers];
 #pragma unroll
@@ -447,7 +473,7 @@ __global__ void __launch_bounds__(32 * kColWarps) column_vjp_warp_kernel(
       float acc = 0.f;
       for (int jj = 0; jj < n; ++jj) {
         const float gj = __shfl_sync(kFull, Gtd_raw, jj);
-        if (lv) acc = fmaf(c.gmat[jj * n + k], gj, acc);
+        if (lv) acc = fmaf(csh.g[jj][k], gj, acc);
       }
       Gtd = acc;
     }

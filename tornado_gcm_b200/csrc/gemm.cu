@@ -132,6 +132,29 @@ static void launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmP
   if (e != cudaSuccess) throw std::runtime_error(std::string("tgcm gemm launch: ") + cudaGetErrorString(e));
 }
 
+// Gathered-B launch (fused weight all-gather): BF16, K-major A and B, BN in {64, 128}.
+template <int BN>
+static void launch_gather(const CUtensorMap& ta, const BMapSet& bm, const GemmParams& p, cudaStream_t stream) {
+  constexpr int ST = StagesFor<BN>::value;
+  using S = GemmSmem<1, BN, ST>;
+  auto kern = gemm_sm100_gather_kernel<1, BN, ST>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64 || !attr_set[dev]) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
+    if (dev < 64) attr_set[dev] = true;
+  }
+  int n_sm = 148;
+  cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+  const int tiles = gemm_total_tiles(p);
+  if (tiles == 0) return;
+  dim3 grid(tiles < n_sm ? tiles : n_sm);
+  kern<<<grid, kGemmThreads, S::kTotal, stream>>>(ta, bm, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string("tgcm gather gemm launch: ") + cudaGetErrorString(e));
+}
+
 // Runtime dispatch over the instantiated configurations.
 static void gemm_dispatch(int fmt, int bn, bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
                           const GemmParams& p, cudaStream_t st) {
@@ -331,6 +354,50 @@ void linear_fwd(const at::Tensor& X, const at::Tensor& W, const c10::optional<at
   gemm_dispatch(1, bn, false, false, ta, tb, p, at::cuda::getCurrentCUDAStream());
 }
 
+// Fused all-gather + linear: out (T, O) = act(X . W^T + bias) where the
+// weight W (O, Kp) is row-sharded over the ranks: shard r holds rows
+// [r * rows, (r + 1) * rows) in symmetric memory and w_ptrs lists the
+// shards' addresses (int64, CPU).  The producer warp reads every B tile
+// straight from its owner's shard with plain TMA loads over NVLink, so the
+// gathered weight is never materialised.  rows must be a multiple of 16.
+void linear_fwd_gathered(const at::Tensor& X, const at::Tensor& w_ptrs, int64_t rows, int64_t O,
+                         const c10::optional<at::Tensor>& bias, int64_t act, at::Tensor& out,
+                         const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& err) {
+  TORCH_CHECK(X.scalar_type() == at::kBFloat16 && X.is_contiguous() && out.is_contiguous(), "bf16 X expected");
+  TORCH_CHECK(!w_ptrs.is_cuda() && w_ptrs.scalar_type() == at::kLong && w_ptrs.numel() >= 1 && w_ptrs.numel() <= 8,
+              "w_ptrs must hold 1..8 int64 addresses on the CPU");
+  TORCH_CHECK(rows > 0 && rows % 16 == 0, "shard rows must be a positive multiple of 16");
+  const int64_t nmaps = w_ptrs.numel();
+  TORCH_CHECK(O <= rows * nmaps && O > rows * (nmaps - 1), "O inconsistent with the shard layout");
+  c10::cuda::CUDAGuard guard(X.device());
+  const int64_t T = X.size(0), Kp = X.size(1);
+  TORCH_CHECK(Kp % 8 == 0, "feature dim must be padded to a multiple of 8");
+  TORCH_CHECK(out.size(0) == T && out.size(1) == O, "out shape mismatch");
+  const int bn = O <= 64 ? 64 : 128;
+  CUtensorMap ta = make_tmap(X.data_ptr(), 1, Kp, T, 1, Kp * 2, T * Kp * 2, 64, 128, 1);
+  BMapSet bm;
+  memset(&bm, 0, sizeof(bm));
+  for (int64_t i = 0; i < nmaps; ++i) {
+    const void* ptr = reinterpret_cast<const void*>(w_ptrs.data_ptr<int64_t>()[i]);
+    bm.m[i] = make_tmap(ptr, 1, Kp, rows, 1, Kp * 2, rows * Kp * 2, 64, 16, 1);
+  }
+  GemmParams p = default_params();
+  p.M = T; p.N = O; p.K = Kp; p.groups = 1;
+  p.tiles_m = cdiv(T, 128); p.tiles_n = cdiv(O, bn);
+  p.C = out.data_ptr(); p.c_sr = O; p.c_sc = 1; p.c_sg = 0;
+  p.out_bf16 = out.scalar_type() == at::kBFloat16 ? 1 : 0;
+  if (bias.has_value() && bias->defined()) p.bias = bias->data_ptr<float>();
+  p.act = static_cast<int>(act);
+  if (aux.has_value() && aux->defined()) p.aux = reinterpret_cast<__nv_bfloat16*>(aux->data_ptr());
+  p.err = err_ptr(err);
+  p.n_bmaps = static_cast<int>(nmaps);
+  p.b_rows_per_map = static_cast<int>(rows);
+  if (bn == 64)
+    launch_gather<64>(ta, bm, p, at::cuda::getCurrentCUDAStream());
+  else
+    launch_gather<128>(ta, bm, p, at::cuda::getCurrentCUDAStream());
+}
+
 // dX (T, Kp) = dY (T, O) . W (O, Kp), optionally times act'(pre) of the layer input.
 void linear_dgrad(const at::Tensor& dY, const at::Tensor& W, at::Tensor& dX,
                   const c10::optional<at::Tensor>& pre, int64_t pre_act, const c10::optional<at::Tensor>& err) {
@@ -431,6 +498,8 @@ TORCH_LIBRARY_FRAGMENT(tgcm, m) {
   m.def("sht_anal(Tensor N, Tensor Ft, Tensor Pt, int Lo, Tensor ws, Tensor? col_scale, Tensor? err, bool lat_major, "
         "Tensor? peer_ptrs=None) -> Tensor");
   m.def("linear_fwd(Tensor X, Tensor W, Tensor? bias, int act, Tensor(a!) out, Tensor? aux, Tensor? err) -> ()");
+  m.def("linear_fwd_gathered(Tensor X, Tensor w_ptrs, int rows, int O, Tensor? bias, int act, Tensor(a!) out, "
+        "Tensor? aux, Tensor? err) -> ()");
   m.def("linear_dgrad(Tensor dY, Tensor W, Tensor(a!) dX, Tensor? pre, int pre_act, Tensor? err) -> ()");
   m.def("linear_wgrad(Tensor dY, Tensor X, Tensor(a!) dW, int splits, Tensor? err) -> ()");
 }
@@ -439,6 +508,7 @@ TORCH_LIBRARY_IMPL(tgcm, CUDA, m) {
   m.impl("sht_synth", &tgcm::sht_synth);
   m.impl("sht_anal", &tgcm::sht_anal);
   m.impl("linear_fwd", &tgcm::linear_fwd);
+  m.impl("linear_fwd_gathered", &tgcm::linear_fwd_gathered);
   m.impl("linear_dgrad", &tgcm::linear_dgrad);
   m.impl("linear_wgrad", &tgcm::linear_wgrad);
   m.impl("bgemm_tf32", &tgcm::bgemm_tf32);

@@ -52,6 +52,12 @@ struct GemmParams {
   // being stored to C.  Plain red.add over NVLink, no TMA, no multicast.
   int n_peers;
   float* peer_C[8];
+  // Gathered B (fused all-gather): when n_bmaps > 0 the B rows are spread over
+  // n_bmaps tensor maps of b_rows_per_map rows each (the ranks' weight shards,
+  // read in place from peer memory with plain, non-multicast TMA loads); a
+  // B tile is fetched as BN/16 boxes of 16 rows, each from the map owning it.
+  int n_bmaps;
+  int b_rows_per_map;
   // optional per-CTA cycle counters (diagnostics): [cta][0..7] =
   // producer wait, producer issue, mma wait-empty-acc, mma wait-full, mma issue,
   // epilogue wait, epilogue work, tiles
@@ -305,10 +311,14 @@ __device__ __forceinline__ void epilogue_rowmajor_dispatch(const GemmParams& p, 
 // Barriers: full/empty per ring stage (phase from a CTA-wide k-block
 // counter), tmem_full/tmem_empty per accumulator buffer (phase from the
 // CTA's count of non-empty tiles).
+struct BMapSet {
+  CUtensorMap m[8];
+};
+
 template <int FMT, int BN, int STAGES, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                      const GemmParams p) {
+__device__ __forceinline__ void gemm_sm100_body(const CUtensorMap& tmap_a, const CUtensorMap* tmaps_b,
+                                                const GemmParams& p) {
+  const CUtensorMap& tmap_b = tmaps_b[0];
   using T = FmtTraits<FMT>;
   using S = GemmSmem<FMT, BN, STAGES>;
   constexpr int BK = T::kBK;
@@ -392,7 +402,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             for (int q = 0; q < 128 / CH; ++q)
               tma_load_3d(sa + q * BK * 128, &tmap_a, &full_bar[s], tc.tm * 128 + q * CH, k0, a_batch);
           }
-          if (!B_MN) {
+          if (p.n_bmaps > 0) {
+#pragma unroll
+            for (int q = 0; q < BN / 16; ++q) {
+              const int row = tc.tn * BN + q * 16;
+              int owner = row / p.b_rows_per_map;
+              if (owner >= p.n_bmaps) owner = p.n_bmaps - 1;  // tail rows: out of bounds, zero fill
+              tma_load_3d(sb + q * 16 * 128, &tmaps_b[owner], &full_bar[s], k0, row - owner * p.b_rows_per_map,
+                          b_batch);
+            }
+          } else if (!B_MN) {
             tma_load_3d(sb, &tmap_b, &full_bar[s], k0, tc.tn * BN, b_batch);
           } else {
 #pragma unroll
@@ -616,6 +635,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
+}
+
+template <int FMT, int BN, int STAGES, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                      const GemmParams p) {
+  gemm_sm100_body<FMT, BN, STAGES, A_MN, B_MN>(tmap_a, &tmap_b, p);
+}
+
+// B gathered from up to 8 tensor maps (peer weight shards), K-major B only.
+template <int FMT, int BN, int STAGES>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_sm100_gather_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ BMapSet bmaps,
+                             const GemmParams p) {
+  gemm_sm100_body<FMT, BN, STAGES, false, false>(tmap_a, bmaps.m, p);
 }
 
 }  // namespace tgcm
