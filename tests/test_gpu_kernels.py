@@ -346,3 +346,14 @@ def test_latitude_sharded_sht_on_device():
             assert _rel(s.to_nodal(x), s.scatter(nodal)) < 1e-12
             total = total + s.partial_to_modal(s.scatter(nodal))
         assert _rel(total, g.to_modal(nodal.cpu()).to(DEV)) < 1e-12
+
+
+@pytest.mark.parametrize("T,ld,n", [(32768, 384, 384), (1000, 200, 193), (7, 16, 9)])
+def test_colsum_bf16_vs_fp64(T, ld, n):
+    _require()
+    ops = _ext.require("colsum")
+    torch.manual_seed(T)
+    x = torch.randn(T, ld).to(torch.bfloat16)
+    out = ops.colsum_bf16(x.to(DEV), n).cpu()
+    ref = x[:, :n].double().sum(0)
+    assert _rel(out, ref) < 1e-5

@@ -162,3 +162,58 @@ def test_fused_sharded_transform_two_gpus():
         assert isinstance(res, dict), res
         assert res["nodal"] < 2e-3 and res["modal"] < 2e-3     # TF32 transforms
         assert res["flag"] == 0
+
+
+def _worker_gathered_linear(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=torch.device("cuda", rank))
+        from tornado_gcm_b200.ops import _ext
+        from tornado_gcm_b200.parallel.fsdp_gather import GatheredLinear
+
+        dev = torch.device("cuda", rank)
+        res = {}
+        for O, K, T in ((384, 384, 4096), (193, 197, 1000)):
+            torch.manual_seed(O)
+            w = torch.randn(O, K) / K ** 0.5
+            b = torch.randn(O) * 0.1
+            x = torch.randn(T, K)
+            lin = GatheredLinear(w.to(dev), b.to(dev), "gelu_tanh")
+            out = lin(x.to(dev), out_dtype=torch.float32).cpu()
+            xb, wb = x.to(torch.bfloat16).float(), w.to(torch.bfloat16).float()
+            ref = torch.nn.functional.gelu(xb @ wb.T + b, approximate="tanh")
+            res[f"rel_{O}"] = float((out - ref).norm() / ref.norm())
+            base = lin.baseline_forward(x.to(dev), out_dtype=torch.float32).cpu()
+            res[f"base_{O}"] = float((out - base).abs().max())
+        torch.cuda.synchronize(dev)
+        res["flag"] = _ext.check_error_flag(dev)
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, res))
+    except Exception:  # pragma: no cover
+        q.put((rank, traceback.format_exc()))
+
+
+def test_gathered_linear_two_gpus():
+    """Weight rows on two GPUs, read in place by the GEMM's TMA producer."""
+    import torch.multiprocessing as mp
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker_gathered_linear, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+    for rank, res in out:
+        assert isinstance(res, dict), res
+        assert res["rel_384"] < 1e-2 and res["rel_193"] < 1e-2
+        assert res["base_384"] < 1e-3 and res["base_193"] < 1e-3
+        assert res["flag"] == 0

@@ -135,7 +135,7 @@ static void launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmP
 // Gathered-B launch (fused weight all-gather): BF16, K-major A and B, BN in {64, 128}.
 template <int BN>
 static void launch_gather(const CUtensorMap& ta, const BMapSet& bm, const GemmParams& p, cudaStream_t stream) {
-  constexpr int ST = StagesFor<BN>::value;
+  constexpr int ST = 3;  // leaves room for a resident 64-row B block up to K = 768
   using S = GemmSmem<1, BN, ST>;
   auto kern = gemm_sm100_gather_kernel<1, BN, ST>;
   static bool attr_set[64] = {false};
@@ -149,8 +149,25 @@ static void launch_gather(const CUtensorMap& ta, const BMapSet& bm, const GemmPa
   cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
   const int tiles = gemm_total_tiles(p);
   if (tiles == 0) return;
+  GemmParams q = p;
+  size_t smem = S::kTotal;
   dim3 grid(tiles < n_sm ? tiles : n_sm);
-  kern<<<grid, kGemmThreads, S::kTotal, stream>>>(ta, bm, p);
+  // resident B when the whole (BN x K) block fits next to the ring: every CTA keeps one column block
+  const int nkb = (p.K + 63) / 64;
+  const size_t res_bytes = static_cast<size_t>(nkb) * BN * 128;
+  const size_t res_off = (static_cast<size_t>(S::kTotal) + 1023) / 1024 * 1024;
+  if (res_off + res_bytes <= 227 * 1024 && p.tiles_n <= n_sm) {
+    q.b_res_kb = nkb;
+    q.b_res_off = static_cast<int>(res_off - 1024);  // offsets are taken from the 1024-aligned base
+    smem = res_off + res_bytes;
+    const int per = n_sm / p.tiles_n;
+    grid.x = static_cast<unsigned>(per * p.tiles_n);
+    if (static_cast<int>(grid.x) > tiles) grid.x = static_cast<unsigned>(tiles);
+    grid.x = grid.x / p.tiles_n * p.tiles_n;
+    if (grid.x == 0) grid.x = static_cast<unsigned>(p.tiles_n);
+  }
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  kern<<<grid, kGemmThreads, smem, stream>>>(ta, bm, q);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("tgcm gather gemm launch: ") + cudaGetErrorString(e));
 }
@@ -373,7 +390,7 @@ void linear_fwd_gathered(const at::Tensor& X, const at::Tensor& w_ptrs, int64_t 
   const int64_t T = X.size(0), Kp = X.size(1);
   TORCH_CHECK(Kp % 8 == 0, "feature dim must be padded to a multiple of 8");
   TORCH_CHECK(out.size(0) == T && out.size(1) == O, "out shape mismatch");
-  const int bn = O <= 64 ? 64 : 128;
+  const int bn = 64;  // resident B blocks of 64 rows
   CUtensorMap ta = make_tmap(X.data_ptr(), 1, Kp, T, 1, Kp * 2, T * Kp * 2, 64, 128, 1);
   BMapSet bm;
   memset(&bm, 0, sizeof(bm));
@@ -392,10 +409,7 @@ void linear_fwd_gathered(const at::Tensor& X, const at::Tensor& w_ptrs, int64_t 
   p.err = err_ptr(err);
   p.n_bmaps = static_cast<int>(nmaps);
   p.b_rows_per_map = static_cast<int>(rows);
-  if (bn == 64)
-    launch_gather<64>(ta, bm, p, at::cuda::getCurrentCUDAStream());
-  else
-    launch_gather<128>(ta, bm, p, at::cuda::getCurrentCUDAStream());
+  launch_gather<64>(ta, bm, p, at::cuda::getCurrentCUDAStream());
 }
 
 // dX (T, Kp) = dY (T, O) . W (O, Kp), optionally times act'(pre) of the layer input.

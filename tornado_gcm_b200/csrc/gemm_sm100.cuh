@@ -58,6 +58,13 @@ struct GemmParams {
   // B tile is fetched as BN/16 boxes of 16 rows, each from the map owning it.
   int n_bmaps;
   int b_rows_per_map;
+  // Resident B (gathered mode only): every CTA owns one column block tn
+  // (gridDim.x is a multiple of tiles_n) and loads its whole B block
+  // (b_res_kb k-blocks) once into shared memory at byte offset b_res_off of
+  // the aligned dynamic smem; the ring then carries A only.  Each remote
+  // weight row then crosses NVLink once per CTA instead of once per tile.
+  int b_res_kb;
+  int b_res_off;
   // optional per-CTA cycle counters (diagnostics): [cta][0..7] =
   // producer wait, producer issue, mma wait-empty-acc, mma wait-full, mma issue,
   // epilogue wait, epilogue work, tiles
@@ -214,12 +221,53 @@ __device__ __forceinline__ void chunk_store_f32(const uint8_t* stage, float* g, 
   }
 }
 
+// act(x) / act'(pre) on a 32-value chunk; the switch is warp-uniform and sits
+// outside the element loops, so one epilogue instance serves every activation
+// (six inlined instances of the whole epilogue made the kernel spill).
+__device__ __forceinline__ void act_chunk(int act, float (&x)[32]) {
+  switch (act) {
+#define TGCM_ACT_CASE(A)                                    \
+  case A:                                                  \
+    _Pragma("unroll") for (int j = 0; j < 32; ++j) x[j] = act_fast<A>(x[j]); \
+    break;
+    TGCM_ACT_CASE(kActRelu)
+    TGCM_ACT_CASE(kActGelu)
+    TGCM_ACT_CASE(kActGeluTanh)
+    TGCM_ACT_CASE(kActSilu)
+    TGCM_ACT_CASE(kActTanh)
+#undef TGCM_ACT_CASE
+    default: break;
+  }
+}
+
+// x[j] *= act'(pre[j]) with the bf16 pre-activations of the chunk at `pre`.
+__device__ __forceinline__ void act_grad_chunk(int act, float (&x)[32], const uint8_t* pre) {
+  switch (act) {
+#define TGCM_ACTG_CASE(A)                                                                        \
+  case A:                                                                                        \
+    _Pragma("unroll") for (int j = 0; j < 32; j += 2) {                                          \
+      const float2 pr = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(pre + 2 * j)); \
+      x[j] *= act_grad_fast<A>(pr.x);                                                           \
+      x[j + 1] *= act_grad_fast<A>(pr.y);                                                       \
+    }                                                                                            \
+    break;
+    TGCM_ACTG_CASE(kActRelu)
+    TGCM_ACTG_CASE(kActGelu)
+    TGCM_ACTG_CASE(kActGeluTanh)
+    TGCM_ACTG_CASE(kActSilu)
+    TGCM_ACTG_CASE(kActTanh)
+#undef TGCM_ACTG_CASE
+    default: break;
+  }
+}
+
 // Epilogue of one 32-row x BN tile slice for row-major C with 16-byte aligned
 // rows.  ACT is the forward activation (or, with grad_pre, the activation
 // whose derivative multiplies the result).
-template <int ACT, int BN>
-__device__ __forceinline__ void epilogue_rowmajor_vec(const GemmParams& p, uint32_t taddr_row, uint8_t* stage,
-                                                      int tm, int tn, int g, int q, int half, int lane) {
+template <int BN>
+__device__ __forceinline__ void epilogue_rowmajor_vec(const GemmParams& p, int ACT, uint32_t taddr_row,
+                                                      uint8_t* stage, int tm, int tn, int g, int q, int half,
+                                                      int lane) {
   const int row0 = tm * 128 + q * 32;
   const int nrows = p.M - row0 < 32 ? p.M - row0 : 32;
 #pragma unroll 1
@@ -259,16 +307,10 @@ __device__ __forceinline__ void epilogue_rowmajor_vec(const GemmParams& p, uint3
     if (p.grad_pre) {  // x *= act'(pre)
       chunk_copy_bf16(stage, const_cast<__nv_bfloat16*>(p.grad_pre) + base, p.c_sr, nrows, ncols, lane, 1);
       __syncwarp();
-#pragma unroll
-      for (int j = 0; j < 32; j += 2) {
-        const float2 pr = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(my + 2 * j));
-        x[j] *= act_grad_fast<ACT>(pr.x);
-        x[j + 1] *= act_grad_fast<ACT>(pr.y);
-      }
+      act_grad_chunk(ACT, x, my);
       __syncwarp();
     } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) x[j] = act_fast<ACT>(x[j]);
+      act_chunk(ACT, x);
     }
     if (p.out_bf16) {
 #pragma unroll
@@ -292,14 +334,7 @@ template <int BN>
 __device__ __forceinline__ void epilogue_rowmajor_dispatch(const GemmParams& p, int act, uint32_t taddr_row,
                                                            uint8_t* stage, int tm, int tn, int g, int q, int half,
                                                            int lane) {
-  switch (act) {
-    case kActRelu: epilogue_rowmajor_vec<kActRelu, BN>(p, taddr_row, stage, tm, tn, g, q, half, lane); break;
-    case kActGelu: epilogue_rowmajor_vec<kActGelu, BN>(p, taddr_row, stage, tm, tn, g, q, half, lane); break;
-    case kActGeluTanh: epilogue_rowmajor_vec<kActGeluTanh, BN>(p, taddr_row, stage, tm, tn, g, q, half, lane); break;
-    case kActSilu: epilogue_rowmajor_vec<kActSilu, BN>(p, taddr_row, stage, tm, tn, g, q, half, lane); break;
-    case kActTanh: epilogue_rowmajor_vec<kActTanh, BN>(p, taddr_row, stage, tm, tn, g, q, half, lane); break;
-    default: epilogue_rowmajor_vec<kActNone, BN>(p, taddr_row, stage, tm, tn, g, q, half, lane); break;
-  }
+  epilogue_rowmajor_vec<BN>(p, act, taddr_row, stage, tm, tn, g, q, half, lane);
 }
 
 // Persistent kernel: each CTA walks tiles t = blockIdx.x, +gridDim.x, ….
@@ -337,6 +372,9 @@ __device__ __forceinline__ void gemm_sm100_body(const CUtensorMap& tmap_a, const
   uint64_t* tmem_empty_bar = tmem_full_bar + 2;   // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* bres_bar = reinterpret_cast<uint64_t*>(bar_area + 512);  // resident-B arrival
+  uint8_t* bres = smem + p.b_res_off;
+  const bool b_resident = p.b_res_kb > 0;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -352,6 +390,7 @@ __device__ __forceinline__ void gemm_sm100_body(const CUtensorMap& tmap_a, const
       mbar_init(&tmem_empty_bar[b], kEpiWarps * 32);
     }
     *abort_flag = 0;
+    mbar_init(bres_bar, 1);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -371,6 +410,18 @@ __device__ __forceinline__ void gemm_sm100_body(const CUtensorMap& tmap_a, const
     if (lane == 0) {
       int kb_global = 0;
       unsigned long long t_wait = 0, t_issue = 0;
+      if (b_resident) {  // this CTA's B block, once: BN/16 boxes of 16 rows per k-block
+        const int tn = blockIdx.x % p.tiles_n;
+        mbar_arrive_expect_tx(bres_bar, static_cast<uint32_t>(p.b_res_kb) * BN * 128);
+        for (int kb = 0; kb < p.b_res_kb; ++kb)
+          for (int q = 0; q < BN / 16; ++q) {
+            const int row = tn * BN + q * 16;
+            int owner = row / p.b_rows_per_map;
+            if (owner >= p.n_bmaps) owner = p.n_bmaps - 1;
+            tma_load_3d(bres + (kb * BN + q * 16) * 128, &tmaps_b[owner], bres_bar, kb * BK,
+                        row - owner * p.b_rows_per_map, 0);
+          }
+      }
       for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x) {
         const TileCoord tc = tile_coord(p, t);
         int kb0, k_begin;
@@ -391,7 +442,7 @@ __device__ __forceinline__ void gemm_sm100_body(const CUtensorMap& tmap_a, const
           uint8_t* sa = smem + s * S::kStage;
           uint8_t* sb = sa + S::kA;
           const int k0 = k_begin + (kb0 + i) * BK;
-          mbar_arrive_expect_tx(&full_bar[s], S::kStage);
+          mbar_arrive_expect_tx(&full_bar[s], b_resident ? S::kA : S::kStage);
           if (!A_MN) {
             if (p.a_pair)
               tma_load_3d(sa, &tmap_a, &full_bar[s], k0, a_mr, tc.tm * 64);
@@ -402,7 +453,9 @@ __device__ __forceinline__ void gemm_sm100_body(const CUtensorMap& tmap_a, const
             for (int q = 0; q < 128 / CH; ++q)
               tma_load_3d(sa + q * BK * 128, &tmap_a, &full_bar[s], tc.tm * 128 + q * CH, k0, a_batch);
           }
-          if (p.n_bmaps > 0) {
+          if (b_resident) {
+            // B is resident
+          } else if (p.n_bmaps > 0) {
 #pragma unroll
             for (int q = 0; q < BN / 16; ++q) {
               const int row = tc.tn * BN + q * 16;
@@ -423,6 +476,7 @@ __device__ __forceinline__ void gemm_sm100_body(const CUtensorMap& tmap_a, const
       // drain: every load this thread issued has landed before the CTA exits
       for (int i = (kb_global > STAGES ? kb_global - STAGES : 0); i < kb_global; ++i)
         mbar_wait(&full_bar[i % STAGES], (i / STAGES) & 1, p.err, kErrTimeoutDrain);
+      if (b_resident) mbar_wait(bres_bar, 0, p.err, kErrTimeoutDrain);
       if (p.prof) {
         p.prof[blockIdx.x * 8 + 0] = t_wait;
         p.prof[blockIdx.x * 8 + 1] = t_issue;
@@ -432,6 +486,7 @@ __device__ __forceinline__ void gemm_sm100_body(const CUtensorMap& tmap_a, const
     if (lane == 0) {
       int kb_global = 0, tile_i = 0;
       unsigned long long t_acc = 0, t_full = 0;
+      if (b_resident && !mbar_wait(bres_bar, 0, p.err, kErrTimeoutFull)) *abort_flag = 1;
       for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x) {
         const TileCoord tc = tile_coord(p, t);
         int kb0, k_begin;
@@ -458,7 +513,7 @@ __device__ __forceinline__ void gemm_sm100_body(const CUtensorMap& tmap_a, const
           if (p.prof) t_full += clock64() - c0;
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + s * S::kStage);
-          const uint32_t sb = sa + S::kA;
+          const uint32_t sb = b_resident ? smem_u32(bres + (kb0 + i) * BN * 128) : sa + S::kA;
 #pragma unroll
           for (int k = 0; k < BK / T::kUK; ++k) {
             uint64_t adesc, bdesc;

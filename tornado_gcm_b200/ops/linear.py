@@ -123,7 +123,7 @@ class MlpFn(torch.autograd.Function):
             dw = torch.zeros(wp.shape, dtype=torch.float32, device=g.device)
             ops.linear_wgrad(dy, hs[i], dw, 0, err)
             O, K = lin.weight.shape
-            gb = dy[:, :O].float().sum(0) if lin.bias is not None else None
+            gb = ops.colsum_bf16(dy, O) if lin.bias is not None else None
             grads.append((dw[:O, :K].to(lin.weight.dtype), gb))
             if i > 0:
                 prev = zs[i - 1]

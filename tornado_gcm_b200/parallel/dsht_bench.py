@@ -84,7 +84,7 @@ def run(grids, fields, iters: int, warmup: int) -> list:
                         sht.to_modal_fused(sht.to_nodal_gpu(modal))
 
                 def nccl():
-                    part = sht.partial_to_modal(sht.to_nodal_gpu(modal))
+                    part = sht.partial_to_modal(sht.to_nodal_gpu(modal)).contiguous()
                     dist.all_reduce(part)
 
                 res["fused_ms"] = _time(fused, iters, warmup)
@@ -94,7 +94,7 @@ def run(grids, fields, iters: int, warmup: int) -> list:
                 m64 = modal.double()
 
                 def fp64():
-                    part = s64.partial_to_modal(s64.to_nodal(m64))
+                    part = s64.partial_to_modal(s64.to_nodal(m64)).contiguous()
                     dist.all_reduce(part)
 
                 if F <= 32:

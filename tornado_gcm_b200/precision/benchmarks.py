@@ -336,6 +336,56 @@ def _bgemm_case(args):
     return (lambda: ops.bgemm_tf32(A, B, C, 1.0, err)), 2.0 * args.groups * args.m * args.n * args.k
 
 
+def _single_rank_group() -> None:
+    """A one-rank NCCL group so the peer-memory paths run on one GPU (kernel captures)."""
+    import datetime
+    import os
+
+    import torch.distributed as dist
+
+    if not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29533")
+        dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=60),
+                                device_id=torch.device("cuda", torch.cuda.current_device()))
+
+
+def _fused_sht_case(args):
+    """Latitude-sharded analysis with the cross-GPU sum in the Legendre GEMM epilogue (one rank:
+    the same kernels, the peer list holds this GPU's own buffer)."""
+    from tornado_gcm_b200.core import spherical_harmonic as sh
+    from tornado_gcm_b200.parallel.sharded_sht import LatitudeShardedSHT
+
+    _single_rank_group()
+    g = getattr(sh.Grid, args.grid)(precision="tf32")
+    M2, L = g.modal_shape
+    I, J = g.nodal_shape
+    sht = LatitudeShardedSHT(g, scheme="mirrored")
+    sht.enable_fused(args.slices, torch.device("cuda"))
+    nodal = torch.randn(args.slices, I, J, device="cuda")
+
+    def step():
+        with torch.no_grad():
+            sht.to_modal_fused(nodal)
+
+    return step, 2.0 * args.slices * (M2 * I * J + M2 * J * L)
+
+
+def _gathered_linear_case(args):
+    """Linear layer whose weight is read from the ranks' shards by the GEMM producer (one rank)."""
+    from tornado_gcm_b200.parallel.fsdp_gather import GatheredLinear
+
+    _single_rank_group()
+    w = torch.randn(args.width, args.width, device="cuda") / args.width ** 0.5
+    lin = GatheredLinear(w, torch.zeros(args.width, device="cuda"), "gelu_tanh")
+    x = torch.randn(args.tokens, args.width, device="cuda").to(torch.bfloat16)
+
+    def step():
+        lin(x)
+
+    return step, 2.0 * args.tokens * args.width * args.width
+
+
 def gemm_cycle_breakdown(fn, launch_index: int = -1) -> list:
     """Run ``fn`` once per GEMM launch recorded and return per-CTA-averaged cycle counters.
 
@@ -363,7 +413,8 @@ def gemm_cycle_breakdown(fn, launch_index: int = -1) -> list:
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description="kernel micro-benchmarks (CUDA events)")
-    ap.add_argument("case", choices=["mlp", "sht", "stage", "linear", "bgemm", "recipe"])
+    ap.add_argument("case", choices=["mlp", "sht", "stage", "linear", "bgemm", "recipe", "fused_sht",
+                                     "gathered_linear"])
     ap.add_argument("--recipe", default="pre", choices=["pre", "post"])
     ap.add_argument("--transpose", action="store_true")
     ap.add_argument("--mode", default="fwd", choices=["fwd", "dgrad", "wgrad", "both"],
@@ -386,7 +437,8 @@ def main(argv=None) -> None:
     ap.add_argument("--launch", type=int, default=-1, help="which GEMM launch of the call to break down (-1: last)")
     args = ap.parse_args(argv)
     fn, flops = {"mlp": _mlp_case, "sht": _sht_case, "stage": _stage_case, "linear": _linear_case,
-                 "bgemm": _bgemm_case, "recipe": _recipe_case}[args.case](args)
+                 "bgemm": _bgemm_case, "recipe": _recipe_case, "fused_sht": _fused_sht_case,
+                 "gathered_linear": _gathered_linear_case}[args.case](args)
     tb = TimingBenchmark(warmup=args.warmup, iterations=args.iters)
     r = tb.time_fn(args.case, fn)
     out = {"case": args.case, "mean_ms": r.mean_ms, "min_ms": r.min_ms}
