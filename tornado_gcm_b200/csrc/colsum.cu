@@ -4,8 +4,8 @@
 // Pass 1: block b sums its slice of rows; each thread owns one 16-byte
 // vector (8 columns) and a row lane, so every warp load is a run of full
 // sectors; the row lanes are folded in shared memory and the block writes
-// one row of partial sums.  Pass 2: one thread per column adds the block
-// partials in a fixed order — the result does not depend on scheduling
+// one row of partial sums.  Pass 2: 8 row groups per 32-column block add the
+// block partials in a fixed order — the result does not depend on scheduling
 // (no atomics).
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>

@@ -105,6 +105,12 @@ __device__ __forceinline__ void red_add_sys(float* addr, float v) {
   asm volatile("red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(addr), "f"(v) : "memory");
 }
 
+__device__ __forceinline__ void red_add_sys_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
+}
+
 __device__ __forceinline__ void store_out(const GemmParams& p, long long off, float v) {
   if (p.n_peers > 0) {
     for (int i = 0; i < p.n_peers; ++i) red_add_sys(p.peer_C[i] + off, v);
@@ -651,6 +657,18 @@ __device__ __forceinline__ void gemm_sm100_body(const CUtensorMap& tmap_a, const
           tmem_ld_wait();
           if (!row_ok) continue;
           const int colb = tn * BN + c0;
+          if (p.n_peers > 0 && p.c_sc == 1 && colb + 16 <= p.N && !p.bias && !p.col_scale && p.act == 0 &&
+              ((row_off + colb) & 3) == 0) {
+            // peer reduction of 16 consecutive outputs: four 16-byte reductions per peer
+            for (int i = 0; i < p.n_peers; ++i) {
+              float* dst = p.peer_C[i] + row_off + colb;
+#pragma unroll
+              for (int j = 0; j < 16; j += 4)
+                red_add_sys_v4(dst + j, __uint_as_float(v[j]) * p.alpha, __uint_as_float(v[j + 1]) * p.alpha,
+                               __uint_as_float(v[j + 2]) * p.alpha, __uint_as_float(v[j + 3]) * p.alpha);
+            }
+            continue;
+          }
           if (plain && colb + 16 <= p.N) {
             float* cp = reinterpret_cast<float*>(p.C) + row_off + static_cast<long long>(colb) * p.c_sc;
 #pragma unroll

@@ -258,7 +258,8 @@ class LatitudeShardedSHT:
         M2, L = self.modal_shape
         if self.local_latitudes % 4:
             raise ValueError("the fused path needs a multiple of 4 latitude rows per rank")
-        self._numel = int(max_fields) * M2 * L
+        self._Lp = (L + 3) // 4 * 4  # 16-byte rows: the GEMM epilogue adds 4 values per reduction
+        self._numel = int(max_fields) * M2 * self._Lp
         group = self.group or dist.group.WORLD
         gname = group.group_name
         self._bufs, self._peer_tabs = [], []
@@ -291,18 +292,19 @@ class LatitudeShardedSHT:
         n3 = nodal_local.reshape((-1,) + tuple(nodal_local.shape[-2:])).float()
         S = n3.shape[0]
         M2, L = self.modal_shape
-        if S * M2 * L > self._numel:
-            raise ValueError(f"{S} fields exceed the {self._numel // (M2 * L)} reserved by enable_fused")
+        Lp = self._Lp
+        if S * M2 * Lp > self._numel:
+            raise ValueError(f"{S} fields exceed the {self._numel // (M2 * Lp)} reserved by enable_fused")
         k = self._call % 2
         self._call += 1
         buf = self._bufs[k][0]
         lb = self._lb
         ws = _ext.empty(S * lb.M2 * lb.J, dtype=torch.float32, device=n3.device)
         flag = _ext.error_flag(n3.device)
-        ops.sht_anal(n3, lb.Ft, lb.Ptw, L, ws, None, flag, False, self._peer_tabs[k])
+        ops.sht_anal(n3, lb.Ft, lb.Ptw, Lp, ws, None, flag, False, self._peer_tabs[k])
         ops.peer_barrier(self._pad_tab, self.rank, flag, n3.device.index)
-        view = buf[: S * M2 * L].view(S, M2, L)
-        out = view.clone()
+        view = buf[: S * M2 * Lp].view(S, M2, Lp)
+        out = view[..., :L].contiguous()
         view.zero_()
         return out.reshape(lead + (M2, L)).to(nodal_local.dtype)
 
