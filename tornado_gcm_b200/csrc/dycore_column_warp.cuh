@@ -315,7 +315,7 @@ __global__ void __launch_bounds__(32 * kColWarps) column_fwd_warp_kernel(
 
 // ── reverse mode ────────────────────────────────────────────────────────────
 // dynamic shared memory: in_fields + out_fields slots (inputs, then output cotangents)
-__global__ void __launch_bounds__(32 * kColWarps) column_vjp_warp_kernel(
+__global__ void __launch_bounds__(32 * kColWarps, 4) column_vjp_warp_kernel(
     ColumnConsts c, SliceIndex ix, const float* __restrict__ in, const float* __restrict__ gout,
     float* __restrict__ gin, const float* __restrict__ sec2, const float* __restrict__ cor, int B, int I, int J,
     int lat_major) {

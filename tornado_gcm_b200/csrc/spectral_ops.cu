@@ -204,8 +204,10 @@ constexpr int kRowWarps = 8;
 // so each term's metadata, coefficient, diagonal and recurrence weights are
 // read once and applied to NB rows (the kernel is instruction-bound on that
 // per-term work).  grid = (m-row blocks, C_out, ceil(B / NB)).
+// Up to three 32-wide l chunks fit in 64 registers, which allows four blocks
+// (32 warps) per SM: the kernel is latency-bound, so occupancy is what counts.
 template <int NL, int NB>
-__global__ void __launch_bounds__(32 * kRowWarps) spectral_linear_rows_kernel(LinearArgs a) {
+__global__ void __launch_bounds__(32 * kRowWarps, (NL <= 3 ? 4 : 2)) spectral_linear_rows_kernel(LinearArgs a) {
   __shared__ float sbuf[kRowWarps][NB][32 * NL + 2];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int mr = blockIdx.x * kRowWarps + warp;
