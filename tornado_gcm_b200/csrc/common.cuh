@@ -177,6 +177,21 @@ __device__ __forceinline__ uint64_t make_sw128_desc(uint32_t smem_addr, uint32_t
   return d;
 }
 
+// Shared-memory descriptor for an MN-major 32-bit (TF32) operand: 128-byte
+// rows along MN with 32-byte swizzle atoms (layout type 1, the pattern the
+// TMA writes with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B: 32-byte chunk index
+// XOR (row mod 4)).  lbo = bytes between 128-byte MN chunks, sbo = bytes
+// between groups of 4 K-rows.
+__device__ __forceinline__ uint64_t make_sw128b32_desc(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= 1ull << 46;
+  d |= 1ull << 61;
+  return d;
+}
+
 // Instruction descriptor: f32 accumulate; fmt 1 = BF16, 2 = TF32;
 // major 0 = K-major, 1 = MN-major.
 __host__ __device__ constexpr uint32_t make_idesc(uint32_t fmt, uint32_t a_major, uint32_t b_major, uint32_t M,

@@ -43,26 +43,29 @@ struct TmapKey {
   int dtype;
   uint64_t d0, d1, d2, s1, s2;
   uint32_t b0, b1, b2;
+  int swz;
   bool operator==(const TmapKey& o) const {
     return ptr == o.ptr && dtype == o.dtype && d0 == o.d0 && d1 == o.d1 && d2 == o.d2 && s1 == o.s1 &&
-           s2 == o.s2 && b0 == o.b0 && b1 == o.b1 && b2 == o.b2;
+           s2 == o.s2 && b0 == o.b0 && b1 == o.b1 && b2 == o.b2 && swz == o.swz;
   }
 };
 struct TmapKeyHash {
   size_t operator()(const TmapKey& k) const {
     size_t h = std::hash<uint64_t>()(k.ptr);
     auto mix = [&h](uint64_t v) { h ^= std::hash<uint64_t>()(v) + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2); };
-    mix(k.dtype); mix(k.d0); mix(k.d1); mix(k.d2); mix(k.s1); mix(k.s2); mix(k.b0); mix(k.b1); mix(k.b2);
+    mix(k.dtype); mix(k.d0); mix(k.d1); mix(k.d2); mix(k.s1); mix(k.s2); mix(k.b0); mix(k.b1); mix(k.b2); mix(k.swz);
     return h;
   }
 };
 
 // dtype: 1 = bf16, 2 = fp32.  dims innermost first; strides in bytes for dims 1, 2.
+// swz: 0 = 128-byte swizzle of 16-byte chunks (K-major operands, MN-major BF16),
+//      1 = 128-byte swizzle of 32-byte chunks (MN-major TF32 operands).
 static CUtensorMap make_tmap(const void* ptr, int dtype, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1,
-                             uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2) {
+                             uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2, int swz = 0) {
   static std::mutex mu;
   static std::unordered_map<TmapKey, CUtensorMap, TmapKeyHash> cache;
-  TmapKey key{reinterpret_cast<uint64_t>(ptr), dtype, d0, d1, d2, s1, s2, b0, b1, b2};
+  TmapKey key{reinterpret_cast<uint64_t>(ptr), dtype, d0, d1, d2, s1, s2, b0, b1, b2, swz};
   {
     std::lock_guard<std::mutex> lock(mu);
     auto it = cache.find(key);
@@ -80,7 +83,8 @@ static CUtensorMap make_tmap(const void* ptr, int dtype, uint64_t d0, uint64_t d
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = get_encode_fn()(&map, dtype == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
                                3, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               swz == 1 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw std::runtime_error("tgcm: cuTensorMapEncodeTiled failed with code " + std::to_string(int(r)));
   std::lock_guard<std::mutex> lock(mu);
@@ -185,6 +189,9 @@ static void gemm_dispatch(int fmt, int bn, bool a_mn, bool b_mn, const CUtensorM
   TGCM_CASE(2, 256, false, false)
   TGCM_CASE(2, 80, false, false)
   TGCM_CASE(2, 144, false, false)
+  TGCM_CASE(2, 64, false, true)
+  TGCM_CASE(2, 128, false, true)
+  TGCM_CASE(2, 256, false, true)
   TGCM_CASE(1, 64, false, false)
   TGCM_CASE(1, 128, false, false)
   TGCM_CASE(1, 64, false, true)
@@ -216,12 +223,14 @@ static int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 // ── spherical-harmonic transforms ───────────────────────────────────────────
 // Nodal layouts: "lon-major" (S, I, J) = the public (…, lon, lat) layout, and
-// "lat-major" (S, J, I) used inside the fused dycore.  Both TF32 GEMMs of the
-// analysis take K-major operands only (TF32 MN-major operands would need the
-// 32-byte-atom swizzle), so a lon-major analysis input is transposed first.
+// "lat-major" (S, J, I) used inside the fused dycore.  The synthesis keeps its
+// intermediate m-major, W (M2, S·J): the per-m Legendre GEMM then writes whole
+// rows of J values (16-byte stores) and the DFT GEMM reads W as an MN-major
+// TF32 operand (32-byte-atom swizzle).  The analysis GEMMs take K-major
+// operands, so a lon-major analysis input is transposed first.
 //
 // x: (S, M2, L) fp32 modal view (last-dim stride 1, row stride 16B-aligned), logical L;
-// P: (Mw, J, Lp);  F: (I, M2p).  Returns nodal (S, I, J) or (S, J, I).  ws: (S, J, M2p).
+// P: (Mw, J, Lp);  F: (I, M2p).  Returns nodal (S, I, J) or (S, J, I).  ws: >= M2·S·J floats.
 at::Tensor sht_synth(const at::Tensor& x, int64_t L, const at::Tensor& P, const at::Tensor& F, const at::Tensor& ws,
                      const c10::optional<at::Tensor>& col_scale, const c10::optional<at::Tensor>& err,
                      bool lat_major) {
@@ -233,7 +242,7 @@ at::Tensor sht_synth(const at::Tensor& x, int64_t L, const at::Tensor& P, const 
   const int64_t Mw = P.size(0), J = P.size(1), Lp = P.size(2);
   const int64_t I = F.size(0), M2p = F.size(1);
   TORCH_CHECK(M2 == 2 * Mw - 1 && M2p % 4 == 0 && M2p >= M2 && Lp >= L, "basis shape mismatch");
-  TORCH_CHECK(ws.numel() >= S * J * M2p, "workspace too small");
+  TORCH_CHECK(ws.numel() >= S * J * M2, "workspace too small");
   auto out = lat_major ? out_empty({S, J, I}, x.options()) : out_empty({S, I, J}, x.options());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const int bnj = pick_bn_j(J);
@@ -244,25 +253,27 @@ at::Tensor sht_synth(const at::Tensor& x, int64_t L, const at::Tensor& P, const 
     p.M = 2 * S; p.N = J; p.K = L; p.groups = Mw;
     p.tiles_m = cdiv(S, 64); p.tiles_n = cdiv(J, bnj);
     p.a_pair = 1; p.k_tri = 1;
-    p.C = ws.data_ptr(); p.c_pair = 1; p.c_ps = J * M2p; p.c_pmr = 1; p.c_sc = M2p;
+    p.C = ws.data_ptr(); p.c_pair = 1; p.c_ps = J; p.c_pmr = S * J; p.c_sc = 1;  // W[mrow][s·J + j]
     p.err = err_ptr(err);
     gemm_dispatch(2, bnj, false, false, ta, tb, p, st);
   }
   const bool one_gemm = lat_major && !(col_scale.has_value() && col_scale->defined());
   if (one_gemm) {
-    // lat-major output: out[s, j, i] = Σ_k F[i, k] W[(s, j), k] is ONE GEMM with
-    // N = S·J (the (s, j) rows of W are contiguous) and a linear output map n·I + i.
+    // lat-major output: out[s, j, i] = Σ_k F[i, k] W[k, (s, j)] is ONE GEMM with
+    // N = S·J (MN-major B: the (s, j) columns of W are contiguous) and a linear
+    // output map n·I + i.
     CUtensorMap ta = make_tmap(F.data_ptr(), 2, M2, I, 1, M2p * 4, I * M2p * 4, 32, 128, 1);
-    CUtensorMap tb = make_tmap(ws.data_ptr(), 2, M2, S * J, 1, M2p * 4, S * J * M2p * 4, 32, 256, 1);
+    CUtensorMap tb = make_tmap(ws.data_ptr(), 2, S * J, M2, 1, S * J * 4, M2 * S * J * 4, 32, 32, 1, 1);
     GemmParams p = default_params();
     p.M = I; p.N = S * J; p.K = M2; p.groups = 1;
     p.tiles_m = cdiv(I, 128); p.tiles_n = cdiv(S * J, 256);
     p.C = out.data_ptr(); p.c_sg = 0; p.c_sr = 1; p.c_sc = I;
     p.err = err_ptr(err);
-    gemm_dispatch(2, 256, false, false, ta, tb, p, st);
+    gemm_dispatch(2, 256, false, true, ta, tb, p, st);
   } else {
+    // one GEMM per slice s: B[j][k] = W[k][s·J + j] (MN-major, batch coordinate s)
     CUtensorMap ta = make_tmap(F.data_ptr(), 2, M2, I, 1, M2p * 4, I * M2p * 4, 32, 128, 1);
-    CUtensorMap tb = make_tmap(ws.data_ptr(), 2, M2, J, S, M2p * 4, J * M2p * 4, 32, bnj, 1);
+    CUtensorMap tb = make_tmap(ws.data_ptr(), 2, J, M2, S, S * J * 4, J * 4, 32, 32, 1, 1);
     GemmParams p = default_params();
     p.M = I; p.N = J; p.K = M2; p.groups = S;
     p.tiles_m = cdiv(I, 128); p.tiles_n = cdiv(J, bnj);
@@ -271,7 +282,7 @@ at::Tensor sht_synth(const at::Tensor& x, int64_t L, const at::Tensor& P, const 
     if (lat_major) { p.c_sr = 1; p.c_sc = I; } else { p.c_sr = J; p.c_sc = 1; }
     if (col_scale.has_value() && col_scale->defined()) p.col_scale = col_scale->data_ptr<float>();
     p.err = err_ptr(err);
-    gemm_dispatch(2, bnj, false, false, ta, tb, p, st);
+    gemm_dispatch(2, bnj, false, true, ta, tb, p, st);
   }
   return out;
 }

@@ -336,6 +336,76 @@ __device__ __forceinline__ void epilogue_rowmajor_vec(const GemmParams& p, int A
   }
 }
 
+// Epilogue of a pair-addressed tile (per-wavenumber Legendre GEMMs) whose
+// output rows are contiguous (c_sc == 1): tile row r = 2·s + {cos, sin} of
+// slice tm·64 + s goes to C + s·c_ps + mrow·c_pmr.  Plain fp32 stores scaled
+// by alpha.  The 32 x 32 chunk is staged in shared memory; with 16-byte
+// aligned rows eight lanes cover one row with 16-byte stores, otherwise the
+// 32 lanes write 32 consecutive values of one row per instruction.
+template <int BN>
+__device__ __noinline__ void epilogue_pair_rows(const GemmParams& p, uint32_t taddr_row, uint8_t* stage, int tm,
+                                                   int tn, int g, int q, int half, int lane) {
+  const int S = p.M / 2;
+  const bool vec = (reinterpret_cast<uintptr_t>(p.C) % 16 == 0) && (p.c_ps % 4 == 0) && (p.c_pmr % 4 == 0);
+  float* C = reinterpret_cast<float*>(p.C);
+  auto row_off = [&](int r, bool* ok) -> long long {
+    const int s_idx = tm * 64 + (r >> 1);
+    const int pm = r & 1;
+    const int mr = (g == 0) ? 0 : 2 * g - 1 + pm;
+    *ok = (s_idx < S) && !(g == 0 && pm == 1);
+    return static_cast<long long>(s_idx) * p.c_ps + static_cast<long long>(mr) * p.c_pmr;
+  };
+#pragma unroll 1
+  for (int c0 = half * 32; c0 < BN; c0 += 64) {
+    const int ncolc = (BN - c0) >= 32 ? 32 : (BN - c0);
+    const int col0 = tn * BN + c0;
+    int ncols = p.N - col0;
+    if (ncols > ncolc) ncols = ncolc;
+    uint8_t* my = stage + lane * kStageRowF32;
+    // 16 columns at a time: load, scale, stage (keeps 16 accumulator registers live)
+#pragma unroll 1
+    for (int h = 0; h < ncolc; h += 16) {
+      uint32_t v[16];
+      tmem_ld_32x32b_x16(taddr_row + c0 + h, v);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 16; j += 4)
+        *reinterpret_cast<float4*>(my + 4 * (h + j)) =
+            make_float4(__uint_as_float(v[j]) * p.alpha, __uint_as_float(v[j + 1]) * p.alpha,
+                        __uint_as_float(v[j + 2]) * p.alpha, __uint_as_float(v[j + 3]) * p.alpha);
+    }
+    if (ncols <= 0) continue;
+    __syncwarp();
+    if (vec) {
+#pragma unroll 2
+      for (int i = 0; i < 8; ++i) {
+        const int v = lane + 32 * i;
+        const int rr = v >> 3, seg = v & 7;
+        bool ok;
+        const long long off = row_off(q * 32 + rr, &ok);
+        if (!ok || seg * 4 >= ncols) continue;
+        const uint8_t* sp = stage + rr * kStageRowF32 + seg * 16;
+        float* gp = C + off + col0 + seg * 4;
+        if (seg * 4 + 4 <= ncols) {
+          *reinterpret_cast<float4*>(gp) = *reinterpret_cast<const float4*>(sp);
+        } else {
+          const float* se = reinterpret_cast<const float*>(sp);
+          for (int e = 0; seg * 4 + e < ncols; ++e) gp[e] = se[e];
+        }
+      }
+    } else {
+      const float* sf = reinterpret_cast<const float*>(stage);
+#pragma unroll 4
+      for (int rr = 0; rr < 32; ++rr) {
+        bool ok;
+        const long long off = row_off(q * 32 + rr, &ok);
+        if (ok && lane < ncols) C[off + col0 + lane] = sf[rr * (kStageRowF32 / 4) + lane];
+      }
+    }
+    __syncwarp();
+  }
+}
+
 template <int BN>
 __device__ __forceinline__ void epilogue_rowmajor_dispatch(const GemmParams& p, int act, uint32_t taddr_row,
                                                            uint8_t* stage, int tm, int tn, int g, int q, int half,
@@ -523,12 +593,19 @@ __device__ __forceinline__ void gemm_sm100_body(const CUtensorMap& tmap_a, const
 #pragma unroll
           for (int k = 0; k < BK / T::kUK; ++k) {
             uint64_t adesc, bdesc;
+            // MN-major operands: BF16 uses the 16-byte-atom 128-byte swizzle
+            // (8-row K groups, sbo 1024); TF32 needs the 32-byte-atom swizzle
+            // (4-row K groups, sbo 512).
             if (!A_MN)
               adesc = make_sw128_desc(sa + k * 32, 16, 1024);
+            else if (FMT == 2)
+              adesc = make_sw128b32_desc(sa + k * T::kUK * 128, BK * 128, 512);
             else
               adesc = make_sw128_desc(sa + k * T::kUK * 128, BK * 128, 1024);
             if (!B_MN)
               bdesc = make_sw128_desc(sb + k * 32, 16, 1024);
+            else if (FMT == 2)
+              bdesc = make_sw128b32_desc(sb + k * T::kUK * 128, BK * 128, 512);
             else
               bdesc = make_sw128_desc(sb + k * T::kUK * 128, BK * 128, 1024);
             const uint32_t accum = (i > 0 || k > 0) ? 1u : 0u;
@@ -582,7 +659,10 @@ __device__ __forceinline__ void gemm_sm100_body(const CUtensorMap& tmap_a, const
                                       (p.c_sg * 2) % 16 == 0)) &&
                           (!p.grad_pre || (reinterpret_cast<uintptr_t>(p.grad_pre) % 16 == 0 &&
                                            (p.c_sr * 2) % 16 == 0 && (p.c_sg * 2) % 16 == 0));
-      if (vec_ok) {
+      if (p.c_pair && p.c_sc == 1 && plain) {
+        uint8_t* stage = reinterpret_cast<uint8_t*>(staging) + (warp - 2) * (32 * kStageRowF32);
+        epilogue_pair_rows<BN>(p, taddr_row, stage, tm, tn, g, q, half, lane);
+      } else if (vec_ok) {
         uint8_t* stage = reinterpret_cast<uint8_t*>(staging) + (warp - 2) * (32 * kStageRowF32);
         epilogue_rowmajor_dispatch<BN>(p, p.grad_pre ? p.grad_act : p.act, taddr_row, stage, tm, tn, g, q, half,
                                        lane);
