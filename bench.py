@@ -65,6 +65,8 @@ def parse_args():
     p.add_argument("--mode", choices=["train", "forecast"], default="train",
                    help="train: backprop through the rollout (default); forecast: ensemble 6-h forecast")
     p.add_argument("--members", type=int, default=16, help="forecast: ensemble members per GPU")
+    p.add_argument("--checkpoint", choices=["auto", "on", "off"], default="auto",
+                   help="train: recompute each 6-h block in backward (auto: on above 2.8 degrees)")
     p.add_argument("--batch", type=int, default=4, help="per-GPU batch")
     p.add_argument("--rollout", type=int, default=4, help="6-h steps per training example")
     p.add_argument("--no-graph", action="store_true")
@@ -208,6 +210,8 @@ def run_b200(args, rank, world):
     dev = torch.device("cuda", torch.cuda.current_device())
     gcm, data = build_hybrid_gcm(args.resolution, dev, seed=0)
     spec = RESOLUTIONS[args.resolution]
+    gcm.checkpoint_outer_steps = (args.checkpoint == "on" or
+                                  (args.checkpoint == "auto" and args.resolution not in ("2.8deg", "5.6deg")))
     trainer = GCMTrainer(gcm, lr=1e-4, graph=not args.no_graph, data_parallel=world > 1)
     B, K = args.batch, args.rollout
     enc = gcm.encoder
@@ -273,11 +277,13 @@ def run_b200(args, rank, world):
         x0, tg = dev_pool[0]
         use_graph = trainer.use_graph
         trainer.use_graph = False
-        with profile(activities=[ProfilerActivity.CUDA]) as prof:
-            trainer._zero()
-            trainer._step_body(x0, tg, forc_dev)
-            torch.cuda.synchronize()
-        trainer.use_graph = use_graph
+        try:
+            with profile(activities=[ProfilerActivity.CUDA]) as prof:
+                trainer._zero()
+                trainer._step_body(x0, tg, forc_dev)
+                torch.cuda.synchronize()
+        finally:
+            trainer.use_graph = use_graph
         n_mine = 0
         n_all = 0
         for ev in prof.events():
@@ -316,8 +322,11 @@ def run_b200(args, rank, world):
                 "parallelism": f"dp{world}",
                 "zones": "Z1 TF32 tcgen05 transforms, Z3 BF16 tcgen05 towers, Z2 FP64-accumulated fixer",
                 "cuda_graph": trainer.use_graph,
-                "l2": "working set per step (activations of 72 physics steps) far exceeds the 126 MB L2",
+                "activation_checkpointing": "per 6-h block" if gcm.checkpoint_outer_steps else "none",
+                "l2": f"working set per step (activations of {K * spec.physics_steps_per_output} physics steps) "
+                      "far exceeds the 126 MB L2",
                 "loss": loss_last,
+                "peak_mem_gb": torch.cuda.max_memory_allocated() / 1e9,
             },
             "clocks": clocks,
             "e2e": e2e,
@@ -431,6 +440,7 @@ def run_b200_forecast(args, rank, world):
                 "zones": "Z1 TF32 tcgen05 transforms, Z3 BF16 tcgen05 towers, Z2 FP64-accumulated fixer",
                 "cuda_graph": True,
                 "l2": "ensemble state and decoded outputs exceed the 126 MB L2",
+                "peak_mem_gb": torch.cuda.max_memory_allocated() / 1e9,
             },
             "clocks": clocks, "e2e": e2e,
             "gpu_launches": (launches or {}).get("per_6h_step", 0) * K, "launch_detail": launches,

@@ -102,12 +102,13 @@ def test_sht_roundtrip_vs_fp64(name, S):
     assert _ext.check_error_flag(torch.device(DEV)) == 0
 
 
-def test_sht_lat_major_roundtrip():
+@pytest.mark.parametrize("name,S", [("TL63", 7), ("TL127", 5)])
+def test_sht_lat_major_roundtrip(name, S):
     _require()
     from tornado_gcm_b200.ops import sht as sht_ops
 
-    g = _grid("TL63")
-    x = _modal(g, 7).float().to(DEV)
+    g = _grid(name)
+    x = _modal(g, S).float().to(DEV)
     nod = sht_ops.to_nodal_lat_major(x, g.spherical_harmonics)
     nod_ref = g.with_precision("highest").to_nodal(x.cpu().double()).transpose(-1, -2)
     assert _rel(nod.cpu(), nod_ref) < 3e-3
@@ -357,3 +358,23 @@ def test_colsum_bf16_vs_fp64(T, ld, n):
     out = ops.colsum_bf16(x.to(DEV), n).cpu()
     ref = x[:, :n].double().sum(0)
     assert _rel(out, ref) < 1e-5
+
+
+def test_offloaded_rollout_matches_device_rollout():
+    _require()
+    from tornado_gcm_b200.inference.runner import MPInference
+    from tornado_gcm_b200.models.builders import build_hybrid_gcm
+
+    gcm, data = build_hybrid_gcm("5.6deg", DEV)
+    enc = gcm.encoder
+    x0 = {k: ((v.to(DEV) - getattr(enc, f"mean_{k}")) / getattr(enc, f"std_{k}")) for k, v in data.sample(2, 0).items()}
+    f = {k: v.to(DEV) for k, v in data.forcings(2).items()}
+    engine = MPInference(gcm)
+    dev_traj = engine.rollout(x0, 3, forcings=f)
+    host_traj = engine.rollout(x0, 3, forcings=f, offload=True)
+    assert len(host_traj) == 3
+    for a, b in zip(dev_traj, host_traj):
+        for k in a:
+            assert b[k].device.type == "cpu" and not b[k].is_pinned()
+            torch.testing.assert_close(b[k], a[k].cpu(), rtol=1e-5, atol=1e-6)
+

@@ -189,3 +189,28 @@ def test_sda_trainer_and_cli(tmp_path):
                                     "--no-sda"])
     assert res.exit_code == 0, res.output
     assert np.load(tmp_path / "fc.npz")["t"].shape[0] == 2
+
+
+def test_checkpointed_outer_steps_give_the_same_gradients():
+    gcm, data, norm = _small()
+    x0 = norm(data.sample(2, 0))
+    tg = [norm(data.sample(2, i + 1)) for i in range(2)]
+    forc = data.forcings(2)
+    params = [p for p in gcm.parameters() if p.requires_grad]
+
+    def grads(ckpt: bool):
+        gcm.checkpoint_outer_steps = ckpt
+        gcm.model._step_count = 0
+        for p in params:
+            p.grad = None
+        loss = gcm.loss(x0, tg, forc)
+        loss.backward()
+        return float(loss), [p.grad.clone() for p in params], gcm.model._step_count
+
+    l0, g0, n0 = grads(False)
+    l1, g1, n1 = grads(True)
+    gcm.checkpoint_outer_steps = False
+    assert l0 == pytest.approx(l1, rel=1e-6)
+    assert n0 == n1 == 2 * gcm.physics_steps_per_output  # recompute leaves the fixer counter alone
+    for a, b in zip(g0, g1):
+        torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-7)

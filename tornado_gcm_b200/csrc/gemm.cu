@@ -305,7 +305,11 @@ at::Tensor sht_anal(const at::Tensor& N_in, const at::Tensor& Ft, const at::Tens
   TORCH_CHECK(Ft.size(1) == I && Pt.size(2) == J && J % 4 == 0 && I % 4 == 0, "basis shape mismatch");
   TORCH_CHECK(ws.numel() >= S * M2 * J, "workspace too small");
   TORCH_CHECK(Lo >= L, "output row length too small");
-  auto out = Lo > L ? at::zeros({S, M2, Lo}, N.options()) : out_empty({S, M2, Lo}, N.options());
+  // Columns L..Lo-1 of a padded row are never written or read (consumers take
+  // the [..., :L] view; TMA maps of the modal rows stop at L).  With peer
+  // reductions the result lands in the peers' buffers and `out` stays empty.
+  const bool to_peers = peer_ptrs.has_value() && peer_ptrs->defined();
+  auto out = to_peers ? out_empty({0}, N.options()) : out_empty({S, M2, Lo}, N.options());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const int bnj = pick_bn_j(J);
   // 1) real DFT analysis.  Without a column scale it is ONE GEMM over all (s, j):
@@ -346,7 +350,7 @@ at::Tensor sht_anal(const at::Tensor& N_in, const at::Tensor& Ft, const at::Tens
     p.a_pair = 1;
     p.C = out.data_ptr(); p.c_pair = 1; p.c_ps = M2 * Lo; p.c_pmr = Lo; p.c_sc = 1;
     p.err = err_ptr(err);
-    if (peer_ptrs.has_value() && peer_ptrs->defined()) {
+    if (to_peers) {
       TORCH_CHECK(!peer_ptrs->is_cuda() && peer_ptrs->scalar_type() == at::kLong && peer_ptrs->numel() >= 1 &&
                       peer_ptrs->numel() <= 8,
                   "peer_ptrs must be 1..8 int64 addresses on the CPU");

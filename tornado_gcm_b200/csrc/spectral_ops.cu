@@ -14,6 +14,7 @@
 //    implicit solve, and on the last stage the spectral filter and the
 //    inner-state sanitiser — plus its adjoint.
 #include "alloc.h"
+#include <cstdlib>
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -338,11 +339,206 @@ __global__ void __launch_bounds__(32 * kRowWarps, (NL <= 3 ? 4 : 2)) spectral_li
   }
 }
 
+// Pipelined row kernel.  The warps of a block share one output channel, so
+// the channel's term table (up to kPfTerms entries) is staged once in shared
+// memory; each warp then issues the source-row loads of term t + 1 before it
+// works on term t, so the latency of one term's loads overlaps the previous
+// term's arithmetic instead of adding to it.  Arithmetic is that of
+// spectral_linear_rows_kernel.
+constexpr int kPfTerms = 64;
+
+struct PfTerm {
+  int src, st, pre, post, mat, row;
+  float cf;
+};
+
+// Blocks per SM: the pipeline keeps three NB x NL register arrays (sums, the
+// current and the next source rows) live.
+template <int NL, int NB>
+struct PfOcc {
+  static constexpr int value = NB * NL <= 8 ? 4 : (NB * NL <= 12 ? 3 : 2);
+};
+
+template <int NL, int NB>
+__global__ void __launch_bounds__(32 * kRowWarps, (PfOcc<NL, NB>::value)) spectral_linear_rows_pf_kernel(LinearArgs a) {
+  __shared__ float sbuf[kRowWarps][NB][32 * NL + 2];
+  __shared__ PfTerm sterm[kPfTerms];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int s = blockIdx.y;
+  const int t0 = __ldg(a.row_ptr + s), t1 = __ldg(a.row_ptr + s + 1);
+  const int nt = t1 - t0;
+  for (int i = threadIdx.x; i < nt && i < kPfTerms; i += blockDim.x) {
+    const int* T = a.terms + 7 * (t0 + i);
+    sterm[i] = PfTerm{__ldg(T + 1), __ldg(T + 2), __ldg(T + 3), __ldg(T + 4), __ldg(T + 5), __ldg(T + 6),
+                      __ldg(a.coef + t0 + i)};
+  }
+  __syncthreads();
+  const int mr = blockIdx.x * kRowWarps + warp;
+  if (mr >= a.M2) return;
+  const int b0 = blockIdx.z * NB;
+  const int nb = min(NB, a.B - b0);
+  const int L = a.L;
+  auto term = [&](int i) -> PfTerm {
+    if (i < kPfTerms) return sterm[i];
+    const int* T = a.terms + 7 * (t0 + i);
+    return PfTerm{__ldg(T + 1), __ldg(T + 2), __ldg(T + 3), __ldg(T + 4), __ldg(T + 5), __ldg(T + 6),
+                  __ldg(a.coef + t0 + i)};
+  };
+  // source row of a non-vertical term (the paired ±m row for ∂/∂λ); -1: term contributes nothing
+  auto source_row = [&](const PfTerm& m) -> int {
+    if (m.st == kStVert || m.st == kStVertT) return -1;
+    if (m.st == kStDlon) return mr == 0 ? -1 : ((mr & 1) ? mr + 1 : mr - 1);
+    return mr;
+  };
+  auto issue = [&](int i, float (&xo)[NB][NL]) {
+    const PfTerm m = term(i);
+    const int srow = source_row(m);
+    const float* xr0 = a.x + m.src * a.xs_c + (srow < 0 ? 0 : srow) * a.xs_m;
+#pragma unroll
+    for (int q = 0; q < NB; ++q)
+#pragma unroll
+      for (int j = 0; j < NL; ++j) {
+        const int l = lane + 32 * j;
+        xo[q][j] = (srow >= 0 && q < nb && l < L) ? __ldg(xr0 + (b0 + q) * a.xs_b + l) : 0.f;
+      }
+  };
+  float acc[NB][NL];
+#pragma unroll
+  for (int q = 0; q < NB; ++q)
+#pragma unroll
+    for (int j = 0; j < NL; ++j) acc[q][j] = 0.f;
+  float xn[NB][NL];
+  if (nt > 0) issue(0, xn);
+  for (int i = 0; i < nt; ++i) {
+    float xv[NB][NL];
+#pragma unroll
+    for (int q = 0; q < NB; ++q)
+#pragma unroll
+      for (int j = 0; j < NL; ++j) xv[q][j] = xn[q][j];
+    if (i + 1 < nt) issue(i + 1, xn);
+    const PfTerm m = term(i);
+    if (m.st == kStVert || m.st == kStVertT) {
+#pragma unroll
+      for (int q = 0; q < NB; ++q) {
+        if (q >= nb) break;
+        LinearArgs ab = a;
+        ab.x = a.x + (b0 + q) * a.xs_b;
+#pragma unroll
+        for (int j = 0; j < NL; ++j) {
+          const int l = lane + 32 * j;
+          if (l < L) {
+            float v = stencil_val(ab, 0, m.src, m.st, m.pre, mr, l, m.mat, m.row);
+            if (m.post >= 0) v *= __ldg(a.diag + m.post * L + l);
+            acc[q][j] = fmaf(m.cf, v, acc[q][j]);
+          }
+        }
+      }
+      continue;
+    }
+    if (source_row(m) < 0) continue;
+    float fac = 1.f;
+    if (m.st == kStDlon) {
+      const int jm = (mr + 1) >> 1;
+      fac = (mr & 1) ? static_cast<float>(jm) : -static_cast<float>(jm);
+    }
+    float qdiag[NL];
+#pragma unroll
+    for (int j = 0; j < NL; ++j) {
+      const int l = lane + 32 * j;
+      const float pd = (m.pre >= 0 && l < L) ? __ldg(a.diag + m.pre * L + l) : 1.f;
+#pragma unroll
+      for (int q = 0; q < NB; ++q) xv[q][j] *= pd;
+      qdiag[j] = (m.post >= 0 && l < L) ? m.cf * __ldg(a.diag + m.post * L + l) : m.cf;
+    }
+    const bool lat = m.st == kStCdlat || m.st == kStHdlat || m.st == kStCdlatT || m.st == kStHdlatT;
+    if (!lat) {
+#pragma unroll
+      for (int q = 0; q < NB; ++q)
+#pragma unroll
+        for (int j = 0; j < NL; ++j) acc[q][j] = fmaf(qdiag[j] * fac, xv[q][j], acc[q][j]);
+      continue;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < NB; ++q) {
+      float* buf = sbuf[warp][q] + 1;  // buf[l] for l in [-1, 32*NL]
+#pragma unroll
+      for (int j = 0; j < NL; ++j) buf[lane + 32 * j] = xv[q][j];
+      if (lane == 0) {
+        buf[-1] = 0.f;
+        buf[32 * NL] = 0.f;
+      }
+    }
+    __syncwarp();
+    const float* ra = a.rec_a + mr * L;
+    const float* rb = a.rec_b + mr * L;
+#pragma unroll
+    for (int j = 0; j < NL; ++j) {
+      const int l = lane + 32 * j;
+      if (l >= L) continue;
+      float cp, cm;
+      if (m.st == kStCdlat) {
+        cp = (l + 1 < L) ? (l + 2) * __ldg(ra + l + 1) : 0.f;
+        cm = (l >= 1) ? -(l - 1) * __ldg(rb + l - 1) : 0.f;
+      } else if (m.st == kStHdlat) {
+        cp = (l + 1 < L) ? l * __ldg(ra + l + 1) : 0.f;
+        cm = (l >= 1) ? -(l + 1) * __ldg(rb + l - 1) : 0.f;
+      } else if (m.st == kStCdlatT) {
+        cm = (l >= 1) ? (l + 1) * __ldg(ra + l) : 0.f;
+        cp = (l + 1 < L) ? -l * __ldg(rb + l) : 0.f;
+      } else {
+        cm = (l >= 1) ? (l - 1) * __ldg(ra + l) : 0.f;
+        cp = (l + 1 < L) ? -(l + 2) * __ldg(rb + l) : 0.f;
+      }
+      cp *= qdiag[j];
+      cm *= qdiag[j];
+#pragma unroll
+      for (int q = 0; q < NB; ++q) {
+        const float* buf = sbuf[warp][q] + 1;
+        const float xp = (l + 1 < L) ? buf[l + 1] : 0.f;
+        const float xm = (l >= 1) ? buf[l - 1] : 0.f;
+        acc[q][j] = fmaf(cp, xp, fmaf(cm, xm, acc[q][j]));
+      }
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < NB; ++q) {
+    if (q >= nb) break;
+    float* yrow = a.y + (b0 + q) * a.ys_b + s * a.ys_c + mr * a.ys_m;
+#pragma unroll
+    for (int j = 0; j < NL; ++j) {
+      const int l = lane + 32 * j;
+      if (l < L)
+        yrow[l] = acc[q][j];
+      else if (l < a.ys_m)
+        yrow[l] = 0.f;  // 16-byte row padding
+    }
+    for (long long z = 32 * NL + lane; z < a.ys_m; z += 32) yrow[z] = 0.f;
+  }
+}
+
+// Row-kernel variant: the pipelined kernel up to five 32-wide l chunks (measured
+// at TL63, post recipe and its adjoint: 0.142 -> 0.130 ms and 0.119 -> 0.101 ms;
+// whole training step 389 -> 379 ms); beyond that its three register arrays
+// spill and the unpipelined kernel runs.  TGCM_RECIPE_PIPELINE=0 / 1 forces
+// one variant (for comparisons).
+static bool recipe_pipelined(int nl) {
+  static int v = -2;
+  if (v == -2) {
+    const char* e = std::getenv("TGCM_RECIPE_PIPELINE");
+    v = (e == nullptr || e[0] == '\0') ? -1 : (e[0] == '0' ? 0 : 1);
+  }
+  return v < 0 ? nl <= 5 : v == 1;
+}
+
 template <int NL, int NB>
 static void launch_rows_nb(const LinearArgs& a, cudaStream_t st) {
   dim3 grid(static_cast<unsigned>((a.M2 + kRowWarps - 1) / kRowWarps), static_cast<unsigned>(a.C_out),
             static_cast<unsigned>((a.B + NB - 1) / NB));
-  spectral_linear_rows_kernel<NL, NB><<<grid, 32 * kRowWarps, 0, st>>>(a);
+  if (recipe_pipelined(NL))
+    spectral_linear_rows_pf_kernel<NL, NB><<<grid, 32 * kRowWarps, 0, st>>>(a);
+  else
+    spectral_linear_rows_kernel<NL, NB><<<grid, 32 * kRowWarps, 0, st>>>(a);
 }
 
 template <int NL>

@@ -15,6 +15,7 @@ defines: :meth:`MPInference.from_state_dict` and :meth:`MPInference.rollout`.
 from __future__ import annotations
 
 import logging
+from concurrent.futures import Future, ThreadPoolExecutor
 from typing import Any, Callable, Optional
 
 import torch
@@ -43,6 +44,62 @@ def _offload(obj: Any, device: str | torch.device = "cpu", async_transfer: bool 
     if isinstance(obj, dict):
         return {k: _offload(v, device, async_transfer) for k, v in obj.items()}
     return obj
+
+
+def _map_tensors(obj: Any, fn: Callable) -> Any:
+    if hasattr(obj, "tree_map"):
+        return obj.tree_map(fn)
+    if isinstance(obj, (torch.Tensor, Future)):
+        return fn(obj)
+    if isinstance(obj, dict):
+        return {k: _map_tensors(v, fn) for k, v in obj.items()}
+    if isinstance(obj, (list, tuple)):
+        return type(obj)(_map_tensors(v, fn) for v in obj)
+    return obj
+
+
+class HostOffloader:
+    """Device → host copies of forecast outputs, overlapped with later steps.
+
+    ``submit(obj)`` issues, for every CUDA tensor of ``obj``, a non-blocking
+    copy into a pinned staging block and records an event; a worker thread
+    waits for the event and moves the block into ordinary host memory.  The
+    staging block is then freed, and PyTorch's caching host allocator hands it
+    to a later copy once that copy's predecessor has completed — after the
+    first steps no new memory is page-locked (allocating fresh pinned memory
+    for every output costs more than the copy itself).  ``resolve`` waits and
+    returns the host objects in the structure that was submitted.
+    """
+
+    def __init__(self, workers: int = 2):
+        self._pool = ThreadPoolExecutor(max_workers=workers, thread_name_prefix="tgcm-offload")
+
+    def _one(self, t):
+        if not (isinstance(t, torch.Tensor) and t.is_cuda):
+            done: Future = Future()
+            done.set_result(t)
+            return done
+        stage = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+        stage.copy_(t, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+
+        def finish(stage=stage, ev=ev):
+            ev.synchronize()
+            out = torch.empty(stage.shape, dtype=stage.dtype)  # pageable
+            out.copy_(stage)
+            return out  # the pinned block returns to the allocator's cache
+
+        return self._pool.submit(finish)
+
+    def submit(self, obj: Any) -> Any:
+        return _map_tensors(obj, self._one)
+
+    def resolve(self, obj: Any) -> Any:
+        return _map_tensors(obj, lambda f: f.result() if isinstance(f, Future) else f)
+
+    def close(self) -> None:
+        self._pool.shutdown(wait=True)
 
 
 def _has_nan(obj: Any) -> bool:
@@ -190,6 +247,9 @@ class MPInference:
         ckpt = None
         retries = 0
         device = state.vorticity.device if hasattr(state, "vorticity") else None
+        off = (HostOffloader() if async_offload and torch.device(offload_device).type == "cpu"
+               and torch.cuda.is_available() else None)
+        keep = (lambda o: off.submit(o)) if off is not None else (lambda o: _offload(o, offload_device, async_offload))
         while step < outer_steps:
             if checkpoint_interval > 0 and step % checkpoint_interval == 0:
                 ckpt = (step, _offload(state, "cpu", False))
@@ -211,10 +271,13 @@ class MPInference:
                 if on_step_fn is not None:
                     on_step_fn(gstep, out)
                 if keep_steps is None or gstep in keep_steps:
-                    saved.append((gstep, _offload(out, offload_device, async_offload)))
+                    saved.append((gstep, keep(out)))
             if reverted:
                 continue
             step += n
+        if off is not None:
+            saved = [(g, off.resolve(v)) for g, v in saved]
+            off.close()
         if torch.cuda.is_available():
             torch.cuda.synchronize()
         return state, saved
@@ -237,11 +300,16 @@ class MPInference:
         if decode and self.hybrid is not None:
             nf = self.hybrid.normalize_forcings(f) if f else {}
             dec = (lambda s: self.hybrid.decoder(s, nf))
-        _, traj = self._unroll(state, steps, None, f, dec)
-        if offload:
-            traj = [_offload(t, "cpu", True) for t in traj]
-            if torch.cuda.is_available():
-                torch.cuda.synchronize()
+        off = HostOffloader() if offload and torch.cuda.is_available() else None
+        post = dec
+        if off is not None:  # each 6-h output leaves the GPU while the next steps run
+            post = (lambda s: off.submit(dec(s) if dec is not None else s))
+        _, traj = self._unroll(state, steps, None, f, post)
+        if off is not None:
+            traj = [off.resolve(t) for t in traj]
+            off.close()
+        elif offload:
+            traj = [_offload(t, "cpu", False) for t in traj]
         return traj
 
     def audit(self) -> dict:

@@ -26,6 +26,7 @@ from typing import Optional
 import numpy as np
 import torch
 import torch.nn as nn
+import torch.utils.checkpoint as torch_checkpoint
 
 from tornado_gcm_b200.core import coordinate_systems, sigma_coordinates, spherical_harmonic
 from tornado_gcm_b200.models.api import ModelConfig, NeuralGCMModel
@@ -82,6 +83,9 @@ class HybridGCM(nn.Module):
         self.physics_steps_per_output = physics_steps_per_output
         self.forcing_keys = tuple(forcing_keys)
         self._forcing_scale = forcing_scale or {}
+        # recompute each 6-h block of physics steps in backward instead of keeping its
+        # activations (the reference's checkpoint_outer_steps, model/api.py:788)
+        self.checkpoint_outer_steps = False
 
     def normalize_forcings(self, forcings: dict) -> dict:
         out = {}
@@ -90,13 +94,35 @@ class HybridGCM(nn.Module):
             out[k] = (v - off) * sc
         return out
 
-    def rollout(self, data0: dict, forcings: dict, outer_steps: int, decode: bool = True):
+    def _outer_block(self, state, f, start: int):
+        # The step counter drives the fixer cadence: a recompute in backward runs
+        # with the counter the forward pass saw and leaves the current one alone.
+        # (A recompute may also stop early, once the tensors it needs exist.)
+        m = self.model
+        before = m._step_count
+        m._step_count = start
+        try:
+            for _ in range(self.physics_steps_per_output):
+                state = m.step(state, f)
+        finally:
+            m._step_count = max(before, start + self.physics_steps_per_output)
+        return state
+
+    def rollout(self, data0: dict, forcings: dict, outer_steps: int, decode: bool = True,
+                checkpoint_outer_steps: Optional[bool] = None):
+        ckpt = self.checkpoint_outer_steps if checkpoint_outer_steps is None else checkpoint_outer_steps
         f = self.normalize_forcings(forcings)
         state = self.encoder(data0, f)
         outs = []
         for _ in range(outer_steps):
-            for _ in range(self.physics_steps_per_output):
-                state = self.model.step(state, f)
+            if ckpt and torch.is_grad_enabled():
+                # no RNG state capture: the step draws no random numbers, and reading the
+                # generator state is not allowed inside CUDA-graph capture
+                state = torch_checkpoint.checkpoint(self._outer_block, state, f, self.model._step_count,
+                                                    use_reentrant=False, preserve_rng_state=False)
+            else:
+                for _ in range(self.physics_steps_per_output):
+                    state = self.model.step(state, f)
             outs.append(self.decoder(state, f) if decode else state)
         return state, outs
 

@@ -89,12 +89,20 @@ def _synth(x3: torch.Tensor, b: _Bases, col_scale=None, lat_major: bool = False,
 
 def _anal(n3: torch.Tensor, b: _Bases, col_scale=None, lat_major: bool = False,
           weighted: bool = False) -> torch.Tensor:
-    """Nodal (S, I, J) (or (S, J, I) when lat_major) → modal (S, M2, L)."""
+    """Nodal (S, I, J) (or (S, J, I) when lat_major) → modal (S, M2, L).
+
+    The lat-major (internal) result is the ``[..., :L]`` view of rows padded
+    to ``Lp`` (a multiple of 4): the Legendre epilogue then stores whole
+    16-byte vectors, and the spectral operators that consume it take strided
+    rows.  The public lon-major result stays contiguous.
+    """
     ops = _ext.require("spherical-harmonic analysis")
     S = n3.shape[0]
     ws = _ext.empty(S * b.M2 * b.J, dtype=torch.float32, device=n3.device)
-    return ops.sht_anal(n3.float(), b.Ft, b.Ptw if weighted else b.Pt, b.L, ws, col_scale,
-                        _ext.error_flag(n3.device), lat_major)
+    lo = b.Lp if lat_major else b.L
+    out = ops.sht_anal(n3.float(), b.Ft, b.Ptw if weighted else b.Pt, lo, ws, col_scale,
+                       _ext.error_flag(n3.device), lat_major)
+    return out[..., : b.L] if lo != b.L else out
 
 
 class ToNodalFn(torch.autograd.Function):
