@@ -67,6 +67,8 @@ def parse_args():
     p.add_argument("--members", type=int, default=16, help="forecast: ensemble members per GPU")
     p.add_argument("--checkpoint", choices=["auto", "on", "off"], default="auto",
                    help="train: recompute each 6-h block in backward (auto: on above 2.8 degrees)")
+    p.add_argument("--checkpoint-segment", type=int, default=-1,
+                   help="physics steps per recomputed segment (0: whole 6-h block; default 8 at 0.7 degrees)")
     p.add_argument("--batch", type=int, default=4, help="per-GPU batch")
     p.add_argument("--rollout", type=int, default=4, help="6-h steps per training example")
     p.add_argument("--no-graph", action="store_true")
@@ -212,6 +214,8 @@ def run_b200(args, rank, world):
     spec = RESOLUTIONS[args.resolution]
     gcm.checkpoint_outer_steps = (args.checkpoint == "on" or
                                   (args.checkpoint == "auto" and args.resolution not in ("2.8deg", "5.6deg")))
+    gcm.checkpoint_segment = args.checkpoint_segment if args.checkpoint_segment >= 0 else (
+        8 if args.resolution == "0.7deg" else 0)
     trainer = GCMTrainer(gcm, lr=1e-4, graph=not args.no_graph, data_parallel=world > 1)
     B, K = args.batch, args.rollout
     enc = gcm.encoder
@@ -322,7 +326,9 @@ def run_b200(args, rank, world):
                 "parallelism": f"dp{world}",
                 "zones": "Z1 TF32 tcgen05 transforms, Z3 BF16 tcgen05 towers, Z2 FP64-accumulated fixer",
                 "cuda_graph": trainer.use_graph,
-                "activation_checkpointing": "per 6-h block" if gcm.checkpoint_outer_steps else "none",
+                "activation_checkpointing": ("none" if not gcm.checkpoint_outer_steps else
+                                             f"segments of {gcm.checkpoint_segment} physics steps"
+                                             if gcm.checkpoint_segment else "per 6-h block"),
                 "l2": f"working set per step (activations of {K * spec.physics_steps_per_output} physics steps) "
                       "far exceeds the 126 MB L2",
                 "loss": loss_last,

@@ -209,8 +209,12 @@ def test_checkpointed_outer_steps_give_the_same_gradients():
 
     l0, g0, n0 = grads(False)
     l1, g1, n1 = grads(True)
+    gcm.checkpoint_segment = 2  # segments of 2 and 1 physics steps per 3-step block
+    l2, g2, n2 = grads(True)
     gcm.checkpoint_outer_steps = False
-    assert l0 == pytest.approx(l1, rel=1e-6)
-    assert n0 == n1 == 2 * gcm.physics_steps_per_output  # recompute leaves the fixer counter alone
-    for a, b in zip(g0, g1):
+    gcm.checkpoint_segment = 0
+    assert l0 == pytest.approx(l1, rel=1e-6) and l0 == pytest.approx(l2, rel=1e-6)
+    assert n0 == n1 == n2 == 2 * gcm.physics_steps_per_output  # recompute leaves the fixer counter alone
+    for a, b, c in zip(g0, g1, g2):
         torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-7)
+        torch.testing.assert_close(a, c, rtol=1e-5, atol=1e-7)

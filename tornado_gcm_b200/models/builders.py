@@ -86,6 +86,9 @@ class HybridGCM(nn.Module):
         # recompute each 6-h block of physics steps in backward instead of keeping its
         # activations (the reference's checkpoint_outer_steps, model/api.py:788)
         self.checkpoint_outer_steps = False
+        # physics steps per recomputed segment (0: the whole 6-h block); at 0.7° one
+        # physics step keeps ~2 GB of tower activations, so a 72-step block does not fit
+        self.checkpoint_segment = 0
 
     def normalize_forcings(self, forcings: dict) -> dict:
         out = {}
@@ -94,7 +97,7 @@ class HybridGCM(nn.Module):
             out[k] = (v - off) * sc
         return out
 
-    def _outer_block(self, state, f, start: int):
+    def _segment(self, state, f, start: int, n: int):
         # The step counter drives the fixer cadence: a recompute in backward runs
         # with the counter the forward pass saw and leaves the current one alone.
         # (A recompute may also stop early, once the tensors it needs exist.)
@@ -102,10 +105,10 @@ class HybridGCM(nn.Module):
         before = m._step_count
         m._step_count = start
         try:
-            for _ in range(self.physics_steps_per_output):
+            for _ in range(n):
                 state = m.step(state, f)
         finally:
-            m._step_count = max(before, start + self.physics_steps_per_output)
+            m._step_count = max(before, start + n)
         return state
 
     def rollout(self, data0: dict, forcings: dict, outer_steps: int, decode: bool = True,
@@ -118,8 +121,14 @@ class HybridGCM(nn.Module):
             if ckpt and torch.is_grad_enabled():
                 # no RNG state capture: the step draws no random numbers, and reading the
                 # generator state is not allowed inside CUDA-graph capture
-                state = torch_checkpoint.checkpoint(self._outer_block, state, f, self.model._step_count,
-                                                    use_reentrant=False, preserve_rng_state=False)
+                n_phys = self.physics_steps_per_output
+                seg = self.checkpoint_segment if self.checkpoint_segment > 0 else n_phys
+                done = 0
+                while done < n_phys:
+                    k = min(seg, n_phys - done)
+                    state = torch_checkpoint.checkpoint(self._segment, state, f, self.model._step_count, k,
+                                                        use_reentrant=False, preserve_rng_state=False)
+                    done += k
             else:
                 for _ in range(self.physics_steps_per_output):
                     state = self.model.step(state, f)
