@@ -379,7 +379,8 @@ def run_b200_forecast(args, rank, world):
     forc_host = {k: v.pin_memory() for k, v in data.forcings(M).items()}
     forc_dev = {k: v.to(dev) for k, v in forc_host.items()}
 
-    engine.rollout(ens, max(1, args.warmup), forcings=forc_dev)  # graph capture + warm-up
+    warm = engine.rollout(ens, max(1, args.warmup), forcings=forc_dev)  # graph capture + warm-up
+    finite = all(bool(torch.isfinite(v).all()) for v in warm[-1].values())
     torch.cuda.synchronize()
     _ext.check_error_flag(dev)
     sampler = ClockSampler(device_uuid()) if rank == 0 else None
@@ -443,6 +444,7 @@ def run_b200_forecast(args, rank, world):
                 "seq_len_meaning": "6-h forecast steps (one timed rollout)",
                 "parallelism": f"dp{world} (ensemble members over GPUs)",
                 "members_per_gpu": M, "perturbation": "GRF sigma=1 (normalised units), 1000 km",
+                "outputs_finite_after_warmup": finite,
                 "zones": "Z1 TF32 tcgen05 transforms, Z3 BF16 tcgen05 towers, Z2 FP64-accumulated fixer",
                 "cuda_graph": True,
                 "l2": "ensemble state and decoded outputs exceed the 126 MB L2",

@@ -378,3 +378,57 @@ def test_offloaded_rollout_matches_device_rollout():
             assert b[k].device.type == "cpu" and not b[k].is_pinned()
             torch.testing.assert_close(b[k], a[k].cpu(), rtol=1e-5, atol=1e-6)
 
+
+
+@pytest.mark.parametrize("B,C,J,I,F,ld", [(2, 49, 32, 64, 4, 56), (3, 193, 64, 128, 0, 200), (1, 7, 12, 20, 2, 16)])
+def test_nodal_token_layout_kernels_vs_torch(B, C, J, I, F, ld):
+    _require()
+    from tornado_gcm_b200.ops import tokens as tok_ops
+
+    g = torch.Generator().manual_seed(3)
+    nod = torch.randn(B, C, J, I, generator=g).to(DEV)
+    scale = torch.rand(C, J, generator=g).add(0.5).to(DEV)
+    ex = torch.randn(B * J * I, F, generator=g).to(DEV).to(torch.bfloat16) if F else None
+    tok = tok_ops.nodal_to_tokens(nod, scale, ex, ld)
+    ref = torch.zeros(B * J * I, ld, device=DEV)
+    ref[:, :C] = (nod * scale[None, :, :, None]).permute(0, 2, 3, 1).reshape(-1, C)
+    if F:
+        ref[:, C:C + F] = ex.float()
+    assert tok.dtype == torch.bfloat16 and tok.shape == (B * J * I, ld)
+    torch.testing.assert_close(tok.float(), ref.to(torch.bfloat16).float(), rtol=0, atol=0)
+    for dt in (torch.float32, torch.bfloat16):
+        t = torch.randn(B * J * I, ld, generator=g).to(DEV).to(dt)
+        back = tok_ops.tokens_to_nodal(t[:, :C], scale, B, J, I, ld)
+        want = t[:, :C].float().reshape(B, J, I, C).permute(0, 3, 1, 2) * scale[None, :, :, None]
+        torch.testing.assert_close(back, want, rtol=1e-6, atol=1e-6)
+
+
+def test_token_tower_path_matches_permuted_path():
+    _require()
+    from tornado_gcm_b200.models.builders import build_hybrid_gcm
+    from tornado_gcm_b200.ops import spectral
+
+    gcm, data = build_hybrid_gcm("5.6deg", DEV)
+    param = gcm.model.parameterization
+    f = gcm.normalize_forcings({k: v.to(DEV) for k, v in data.forcings(2).items()})
+    enc = gcm.encoder
+    x0 = {k: ((v.to(DEV) - getattr(enc, f"mean_{k}")) / getattr(enc, f"std_{k}")) for k, v in data.sample(2, 0).items()}
+    with torch.no_grad():
+        s0 = gcm.encoder(x0, f)
+    keys = sorted(s0.tracers)
+    y = torch.cat([s0.vorticity, s0.divergence, s0.temperature_variation, s0.log_surface_pressure]
+                  + [s0.tracers[k] for k in keys], dim=-3).detach().requires_grad_(True)
+    outs = {}
+    for use in (True, False):
+        param._token_path_ok = (lambda nod, u=use: u and type(param)._token_path_ok(param, nod))
+        y.grad = None
+        for p in param.parameters():
+            p.grad = None
+        out = param.forward_packed(y, keys, f)
+        (out.float() ** 2).sum().backward()
+        outs[use] = (out.detach().clone(), y.grad.clone(), [p.grad.clone() for p in param.parameters() if p.grad is not None])
+    del param._token_path_ok
+    a, b = outs[True], outs[False]
+    assert _rel(a[0], b[0]) < 2e-2 and _rel(a[1], b[1]) < 3e-2
+    for ga, gb in zip(a[2], b[2]):
+        assert _rel(ga, gb) < 3e-2

@@ -212,6 +212,49 @@ class NodalColumnParameterization(nn.Module):
         fout[: 2 * n] = fout[: 2 * n] * sec
         return fin, fout
 
+    def _token_path_ok(self, nod: torch.Tensor) -> bool:
+        """The column tower can run on BF16 token rows (ops/tokens.py) instead of a permuted copy."""
+        from tornado_gcm_b200.neural.standard_layers import Mlp
+        from tornado_gcm_b200.neural.towers import ForwardTower
+        from tornado_gcm_b200.ops import linear as linear_ops
+
+        t = self.tower
+        if not (nod.is_cuda and isinstance(t, ForwardTower) and isinstance(t.neural_net, Mlp)
+                and t.final_activation is None and t.feature_axis % 4 == 1 and self.compute_dtype == torch.bfloat16):
+            return False
+        return None not in t.neural_net.layer_activations() and linear_ops.supports(nod, t.neural_net.layers)
+
+    def _lat_factors_2d(self, device):
+        """(C, J) fp32 input and output factors (cached per device)."""
+        cache = self.__dict__.setdefault("_latf2d", {})
+        key = (str(device), self.input_scale._version, self.output_scale._version)
+        ent = cache.get(key)
+        if ent is None:
+            fin, fout = self._lat_factors(device, torch.float32)
+            ent = (fin[..., 0].contiguous(), fout[..., 0].contiguous())
+            cache.clear()
+            cache[key] = ent
+        return ent
+
+    def _tower_tokens(self, nod, forcings, B: int, C: int, J: int, I: int) -> torch.Tensor:
+        """Column tower on BF16 token rows: scale + forcing columns + layout change in one kernel each way."""
+        from tornado_gcm_b200.ops import linear as linear_ops, tokens as tok_ops
+
+        net = self.tower.neural_net
+        nf = len(self.forcing_keys)
+        ld = (C + nf + 7) // 8 * 8
+        ex = None
+        if nf:
+            like = nod.new_empty((1, 1, I, J))
+            extra = _forcing_channels(forcings, like, (B,), self.forcing_keys)
+            if extra:  # (B, nf, I, J) → (B·J·I, nf) rows, input-scaled, BF16
+                f = torch.cat(extra, dim=-3) * self.input_scale[C:].to(nod.dtype)
+                ex = f.permute(0, 3, 2, 1).reshape(B * J * I, nf).to(torch.bfloat16).contiguous()
+        fin, fout = self._lat_factors_2d(nod.device)
+        tok = tok_ops.nodal_to_tokens(nod, fin, ex, ld)
+        hid = linear_ops.mlp_forward(tok, net.layers, net.layer_activations(), last_bf16=True)
+        return tok_ops.tokens_to_nodal(hid, fout, B, J, I, ld_grad=(C + 7) // 8 * 8)
+
     def forward_packed(self, y: torch.Tensor, state_keys, forcings=None) -> torch.Tensor:
         """Packed state ``(B, C, 2M-1, L)`` → packed tendency of the same layout.
 
@@ -232,6 +275,11 @@ class NodalColumnParameterization(nn.Module):
         xm = spectral.spectral_linear(y, pre, out_lpad=lp, grad_lpad=L)
         C = self.n_outputs
         nod = dyops._synth_lat(xm.reshape(B * C, M2, L), g).reshape(B, C, J, I)
+        if self._token_path_ok(nod):
+            out = self._tower_tokens(nod, forcings, B, C, J, I)
+            modal = dyops._anal_lat(out.reshape(B * C, J, I), g).reshape(B, C, M2, L)
+            res = spectral.spectral_linear(modal, post, out_lpad=L, grad_lpad=lp)
+            return self.filter_fn(res) if self.filter_fn is not None else res
         fin, fout = self._lat_factors(y.device, nod.dtype)
         x = nod * fin
         if self.forcing_keys:

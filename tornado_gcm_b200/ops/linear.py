@@ -68,6 +68,30 @@ class _WeightCache:
 _CACHE = _WeightCache()
 
 
+class _BiasCache:
+    """fp32 copies of Linear biases zero-padded to the padded output width (refreshed per step)."""
+
+    def __init__(self):
+        self.store = {}
+
+    def get(self, lin: nn.Linear, width: int):
+        b = lin.bias
+        key = id(lin)
+        ver = (b._version, b.data_ptr(), str(b.device))
+        ent = self.store.get(key)
+        if ent is not None and (ent[3]() is not lin or ent[2].shape[0] != width or ent[2].device != b.device):
+            ent = None
+        if ent is not None and ent[0] == ver and ent[1] == _CACHE.token:
+            return ent[2]
+        buf = ent[2] if ent is not None else torch.zeros(width, dtype=torch.float32, device=b.device)
+        buf[: b.shape[0]].copy_(b.detach())
+        self.store[key] = (ver, _CACHE.token, buf, weakref.ref(lin))
+        return buf
+
+
+_BIAS = _BiasCache()
+
+
 def begin_step() -> None:
     """Mark a new optimizer step: BF16 weight copies refresh on next use."""
     _CACHE.token += 1
@@ -75,24 +99,25 @@ def begin_step() -> None:
 
 class MlpFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x2d, acts, layers, *params):
+    def forward(ctx, x2d, acts, last_bf16, layers, *params):
         ops = _ext.require("column MLP")
         err = _ext.error_flag(x2d.device)
         T, K0 = x2d.shape
-        h = torch.zeros(T, _pad8(K0), dtype=torch.bfloat16, device=x2d.device)
-        h[:, :K0] = x2d
+        if x2d.dtype == torch.bfloat16 and K0 % 8 == 0 and x2d.is_contiguous():
+            h = x2d  # already BF16 rows of the padded width (token rows)
+        else:
+            h = torch.zeros(T, _pad8(K0), dtype=torch.bfloat16, device=x2d.device)
+            h[:, :K0] = x2d
         hs, zs, ws = [h], [], []
         n = len(layers)
         for i, lin in enumerate(layers):
             wp = _CACHE.get(lin)
             ws.append(wp)
             Op = wp.shape[0]
-            bias = None
-            if lin.bias is not None:
-                bias = torch.zeros(Op, dtype=torch.float32, device=x2d.device)
-                bias[: lin.bias.shape[0]] = lin.bias.detach().float()
+            bias = _BIAS.get(lin, Op) if lin.bias is not None else None
             last = i == n - 1
-            out = _ext.empty(T, Op, dtype=torch.float32 if last else torch.bfloat16, device=x2d.device)
+            out_dt = torch.bfloat16 if (not last or last_bf16) else torch.float32
+            out = _ext.empty(T, Op, dtype=out_dt, device=x2d.device)
             code = ACT_CODES[acts[i]]
             aux = _ext.empty(T, Op, dtype=torch.bfloat16, device=x2d.device) if (code and not last) else None
             ops.linear_fwd(hs[-1], wp, bias, code, out, aux, err)
@@ -113,8 +138,14 @@ class MlpFn(torch.autograd.Function):
         err = _ext.error_flag(g.device)
         T = g.shape[0]
         O_last = ctx.layers[-1].weight.shape[0]
-        dy = torch.zeros(T, ws[-1].shape[0], dtype=torch.bfloat16, device=g.device)
-        dy[:, :O_last] = g
+        Op_last = ws[-1].shape[0]
+        full = getattr(g, "_tgcm_zero_padded", None)
+        if (full is not None and full.dtype == torch.bfloat16 and tuple(full.shape) == (T, Op_last)
+                and full.is_contiguous() and full.data_ptr() == g.data_ptr()):
+            dy = full  # zero-padded BF16 rows written by the consumer's adjoint
+        else:
+            dy = torch.zeros(T, Op_last, dtype=torch.bfloat16, device=g.device)
+            dy[:, :O_last] = g
         grads = []
         dx_out = None
         for i in range(n - 1, -1, -1):
@@ -132,24 +163,28 @@ class MlpFn(torch.autograd.Function):
                 ops.linear_dgrad(dy, wp, dprev, prev if prev.numel() else None, code, err)
                 dy = dprev
             else:
-                dx = _ext.empty(T, wp.shape[1], dtype=torch.float32, device=g.device)
+                dx_dt = torch.bfloat16 if ctx.x_dtype == torch.bfloat16 else torch.float32
+                dx = _ext.empty(T, wp.shape[1], dtype=dx_dt, device=g.device)
                 ops.linear_dgrad(dy, wp, dx, None, 0, err)
-                dx_out = dx[:, : ctx.K0].to(ctx.x_dtype)
+                dx_out = dx[:, : ctx.K0] if ctx.K0 < dx.shape[1] else dx
+                if dx_out.dtype != ctx.x_dtype:
+                    dx_out = dx_out.to(ctx.x_dtype)
         grads.reverse()
         flat = []
         for lin, (gw, gb) in zip(ctx.layers, grads):
             flat.append(gw)
             if lin.bias is not None:
                 flat.append(gb)
-        return (dx_out, None, None) + tuple(flat)
+        return (dx_out, None, None, None) + tuple(flat)
 
 
-def mlp_forward(x: torch.Tensor, layers, acts) -> torch.Tensor:
+def mlp_forward(x: torch.Tensor, layers, acts, last_bf16: bool = False) -> torch.Tensor:
+    """The network on the last axis; ``last_bf16`` makes the final layer write BF16 (Z3 output)."""
     lead = x.shape[:-1]
     params = []
     for lin in layers:
         params.append(lin.weight)
         if lin.bias is not None:
             params.append(lin.bias)
-    out = MlpFn.apply(x.reshape(-1, x.shape[-1]), tuple(acts), tuple(layers), *params)
+    out = MlpFn.apply(x.reshape(-1, x.shape[-1]), tuple(acts), bool(last_bf16), tuple(layers), *params)
     return out.reshape(*lead, out.shape[-1])

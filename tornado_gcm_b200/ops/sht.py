@@ -153,11 +153,15 @@ def to_modal(x: torch.Tensor, sh) -> torch.Tensor:
 
 def to_nodal_lat_major(x3: torch.Tensor, sh) -> torch.Tensor:
     """(S, 2M-1, L) modal (may be a row-padded view) → (S, J, I) nodal (internal layout)."""
+    if sh.precision == "highest":
+        return _highest(x3, sh, inverse=True).transpose(-1, -2).contiguous()
     return ToNodalFn.apply(x3, bases(sh, x3.device), True)
 
 
 def to_modal_lat_major(n3: torch.Tensor, sh) -> torch.Tensor:
     """(S, J, I) nodal → (S, 2M-1, L) modal."""
+    if sh.precision == "highest":
+        return _highest(n3.transpose(-1, -2), sh, inverse=False)
     return ToModalFn.apply(n3, bases(sh, n3.device), True)
 
 
