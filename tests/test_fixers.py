@@ -91,6 +91,25 @@ def test_lite_fixer_matches_reference(ref):
     mk = lambda s: rpe.State(vorticity=s.vorticity, divergence=s.divergence, temperature_variation=s.temperature_variation,
                              log_surface_pressure=s.log_surface_pressure, tracers=s.tracers, sim_time=s.sim_time)
     r = rfix.LiteConservationFixer()(mk(st), mk(before))
-    out = fops.lite_fix(st.tree_map(lambda t: t[None]), before.tree_map(lambda t: t[None]))
+    out = fops.lite_fix(st.tree_map(lambda t: t[None]), before.tree_map(lambda t: t[None]), energy_split="reference")
     torch.testing.assert_close(out.temperature_variation[0], r.temperature_variation, rtol=1e-6, atol=1e-5)
     torch.testing.assert_close(out.log_surface_pressure[0], r.log_surface_pressure, rtol=1e-6, atol=1e-7)
+
+
+@needs_ext
+@pytest.mark.parametrize("n", [4, 32])
+def test_energy_split_restores_the_proxy_exactly(n):
+    """Splitting the deficit over the levels restores E exactly; the reference formula adds (n-1)·D too much."""
+    from tornado_gcm_b200.ops import fixers as fops
+
+    st = _state(6, n=n).tree_map(lambda t: t.float())
+    before = pe.State(st.vorticity * 3.0, st.divergence, st.temperature_variation, st.log_surface_pressure,
+                      st.tracers, 0.0)  # the step lost vorticity energy: deficit > 0
+    e = lambda s: fixers.compute_total_energy_lite(s)
+    D = e(before) - e(st)
+    assert bool((D > 0).all())
+    split = fops.lite_fix(st, before, False, True, "levels")
+    torch.testing.assert_close(e(split), e(before), rtol=1e-6, atol=0)
+    refm = fops.lite_fix(st, before, False, True, "reference")
+    torch.testing.assert_close(e(refm) - e(before), (n - 1) * D, rtol=1e-4, atol=0)
+

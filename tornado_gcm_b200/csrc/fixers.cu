@@ -5,8 +5,14 @@
 //   E(y)   = Σ over the first 3n channels of y²      (FP64)
 //   D      = E(y_before) − E(y)                      (energy deficit)
 //   mass   : ln ps(0,0) ← ln ps_before(0,0)
-//   energy : T'_k(0,0) ← sign(T'_k(0,0)) · sqrt(T'_k(0,0)² + D)  for every level k,
-//            applied only when T'_k(0,0)² + D > 0 for all k (else unchanged).
+//   energy : T'_k(0,0) ← sign(T'_k(0,0)) · sqrt(T'_k(0,0)² + s·D)  for every level k,
+//            applied only when T'_k(0,0)² + s·D > 0 for all k (else unchanged).
+//   s = 1/n (mode 2, the default of the Python classes) spreads the deficit
+//   over the n levels, so E(out) = E(y_before) exactly; s = 1 (mode 1) is the
+//   reference's formula, which adds the whole deficit at every level and so
+//   injects (n - 1)·D of spurious energy per step (the global-mean
+//   temperature modes grow until the state blows up in long rollouts with
+//   strong dissipation: at 1.4° with 32 levels, after about 21 hours).
 // This is the lite fixer of reference neural/fixers.py:228-326 (mass fix of
 // :113-143 followed by the energy fix of :146-190); squares are formed in
 // FP64, which is at least as accurate as the reference's input-precision
@@ -46,6 +52,7 @@ struct FixArgs {
   long long chan;      // M2 * L
   long long energy_n;  // 3n * M2 * L
   int n, B, fix_mass, fix_energy;
+  double dscale;       // share of the deficit added at each level (1/n or 1)
 };
 
 // Deficit and admissibility of sample b from the partial sums (fixed order).
@@ -55,7 +62,7 @@ __host__ __device__ inline void deficit_of(const FixArgs& a, int b, double* D, i
     e += a.part[(static_cast<long long>(b) * kFixBlocks + i) * 2 + 0];
     eb += a.part[(static_cast<long long>(b) * kFixBlocks + i) * 2 + 1];
   }
-  *D = eb - e;
+  *D = (eb - e) * a.dscale;  // increment of T'_k(0,0)^2 at each level
   int good = 1;
   const float* t00 = a.y + b * a.sample + 2LL * a.n * a.chan;
   for (int k = 0; k < a.n; ++k) {
@@ -111,7 +118,7 @@ __host__ __device__ inline double deficit_cotangent(const FixArgs& a, int b, dou
     const double s = sqrt(t * t + D);
     if (s > 0.0) gD += static_cast<double>(a.gout[i]) * sgn(t) / (2.0 * s);
   }
-  return gD;
+  return gD * a.dscale;  // cotangent of the raw deficit E(y_before) - E(y)
 }
 
 __device__ inline double block_sum(double v, double* sh) {
@@ -185,7 +192,8 @@ __global__ void __launch_bounds__(kFixThreads) fix_adjoint_kernel(FixArgs a) {
     adjoint_point(a, b, off, D, ok, gD);
 }
 
-FixArgs make_args(const at::Tensor& y, const at::Tensor& yb, int64_t n, bool fix_mass, bool fix_energy) {
+// fix_energy: 0 off, 1 whole deficit at every level (reference formula), 2 deficit split over the levels.
+FixArgs make_args(const at::Tensor& y, const at::Tensor& yb, int64_t n, bool fix_mass, int64_t fix_energy) {
   TORCH_CHECK(y.dim() == 4 && y.is_contiguous() && y.scalar_type() == at::kFloat, "packed state must be contiguous fp32 (B, C, M2, L)");
   TORCH_CHECK(yb.sizes() == y.sizes() && yb.is_contiguous() && yb.scalar_type() == at::kFloat, "before-state shape");
   TORCH_CHECK(n >= 1 && n <= kFixMaxLev && 3 * n + 1 <= y.size(1), "level count does not fit the packed channels");
@@ -199,7 +207,9 @@ FixArgs make_args(const at::Tensor& y, const at::Tensor& yb, int64_t n, bool fix
   a.energy_n = 3 * n * a.chan;
   a.n = static_cast<int>(n);
   a.fix_mass = fix_mass ? 1 : 0;
+  TORCH_CHECK(fix_energy >= 0 && fix_energy <= 2, "fix_energy: 0 off, 1 reference formula, 2 split over levels");
   a.fix_energy = fix_energy ? 1 : 0;
+  a.dscale = fix_energy == 2 ? 1.0 / static_cast<double>(n) : 1.0;
   return a;
 }
 
@@ -236,7 +246,7 @@ int apply_blocks(const FixArgs& a) {
 
 // Returns (fixed state, partial sums); the partial sums feed the backward.
 std::vector<at::Tensor> packed_fix(const at::Tensor& y, const at::Tensor& yb, int64_t n, bool fix_mass,
-                                   bool fix_energy) {
+                                   int64_t fix_energy) {
   c10::OptionalDeviceGuard guard(y.device());
   FixArgs a = make_args(y, yb, n, fix_mass, fix_energy);
   auto part = out_empty({a.B, kFixBlocks, 2}, y.options().dtype(at::kDouble));
@@ -258,7 +268,7 @@ std::vector<at::Tensor> packed_fix(const at::Tensor& y, const at::Tensor& yb, in
 }
 
 std::vector<at::Tensor> packed_fix_adjoint(const at::Tensor& gout, const at::Tensor& y, const at::Tensor& yb,
-                                           const at::Tensor& part, int64_t n, bool fix_mass, bool fix_energy,
+                                           const at::Tensor& part, int64_t n, bool fix_mass, int64_t fix_energy,
                                            bool need_before) {
   c10::OptionalDeviceGuard guard(y.device());
   FixArgs a = make_args(y, yb, n, fix_mass, fix_energy);
@@ -374,9 +384,9 @@ at::Tensor sum_squares(const at::Tensor& x, int64_t n_trailing) {
 TORCH_LIBRARY_FRAGMENT(tgcm, m) {
   m.def("sphere_integrate(Tensor z, Tensor w) -> Tensor");
   m.def("sum_squares(Tensor x, int n_trailing) -> Tensor");
-  m.def("packed_fix(Tensor y, Tensor y_before, int n, bool fix_mass, bool fix_energy) -> Tensor[]");
+  m.def("packed_fix(Tensor y, Tensor y_before, int n, bool fix_mass, int fix_energy) -> Tensor[]");
   m.def("packed_fix_adjoint(Tensor gout, Tensor y, Tensor y_before, Tensor part, int n, bool fix_mass, "
-        "bool fix_energy, bool need_before) -> Tensor[]");
+        "int fix_energy, bool need_before) -> Tensor[]");
 }
 
 TORCH_LIBRARY_IMPL(tgcm, CompositeExplicitAutograd, m) {

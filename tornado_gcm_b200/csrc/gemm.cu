@@ -462,7 +462,9 @@ void linear_wgrad(const at::Tensor& dY, const at::Tensor& X, at::Tensor& dW, int
   p.M = O; p.N = Kp; p.K = T; p.groups = 1;
   p.tiles_m = cdiv(O, 128); p.tiles_n = cdiv(Kp, bn);
   const int64_t kblocks = cdiv(T, 64);
-  int64_t sp = splits > 0 ? splits : std::max<int64_t>(1, 296 / (p.tiles_m * p.tiles_n));
+  // one wave of tiles: every split adds its partial tile into dW once, so fewer
+  // splits mean fewer reductions into the same addresses
+  int64_t sp = splits > 0 ? splits : std::max<int64_t>(1, 148 / (p.tiles_m * p.tiles_n));
   sp = std::min<int64_t>(sp, kblocks);
   p.k_splits = static_cast<int>(sp);
   p.beta = 1.f;

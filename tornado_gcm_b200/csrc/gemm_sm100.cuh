@@ -227,6 +227,68 @@ __device__ __forceinline__ void chunk_store_f32(const uint8_t* stage, float* g, 
   }
 }
 
+__device__ __forceinline__ void red_add_gpu_v4(float* addr, float4 v) {
+  asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}
+
+// Split-K partial sums of a 32 x 32 fp32 chunk added into global memory with
+// 16-byte reductions (eight lanes per row), from the staging tile.
+__device__ __forceinline__ void chunk_red_f32(const uint8_t* stage, float* g, long long ld, int nrows, int ncols,
+                                              int lane) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int v = lane + 32 * i;
+    const int row = v >> 3, seg = v & 7;
+    if (row >= nrows) continue;
+    const uint8_t* sp = stage + row * kStageRowF32 + seg * 16;
+    float* gp = g + row * ld + seg * 4;
+    if (seg * 4 + 4 <= ncols) {
+      red_add_gpu_v4(gp, *reinterpret_cast<const float4*>(sp));
+    } else {
+      const float* se = reinterpret_cast<const float*>(sp);
+      for (int e = 0; e < 4 && seg * 4 + e < ncols; ++e) atomicAdd(gp + e, se[e]);
+    }
+  }
+}
+
+// Epilogue of one 32-row x BN tile slice for split-K fp32 row-major C with
+// 16-byte aligned rows: alpha-scaled partial sums added with vector reductions
+// (the scalar atomics of the generic path made the weight-gradient GEMM bound
+// by the L2 atomic units: 16 384 atomics per tile, 32 partial tiles per output).
+template <int BN>
+__device__ __noinline__ void epilogue_splitk_red(const GemmParams& p, uint32_t taddr_row, uint8_t* stage, int tm,
+                                                    int tn, int g, int q, int half, int lane) {
+  const int row0 = tm * 128 + q * 32;
+  const int nrows = p.M - row0 < 32 ? p.M - row0 : 32;
+  uint8_t* my = stage + lane * kStageRowF32;
+#pragma unroll 1
+  for (int c0 = half * 32; c0 < BN; c0 += 64) {
+    const int ncolc = (BN - c0) >= 32 ? 32 : (BN - c0);
+    const int col0 = tn * BN + c0;
+    int ncols = p.N - col0;
+    if (ncols > ncolc) ncols = ncolc;
+#pragma unroll 1
+    for (int h = 0; h < ncolc; h += 16) {
+      uint32_t v[16];
+      tmem_ld_32x32b_x16(taddr_row + c0 + h, v);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 16; j += 4)
+        *reinterpret_cast<float4*>(my + 4 * (h + j)) =
+            make_float4(__uint_as_float(v[j]) * p.alpha, __uint_as_float(v[j + 1]) * p.alpha,
+                        __uint_as_float(v[j + 2]) * p.alpha, __uint_as_float(v[j + 3]) * p.alpha);
+    }
+    if (ncols <= 0 || nrows <= 0) continue;
+    __syncwarp();
+    chunk_red_f32(stage, reinterpret_cast<float*>(p.C) + static_cast<long long>(g) * p.c_sg +
+                             static_cast<long long>(row0) * p.c_sr + col0,
+                  p.c_sr, nrows, ncols, lane);
+    __syncwarp();
+  }
+}
+
 // act(x) / act'(pre) on a 32-value chunk; the switch is warp-uniform and sits
 // outside the element loops, so one epilogue instance serves every activation
 // (six inlined instances of the whole epilogue made the kernel spill).
@@ -659,7 +721,14 @@ __device__ __forceinline__ void gemm_sm100_body(const CUtensorMap& tmap_a, const
                                       (p.c_sg * 2) % 16 == 0)) &&
                           (!p.grad_pre || (reinterpret_cast<uintptr_t>(p.grad_pre) % 16 == 0 &&
                                            (p.c_sr * 2) % 16 == 0 && (p.c_sg * 2) % 16 == 0));
-      if (p.c_pair && p.c_sc == 1 && plain) {
+      const bool red_ok = p.k_splits > 1 && !p.c_pair && p.c_sc == 1 && p.c_sr != 1 && !p.bias && !p.col_scale &&
+                          !p.aux && !p.grad_pre && p.act == 0 && !p.out_bf16 && p.n_peers == 0 &&
+                          (reinterpret_cast<uintptr_t>(p.C) % 16 == 0) && ((p.c_sr * 4) % 16 == 0) &&
+                          ((p.c_sg * 4) % 16 == 0);
+      if (red_ok) {
+        uint8_t* stage = reinterpret_cast<uint8_t*>(staging) + (warp - 2) * (32 * kStageRowF32);
+        epilogue_splitk_red<BN>(p, taddr_row, stage, tm, tn, g, q, half, lane);
+      } else if (p.c_pair && p.c_sc == 1 && plain) {
         uint8_t* stage = reinterpret_cast<uint8_t*>(staging) + (warp - 2) * (32 * kStageRowF32);
         epilogue_pair_rows<BN>(p, taddr_row, stage, tm, tn, g, q, half, lane);
       } else if (vec_ok) {

@@ -88,10 +88,20 @@ def _mass_fix(state: State, before: State) -> State:
     return State(state.vorticity, state.divergence, state.temperature_variation, new, state.tracers, state.sim_time)
 
 
-def _energy_fix(state: State, deficit: torch.Tensor) -> State:
+def _energy_fix(state: State, deficit: torch.Tensor, energy_split: str = "levels") -> State:
+    """Restore the energy proxy through the T'(0,0) mode of every level.
+
+    ``energy_split="levels"`` adds deficit / n to each level's T'(0,0)² (the
+    proxy is then restored exactly).  ``"reference"`` is the formula of
+    reference ``neural/fixers.py:171-190`` / ``:309-321``, which adds the whole
+    deficit at every level, i.e. n times the deficit in total: with strong
+    dissipation the global-mean temperature modes then grow until the state
+    fails (1.4°, 32 levels: after about 21 simulated hours).
+    """
     t = state.temperature_variation
     t00 = t[..., 0, 0].to(torch.float64)  # (..., levels)
-    disc = t00 * t00 + deficit.unsqueeze(-1)
+    share = deficit / t00.shape[-1] if energy_split == "levels" else deficit
+    disc = t00 * t00 + share.unsqueeze(-1)
     ok = (disc > 0).all(dim=-1, keepdim=True)
     delta = -t00 + torch.sign(t00) * torch.sqrt(torch.clamp(disc, min=0.0))
     delta = torch.where(ok, delta, torch.zeros_like(delta))
@@ -106,19 +116,24 @@ class GlobalDryAirMassFixer(nn.Module):
 
 
 class GlobalEnergyFixer(nn.Module):
+    def __init__(self, energy_split: str = "levels"):
+        super().__init__()
+        self.energy_split = energy_split
+
     def forward(self, state: State, state_before: State) -> State:
         deficit = compute_total_energy(state_before).to(torch.float64) - compute_total_energy(state).to(torch.float64)
-        return _energy_fix(state, deficit)
+        return _energy_fix(state, deficit, self.energy_split)
 
 
 class F64ConservationFixer(nn.Module):
     """Mass then energy fix; the caller casts the state to the Z2 dtype first."""
 
-    def __init__(self, fix_mass: bool = True, fix_energy: bool = True, dtype: torch.dtype = torch.float64):
+    def __init__(self, fix_mass: bool = True, fix_energy: bool = True, dtype: torch.dtype = torch.float64,
+                 energy_split: str = "levels"):
         super().__init__()
         self.dtype = dtype
         self.mass_fixer = GlobalDryAirMassFixer() if fix_mass else None
-        self.energy_fixer = GlobalEnergyFixer() if fix_energy else None
+        self.energy_fixer = GlobalEnergyFixer(energy_split) if fix_energy else None
 
     def forward(self, state: State, state_before: State) -> State:
         if self.mass_fixer is not None:
@@ -134,10 +149,11 @@ class LiteConservationFixer(nn.Module):
     On CUDA this is one fused kernel (:func:`tornado_gcm_b200.ops.fixers.lite_fix`).
     """
 
-    def __init__(self, fix_mass: bool = True, fix_energy: bool = True):
+    def __init__(self, fix_mass: bool = True, fix_energy: bool = True, energy_split: str = "levels"):
         super().__init__()
         self.fix_mass = fix_mass
         self.fix_energy = fix_energy
+        self.energy_split = energy_split  # "levels" (exact) or "reference" (see _energy_fix)
 
     @property
     def bypass_upcast(self) -> bool:
@@ -147,16 +163,16 @@ class LiteConservationFixer(nn.Module):
         """Fix a packed ``[ζ | δ | T' | ln ps | …]`` state (differentiable kernel pair)."""
         from tornado_gcm_b200.ops import fixers as fixer_ops
 
-        return fixer_ops.packed_fix(y, y_before, n, self.fix_mass, self.fix_energy)
+        return fixer_ops.packed_fix(y, y_before, n, self.fix_mass, self.fix_energy, self.energy_split)
 
     def forward(self, state: State, state_before: State) -> State:
         if state.vorticity.is_cuda:
             from tornado_gcm_b200.ops import fixers as fixer_ops
 
-            return fixer_ops.lite_fix(state, state_before, self.fix_mass, self.fix_energy)
+            return fixer_ops.lite_fix(state, state_before, self.fix_mass, self.fix_energy, self.energy_split)
         if self.fix_mass:
             state = _mass_fix(state, state_before)
         if self.fix_energy:
             deficit = compute_total_energy_lite(state_before) - compute_total_energy_lite(state)
-            state = _energy_fix(state, deficit)
+            state = _energy_fix(state, deficit, self.energy_split)
         return state

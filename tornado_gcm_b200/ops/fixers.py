@@ -24,7 +24,7 @@ def available() -> bool:
 
 class PackedFixFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, y, y_before, n: int, fix_mass: bool, fix_energy: bool):
+    def forward(ctx, y, y_before, n: int, fix_mass: bool, fix_energy: int):
         ops = _ext.require("conservation fixer")
         y = y.contiguous()
         y_before = y_before.contiguous()
@@ -43,15 +43,25 @@ class PackedFixFn(torch.autograd.Function):
         return res[0], (res[1] if need_b else None), None, None, None
 
 
+ENERGY_SPLIT = {"levels": 2, "reference": 1}
+
+
 def packed_fix(y: torch.Tensor, y_before: torch.Tensor, n: int, fix_mass: bool = True,
-               fix_energy: bool = True) -> torch.Tensor:
-    """Packed ``[ζ | δ | T' | ln ps | …]`` state with mass and energy restored to ``y_before``'s."""
+               fix_energy: bool = True, energy_split: str = "levels") -> torch.Tensor:
+    """Packed ``[ζ | δ | T' | ln ps | …]`` state with mass and energy restored to ``y_before``'s.
+
+    ``energy_split="levels"`` adds 1/n of the energy deficit to each level's
+    T'(0,0)², which restores the energy proxy exactly; ``"reference"`` adds the
+    whole deficit at every level, as reference ``neural/fixers.py:309-321``
+    does (n times the deficit in total).
+    """
     if not (fix_mass or fix_energy):
         return y
-    return PackedFixFn.apply(y, y_before, int(n), bool(fix_mass), bool(fix_energy))
+    mode = ENERGY_SPLIT[energy_split] if fix_energy else 0
+    return PackedFixFn.apply(y, y_before, int(n), bool(fix_mass), mode)
 
 
-def lite_fix(state, state_before, fix_mass: bool = True, fix_energy: bool = True):
+def lite_fix(state, state_before, fix_mass: bool = True, fix_energy: bool = True, energy_split: str = "levels"):
     """:class:`State` version of :func:`packed_fix` (tracers pass through)."""
     from tornado_gcm_b200.core.primitive_equations import State
 
@@ -63,7 +73,7 @@ def lite_fix(state, state_before, fix_mass: bool = True, fix_energy: bool = True
         x = torch.cat([p.float() for p in parts], dim=-3)
         return x.reshape(-1, *x.shape[-3:])
 
-    out = packed_fix(pack(state), pack(state_before), n, fix_mass, fix_energy)
+    out = packed_fix(pack(state), pack(state_before), n, fix_mass, fix_energy, energy_split)
     out = out.reshape(*lead, *out.shape[-3:]).to(state.vorticity.dtype)
     return State(out[..., :n, :, :], out[..., n:2 * n, :, :], out[..., 2 * n:3 * n, :, :],
                  out[..., 3 * n:3 * n + 1, :, :], state.tracers, state.sim_time)
