@@ -852,8 +852,12 @@ __device__ __forceinline__ void mv_group(const Mat& M, const float (&xo)[P], flo
 // instead of 3 x N (occupancy) while the arithmetic is that of
 // stage_column_fwd / stage_column_adj.  A warp covers 8 consecutive l of one
 // (b, m) row: every channel access is a 32-byte run per quarter.
+// Four blocks per SM (64 registers, a 104-byte spill): at batch 4 on TL63 the
+// 516 blocks of a launch then run in one wave instead of 1.16 waves of three
+// blocks per SM (80 registers); the latency-bound kernel went from 53.8 to
+// 38.0 ms per training step.
 template <int N>
-__global__ void __launch_bounds__(256) sil3_stage_q4_kernel(StageArgs a, int adjoint) {
+__global__ void __launch_bounds__(256, 4) sil3_stage_q4_kernel(StageArgs a, int adjoint) {
   constexpr int Q = 4;
   constexpr int P = N / Q;
   constexpr int LD = N + 1;  // padded row stride of G, H in shared memory (conflict-free)
