@@ -102,7 +102,7 @@ def test_sht_roundtrip_vs_fp64(name, S):
     assert _ext.check_error_flag(torch.device(DEV)) == 0
 
 
-@pytest.mark.parametrize("name,S", [("TL63", 7), ("TL127", 5)])
+@pytest.mark.parametrize("name,S", [("TL63", 7), ("TL127", 5), ("TL63", 1292)])  # 1292: 192-wide DFT tiles
 def test_sht_lat_major_roundtrip(name, S):
     _require()
     from tornado_gcm_b200.ops import sht as sht_ops

@@ -191,7 +191,9 @@ static void gemm_dispatch(int fmt, int bn, bool a_mn, bool b_mn, const CUtensorM
   TGCM_CASE(2, 144, false, false)
   TGCM_CASE(2, 64, false, true)
   TGCM_CASE(2, 128, false, true)
+  TGCM_CASE(2, 192, false, true)
   TGCM_CASE(2, 256, false, true)
+  TGCM_CASE(2, 192, false, false)
   TGCM_CASE(1, 64, false, false)
   TGCM_CASE(1, 128, false, false)
   TGCM_CASE(1, 64, false, true)
@@ -218,6 +220,34 @@ static int* err_ptr(const c10::optional<at::Tensor>& err) {
 }
 
 static int pick_bn_j(int64_t j) { return j <= 64 ? 64 : (j <= 128 ? 128 : 256); }
+
+static int sm_count() {
+  static int sms[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64) return 148;
+  if (sms[dev] == 0) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  return sms[dev] > 0 ? sms[dev] : 148;
+}
+
+// Tile width for the one-GEMM Fourier transforms (N = S·J columns): the
+// persistent grid runs ceil(tiles / SMs) rounds, so the width that minimises
+// rounds x width wastes least of the last round (S·J = 82 688 on 148 SMs:
+// 256 -> 2.18 rounds run as 3; 192 -> 2.91 rounds).
+static int pick_bn_wide(int64_t n_cols, int64_t tiles_m) {
+  const int64_t sms = sm_count();
+  int best = 256;
+  int64_t best_cost = -1;
+  for (int bn : {256, 192, 128}) {
+    const int64_t tiles = tiles_m * ((n_cols + bn - 1) / bn);
+    const int64_t cost = ((tiles + sms - 1) / sms) * bn;
+    if (best_cost < 0 || cost < best_cost) {
+      best = bn;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
 static int pick_bn_l(int64_t l) { return l <= 80 ? 80 : 144; }
 static int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
@@ -266,10 +296,12 @@ at::Tensor sht_synth(const at::Tensor& x, int64_t L, const at::Tensor& P, const 
     CUtensorMap tb = make_tmap(ws.data_ptr(), 2, S * J, M2, 1, S * J * 4, M2 * S * J * 4, 32, 32, 1, 1);
     GemmParams p = default_params();
     p.M = I; p.N = S * J; p.K = M2; p.groups = 1;
-    p.tiles_m = cdiv(I, 128); p.tiles_n = cdiv(S * J, 256);
+    p.tiles_m = cdiv(I, 128);
+    const int bnw = pick_bn_wide(S * J, p.tiles_m);
+    p.tiles_n = cdiv(S * J, bnw);
     p.C = out.data_ptr(); p.c_sg = 0; p.c_sr = 1; p.c_sc = I;
     p.err = err_ptr(err);
-    gemm_dispatch(2, 256, false, true, ta, tb, p, st);
+    gemm_dispatch(2, bnw, false, true, ta, tb, p, st);
   } else {
     // one GEMM per slice s: B[j][k] = W[k][s·J + j] (MN-major, batch coordinate s)
     CUtensorMap ta = make_tmap(F.data_ptr(), 2, M2, I, 1, M2p * 4, I * M2p * 4, 32, 128, 1);
@@ -317,14 +349,16 @@ at::Tensor sht_anal(const at::Tensor& N_in, const at::Tensor& Ft, const at::Tens
   //    scale (w_j) it is S grouped GEMMs storing (S, M2, J).
   const bool one_gemm = !(col_scale.has_value() && col_scale->defined());
   if (one_gemm) {
+    const int64_t tm_a = cdiv(M2, 128);
+    const int bnw = pick_bn_wide(S * J, tm_a);
     CUtensorMap ta = make_tmap(Ft.data_ptr(), 2, I, M2, 1, I * 4, M2 * I * 4, 32, 128, 1);
-    CUtensorMap tb = make_tmap(N.data_ptr(), 2, I, S * J, 1, I * 4, S * J * I * 4, 32, 256, 1);
+    CUtensorMap tb = make_tmap(N.data_ptr(), 2, I, S * J, 1, I * 4, S * J * I * 4, 32, bnw, 1);
     GemmParams p = default_params();
     p.M = M2; p.N = S * J; p.K = I; p.groups = 1;
-    p.tiles_m = cdiv(M2, 128); p.tiles_n = cdiv(S * J, 256);
+    p.tiles_m = tm_a; p.tiles_n = cdiv(S * J, bnw);
     p.C = ws.data_ptr(); p.c_sg = 0; p.c_sr = S * J; p.c_sc = 1;
     p.err = err_ptr(err);
-    gemm_dispatch(2, 256, false, false, ta, tb, p, st);
+    gemm_dispatch(2, bnw, false, false, ta, tb, p, st);
   } else {
     CUtensorMap ta = make_tmap(Ft.data_ptr(), 2, I, M2, 1, I * 4, M2 * I * 4, 32, 128, 1);
     CUtensorMap tb = make_tmap(N.data_ptr(), 2, I, J, S, I * 4, J * I * 4, 32, bnj, 1);
