@@ -260,14 +260,20 @@ __device__ __forceinline__ void chunk_red_f32(const uint8_t* stage, float* g, lo
 template <int BN>
 __device__ __noinline__ void epilogue_splitk_red(const GemmParams& p, uint32_t taddr_row, uint8_t* stage, int tm,
                                                     int tn, int g, int q, int half, int lane) {
+  // parameters in registers (see epilogue_pair_rows)
+  const int N = p.N;
+  const float alpha = p.alpha;
+  const long long c_sr = p.c_sr;
   const int row0 = tm * 128 + q * 32;
   const int nrows = p.M - row0 < 32 ? p.M - row0 : 32;
+  float* __restrict__ Cb = reinterpret_cast<float*>(p.C) + static_cast<long long>(g) * p.c_sg +
+                           static_cast<long long>(row0) * c_sr;
   uint8_t* my = stage + lane * kStageRowF32;
 #pragma unroll 1
   for (int c0 = half * 32; c0 < BN; c0 += 64) {
     const int ncolc = (BN - c0) >= 32 ? 32 : (BN - c0);
     const int col0 = tn * BN + c0;
-    int ncols = p.N - col0;
+    int ncols = N - col0;
     if (ncols > ncolc) ncols = ncolc;
 #pragma unroll 1
     for (int h = 0; h < ncolc; h += 16) {
@@ -277,14 +283,12 @@ __device__ __noinline__ void epilogue_splitk_red(const GemmParams& p, uint32_t t
 #pragma unroll
       for (int j = 0; j < 16; j += 4)
         *reinterpret_cast<float4*>(my + 4 * (h + j)) =
-            make_float4(__uint_as_float(v[j]) * p.alpha, __uint_as_float(v[j + 1]) * p.alpha,
-                        __uint_as_float(v[j + 2]) * p.alpha, __uint_as_float(v[j + 3]) * p.alpha);
+            make_float4(__uint_as_float(v[j]) * alpha, __uint_as_float(v[j + 1]) * alpha,
+                        __uint_as_float(v[j + 2]) * alpha, __uint_as_float(v[j + 3]) * alpha);
     }
     if (ncols <= 0 || nrows <= 0) continue;
     __syncwarp();
-    chunk_red_f32(stage, reinterpret_cast<float*>(p.C) + static_cast<long long>(g) * p.c_sg +
-                             static_cast<long long>(row0) * p.c_sr + col0,
-                  p.c_sr, nrows, ncols, lane);
+    chunk_red_f32(stage, Cb + col0, c_sr, nrows, ncols, lane);
     __syncwarp();
   }
 }
@@ -407,21 +411,26 @@ __device__ __forceinline__ void epilogue_rowmajor_vec(const GemmParams& p, int A
 template <int BN>
 __device__ __noinline__ void epilogue_pair_rows(const GemmParams& p, uint32_t taddr_row, uint8_t* stage, int tm,
                                                    int tn, int g, int q, int half, int lane) {
-  const int S = p.M / 2;
-  const bool vec = (reinterpret_cast<uintptr_t>(p.C) % 16 == 0) && (p.c_ps % 4 == 0) && (p.c_pmr % 4 == 0);
-  float* C = reinterpret_cast<float*>(p.C);
+  // Parameters are read once into registers: `p` is reached through a generic
+  // pointer here, so every global store below would otherwise force the
+  // compiler to load the fields again.
+  const int S = p.M / 2, N = p.N;
+  const long long c_ps = p.c_ps, c_pmr = p.c_pmr;
+  const float alpha = p.alpha;
+  float* __restrict__ C = reinterpret_cast<float*>(p.C);
+  const bool vec = (reinterpret_cast<uintptr_t>(C) % 16 == 0) && (c_ps % 4 == 0) && (c_pmr % 4 == 0);
   auto row_off = [&](int r, bool* ok) -> long long {
     const int s_idx = tm * 64 + (r >> 1);
     const int pm = r & 1;
     const int mr = (g == 0) ? 0 : 2 * g - 1 + pm;
     *ok = (s_idx < S) && !(g == 0 && pm == 1);
-    return static_cast<long long>(s_idx) * p.c_ps + static_cast<long long>(mr) * p.c_pmr;
+    return static_cast<long long>(s_idx) * c_ps + static_cast<long long>(mr) * c_pmr;
   };
 #pragma unroll 1
   for (int c0 = half * 32; c0 < BN; c0 += 64) {
     const int ncolc = (BN - c0) >= 32 ? 32 : (BN - c0);
     const int col0 = tn * BN + c0;
-    int ncols = p.N - col0;
+    int ncols = N - col0;
     if (ncols > ncolc) ncols = ncolc;
     uint8_t* my = stage + lane * kStageRowF32;
     // 16 columns at a time: load, scale, stage (keeps 16 accumulator registers live)
@@ -433,16 +442,16 @@ __device__ __noinline__ void epilogue_pair_rows(const GemmParams& p, uint32_t ta
 #pragma unroll
       for (int j = 0; j < 16; j += 4)
         *reinterpret_cast<float4*>(my + 4 * (h + j)) =
-            make_float4(__uint_as_float(v[j]) * p.alpha, __uint_as_float(v[j + 1]) * p.alpha,
-                        __uint_as_float(v[j + 2]) * p.alpha, __uint_as_float(v[j + 3]) * p.alpha);
+            make_float4(__uint_as_float(v[j]) * alpha, __uint_as_float(v[j + 1]) * alpha,
+                        __uint_as_float(v[j + 2]) * alpha, __uint_as_float(v[j + 3]) * alpha);
     }
     if (ncols <= 0) continue;
     __syncwarp();
     if (vec) {
+      const int seg = lane & 7;
 #pragma unroll 2
       for (int i = 0; i < 8; ++i) {
-        const int v = lane + 32 * i;
-        const int rr = v >> 3, seg = v & 7;
+        const int rr = (lane + 32 * i) >> 3;
         bool ok;
         const long long off = row_off(q * 32 + rr, &ok);
         if (!ok || seg * 4 >= ncols) continue;
