@@ -12,7 +12,10 @@ REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if REPO not in sys.path:
     sys.path.insert(0, REPO)
 
-REFERENCE_DIR = os.environ.get("TGCM_REFERENCE_DIR", "/root/reference")
+# The oracle is the reference package: TGCM_REFERENCE_DIR when set, else the
+# unmodified copy that the benchmark's reference arm installs under
+# baseline/_ref; the oracle tests skip when neither exists.
+REFERENCE_DIR = os.environ.get("TGCM_REFERENCE_DIR") or os.path.join(REPO, "baseline", "_ref", "tornado_gcm")
 
 
 def pytest_configure(config):

@@ -45,3 +45,34 @@ def test_split_precision_transform_matches_dense():
     assert float((nod.double() - ref).norm() / ref.norm()) < 1e-3
     back = tr.forward_transform(ref.float() * torch.as_tensor(g.spherical_harmonics.basis.w))
     assert back.to_dense().shape == x.shape
+
+
+def test_packed_storage_saves_memory_and_roundtrips_exactly():
+    g = sh.Grid.T21()
+    mask = torch.as_tensor(g.mask)
+    x = torch.randn(3, 4, *g.modal_shape) * mask
+    lay = sparse.TriangleLayout(*g.modal_shape)
+    assert lay.count == int(mask.sum())
+    # l-major: the packed entries of total wavenumber l sit in [l_offsets[l], l_offsets[l+1])
+    m, l = g.modal_mesh
+    ls = torch.as_tensor(l).flatten()[lay.index]
+    assert bool((ls[1:] >= ls[:-1]).all())
+    st = sparse.SpectralSparseState.from_state_dict({"t": x}, sparse.SparseConfig(mode="structural"))
+    torch.testing.assert_close(st.to_dense_dict()["t"], x, rtol=0, atol=0)
+    assert abs(st.memory_savings - (1 - lay.count / mask.numel())) < 1e-12 and st.memory_savings > 0.4
+    # adaptive: small entries dropped, the rest exact, fewer bytes than the packed triangle
+    y = x.clone()
+    y[..., 5:, :] *= 1e-9
+    ad = sparse.SpectralSparseState.from_state_dict({"t": y}, sparse.SparseConfig(mode="adaptive",
+                                                                                  adaptive_threshold=1e-6))
+    back = ad.to_dense_dict()["t"]
+    keep = y.abs() >= 1e-6
+    torch.testing.assert_close(back[keep], y[keep], rtol=0, atol=0)
+    assert float(back[~keep].abs().max()) == 0.0
+    assert ad.memory_bytes < st.memory_bytes
+    # mixed: split at one packed position; low part exact, high part BF16
+    mx = sparse.MixedPrecisionSparse.from_dense(x, 11)
+    assert mx.low.shape[-1] == lay.split(11) and mx.high.dtype == torch.bfloat16
+    d = mx.to_dense()
+    torch.testing.assert_close(d[..., :11], x[..., :11], rtol=0, atol=0)
+    torch.testing.assert_close(d[..., 11:], x[..., 11:].bfloat16().float(), rtol=0, atol=0)

@@ -97,3 +97,17 @@ def test_noalloc_synthesis_rejects_oversized_request():
     assert _call(fn, b, xbuf, S, out, False, err) == ERR_TOO_LARGE
     bad = xbuf.flatten()[1:]  # 4-byte offset: not 16-byte aligned
     assert _call(fn, b, bad, 1, out, False, err) == ERR_ARGS
+
+
+def test_noalloc_synthesis_rejects_groups_without_k_blocks():
+    """A wavenumber group whose triangular K range is empty would leave its W rows unwritten."""
+    fn = _entry()
+    g, b = _bases("TL63")
+    xbuf = _modal_padded(g, b, 1, seed=0)
+    out = torch.empty(1, b.I, b.J, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    L, Mw = 32, 33  # group m = 32 would start its K loop at l = 32 = L
+    rc = fn(xbuf.data_ptr(), 1, 2 * Mw - 1, L, b.Lp, b.M2 * b.Lp, b.P.data_ptr(), Mw, b.J, b.Lp,
+            b.F.data_ptr(), b.I, b.M2p, out.data_ptr(), 0, err.data_ptr(), stream)
+    assert rc == ERR_ARGS

@@ -73,7 +73,7 @@ def train(config: str, checkpoint: Optional[str], jax_weights: Optional[str], st
 
         gcm = load_jax_checkpoint(jax_weights, device=dev, resolution=cfg.model.resolution)
     else:
-        gcm, _ = build_hybrid_gcm(cfg.model.resolution, dev, policy=cfg.policy)
+        gcm, _ = build_hybrid_gcm(cfg.model.resolution, dev, policy=cfg.policy, fixer=cfg.fixer)
     if not use_sda:
         cfg.scheduler.mode = "milestone"
         cfg.scheduler.check_interval = 10 ** 9

@@ -168,6 +168,10 @@ extern "C" __attribute__((visibility("default"))) int tgcm_sht_synth_noalloc(
     return reject("x, P, F and out must be non-null and 16-byte aligned");
   if (S < 1 || L < 1 || Mw < 1 || J < 1 || I < 1) return reject("all sizes must be positive");
   if (M2 != 2 * Mw - 1) return reject("M2 must equal 2 * Mw - 1");
+  // The triangular Legendre GEMM starts group m at K = floor(m / 32) * 32;
+  // a group whose start is at or beyond L would write none of its W rows,
+  // and the Fourier GEMM would then read stale scratch.
+  if (((Mw - 1) / 32) * 32 >= L) return reject("floor((Mw - 1) / 32) * 32 must be below L (use Mw <= L)");
   if (Lp < L || Lp % 4 != 0) return reject("Lp must be >= L and a multiple of 4");
   if (M2p < M2 || M2p % 4 != 0) return reject("M2p must be >= M2 and a multiple of 4");
   if (x_row_stride < L || x_row_stride % 4 != 0 || x_slice_stride % 4 != 0 ||

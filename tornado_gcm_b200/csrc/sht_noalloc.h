@@ -50,14 +50,25 @@ extern "C" {
 //            (s, r, l) at x[s * x_slice_stride + r * x_row_stride + l].
 //            16-byte aligned; both strides multiples of 4 floats.
 //   P        Legendre table (Mw, J, Lp) contiguous, Lp >= L, Lp % 4 == 0.
+//            It must be lower-triangular in the sense of the associated
+//            Legendre functions: P[m, j, l] == 0 for l < m.  The Legendre
+//            GEMM of group m starts its K loop at floor(m / 32) * 32 and
+//            skips the columns before it, so non-zero entries there would be
+//            dropped.  For the same reason every group must have at least
+//            one K block: floor((Mw - 1) / 32) * 32 < L, which holds for
+//            every spectral truncation with Mw <= L.  Calls that break it are
+//            rejected with TGCM_SHT_NOALLOC_ERR_ARGS.
 //   F        real Fourier table (I, M2p) contiguous, M2p >= M2, M2p % 4 == 0.
 //   out      nodal output, contiguous (S, I, J), or (S, J, I) when lat_major.
 //   err      optional int flag (device memory, caller sets it to 0); a bounded
 //            wait that expires inside a kernel writes a non-zero code there.
 //            May be NULL.
 //   stream   stream to launch on (0 = legacy default stream).
-// Returns one of the TGCM_SHT_NOALLOC_* codes; on a non-zero code nothing
-// was launched.
+// Returns one of the TGCM_SHT_NOALLOC_* codes.  TGCM_SHT_NOALLOC_ERR_ARGS
+// and TGCM_SHT_NOALLOC_ERR_TOO_LARGE are decided before anything is
+// launched.  On TGCM_SHT_NOALLOC_ERR_CUDA the first (Legendre) GEMM may
+// already be queued on the stream and writing the shared scratch array when
+// the second launch is the one that failed; `out` is then not valid.
 int tgcm_sht_synth_noalloc(const float* x, long long S, long long M2, long long L, long long x_row_stride,
                            long long x_slice_stride, const float* P, long long Mw, long long J, long long Lp,
                            const float* F, long long I, long long M2p, float* out, int lat_major, int* err,

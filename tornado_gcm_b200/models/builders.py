@@ -31,7 +31,7 @@ import torch.utils.checkpoint as torch_checkpoint
 from tornado_gcm_b200.core import coordinate_systems, sigma_coordinates, spherical_harmonic
 from tornado_gcm_b200.models.api import ModelConfig, NeuralGCMModel
 from tornado_gcm_b200.neural.column_codecs import TRACERS, VELOCITY_SCALE, ColumnDecoder, ColumnEncoder
-from tornado_gcm_b200.neural.fixers import LiteConservationFixer
+from tornado_gcm_b200.neural.fixers import F64ConservationFixer, LiteConservationFixer
 from tornado_gcm_b200.neural.parameterizations import NodalColumnParameterization
 from tornado_gcm_b200.neural.standard_layers import Mlp, gelu_tanh
 from tornado_gcm_b200.neural.towers import ForwardTower
@@ -155,11 +155,35 @@ def resolve_resolution(name) -> str:
     raise KeyError(f"unknown resolution {name!r}; known: {sorted(RESOLUTIONS)}")
 
 
+def make_fixer(section=None) -> Optional[nn.Module]:
+    """Conservation fixer from a config ``fixer`` section (kind, fix_mass, fix_energy, energy_split).
+
+    ``None`` gives the default: the FP64-accumulated packed fixer with the
+    level-split energy correction.
+    """
+    if section is None:
+        return LiteConservationFixer()
+    kind = str(getattr(section, "kind", "lite")).lower()
+    kw = dict(fix_mass=bool(section.fix_mass), fix_energy=bool(section.fix_energy),
+              energy_split=str(getattr(section, "energy_split", "levels")))
+    if kind == "none":
+        return None
+    if kind in ("f64", "fp64", "float64"):
+        return F64ConservationFixer(**kw)
+    if kind != "lite":
+        raise ValueError(f"unknown fixer kind {kind!r} (lite | f64 | none)")
+    return LiteConservationFixer(**kw)
+
+
 def build_hybrid_gcm(resolution: str = "2.8deg", device: str | torch.device = "cpu",
                      policy: Optional[PrecisionPolicy] = None, seed: int = 0,
                      sht_precision: Optional[str] = None,
-                     output_init_scale: float = 0.01, **config_overrides) -> tuple[HybridGCM, SyntheticReanalysis]:
+                     output_init_scale: float = 0.01, fixer=None,
+                     **config_overrides) -> tuple[HybridGCM, SyntheticReanalysis]:
     """Random-init hybrid model of the given resolution plus its synthetic data source.
+
+    ``fixer`` is a config ``fixer`` section (see :func:`make_fixer`); its
+    ``cadence`` sets how often the fixer runs.
 
     ``output_init_scale`` multiplies the tower's last weight matrix: the random
     tendencies then stay small enough that multi-day rollouts of the random
@@ -214,7 +238,9 @@ def build_hybrid_gcm(resolution: str = "2.8deg", device: str | torch.device = "c
                                [np.full(n, tr_out[k]) for k in tracer_keys] + [[1e-5]])
     param = NodalColumnParameterization(grid, n, tracer_keys, tower, forcing_keys=FORCING_FIELDS,
                                         output_scale=out_scale, input_scale=in_scale)
-    model = NeuralGCMModel(cfg, parameterization=param, conservation_fixer=LiteConservationFixer())
+    model = NeuralGCMModel(cfg, parameterization=param, conservation_fixer=make_fixer(fixer))
+    if fixer is not None:
+        model.set_fixer_cadence(int(getattr(fixer, "cadence", 1)))
     stats = data.stats()
     forcing_scale = {"sea_surface_temperature": (288.0, 0.1), "orography": (0.0, 1e-3)}
     enc = ColumnEncoder(coords, t_ref, data.levels, stats, FORCING_FIELDS, hidden=spec.encoder_width,

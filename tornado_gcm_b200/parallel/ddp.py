@@ -184,22 +184,36 @@ class GradientAllReducer:
     must call :meth:`reduce` at the same point (after backward).
     """
 
-    def __init__(self, params: Sequence[torch.nn.Parameter], bucket_mb: float = 0.0, use_fused: bool = True):
+    def __init__(self, params: Sequence[torch.nn.Parameter], bucket_mb: float = 0.0, use_fused: bool = True,
+                 average: bool = True):
         self.params = [p for p in params if p.requires_grad]
         dev = self.params[0].device
         sizes = [p.numel() for p in self.params]
         self.numel = sum(sizes)
         self.world = get_world_size()
+        self.average = average
         self.bucket_elems = int(bucket_mb * 1e6 / 4) if bucket_mb > 0 else self.numel
         self.fused = None
-        if use_fused and self.world > 1 and dev.type == "cuda" and os.environ.get("TGCM_FUSED_ALLREDUCE", "1") != "0":
-            try:
-                from tornado_gcm_b200.parallel import fused_allreduce
+        # The fused NVLink kernel is the reducer on CUDA with more than one rank.
+        # It is turned off only on request (use_fused=False or
+        # TGCM_FUSED_ALLREDUCE=0); when it was requested and cannot be set up the
+        # constructor raises instead of silently running the NCCL path.
+        want_fused = (use_fused and self.world > 1 and dev.type == "cuda"
+                      and os.environ.get("TGCM_FUSED_ALLREDUCE", "1") != "0")
+        if want_fused:
+            from tornado_gcm_b200.parallel import fused_allreduce
 
+            try:
                 self.fused = fused_allreduce.make_reducer(self.numel, dev)
-            except Exception as exc:  # pragma: no cover - depends on platform
-                logger.warning("fused all-reduce unavailable (%s); using NCCL", exc)
-                self.fused = None
+            except Exception as exc:
+                raise RuntimeError(f"fused gradient all-reduce requested but unavailable: {exc}; "
+                                   "set TGCM_FUSED_ALLREDUCE=0 to use NCCL") from exc
+        if self.world <= 1:
+            self.backend = "none (one rank)"
+        elif self.fused is not None:
+            self.backend = "fused NVLink peer-memory kernel (csrc/comm.cu)"
+        else:
+            self.backend = "nccl" if dev.type == "cuda" else str(dist.get_backend())
         # the flat buffer is the reducer's symmetric allocation when fused
         self.flat = self.fused.flat if self.fused is not None else torch.zeros(self.numel, dtype=torch.float32,
                                                                                device=dev)
@@ -227,12 +241,16 @@ class GradientAllReducer:
                 v.copy_(p.grad)
                 p.grad = v
         if self.fused is not None:
-            self.fused.all_reduce_mean(self.flat)
+            if self.average:
+                self.fused.all_reduce_mean(self.flat)
+            else:
+                self.fused.all_reduce_sum(self.flat)
             return
         for s in range(0, self.numel, self.bucket_elems):
             chunk = self.flat[s:s + self.bucket_elems]
             dist.all_reduce(chunk, op=dist.ReduceOp.SUM)
-        self.flat.mul_(1.0 / self.world)
+        if self.average:
+            self.flat.mul_(1.0 / self.world)
 
     def broadcast_parameters(self, src: int = 0) -> None:
         if self.world <= 1:

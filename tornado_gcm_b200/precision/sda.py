@@ -134,6 +134,9 @@ class FixerSection:
     cadence: int = 1
     fix_mass: bool = True
     fix_energy: bool = True
+    # "levels": each level's T'(0,0) takes deficit / n (restores the energy proxy exactly);
+    # "reference": the whole deficit at every level, as reference neural/fixers.py:171-190
+    energy_split: str = "levels"
 
 
 def _section(cls, d: Optional[dict]):

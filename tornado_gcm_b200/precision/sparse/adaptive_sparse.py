@@ -37,16 +37,16 @@ class SparseSpectralTransform:
         return d
 
     def inverse_legendre(self, c: MixedPrecisionSparse) -> torch.Tensor:
-        lo, hi = self._on(c.low.device)
-        y = torch.einsum("mjl,...ml->...mj", lo, c.low.double())
-        y = y + torch.einsum("mjl,...ml->...mj", hi, c.high.float()).double()
+        lo, hi = self._on(c.device)
+        y = torch.einsum("mjl,...ml->...mj", lo, c.low_block().double())
+        y = y + torch.einsum("mjl,...ml->...mj", hi, c.high_block().float()).double()
         return y.float()
 
     def forward_legendre(self, x: torch.Tensor) -> MixedPrecisionSparse:
         lo, hi = self._on(x.device)
         low = torch.einsum("mjl,...mj->...ml", lo, x.double()).float()
-        high = torch.einsum("mjl,...mj->...ml", hi, x.float()).to(self.config.high_order_dtype)
-        return MixedPrecisionSparse(low, high, self.cutoff_l)
+        high = torch.einsum("mjl,...mj->...ml", hi, x.float())
+        return MixedPrecisionSparse.from_blocks(low, high, self.config.high_order_dtype)
 
     def inverse_transform(self, c: MixedPrecisionSparse) -> torch.Tensor:
         mid = self.inverse_legendre(c)
