@@ -157,6 +157,48 @@ def test_linear_kernels_vs_fp32(T, K, O, act):
         assert _rel(a, b) < 3e-2
 
 
+@pytest.mark.parametrize("K,H,O", [(197, 384, 193), (64, 128, 40)])
+def test_mlp_in_place_grad_accumulation_matches_autograd(K, H, O):
+    """Weights used three times per backward: in-place accumulation (padded and unpadded
+    layers, bias column sums) gives the gradients autograd accumulates from returned grads."""
+    _require()
+    from tornado_gcm_b200.ops import linear as lops
+
+    torch.manual_seed(5)
+    layers = [torch.nn.Linear(K, H).to(DEV), torch.nn.Linear(H, H).to(DEV), torch.nn.Linear(H, O).to(DEV)]
+    acts = ["gelu_tanh", "gelu_tanh", "none"]
+    params = [p for lyr in layers for p in lyr.parameters()]
+    xs = [torch.randn(777, K, device=DEV) for _ in range(3)]
+
+    def loss_fn():
+        return sum((lops.mlp_forward(x, layers, acts) ** 2).mean() for x in xs)
+
+    for p in params:
+        p.grad = None
+    loss_fn().backward()
+    ref = [p.grad.clone() for p in params]
+    prev = lops.fused_grad_accumulation()
+    lops.set_fused_grad_accumulation(True)
+    try:
+        for p in params:
+            p.grad = torch.zeros_like(p)
+        loss_fn().backward()
+    finally:
+        lops.set_fused_grad_accumulation(prev)
+    for p, r in zip(params, ref):
+        assert _rel(p.grad, r) < 1e-4
+
+
+def test_colsum_bf16_accumulates_in_place():
+    _require()
+    ops = _ext.require("colsum")
+    x = torch.randn(5000, 200, device=DEV).to(torch.bfloat16)
+    out = torch.full((193,), 2.0, device=DEV)
+    ops.colsum_bf16_acc(x, 193, out)
+    ref = x[:, :193].double().sum(0) + 2.0
+    assert _rel(out, ref) < 1e-5
+
+
 def test_fused_sil3_gpu_matches_cpu():
     _require()
     from tornado_gcm_b200.core import filtering, primitive_equations as pe

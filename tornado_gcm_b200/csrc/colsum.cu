@@ -71,7 +71,7 @@ __global__ void __launch_bounds__(kColsumThreads) colsum_partial_kernel(const __
 
 // 32 columns per block, 8 row groups folding the block partials in a fixed order.
 __global__ void __launch_bounds__(256) colsum_final_kernel(const float* __restrict__ part, int nblocks, int ncols,
-                                                           float* __restrict__ out) {
+                                                           float* __restrict__ out, int accumulate) {
   __shared__ float red[8][33];
   const int cl = threadIdx.x & 31, grp = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + cl;
@@ -84,21 +84,20 @@ __global__ void __launch_bounds__(256) colsum_final_kernel(const float* __restri
     float t = 0.f;
 #pragma unroll
     for (int g2 = 0; g2 < 8; ++g2) t += red[g2][cl];
-    out[c] = t;
+    out[c] = accumulate ? out[c] + t : t;
   }
 }
 
 }  // namespace
 
-// x: (T, ld) bf16 row-major; returns fp32 (ncols) sums of the first ncols columns.
-at::Tensor colsum_bf16(const at::Tensor& x, int64_t ncols) {
-  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1,
-              "colsum_bf16 expects a (T, ld) bf16 CUDA matrix with unit column stride");
-  TORCH_CHECK(ncols >= 1 && ncols <= x.size(1) && ncols <= 2048, "ncols out of range");
-  c10::cuda::CUDAGuard guard(x.device());
+namespace {
+
+void colsum_launch(const at::Tensor& x, int64_t ncols, at::Tensor& out, int accumulate) {
   const long long T = x.size(0);
-  auto out = out_empty({ncols}, x.options().dtype(at::kFloat));
-  if (T == 0) return out.zero_();
+  if (T == 0) {
+    if (!accumulate) out.zero_();
+    return;
+  }
   const int nb = static_cast<int>(T < kColsumBlocks ? T : kColsumBlocks);
   auto part = out_empty({nb, ncols}, x.options().dtype(at::kFloat));
   auto st = at::cuda::getCurrentCUDAStream();
@@ -108,13 +107,45 @@ at::Tensor colsum_bf16(const at::Tensor& x, int64_t ncols) {
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   colsum_final_kernel<<<static_cast<unsigned>((ncols + 31) / 32), 256, 0, st>>>(part.data_ptr<float>(), nb,
                                                                                   static_cast<int>(ncols),
-                                                                                  out.data_ptr<float>());
+                                                                                  out.data_ptr<float>(), accumulate);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void check_x(const at::Tensor& x, int64_t ncols) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1,
+              "colsum_bf16 expects a (T, ld) bf16 CUDA matrix with unit column stride");
+  TORCH_CHECK(ncols >= 1 && ncols <= x.size(1) && ncols <= 2048, "ncols out of range");
+}
+
+}  // namespace
+
+// x: (T, ld) bf16 row-major; returns fp32 (ncols) sums of the first ncols columns.
+at::Tensor colsum_bf16(const at::Tensor& x, int64_t ncols) {
+  check_x(x, ncols);
+  c10::cuda::CUDAGuard guard(x.device());
+  auto out = out_empty({ncols}, x.options().dtype(at::kFloat));
+  colsum_launch(x, ncols, out, 0);
   return out;
+}
+
+// out[c] += sum_t x[t, c] for c < ncols (the bias gradient accumulated in place).
+void colsum_bf16_acc(const at::Tensor& x, int64_t ncols, at::Tensor& out) {
+  check_x(x, ncols);
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kFloat && out.is_contiguous() && out.numel() >= ncols &&
+                  out.device() == x.device(),
+              "colsum_bf16_acc expects a contiguous fp32 output on the same device with >= ncols elements");
+  c10::cuda::CUDAGuard guard(x.device());
+  colsum_launch(x, ncols, out, 1);
 }
 
 }  // namespace tgcm
 
-TORCH_LIBRARY_FRAGMENT(tgcm, m) { m.def("colsum_bf16(Tensor x, int ncols) -> Tensor"); }
+TORCH_LIBRARY_FRAGMENT(tgcm, m) {
+  m.def("colsum_bf16(Tensor x, int ncols) -> Tensor");
+  m.def("colsum_bf16_acc(Tensor x, int ncols, Tensor(a!) out) -> ()");
+}
 
-TORCH_LIBRARY_IMPL(tgcm, CUDA, m) { m.impl("colsum_bf16", &tgcm::colsum_bf16); }
+TORCH_LIBRARY_IMPL(tgcm, CUDA, m) {
+  m.impl("colsum_bf16", &tgcm::colsum_bf16);
+  m.impl("colsum_bf16_acc", &tgcm::colsum_bf16_acc);
+}

@@ -53,6 +53,7 @@ struct FixArgs {
   long long energy_n;  // 3n * M2 * L
   int n, B, fix_mass, fix_energy;
   double dscale;       // share of the deficit added at each level (1/n or 1)
+  const double* gd;    // (B) deficit cotangents supplied by the caller, or null
 };
 
 // Deficit and admissibility of sample b from the partial sums (fixed order).
@@ -182,7 +183,7 @@ __global__ void __launch_bounds__(kFixThreads) fix_adjoint_kernel(FixArgs a) {
     if (a.fix_energy) deficit_of(a, b, &D, &ok);
     sD = D;
     sOk = ok;
-    sG = deficit_cotangent(a, b, D, ok);
+    sG = a.gd ? a.gd[b] : deficit_cotangent(a, b, D, ok);
   }
   __syncthreads();
   const double D = sD, gD = sG;
@@ -244,13 +245,43 @@ int apply_blocks(const FixArgs& a) {
 
 }  // namespace
 
-// Returns (fixed state, partial sums); the partial sums feed the backward.
-std::vector<at::Tensor> packed_fix(const at::Tensor& y, const at::Tensor& yb, int64_t n, bool fix_mass,
-                                   int64_t fix_energy) {
+namespace {
+
+void check_part(const at::Tensor& part, const FixArgs& a, const at::Tensor& y) {
+  TORCH_CHECK(part.scalar_type() == at::kDouble && part.is_contiguous() &&
+                  part.numel() == static_cast<int64_t>(a.B) * kFixBlocks * 2 && part.device() == y.device(),
+              "partial sums must be a contiguous fp64 (B, 64, 2) tensor on the state's device");
+}
+
+}  // namespace
+
+// Partial energy sums alone: (B, 64, 2) fp64 (sum of y^2, sum of y_before^2 per block).
+// A caller whose modal rows are spread over several GPUs adds the ranks'
+// partial sums (an all-reduce) and passes the total to packed_fix_apply.
+at::Tensor packed_fix_partial(const at::Tensor& y, const at::Tensor& yb, int64_t n, bool fix_mass,
+                              int64_t fix_energy) {
   c10::OptionalDeviceGuard guard(y.device());
   FixArgs a = make_args(y, yb, n, fix_mass, fix_energy);
   auto part = out_empty({a.B, kFixBlocks, 2}, y.options().dtype(at::kDouble));
   partial_sums(a, part, y);
+  return part;
+}
+
+// Returns (fixed state, partial sums); the partial sums feed the backward.
+// part_in: partial sums computed (and possibly reduced over ranks) by the caller.
+std::vector<at::Tensor> packed_fix(const at::Tensor& y, const at::Tensor& yb, int64_t n, bool fix_mass,
+                                   int64_t fix_energy, const c10::optional<at::Tensor>& part_in) {
+  c10::OptionalDeviceGuard guard(y.device());
+  FixArgs a = make_args(y, yb, n, fix_mass, fix_energy);
+  at::Tensor part;
+  if (part_in.has_value() && part_in->defined()) {
+    check_part(*part_in, a, y);
+    part = *part_in;
+    a.part = part.data_ptr<double>();
+  } else {
+    part = out_empty({a.B, kFixBlocks, 2}, y.options().dtype(at::kDouble));
+    partial_sums(a, part, y);
+  }
   auto out = out_empty_like(y);
   a.out = out.data_ptr<float>();
   if (y.is_cuda()) {
@@ -267,15 +298,22 @@ std::vector<at::Tensor> packed_fix(const at::Tensor& y, const at::Tensor& yb, in
   return {out, part};
 }
 
+// gd (optional, (B) fp64): the deficit cotangents, computed by the caller when
+// the (0,0) modes live on another rank; otherwise they come from y's own rows.
 std::vector<at::Tensor> packed_fix_adjoint(const at::Tensor& gout, const at::Tensor& y, const at::Tensor& yb,
                                            const at::Tensor& part, int64_t n, bool fix_mass, int64_t fix_energy,
-                                           bool need_before) {
+                                           bool need_before, const c10::optional<at::Tensor>& gd) {
   c10::OptionalDeviceGuard guard(y.device());
   FixArgs a = make_args(y, yb, n, fix_mass, fix_energy);
   TORCH_CHECK(gout.sizes() == y.sizes() && gout.is_contiguous() && gout.scalar_type() == at::kFloat, "gradient shape");
-  TORCH_CHECK(part.scalar_type() == at::kDouble && part.numel() == static_cast<int64_t>(a.B) * kFixBlocks * 2,
-              "partial sums shape");
+  check_part(part, a, y);
   a.part = part.data_ptr<double>();
+  if (gd.has_value() && gd->defined()) {
+    TORCH_CHECK(gd->scalar_type() == at::kDouble && gd->is_contiguous() && gd->numel() == a.B &&
+                    gd->device() == y.device(),
+                "gd must be a contiguous fp64 (B) tensor on the state's device");
+    a.gd = gd->data_ptr<double>();
+  }
   a.gout = gout.data_ptr<float>();
   auto g_y = out_empty_like(y);
   at::Tensor g_yb = need_before ? out_empty_like(y) : at::Tensor();
@@ -289,7 +327,7 @@ std::vector<at::Tensor> packed_fix_adjoint(const at::Tensor& gout, const at::Ten
       double D = 0.0;
       int ok = 0;
       if (a.fix_energy) deficit_of(a, b, &D, &ok);
-      const double gD = deficit_cotangent(a, b, D, ok);
+      const double gD = a.gd ? a.gd[b] : deficit_cotangent(a, b, D, ok);
       for (long long off = 0; off < a.sample; ++off) adjoint_point(a, b, off, D, ok, gD);
     }
   }
@@ -384,13 +422,15 @@ at::Tensor sum_squares(const at::Tensor& x, int64_t n_trailing) {
 TORCH_LIBRARY_FRAGMENT(tgcm, m) {
   m.def("sphere_integrate(Tensor z, Tensor w) -> Tensor");
   m.def("sum_squares(Tensor x, int n_trailing) -> Tensor");
-  m.def("packed_fix(Tensor y, Tensor y_before, int n, bool fix_mass, int fix_energy) -> Tensor[]");
+  m.def("packed_fix(Tensor y, Tensor y_before, int n, bool fix_mass, int fix_energy, Tensor? part=None) -> Tensor[]");
+  m.def("packed_fix_partial(Tensor y, Tensor y_before, int n, bool fix_mass, int fix_energy) -> Tensor");
   m.def("packed_fix_adjoint(Tensor gout, Tensor y, Tensor y_before, Tensor part, int n, bool fix_mass, "
-        "int fix_energy, bool need_before) -> Tensor[]");
+        "int fix_energy, bool need_before, Tensor? gd=None) -> Tensor[]");
 }
 
 TORCH_LIBRARY_IMPL(tgcm, CompositeExplicitAutograd, m) {
   m.impl("packed_fix", &tgcm::packed_fix);
+  m.impl("packed_fix_partial", &tgcm::packed_fix_partial);
   m.impl("packed_fix_adjoint", &tgcm::packed_fix_adjoint);
   m.impl("sphere_integrate", &tgcm::sphere_integrate);
   m.impl("sum_squares", &tgcm::sum_squares);

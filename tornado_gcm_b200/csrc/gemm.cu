@@ -396,6 +396,133 @@ at::Tensor sht_anal(const at::Tensor& N_in, const at::Tensor& Ft, const at::Tens
   return out;
 }
 
+// ── transforms sharded over zonal wavenumbers and latitude blocks ──────────
+// Modal fields live on the rank that owns their zonal wavenumber (local rows
+// [m=0 slot | (cos, sin) pairs of the owned m]); nodal fields are split into W
+// latitude blocks of Jr rows.  The grid <-> spectral transpose between the two
+// layouts is done by the Legendre GEMMs themselves: their epilogue writes each
+// output element straight into the buffer of the rank that needs it (plain
+// peer stores for synthesis, system-scope reductions for analysis; no TMA and
+// no multicast on peer memory).  The caller synchronises the ranks with a
+// peer barrier after the routed GEMM and double-buffers the destinations.
+static void check_peer_table(const at::Tensor& ptrs, int64_t world) {
+  TORCH_CHECK(!ptrs.is_cuda() && ptrs.scalar_type() == at::kLong && ptrs.numel() == world && world >= 1 && world <= 8,
+              "peer pointer table must hold one int64 address per rank (1..8) on the CPU");
+  for (int64_t i = 0; i < world; ++i)
+    TORCH_CHECK(ptrs.data_ptr<int64_t>()[i] % 16 == 0, "peer buffers must be 16-byte aligned");
+}
+
+// Synthesis, Legendre step.  x: local modal (S, M2_loc, Lx) fp32 view;
+// P_loc: (G, J, Lp) Legendre table of the local groups (zero slots where
+// group_m < 0); group_m: (G) int32 on the device (zonal wavenumber per local
+// group).  Writes W_d[row(m)][s*Jr + (j - d*Jr)] on rank d = j / Jr, where W_d
+// is the (M2, S*Jr) buffer at w_ptrs[d].
+void sht_synth_routed(const at::Tensor& x, int64_t L, const at::Tensor& P_loc, const at::Tensor& group_m,
+                      const at::Tensor& w_ptrs, int64_t Jr, const c10::optional<at::Tensor>& err) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kFloat && x.dim() == 3, "x must be a (S, M2, L) fp32 CUDA tensor");
+  TORCH_CHECK(x.stride(2) == 1 && (x.stride(1) * 4) % 16 == 0 && (x.stride(0) * 4) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0,
+              "x rows must be contiguous with 16-byte aligned strides");
+  TORCH_CHECK(P_loc.is_contiguous() && P_loc.scalar_type() == at::kFloat && P_loc.dim() == 3, "P_loc (G, J, Lp)");
+  TORCH_CHECK(group_m.is_cuda() && group_m.scalar_type() == at::kInt && group_m.numel() == P_loc.size(0),
+              "group_m must be int32 (G) on the device");
+  c10::cuda::CUDAGuard guard(x.device());
+  const int64_t S = x.size(0), M2l = x.size(1);
+  const int64_t G = P_loc.size(0), J = P_loc.size(1), Lp = P_loc.size(2);
+  TORCH_CHECK(M2l <= 2 * G - 1 + 1 && Lp >= L && L <= x.size(2), "layout mismatch");
+  TORCH_CHECK(Jr > 0 && Jr % 4 == 0 && J % Jr == 0, "latitude blocks must be multiples of 4 rows");
+  check_peer_table(w_ptrs, J / Jr);
+  const int bnj = pick_bn_j(J);
+  CUtensorMap ta = make_tmap(x.data_ptr(), 2, L, M2l, S, x.stride(1) * 4, x.stride(0) * 4, 32, 2, 64);
+  CUtensorMap tb = make_tmap(P_loc.data_ptr(), 2, L, J, G, Lp * 4, J * Lp * 4, 32, bnj, 1);
+  GemmParams p = default_params();
+  p.M = 2 * S; p.N = J; p.K = L; p.groups = G;
+  p.tiles_m = cdiv(S, 64); p.tiles_n = cdiv(J, bnj);
+  p.a_pair = 1; p.k_tri = 1;
+  p.c_pair = 1; p.c_ps = Jr; p.c_pmr = S * Jr; p.c_sc = 1;
+  p.route_mode = 1; p.route_cols = static_cast<int>(Jr); p.group_map = group_m.data_ptr<int>();
+  p.n_peers = static_cast<int>(J / Jr);
+  for (int i = 0; i < p.n_peers; ++i) p.peer_C[i] = reinterpret_cast<float*>(w_ptrs.data_ptr<int64_t>()[i]);
+  p.err = err_ptr(err);
+  gemm_dispatch(2, bnj, false, false, ta, tb, p, at::cuda::getCurrentCUDAStream());
+}
+
+// Synthesis, Fourier step on this rank's block: out (S, Jr, I) lat-major =
+// sum_k F[i, k] W[k, s*Jr + j] for the (M2, S*Jr) m-major buffer W (one GEMM).
+at::Tensor sht_synth_dft(const at::Tensor& W, int64_t S, int64_t Jr, const at::Tensor& F,
+                         const c10::optional<at::Tensor>& err) {
+  TORCH_CHECK(W.is_cuda() && W.scalar_type() == at::kFloat && W.is_contiguous(), "W must be contiguous fp32");
+  c10::cuda::CUDAGuard guard(W.device());
+  const int64_t I = F.size(0), M2p = F.size(1);
+  const int64_t M2 = W.numel() / (S * Jr);
+  TORCH_CHECK(W.numel() == M2 * S * Jr && M2 <= M2p && Jr % 4 == 0, "W must be (M2, S*Jr)");
+  auto out = out_empty({S, Jr, I}, W.options());
+  CUtensorMap ta = make_tmap(F.data_ptr(), 2, M2, I, 1, M2p * 4, I * M2p * 4, 32, 128, 1);
+  CUtensorMap tb = make_tmap(W.data_ptr(), 2, S * Jr, M2, 1, S * Jr * 4, M2 * S * Jr * 4, 32, 32, 1, 1);
+  GemmParams p = default_params();
+  p.M = I; p.N = S * Jr; p.K = M2; p.groups = 1;
+  p.tiles_m = cdiv(I, 128);
+  const int bnw = pick_bn_wide(S * Jr, p.tiles_m);
+  p.tiles_n = cdiv(S * Jr, bnw);
+  p.C = out.data_ptr(); p.c_sg = 0; p.c_sr = 1; p.c_sc = I;
+  p.err = err_ptr(err);
+  gemm_dispatch(2, bnw, false, true, ta, tb, p, at::cuda::getCurrentCUDAStream());
+  return out;
+}
+
+// Analysis of this rank's latitude block: N (S, Jr, I) lat-major -> Z (M2, S*Jr)
+// (one-GEMM DFT into ws) -> per zonal wavenumber m the partial Legendre sums over
+// the block's latitudes, added into the (S, M2_loc, Lo) buffer of m's owner
+// (out_ptrs[group_dest[m] >> 16], local group group_dest[m] & 0xffff).
+// Pt_loc: (Mw, L, Jr) — the (weighted) Legendre table restricted to the block.
+void sht_anal_routed(const at::Tensor& N_in, const at::Tensor& Ft, const at::Tensor& Pt_loc, int64_t Lo,
+                     int64_t M2_loc, const at::Tensor& ws, const at::Tensor& group_dest, const at::Tensor& out_ptrs,
+                     const c10::optional<at::Tensor>& err) {
+  TORCH_CHECK(N_in.is_cuda() && N_in.scalar_type() == at::kFloat && N_in.dim() == 3, "N must be fp32 CUDA (S, Jr, I)");
+  c10::cuda::CUDAGuard guard(N_in.device());
+  at::Tensor N = N_in.contiguous();
+  const int64_t S = N.size(0), Jr = N.size(1), I = N.size(2);
+  const int64_t M2 = Ft.size(0);
+  const int64_t Mw = Pt_loc.size(0), L = Pt_loc.size(1);
+  TORCH_CHECK(Ft.size(1) == I && Pt_loc.size(2) == Jr && Jr % 4 == 0 && I % 4 == 0 && M2 == 2 * Mw - 1,
+              "basis shape mismatch");
+  TORCH_CHECK(Pt_loc.is_contiguous() && group_dest.is_cuda() && group_dest.scalar_type() == at::kInt &&
+                  group_dest.numel() == Mw,
+              "Pt_loc contiguous, group_dest int32 (Mw) on the device");
+  TORCH_CHECK(ws.numel() >= S * M2 * Jr, "workspace too small");
+  TORCH_CHECK(Lo >= L && Lo % 4 == 0 && M2_loc >= 1, "output rows must be padded to a multiple of 4");
+  const int64_t world = out_ptrs.numel();
+  check_peer_table(out_ptrs, world);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  {
+    const int64_t tm_a = cdiv(M2, 128);
+    const int bnw = pick_bn_wide(S * Jr, tm_a);
+    CUtensorMap ta = make_tmap(Ft.data_ptr(), 2, I, M2, 1, I * 4, M2 * I * 4, 32, 128, 1);
+    CUtensorMap tb = make_tmap(N.data_ptr(), 2, I, S * Jr, 1, I * 4, S * Jr * I * 4, 32, bnw, 1);
+    GemmParams p = default_params();
+    p.M = M2; p.N = S * Jr; p.K = I; p.groups = 1;
+    p.tiles_m = tm_a; p.tiles_n = cdiv(S * Jr, bnw);
+    p.C = ws.data_ptr(); p.c_sg = 0; p.c_sr = S * Jr; p.c_sc = 1;
+    p.err = err_ptr(err);
+    gemm_dispatch(2, bnw, false, false, ta, tb, p, st);
+  }
+  {
+    const int bnl = pick_bn_l(L);
+    CUtensorMap ta = make_tmap(ws.data_ptr(), 2, Jr, M2, S, S * Jr * 4, Jr * 4, 32, 2, 64);
+    CUtensorMap tb = make_tmap(Pt_loc.data_ptr(), 2, Jr, L, Mw, Jr * 4, L * Jr * 4, 32, bnl, 1);
+    GemmParams p = default_params();
+    p.M = 2 * S; p.N = L; p.K = Jr; p.groups = Mw;
+    p.tiles_m = cdiv(S, 64); p.tiles_n = cdiv(L, bnl);
+    p.a_pair = 1;
+    p.c_pair = 1; p.c_ps = M2_loc * Lo; p.c_pmr = Lo; p.c_sc = 1;
+    p.route_mode = 2; p.group_map = group_dest.data_ptr<int>();
+    p.n_peers = static_cast<int>(world);
+    for (int i = 0; i < p.n_peers; ++i) p.peer_C[i] = reinterpret_cast<float*>(out_ptrs.data_ptr<int64_t>()[i]);
+    p.err = err_ptr(err);
+    gemm_dispatch(2, bnl, false, false, ta, tb, p, st);
+  }
+}
+
 // ── BF16 linear layers ──────────────────────────────────────────────────────
 // X: (T, Kp) bf16;  W: (O, Kp) bf16;  bias (O) fp32.  out (T, O) bf16 or fp32.
 void linear_fwd(const at::Tensor& X, const at::Tensor& W, const c10::optional<at::Tensor>& bias, int64_t act,
@@ -562,6 +689,10 @@ TORCH_LIBRARY_FRAGMENT(tgcm, m) {
   m.def("sht_synth(Tensor x, int L, Tensor P, Tensor F, Tensor ws, Tensor? col_scale, Tensor? err, bool lat_major) -> Tensor");
   m.def("sht_anal(Tensor N, Tensor Ft, Tensor Pt, int Lo, Tensor ws, Tensor? col_scale, Tensor? err, bool lat_major, "
         "Tensor? peer_ptrs=None) -> Tensor");
+  m.def("sht_synth_routed(Tensor x, int L, Tensor P_loc, Tensor group_m, Tensor w_ptrs, int Jr, Tensor? err) -> ()");
+  m.def("sht_synth_dft(Tensor W, int S, int Jr, Tensor F, Tensor? err) -> Tensor");
+  m.def("sht_anal_routed(Tensor N, Tensor Ft, Tensor Pt_loc, int Lo, int M2_loc, Tensor ws, Tensor group_dest, "
+        "Tensor out_ptrs, Tensor? err) -> ()");
   m.def("linear_fwd(Tensor X, Tensor W, Tensor? bias, int act, Tensor(a!) out, Tensor? aux, Tensor? err) -> ()");
   m.def("linear_fwd_gathered(Tensor X, Tensor w_ptrs, int rows, int O, Tensor? bias, int act, Tensor(a!) out, "
         "Tensor? aux, Tensor? err) -> ()");
@@ -572,6 +703,9 @@ TORCH_LIBRARY_FRAGMENT(tgcm, m) {
 TORCH_LIBRARY_IMPL(tgcm, CUDA, m) {
   m.impl("sht_synth", &tgcm::sht_synth);
   m.impl("sht_anal", &tgcm::sht_anal);
+  m.impl("sht_synth_routed", &tgcm::sht_synth_routed);
+  m.impl("sht_synth_dft", &tgcm::sht_synth_dft);
+  m.impl("sht_anal_routed", &tgcm::sht_anal_routed);
   m.impl("linear_fwd", &tgcm::linear_fwd);
   m.impl("linear_fwd_gathered", &tgcm::linear_fwd_gathered);
   m.impl("linear_dgrad", &tgcm::linear_dgrad);

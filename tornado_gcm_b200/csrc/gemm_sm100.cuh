@@ -69,7 +69,24 @@ struct GemmParams {
   // producer wait, producer issue, mma wait-empty-acc, mma wait-full, mma issue,
   // epilogue wait, epilogue work, tiles
   unsigned long long* prof;
+  // Transforms sharded over zonal wavenumbers (modal side) and latitude blocks
+  // (nodal side); pair addressing, output routed to the ranks' buffers
+  // peer_C[rank] with plain peer stores / reductions (no TMA, no multicast).
+  //  route_mode 1 (synthesis Legendre): local group g is zonal wavenumber
+  //    m = group_map[g] (-1: empty slot, nothing stored); output column j goes
+  //    to rank j / route_cols at column j % route_cols and row 2m-1+pm (0 for
+  //    m = 0) of that rank's m-major buffer; k_tri starts K at floor(m/BK)·BK.
+  //  route_mode 2 (analysis Legendre): group g is zonal wavenumber g; it goes
+  //    to rank group_map[g] >> 16 as local group group_map[g] & 0xffff (row
+  //    2·gl-1+pm, 0 for gl = 0), added with system-scope reductions.
+  int route_mode;
+  int route_cols;
+  const int* group_map;
 };
+
+__device__ __forceinline__ void st_global_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("st.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
 
 template <int FMT>
 struct FmtTraits;
@@ -154,7 +171,12 @@ __device__ __forceinline__ TileCoord tile_coord(const GemmParams& p, int t) {
 
 template <int BK>
 __device__ __forceinline__ int tile_kblocks(const GemmParams& p, int g, int split, int* kb0_out, int* kbegin_out) {
-  const int k_begin = p.k_tri ? (g / BK) * BK : 0;
+  int k_m = g;
+  if (p.k_tri && p.route_mode == 1) {
+    k_m = __ldg(p.group_map + g);
+    if (k_m < 0) k_m = 0;
+  }
+  const int k_begin = p.k_tri ? (k_m / BK) * BK : 0;
   int total = (p.K - k_begin + BK - 1) / BK;
   if (total < 0) total = 0;
   const int per = (total + p.k_splits - 1) / p.k_splits;
@@ -399,6 +421,67 @@ __device__ __forceinline__ void epilogue_rowmajor_vec(const GemmParams& p, int A
       chunk_store_f32(stage, reinterpret_cast<float*>(p.C) + base, p.c_sr, nrows, ncols, lane);
     }
     __syncwarp();
+  }
+}
+
+// Routed pair epilogue of the sharded transforms (route_mode 1 / 2, see
+// GemmParams).  One lane per output row r of the tile (slice tm*64 + r/2,
+// cos/sin row r%2); 16 accumulator columns per TMEM load, moved as 4-wide
+// vectors (the routed column blocks and the destination rows are multiples of
+// 4 floats, checked by the host).
+template <int BN>
+__device__ __noinline__ void epilogue_routed(const GemmParams& p, uint32_t taddr_row, int tm, int tn, int g, int half,
+                                             int r) {
+  const int S = p.M / 2, N = p.N, mode = p.route_mode, rc = p.route_cols;
+  const float alpha = p.alpha;
+  const long long c_ps = p.c_ps, c_pmr = p.c_pmr;
+  const int s_idx = tm * 64 + (r >> 1);
+  const int pm = r & 1;
+  const int gm = __ldg(p.group_map + g);
+  int dst = 0, row = 0;
+  bool ok = s_idx < S;
+  if (mode == 1) {
+    ok = ok && gm >= 0 && !(gm == 0 && pm == 1) && !(g == 0 && pm == 1);
+    row = gm == 0 ? 0 : 2 * gm - 1 + pm;
+  } else {
+    dst = gm >> 16;
+    const int gl = gm & 0xffff;
+    ok = ok && !(g == 0 && pm == 1) && !(gl == 0 && pm == 1);
+    row = gl == 0 ? 0 : 2 * gl - 1 + pm;
+  }
+  const long long row_off = static_cast<long long>(s_idx) * c_ps + static_cast<long long>(row) * c_pmr;
+#pragma unroll 1
+  for (int c0 = half * 16; c0 < BN; c0 += 32) {
+    uint32_t v[16];
+    tmem_ld_32x32b_x16(taddr_row + c0, v);
+    tmem_ld_wait();
+    if (!ok) continue;
+    const int colb = tn * BN + c0;
+#pragma unroll
+    for (int j = 0; j < 16; j += 4) {
+      const int col = colb + j;
+      if (col >= N) break;
+      const float a0 = __uint_as_float(v[j]) * alpha, a1 = __uint_as_float(v[j + 1]) * alpha;
+      const float a2 = __uint_as_float(v[j + 2]) * alpha, a3 = __uint_as_float(v[j + 3]) * alpha;
+      if (mode == 1) {
+        const int d = col / rc;
+        float* out = p.peer_C[d] + row_off + (col - d * rc);
+        if (col + 4 <= N) {
+          st_global_v4(out, a0, a1, a2, a3);
+        } else {
+          const float t[4] = {a0, a1, a2, a3};
+          for (int e = 0; col + e < N; ++e) out[e] = t[e];
+        }
+      } else {
+        float* out = p.peer_C[dst] + row_off + col;
+        if (col + 4 <= N) {
+          red_add_sys_v4(out, a0, a1, a2, a3);
+        } else {
+          const float t[4] = {a0, a1, a2, a3};
+          for (int e = 0; col + e < N; ++e) red_add_sys(out + e, t[e]);
+        }
+      }
+    }
   }
 }
 
@@ -797,7 +880,10 @@ __device__ __forceinline__ void gemm_sm100_body(const CUtensorMap& tmap_a, const
         const int r = q * 32 + lane;
         long long row_off = 0;
         bool row_ok;
-        if (p.c_pair) {
+        if (p.route_mode) {
+          epilogue_routed<BN>(p, taddr_row, tm, tn, g, half, r);
+          row_ok = false;
+        } else if (p.c_pair) {
           const int s_idx = tm * 64 + (r >> 1);
           const int pm = r & 1;
           const int mr = (g == 0) ? 0 : 2 * g - 1 + pm;
@@ -809,7 +895,7 @@ __device__ __forceinline__ void gemm_sm100_body(const CUtensorMap& tmap_a, const
           row_off = static_cast<long long>(g) * p.c_sg + static_cast<long long>(row) * p.c_sr;
         }
 #pragma unroll 1
-        for (int c0 = half * 16; c0 < BN; c0 += 32) {
+        for (int c0 = half * 16; c0 < BN && !p.route_mode; c0 += 32) {
           uint32_t v[16];
           tmem_ld_32x32b_x16(taddr_row + c0, v);
           tmem_ld_wait();

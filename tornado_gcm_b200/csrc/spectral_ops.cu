@@ -55,7 +55,15 @@ struct LinearArgs {
   const float* mats;           // (n_mats, n, n)
   int nlev;                    // matrix size n
   int B, C_out, M2, L;
+  // zonal wavenumber of each row, or null for the full layout (row r carries
+  // |m| = (r + 1) / 2).  A wavenumber-sharded layout keeps the (cos, sin) rows
+  // of one m adjacent at odd/even positions, so only |m| needs the table.
+  const int* row_m;
 };
+
+__host__ __device__ __forceinline__ int row_wavenumber(const LinearArgs& a, int mr) {
+  return a.row_m ? a.row_m[mr] : (mr + 1) >> 1;
+}
 
 __host__ __device__ inline float xval(const LinearArgs& a, int b, int c, int mr, int l, int pre) {
   if (l < 0 || l >= a.L) return 0.f;
@@ -70,7 +78,7 @@ __host__ __device__ inline float stencil_val(const LinearArgs& a, int b, int src
       return xval(a, b, src, mr, l, pre);
     case kStDlon: {
       if (mr == 0) return 0.f;
-      const int j = (mr + 1) / 2;
+      const int j = row_wavenumber(a, mr);
       return (mr & 1) ? j * xval(a, b, src, mr + 1, l, pre) : -j * xval(a, b, src, mr - 1, l, pre);
     }
     case kStCdlat: {
@@ -148,7 +156,7 @@ __device__ __forceinline__ float stencil_fast(const LinearArgs& a, const LinSamp
       return xs.at(src, mr, l, a.diag, pre);
     case kStDlon: {
       if (mr == 0) return 0.f;
-      const int j = (mr + 1) >> 1;
+      const int j = row_wavenumber(a, mr);
       return (mr & 1) ? j * xs.at(src, mr + 1, l, a.diag, pre) : -j * xs.at(src, mr - 1, l, a.diag, pre);
     }
     case kStCdlat:
@@ -250,7 +258,7 @@ __global__ void __launch_bounds__(32 * kRowWarps, (NL <= 3 ? 4 : 2)) spectral_li
     float fac = 1.f;
     if (st == kStDlon) {
       if (mr == 0) continue;
-      const int jm = (mr + 1) >> 1;
+      const int jm = row_wavenumber(a, mr);
       srow = (mr & 1) ? mr + 1 : mr - 1;
       fac = (mr & 1) ? static_cast<float>(jm) : -static_cast<float>(jm);
     }
@@ -438,7 +446,7 @@ __global__ void __launch_bounds__(32 * kRowWarps, (PfOcc<NL, NB>::value)) spectr
     if (source_row(m) < 0) continue;
     float fac = 1.f;
     if (m.st == kStDlon) {
-      const int jm = (mr + 1) >> 1;
+      const int jm = row_wavenumber(a, mr);
       fac = (mr & 1) ? static_cast<float>(jm) : -static_cast<float>(jm);
     }
     float qdiag[NL];
@@ -554,7 +562,8 @@ static void launch_rows(const LinearArgs& a, cudaStream_t st) {
 // x: (B, C_in, M2, Lx) ; returns y: (B, C_out, M2, Ly) with Ly = out_lpad (>= L), pad zero.
 at::Tensor spectral_linear(const at::Tensor& x, int64_t L, int64_t C_out, int64_t out_lpad, const at::Tensor& row_ptr,
                            const at::Tensor& terms, const at::Tensor& coef, const at::Tensor& diag,
-                           const at::Tensor& rec_a, const at::Tensor& rec_b, const at::Tensor& mats, int64_t nlev) {
+                           const at::Tensor& rec_a, const at::Tensor& rec_b, const at::Tensor& mats, int64_t nlev,
+                           const c10::optional<at::Tensor>& row_m) {
   TORCH_CHECK(x.dim() == 4 && x.scalar_type() == at::kFloat && x.stride(3) == 1, "x must be (B, C, M2, L) fp32");
   const int64_t B = x.size(0), M2 = x.size(2);
   // the CUDA kernel writes the padding columns itself; the CPU loop does not
@@ -574,6 +583,13 @@ at::Tensor spectral_linear(const at::Tensor& x, int64_t L, int64_t C_out, int64_
   a.mats = mats.data_ptr<float>();
   a.nlev = static_cast<int>(nlev);
   a.B = static_cast<int>(B); a.C_out = static_cast<int>(C_out); a.M2 = static_cast<int>(M2); a.L = static_cast<int>(L);
+  a.row_m = nullptr;
+  if (row_m.has_value() && row_m->defined()) {
+    TORCH_CHECK(row_m->scalar_type() == at::kInt && row_m->numel() == M2 && row_m->is_contiguous() &&
+                    row_m->device() == x.device(),
+                "row_m must be a contiguous int32 (M2) tensor on x's device");
+    a.row_m = row_m->data_ptr<int>();
+  }
   if (x.is_cuda()) {
     c10::cuda::CUDAGuard guard(x.device());
     TORCH_CHECK(C_out <= 65535 && B <= 65535 && M2 * L < (1LL << 31), "spectral_linear: launch grid too large");
@@ -1136,7 +1152,7 @@ std::vector<at::Tensor> sil3_stage_adjoint(const at::Tensor& gout, const at::Ten
 
 TORCH_LIBRARY_FRAGMENT(tgcm, m) {
   m.def("spectral_linear(Tensor x, int L, int C_out, int out_lpad, Tensor row_ptr, Tensor terms, Tensor coef, "
-        "Tensor diag, Tensor rec_a, Tensor rec_b, Tensor mats, int nlev) -> Tensor");
+        "Tensor diag, Tensor rec_a, Tensor rec_b, Tensor mats, int nlev, Tensor? row_m=None) -> Tensor");
   m.def("sil3_stage(Tensor y0, Tensor[] E, Tensor P, Tensor? y2, float[] ce, float cp, float cg, float eta, "
         "Tensor G, Tensor H, Tensor Minv, Tensor lam, Tensor tref, Tensor dsig, Tensor? filt, float clamp_abs, "
         "float R, int final_stage, int n, Tensor? minv_t=None) -> Tensor");

@@ -97,6 +97,85 @@ def begin_step() -> None:
     _CACHE.token += 1
 
 
+# ── in-place gradient accumulation ─────────────────────────────────────────
+# A column network is applied once per physics step, i.e. dozens of times per
+# training step.  Returning a fresh weight gradient for every use makes
+# autograd add it into ``.grad`` (one fill, one copy and one add per use and
+# parameter).  With in-place accumulation on, the weight-gradient GEMM adds
+# straight into ``weight.grad`` (its epilogue reads the destination; split-K
+# partial tiles are reduced there with atomics) and the bias gradient's column
+# sum adds into ``bias.grad``.  Layers whose padded shape differs from the
+# parameter's (feature counts not a multiple of 8) accumulate into a padded
+# fp32 buffer that is added into ``.grad`` once, at the end of the backward
+# pass (an autograd engine callback).  Callers must zero the gradients before
+# each backward pass (``GCMTrainer`` does); the mode is off by default because
+# ``torch.autograd.grad`` callers expect gradients returned, not accumulated.
+_ACCUMULATE = {"on": False, "queued": False}
+_PADDED_ACC: dict = {}   # id(lin) -> (weakref(lin), fp32 (Op, Kp) buffer)
+_PENDING: dict = {}      # id(lin) -> lin, layers with padded gradients to flush
+
+
+def set_fused_grad_accumulation(enabled: bool) -> None:
+    """Accumulate weight and bias gradients in place (see above)."""
+    _ACCUMULATE["on"] = bool(enabled)
+
+
+def fused_grad_accumulation() -> bool:
+    return _ACCUMULATE["on"]
+
+
+def _grad_of(p: torch.Tensor) -> torch.Tensor:
+    if p.grad is None:
+        p.grad = torch.zeros_like(p)
+    return p.grad
+
+
+def _padded_acc(lin: nn.Linear, shape) -> torch.Tensor:
+    ent = _PADDED_ACC.get(id(lin))
+    if ent is None or ent[0]() is not lin or tuple(ent[1].shape) != tuple(shape):
+        buf = torch.zeros(shape, dtype=torch.float32, device=lin.weight.device)
+        ent = (weakref.ref(lin), buf)
+        _PADDED_ACC[id(lin)] = ent
+    return ent[1]
+
+
+def _flush_padded() -> None:
+    _ACCUMULATE["queued"] = False
+    for key, lin in list(_PENDING.items()):
+        acc = _PADDED_ACC[key][1]
+        O, K = lin.weight.shape
+        _grad_of(lin.weight).add_(acc[:O, :K])
+        acc.zero_()
+    _PENDING.clear()
+
+
+def _queue_flush() -> None:
+    if not _ACCUMULATE["queued"]:
+        torch.autograd.Variable._execution_engine.queue_callback(_flush_padded)
+        _ACCUMULATE["queued"] = True
+
+
+def _accumulate_layer_grads(ops, lin: nn.Linear, dy, x, wshape, err) -> None:
+    """Weight and bias gradients of one use of ``lin`` added in place."""
+    O, K = lin.weight.shape
+    w = lin.weight
+    if w.requires_grad:
+        g = _grad_of(w)
+        if (tuple(wshape) == (O, K) and g.dtype == torch.float32 and g.is_contiguous()
+                and g.data_ptr() % 16 == 0):
+            ops.linear_wgrad(dy, x, g, 0, err)
+        else:
+            ops.linear_wgrad(dy, x, _padded_acc(lin, wshape), 0, err)
+            _PENDING[id(lin)] = lin
+            _queue_flush()
+    if lin.bias is not None and lin.bias.requires_grad:
+        gb = _grad_of(lin.bias)
+        if gb.dtype == torch.float32 and gb.is_contiguous():
+            ops.colsum_bf16_acc(dy, O, gb)
+        else:
+            gb.add_(ops.colsum_bf16(dy, O).to(gb.dtype))
+
+
 class MlpFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x2d, acts, last_bf16, layers, *params):
@@ -148,14 +227,19 @@ class MlpFn(torch.autograd.Function):
             dy[:, :O_last] = g
         grads = []
         dx_out = None
+        in_place = _ACCUMULATE["on"]
         for i in range(n - 1, -1, -1):
             lin = ctx.layers[i]
             wp = ws[i]
-            dw = torch.zeros(wp.shape, dtype=torch.float32, device=g.device)
-            ops.linear_wgrad(dy, hs[i], dw, 0, err)
-            O, K = lin.weight.shape
-            gb = ops.colsum_bf16(dy, O) if lin.bias is not None else None
-            grads.append((dw[:O, :K].to(lin.weight.dtype), gb))
+            if in_place:
+                _accumulate_layer_grads(ops, lin, dy, hs[i], wp.shape, err)
+                grads.append((None, None))
+            else:
+                dw = torch.zeros(wp.shape, dtype=torch.float32, device=g.device)
+                ops.linear_wgrad(dy, hs[i], dw, 0, err)
+                O, K = lin.weight.shape
+                gb = ops.colsum_bf16(dy, O) if lin.bias is not None else None
+                grads.append((dw[:O, :K].to(lin.weight.dtype), gb))
             if i > 0:
                 prev = zs[i - 1]
                 code = ACT_CODES[ctx.acts[i - 1]]

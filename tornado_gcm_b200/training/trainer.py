@@ -223,13 +223,25 @@ class GCMTrainer:
         self.gcm = gcm
         params = [p for p in gcm.parameters() if p.requires_grad]
         self.dp = None
+        dev = params[0].device
         if data_parallel:
             from tornado_gcm_b200.parallel.ddp import GradientAllReducer
 
             self.dp = GradientAllReducer(params)
             self.dp.broadcast_parameters()
             self.dp.zero()
-        dev = params[0].device
+            self._flat = self.dp.flat
+        else:
+            # one flat fp32 gradient buffer with each parameter's .grad a view of it:
+            # zeroing is one launch, and gradients accumulate in place
+            self._flat = torch.zeros(sum(p.numel() for p in params), dtype=torch.float32, device=dev)
+        self._grad_views = []
+        off = 0
+        for p in params:
+            self._grad_views.append(self._flat[off:off + p.numel()].view_as(p))
+            off += p.numel()
+        # the column networks add their weight/bias gradients straight into .grad
+        self.fused_grad_accumulation = dev.type == "cuda"
         self.device = dev
         self.optimizer = torch.optim.AdamW(params, lr=lr, weight_decay=weight_decay, betas=betas, eps=eps,
                                            fused=dev.type == "cuda", capturable=graph and dev.type == "cuda")
@@ -263,10 +275,15 @@ class GCMTrainer:
         from tornado_gcm_b200.ops import linear as linear_ops
 
         linear_ops.begin_step()
-        if self.dp is not None:
-            self.dp.flat.zero_()
+        self._flat.zero_()
+        self._attach()
         loss = self.gcm.loss(data0, targets, forcings)
-        loss.backward()
+        prev = linear_ops.fused_grad_accumulation()
+        linear_ops.set_fused_grad_accumulation(self.fused_grad_accumulation)
+        try:
+            loss.backward()
+        finally:
+            linear_ops.set_fused_grad_accumulation(prev)
         if self.dp is not None:
             self.dp.reduce()
         torch.nn.utils.clip_grad_norm_(self.params, self.max_grad_norm, foreach=True)
@@ -274,12 +291,14 @@ class GCMTrainer:
         self.ema.update()
         return loss.detach()
 
+    def _attach(self):
+        for p, v in zip(self.params, self._grad_views):
+            if p.grad is None or p.grad.data_ptr() != v.data_ptr():
+                p.grad = v
+
     def _zero(self):
-        if self.dp is not None:
-            self.dp.zero()
-            return
-        for p in self.params:
-            p.grad = None
+        self._flat.zero_()
+        self._attach()
 
     def train_step(self, data0: dict, targets: list, forcings: dict) -> torch.Tensor:
         """One optimizer step; returns the loss as a 0-d device tensor."""
