@@ -115,6 +115,10 @@ class NeuralGCMModel(nn.Module):
         self._cached_diagnostics: dict = {}
         self._diagnostics_enabled = False
         self.policy = config.precision_policy
+        # wavenumber/latitude sharding over ranks (parallel.spectral_shard.ShardContext)
+        self.shard = None
+        # run the packed (kernel-table) step on CPU tensors too (the kernels' CPU twins)
+        self.packed_on_cpu = False
 
         grid = config.coords.horizontal
         self.exp_filter = filtering.exponential_filter(grid, config.filter_attenuation, config.filter_order,
@@ -281,7 +285,8 @@ class NeuralGCMModel(nn.Module):
 
             st = dycore_ops.PackedSIL3(self._dycore, self._inner_dt, self.combined_filter_scaling(), tracer_keys,
                                        clamp_abs=self._sanitize_inner_clamp_abs if self._sanitize_inner_enabled
-                                       else float("inf"))
+                                       else float("inf"),
+                                       grid=self.shard.grid if self.shard is not None else None)
             self._fused[tracer_keys] = st
         return st
 
@@ -317,8 +322,10 @@ class NeuralGCMModel(nn.Module):
         return time_integration.step_with_filters(raw, filters)
 
     def _use_fused(self, state: State) -> bool:
-        return (state.vorticity.is_cuda and self.use_fused_dycore and self._nanoscope_ctx is None
-                and getattr(self._dycore, "use_fused", True))
+        if self.shard is not None:
+            return True  # the sharded model exists only as the packed step
+        return ((state.vorticity.is_cuda or self.packed_on_cpu) and self.use_fused_dycore
+                and self._nanoscope_ctx is None and getattr(self._dycore, "use_fused", True))
 
     # ── outer step ────────────────────────────────────────────────────
     def step(self, state: State, forcings: dict | None = None, memory=None) -> State:
@@ -353,8 +360,19 @@ class NeuralGCMModel(nn.Module):
                     if (self._step_count % self._fixer_cadence == 0 and fixer is not None
                             and hasattr(fixer, "forward_packed") and not self._diagnostics_enabled):
                         with record_function("Z2_physics_bridge"):
-                            y = fixer.forward_packed(y, y_start, self.config.coords.vertical.layers)
+                            n_lev = self.config.coords.vertical.layers
+                            if self.shard is not None:
+                                from tornado_gcm_b200.parallel.spectral_shard import sharded_packed_fix
+
+                                y = sharded_packed_fix(y, y_start, n_lev, self.shard.group, fixer.fix_mass,
+                                                       fixer.fix_energy, fixer.energy_split)
+                            else:
+                                y = fixer.forward_packed(y, y_start, n_lev)
                         fixed_in_packed = True
+                    elif (self.shard is not None and fixer is not None
+                          and self._step_count % self._fixer_cadence == 0):
+                        raise NotImplementedError("a sharded model step needs a fixer with a packed form "
+                                                  "(LiteConservationFixer)")
                     state = spectral.unpack_state(y, self.config.coords.vertical.layers, keys, state.sim_time)
                 else:
                     inner = self._build_inner_step_fn(phys)

@@ -89,6 +89,10 @@ class HybridGCM(nn.Module):
         # physics steps per recomputed segment (0: the whole 6-h block); at 0.7° one
         # physics step keeps ~2 GB of tower activations, so a 72-step block does not fit
         self.checkpoint_segment = 0
+        # a model sharded over W ranks (parallel.spectral_shard.shard_hybrid_gcm) sees 1/W of
+        # every field: its local mean squared error counts 1/W towards the global loss
+        self.loss_scale = 1.0
+        self.shard = None
 
     def normalize_forcings(self, forcings: dict) -> dict:
         out = {}
@@ -140,7 +144,7 @@ class HybridGCM(nn.Module):
         total = 0.0
         for pred, tgt in zip(preds, targets):
             total = total + sum(((pred[k] - tgt[k]) ** 2).mean() for k in DATA_FIELDS) / len(DATA_FIELDS)
-        return total / len(targets)
+        return total * (self.loss_scale / len(targets))
 
     def forward(self, data0: dict, forcings: dict, outer_steps: int):
         return self.rollout(data0, forcings, outer_steps)[1]

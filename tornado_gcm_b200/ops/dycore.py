@@ -345,6 +345,8 @@ class FusedSIL3:
 # ── packed-state SIL3 (the production GPU path) ─────────────────────────────
 def _synth_lat(x3: torch.Tensor, grid) -> torch.Tensor:
     """(S, M2, L) modal (possibly a padded-row view) → (S, J, I) nodal."""
+    if getattr(grid, "sharded", False):
+        return grid.to_nodal_lat_major(x3)
     if x3.is_cuda:
         from tornado_gcm_b200.ops import sht as sht_ops
 
@@ -354,6 +356,8 @@ def _synth_lat(x3: torch.Tensor, grid) -> torch.Tensor:
 
 def _anal_lat(n3: torch.Tensor, grid) -> torch.Tensor:
     """(S, J, I) nodal → (S, M2, L) modal."""
+    if getattr(grid, "sharded", False):
+        return grid.to_modal_lat_major(n3)
     if n3.is_cuda:
         from tornado_gcm_b200.ops import sht as sht_ops
 
@@ -424,22 +428,30 @@ class PackedSIL3:
     """
 
     def __init__(self, eq: pe.PrimitiveEquationsSigma, dt: float, filter_scaling: np.ndarray, tracer_keys,
-                 clamp_abs: float = 1.0e12):
+                 clamp_abs: float = 1.0e12, grid=None):
+        """``grid``: a sharded grid (parallel.spectral_shard.ShardedGrid) for a model
+        step spread over ranks: modal rows of the owned wavenumbers, nodal rows of
+        the owned latitude block; ``None`` runs on the equation's full grid."""
         from tornado_gcm_b200.ops import spectral
 
         self.eq = eq
+        self.grid = grid if grid is not None else eq.grid
         self.dt = float(dt)
         self.keys = tuple(tracer_keys)
         self.n = eq.vertical.layers
-        self.pre = spectral.explicit_pre_recipe(eq, self.keys)
+        self.pre = spectral.explicit_pre_recipe(eq, self.keys, grid=self.grid)
         # the column kernel applies G to the moist tdiff term; the post recipe keeps only ∇²
-        self.post = spectral.explicit_post_recipe(eq, self.keys, g_fused=True)
+        self.post = spectral.explicit_post_recipe(eq, self.keys, g_fused=True, grid=self.grid)
         self.spec = ColumnSpec.from_equation(eq, self.keys).with_fused_g()
+        if grid is not None and getattr(grid, "sharded", False):
+            sl = grid.layout.lat_slice()
+            self.spec = dataclasses.replace(self.spec, sec2=np.asarray(self.spec.sec2)[..., sl],
+                                            cor=np.asarray(self.spec.cor)[..., sl], _dev={})
         self.ch = spectral.packed_channels(self.n, self.keys)
         self.filter_scaling = np.asarray(filter_scaling, dtype=np.float64)
         self.clamp = float(clamp_abs)
         self._dev: dict = {}
-        g = eq.grid
+        g = self.grid
         self.L = g.modal_shape[-1]
         self.Lp = (self.L + 3) // 4 * 4
 
@@ -454,9 +466,11 @@ class PackedSIL3:
             # l-fastest copies (n*n, L) for the column-parallel stage kernel
             minv_t = {e: m.reshape(m.shape[0], -1).t().contiguous() for e, m in minv.items()}
             filt = torch.as_tensor(self.filter_scaling, dtype=torch.float32, device=device)
-            g = self.eq.grid
+            g = self.grid
             oro = self.eq.orography_tendency(device, torch.float32)
-            oro = g.clip_wavenumbers(oro)
+            oro = self.eq.grid.clip_wavenumbers(oro)
+            if getattr(g, "sharded", False):
+                oro = g.layout.scatter_modal(oro)
             packed_oro = torch.zeros(self.ch["C"], *g.modal_shape, dtype=torch.float32, device=device)
             packed_oro[self.n:2 * self.n] = oro
             d = {"base": base, "minv": minv, "minv_t": minv_t, "filt": filt, "oro": packed_oro}
@@ -470,7 +484,7 @@ class PackedSIL3:
         from tornado_gcm_b200.ops import spectral
 
         B = y.shape[0]
-        grid = self.eq.grid
+        grid = self.grid
         lp = self.Lp if y.is_cuda else self.L
         x_in = spectral.spectral_linear(y, self.pre, out_lpad=lp, grad_lpad=self.L)
         S_in = self.spec.n_in

@@ -114,7 +114,9 @@ class SpectralRecipe:
         ops = _ext.require("spectral linear operator")
         L = self.grid.modal_shape[-1]
         out_lpad = L if out_lpad is None else out_lpad
-        return ops.spectral_linear(x, L, self.c_out, out_lpad, *self.tables(x.device), self.nlev)
+        # a wavenumber-sharded grid supplies |m| of each local row (for ∂/∂λ)
+        row_m = self.grid.row_wavenumbers(x.device) if hasattr(self.grid, "row_wavenumbers") else None
+        return ops.spectral_linear(x, L, self.c_out, out_lpad, *self.tables(x.device), self.nlev, row_m)
 
 
 class SpectralLinearFn(torch.autograd.Function):
@@ -170,8 +172,8 @@ def packed_channels(n: int, tracer_keys) -> dict:
     return ch
 
 
-def explicit_pre_recipe(eq, tracer_keys) -> SpectralRecipe:
-    grid = eq.grid
+def explicit_pre_recipe(eq, tracer_keys, grid=None) -> SpectralRecipe:
+    grid = eq.grid if grid is None else grid
     n = eq.vertical.layers
     inv_r = 1.0 / grid.radius
     b = _Builder(grid, n)
@@ -217,9 +219,9 @@ def explicit_pre_recipe(eq, tracer_keys) -> SpectralRecipe:
     return b.recipe(ch["C"], s)
 
 
-def explicit_post_recipe(eq, tracer_keys, g_fused: bool = False) -> SpectralRecipe:
+def explicit_post_recipe(eq, tracer_keys, g_fused: bool = False, grid=None) -> SpectralRecipe:
     """``g_fused``: the column kernel already applied G to the tdiff outputs."""
-    grid = eq.grid
+    grid = eq.grid if grid is None else grid
     n = eq.vertical.layers
     inv_r = 1.0 / grid.radius
     b = _Builder(grid, n)

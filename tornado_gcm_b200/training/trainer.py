@@ -219,7 +219,11 @@ class GCMTrainer:
 
     def __init__(self, gcm: nn.Module, lr: float = 1e-4, weight_decay: float = 0.0, max_grad_norm: float = 1.0,
                  ema_num_steps: int = 1999, graph: bool = False, betas=(0.9, 0.95), eps: float = 1e-6,
-                 data_parallel: bool = False):
+                 data_parallel: bool = False, grad_average: bool = True):
+        """``data_parallel``: replicated weights, gradients reduced over the ranks after
+        backward — averaged (data parallelism: each rank's loss is a full loss of its own
+        samples) or summed with ``grad_average=False`` (a model sharded over the ranks:
+        each rank's loss is its share of one global loss)."""
         self.gcm = gcm
         params = [p for p in gcm.parameters() if p.requires_grad]
         self.dp = None
@@ -227,7 +231,7 @@ class GCMTrainer:
         if data_parallel:
             from tornado_gcm_b200.parallel.ddp import GradientAllReducer
 
-            self.dp = GradientAllReducer(params)
+            self.dp = GradientAllReducer(params, average=grad_average)
             self.dp.broadcast_parameters()
             self.dp.zero()
             self._flat = self.dp.flat
