@@ -84,6 +84,10 @@ def parse_args():
     p.add_argument("--checkpoint-segment", type=int, default=-1,
                    help="physics steps per recomputed segment (0: whole 6-h block; default 8 at 0.7 degrees)")
     p.add_argument("--batch", type=int, default=4, help="per-GPU batch")
+    p.add_argument("--parallel", choices=["dp", "lat"], default="dp",
+                   help="train: dp = data parallel (replicated model, batch per GPU); lat = the model sharded "
+                        "over the GPUs (modal rows by zonal wavenumber, nodal columns by latitude block), all "
+                        "GPUs on one global batch of batch x GPUs samples")
     p.add_argument("--rollout", type=int, default=4, help="6-h steps per training example")
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
@@ -154,18 +158,21 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def dist_setup(gpus: int):
+def dist_setup(gpus: int, need_group: bool = False):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
+    if world > 1 or need_group:
+        os.environ.setdefault("MASTER_PORT", "29533")
+        os.environ.setdefault("WORLD_SIZE", str(world))
+        os.environ.setdefault("RANK", str(rank))
         import datetime
 
         import torch.distributed as dist
 
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     else:
         torch.cuda.set_device(0)
     return rank, world, local
@@ -232,22 +239,32 @@ def run_b200(args, rank, world):
                                   (args.checkpoint == "auto" and args.resolution not in ("2.8deg", "5.6deg")))
     gcm.checkpoint_segment = args.checkpoint_segment if args.checkpoint_segment >= 0 else (
         8 if args.resolution == "0.7deg" else 0)
-    trainer = GCMTrainer(gcm, lr=1e-4, graph=not args.no_graph, data_parallel=world > 1)
-    B, K = args.batch, args.rollout
+    lat = args.parallel == "lat"
+    shard = None
+    if lat:
+        from tornado_gcm_b200.parallel import spectral_shard as ss
+
+        ss.shard_hybrid_gcm(gcm, None, "fused")
+        shard = gcm.shard
+    trainer = GCMTrainer(gcm, lr=1e-4, graph=not args.no_graph, data_parallel=world > 1, grad_average=not lat)
+    # lat: every rank holds 1/W of each of the batch x W samples (same per-GPU work as dp)
+    B, K = (args.batch * world if lat else args.batch), args.rollout
     enc = gcm.encoder
+    local = (lambda d: ss.scatter_fields(d, shard)) if lat else (lambda d: d)
 
     def norm(d):
-        return {k: ((v.to(dev) - getattr(enc, f"mean_{k}")) / getattr(enc, f"std_{k}")).cpu() for k, v in d.items()}
+        return local({k: ((v.to(dev) - getattr(enc, f"mean_{k}")) / getattr(enc, f"std_{k}")).cpu()
+                      for k, v in d.items()})
 
-    # pinned host pool of a few batches (cycled); distinct per rank
+    # pinned host pool of a few batches (cycled); distinct per rank (dp) or shared (lat)
     pool = []
     for j in range(2):
-        s = 100 * rank + 10 * j
+        s = (0 if lat else 100 * rank) + 10 * j
         x0 = norm(data.sample(B, s))
         tg = [norm(data.sample(B, s + i + 1)) for i in range(K)]
         pool.append(({k: v.pin_memory() for k, v in x0.items()},
                      [{k: v.pin_memory() for k, v in t.items()} for t in tg]))
-    forc_host = {k: v.pin_memory() for k, v in data.forcings(B).items()}
+    forc_host = {k: v.contiguous().pin_memory() for k, v in local(data.forcings(B)).items()}
     to_dev = lambda d: {k: v.to(dev, non_blocking=True) for k, v in d.items()}
     dev_pool = [(to_dev(a), [to_dev(t) for t in b]) for a, b in pool]
     forc_dev = to_dev(forc_host)
@@ -270,7 +287,14 @@ def run_b200(args, rank, world):
     _ext.check_error_flag(dev)
     ms_per_step = ms / args.steps
     loss_last = float(losses[-1].item()) if losses else float("nan")
+    if lat and world > 1:  # each rank's loss is its share of the global loss
+        import torch.distributed as dist
 
+        t = torch.tensor([loss_last], dtype=torch.float64, device=dev)
+        dist.all_reduce(t)
+        loss_last = float(t.item())
+
+    samples_per_step = B if lat else world * B
     e2e = None
     if not args.no_e2e:
         host_loss = []
@@ -284,7 +308,7 @@ def run_b200(args, rank, world):
             host_loss.append(float(loss.item()))  # D2H read of the step's result
 
         ms_e2e, _ = timed_region(step_e2e, args.steps, world, None)
-        e2e = {"value": world * B * K / (ms_e2e / args.steps / 1000.0), "unit": E2E_UNIT,
+        e2e = {"value": samples_per_step * K / (ms_e2e / args.steps / 1000.0), "unit": E2E_UNIT,
                "h2d_bytes_per_step": int(h2d_bytes), "d2h_bytes_per_step": 4,
                "ms_per_step": ms_e2e / args.steps}
 
@@ -316,7 +340,7 @@ def run_b200(args, rank, world):
     except Exception as exc:  # pragma: no cover
         launches = {"error": str(exc)}
 
-    value = world * B * K / (ms_per_step / 1000.0)
+    value = samples_per_step * K / (ms_per_step / 1000.0)
     if rank == 0:
         out = {
             "metric": METRIC,
@@ -335,10 +359,11 @@ def run_b200(args, rank, world):
                 "model": f"{args.resolution} {spec.grid} L{spec.layers} hybrid GCM (encoder 3x256, tower 5x"
                          f"{spec.tower_width}, decoder 3x256, IMEX-SIL3 dt={spec.dt_minutes:g} min, "
                          f"{spec.physics_steps_per_output} physics steps per 6 h)",
-                "global_batch": world * B,
+                "global_batch": samples_per_step,
                 "seq_len": K,
                 "seq_len_meaning": "6-h rollout steps per example (backprop through the whole rollout)",
-                "parallelism": f"dp{world}",
+                "parallelism": (f"lat{world} (modal rows by zonal wavenumber, nodal columns by latitude block; "
+                                f"transposes fused into the Legendre GEMMs)") if lat else f"dp{world}",
                 "zones": "Z1 TF32 tcgen05 transforms, Z3 BF16 tcgen05 towers, Z2 FP64-accumulated fixer",
                 "grad_reducer": trainer.dp.backend if trainer.dp is not None else "none (one rank)",
                 "cuda_graph": trainer.use_graph,
@@ -688,16 +713,16 @@ def run_reference_forecast(args, rank, world):
 
 def main():
     args = parse_args()
-    rank, world, local = dist_setup(args.gpus)
+    rank, world, local = dist_setup(args.gpus, need_group=args.parallel == "lat" and args.impl == "b200")
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
         else:
             run_b200(args, rank, world)
     finally:
-        if world > 1:
-            import torch.distributed as dist
+        import torch.distributed as dist
 
+        if dist.is_initialized():
             dist.barrier()
             dist.destroy_process_group()
 

@@ -199,6 +199,29 @@ def test_colsum_bf16_accumulates_in_place():
     assert _rel(out, ref) < 1e-5
 
 
+@pytest.mark.parametrize("name,S", [("T21", 5), ("TL63", 33), ("TL127", 3)])
+def test_fp64_transforms_vs_cpu_fp64(name, S):
+    """FP64 tensor-core transforms (Z0 / "highest") against the CPU float64 contraction, and adjoints."""
+    _require()
+    g = _grid(name, "highest")
+    x = _modal(g, S, seed=3)
+    ref_n = g.to_nodal(x)
+    out_n = g.to_nodal(x.to(DEV))
+    assert out_n.dtype == torch.float64 and _rel(out_n.cpu(), ref_n) < 1e-13
+    ref_m = g.to_modal(ref_n)
+    out_m = g.to_modal(ref_n.to(DEV))
+    assert _rel(out_m.cpu(), ref_m) < 1e-13
+    # adjoint identities through autograd
+    xr = x.to(DEV).requires_grad_(True)
+    y = torch.randn(S, *g.nodal_shape, dtype=torch.float64, device=DEV)
+    (g.to_nodal(xr) * y).sum().backward()
+    assert abs(float((g.to_nodal(x.to(DEV)) * y).sum() - (x.to(DEV) * xr.grad).sum())) < 1e-10 * float(y.abs().sum())
+    nr = ref_n.to(DEV).requires_grad_(True)
+    z = torch.randn(S, *g.modal_shape, dtype=torch.float64, device=DEV)
+    (g.to_modal(nr) * z).sum().backward()
+    assert abs(float((g.to_modal(ref_n.to(DEV)) * z).sum() - (ref_n.to(DEV) * nr.grad).sum())) < 1e-10 * float(z.abs().sum())
+
+
 def test_fused_sil3_gpu_matches_cpu():
     _require()
     from tornado_gcm_b200.core import filtering, primitive_equations as pe

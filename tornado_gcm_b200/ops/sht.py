@@ -11,8 +11,8 @@ weighted DFT analysis followed by Legendre analysis.  Both are
 
 Bases are built once per grid in FP64, cast to fp32 and kept on the device:
 ``P (Mw, J, Lp)``, ``Pt (Mw, L, J)``, ``F (I, M2p)``, ``Ft (M2, I)``, ``w (J)``.
-The "highest" precision setting runs FP64 torch contractions instead (the
-numerical oracle mode).
+The "highest" precision setting runs the FP64 transforms on the FP64 tensor
+cores instead (``csrc/dgemm.cu``; the Z0 zone and the numerical oracle mode).
 """
 
 from __future__ import annotations
@@ -165,13 +165,73 @@ def to_modal_lat_major(n3: torch.Tensor, sh) -> torch.Tensor:
     return ToModalFn.apply(n3, bases(sh, n3.device), True)
 
 
+# ── FP64 transforms on the FP64 tensor cores (csrc/dgemm.cu) ────────────────
+# Four batched strided DGEMMs, no transposed copies:
+#   synthesis  W[k, s, j]   = sum_l x[s, k, l] p[k, j, l]           (batch: zonal row k)
+#              out[s, i, j] = sum_k F[i, k] W[k, s, j]              (batch: slice s)
+#   analysis   Z[k, s, j]   = w_j sum_i F[i, k] x[s, i, j]          (batch: slice s)
+#              out[s, k, l] = sum_j Z[k, s, j] p[k, j, l]           (batch: zonal row k)
+# with p the per-row Legendre table (M2, J, L).  The adjoint of synthesis is
+# the unweighted analysis and the adjoint of analysis the weighted synthesis.
+def _f64_synth(x3: torch.Tensor, sh, weighted: bool) -> torch.Tensor:
+    ops = _ext.require("FP64 synthesis")
+    S, M2, L = x3.shape
+    p = sh.device_basis("p", x3.device, torch.float64)
+    f = sh.device_basis("f", x3.device, torch.float64)
+    I, J = f.shape[0], p.shape[1]
+    x3 = x3.to(torch.float64).contiguous()
+    if weighted:
+        p = p * sh.device_basis("w", x3.device, torch.float64)[None, :, None]
+    W = torch.empty(M2, S, J, dtype=torch.float64, device=x3.device)
+    ops.dgemm_strided(x3, p, W, S, J, L, M2, [M2 * L, 1, L], [L, 1, J * L], [J, 1, S * J], 1.0, 0.0, None)
+    out = torch.empty(S, I, J, dtype=torch.float64, device=x3.device)
+    ops.dgemm_strided(f, W, out, I, J, M2, S, [M2, 1, 0], [1, S * J, J], [J, 1, I * J], 1.0, 0.0, None)
+    return out
+
+
+def _f64_anal(n3: torch.Tensor, sh, weighted: bool) -> torch.Tensor:
+    ops = _ext.require("FP64 analysis")
+    S, I, J = n3.shape
+    p = sh.device_basis("p", n3.device, torch.float64)
+    f = sh.device_basis("f", n3.device, torch.float64)
+    M2, L = p.shape[0], p.shape[2]
+    n3 = n3.to(torch.float64).contiguous()
+    w = sh.device_basis("w", n3.device, torch.float64) if weighted else None
+    Z = torch.empty(M2, S, J, dtype=torch.float64, device=n3.device)
+    ops.dgemm_strided(f, n3, Z, M2, J, I, S, [1, M2, 0], [1, J, I * J], [S * J, 1, J], 1.0, 0.0, w)
+    out = torch.empty(S, M2, L, dtype=torch.float64, device=n3.device)
+    ops.dgemm_strided(Z, p, out, S, L, J, M2, [J, 1, S * J], [1, L, J * L], [M2 * L, 1, L], 1.0, 0.0, None)
+    return out
+
+
+class _F64SynthFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x3, sh):
+        ctx.sh = sh
+        return _f64_synth(x3, sh, False)
+
+    @staticmethod
+    def backward(ctx, g):
+        return _f64_anal(g, ctx.sh, False), None
+
+
+class _F64AnalFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, n3, sh):
+        ctx.sh = sh
+        return _f64_anal(n3, sh, True)
+
+    @staticmethod
+    def backward(ctx, g):
+        return _f64_synth(g, ctx.sh, True), None
+
+
 def _highest(x, sh, inverse: bool):
-    p = sh.device_basis("p", x.device, torch.float64)
-    f = sh.device_basis("f", x.device, torch.float64)
-    x64 = x.to(torch.float64)
-    if inverse:
-        out = torch.einsum("im,...mj->...ij", f, torch.einsum("mjl,...ml->...mj", p, x64))
-    else:
-        w = sh.device_basis("w", x.device, torch.float64)
-        out = torch.einsum("mjl,...mj->...ml", p, torch.einsum("im,...ij->...mj", f, x64 * w))
-    return out.to(x.dtype)
+    """FP64 transform of a CUDA tensor on the FP64 tensor cores; the result keeps ``x``'s dtype."""
+    lead = x.shape[:-2]
+    x3 = x.reshape((-1,) + tuple(x.shape[-2:]))
+    if x3.shape[0] == 0:
+        shape = (sh.longitude_nodes, sh.latitude_nodes) if inverse else tuple(sh.modal_shape)
+        return x.new_zeros(lead + shape)
+    out = _F64SynthFn.apply(x3, sh) if inverse else _F64AnalFn.apply(x3, sh)
+    return out.reshape(lead + tuple(out.shape[-2:])).to(x.dtype)

@@ -289,6 +289,14 @@ class FusedTransforms:
             self._out_cap = cap
         torch.cuda.synchronize(device)
 
+    def _grow(self, device, w_numel: int = 0, out_numel: int = 0) -> None:
+        # every rank makes the same sequence of transform calls, so every rank
+        # reaches this collective re-allocation at the same call
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("sharded transform buffers must be sized before CUDA-graph capture "
+                               "(run a warm-up step first or call prepare())")
+        self._ensure(device, w_numel, out_numel)
+
     def prepare(self, device, max_slices: int) -> None:
         """Reserve buffers for up to ``max_slices`` fields per call (collective; call on every rank)."""
         lay = self.lay
@@ -313,8 +321,8 @@ class FusedTransforms:
         if not (x3.stride(-1) == 1 and (x3.stride(-2) * 4) % 16 == 0 and (x3.stride(0) * 4) % 16 == 0
                 and x3.data_ptr() % 16 == 0):
             x3 = torch.nn.functional.pad(x3, (0, lay.Lp - lay.L)).contiguous()[..., :lay.L]
-        if lay.M2 * S * lay.Jr > self._w_cap:
-            raise RuntimeError(f"sharded synthesis of {S} fields exceeds the reserved buffers; call prepare()")
+        if lay.M2 * S * lay.Jr > self._w_cap or self._pad is None:
+            self._grow(dev, w_numel=lay.M2 * S * lay.Jr)
         k = self._k_w
         self._k_w ^= 1
         wbuf, wtab = self._w[k]
@@ -333,8 +341,8 @@ class FusedTransforms:
         S = n_lat.shape[0]
         b = self.bases(dev)
         n = S * lay.M2_loc * lay.Lp
-        if n > self._out_cap:
-            raise RuntimeError(f"sharded analysis of {S} fields exceeds the reserved buffers; call prepare()")
+        if n > self._out_cap or self._pad is None:
+            self._grow(dev, out_numel=n)
         k = self._k_out
         self._k_out ^= 1
         obuf, otab = self._out[k]
