@@ -164,3 +164,29 @@ def test_packed_parameterization_matches_state_path():
     gref = torch.cat([x if x is not None else torch.zeros_like(t)
                       for x, t in zip(gref, st_leaves + [trs[k] for k in keys])], dim=-3)
     torch.testing.assert_close(gy, gref, rtol=2e-3, atol=1e-6)
+
+
+def test_bounds_checked_recipe_skips_out_of_range_terms_on_cpu():
+    import copy
+
+    from tornado_gcm_b200.ops import _ext, spectral
+
+    if not _ext.available():
+        pytest.skip("extension not built")
+    eq, _, _ = _setup(4)
+    rec = spectral.explicit_pre_recipe(eq, ("specific_humidity",))
+    bad = copy.copy(rec)
+    bad.terms = [copy.copy(t) for t in rec.terms]
+    bad._dev, bad._transpose = {}, None
+    bad.terms[0].pre = 99  # no such diagonal
+    clean = copy.copy(rec)
+    clean.terms = rec.terms[1:]
+    clean._dev, clean._transpose = {}, None
+    x = torch.randn(1, rec.c_in, *eq.grid.modal_shape)
+    ops = _ext.require("bounds checks")
+    ops.set_bounds_check(True)
+    try:
+        y = bad.apply(x)
+    finally:
+        ops.set_bounds_check(False)
+    torch.testing.assert_close(y, clean.apply(x), rtol=0, atol=0)

@@ -497,3 +497,36 @@ def test_token_tower_path_matches_permuted_path():
     assert _rel(a[0], b[0]) < 2e-2 and _rel(a[1], b[1]) < 3e-2
     for ga, gb in zip(a[2], b[2]):
         assert _rel(ga, gb) < 3e-2
+
+
+def test_bounds_checked_recipe_records_error_and_skips_bad_term():
+    """Debug mode: a recipe term whose source channel is out of range is skipped and
+    reported as error code 5 instead of being read."""
+    _require()
+    import copy
+
+    from tornado_gcm_b200.ops import spectral
+
+    eq = _eq("T21", 8)
+    rec = spectral.explicit_pre_recipe(eq, ("specific_humidity",))
+    bad = copy.copy(rec)
+    bad.terms = [copy.copy(t) for t in rec.terms]
+    bad._dev, bad._transpose = {}, None
+    victim = bad.terms[3]
+    victim.src = rec.c_in  # one channel past the input
+    clean = copy.copy(rec)
+    clean.terms = [t for i, t in enumerate(rec.terms) if i != 3]
+    clean._dev, clean._transpose = {}, None
+    x = torch.randn(2, rec.c_in, *eq.grid.modal_shape, device=DEV)
+    ops = _ext.require("bounds checks")
+    _ext.check_error_flag(DEV)
+    ops.set_bounds_check(True)
+    try:
+        y = bad.apply(x)
+        torch.cuda.synchronize()
+        with pytest.raises(RuntimeError, match="code 5"):
+            _ext.check_error_flag(DEV)
+    finally:
+        ops.set_bounds_check(False)
+    torch.testing.assert_close(y, clean.apply(x), rtol=0, atol=0)
+    assert _ext.check_error_flag(DEV) == 0

@@ -418,7 +418,7 @@ static void check_peer_table(const at::Tensor& ptrs, int64_t world) {
 // group).  Writes W_d[row(m)][s*Jr + (j - d*Jr)] on rank d = j / Jr, where W_d
 // is the (M2, S*Jr) buffer at w_ptrs[d].
 void sht_synth_routed(const at::Tensor& x, int64_t L, const at::Tensor& P_loc, const at::Tensor& group_m,
-                      const at::Tensor& w_ptrs, int64_t Jr, const c10::optional<at::Tensor>& err) {
+                      const at::Tensor& w_ptrs, int64_t Jr, int64_t M2_full, const c10::optional<at::Tensor>& err) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kFloat && x.dim() == 3, "x must be a (S, M2, L) fp32 CUDA tensor");
   TORCH_CHECK(x.stride(2) == 1 && (x.stride(1) * 4) % 16 == 0 && (x.stride(0) * 4) % 16 == 0 &&
                   reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0,
@@ -441,6 +441,7 @@ void sht_synth_routed(const at::Tensor& x, int64_t L, const at::Tensor& P_loc, c
   p.a_pair = 1; p.k_tri = 1;
   p.c_pair = 1; p.c_ps = Jr; p.c_pmr = S * Jr; p.c_sc = 1;
   p.route_mode = 1; p.route_cols = static_cast<int>(Jr); p.group_map = group_m.data_ptr<int>();
+  p.route_rows = static_cast<int>(M2_full);
   p.n_peers = static_cast<int>(J / Jr);
   for (int i = 0; i < p.n_peers; ++i) p.peer_C[i] = reinterpret_cast<float*>(w_ptrs.data_ptr<int64_t>()[i]);
   p.err = err_ptr(err);
@@ -515,7 +516,7 @@ void sht_anal_routed(const at::Tensor& N_in, const at::Tensor& Ft, const at::Ten
     p.tiles_m = cdiv(S, 64); p.tiles_n = cdiv(L, bnl);
     p.a_pair = 1;
     p.c_pair = 1; p.c_ps = M2_loc * Lo; p.c_pmr = Lo; p.c_sc = 1;
-    p.route_mode = 2; p.group_map = group_dest.data_ptr<int>();
+    p.route_mode = 2; p.group_map = group_dest.data_ptr<int>(); p.route_rows = static_cast<int>(M2_loc);
     p.n_peers = static_cast<int>(world);
     for (int i = 0; i < p.n_peers; ++i) p.peer_C[i] = reinterpret_cast<float*>(out_ptrs.data_ptr<int64_t>()[i]);
     p.err = err_ptr(err);
@@ -689,7 +690,8 @@ TORCH_LIBRARY_FRAGMENT(tgcm, m) {
   m.def("sht_synth(Tensor x, int L, Tensor P, Tensor F, Tensor ws, Tensor? col_scale, Tensor? err, bool lat_major) -> Tensor");
   m.def("sht_anal(Tensor N, Tensor Ft, Tensor Pt, int Lo, Tensor ws, Tensor? col_scale, Tensor? err, bool lat_major, "
         "Tensor? peer_ptrs=None) -> Tensor");
-  m.def("sht_synth_routed(Tensor x, int L, Tensor P_loc, Tensor group_m, Tensor w_ptrs, int Jr, Tensor? err) -> ()");
+  m.def("sht_synth_routed(Tensor x, int L, Tensor P_loc, Tensor group_m, Tensor w_ptrs, int Jr, int M2_full, "
+        "Tensor? err) -> ()");
   m.def("sht_synth_dft(Tensor W, int S, int Jr, Tensor F, Tensor? err) -> Tensor");
   m.def("sht_anal_routed(Tensor N, Tensor Ft, Tensor Pt_loc, int Lo, int M2_loc, Tensor ws, Tensor group_dest, "
         "Tensor out_ptrs, Tensor? err) -> ()");

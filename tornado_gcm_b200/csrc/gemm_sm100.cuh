@@ -81,6 +81,7 @@ struct GemmParams {
   //    2·gl-1+pm, 0 for gl = 0), added with system-scope reductions.
   int route_mode;
   int route_cols;
+  int route_rows;    // rows of each destination buffer (entries beyond it: kErrBounds, skipped)
   const int* group_map;
 };
 
@@ -448,6 +449,10 @@ __device__ __noinline__ void epilogue_routed(const GemmParams& p, uint32_t taddr
     const int gl = gm & 0xffff;
     ok = ok && !(g == 0 && pm == 1) && !(gl == 0 && pm == 1);
     row = gl == 0 ? 0 : 2 * gl - 1 + pm;
+  }
+  if (ok && (row >= p.route_rows || dst < 0 || dst >= p.n_peers)) {  // a corrupt routing table
+    record_error(p.err, kErrBounds);
+    ok = false;
   }
   const long long row_off = static_cast<long long>(s_idx) * c_ps + static_cast<long long>(row) * c_pmr;
 #pragma unroll 1

@@ -59,7 +59,30 @@ struct LinearArgs {
   // |m| = (r + 1) / 2).  A wavenumber-sharded layout keeps the (cos, sin) rows
   // of one m adjacent at odd/even positions, so only |m| needs the table.
   const int* row_m;
+  // Bounds-checked mode (ops.set_bounds_check): every term's channel, stencil,
+  // diagonal and matrix indices are checked before use; a bad term records
+  // kErrBounds in *err and is skipped instead of being dereferenced.
+  int check;
+  int* err;
+  int C_in, n_diag, n_mats;
 };
+
+__host__ __device__ __forceinline__ bool term_in_bounds(const LinearArgs& a, int src, int st, int pre, int post,
+                                                        int mat, int row) {
+  if (st < 0 || st > 7 || pre < -1 || pre >= a.n_diag || post < -1 || post >= a.n_diag) return false;
+  if (st == 6 || st == 7)  // vertical terms read an n-level block and one matrix row
+    return mat >= 0 && mat < a.n_mats && row >= 0 && row < a.nlev && src >= 0 && src + a.nlev <= a.C_in;
+  return src >= 0 && src < a.C_in;
+}
+
+__host__ __device__ __forceinline__ bool term_rejected(const LinearArgs& a, int src, int st, int pre, int post,
+                                                       int mat, int row) {
+  if (!a.check || term_in_bounds(a, src, st, pre, post, mat, row)) return false;
+#ifdef __CUDA_ARCH__
+  if (a.err != nullptr) atomicCAS(a.err, 0, 5 /* kErrBounds */);
+#endif
+  return true;
+}
 
 __host__ __device__ __forceinline__ int row_wavenumber(const LinearArgs& a, int mr) {
   return a.row_m ? a.row_m[mr] : (mr + 1) >> 1;
@@ -126,6 +149,7 @@ __host__ __device__ inline void linear_point(const LinearArgs& a, int b, int s, 
   float acc = 0.f;
   for (int t = a.row_ptr[s]; t < a.row_ptr[s + 1]; ++t) {
     const int* T = a.terms + 7 * t;
+    if (term_rejected(a, T[1], T[2], T[3], T[4], T[5], T[6])) continue;
     float v = stencil_val(a, b, T[1], T[2], T[3], mr, l, T[5], T[6]);
     if (T[4] >= 0) v *= a.diag[T[4] * a.L + l];
     acc += a.coef[t] * v;
@@ -191,6 +215,8 @@ __global__ void __launch_bounds__(kLinThreads) spectral_linear_kernel(LinearArgs
   float acc = 0.f;
   for (int t = t0; t < t1; ++t) {
     const int* T = a.terms + 7 * t;
+    if (term_rejected(a, __ldg(T + 1), __ldg(T + 2), __ldg(T + 3), __ldg(T + 4), __ldg(T + 5), __ldg(T + 6)))
+      continue;
     float v = stencil_fast(ab, xs, __ldg(T + 1), __ldg(T + 2), __ldg(T + 3), mr, l, __ldg(T + 5), __ldg(T + 6));
     const int post = __ldg(T + 4);
     if (post >= 0) v *= __ldg(a.diag + post * a.L + l);
@@ -235,6 +261,7 @@ __global__ void __launch_bounds__(32 * kRowWarps, (NL <= 3 ? 4 : 2)) spectral_li
     const int* T = a.terms + 7 * t;
     const int src = __ldg(T + 1), st = __ldg(T + 2), pre = __ldg(T + 3), post = __ldg(T + 4);
     const float cf = __ldg(a.coef + t);
+    if (term_rejected(a, src, st, pre, post, __ldg(T + 5), __ldg(T + 6))) continue;
     if (st == kStVert || st == kStVertT) {
       const int mat = __ldg(T + 5), row = __ldg(T + 6);
 #pragma unroll
@@ -394,6 +421,7 @@ __global__ void __launch_bounds__(32 * kRowWarps, (PfOcc<NL, NB>::value)) spectr
   };
   // source row of a non-vertical term (the paired ±m row for ∂/∂λ); -1: term contributes nothing
   auto source_row = [&](const PfTerm& m) -> int {
+    if (a.check && !term_in_bounds(a, m.src, m.st, m.pre, m.post, m.mat, m.row)) return -1;
     if (m.st == kStVert || m.st == kStVertT) return -1;
     if (m.st == kStDlon) return mr == 0 ? -1 : ((mr & 1) ? mr + 1 : mr - 1);
     return mr;
@@ -425,6 +453,7 @@ __global__ void __launch_bounds__(32 * kRowWarps, (PfOcc<NL, NB>::value)) spectr
       for (int j = 0; j < NL; ++j) xv[q][j] = xn[q][j];
     if (i + 1 < nt) issue(i + 1, xn);
     const PfTerm m = term(i);
+    if (term_rejected(a, m.src, m.st, m.pre, m.post, m.mat, m.row)) continue;
     if (m.st == kStVert || m.st == kStVertT) {
 #pragma unroll
       for (int q = 0; q < NB; ++q) {
@@ -559,11 +588,18 @@ static void launch_rows(const LinearArgs& a, cudaStream_t st) {
     launch_rows_nb<NL, 1>(a, st);
 }
 
+// Bounds-checked mode of the table-driven kernels (debug; off by default).
+static bool g_bounds_check = false;
+
+void set_bounds_check(bool on) { g_bounds_check = on; }
+
+bool bounds_check_enabled() { return g_bounds_check; }
+
 // x: (B, C_in, M2, Lx) ; returns y: (B, C_out, M2, Ly) with Ly = out_lpad (>= L), pad zero.
 at::Tensor spectral_linear(const at::Tensor& x, int64_t L, int64_t C_out, int64_t out_lpad, const at::Tensor& row_ptr,
                            const at::Tensor& terms, const at::Tensor& coef, const at::Tensor& diag,
                            const at::Tensor& rec_a, const at::Tensor& rec_b, const at::Tensor& mats, int64_t nlev,
-                           const c10::optional<at::Tensor>& row_m) {
+                           const c10::optional<at::Tensor>& row_m, const c10::optional<at::Tensor>& err) {
   TORCH_CHECK(x.dim() == 4 && x.scalar_type() == at::kFloat && x.stride(3) == 1, "x must be (B, C, M2, L) fp32");
   const int64_t B = x.size(0), M2 = x.size(2);
   // the CUDA kernel writes the padding columns itself; the CPU loop does not
@@ -583,6 +619,11 @@ at::Tensor spectral_linear(const at::Tensor& x, int64_t L, int64_t C_out, int64_
   a.mats = mats.data_ptr<float>();
   a.nlev = static_cast<int>(nlev);
   a.B = static_cast<int>(B); a.C_out = static_cast<int>(C_out); a.M2 = static_cast<int>(M2); a.L = static_cast<int>(L);
+  a.check = g_bounds_check ? 1 : 0;
+  a.err = (err.has_value() && err->defined() && err->is_cuda() == x.is_cuda()) ? err->data_ptr<int>() : nullptr;
+  a.C_in = static_cast<int>(x.size(1));
+  a.n_diag = static_cast<int>(diag.size(0));
+  a.n_mats = static_cast<int>(mats.size(0));
   a.row_m = nullptr;
   if (row_m.has_value() && row_m->defined()) {
     TORCH_CHECK(row_m->scalar_type() == at::kInt && row_m->numel() == M2 && row_m->is_contiguous() &&
@@ -1152,7 +1193,9 @@ std::vector<at::Tensor> sil3_stage_adjoint(const at::Tensor& gout, const at::Ten
 
 TORCH_LIBRARY_FRAGMENT(tgcm, m) {
   m.def("spectral_linear(Tensor x, int L, int C_out, int out_lpad, Tensor row_ptr, Tensor terms, Tensor coef, "
-        "Tensor diag, Tensor rec_a, Tensor rec_b, Tensor mats, int nlev, Tensor? row_m=None) -> Tensor");
+        "Tensor diag, Tensor rec_a, Tensor rec_b, Tensor mats, int nlev, Tensor? row_m=None, Tensor? err=None) -> Tensor");
+  m.def("set_bounds_check(bool on) -> ()", &tgcm::set_bounds_check);
+  m.def("bounds_check_enabled() -> bool", &tgcm::bounds_check_enabled);
   m.def("sil3_stage(Tensor y0, Tensor[] E, Tensor P, Tensor? y2, float[] ce, float cp, float cg, float eta, "
         "Tensor G, Tensor H, Tensor Minv, Tensor lam, Tensor tref, Tensor dsig, Tensor? filt, float clamp_abs, "
         "float R, int final_stage, int n, Tensor? minv_t=None) -> Tensor");

@@ -68,6 +68,14 @@ def empty(*shape, dtype, device) -> torch.Tensor:
     return t
 
 
+def set_bounds_check(on: bool) -> None:
+    """Bounds-checked mode of the table-driven kernels: every index read from a
+    table (recipe terms: channels, stencils, diagonals, matrices) is checked on
+    the device before use; a bad one records error code 5 in the device error
+    flag and is skipped instead of dereferenced (:func:`check_error_flag` raises)."""
+    require("bounds checks").set_bounds_check(bool(on))
+
+
 def error_flag(device) -> torch.Tensor:
     """Per-device int32 flag that kernels set on a bounded-wait timeout."""
     key = str(device)
@@ -89,5 +97,6 @@ def check_error_flag(device) -> int:
     code = int(f.item())
     if code:
         f.zero_()
-        raise RuntimeError(f"tornado_gcm_b200 kernel reported error code {code} (bounded wait expired)")
+        what = "index out of bounds" if code == 5 else "bounded wait expired"
+        raise RuntimeError(f"tornado_gcm_b200 kernel reported error code {code} ({what})")
     return 0

@@ -116,7 +116,8 @@ class SpectralRecipe:
         out_lpad = L if out_lpad is None else out_lpad
         # a wavenumber-sharded grid supplies |m| of each local row (for ∂/∂λ)
         row_m = self.grid.row_wavenumbers(x.device) if hasattr(self.grid, "row_wavenumbers") else None
-        return ops.spectral_linear(x, L, self.c_out, out_lpad, *self.tables(x.device), self.nlev, row_m)
+        err = _ext.error_flag(x.device) if x.is_cuda else None
+        return ops.spectral_linear(x, L, self.c_out, out_lpad, *self.tables(x.device), self.nlev, row_m, err)
 
 
 class SpectralLinearFn(torch.autograd.Function):

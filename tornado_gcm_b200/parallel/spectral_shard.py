@@ -327,7 +327,7 @@ class FusedTransforms:
         self._k_w ^= 1
         wbuf, wtab = self._w[k]
         flag = _ext.error_flag(dev)
-        ops.sht_synth_routed(x3, lay.L, b.Pw_loc if weighted else b.P_loc, b.group_m, wtab, lay.Jr, flag)
+        ops.sht_synth_routed(x3, lay.L, b.Pw_loc if weighted else b.P_loc, b.group_m, wtab, lay.Jr, lay.M2, flag)
         self._barrier(dev, flag)
         return ops.sht_synth_dft(wbuf[: lay.M2 * S * lay.Jr], S, lay.Jr, b.F, flag)
 
