@@ -2,11 +2,12 @@
 
 Multi-head attention with optional QK layer-norm (ViT-22B style), a pre-norm
 block with optional cross-attention, encoder / decoder stacks and a
-sinusoidal positional encoding.  Attention runs through
-``torch.nn.functional.scaled_dot_product_attention`` (the fused attention
-kernels on the GPU) instead of materialising the score matrix and a separate
-softmax; self-attention projects Q, K and V with one GEMM over the
-concatenated weights.  Parameter names (``q_proj`` / ``k_proj`` / ``v_proj`` /
+sinusoidal positional encoding.  On the GPU, unmasked attention runs on this
+framework's column-attention kernel (``csrc/attention.cu``: one warp per
+(column, head), online softmax in fp32, forward and backward, no score
+matrix in memory); masked or biased attention and CPU tensors use
+``torch.nn.functional.scaled_dot_product_attention``.  Self-attention
+projects Q, K and V with one GEMM over the concatenated weights.  Parameter names (``q_proj`` / ``k_proj`` / ``v_proj`` /
 ``out_proj``, ``ln1`` / ``ln_cross`` / ``ln2`` / ``ffn``) match the reference so
 its state dicts load unchanged.
 
@@ -22,6 +23,48 @@ from typing import Callable, Optional
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
+
+
+class ColumnAttentionFn(torch.autograd.Function):
+    """softmax(q kᵀ · scale) v over ``(G, S, D)`` tensors with the kernel pair of ``csrc/attention.cu``."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, scale: float):
+        from tornado_gcm_b200.ops import _ext
+
+        ops = _ext.require("column attention")
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        o, lse = ops.column_attention_fwd(q, k, v, float(scale))
+        ctx.save_for_backward(q, k, v, o, lse)
+        ctx.scale = float(scale)
+        return o
+
+    @staticmethod
+    def backward(ctx, g):
+        from tornado_gcm_b200.ops import _ext
+
+        q, k, v, o, lse = ctx.saved_tensors
+        dq, dk, dv = _ext.require("column attention backward").column_attention_bwd(
+            q, k, v, o, g.contiguous().to(o.dtype), lse, ctx.scale)
+        return dq, dk, dv, None
+
+
+def column_attention_supported(q: torch.Tensor, k: torch.Tensor) -> bool:
+    """Shapes and dtypes the column-attention kernel takes."""
+    from tornado_gcm_b200.ops import _ext
+
+    D = q.shape[-1]
+    return (q.is_cuda and _ext.available() and q.dtype in (torch.float32, torch.bfloat16) and k.dtype == q.dtype
+            and D in (8, 16, 32, 64) and q.shape[-2] <= 128 and k.shape[-2] <= 128 and k.shape[-2] * D <= 7264)
+
+
+def column_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    """``(…, S, D)`` attention (no mask) on the column-attention kernel."""
+    lead = q.shape[:-2]
+    D = q.shape[-1]
+    out = ColumnAttentionFn.apply(q.reshape(-1, q.shape[-2], D), k.reshape(-1, k.shape[-2], D),
+                                  v.reshape(-1, v.shape[-2], D), 1.0 / math.sqrt(D))
+    return out.reshape(lead + out.shape[-2:])
 
 
 class MultiHeadAttention(nn.Module):
@@ -71,6 +114,9 @@ class MultiHeadAttention(nn.Module):
         q, k, v = (self._heads(t) for t in self._project(query, key, value))
         if self.normalize_qk:
             q, k = self.q_ln(q), self.k_ln(k)
+        if attention_bias is None and mask is None and column_attention_supported(q, k):
+            out = column_attention(q, k, v.to(q.dtype))
+            return self.out_proj(out.transpose(-3, -2).flatten(-2))
         attn_mask = None
         if attention_bias is not None:
             attn_mask = attention_bias.to(q.dtype)
