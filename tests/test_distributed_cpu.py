@@ -159,3 +159,17 @@ def test_rank_failure_detected_and_survivors_resume(tmp_path):
         assert out["attempts"] == 2 and out["world"] == 2
         # steps 0-2 summed over 3 ranks, steps 3-5 over the 2 survivors
         assert out["result"] == 3 * 3 + 3 * 2
+
+
+def test_transport_selection_on_cpu():
+    from tornado_gcm_b200.parallel.transport import GlooTransport, NVLinkTransport, get_transport
+
+    assert isinstance(get_transport("auto", device="cpu"), GlooTransport)
+    assert isinstance(get_transport("nvlink"), NVLinkTransport)
+    with pytest.raises(ValueError):
+        get_transport("carrier-pigeon")
+    t = get_transport("gloo")
+    red = t.gradient_reducer(10, "cpu")
+    red.flat.fill_(3.0)
+    red.all_reduce_mean(red.flat)  # one process: unchanged
+    assert float(red.flat.sum()) == 30.0

@@ -201,10 +201,10 @@ class GradientAllReducer:
         want_fused = (use_fused and self.world > 1 and dev.type == "cuda"
                       and os.environ.get("TGCM_FUSED_ALLREDUCE", "1") != "0")
         if want_fused:
-            from tornado_gcm_b200.parallel import fused_allreduce
+            from tornado_gcm_b200.parallel.transport import get_transport
 
             try:
-                self.fused = fused_allreduce.make_reducer(self.numel, dev)
+                self.fused = get_transport("nvlink", device=dev).gradient_reducer(self.numel, dev)
             except Exception as exc:
                 raise RuntimeError(f"fused gradient all-reduce requested but unavailable: {exc}; "
                                    "set TGCM_FUSED_ALLREDUCE=0 to use NCCL") from exc

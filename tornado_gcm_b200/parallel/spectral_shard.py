@@ -555,14 +555,20 @@ class ShardedGrid:
 
 
 def make_sharded_grid(grid: sh.Grid, group=None, engine: str = "auto", device=None) -> ShardedGrid:
-    """The sharded view of ``grid`` for this rank of ``group`` (``engine``: auto | fused | collective)."""
+    """The sharded view of ``grid`` for this rank of ``group``.
+
+    ``engine``: ``fused`` (NVLink transport: routed Legendre epilogues),
+    ``collective`` (NCCL on CUDA, gloo on the CPU), a transport name, or
+    ``auto`` (:func:`tornado_gcm_b200.parallel.transport.get_transport`).
+    """
+    from tornado_gcm_b200.parallel.transport import get_transport
+
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     lay = ShardLayout(grid, world, rank)
-    dev = torch.device(device) if device is not None else None
-    if engine == "auto":
-        engine = "fused" if (dev is not None and dev.type == "cuda") else "collective"
-    eng = FusedTransforms(lay, group) if engine == "fused" else CollectiveTransforms(lay, group)
+    kind = {"fused": "nvlink", "collective": "gloo" if device is None or torch.device(device).type == "cpu"
+            else "nccl"}.get(engine, engine)
+    eng = get_transport(kind, group, device).spectral_engine(lay)
     return ShardedGrid(grid, lay, eng, group)
 
 
