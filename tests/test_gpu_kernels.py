@@ -400,6 +400,9 @@ def test_poison_mode_leaves_train_step_unchanged():
 
 
 def test_latitude_sharded_sht_on_device():
+    """Replicated-modal latitude sharding (transform-only component): the FP64 partial quadratures of
+    emulated ranks, computed on the device, sum to the full-grid transform."""
+    _require()
     from tornado_gcm_b200.parallel.sharded_sht import LatitudeShardedSHT
 
     g = _grid("TL63", "highest")

@@ -184,6 +184,8 @@ static void gemm_dispatch(int fmt, int bn, bool a_mn, bool b_mn, const CUtensorM
     launch_cfg<F, B, AM, BM>(ta, tb, p, st);                     \
     return;                                                      \
   }
+  TGCM_CASE(2, 16, false, false)
+  TGCM_CASE(2, 32, false, false)
   TGCM_CASE(2, 64, false, false)
   TGCM_CASE(2, 128, false, false)
   TGCM_CASE(2, 256, false, false)
@@ -432,7 +434,14 @@ void sht_synth_routed(const at::Tensor& x, int64_t L, const at::Tensor& P_loc, c
   TORCH_CHECK(M2l <= 2 * G - 1 + 1 && Lp >= L && L <= x.size(2), "layout mismatch");
   TORCH_CHECK(Jr > 0 && Jr % 4 == 0 && J % Jr == 0, "latitude blocks must be multiples of 4 rows");
   check_peer_table(w_ptrs, J / Jr);
-  const int bnj = pick_bn_j(J);
+  // tile width: a divisor of the latitude block where one exists, so that every
+  // tile has one destination rank (staged, coalesced peer stores)
+  int bnj = pick_bn_j(J);
+  for (int cand : {256, 128, 64, 32, 16})
+    if (cand <= bnj && Jr % cand == 0) {
+      bnj = cand;
+      break;
+    }
   CUtensorMap ta = make_tmap(x.data_ptr(), 2, L, M2l, S, x.stride(1) * 4, x.stride(0) * 4, 32, 2, 64);
   CUtensorMap tb = make_tmap(P_loc.data_ptr(), 2, L, J, G, Lp * 4, J * Lp * 4, 32, bnj, 1);
   GemmParams p = default_params();

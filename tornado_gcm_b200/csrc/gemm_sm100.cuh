@@ -496,16 +496,22 @@ __device__ __noinline__ void epilogue_routed(const GemmParams& p, uint32_t taddr
 // by alpha.  The 32 x 32 chunk is staged in shared memory; with 16-byte
 // aligned rows eight lanes cover one row with 16-byte stores, otherwise the
 // 32 lanes write 32 consecutive values of one row per instruction.
+//
+// The routed (sharded-transform) tiles use the same path with a per-tile
+// destination: Cdst = the owning rank's buffer, g the wavenumber index of the
+// destination rows, col_shift subtracted from the column index, and `reduce`
+// turning the 16-byte stores into system-scope 16-byte reductions.
 template <int BN>
 __device__ __noinline__ void epilogue_pair_rows(const GemmParams& p, uint32_t taddr_row, uint8_t* stage, int tm,
-                                                   int tn, int g, int q, int half, int lane) {
+                                                   int tn, int g, int q, int half, int lane, float* Cdst = nullptr,
+                                                   int col_shift = 0, int reduce = 0) {
   // Parameters are read once into registers: `p` is reached through a generic
   // pointer here, so every global store below would otherwise force the
   // compiler to load the fields again.
   const int S = p.M / 2, N = p.N;
   const long long c_ps = p.c_ps, c_pmr = p.c_pmr;
   const float alpha = p.alpha;
-  float* __restrict__ C = reinterpret_cast<float*>(p.C);
+  float* __restrict__ C = (Cdst != nullptr ? Cdst : reinterpret_cast<float*>(p.C)) - col_shift;
   const bool vec = (reinterpret_cast<uintptr_t>(C) % 16 == 0) && (c_ps % 4 == 0) && (c_pmr % 4 == 0);
   auto row_off = [&](int r, bool* ok) -> long long {
     const int s_idx = tm * 64 + (r >> 1);
@@ -546,10 +552,19 @@ __device__ __noinline__ void epilogue_pair_rows(const GemmParams& p, uint32_t ta
         const uint8_t* sp = stage + rr * kStageRowF32 + seg * 16;
         float* gp = C + off + col0 + seg * 4;
         if (seg * 4 + 4 <= ncols) {
-          *reinterpret_cast<float4*>(gp) = *reinterpret_cast<const float4*>(sp);
+          const float4 v4 = *reinterpret_cast<const float4*>(sp);
+          if (reduce)
+            red_add_sys_v4(gp, v4.x, v4.y, v4.z, v4.w);
+          else
+            *reinterpret_cast<float4*>(gp) = v4;
         } else {
           const float* se = reinterpret_cast<const float*>(sp);
-          for (int e = 0; seg * 4 + e < ncols; ++e) gp[e] = se[e];
+          for (int e = 0; seg * 4 + e < ncols; ++e) {
+            if (reduce)
+              red_add_sys(gp + e, se[e]);
+            else
+              gp[e] = se[e];
+          }
         }
       }
     } else {
@@ -558,7 +573,12 @@ __device__ __noinline__ void epilogue_pair_rows(const GemmParams& p, uint32_t ta
       for (int rr = 0; rr < 32; ++rr) {
         bool ok;
         const long long off = row_off(q * 32 + rr, &ok);
-        if (ok && lane < ncols) C[off + col0 + lane] = sf[rr * (kStageRowF32 / 4) + lane];
+        if (ok && lane < ncols) {
+          if (reduce)
+            red_add_sys(C + off + col0 + lane, sf[rr * (kStageRowF32 / 4) + lane]);
+          else
+            C[off + col0 + lane] = sf[rr * (kStageRowF32 / 4) + lane];
+        }
       }
     }
     __syncwarp();
@@ -822,7 +842,38 @@ __device__ __forceinline__ void gemm_sm100_body(const CUtensorMap& tmap_a, const
                           !p.aux && !p.grad_pre && p.act == 0 && !p.out_bf16 && p.n_peers == 0 &&
                           (reinterpret_cast<uintptr_t>(p.C) % 16 == 0) && ((p.c_sr * 4) % 16 == 0) &&
                           ((p.c_sg * 4) % 16 == 0);
-      if (red_ok) {
+      // Routed tiles of the sharded transforms: every tile has one destination rank
+      // (analysis: the owner of wavenumber g; synthesis: the owner of the tile's
+      // latitude block when the block width is a multiple of BN) and goes through
+      // the staged, coalesced pair-row path; other synthesis tiles use the per-lane
+      // routed path.
+      int r_dst = -1, r_g = 0, r_shift = 0;
+      if (p.route_mode == 2) {
+        const int gm = __ldg(p.group_map + g);
+        r_dst = gm >> 16;
+        r_g = gm & 0xffff;
+        if (r_dst >= p.n_peers || 2 * r_g >= p.route_rows) {
+          record_error(p.err, kErrBounds);
+          r_dst = -2;
+        }
+      } else if (p.route_mode == 1 && p.route_cols % BN == 0) {
+        r_g = __ldg(p.group_map + g);
+        r_dst = (tn * BN) / p.route_cols;
+        r_shift = r_dst * p.route_cols;
+        if (r_g < 0) {
+          r_dst = -2;  // empty wavenumber slot: nothing to store
+        } else if (r_dst >= p.n_peers || 2 * r_g >= p.route_rows) {
+          record_error(p.err, kErrBounds);
+          r_dst = -2;
+        }
+      }
+      if (r_dst == -2) {
+        // nothing to write for this tile; fall through to release the accumulator
+      } else if (r_dst >= 0) {
+        uint8_t* stage = reinterpret_cast<uint8_t*>(staging) + (warp - 2) * (32 * kStageRowF32);
+        epilogue_pair_rows<BN>(p, taddr_row, stage, tm, tn, r_g, q, half, lane, p.peer_C[r_dst], r_shift,
+                               p.route_mode == 2);
+      } else if (red_ok) {
         uint8_t* stage = reinterpret_cast<uint8_t*>(staging) + (warp - 2) * (32 * kStageRowF32);
         epilogue_splitk_red<BN>(p, taddr_row, stage, tm, tn, g, q, half, lane);
       } else if (p.c_pair && p.c_sc == 1 && plain) {

@@ -76,9 +76,16 @@ def set_bounds_check(on: bool) -> None:
     require("bounds checks").set_bounds_check(bool(on))
 
 
+def _flag_key(device) -> str:
+    d = torch.device(device)
+    if d.type == "cuda" and d.index is None:
+        d = torch.device("cuda", torch.cuda.current_device())
+    return str(d)
+
+
 def error_flag(device) -> torch.Tensor:
     """Per-device int32 flag that kernels set on a bounded-wait timeout."""
-    key = str(device)
+    key = _flag_key(device)
     t = _FLAGS.get(key)
     if t is None:
         t = torch.zeros(1, dtype=torch.int32, device=device)
@@ -91,7 +98,7 @@ _FLAGS: dict = {}
 
 def check_error_flag(device) -> int:
     """Read (and clear) the device error flag; raises on a recorded timeout."""
-    f = _FLAGS.get(str(device))
+    f = _FLAGS.get(_flag_key(device))
     if f is None:
         return 0
     code = int(f.item())
