@@ -79,6 +79,11 @@ def parse_args():
     p.add_argument("--mode", choices=["train", "forecast"], default="train",
                    help="train: backprop through the rollout (default); forecast: ensemble 6-h forecast")
     p.add_argument("--members", type=int, default=16, help="forecast: ensemble members per GPU")
+    p.add_argument("--fsdp", action="store_true",
+                   help="forecast: shard the column tower's weights over the GPUs; every GEMM reads the other "
+                        "ranks' rows from their memory as it runs (all-gather fused into the GEMM)")
+    p.add_argument("--save-forecast", default=None,
+                   help="forecast: write the last 6-h output of rank 0 to this .pt file (for comparisons)")
     p.add_argument("--checkpoint", choices=["auto", "on", "off"], default="auto",
                    help="train: recompute each 6-h block in backward (auto: on above 2.8 degrees)")
     p.add_argument("--checkpoint-segment", type=int, default=-1,
@@ -404,24 +409,38 @@ def run_b200_forecast(args, rank, world):
     dev = torch.device("cuda", torch.cuda.current_device())
     gcm, data = build_hybrid_gcm(args.resolution, dev, seed=0)
     spec = RESOLUTIONS[args.resolution]
-    engine = MPInference(gcm)
-    M, K = args.members, args.steps
+    lat = args.parallel == "lat"
+    M, K = (args.members * world if lat else args.members), args.steps
     enc = gcm.encoder
     grid = gcm.model.config.coords.horizontal
     grf = GaussianRandomField(grid, correlation_length_km=1000.0, variance=1.0).to(dev)
-    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    # lat: one ensemble of members x GPUs shared by all ranks (each holds its latitude block)
+    gen = torch.Generator(device=dev).manual_seed(1234 + (0 if lat else rank))
     with torch.no_grad():
         ens = {}
-        for k, v in data.sample(1, 100 * rank).items():
+        for k, v in data.sample(1, 0 if lat else 100 * rank).items():
             x = (v.to(dev) - getattr(enc, f"mean_{k}")) / getattr(enc, f"std_{k}")
             noise = grid.to_nodal(grf.sample_modal((M,) + tuple(x.shape[1:-2]), generator=gen, device=dev))
             ens[k] = (x + noise).contiguous()
+    forc_full = data.forcings(M)
+    if lat:
+        from tornado_gcm_b200.parallel import spectral_shard as ss
+
+        ss.shard_hybrid_gcm(gcm, None, "fused")
+        ens = ss.scatter_fields(ens, gcm.shard)
+        forc_full = ss.scatter_fields(forc_full, gcm.shard)
+    if args.fsdp:
+        gcm.model.parameterization.shard_tower_weights()
+    engine = MPInference(gcm)
     ens_host = {k: v.cpu().pin_memory() for k, v in ens.items()}
-    forc_host = {k: v.pin_memory() for k, v in data.forcings(M).items()}
+    forc_host = {k: v.contiguous().pin_memory() for k, v in forc_full.items()}
     forc_dev = {k: v.to(dev) for k, v in forc_host.items()}
 
+    members_total = M if lat else world * M
     warm = engine.rollout(ens, max(1, args.warmup), forcings=forc_dev)  # graph capture + warm-up
     finite = all(bool(torch.isfinite(v).all()) for v in warm[-1].values())
+    if args.save_forecast and rank == 0:
+        torch.save({k: v.detach().cpu() for k, v in warm[-1].items()}, args.save_forecast)
     torch.cuda.synchronize()
     _ext.check_error_flag(dev)
     sampler = ClockSampler(device_uuid()) if rank == 0 else None
@@ -441,7 +460,7 @@ def run_b200_forecast(args, rank, world):
         ms_e2e, _ = timed_region(e2e_run, 1, world, None)
         h2d = sum(v.numel() * v.element_size() for v in ens_host.values())
         h2d += sum(v.numel() * v.element_size() for v in forc_host.values())
-        e2e = {"value": world * M * K / (ms_e2e / 1000.0),
+        e2e = {"value": members_total * K / (ms_e2e / 1000.0),
                "unit": "6h model-steps/s (ensemble members x 6-h steps, all GPUs), end to end",
                "h2d_bytes_per_step": int(h2d / K), "d2h_bytes_per_step": int(d2h),
                "h2d_note": "initial ensemble + forcings copied once per forecast, amortised over its steps",
@@ -469,7 +488,7 @@ def run_b200_forecast(args, rank, world):
     except Exception as exc:  # pragma: no cover
         launches = {"error": str(exc)}
 
-    value = world * M * K / (ms / 1000.0)
+    value = members_total * K / (ms / 1000.0)
     if rank == 0:
         print(json.dumps({
             "metric": METRIC, "mode": "forecast", "value": value,
@@ -481,10 +500,13 @@ def run_b200_forecast(args, rank, world):
             "config": {
                 "model": f"{args.resolution} {spec.grid} L{spec.layers} hybrid GCM (tower 5x{spec.tower_width}, "
                          f"IMEX-SIL3 dt={spec.dt_minutes:g} min, {spec.physics_steps_per_output} physics steps per 6 h)",
-                "global_batch": world * M, "seq_len": K,
+                "global_batch": members_total, "seq_len": K,
                 "seq_len_meaning": "6-h forecast steps (one timed rollout)",
-                "parallelism": f"dp{world} (ensemble members over GPUs)",
-                "members_per_gpu": M, "perturbation": "GRF sigma=1 (normalised units), 1000 km",
+                "parallelism": ((f"lat{world} (model sharded over GPUs: modal rows by wavenumber, nodal columns "
+                                 f"by latitude block)" if lat else f"dp{world} (ensemble members over GPUs)")
+                                + (", tower weights FSDP-sharded (all-gather fused into the GEMM)"
+                                   if args.fsdp else "")),
+                "members_per_gpu": args.members, "perturbation": "GRF sigma=1 (normalised units), 1000 km",
                 "outputs_finite_after_warmup": finite,
                 "zones": "Z1 TF32 tcgen05 transforms, Z3 BF16 tcgen05 towers, Z2 FP64-accumulated fixer",
                 "cuda_graph": True,

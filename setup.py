@@ -25,7 +25,7 @@ setup(
     name="tornado_gcm_b200",
     version="0.1.0",
     packages=find_packages(include=["tornado_gcm_b200", "tornado_gcm_b200.*"]),
-    package_data={"tornado_gcm_b200": ["configs/*.yaml", "data/*.csv"]},
+    package_data={"tornado_gcm_b200": ["configs/*.yaml", "data/*.csv", "data/*.json"]},
     ext_modules=[
         CUDAExtension(
             name="tornado_gcm_b200._C",

@@ -170,3 +170,46 @@ def test_sharded_model_matches_one_gpu():
         assert flag == 0
         assert abs(l_shd - l_ref) <= 2e-3 * abs(l_ref)   # TF32 transforms, different summation order
         assert worst < 3e-2
+
+
+def _worker_fsdp(rank, world, port, q):
+    try:
+        dist = _init(rank, world, port)
+        from tornado_gcm_b200.models.builders import build_hybrid_gcm
+        from tornado_gcm_b200.ops import _ext
+        from tornado_gcm_b200.parallel import spectral_shard as ss
+
+        dev = torch.device("cuda", rank)
+        gcm, data = build_hybrid_gcm("2.8deg", dev, seed=0)
+        ss.shard_hybrid_gcm(gcm, None, "fused")
+        enc = gcm.encoder
+        norm = {k: ((v.to(dev) - getattr(enc, f"mean_{k}")) / getattr(enc, f"std_{k}"))
+                for k, v in data.sample(3, 0).items()}
+        forc = ss.scatter_fields({k: v.to(dev) for k, v in data.forcings(3).items()}, gcm.shard)
+        with torch.no_grad():
+            f = gcm.normalize_forcings(forc)
+            s0 = gcm.encoder(ss.scatter_fields(norm, gcm.shard), f)
+            outs = []
+            for fsdp in (False, True):
+                if fsdp:
+                    gcm.model.parameterization.shard_tower_weights()
+                s = s0
+                for _ in range(3):
+                    s = gcm.model.step(s, f)
+                outs.append(gcm.decoder(s, f))
+        err = max(_rel(outs[1][k], outs[0][k]) for k in outs[0])
+        torch.cuda.synchronize(dev)
+        q.put((rank, err, _ext.check_error_flag(dev)))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:  # pragma: no cover - reported to the parent
+        q.put((rank, traceback.format_exc()))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fsdp_tower_weights_match_replicated_weights():
+    """Sharded model with the tower's weights FSDP-sharded (GEMMs read peer rows as they run)
+    gives the decoded forecast of the replicated-weight run."""
+    for _, err, flag in _spawn(_worker_fsdp, 2):
+        assert flag == 0
+        assert err < 1e-3

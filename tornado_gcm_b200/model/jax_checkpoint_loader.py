@@ -288,3 +288,122 @@ def load_jax_hybrid(flat: dict, device: str | torch.device = "cpu", resolution: 
                 "%s hybrid model", len(report["loaded"]), copied, resolution)
     gcm.jax_load_report = {**report, "linear_layers_copied": copied}
     return gcm
+
+
+# ── the runnable 2.8° NeuralGCM model ────────────────────────────────────────
+# The checkpoint's physics step: TL63 (128 x 64 Gaussian grid), 32 equidistant
+# sigma layers, dt = 0.525024 (one hour in the checkpoint's time unit), five
+# dycore substeps, dycore filter tau 120 min order 3, stability filter
+# tau 4 min order 10 cutoff 0.4 (also applied to the parameterization's
+# tendencies), FP64 conservation fixer.  Features: surface embeddings (land /
+# sea / sea-ice towers), the vertical conv tower's 32 CNN1D features,
+# pressure, radiation, latitude, prognostics with their gradients and
+# Laplacians, memory values, geopotential at the surface (with gradients),
+# land-sea mask and the learned positional features -> ShiftAndNormalize ->
+# InverseLevelScale (humidity) -> SoftClip(16), 2365 channels in sorted-key
+# order into the physics EPD; its 192 outputs -> InverseShiftAndNormalize
+# (global scale 0.02) -> humidity level scales -> (zeta, delta, T', tracers)
+# tendencies.  Normalisation statistics: data/neuralgcm_2p8deg_normalization.json.
+JAX_DT_NONDIM = 0.525024
+JAX_DYCORE_SUBSTEPS = 5
+_STATS_FILE = Path(__file__).resolve().parent.parent / "data" / "neuralgcm_2p8deg_normalization.json"
+
+
+def jax_normalization_stats() -> dict:
+    import json
+
+    with open(_STATS_FILE, encoding="utf-8") as fh:
+        st = json.load(fh)
+    cnn = {f"CNN1D_{i}": st["cnn_feature_scale"] for i in range(st["n_cnn_features"])}
+    cnn_shift = {f"CNN1D_{i}": st["cnn_feature_shift"] for i in range(st["n_cnn_features"])}
+    st["advance_scales"] = {**cnn, **st["feature_scales"]}
+    st["advance_shifts"] = {**cnn_shift, **st["feature_shifts"]}
+    return st
+
+
+def build_jax_aligned_model(checkpoint: str | Path | dict | None = None, device: str | torch.device = "cpu",
+                            strict: bool = True, geopotential_at_surface: Optional[torch.Tensor] = None,
+                            land_sea_mask: Optional[torch.Tensor] = None):
+    """NeuralGCM 2.8° deterministic model wired to :class:`JaxNeuralComponents` — reference
+    ``model/jax_checkpoint_loader.py:885-1241`` (``build_jax_aligned_experiment_model``).
+
+    ``checkpoint``: a pickle path or an already flattened parameter dict; the
+    weights are loaded with the strict path map (every leaf mapped, every
+    parameter filled).  ``geopotential_at_surface`` / ``land_sea_mask``
+    ``(1, lon, lat)`` come from the checkpoint's auxiliary data (zeros when
+    absent).  Returns ``(model, components, coords, config, report)``.
+    """
+    from tornado_gcm_b200.core import coordinate_systems, filtering, sigma_coordinates, spherical_harmonic
+    from tornado_gcm_b200.models.api import ModelConfig, NeuralGCMModel
+    from tornado_gcm_b200.neural import features as ft
+    from tornado_gcm_b200.neural import transforms as tr
+    from tornado_gcm_b200.neural.fixers import F64ConservationFixer
+    from tornado_gcm_b200.neural.parameterizations import JaxAlignedDivCurlParameterization
+    from tornado_gcm_b200.neural.towers import ForwardTower
+    from tornado_gcm_b200.precision.policy import PrecisionPolicy
+    from tornado_gcm_b200.utils.units import SimUnits, minutes_to_nondim
+
+    stats = jax_normalization_stats()
+    grid = spherical_harmonic.Grid.TL63()
+    vertical = sigma_coordinates.SigmaCoordinates.equidistant(N_SIGMA_LAYERS)
+    coords = coordinate_systems.CoordinateSystem(grid, vertical)
+    I, J = grid.nodal_shape
+    geo = geopotential_at_surface if geopotential_at_surface is not None else torch.zeros(1, I, J)
+    lsm = land_sea_mask if land_sea_mask is not None else torch.zeros(1, I, J)
+
+    comps = JaxNeuralComponents()
+    report = None
+    if checkpoint is not None:
+        flat = checkpoint if isinstance(checkpoint, dict) else read_jax_checkpoint(checkpoint)
+        report = load_jax_weights(comps, {k: v for k, v in flat.items() if k.startswith("params/")}, strict=strict)
+
+    scales, shifts = stats["advance_scales"], stats["advance_shifts"]
+    fields = ["divergence", "vorticity", "u", "v", "temperature_variation", "log_surface_pressure",
+              "specific_humidity", "specific_cloud_liquid_water_content", "specific_cloud_ice_water_content"]
+    norm = (scales, shifts)
+    surface = ft.EmbeddingSurfaceFeatures(
+        grid, ForwardTower(comps.surface_epd[0], feature_axis=-3), ForwardTower(comps.surface_epd[1], feature_axis=-3),
+        ForwardTower(comps.surface_epd[2], feature_axis=-3), lsm.clone(), norm, norm, norm)
+    volume = ft.EmbeddingVolumeFeatures(grid, comps.volume_conv, vertical.centers, n_output=VOLUME_CONV_OUT,
+                                        feature_name="CNN1D", embedding_scales=scales, embedding_shifts=shifts)
+    extractor = ft.CombinedFeatures([
+        surface, volume, ft.PressureFeatures(grid, vertical.centers), ft.RadiationFeatures(grid),
+        ft.LatitudeFeatures(grid),
+        ft.VelocityAndPrognostics(grid, fields_to_include=fields, compute_gradients_fn=tr.ToModalDiffOperators(grid)),
+        ft.MemoryVelocityAndValues(grid, fields_to_include=fields, compute_gradients_fn=None),
+        ft.FloatDataFeatures(grid, {"geopotential_at_surface": geo}, compute_gradients_fn=tr.ToModalDiffOperators(grid)),
+        ft.FloatDataFeatures(grid, {"land_sea_mask": lsm}, compute_gradients_fn=None),
+        ft.LearnedPositionalFeatures(comps.physics_positional),
+    ])
+    feature_transform = tr.SequentialTransform([
+        tr.ShiftAndNormalize(shifts=shifts, scales=scales),
+        tr.InverseLevelScale(["specific_humidity", "specific_humidity_del2", "specific_humidity_dlat",
+                              "specific_humidity_dlon"], stats["humidity_inverse_level_scales"]),
+        tr.SoftClip(max_value=16.0, hinge_softness=1.0),
+    ])
+    tendency_transform = tr.SequentialTransform([
+        tr.InverseShiftAndNormalize(shifts=stats["tendency_shifts"], scales=stats["tendency_scales"],
+                                    global_scale=stats["tendency_global_scale"]),
+        tr.TendencyTransform(level_scales={"specific_humidity": torch.tensor(
+            stats["tendency_humidity_level_scales"], dtype=torch.float32)}),
+    ])
+    dycore_att = JAX_DT_NONDIM / minutes_to_nondim(120.0)
+    stab_att = JAX_DT_NONDIM / minutes_to_nondim(4.0)
+    param = JaxAlignedDivCurlParameterization(grid, ForwardTower(comps.physics_epd, feature_axis=-3), extractor,
+                                              feature_transform, tendency_transform, n_levels=N_SIGMA_LAYERS)
+    param.filter_fn = filtering.exponential_filter(grid, attenuation=stab_att, order=10, cutoff=0.4)
+    # orography from the surface geopotential (m^2/s^2 over the squared velocity scale)
+    vel2 = (6371220.0 * 2 * 7.292e-5) ** 2
+    orography = grid.to_modal(geo[0].double() / vel2).float()
+    cfg = ModelConfig(coords=coords, dt=JAX_DT_NONDIM, dycore_substeps=JAX_DYCORE_SUBSTEPS,
+                      physics_specs=SimUnits.from_si(), reference_temperature=np.asarray(
+                          stats["reference_temperatures"]), orography=orography,
+                      cloud_keys=("specific_cloud_liquid_water_content", "specific_cloud_ice_water_content"),
+                      precision_policy=PrecisionPolicy(), filter_attenuation=dycore_att, filter_order=3,
+                      filter_cutoff=0.0, stability_filter_attenuation=stab_att, stability_filter_order=10,
+                      stability_filter_cutoff=0.4)
+    model = NeuralGCMModel(cfg, param, F64ConservationFixer(energy_split="reference")).to(device)
+    comps = comps.to(device)
+    config = {"resolution": "2.8", "n_levels": N_SIGMA_LAYERS, "dt_hours": 1.0, "grid": "TL63",
+              "latent_size": LATENT_SIZE, "num_blocks": NUM_BLOCKS, "physics_features": PHYSICS_EPD_INPUT}
+    return model, comps, coords, config, report

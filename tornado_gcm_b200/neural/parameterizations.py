@@ -252,8 +252,23 @@ class NodalColumnParameterization(nn.Module):
                 ex = f.permute(0, 3, 2, 1).reshape(B * J * I, nf).to(torch.bfloat16).contiguous()
         fin, fout = self._lat_factors_2d(nod.device)
         tok = tok_ops.nodal_to_tokens(nod, fin, ex, ld)
-        hid = linear_ops.mlp_forward(tok, net.layers, net.layer_activations(), last_bf16=True)
+        fsdp = self.__dict__.get("_fsdp_layers")
+        if fsdp is not None and not torch.is_grad_enabled():
+            from tornado_gcm_b200.parallel.fsdp_gather import gathered_mlp_forward
+
+            hid = gathered_mlp_forward(fsdp, tok)[:, : self.n_outputs]
+        else:
+            hid = linear_ops.mlp_forward(tok, net.layers, net.layer_activations(), last_bf16=True)
         return tok_ops.tokens_to_nodal(hid, fout, B, J, I, ld_grad=(C + 7) // 8 * 8)
+
+    def shard_tower_weights(self, group=None) -> None:
+        """FSDP-style inference: every rank keeps 1/W of each tower layer's BF16 weight rows in
+        symmetric memory and the GEMMs read the other rows from the peers as they run (the
+        all-gather fused into the consuming GEMM, ``parallel/fsdp_gather.py``).  Used when no
+        gradient is being recorded; training keeps the replicated weights."""
+        from tornado_gcm_b200.parallel.fsdp_gather import shard_mlp
+
+        self.__dict__["_fsdp_layers"] = shard_mlp(self.tower.neural_net, group=group)
 
     def forward_packed(self, y: torch.Tensor, state_keys, forcings=None) -> torch.Tensor:
         """Packed state ``(B, C, 2M-1, L)`` → packed tendency of the same layout.

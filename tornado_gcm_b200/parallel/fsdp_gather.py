@@ -42,7 +42,10 @@ def _pad8(k: int) -> int:
 class GatheredLinear:
     """``y = act(x W^T + b)`` with ``W`` row-sharded over the ranks in symmetric memory."""
 
-    def __init__(self, weight: torch.Tensor, bias: Optional[torch.Tensor] = None, act: str = "none", group=None):
+    def __init__(self, weight: torch.Tensor, bias: Optional[torch.Tensor] = None, act: str = "none", group=None,
+                 pad_out: bool = False):
+        """``pad_out``: round the output width up to a multiple of 8 (zero weight rows), so that the
+        BF16 output rows are 16-byte aligned for the next kernel; ``out_features`` stays the layer's."""
         import torch.distributed._symmetric_memory as symm_mem
 
         _ext.require("fused all-gather linear")
@@ -52,12 +55,16 @@ class GatheredLinear:
         if self.world > 8:
             raise ValueError("at most 8 shards")
         dev = weight.device
-        self.O, K = weight.shape
+        self.out_features, K = weight.shape
+        if pad_out and self.out_features % 8:
+            weight = torch.cat([weight, weight.new_zeros(_pad8(self.out_features) - self.out_features, K)], 0)
+            if bias is not None:
+                bias = torch.cat([bias, bias.new_zeros(_pad8(self.out_features) - self.out_features)], 0)
+        self.O = weight.shape[0]
         self.Kp = _pad8(K)
+        # shards of a multiple of 16 rows in rank order; trailing ranks may own no row
         self.rows = -(-self.O // self.world)
         self.rows = (self.rows + 15) // 16 * 16
-        if self.rows * (self.world - 1) >= self.O:
-            raise ValueError(f"{self.O} rows cannot be split over {self.world} ranks in multiples of 16")
         self.act = _ACT[act]
         shard = symm_mem.empty(self.rows * self.Kp, dtype=torch.bfloat16, device=dev)
         shard.zero_()
@@ -101,11 +108,20 @@ class GatheredLinear:
         return out.reshape(x.shape[:-1] + (self.O,))
 
 
-def shard_mlp(mlp, act: str = "gelu_tanh", group=None) -> list:
-    """GatheredLinear for every layer of an Mlp (hidden layers use ``act``, the last none)."""
+def shard_mlp(mlp, act: Optional[str] = None, group=None, pad_out: bool = True) -> list:
+    """GatheredLinear for every layer of an Mlp (its own activations unless ``act`` is given)."""
     layers = list(mlp.layers)
+    acts = mlp.layer_activations() if act is None else [act] * (len(layers) - 1) + ["none"]
     return [GatheredLinear(l.weight.detach(), l.bias.detach() if l.bias is not None else None,
-                           act if i < len(layers) - 1 else "none", group) for i, l in enumerate(layers)]
+                           acts[i] or "none", group, pad_out=pad_out) for i, l in enumerate(layers)]
+
+
+def gathered_mlp_forward(layers: list, x: torch.Tensor) -> torch.Tensor:
+    """BF16 token rows through sharded layers; returns the last layer's padded BF16 rows."""
+    h = x
+    for lin in layers:
+        h = lin(h)
+    return h
 
 
 def _time(fn, iters: int, warmup: int) -> float:
