@@ -617,3 +617,35 @@ def test_fused_rollout_and_gradient_vs_fp64_cpu_oracle():
     for a, b in zip(g_g, g_c):
         assert _rel(a, b) < 3e-2
     assert _ext.check_error_flag(DEV) == 0
+
+
+@pytest.mark.parametrize("batch,c,levels,lon,lat", [((2,), 9, 32, 8, 4), ((), 5, 37, 6, 3)])
+def test_level_conv_tower_vs_torch_conv(batch, c, levels, lon, lat):
+    """Vertical conv tower on the lowered tcgen05 GEMMs against fp32 nn.Conv1d with BF16 operands."""
+    _require()
+    from tornado_gcm_b200.neural.towers import VerticalConvTower
+    from tornado_gcm_b200.ops import levelconv
+
+    torch.manual_seed(3)
+    tower = VerticalConvTower(c, 32, channels=(64, 48), kernel_size=5).to(DEV)
+    x = torch.randn(*batch, c, levels, lon, lat, device=DEV, requires_grad=True)
+    assert levelconv.supports(tower, x)
+    y = tower(x)
+    # fp32 reference with the same BF16 rounding of operands
+    bf = lambda t: t.to(torch.bfloat16).float()
+    xr = x.detach().clone().requires_grad_(True)
+    h = xr.movedim((-2, -1), (-4, -3)).reshape(-1, c, levels)
+    n = len(tower.layers)
+    for i, lyr in enumerate(tower.layers):
+        cv = lyr.conv
+        h = torch.nn.functional.conv1d(bf(h), bf(cv.weight), cv.bias, padding=cv.kernel_size[0] // 2)
+        if i < n - 1:
+            h = torch.relu(h)
+    yr = h.reshape(*batch, lon, lat, 32, levels).movedim((-4, -3), (-2, -1))
+    assert y.shape == yr.shape and _rel(y, yr) < 2e-2
+    gy = torch.randn_like(yr)
+    params = [p for lyr in tower.layers for p in lyr.conv.parameters()]
+    g1 = torch.autograd.grad(y, [x] + params, gy)
+    g2 = torch.autograd.grad(yr, [xr] + params, gy)
+    for a, b in zip(g1, g2):
+        assert _rel(a, b) < 3e-2

@@ -90,6 +90,12 @@ class VerticalConvTower(nn.Module):
         self.activate_final = activate_final
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if x.is_cuda:
+            from tornado_gcm_b200.ops import levelconv
+
+            if levelconv.supports(self, x):
+                # level convolutions as tcgen05 GEMMs on (column, level) token rows
+                return levelconv.level_conv_tower(self, x)
         *batch, c, levels, lon, lat = x.shape
         xt = x.movedim((-2, -1), (-4, -3)).reshape(-1, c, levels)
         xt = _net_dtype(self, xt)
