@@ -12,7 +12,7 @@ A 6-h model step is ``6 h / dt`` physics steps; the neural tendency is
 called every physics step and each physics step is one IMEX-SIL3 dycore
 substep followed by the dycore (τ = 120 min, order 3), stability
 (τ = 4 min, order 10, cutoff 0.4) and hyperdiffusion (∇⁴, τ = 12 h at the
-largest wavenumber) spectral filters.  Data enter through a column
+largest wavenumber; 3 h at 0.7°) spectral filters.  Data enter through a column
 encoder (3 × 256) from 7 fields on 37 pressure levels and leave through
 a column decoder back to the same fields; the Z2 fixer restores mass and
 the energy proxy with FP64 accumulation every physics step.
@@ -51,6 +51,8 @@ class ResolutionSpec:
     outer_hours: float = 6.0
     encoder_width: int = 256
     encoder_hidden_layers: int = 3
+    # ∇⁴ hyperdiffusion e-folding time at the truncation wavenumber
+    hyperdiffusion_hours: float = 12.0
 
     @property
     def physics_steps_per_output(self) -> int:
@@ -60,7 +62,8 @@ class ResolutionSpec:
 RESOLUTIONS = {
     "2.8deg": ResolutionSpec("2.8deg", "TL63", 20.0, 384),
     "1.4deg": ResolutionSpec("1.4deg", "TL127", 10.0, 512),
-    "0.7deg": ResolutionSpec("0.7deg", "TL255", 5.0, 768),
+    # TL255: a 3-h hyperdiffusion time scale damps the near-truncation growth of random-init rollouts
+    "0.7deg": ResolutionSpec("0.7deg", "TL255", 5.0, 768, hyperdiffusion_hours=3.0),
     # small configuration for tests and CPU demonstrations: T21 (64 x 32 grid), 8 levels, dt 2 h
     "5.6deg": ResolutionSpec("5.6deg", "T21", 120.0, 32, tower_hidden_layers=2, layers=8, encoder_width=32,
                              encoder_hidden_layers=1),
@@ -219,7 +222,7 @@ def build_hybrid_gcm(resolution: str = "2.8deg", device: str | torch.device = "c
         stability_filter_attenuation=dt / tau_stab, stability_filter_order=10, stability_filter_cutoff=0.4,
         humidity_key="specific_humidity",
         cloud_keys=("specific_cloud_ice_water_content", "specific_cloud_liquid_water_content"),
-        hyperdiffusion_order=2, hyperdiffusion_tau=minutes_to_nondim(12 * 60.0),
+        hyperdiffusion_order=2, hyperdiffusion_tau=minutes_to_nondim(spec.hyperdiffusion_hours * 60.0),
     )
     if config_overrides:  # e.g. hyperdiffusion_tau, filter settings
         cfg = dataclasses.replace(cfg, **config_overrides)
