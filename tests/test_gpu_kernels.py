@@ -649,3 +649,38 @@ def test_level_conv_tower_vs_torch_conv(batch, c, levels, lon, lat):
     g2 = torch.autograd.grad(yr, [xr] + params, gy)
     for a, b in zip(g1, g2):
         assert _rel(a, b) < 3e-2
+
+
+@pytest.mark.parametrize("dil", [1, 2])
+def test_lonlat_conv_tower_vs_torch_conv(dil):
+    """Conv2DTower (circular in longitude, zero-padded in latitude) on the lowered tcgen05 GEMMs
+    against fp32 torch convolutions with BF16 operands."""
+    _require()
+    from tornado_gcm_b200.neural.standard_layers import ConvLonLat
+    from tornado_gcm_b200.neural.towers import Conv2DTower
+    from tornado_gcm_b200.ops import levelconv
+
+    torch.manual_seed(4)
+    tower = Conv2DTower(6, 16, channels=(24,), kernel_size=(3, 5)).to(DEV)
+    for lyr in tower.layers:
+        lyr.dilation = dil
+        lyr.conv.dilation = (dil, dil)
+    x = torch.randn(2, 6, 20, 12, device=DEV, requires_grad=True)
+    assert levelconv.supports_lonlat(tower, x)
+    y = tower(x)
+    bf = lambda t: t.to(torch.bfloat16).float()
+    xr = x.detach().clone().requires_grad_(True)
+    h = xr
+    for i, lyr in enumerate(tower.layers):
+        cv = lyr.conv
+        kl, kt = cv.kernel_size
+        hp = torch.nn.functional.pad(bf(h), (0, 0, dil * (kl // 2), dil * (kl // 2)), mode="circular")
+        hp = torch.nn.functional.pad(hp, (dil * (kt // 2), dil * (kt // 2), 0, 0))
+        h = torch.nn.functional.conv2d(hp, bf(cv.weight), cv.bias, dilation=dil)
+        if i < len(tower.layers) - 1:
+            h = torch.relu(h)
+    assert y.shape == h.shape and _rel(y, h) < 2e-2
+    gy = torch.randn_like(h)
+    params = [p for lyr in tower.layers for p in lyr.conv.parameters()]
+    for a, b in zip(torch.autograd.grad(y, [x] + params, gy), torch.autograd.grad(h, [xr] + params, gy)):
+        assert _rel(a, b) < 3e-2

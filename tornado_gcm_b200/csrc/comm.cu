@@ -190,11 +190,68 @@ void fused_allreduce_mean(at::Tensor& buf, const at::Tensor& buf_ptrs, const at:
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+namespace {
+
+// out[i, l] = sum_w slots[w][i, l] for l < L (slots: W blocks of rows x ld floats);
+// rows whose local row (i % period) is not valid are written as zeros (nobody
+// stores into them, so the slots may hold a previous call's data there).
+__global__ void slot_sum_kernel(const float* __restrict__ slots, float* __restrict__ out, int W, long long rows,
+                                int ld, int L, long long slot_stride, const int* __restrict__ valid, int period) {
+  const long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  const long long n = rows * L;
+  if (idx >= n) return;
+  const long long r = idx / L;
+  const int l = static_cast<int>(idx - r * L);
+  if (valid != nullptr && !__ldg(valid + r % period)) {
+    out[idx] = 0.f;
+    return;
+  }
+  const float* src = slots + r * ld + l;
+  float s = 0.f;
+  for (int w = 0; w < W; ++w) s += __ldg(src + w * slot_stride);
+  out[idx] = s;
+}
+
+}  // namespace
+
+// The owner's side of the sharded analysis: every rank stored its partial
+// Legendre sums into its own slot of the owner's buffer (plain peer stores);
+// after the barrier the owner adds the W slots.  slots: (W, rows, ld) fp32
+// contiguous; returns (rows, L).
+at::Tensor slot_sum(const at::Tensor& slots, int64_t W, int64_t rows, int64_t ld, int64_t L,
+                    const c10::optional<at::Tensor>& valid) {
+  TORCH_CHECK(slots.is_cuda() && slots.scalar_type() == at::kFloat && slots.is_contiguous() &&
+                  slots.numel() >= W * rows * ld && L <= ld && W >= 1,
+              "slot_sum: contiguous fp32 (W, rows, ld) slots expected");
+  c10::cuda::CUDAGuard guard(slots.device());
+  const int* vp = nullptr;
+  int period = 1;
+  if (valid.has_value() && valid->defined()) {
+    TORCH_CHECK(valid->is_cuda() && valid->scalar_type() == at::kInt && valid->is_contiguous() &&
+                    valid->numel() >= 1 && rows % valid->numel() == 0,
+                "slot_sum: valid must be an int32 CUDA vector whose length divides rows");
+    vp = valid->data_ptr<int>();
+    period = static_cast<int>(valid->numel());
+  }
+  auto out = at::empty({rows, L}, slots.options());
+  const long long n = rows * L;
+  if (n == 0) return out;
+  slot_sum_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      slots.data_ptr<float>(), out.data_ptr<float>(), static_cast<int>(W), rows, static_cast<int>(ld),
+      static_cast<int>(L), rows * ld, vp, period);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return out;
+}
+
 }  // namespace tgcm
 
 TORCH_LIBRARY_FRAGMENT(tgcm, m) {
+  m.def("slot_sum(Tensor slots, int W, int rows, int ld, int L, Tensor? valid=None) -> Tensor");
   m.def("fused_allreduce_mean(Tensor(a!) buf, Tensor buf_ptrs, Tensor pad_ptrs, int rank, int blocks, Tensor? err, float scale=0.0) -> ()");
   m.def("peer_barrier(Tensor pad_ptrs, int rank, Tensor? err, int device) -> ()", &tgcm::peer_barrier);
 }
 
-TORCH_LIBRARY_IMPL(tgcm, CUDA, m) { m.impl("fused_allreduce_mean", &tgcm::fused_allreduce_mean); }
+TORCH_LIBRARY_IMPL(tgcm, CUDA, m) {
+  m.impl("fused_allreduce_mean", &tgcm::fused_allreduce_mean);
+  m.impl("slot_sum", &tgcm::slot_sum);
+}

@@ -209,6 +209,7 @@ static void gemm_dispatch(int fmt, int bn, bool a_mn, bool b_mn, const CUtensorM
 static GemmParams default_params() {
   GemmParams p;
   memset(&p, 0, sizeof(p));
+  p.route_slot = -1;
   p.k_splits = 1;
   p.alpha = 1.f;
   p.a_group_div = 1;
@@ -487,7 +488,7 @@ at::Tensor sht_synth_dft(const at::Tensor& W, int64_t S, int64_t Jr, const at::T
 // Pt_loc: (Mw, L, Jr) — the (weighted) Legendre table restricted to the block.
 void sht_anal_routed(const at::Tensor& N_in, const at::Tensor& Ft, const at::Tensor& Pt_loc, int64_t Lo,
                      int64_t M2_loc, const at::Tensor& ws, const at::Tensor& group_dest, const at::Tensor& out_ptrs,
-                     const c10::optional<at::Tensor>& err) {
+                     const c10::optional<at::Tensor>& err, int64_t slot) {
   TORCH_CHECK(N_in.is_cuda() && N_in.scalar_type() == at::kFloat && N_in.dim() == 3, "N must be fp32 CUDA (S, Jr, I)");
   c10::cuda::CUDAGuard guard(N_in.device());
   at::Tensor N = N_in.contiguous();
@@ -526,6 +527,7 @@ void sht_anal_routed(const at::Tensor& N_in, const at::Tensor& Ft, const at::Ten
     p.a_pair = 1;
     p.c_pair = 1; p.c_ps = M2_loc * Lo; p.c_pmr = Lo; p.c_sc = 1;
     p.route_mode = 2; p.group_map = group_dest.data_ptr<int>(); p.route_rows = static_cast<int>(M2_loc);
+    p.route_slot = slot;  // >= 0: this rank's slot of the owners' buffers (plain stores)
     p.n_peers = static_cast<int>(world);
     for (int i = 0; i < p.n_peers; ++i) p.peer_C[i] = reinterpret_cast<float*>(out_ptrs.data_ptr<int64_t>()[i]);
     p.err = err_ptr(err);
@@ -704,7 +706,7 @@ TORCH_LIBRARY_FRAGMENT(tgcm, m) {
         "Tensor? err) -> ()");
   m.def("sht_synth_dft(Tensor W, int S, int Jr, Tensor F, Tensor? err) -> Tensor");
   m.def("sht_anal_routed(Tensor N, Tensor Ft, Tensor Pt_loc, int Lo, int M2_loc, Tensor ws, Tensor group_dest, "
-        "Tensor out_ptrs, Tensor? err) -> ()");
+        "Tensor out_ptrs, Tensor? err, int slot=-1) -> ()");
   m.def("linear_fwd(Tensor X, Tensor W, Tensor? bias, int act, Tensor(a!) out, Tensor? aux, Tensor? err) -> ()");
   m.def("linear_fwd_gathered(Tensor X, Tensor w_ptrs, int rows, int O, Tensor? bias, int act, Tensor(a!) out, "
         "Tensor? aux, Tensor? err) -> ()");

@@ -83,6 +83,10 @@ struct GemmParams {
   int route_cols;
   int route_rows;    // rows of each destination buffer (entries beyond it: kErrBounds, skipped)
   const int* group_map;
+  // route_mode 2 with route_slot >= 0: plain stores into this rank's slot of the
+  // owner's buffer (element offset route_slot) instead of reductions; the owner
+  // adds the ranks' slots after the barrier.
+  long long route_slot;
 };
 
 __device__ __forceinline__ void st_global_v4(float* addr, float a, float b, float c, float d) {
@@ -871,8 +875,10 @@ __device__ __forceinline__ void gemm_sm100_body(const CUtensorMap& tmap_a, const
         // nothing to write for this tile; fall through to release the accumulator
       } else if (r_dst >= 0) {
         uint8_t* stage = reinterpret_cast<uint8_t*>(staging) + (warp - 2) * (32 * kStageRowF32);
-        epilogue_pair_rows<BN>(p, taddr_row, stage, tm, tn, r_g, q, half, lane, p.peer_C[r_dst], r_shift,
-                               p.route_mode == 2);
+        const bool slot = p.route_mode == 2 && p.route_slot >= 0;
+        epilogue_pair_rows<BN>(p, taddr_row, stage, tm, tn, r_g, q, half, lane,
+                               p.peer_C[r_dst] + (slot ? p.route_slot : 0), r_shift,
+                               p.route_mode == 2 && !slot);
       } else if (red_ok) {
         uint8_t* stage = reinterpret_cast<uint8_t*>(staging) + (warp - 2) * (32 * kStageRowF32);
         epilogue_splitk_red<BN>(p, taddr_row, stage, tm, tn, g, q, half, lane);

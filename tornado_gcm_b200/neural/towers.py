@@ -121,6 +121,12 @@ class Conv2DTower(nn.Module):
         self.activate_final = activate_final
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if x.is_cuda:
+            from tornado_gcm_b200.ops import levelconv
+
+            if levelconv.supports_lonlat(self, x):
+                # lon-lat convolutions as tcgen05 GEMMs on (batch, lon, lat) token rows
+                return levelconv.lonlat_conv_tower(self, x)
         *batch, c, lon, lat = x.shape
         xt = _net_dtype(self, x.reshape(-1, c, lon, lat))
         n = len(self.layers)

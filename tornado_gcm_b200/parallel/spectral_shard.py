@@ -162,6 +162,7 @@ class _Bases:
         self.F = t(fp)                                             # (I, M2p)
         self.Ft = t(f.T)                                           # (M2, I)
         self.group_m = torch.as_tensor(gm, dtype=torch.int32, device=device)
+        self.row_valid = torch.as_tensor((lay.rows[lay.rank] >= 0).astype(np.int32), device=device)
         self.group_dest = torch.as_tensor(lay.group_dest, dtype=torch.int32, device=device)
         # fp64 host-precision copies for the collective engine
         self.p64 = torch.as_tensor(p, dtype=torch.float64, device=device)
@@ -276,6 +277,7 @@ class FusedTransforms:
         self._handles.append(h)
         return t, torch.tensor([int(x) for x in h.buffer_ptrs], dtype=torch.int64)
 
+    # analysis destinations hold one slot per source rank (plain peer stores, summed by the owner)
     def _ensure(self, device, w_numel: int, out_numel: int) -> None:
         if self._pad is None:
             self._pad, self._pad_tab = self._sym(2 * 8, device, torch.int32)
@@ -285,7 +287,7 @@ class FusedTransforms:
             self._w_cap = cap
         if out_numel > self._out_cap:
             cap = max(out_numel, int(self._out_cap * 1.25))
-            self._out = [self._sym(cap, device) for _ in range(2)]
+            self._out = [self._sym(cap * self.lay.world, device) for _ in range(2)]
             self._out_cap = cap
         torch.cuda.synchronize(device)
 
@@ -348,13 +350,12 @@ class FusedTransforms:
         obuf, otab = self._out[k]
         flag = _ext.error_flag(dev)
         ws = _ext.empty(S * lay.M2 * lay.Jr, dtype=torch.float32, device=dev)
+        # this rank's partial sums go into slot `rank` of every owner's buffer (slot stride n)
         ops.sht_anal_routed(n_lat.float().contiguous(), b.Ft, b.Ptw_lat if weighted else b.Pt_lat, lay.Lp,
-                            lay.M2_loc, ws, b.group_dest, otab, flag)
+                            lay.M2_loc, ws, b.group_dest, otab, flag, lay.rank * n)
         self._barrier(dev, flag)
-        view = obuf[:n].view(S, lay.M2_loc, lay.Lp)
-        out = view[..., :lay.L].clone()
-        view.zero_()
-        return out
+        out = ops.slot_sum(obuf, lay.world, S * lay.M2_loc, lay.Lp, lay.L, b.row_valid)
+        return out.view(S, lay.M2_loc, lay.L)
 
 
 # ── autograd ops ────────────────────────────────────────────────────────────
