@@ -39,7 +39,7 @@ REFERENCE_DIFFERENCES = [
     "(+4 forcings) and returns 3n+1 tendencies (no tracers); this framework's column tower maps 6n+1+4 -> 6n+1 "
     "(tracers included), i.e. more tower work per column",
     "transforms: FP64 einsum (the reference selects FP64 above total wavenumber 42) vs TF32 tcgen05 GEMMs (Z1)",
-    "towers: fp32 eager nn.Linear vs BF16 tcgen05 GEMMs (Z3)",
+    "towers: BF16 autocast over eager nn.Linear (the reference trainer's Z3 path) vs BF16 tcgen05 GEMMs (Z3)",
     "fixer: F64ConservationFixer (full FP64 upcast) vs FP64-accumulated packed fixer kernel",
     "batching: the reference modules take one sample at a time, so the arm loops over the 4 samples "
     "(one backward each); this framework runs the batch as one tensor",
@@ -623,6 +623,11 @@ def run_reference(args, rank, world):
     mk = lambda *s: torch.randn(*s, generator=ref.gen)
     pool = [(mk(B, 7 * 37, I, J).pin_memory(), mk(B, K, 7 * 37, I, J).pin_memory()) for _ in range(2)]
 
+    # the reference trainer's own precision handling (training/trainer.py:219-309): the policy's
+    # TF32 setting, and the forward under BF16 autocast when Z3 computes in BF16 (its default)
+    cfg.precision_policy.apply_tf32_setting()
+    autocast_bf16 = cfg.precision_policy.z3_compute_dtype == torch.bfloat16
+
     def step_fn(i, read_loss=False):
         xh, th = pool[i % 2]
         x = xh.to(dev, non_blocking=True)
@@ -630,12 +635,13 @@ def run_reference(args, rank, world):
         opt.zero_grad(set_to_none=True)
         total = torch.zeros((), device=dev)
         for b in range(B):
-            state = encode(x[b])
-            loss = 0.0
-            for k in range(K):
-                for _ in range(cfg.inner_steps):
-                    state = model.step(state, forcings={"f": forc})
-                loss = loss + ((decode(state) - tgt[b, k]) ** 2).mean()
+            with torch.autocast("cuda", dtype=torch.bfloat16, enabled=autocast_bf16):
+                state = encode(x[b])
+                loss = 0.0
+                for k in range(K):
+                    for _ in range(cfg.inner_steps):
+                        state = model.step(state, forcings={"f": forc})
+                    loss = loss + ((decode(state).float() - tgt[b, k]) ** 2).mean()
             (loss / (K * B)).backward()
             total = total + loss.detach() / (K * B)
         if world > 1:
@@ -680,7 +686,8 @@ def run_reference(args, rank, world):
             "unit": "6h model-steps/s (samples x 6-h steps, all GPUs)", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": value / PUBLISHED[args.resolution],
-            "dtype": "fp32 towers and dycore, FP64 transforms (the reference's stock TL63 path), FP64 fixer",
+            "dtype": "bf16 autocast (Z3 towers) + tf32 matmul setting + FP64 transforms (the reference's stock "
+                     "TL63 path) + FP64 fixer",
             "data": "synthetic, random-init weights",
             "config": {"model": "2.8deg TL63 L32 (reference NeuralGCMModel + ModalNeuralDivCurlParameterization "
                                 "tower 5x384, encoder/decoder 3x256, F64ConservationFixer, built from reference "
