@@ -61,3 +61,14 @@ def rng():
 
 def requires_cuda():
     return pytest.mark.skipif(not torch.cuda.is_available(), reason="needs CUDA")
+
+
+@pytest.fixture(autouse=True)
+def _restore_matmul_precision():
+    """Tests that apply a precision policy switch TF32 on process-wide; undo it after each test so that
+    fp32 oracles computed by later tests stay fp32."""
+    saved = (torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32,
+             torch.get_float32_matmul_precision())
+    yield
+    torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32 = saved[:2]
+    torch.set_float32_matmul_precision(saved[2])

@@ -12,6 +12,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <stdexcept>
 #include <unordered_map>
@@ -206,6 +207,27 @@ static void gemm_dispatch(int fmt, int bn, bool a_mn, bool b_mn, const CUtensorM
   throw std::runtime_error("tgcm: no GEMM configuration for fmt=" + std::to_string(fmt) + " bn=" + std::to_string(bn));
 }
 
+// Row-major epilogue of the plain GEMMs: 0 = staged through shared memory,
+// 1 = direct 16-byte row stores for BF16 outputs (default), 2 = direct stores
+// for every output type.  TGCM_GEMM_EPI selects one (for comparisons).
+static int g_epi_mode = -1;
+
+static int epi_direct_mode() {
+  if (g_epi_mode < 0) {
+    const char* e = std::getenv("TGCM_GEMM_EPI");
+    g_epi_mode = (e == nullptr || e[0] < '0' || e[0] > '2') ? 1 : e[0] - '0';
+  }
+  return g_epi_mode;
+}
+
+// Select the row-major epilogue variant for later launches; returns the previous one.
+int64_t gemm_set_epilogue(int64_t mode) {
+  TORCH_CHECK(mode >= 0 && mode <= 2, "epilogue mode must be 0, 1 or 2");
+  const int64_t prev = epi_direct_mode();
+  g_epi_mode = static_cast<int>(mode);
+  return prev;
+}
+
 static GemmParams default_params() {
   GemmParams p;
   memset(&p, 0, sizeof(p));
@@ -214,6 +236,7 @@ static GemmParams default_params() {
   p.alpha = 1.f;
   p.a_group_div = 1;
   p.b_group_div = 1;
+  p.epi_direct = epi_direct_mode();
   return p;
 }
 
@@ -698,6 +721,7 @@ void gemm_profile_buffer(const c10::optional<at::Tensor>& buf, int64_t launch_in
 
 TORCH_LIBRARY_FRAGMENT(tgcm, m) {
   m.def("gemm_profile_buffer(Tensor? buf, int launch_index=-1) -> ()");
+  m.def("gemm_set_epilogue(int mode) -> int");
   m.def("bgemm_tf32(Tensor A, Tensor B, Tensor(a!) C, float alpha, Tensor? err) -> ()");
   m.def("sht_synth(Tensor x, int L, Tensor P, Tensor F, Tensor ws, Tensor? col_scale, Tensor? err, bool lat_major) -> Tensor");
   m.def("sht_anal(Tensor N, Tensor Ft, Tensor Pt, int Lo, Tensor ws, Tensor? col_scale, Tensor? err, bool lat_major, "
@@ -729,4 +753,5 @@ TORCH_LIBRARY_IMPL(tgcm, CUDA, m) {
 
 TORCH_LIBRARY_IMPL(tgcm, CompositeExplicitAutograd, m) {
   m.impl("gemm_profile_buffer", &tgcm::gemm_profile_buffer);
+  m.impl("gemm_set_epilogue", &tgcm::gemm_set_epilogue);
 }

@@ -87,6 +87,8 @@ struct GemmParams {
   // owner's buffer (element offset route_slot) instead of reductions; the owner
   // adds the ranks' slots after the barrier.
   long long route_slot;
+  // row-major epilogue variant (see epilogue_rowmajor_dispatch)
+  int epi_direct;
 };
 
 __device__ __forceinline__ void st_global_v4(float* addr, float a, float b, float c, float d) {
@@ -589,11 +591,156 @@ __device__ __noinline__ void epilogue_pair_rows(const GemmParams& p, uint32_t ta
   }
 }
 
+__device__ __forceinline__ uint32_t u4_word(const uint4& v, int i) {
+  return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
+}
+
+__device__ __forceinline__ void u4_set(uint4& v, int i, uint32_t w) {
+  if (i == 0) v.x = w; else if (i == 1) v.y = w; else if (i == 2) v.z = w; else v.w = w;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// x[j] *= act'(pre[j]) with the chunk's 32 bf16 pre-activations held in registers
+// (word w of pre4 carries columns 2w (low half) and 2w + 1 (high half)).
+__device__ __forceinline__ void act_grad_regs(int act, float (&x)[32], const uint4 (&pre4)[4]) {
+  switch (act) {
+#define TGCM_ACTR_CASE(A)                                                         \
+  case A:                                                                         \
+    _Pragma("unroll") for (int w = 0; w < 16; ++w) {                              \
+      const uint32_t u = u4_word(pre4[w >> 2], w & 3);                            \
+      x[2 * w] *= act_grad_fast<A>(__uint_as_float(u << 16));                     \
+      x[2 * w + 1] *= act_grad_fast<A>(__uint_as_float(u & 0xffff0000u));         \
+    }                                                                             \
+    break;
+    TGCM_ACTR_CASE(kActRelu)
+    TGCM_ACTR_CASE(kActGelu)
+    TGCM_ACTR_CASE(kActGeluTanh)
+    TGCM_ACTR_CASE(kActSilu)
+    TGCM_ACTR_CASE(kActTanh)
+#undef TGCM_ACTR_CASE
+    default: break;
+  }
+}
+
+// Row-major epilogue without a staging tile.  Lane r of the warp owns row r of
+// its 32-row slice: the pre-activations of a chunk (dgrad) and the bias (one
+// value per lane, broadcast by shuffles) are requested before the accumulator
+// is read, so their latency overlaps tcgen05.ld, and the lane's 32 results
+// leave as 16-byte vectors along its own row (four per bf16 chunk, eight per
+// fp32 chunk).  No shared memory and no warp barriers sit on the path; the
+// staged epilogue above trades those for fully covered 128-byte lines.
+template <int BN>
+__device__ __noinline__ void epilogue_rowmajor_direct(const GemmParams& p, int ACT, uint32_t taddr_row, int tm, int tn,
+                                                      int g, int q, int half, int lane) {
+  const int row = tm * 128 + q * 32 + lane;
+  const bool row_ok = row < p.M;
+  const long long rbase = static_cast<long long>(g) * p.c_sg + static_cast<long long>(row) * p.c_sr;
+  const float alpha = p.alpha;
+  const float* bias = p.bias;
+  const __nv_bfloat16* gpre = p.grad_pre;
+  __nv_bfloat16* aux = p.aux;
+  const int out_bf16 = p.out_bf16;
+  const int N = p.N;
+#pragma unroll 1
+  for (int c0 = half * 32; c0 < BN; c0 += 64) {
+    const int ncolc = (BN - c0) >= 32 ? 32 : (BN - c0);
+    const int col0 = tn * BN + c0;
+    int ncols = N - col0;
+    if (ncols > ncolc) ncols = ncolc;
+    const bool full = ncols == 32;
+    uint4 pre4[4];
+    if (gpre != nullptr && row_ok && full) {
+      const uint4* src = reinterpret_cast<const uint4*>(gpre + rbase + col0);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) pre4[i] = __ldg(src + i);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) pre4[i] = make_uint4(0u, 0u, 0u, 0u);
+      if (gpre != nullptr && row_ok) {  // ragged chunk: scalar loads of the valid columns
+        const __nv_bfloat16* src = gpre + rbase + col0;
+#pragma unroll
+        for (int w = 0; w < 16; ++w) {
+          const uint32_t lo = (2 * w < ncols) ? static_cast<uint32_t>(__bfloat16_as_ushort(src[2 * w])) : 0u;
+          const uint32_t hi = (2 * w + 1 < ncols) ? static_cast<uint32_t>(__bfloat16_as_ushort(src[2 * w + 1])) : 0u;
+          u4_set(pre4[w >> 2], w & 3, lo | (hi << 16));
+        }
+      }
+    }
+    const float bl = (bias != nullptr && lane < ncols) ? __ldg(bias + col0 + lane) : 0.f;
+    uint32_t v0[16], v1[16];
+    tmem_ld_32x32b_x16(taddr_row + c0, v0);
+    if (ncolc == 32) tmem_ld_32x32b_x16(taddr_row + c0 + 16, v1);
+    tmem_ld_wait();
+    if (ncols <= 0) continue;
+    float x[32];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) x[j] = __uint_as_float(v0[j]) * alpha;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) x[16 + j] = (ncolc == 32) ? __uint_as_float(v1[j]) * alpha : 0.f;
+    if (bias != nullptr) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) x[j] += __shfl_sync(0xffffffffu, bl, j);
+    }
+    if (aux != nullptr && row_ok) {
+      __nv_bfloat16* ap = aux + rbase + col0;
+      if (full) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          reinterpret_cast<uint4*>(ap)[i] =
+              make_uint4(pack_bf16x2(x[8 * i], x[8 * i + 1]), pack_bf16x2(x[8 * i + 2], x[8 * i + 3]),
+                         pack_bf16x2(x[8 * i + 4], x[8 * i + 5]), pack_bf16x2(x[8 * i + 6], x[8 * i + 7]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < ncols) ap[j] = __float2bfloat16(x[j]);
+      }
+    }
+    if (gpre != nullptr)
+      act_grad_regs(ACT, x, pre4);
+    else
+      act_chunk(ACT, x);
+    if (row_ok && out_bf16) {
+      __nv_bfloat16* cp = reinterpret_cast<__nv_bfloat16*>(p.C) + rbase + col0;
+      if (full) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          reinterpret_cast<uint4*>(cp)[i] =
+              make_uint4(pack_bf16x2(x[8 * i], x[8 * i + 1]), pack_bf16x2(x[8 * i + 2], x[8 * i + 3]),
+                         pack_bf16x2(x[8 * i + 4], x[8 * i + 5]), pack_bf16x2(x[8 * i + 6], x[8 * i + 7]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < ncols) cp[j] = __float2bfloat16(x[j]);
+      }
+    } else if (row_ok) {
+      float* cp = reinterpret_cast<float*>(p.C) + rbase + col0;
+      if (full) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          reinterpret_cast<float4*>(cp)[i] = make_float4(x[4 * i], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < ncols) cp[j] = x[j];
+      }
+    }
+    __syncwarp();  // reconverge before the next chunk's tcgen05.ld
+  }
+}
+
 template <int BN>
 __device__ __forceinline__ void epilogue_rowmajor_dispatch(const GemmParams& p, int act, uint32_t taddr_row,
                                                            uint8_t* stage, int tm, int tn, int g, int q, int half,
                                                            int lane) {
-  epilogue_rowmajor_vec<BN>(p, act, taddr_row, stage, tm, tn, g, q, half, lane);
+  // epi_direct: 1 = direct stores for bf16 outputs, 2 = for every output type
+  if (!p.col_scale && (p.epi_direct >= 2 || (p.epi_direct == 1 && p.out_bf16)))
+    epilogue_rowmajor_direct<BN>(p, act, taddr_row, tm, tn, g, q, half, lane);
+  else
+    epilogue_rowmajor_vec<BN>(p, act, taddr_row, stage, tm, tn, g, q, half, lane);
 }
 
 // Persistent kernel: each CTA walks tiles t = blockIdx.x, +gridDim.x, ….
