@@ -45,14 +45,39 @@ REFERENCE_DIFFERENCES = [
     "(one backward each); this framework runs the batch as one tensor",
     "step capture: eager PyTorch vs one CUDA graph for the whole training step",
 ]
-MY_KERNELS = ("gemm_sm100_kernel", "column_fwd_kernel", "column_vjp_kernel", "implicit_kernel",
-              "sil3_stage_kernel", "spectral_linear_kernel", "fix_partial_kernel", "fix_apply_kernel",
-              "fix_adjoint_kernel", "fused_allreduce", "tgcm_")
+# this framework's kernels live in the tgcm namespace (device-side names "tgcm::…")
+MY_KERNELS = ("tgcm::",)
 
 
 # ── helpers ─────────────────────────────────────────────────────────────────
-def write_kernel_table(prof, path: str) -> None:
-    """Per-kernel count and summed device time of one profiled step, largest first."""
+def measured_peaks() -> dict:
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            d = json.load(fh)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "source": "measured"}
+    except (OSError, KeyError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def step_roofline(acc: dict, ms_per_step: float) -> dict:
+    """Roofline of one training step from the op accounting of an eager step: the
+    algorithmic bytes of every native op at the measured HBM bandwidth against its
+    FLOPs at the measured BF16 rate (TF32 at half of it), and the timed step."""
+    from tornado_gcm_b200.ops import accounting
+
+    pk = measured_peaks()
+    sm = accounting.summary(acc, pk["hbm_gbs"], pk["bf16_tflops"])
+    sm = {k: (round(v, 4) if isinstance(v, float) else v) for k, v in sm.items()}
+    sm["tflop"] = {k: round(v, 4) for k, v in sm["tflop"].items()}
+    sm["peaks"] = pk["source"]
+    sm["frac_of_roofline"] = round(sm["roofline_ms"] / ms_per_step, 4) if ms_per_step > 0 else None
+    return sm
+
+
+def write_kernel_table(prof, path: str, acc: dict | None = None) -> None:
+    """Per-kernel count and summed device time of one profiled step, largest first;
+    with ``acc`` (op accounting of the same step) the per-op traffic table follows."""
     agg: dict = {}
     for ev in prof.events():
         if ev.device_type != torch.autograd.DeviceType.CUDA:
@@ -67,6 +92,17 @@ def write_kernel_table(prof, path: str) -> None:
         fh.write("share%  time_ms  count  kernel\n")
         for name, (c, t) in rows:
             fh.write(f"{100.0 * t / total:6.2f} {t / 1000.0:8.3f} {c:6d}  {name}\n")
+        if acc:
+            from tornado_gcm_b200.ops import accounting
+
+            pk = measured_peaks()
+            sm = accounting.summary(acc, pk["hbm_gbs"], pk["bf16_tflops"])
+            fh.write(f"\n# native-op accounting of the same step ({pk['source']} peaks: "
+                     f"{pk['hbm_gbs']} GB/s, {pk['bf16_tflops']} TFLOP/s BF16)\n")
+            fh.write(f"# total {sm['alg_bytes_gb']:.2f} GB -> {sm['t_hbm_ms']:.1f} ms at HBM; "
+                     f"TFLOP {sm['tflop']} -> {sm['t_flop_ms']:.1f} ms\n")
+            for line in accounting.table_lines(acc, pk["hbm_gbs"]):
+                fh.write(line + "\n")
 
 
 def parse_args():
@@ -319,6 +355,7 @@ def run_b200(args, rank, world):
 
     # count this framework's kernels in one (eager) step, outside the timed region
     launches = None
+    roofline = None
     try:
         from torch.profiler import ProfilerActivity, profile
 
@@ -326,7 +363,9 @@ def run_b200(args, rank, world):
         use_graph = trainer.use_graph
         trainer.use_graph = False
         try:
-            with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            from tornado_gcm_b200.ops import accounting
+
+            with accounting.counting() as acc, profile(activities=[ProfilerActivity.CUDA]) as prof:
                 trainer._zero()
                 trainer._step_body(x0, tg, forc_dev)
                 torch.cuda.synchronize()
@@ -340,8 +379,9 @@ def run_b200(args, rank, world):
                 if any(k in ev.name for k in MY_KERNELS):
                     n_mine += 1
         launches = {"per_step_mine": n_mine, "per_step_all": n_all}
+        roofline = step_roofline(acc, ms_per_step)
         if args.kernel_table and rank == 0:
-            write_kernel_table(prof, args.kernel_table)
+            write_kernel_table(prof, args.kernel_table, acc)
     except Exception as exc:  # pragma: no cover
         launches = {"error": str(exc)}
 
@@ -379,6 +419,7 @@ def run_b200(args, rank, world):
                       "far exceeds the 126 MB L2",
                 "loss": loss_last,
                 "peak_mem_gb": torch.cuda.max_memory_allocated() / 1e9,
+                "roofline": roofline,
             },
             "clocks": clocks,
             "e2e": e2e,

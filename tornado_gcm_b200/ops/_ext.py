@@ -41,6 +41,10 @@ def require(what: str = "kernel"):
         raise RuntimeError(
             f"tornado_gcm_b200 CUDA extension required for {what} but not loaded "
             f"(found {found}; error: {_ERROR}). Build it with `python setup.py build_ext --inplace`.")
+    from tornado_gcm_b200.ops import accounting
+
+    if accounting.active() is not None:
+        return accounting.CountingOps(torch.ops.tgcm)
     return torch.ops.tgcm
 
 
