@@ -208,8 +208,8 @@ static void gemm_dispatch(int fmt, int bn, bool a_mn, bool b_mn, const CUtensorM
 }
 
 // Row-major epilogue of the plain GEMMs: 0 = staged through shared memory,
-// 1 = direct 16-byte row stores for BF16 outputs (default), 2 = direct stores
-// for every output type.  TGCM_GEMM_EPI selects one (for comparisons).
+// 1 = direct 16-byte row stores for the data-gradient GEMMs (default), 2 = direct
+// stores for every output type.  TGCM_GEMM_EPI selects one (for comparisons).
 static int g_epi_mode = -1;
 
 static int epi_direct_mode() {
@@ -220,11 +220,25 @@ static int epi_direct_mode() {
   return g_epi_mode;
 }
 
-// Select the row-major epilogue variant for later launches; returns the previous one.
+// Software pipelining of the row-major epilogues (1, default) or none (0);
+// TGCM_GEMM_EPI_PIPE selects one (for comparisons).
+static int g_epi_pipe = -1;
+
+static int epi_pipe_mode() {
+  if (g_epi_pipe < 0) {
+    const char* e = std::getenv("TGCM_GEMM_EPI_PIPE");
+    g_epi_pipe = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return g_epi_pipe;
+}
+
+// Select the row-major epilogue variant (mode + 4 * pipelined) for later
+// launches; returns the previous setting in the same encoding.
 int64_t gemm_set_epilogue(int64_t mode) {
-  TORCH_CHECK(mode >= 0 && mode <= 2, "epilogue mode must be 0, 1 or 2");
-  const int64_t prev = epi_direct_mode();
-  g_epi_mode = static_cast<int>(mode);
+  TORCH_CHECK(mode >= 0 && mode <= 6 && (mode & 3) <= 2, "epilogue mode must be 0..2, plus 4 for pipelining");
+  const int64_t prev = epi_direct_mode() + 4 * epi_pipe_mode();
+  g_epi_mode = static_cast<int>(mode & 3);
+  g_epi_pipe = static_cast<int>(mode >> 2);
   return prev;
 }
 
@@ -237,6 +251,7 @@ static GemmParams default_params() {
   p.a_group_div = 1;
   p.b_group_div = 1;
   p.epi_direct = epi_direct_mode();
+  p.epi_pipe = epi_pipe_mode();
   return p;
 }
 

@@ -388,29 +388,23 @@ struct PfTerm {
 };
 
 // Blocks per SM: the pipeline keeps three NB x NL register arrays (sums, the
-// current and the next source rows) plus the tail items live; at NB·NL = 8 the
-// 64-register cap of four blocks spilled, so that size runs three.
+// current and the next source rows) live.
 template <int NL, int NB>
 struct PfOcc {
-  static constexpr int value = NB * NL < 8 ? 4 : (NB * NL <= 12 ? 3 : 2);
+  static constexpr int value = NB * NL <= 8 ? 4 : (NB * NL <= 12 ? 3 : 2);
 };
 
-// L = 32·NL + T with a short tail (0 < T, NB·T ≤ 32, e.g. L = 65 at TL63): the
-// tail columns of the NB samples are spread over the lanes as one extra item
-// per lane (sample lane / T, column 32·NL + lane % T) instead of a whole
-// 32-wide chunk per sample that would leave 31 of 32 lanes idle.
 template <int NL, int NB>
-__global__ void __launch_bounds__(32 * kRowWarps, (PfOcc<NL, NB>::value))
-    spectral_linear_rows_pf_kernel(LinearArgs a, int T) {
-  __shared__ float sbuf[kRowWarps][NB][32 * NL + 34];
+__global__ void __launch_bounds__(32 * kRowWarps, (PfOcc<NL, NB>::value)) spectral_linear_rows_pf_kernel(LinearArgs a) {
+  __shared__ float sbuf[kRowWarps][NB][32 * NL + 2];
   __shared__ PfTerm sterm[kPfTerms];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int s = blockIdx.y;
   const int t0 = __ldg(a.row_ptr + s), t1 = __ldg(a.row_ptr + s + 1);
   const int nt = t1 - t0;
   for (int i = threadIdx.x; i < nt && i < kPfTerms; i += blockDim.x) {
-    const int* Tt = a.terms + 7 * (t0 + i);
-    sterm[i] = PfTerm{__ldg(Tt + 1), __ldg(Tt + 2), __ldg(Tt + 3), __ldg(Tt + 4), __ldg(Tt + 5), __ldg(Tt + 6),
+    const int* T = a.terms + 7 * (t0 + i);
+    sterm[i] = PfTerm{__ldg(T + 1), __ldg(T + 2), __ldg(T + 3), __ldg(T + 4), __ldg(T + 5), __ldg(T + 6),
                       __ldg(a.coef + t0 + i)};
   }
   __syncthreads();
@@ -419,14 +413,10 @@ __global__ void __launch_bounds__(32 * kRowWarps, (PfOcc<NL, NB>::value))
   const int b0 = blockIdx.z * NB;
   const int nb = min(NB, a.B - b0);
   const int L = a.L;
-  // tail item of this lane
-  const int tq = T > 0 ? lane / T : NB;
-  const int tl = 32 * NL + (T > 0 ? lane - (lane / T) * T : 0);
-  const bool tv = T > 0 && tq < nb;
   auto term = [&](int i) -> PfTerm {
     if (i < kPfTerms) return sterm[i];
-    const int* Tt = a.terms + 7 * (t0 + i);
-    return PfTerm{__ldg(Tt + 1), __ldg(Tt + 2), __ldg(Tt + 3), __ldg(Tt + 4), __ldg(Tt + 5), __ldg(Tt + 6),
+    const int* T = a.terms + 7 * (t0 + i);
+    return PfTerm{__ldg(T + 1), __ldg(T + 2), __ldg(T + 3), __ldg(T + 4), __ldg(T + 5), __ldg(T + 6),
                   __ldg(a.coef + t0 + i)};
   };
   // source row of a non-vertical term (the paired ±m row for ∂/∂λ); -1: term contributes nothing
@@ -436,7 +426,7 @@ __global__ void __launch_bounds__(32 * kRowWarps, (PfOcc<NL, NB>::value))
     if (m.st == kStDlon) return mr == 0 ? -1 : ((mr & 1) ? mr + 1 : mr - 1);
     return mr;
   };
-  auto issue = [&](int i, float (&xo)[NB][NL], float& xto) {
+  auto issue = [&](int i, float (&xo)[NB][NL]) {
     const PfTerm m = term(i);
     const int srow = source_row(m);
     const float* xr0 = a.x + m.src * a.xs_c + (srow < 0 ? 0 : srow) * a.xs_m;
@@ -447,25 +437,21 @@ __global__ void __launch_bounds__(32 * kRowWarps, (PfOcc<NL, NB>::value))
         const int l = lane + 32 * j;
         xo[q][j] = (srow >= 0 && q < nb && l < L) ? __ldg(xr0 + (b0 + q) * a.xs_b + l) : 0.f;
       }
-    xto = (srow >= 0 && tv) ? __ldg(xr0 + (b0 + tq) * a.xs_b + tl) : 0.f;
   };
   float acc[NB][NL];
 #pragma unroll
   for (int q = 0; q < NB; ++q)
 #pragma unroll
     for (int j = 0; j < NL; ++j) acc[q][j] = 0.f;
-  float acct = 0.f;
   float xn[NB][NL];
-  float xtn = 0.f;
-  if (nt > 0) issue(0, xn, xtn);
+  if (nt > 0) issue(0, xn);
   for (int i = 0; i < nt; ++i) {
     float xv[NB][NL];
 #pragma unroll
     for (int q = 0; q < NB; ++q)
 #pragma unroll
       for (int j = 0; j < NL; ++j) xv[q][j] = xn[q][j];
-    float xt = xtn;
-    if (i + 1 < nt) issue(i + 1, xn, xtn);
+    if (i + 1 < nt) issue(i + 1, xn);
     const PfTerm m = term(i);
     if (term_rejected(a, m.src, m.st, m.pre, m.post, m.mat, m.row)) continue;
     if (m.st == kStVert || m.st == kStVertT) {
@@ -484,13 +470,6 @@ __global__ void __launch_bounds__(32 * kRowWarps, (PfOcc<NL, NB>::value))
           }
         }
       }
-      if (tv) {
-        LinearArgs ab = a;
-        ab.x = a.x + (b0 + tq) * a.xs_b;
-        float v = stencil_val(ab, 0, m.src, m.st, m.pre, mr, tl, m.mat, m.row);
-        if (m.post >= 0) v *= __ldg(a.diag + m.post * L + tl);
-        acct = fmaf(m.cf, v, acct);
-      }
       continue;
     }
     if (source_row(m) < 0) continue;
@@ -508,37 +487,33 @@ __global__ void __launch_bounds__(32 * kRowWarps, (PfOcc<NL, NB>::value))
       for (int q = 0; q < NB; ++q) xv[q][j] *= pd;
       qdiag[j] = (m.post >= 0 && l < L) ? m.cf * __ldg(a.diag + m.post * L + l) : m.cf;
     }
-    float qdt = m.cf;
-    if (tv) {
-      if (m.pre >= 0) xt *= __ldg(a.diag + m.pre * L + tl);
-      if (m.post >= 0) qdt = m.cf * __ldg(a.diag + m.post * L + tl);
-    }
     const bool lat = m.st == kStCdlat || m.st == kStHdlat || m.st == kStCdlatT || m.st == kStHdlatT;
     if (!lat) {
 #pragma unroll
       for (int q = 0; q < NB; ++q)
 #pragma unroll
         for (int j = 0; j < NL; ++j) acc[q][j] = fmaf(qdiag[j] * fac, xv[q][j], acc[q][j]);
-      acct = fmaf(qdt * fac, xt, acct);
       continue;
     }
     __syncwarp();
 #pragma unroll
     for (int q = 0; q < NB; ++q) {
-      float* buf = sbuf[warp][q] + 1;  // buf[l] for l in [-1, L]
+      float* buf = sbuf[warp][q] + 1;  // buf[l] for l in [-1, 32*NL]
 #pragma unroll
       for (int j = 0; j < NL; ++j) buf[lane + 32 * j] = xv[q][j];
       if (lane == 0) {
         buf[-1] = 0.f;
-        buf[L] = 0.f;
+        buf[32 * NL] = 0.f;
       }
     }
-    if (tv) sbuf[warp][tq][1 + tl] = xt;
     __syncwarp();
     const float* ra = a.rec_a + mr * L;
     const float* rb = a.rec_b + mr * L;
-    // coefficients of x[l + 1] (cp) and x[l - 1] (cm) at column l
-    auto lat_coefs = [&](int l, float& cp, float& cm) {
+#pragma unroll
+    for (int j = 0; j < NL; ++j) {
+      const int l = lane + 32 * j;
+      if (l >= L) continue;
+      float cp, cm;
       if (m.st == kStCdlat) {
         cp = (l + 1 < L) ? (l + 2) * __ldg(ra + l + 1) : 0.f;
         cm = (l >= 1) ? -(l - 1) * __ldg(rb + l - 1) : 0.f;
@@ -552,13 +527,6 @@ __global__ void __launch_bounds__(32 * kRowWarps, (PfOcc<NL, NB>::value))
         cm = (l >= 1) ? (l - 1) * __ldg(ra + l) : 0.f;
         cp = (l + 1 < L) ? -(l + 2) * __ldg(rb + l) : 0.f;
       }
-    };
-#pragma unroll
-    for (int j = 0; j < NL; ++j) {
-      const int l = lane + 32 * j;
-      if (l >= L) continue;
-      float cp, cm;
-      lat_coefs(l, cp, cm);
       cp *= qdiag[j];
       cm *= qdiag[j];
 #pragma unroll
@@ -568,14 +536,6 @@ __global__ void __launch_bounds__(32 * kRowWarps, (PfOcc<NL, NB>::value))
         const float xm = (l >= 1) ? buf[l - 1] : 0.f;
         acc[q][j] = fmaf(cp, xp, fmaf(cm, xm, acc[q][j]));
       }
-    }
-    if (tv) {
-      float cp, cm;
-      lat_coefs(tl, cp, cm);
-      const float* buf = sbuf[warp][tq] + 1;
-      const float xp = (tl + 1 < L) ? buf[tl + 1] : 0.f;
-      const float xm = buf[tl - 1];
-      acct = fmaf(cp * qdt, xp, fmaf(cm * qdt, xm, acct));
     }
   }
 #pragma unroll
@@ -590,9 +550,8 @@ __global__ void __launch_bounds__(32 * kRowWarps, (PfOcc<NL, NB>::value))
       else if (l < a.ys_m)
         yrow[l] = 0.f;  // 16-byte row padding
     }
-    for (long long z = (L > 32 * NL ? L : 32 * NL) + lane; z < a.ys_m; z += 32) yrow[z] = 0.f;
+    for (long long z = 32 * NL + lane; z < a.ys_m; z += 32) yrow[z] = 0.f;
   }
-  if (tv) a.y[(b0 + tq) * a.ys_b + s * a.ys_c + mr * a.ys_m + tl] = acct;
 }
 
 // Row-kernel variant: the pipelined kernel up to five 32-wide l chunks (measured
@@ -609,36 +568,24 @@ static bool recipe_pipelined(int nl) {
   return v < 0 ? nl <= 5 : v == 1;
 }
 
-// tail: L - 32·NL tail columns for the pipelined kernel (0: none; needs NB·tail ≤ 32)
 template <int NL, int NB>
-static void launch_rows_nb(const LinearArgs& a, cudaStream_t st, int tail) {
+static void launch_rows_nb(const LinearArgs& a, cudaStream_t st) {
   dim3 grid(static_cast<unsigned>((a.M2 + kRowWarps - 1) / kRowWarps), static_cast<unsigned>(a.C_out),
             static_cast<unsigned>((a.B + NB - 1) / NB));
-  if (tail > 0 || recipe_pipelined(NL))
-    spectral_linear_rows_pf_kernel<NL, NB><<<grid, 32 * kRowWarps, 0, st>>>(a, tail);
+  if (recipe_pipelined(NL))
+    spectral_linear_rows_pf_kernel<NL, NB><<<grid, 32 * kRowWarps, 0, st>>>(a);
   else
     spectral_linear_rows_kernel<NL, NB><<<grid, 32 * kRowWarps, 0, st>>>(a);
 }
 
 template <int NL>
-static void launch_rows(const LinearArgs& a, cudaStream_t st, int tail = 0) {
+static void launch_rows(const LinearArgs& a, cudaStream_t st) {
   if (a.B >= 4 && NL <= 5)
-    launch_rows_nb<NL, 4>(a, st, tail);
+    launch_rows_nb<NL, 4>(a, st);
   else if (a.B >= 2)
-    launch_rows_nb<NL, 2>(a, st, tail);
+    launch_rows_nb<NL, 2>(a, st);
   else
-    launch_rows_nb<NL, 1>(a, st, tail);
-}
-
-// Short-tail rows (L = 32·k + T, 1 ≤ k ≤ 5, 1 ≤ T ≤ 8) run the pipelined kernel with
-// k full chunks and the tail spread over the lanes; TGCM_RECIPE_TAIL=0 turns it off.
-static bool recipe_tail_enabled() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = std::getenv("TGCM_RECIPE_TAIL");
-    v = (e != nullptr && e[0] == '0') ? 0 : 1;
-  }
-  return v == 1;
+    launch_rows_nb<NL, 1>(a, st);
 }
 
 // Bounds-checked mode of the table-driven kernels (debug; off by default).
@@ -690,15 +637,7 @@ at::Tensor spectral_linear(const at::Tensor& x, int64_t L, int64_t C_out, int64_
     TORCH_CHECK(x.stride(1) < (1LL << 31) && x.size(1) * x.stride(1) < (1LL << 31),
                 "spectral_linear: one batch sample must fit 32-bit offsets");
     auto st = at::cuda::getCurrentCUDAStream();
-    const int64_t nlf = L / 32, tail = L % 32;
-    if (recipe_tail_enabled() && tail >= 1 && tail <= 8 && nlf >= 1 && nlf <= 5 && recipe_pipelined(nlf)) {
-      const int t = static_cast<int>(tail);
-      if (nlf == 1) launch_rows<1>(a, st, t);
-      else if (nlf == 2) launch_rows<2>(a, st, t);
-      else if (nlf == 3) launch_rows<3>(a, st, t);
-      else if (nlf == 4) launch_rows<4>(a, st, t);
-      else launch_rows<5>(a, st, t);
-    } else if (L <= 32) launch_rows<1>(a, st);
+    if (L <= 32) launch_rows<1>(a, st);
     else if (L <= 64) launch_rows<2>(a, st);
     else if (L <= 96) launch_rows<3>(a, st);
     else if (L <= 160) launch_rows<5>(a, st);
