@@ -220,25 +220,11 @@ static int epi_direct_mode() {
   return g_epi_mode;
 }
 
-// Software pipelining of the row-major epilogues (1, default) or none (0);
-// TGCM_GEMM_EPI_PIPE selects one (for comparisons).
-static int g_epi_pipe = -1;
-
-static int epi_pipe_mode() {
-  if (g_epi_pipe < 0) {
-    const char* e = std::getenv("TGCM_GEMM_EPI_PIPE");
-    g_epi_pipe = (e != nullptr && e[0] == '0') ? 0 : 1;
-  }
-  return g_epi_pipe;
-}
-
-// Select the row-major epilogue variant (mode + 4 * pipelined) for later
-// launches; returns the previous setting in the same encoding.
+// Select the row-major epilogue variant for later launches; returns the previous one.
 int64_t gemm_set_epilogue(int64_t mode) {
-  TORCH_CHECK(mode >= 0 && mode <= 6 && (mode & 3) <= 2, "epilogue mode must be 0..2, plus 4 for pipelining");
-  const int64_t prev = epi_direct_mode() + 4 * epi_pipe_mode();
-  g_epi_mode = static_cast<int>(mode & 3);
-  g_epi_pipe = static_cast<int>(mode >> 2);
+  TORCH_CHECK(mode >= 0 && mode <= 2, "epilogue mode must be 0, 1 or 2");
+  const int64_t prev = epi_direct_mode();
+  g_epi_mode = static_cast<int>(mode);
   return prev;
 }
 
@@ -251,7 +237,6 @@ static GemmParams default_params() {
   p.a_group_div = 1;
   p.b_group_div = 1;
   p.epi_direct = epi_direct_mode();
-  p.epi_pipe = epi_pipe_mode();
   return p;
 }
 

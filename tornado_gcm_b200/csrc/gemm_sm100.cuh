@@ -87,10 +87,8 @@ struct GemmParams {
   // owner's buffer (element offset route_slot) instead of reductions; the owner
   // adds the ranks' slots after the barrier.
   long long route_slot;
-  // row-major epilogue variant (see epilogue_rowmajor_dispatch) and its
-  // software pipelining (next chunk's tcgen05.ld issued ahead, per-lane bias)
+  // row-major epilogue variant (see epilogue_rowmajor_dispatch)
   int epi_direct;
-  int epi_pipe;
 };
 
 __device__ __forceinline__ void st_global_v4(float* addr, float a, float b, float c, float d) {
@@ -368,50 +366,33 @@ __device__ __forceinline__ void act_grad_chunk(int act, float (&x)[32], const ui
 // rows.  ACT is the forward activation (or, with grad_pre, the activation
 // whose derivative multiplies the result).
 template <int BN>
-__device__ __noinline__ void epilogue_rowmajor_vec(const GemmParams& p, int ACT, uint32_t taddr_row,
+__device__ __forceinline__ void epilogue_rowmajor_vec(const GemmParams& p, int ACT, uint32_t taddr_row,
                                                       uint8_t* stage, int tm, int tn, int g, int q, int half,
                                                       int lane) {
   const int row0 = tm * 128 + q * 32;
   const int nrows = p.M - row0 < 32 ? p.M - row0 : 32;
-  // epi_pipe: the next chunk's tcgen05.ld is in flight while this chunk is
-  // processed, and the bias arrives as one value per lane broadcast by shuffles
-  const bool pipe = p.epi_pipe != 0;
-  uint32_t v0[16], v1[16];
-  if (pipe && half * 32 < BN) {
-    tmem_ld_32x32b_x16(taddr_row + half * 32, v0);
-    if (BN - half * 32 >= 32) tmem_ld_32x32b_x16(taddr_row + half * 32 + 16, v1);
-  }
 #pragma unroll 1
   for (int c0 = half * 32; c0 < BN; c0 += 64) {
     const int ncolc = (BN - c0) >= 32 ? 32 : (BN - c0);
     const int col0 = tn * BN + c0;
     int ncols = p.N - col0;
     if (ncols > ncolc) ncols = ncolc;
-    const float bl = (pipe && p.bias && lane < ncols) ? __ldg(p.bias + col0 + lane) : 0.f;
-    if (!pipe) {
-      tmem_ld_32x32b_x16(taddr_row + c0, v0);
-      if (ncolc == 32) tmem_ld_32x32b_x16(taddr_row + c0 + 16, v1);
-    }
+    uint32_t v0[16], v1[16];
+    tmem_ld_32x32b_x16(taddr_row + c0, v0);
+    if (ncolc == 32) tmem_ld_32x32b_x16(taddr_row + c0 + 16, v1);
     tmem_ld_wait();
+    if (ncols <= 0 || nrows <= 0) continue;
+    const long long base = static_cast<long long>(g) * p.c_sg + static_cast<long long>(row0) * p.c_sr + col0;
     float x[32];
 #pragma unroll
     for (int j = 0; j < 16; ++j) x[j] = __uint_as_float(v0[j]) * p.alpha;
 #pragma unroll
     for (int j = 0; j < 16; ++j) x[16 + j] = (ncolc == 32) ? __uint_as_float(v1[j]) * p.alpha : 0.f;
-    if (pipe && c0 + 64 < BN) {
-      tmem_ld_32x32b_x16(taddr_row + c0 + 64, v0);
-      if (BN - (c0 + 64) >= 32) tmem_ld_32x32b_x16(taddr_row + c0 + 64 + 16, v1);
-    }
-    if (ncols <= 0 || nrows <= 0) continue;
-    const long long base = static_cast<long long>(g) * p.c_sg + static_cast<long long>(row0) * p.c_sr + col0;
     if (p.col_scale) {
 #pragma unroll
       for (int j = 0; j < 32; ++j) x[j] *= (j < ncols) ? __ldg(p.col_scale + col0 + j) : 0.f;
     }
-    if (p.bias && pipe) {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) x[j] += __shfl_sync(0xffffffffu, bl, j);
-    } else if (p.bias) {
+    if (p.bias) {
 #pragma unroll
       for (int j = 0; j < 32; ++j) x[j] += (j < ncols) ? __ldg(p.bias + col0 + j) : 0.f;
     }
@@ -664,12 +645,6 @@ __device__ __noinline__ void epilogue_rowmajor_direct(const GemmParams& p, int A
   __nv_bfloat16* aux = p.aux;
   const int out_bf16 = p.out_bf16;
   const int N = p.N;
-  const bool pipe = p.epi_pipe != 0;
-  uint32_t v0[16], v1[16];
-  if (pipe && half * 32 < BN) {
-    tmem_ld_32x32b_x16(taddr_row + half * 32, v0);
-    if (BN - half * 32 >= 32) tmem_ld_32x32b_x16(taddr_row + half * 32 + 16, v1);
-  }
 #pragma unroll 1
   for (int c0 = half * 32; c0 < BN; c0 += 64) {
     const int ncolc = (BN - c0) >= 32 ? 32 : (BN - c0);
@@ -696,20 +671,15 @@ __device__ __noinline__ void epilogue_rowmajor_direct(const GemmParams& p, int A
       }
     }
     const float bl = (bias != nullptr && lane < ncols) ? __ldg(bias + col0 + lane) : 0.f;
-    if (!pipe) {
-      tmem_ld_32x32b_x16(taddr_row + c0, v0);
-      if (ncolc == 32) tmem_ld_32x32b_x16(taddr_row + c0 + 16, v1);
-    }
+    uint32_t v0[16], v1[16];
+    tmem_ld_32x32b_x16(taddr_row + c0, v0);
+    if (ncolc == 32) tmem_ld_32x32b_x16(taddr_row + c0 + 16, v1);
     tmem_ld_wait();
     float x[32];
 #pragma unroll
     for (int j = 0; j < 16; ++j) x[j] = __uint_as_float(v0[j]) * alpha;
 #pragma unroll
     for (int j = 0; j < 16; ++j) x[16 + j] = (ncolc == 32) ? __uint_as_float(v1[j]) * alpha : 0.f;
-    if (pipe && c0 + 64 < BN) {  // next chunk's accumulator columns in flight during this one
-      tmem_ld_32x32b_x16(taddr_row + c0 + 64, v0);
-      if (BN - (c0 + 64) >= 32) tmem_ld_32x32b_x16(taddr_row + c0 + 64 + 16, v1);
-    }
     if (ncols <= 0) continue;
     if (bias != nullptr) {
 #pragma unroll
@@ -762,7 +732,7 @@ __device__ __noinline__ void epilogue_rowmajor_direct(const GemmParams& p, int A
   }
 }
 
-template <int BN>
+template <int FMT, int BN>
 __device__ __forceinline__ void epilogue_rowmajor_dispatch(const GemmParams& p, int act, uint32_t taddr_row,
                                                            uint8_t* stage, int tm, int tn, int g, int q, int half,
                                                            int lane) {
@@ -770,7 +740,9 @@ __device__ __forceinline__ void epilogue_rowmajor_dispatch(const GemmParams& p, 
   // gradients; measured at T = 32768, 384 x 384: dgrad 0.069 -> 0.055 ms, while
   // the forward with its two outputs stayed at 0.055 ms staged, 0.056 direct),
   // 2 = direct stores for every output type
-  if (!p.col_scale && (p.epi_direct >= 2 || (p.epi_direct == 1 && p.grad_pre != nullptr)))
+  // (BF16 GEMMs with 128-wide tiles only: the TF32 transforms and the 64-wide tiles keep
+  // the staged path and their register budget)
+  if (FMT == 1 && BN >= 128 && !p.col_scale && (p.epi_direct >= 2 || (p.epi_direct == 1 && p.grad_pre != nullptr)))
     epilogue_rowmajor_direct<BN>(p, act, taddr_row, tm, tn, g, q, half, lane);
   else
     epilogue_rowmajor_vec<BN>(p, act, taddr_row, stage, tm, tn, g, q, half, lane);
@@ -1067,7 +1039,7 @@ __device__ __forceinline__ void gemm_sm100_body(const CUtensorMap& tmap_a, const
         epilogue_pair_rows<BN>(p, taddr_row, stage, tm, tn, g, q, half, lane);
       } else if (vec_ok) {
         uint8_t* stage = reinterpret_cast<uint8_t*>(staging) + (warp - 2) * (32 * kStageRowF32);
-        epilogue_rowmajor_dispatch<BN>(p, p.grad_pre ? p.grad_act : p.act, taddr_row, stage, tm, tn, g, q, half,
+        epilogue_rowmajor_dispatch<FMT, BN>(p, p.grad_pre ? p.grad_act : p.act, taddr_row, stage, tm, tn, g, q, half,
                                        lane);
       } else if (!p.c_pair && p.c_sc == 1 && p.c_sr != 1) {
         // Row-major C: stage each 32-row x 32-column block through shared
@@ -1197,7 +1169,7 @@ __device__ __forceinline__ void gemm_sm100_body(const CUtensorMap& tmap_a, const
 }
 
 template <int FMT, int BN, int STAGES, bool A_MN, bool B_MN>
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                       const GemmParams p) {
   gemm_sm100_body<FMT, BN, STAGES, A_MN, B_MN>(tmap_a, &tmap_b, p);
