@@ -20,6 +20,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
 
+#include <type_traits>
 #include <vector>
 
 #ifndef __CUDACC__
@@ -913,12 +914,32 @@ __device__ __forceinline__ void mv_group(const Mat& M, const float (&xo)[P], flo
 // 516 blocks of a launch then run in one wave instead of 1.16 waves of three
 // blocks per SM (80 registers); the latency-bound kernel went from 53.8 to
 // 38.0 ms per training step.
-template <int N>
+//
+// SMI (shared-memory inverse): a block covers kStageLT consecutive l of eight
+// (b, m) rows (warp w: row w, lane group g: l = tile + g), so the per-l
+// inverses of its columns are the kStageLT matrices of one tile, staged once in
+// shared memory (row stride N + 1, matrix stride ≡ 1 mod 32 banks: the 32 lanes
+// of a matvec step hit 32 distinct banks) instead of being read per column
+// from the l-fastest global copy.
+constexpr int kStageLT = 8;
+
+template <bool SMI, bool TR>
+__device__ __forceinline__ typename std::conditional<SMI, SMat<TR>, GMat<TR>>::type stage_minv(
+    const float* smi, int ld, const float* gmi, long long ms, int n) {
+  if constexpr (SMI)
+    return SMat<TR>{smi, ld};
+  else
+    return GMat<TR>{gmi, ms, n};
+}
+
+template <int N, bool SMI>
 __global__ void __launch_bounds__(256, 4) sil3_stage_q4_kernel(StageArgs a, int adjoint) {
   constexpr int Q = 4;
   constexpr int P = N / Q;
   constexpr int LD = N + 1;  // padded row stride of G, H in shared memory (conflict-free)
+  constexpr int MS = N * LD + 1;  // stride of the per-l inverses in the shared tile
   __shared__ float sG[N * LD], sH[N * LD], sTr[N], sDs[N];
+  __shared__ float sMi[SMI ? kStageLT * MS : 1];
   for (int i = threadIdx.x; i < N * N; i += blockDim.x) {
     sG[(i / N) * LD + i % N] = a.G[i];
     sH[(i / N) * LD + i % N] = a.H[i];
@@ -927,21 +948,44 @@ __global__ void __launch_bounds__(256, 4) sil3_stage_q4_kernel(StageArgs a, int 
     sTr[i] = a.tref[i];
     sDs[i] = a.dsig[i];
   }
+  const int n_lt = (a.L + kStageLT - 1) / kStageLT;
+  if constexpr (SMI) {
+    const int l0 = (blockIdx.x % n_lt) * kStageLT;
+    for (int i = threadIdx.x; i < kStageLT * N * N; i += blockDim.x) {
+      const int ll = i % kStageLT, ij = i / kStageLT;
+      const int lg = l0 + ll;
+      sMi[ll * MS + (ij / N) * LD + ij % N] = lg < a.L ? a.MinvT[static_cast<long long>(ij) * a.L + lg] : 0.f;
+    }
+  }
   __syncthreads();
   const int lane = threadIdx.x & 31;
   const int q = lane & (Q - 1);
   const int gl = lane & ~(Q - 1);
-  const int total = a.B * a.M2 * a.L;
-  const int t = blockIdx.x * (blockDim.x / Q) + threadIdx.x / Q;
-  const bool valid = t < total;
-  const int tt = valid ? t : 0;
-  const int bm = tt / a.L;
-  const int l = tt - bm * a.L;
-  const int b = bm / a.M2;
-  const int mr = bm - b * a.M2;
+  bool valid;
+  int b, mr, l;
+  if constexpr (SMI) {
+    const int lloc = lane >> 2;
+    l = (blockIdx.x % n_lt) * kStageLT + lloc;
+    const int bm = (blockIdx.x / n_lt) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    valid = l < a.L && bm < a.B * a.M2;
+    const int bmv = valid ? bm : 0;
+    if (!valid) l = 0;
+    b = bmv / a.M2;
+    mr = bmv - b * a.M2;
+  } else {
+    const int total = a.B * a.M2 * a.L;
+    const int t = blockIdx.x * (blockDim.x / Q) + threadIdx.x / Q;
+    valid = t < total;
+    const int tt = valid ? t : 0;
+    const int bm = tt / a.L;
+    l = tt - bm * a.L;
+    b = bm / a.M2;
+    mr = bm - b * a.M2;
+  }
   const long long cs = static_cast<long long>(a.M2) * a.L;
   const long long base = static_cast<long long>(b) * a.C * cs + static_cast<long long>(mr) * a.L + l;
   const float* mi = a.MinvT + l;
+  const float* smi = sMi + (SMI ? (lane >> 2) * MS : 0);
   const long long ms = a.L;
   const float f = a.filt ? a.filt[l] : 1.f;
   const float lam = a.lam[l];
@@ -957,8 +1001,8 @@ __global__ void __launch_bounds__(256, 4) sil3_stage_q4_kernel(StageArgs a, int 
   const SMat<false> H_{sH, LD};
   const SMat<true> Gt{sG, LD};
   const SMat<true> Ht{sH, LD};
-  const GMat<false> Mi{mi, ms, N};
-  const GMat<true> Mit{mi, ms, N};
+  const auto Mi = stage_minv<SMI, false>(smi, LD, mi, ms, N);
+  const auto Mit = stage_minv<SMI, true>(smi, LD, mi, ms, N);
 
   if (!adjoint) {
     auto finish = [&](float v) -> float {
@@ -1077,12 +1121,31 @@ static const float* ptr_or_null(const c10::optional<at::Tensor>& t) {
   return (t.has_value() && t->defined()) ? t->data_ptr<float>() : nullptr;
 }
 
+// Stage kernel variant: 1 (default) = per-l inverses staged in shared memory per
+// l tile, 0 = read per column from the l-fastest global copy; TGCM_STAGE_SMEM_MINV
+// selects one (for comparisons).
+static bool stage_smem_minv() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("TGCM_STAGE_SMEM_MINV");
+    v = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 static void run_stage(StageArgs& a, const at::Tensor& like, int adjoint) {
   if (like.is_cuda() && a.n == 32 && a.MinvT != nullptr) {
     c10::cuda::CUDAGuard guard(like.device());
-    const long long total = static_cast<long long>(a.B) * a.M2 * a.L;
-    sil3_stage_q4_kernel<32><<<static_cast<unsigned>((total + 63) / 64), 256, 0,
-                               at::cuda::getCurrentCUDAStream()>>>(a, adjoint);
+    if (stage_smem_minv()) {
+      const long long n_lt = (a.L + kStageLT - 1) / kStageLT;
+      const long long n_bm = (static_cast<long long>(a.B) * a.M2 + 7) / 8;
+      sil3_stage_q4_kernel<32, true><<<static_cast<unsigned>(n_lt * n_bm), 256, 0,
+                                       at::cuda::getCurrentCUDAStream()>>>(a, adjoint);
+    } else {
+      const long long total = static_cast<long long>(a.B) * a.M2 * a.L;
+      sil3_stage_q4_kernel<32, false><<<static_cast<unsigned>((total + 63) / 64), 256, 0,
+                                        at::cuda::getCurrentCUDAStream()>>>(a, adjoint);
+    }
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   } else if (like.is_cuda()) {
     c10::cuda::CUDAGuard guard(like.device());
