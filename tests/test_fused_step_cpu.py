@@ -190,3 +190,27 @@ def test_bounds_checked_recipe_skips_out_of_range_terms_on_cpu():
     finally:
         ops.set_bounds_check(False)
     torch.testing.assert_close(y, clean.apply(x), rtol=0, atol=0)
+
+
+def test_pack_of_unpacked_state_is_the_packed_tensor():
+    """Re-packing an unpacked state returns the packed tensor itself (no copy, and backward
+    needs no per-slice zero-fill and additions); a replaced field falls back to concatenation."""
+    import dataclasses
+
+    from tornado_gcm_b200.ops import spectral
+
+    keys = ("a", "b")
+    n = 3
+    y = torch.randn(2, (3 + len(keys)) * n + 1, 5, 4, requires_grad=True)
+    st = spectral.unpack_state(y * 1.0, n, keys, 0.0)
+    assert spectral.pack_state(st, keys) is st._packed_src[0]
+    st2 = spectral.carry_packed(st, dataclasses.replace(st, sim_time=1.0))
+    assert spectral.pack_state(st2, keys) is st._packed_src[0]
+    w = torch.randn_like(y)
+    (g,) = torch.autograd.grad((spectral.pack_state(st2, keys) * w).sum(), y)
+    torch.testing.assert_close(g, w)
+    st3 = dataclasses.replace(st, vorticity=st.vorticity * 2.0)
+    out = spectral.pack_state(st3, keys)
+    assert out is not st._packed_src[0]
+    torch.testing.assert_close(out[:, :n], 2.0 * (y[:, :n] * 1.0))
+    assert spectral.pack_state(st, ("b", "a")) is not st._packed_src[0]

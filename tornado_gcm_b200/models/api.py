@@ -393,7 +393,9 @@ class NeuralGCMModel(nn.Module):
             with record_function("Z2_physics_bridge"):
                 state = self._apply_conservation_fix(state, before)
         if state.sim_time is not None:
-            state = dataclasses.replace(state, sim_time=state.sim_time + self.config.dt)
+            from tornado_gcm_b200.ops.spectral import carry_packed
+
+            state = carry_packed(state, dataclasses.replace(state, sim_time=state.sim_time + self.config.dt))
         if self.monitor is not None:
             self.monitor.step()
         return state

@@ -265,9 +265,36 @@ def explicit_post_recipe(eq, tracer_keys, g_fused: bool = False, grid=None) -> S
     return b.recipe(o_lnps + 1, ch["C"])
 
 
-def pack_state(state, tracer_keys) -> torch.Tensor:
+def _state_parts(state, tracer_keys) -> list:
     parts = [state.vorticity, state.divergence, state.temperature_variation, state.log_surface_pressure]
-    parts += [state.tracers[k] for k in tracer_keys]
+    return parts + [state.tracers[k] for k in tracer_keys]
+
+
+def _views_of(parts: list, packed: torch.Tensor) -> bool:
+    """Every part is still the channel slice of ``packed`` that unpack_state made."""
+    step = packed.stride(-3) * packed.element_size()
+    off = 0
+    for t in parts:
+        if (t.dim() != packed.dim() or t.data_ptr() != packed.data_ptr() + off * step
+                or t.shape[:-3] != packed.shape[:-3] or t.shape[-2:] != packed.shape[-2:]
+                or t.stride() != packed.stride() or t.requires_grad != packed.requires_grad):
+            return False
+        off += t.shape[-3]
+    return off == packed.shape[-3]
+
+
+def pack_state(state, tracer_keys) -> torch.Tensor:
+    """Channels ``[ζ | δ | T' | ln ps | tracers]`` of ``state`` as one tensor.
+
+    A state made by :func:`unpack_state` whose fields are still the slices of
+    that packed tensor returns the tensor itself: re-packing copies nothing in
+    the forward pass, and backward does not rebuild the packed gradient from
+    per-slice zero-filled copies and additions.
+    """
+    parts = _state_parts(state, tracer_keys)
+    src = getattr(state, "_packed_src", None)
+    if src is not None and src[1] == tuple(tracer_keys) and _views_of(parts, src[0]):
+        return src[0]
     return torch.cat(parts, dim=-3)
 
 
@@ -281,7 +308,18 @@ def unpack_state(packed: torch.Tensor, n: int, tracer_keys, sim_time=None, extra
         tr[k] = packed[..., 3 * n + 1 + i * n:3 * n + 1 + (i + 1) * n, :, :]
     if extra_tracers:
         tr.update(extra_tracers)
-    return State(vort, div, temp, lnps, tr, sim_time)
+    st = State(vort, div, temp, lnps, tr, sim_time)
+    if not extra_tracers and packed.shape[-3] == (3 + len(tracer_keys)) * n + 1:
+        st._packed_src = (packed, tuple(tracer_keys))
+    return st
+
+
+def carry_packed(src_state, dst_state):
+    """Keep the packed-tensor link of ``src_state`` on a copy with other metadata (e.g. sim_time)."""
+    link = getattr(src_state, "_packed_src", None)
+    if link is not None:
+        dst_state._packed_src = link
+    return dst_state
 
 
 def param_pre_recipe(grid, n: int, state_keys, param_keys) -> SpectralRecipe:
