@@ -53,6 +53,10 @@ class ResolutionSpec:
     encoder_hidden_layers: int = 3
     # ∇⁴ hyperdiffusion e-folding time at the truncation wavenumber
     hyperdiffusion_hours: float = 12.0
+    # IMEX-SIL3 dycore substeps per physics step (the tower runs once per physics step)
+    dycore_substeps: int = 1
+    # orography smoothing: modal coefficients times exp(-(l / (f·L))^8) (None: unfiltered)
+    orography_filter: Optional[float] = None
 
     @property
     def physics_steps_per_output(self) -> int:
@@ -210,16 +214,23 @@ def build_hybrid_gcm(resolution: str = "2.8deg", device: str | torch.device = "c
     data = SyntheticReanalysis(grid, seed=seed)
     forc = data.forcings(1)
     oro_nd = forc["orography"][0].double() / 6.37122e6
-    oro_modal = grid.clip_wavenumbers(grid.with_precision("highest").to_modal(oro_nd)).float()
+    oro_modal = grid.clip_wavenumbers(grid.with_precision("highest").to_modal(oro_nd))
+    if spec.orography_filter is not None:
+        _, l_tot = grid.modal_mesh
+        L = grid.modal_shape[-1]
+        oro_modal = oro_modal * torch.as_tensor(np.exp(-(np.asarray(l_tot) / (spec.orography_filter * L)) ** 8))
+    oro_modal = oro_modal.float()
 
     dt = minutes_to_nondim(spec.dt_minutes)
     tau_dycore = minutes_to_nondim(120.0)
     tau_stab = minutes_to_nondim(4.0)
     cfg = ModelConfig(
-        coords=coords, dt=dt, inner_steps=spec.physics_steps_per_output, dycore_substeps=1,
+        coords=coords, dt=dt, inner_steps=spec.physics_steps_per_output, dycore_substeps=spec.dycore_substeps,
         physics_specs=units, reference_temperature=t_ref, orography=oro_modal, precision_policy=policy,
-        filter_attenuation=dt / tau_dycore, filter_order=3, filter_cutoff=0.0,
-        stability_filter_attenuation=dt / tau_stab, stability_filter_order=10, stability_filter_cutoff=0.4,
+        # the filters act once per dycore substep: attenuation per substep = substep dt / τ
+        filter_attenuation=dt / spec.dycore_substeps / tau_dycore, filter_order=3, filter_cutoff=0.0,
+        stability_filter_attenuation=dt / spec.dycore_substeps / tau_stab, stability_filter_order=10,
+        stability_filter_cutoff=0.4,
         humidity_key="specific_humidity",
         cloud_keys=("specific_cloud_ice_water_content", "specific_cloud_liquid_water_content"),
         hyperdiffusion_order=2, hyperdiffusion_tau=minutes_to_nondim(spec.hyperdiffusion_hours * 60.0),
