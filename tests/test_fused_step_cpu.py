@@ -214,3 +214,22 @@ def test_pack_of_unpacked_state_is_the_packed_tensor():
     assert out is not st._packed_src[0]
     torch.testing.assert_close(out[:, :n], 2.0 * (y[:, :n] * 1.0))
     assert spectral.pack_state(st, ("b", "a")) is not st._packed_src[0]
+
+
+def test_hyperdiffusion_damps_the_truncation_wavenumber():
+    """The model's hyperdiffusion filter decays every wavenumber (scaling ≤ 1, exp(-dt/τ) at the
+    truncation), and the step-filter helper builds the same damping."""
+    from tornado_gcm_b200.core import time_integration as ti
+    from tornado_gcm_b200.models.builders import build_hybrid_gcm
+
+    gcm, _ = build_hybrid_gcm("5.6deg", "cpu", seed=0)
+    m = gcm.model
+    s = np.asarray(m.hyperdiffusion_filter.scaling)
+    cfg = m.config
+    assert s[0] == 1.0 and np.all(s <= 1.0) and np.all(np.diff(s) <= 0)
+    np.testing.assert_allclose(s[-1], np.exp(-m._inner_dt / cfg.hyperdiffusion_tau), rtol=1e-6)
+    g = cfg.coords.horizontal
+    f = ti.horizontal_diffusion_step_filter(g, m._inner_dt, cfg.hyperdiffusion_tau, cfg.hyperdiffusion_order)
+    x = torch.ones(1, *g.modal_shape, dtype=torch.float64)
+    y = f(x, x)
+    assert float(y.abs().max()) <= 1.0 + 1e-12

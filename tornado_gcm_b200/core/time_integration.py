@@ -240,8 +240,18 @@ def exponential_step_filter(grid, dt: float, tau: float = 0.010938, order: int =
 
 
 def horizontal_diffusion_step_filter(grid, dt: float, tau: float, order: int = 1):
+    """∇^(2·order) diffusion as a step filter: the truncation wavenumber decays by
+    exp(-dt / tau) per step, lower ones by (λ_l / λ_max)^order of that rate.
+
+    ``filtering.horizontal_diffusion_filter`` applies exp(scale · (-λ)^order)
+    (reference ``core/filtering.py:55-78``), so a damping filter takes a negative
+    scale.  Reference ``core/time_integration.py:358-368`` passes +dt / (τ λ_max^order),
+    which grows the truncation wavenumber by exp(dt/τ) per step: with the 0.7°
+    time scales that anti-diffusion made random-init rollouts blow up after
+    about nine simulated hours.
+    """
     eig = grid.laplacian_eigenvalues
-    scale = dt / (tau * abs(eig[-1]) ** order)
+    scale = -dt / (tau * abs(eig[-1]) ** order)
     filt = filtering.horizontal_diffusion_filter(grid, scale, order)
     return runge_kutta_step_filter(lambda s: tree_map(filt, s))
 

@@ -146,7 +146,10 @@ class NeuralGCMModel(nn.Module):
             self._inner_dt = config.dt / config.dycore_substeps
             if config.hyperdiffusion_order is not None and config.hyperdiffusion_tau is not None:
                 eig = grid.laplacian_eigenvalues
-                scale = self._inner_dt / (config.hyperdiffusion_tau * abs(eig[-1]) ** config.hyperdiffusion_order)
+                # negative: filtering.horizontal_diffusion_filter applies exp(scale · (-λ)^order), so
+                # this damps the truncation wavenumber by exp(-dt / τ) per step (see
+                # core.time_integration.horizontal_diffusion_step_filter for the reference's sign)
+                scale = -self._inner_dt / (config.hyperdiffusion_tau * abs(eig[-1]) ** config.hyperdiffusion_order)
                 self.hyperdiffusion_filter = filtering.horizontal_diffusion_filter(
                     grid, scale, config.hyperdiffusion_order)
         self.use_fused_dycore = True

@@ -66,7 +66,7 @@ class ResolutionSpec:
 RESOLUTIONS = {
     "2.8deg": ResolutionSpec("2.8deg", "TL63", 20.0, 384),
     "1.4deg": ResolutionSpec("1.4deg", "TL127", 10.0, 512),
-    # TL255: a 3-h hyperdiffusion time scale damps the near-truncation growth of random-init rollouts
+    # TL255: a 3-h hyperdiffusion time scale at the truncation wavenumber
     "0.7deg": ResolutionSpec("0.7deg", "TL255", 5.0, 768, hyperdiffusion_hours=3.0),
     # small configuration for tests and CPU demonstrations: T21 (64 x 32 grid), 8 levels, dt 2 h
     "5.6deg": ResolutionSpec("5.6deg", "T21", 120.0, 32, tower_hidden_layers=2, layers=8, encoder_width=32,
