@@ -5,7 +5,12 @@ profile plus noise band-limited to total wavenumber ≤ 21 (generated in
 spectral space and synthesised on the grid):
 
 * T: 200–300 K profile, noise σ = 5 K;  u, v: 10 m/s rms, mostly rotational
-  (divergence 10 % of vorticity in spectral amplitude);
+  (divergence 10 % of vorticity in spectral amplitude);  the T, z and wind
+  anomalies are vertically coherent (one horizontal pattern per sample, wind
+  amplitude growing with height), so columns keep the statically stable mean
+  lapse rate and a Richardson number far above 1/4 — independent noise per
+  level made ~18 % of adjacent level pairs convectively unstable, which a
+  dry dynamical core amplifies at the grid scale;
 * q: lognormal in (0, 0.02] kg/kg;  z: hydrostatic 0–4.8e5 m²/s²;
 * cloud liquid / ice: lognormal ≤ 1e-4;
 * forcings: SST 271–305 K, sea ice U[0, 1], orography 0–5 km rising from
@@ -79,6 +84,9 @@ class SyntheticReanalysis:
     levels: np.ndarray = dataclasses.field(default_factory=lambda: PRESSURE_LEVELS_37.copy())
     lmax: int = 21
     seed: int = 0
+    # one horizontal anomaly pattern for every level of T, z and the winds
+    # (False: an independent pattern per level, statically unstable columns)
+    coherent: bool = True
 
     def _profiles(self):
         p = self.levels / 1000.0
@@ -95,13 +103,23 @@ class SyntheticReanalysis:
         t_mean, q_mean, z_mean, cl_mean, ci_mean = self._profiles()
         noise = lambda: band_limited_noise(self.grid, nl, self.lmax, rng, batch)
         sh = (1, nl, 1, 1)
-        u, v = rotational_winds(self.grid, nl, self.lmax, rng, batch, speed=10.0, divergent_fraction=0.1)
+        if self.coherent:
+            shared = lambda: np.broadcast_to(band_limited_noise(self.grid, 1, self.lmax, rng, batch),
+                                             (batch, nl) + self.grid.nodal_shape)
+            u1, v1 = rotational_winds(self.grid, 1, self.lmax, rng, batch, speed=10.0, divergent_fraction=0.1)
+            # wind anomaly amplitude from 0.6 (1000 hPa) to 1.4 (top), mean ≈ 1
+            prof = (0.6 + 0.8 * (1.0 - self.levels / 1000.0)).reshape(sh)
+            u, v = u1 * prof, v1 * prof
+            t_noise, z_noise = shared(), shared()
+        else:
+            u, v = rotational_winds(self.grid, nl, self.lmax, rng, batch, speed=10.0, divergent_fraction=0.1)
+            t_noise, z_noise = noise(), noise()
         out = {
             "u": u,
             "v": v,
-            "t": np.clip(t_mean.reshape(sh) + 5.0 * noise(), 180.0, 320.0),
+            "t": np.clip(t_mean.reshape(sh) + 5.0 * t_noise, 180.0, 320.0),
             "q": np.minimum(q_mean.reshape(sh) * np.exp(0.3 * noise()), 0.02),
-            "z": z_mean.reshape(sh) + 2.0e3 * noise(),
+            "z": z_mean.reshape(sh) + 2.0e3 * z_noise,
             "clwc": np.minimum(cl_mean.reshape(sh) * np.exp(0.5 * noise()), 1e-4),
             "ciwc": np.minimum(ci_mean.reshape(sh) * np.exp(0.5 * noise()), 1e-4),
         }
