@@ -198,6 +198,19 @@ def _worker_fsdp(rank, world, port, q):
                     s = gcm.model.step(s, f)
                 outs.append(gcm.decoder(s, f))
         err = max(_rel(outs[1][k], outs[0][k]) for k in outs[0])
+        # sharded save of the tower: each rank's rows only; the all-gather restores the weights
+        from tornado_gcm_b200.parallel.fsdp_gather import local_state_dict
+        from tornado_gcm_b200.training import sharded_checkpoint as sc
+
+        par = gcm.model.parameterization
+        names = [f"layers.{i}" for i in range(len(par._fsdp_layers))]
+        local, meta = local_state_dict(par._fsdp_layers, names)
+        full = sc.all_gather_state_dict({k: v.to(dev) for k, v in local.items()}, meta)
+        ref = par.tower.neural_net.state_dict()
+        # weights live as BF16 shards, biases in fp32
+        err_ckpt = max(_rel(full[k].float(), (ref[k].to(torch.bfloat16) if k.endswith("weight") else ref[k])
+                            .float().to(dev)) for k in full)
+        err = max(err, err_ckpt)
         torch.cuda.synchronize(dev)
         q.put((rank, err, _ext.check_error_flag(dev)))
         dist.barrier()

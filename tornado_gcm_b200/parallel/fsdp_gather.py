@@ -56,6 +56,7 @@ class GatheredLinear:
             raise ValueError("at most 8 shards")
         dev = weight.device
         self.out_features, K = weight.shape
+        self.in_features = K
         if pad_out and self.out_features % 8:
             weight = torch.cat([weight, weight.new_zeros(_pad8(self.out_features) - self.out_features, K)], 0)
             if bias is not None:
@@ -82,6 +83,12 @@ class GatheredLinear:
 
     def local_weight(self) -> torch.Tensor:
         return self.shard.view(self.rows, self.Kp)
+
+    def local_rows(self) -> torch.Tensor:
+        """This rank's rows of the (out_features, in_features) weight, without padding."""
+        r0 = min(self.rank * self.rows, self.out_features)
+        r1 = min(self.out_features, r0 + self.rows)
+        return self.local_weight()[: r1 - r0, : self.in_features]
 
     def __call__(self, x: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
         ops = _ext.require("fused all-gather linear")
@@ -114,6 +121,24 @@ def shard_mlp(mlp, act: Optional[str] = None, group=None, pad_out: bool = True) 
     acts = mlp.layer_activations() if act is None else [act] * (len(layers) - 1) + ["none"]
     return [GatheredLinear(l.weight.detach(), l.bias.detach() if l.bias is not None else None,
                            acts[i] or "none", group, pad_out=pad_out) for i, l in enumerate(layers)]
+
+
+def local_state_dict(layers: list, names: list, dtype: torch.dtype = torch.float32) -> tuple:
+    """(this rank's weight rows, metadata) of sharded layers under their module names
+    ``names[i] + ".weight"``, in the format of ``training/sharded_checkpoint`` (biases stay
+    whole, on rank 0): a sharded tower is saved without any rank holding its full weights."""
+    local, meta = {}, {}
+    for lin, name in zip(layers, names):
+        key = name + ".weight"
+        local[key] = lin.local_rows().to(dtype).cpu()
+        meta[key] = {"sharded": True, "shape": [lin.out_features, lin.in_features],
+                     "dtype": str(dtype).replace("torch.", ""), "rows": lin.rows}
+        if lin.bias is not None:
+            bkey = name + ".bias"
+            if lin.rank == 0:
+                local[bkey] = lin.bias[: lin.out_features].to(dtype).cpu()
+            meta[bkey] = {"sharded": False, "shape": [lin.out_features], "dtype": str(dtype).replace("torch.", "")}
+    return local, meta
 
 
 def gathered_mlp_forward(layers: list, x: torch.Tensor) -> torch.Tensor:
