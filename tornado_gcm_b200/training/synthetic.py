@@ -13,8 +13,8 @@ spectral space and synthesised on the grid):
   dry dynamical core amplifies at the grid scale;
 * q: lognormal in (0, 0.02] kg/kg;  z: hydrostatic 0–4.8e5 m²/s²;
 * cloud liquid / ice: lognormal ≤ 1e-4;
-* forcings: SST 271–305 K, sea ice U[0, 1], orography 0–5 km rising from
-  0 at the coast of the binary land mask.
+* forcings: SST 271–305 K, sea ice U[0, 1], orography 0–3.5 km rising
+  smoothly from the coast of the binary land mask.
 
 Everything is deterministic given the seed.  Fields are returned in
 physical units on ``(..., levels, lon, lat)`` nodal grids, plus
@@ -132,8 +132,14 @@ class SyntheticReanalysis:
         sst = 271.0 + 34.0 * np.cos(lat)[None, None, :] ** 2 + 0.0 * n1()
         ice = np.clip(0.5 + 0.5 * n1(), 0.0, 1.0)
         relief = n1()
-        # continents where the relief field exceeds 0.3; height grows from 0 at the coast, ≤ 5 km
-        oro = np.clip(2.5e3 * (relief - 0.3), 0.0, 5.0e3)
+        # continents where the relief field exceeds 0.3.  Height rises smoothly from the coast
+        # (softplus ramp of width 0.2) and saturates smoothly below 3.5 km: a clipped linear ramp
+        # (0 at the coast, flat-topped at 5 km) put 1-1.5 km steps between neighbouring grid
+        # points at 1.4°, and the dry core's sigma-coordinate flow over those kinks drove
+        # near-surface temperatures away without bound after ~100 physics steps
+        x = (relief - 0.3) / 0.2
+        ramp = 0.2 * np.logaddexp(0.0, x)
+        oro = 3.5e3 * np.tanh(1.2e3 * ramp / 3.5e3)
         land = (relief > 0.3).astype(np.float64)
         f = {"sea_surface_temperature": sst, "sea_ice_cover": ice, "orography": oro, "land_sea_mask": land}
         return {k: torch.as_tensor(np.broadcast_to(v, (batch,) + self.grid.nodal_shape).copy(), dtype=torch.float32)
