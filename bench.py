@@ -125,10 +125,12 @@ def parse_args():
     p.add_argument("--checkpoint-segment", type=int, default=-1,
                    help="physics steps per recomputed segment (0: whole 6-h block; default 8 at 0.7 degrees)")
     p.add_argument("--batch", type=int, default=4, help="per-GPU batch")
-    p.add_argument("--parallel", choices=["dp", "lat"], default="dp",
+    p.add_argument("--parallel", choices=["dp", "lat", "sharded"], default="dp",
                    help="train: dp = data parallel (replicated model, batch per GPU); lat = the model sharded "
                         "over the GPUs (modal rows by zonal wavenumber, nodal columns by latitude block), all "
-                        "GPUs on one global batch of batch x GPUs samples")
+                        "GPUs on one global batch of batch x GPUs samples; sharded = data parallel with the "
+                        "gradients and AdamW state split over the GPUs (reduce-scatter, sharded AdamW, "
+                        "all-gather of the weights)")
     p.add_argument("--rollout", type=int, default=4, help="6-h steps per training example")
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
@@ -287,7 +289,8 @@ def run_b200(args, rank, world):
 
         ss.shard_hybrid_gcm(gcm, None, "fused")
         shard = gcm.shard
-    trainer = GCMTrainer(gcm, lr=1e-4, graph=not args.no_graph, data_parallel=world > 1, grad_average=not lat)
+    dp_mode = "sharded" if (args.parallel == "sharded" and world > 1) else world > 1
+    trainer = GCMTrainer(gcm, lr=1e-4, graph=not args.no_graph, data_parallel=dp_mode, grad_average=not lat)
     # lat: every rank holds 1/W of each of the batch x W samples (same per-GPU work as dp)
     B, K = (args.batch * world if lat else args.batch), args.rollout
     enc = gcm.encoder
@@ -408,9 +411,10 @@ def run_b200(args, rank, world):
                 "seq_len": K,
                 "seq_len_meaning": "6-h rollout steps per example (backprop through the whole rollout)",
                 "parallelism": (f"lat{world} (modal rows by zonal wavenumber, nodal columns by latitude block; "
-                                f"transposes fused into the Legendre GEMMs)") if lat else f"dp{world}",
+                                f"transposes fused into the Legendre GEMMs)") if lat else (
+                    f"dp{world} (gradients and AdamW state sharded)" if args.parallel == "sharded" else f"dp{world}"),
                 "zones": "Z1 TF32 tcgen05 transforms, Z3 BF16 tcgen05 towers, Z2 FP64-accumulated fixer",
-                "grad_reducer": trainer.dp.backend if trainer.dp is not None else "none (one rank)",
+                "grad_reducer": trainer.grad_reducer,
                 "cuda_graph": trainer.use_graph,
                 "activation_checkpointing": ("none" if not gcm.checkpoint_outer_steps else
                                              f"segments of {gcm.checkpoint_segment} physics steps"

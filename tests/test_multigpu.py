@@ -217,3 +217,102 @@ def test_gathered_linear_two_gpus():
         assert res["rel_384"] < 1e-2 and res["rel_193"] < 1e-2
         assert res["base_384"] < 1e-3 and res["base_193"] < 1e-3
         assert res["flag"] == 0
+
+
+def _worker_sharded_optim(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=torch.device("cuda", rank))
+        from tornado_gcm_b200.ops import _ext
+        from tornado_gcm_b200.parallel.sharded_optim import _FusedChunkComm
+        from tornado_gcm_b200.training.trainer import GCMTrainer
+
+        dev = torch.device("cuda", rank)
+        res = {}
+        n = 4 * world * 100003
+        comm = _FusedChunkComm(n, dev, dist.group.WORLD)
+        c = n // world
+        for it in range(2):  # two calls: the epochs advance
+            gen = torch.Generator(device=dev).manual_seed(10 * it + rank)
+            x = torch.randn(n, device=dev, generator=gen)
+            ref = x.clone()
+            dist.all_reduce(ref)
+            comm.G.copy_(x)
+            comm.reduce_scatter_mean()
+            own = slice(rank * c, (rank + 1) * c)
+            res[f"rs{it}"] = float((comm.G[own] - ref[own] / world).abs().max())
+            rest = torch.ones(n, dtype=torch.bool, device=dev)
+            rest[own] = False
+            res[f"rs_rest{it}"] = float((comm.G[rest] - x[rest]).abs().max())
+            y = torch.randn(n, device=dev, generator=gen)
+            ys = [torch.empty_like(y) for _ in range(world)]
+            dist.all_gather(ys, y)
+            expect = torch.cat([ys[p][p * c:(p + 1) * c] for p in range(world)])
+            comm.P.copy_(y)
+            comm.all_gather_params()
+            res[f"ag{it}"] = float((comm.P - expect).abs().max())
+        # trainer: sharded against replicated data parallelism
+        torch.manual_seed(0)
+        mods = [torch.nn.Sequential(torch.nn.Linear(33, 64), torch.nn.GELU(), torch.nn.Linear(64, 17)).to(dev)
+                for _ in range(2)]
+        mods[1].load_state_dict(mods[0].state_dict())
+
+        class _M(torch.nn.Module):
+            def __init__(self, net):
+                super().__init__()
+                self.net = net
+
+            def loss(self, data0, targets, forcings):
+                return ((self.net(data0["x"]) - targets[0]["y"]) ** 2).mean()
+
+        # both captured: the capture's warm-up steps are the same on both trainers
+        t_rep = GCMTrainer(_M(mods[0]), lr=1e-3, max_grad_norm=0.5, data_parallel=True, graph=True)
+        t_sh = GCMTrainer(_M(mods[1]), lr=1e-3, max_grad_norm=0.5, data_parallel="sharded", graph=True)
+        errs = []
+        for step in range(5):
+            g = torch.Generator().manual_seed(100 * step + rank)
+            b = ({"x": torch.randn(256, 33, generator=g).pin_memory()},
+                 [{"y": torch.randn(256, 17, generator=g).pin_memory()}], {})
+            t_rep.train_step(b[0], b[1], b[2])
+            t_sh.train_step(b[0], b[1], b[2])
+            torch.cuda.synchronize(dev)
+            errs.append(max(float((p - s).abs().max()) for p, s in zip(mods[0].parameters(), mods[1].parameters())))
+        res["trainer"] = max(errs)
+        res["backend"] = t_sh.grad_reducer
+        t_sh.release_graph()
+        t_rep.release_graph()
+        torch.cuda.synchronize(dev)
+        res["flag"] = _ext.check_error_flag(dev)
+        dist.barrier()
+        del comm, t_sh, t_rep
+        dist.destroy_process_group()
+        q.put((rank, res))
+    except Exception:  # pragma: no cover
+        q.put((rank, traceback.format_exc()))
+
+
+def test_sharded_optimizer_collectives_two_gpus():
+    """Fused reduce-scatter / all-gather kernels against NCCL, and the sharded trainer against DP."""
+    import torch.multiprocessing as mp
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker_sharded_optim, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+    for rank, res in out:
+        assert isinstance(res, dict), res
+        for it in range(2):
+            assert res[f"rs{it}"] < 1e-5 and res[f"rs_rest{it}"] == 0.0 and res[f"ag{it}"] == 0.0
+        assert res["trainer"] < 1e-5
+        assert "fused NVLink" in res["backend"]
+        assert res["flag"] == 0

@@ -130,6 +130,70 @@ __global__ void __launch_bounds__(kArThreads) fused_allreduce_kernel(ArArgs a) {
   ar_barrier(a, 1, epoch);
 }
 
+// The two halves of the sharded-optimizer step (gradients and AdamW state
+// split over the ranks by flat chunk; chunk r of the flat buffers belongs to
+// rank r, the buffers hold a multiple of 4 * world elements):
+//
+//   fused_reduce_scatter_kernel  barrier on pad phase 0, then rank r sums
+//       chunk r of every peer's gradient buffer (16-byte peer loads), scales
+//       it and stores it into its OWN buffer only; nothing is pushed.
+//   fused_all_gather_kernel      barrier on pad phase 1 (every rank's
+//       optimizer has updated its chunk of the parameters), then rank r pulls
+//       chunk p of the parameters from every peer p into its own buffer.
+//
+// Neither needs a closing barrier: a peer overwrites its gradient buffer only
+// when it zeroes it for the next step, which follows its own all-gather and
+// therefore our arrival at phase 1; it overwrites its parameter chunk only in
+// its next optimizer step, which follows its next reduce-scatter and
+// therefore our arrival at the next phase 0.  Each kernel keeps its own
+// epoch on its own phase of the pad.
+__device__ __forceinline__ void chunk_block_range(const ArArgs& a, int owner, long long& b0, long long& b1) {
+  const long long chunk = a.n / a.world;
+  const long long c0 = static_cast<long long>(owner) * chunk;
+  const long long per = ((chunk + a.blocks - 1) / a.blocks + 3) / 4 * 4;
+  b0 = c0 + per * blockIdx.x;
+  b1 = b0 + per;
+  if (b1 > c0 + chunk) b1 = c0 + chunk;
+}
+
+__global__ void __launch_bounds__(kArThreads) fused_reduce_scatter_kernel(ArArgs a) {
+  __shared__ uint32_t s_epoch;
+  if (threadIdx.x == 0)
+    s_epoch = *(volatile uint32_t*)(a.pads[a.rank] + (0 * kArMaxRanks + a.rank) * a.blocks + blockIdx.x) + 1u;
+  __syncthreads();
+  if (!ar_barrier(a, 0, s_epoch)) return;
+  long long b0, b1;
+  chunk_block_range(a, a.rank, b0, b1);
+  float* dst = a.bufs[a.rank];
+  for (long long e = b0 + 4 * threadIdx.x; e < b1; e += 4 * blockDim.x) {
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int q = 0; q < a.world; ++q) {
+      const int p = (a.rank + q) % a.world;  // staggered: ranks start on different peers
+      const float4 v = __ldcv(reinterpret_cast<const float4*>(a.bufs[p] + e));
+      s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+    }
+    s.x *= a.scale; s.y *= a.scale; s.z *= a.scale; s.w *= a.scale;
+    *reinterpret_cast<float4*>(dst + e) = s;
+  }
+}
+
+__global__ void __launch_bounds__(kArThreads) fused_all_gather_kernel(ArArgs a) {
+  __shared__ uint32_t s_epoch;
+  if (threadIdx.x == 0)
+    s_epoch = *(volatile uint32_t*)(a.pads[a.rank] + (1 * kArMaxRanks + a.rank) * a.blocks + blockIdx.x) + 1u;
+  __syncthreads();
+  if (!ar_barrier(a, 1, s_epoch)) return;
+  float* dst = a.bufs[a.rank];
+  for (int q = 1; q < a.world; ++q) {
+    const int p = (a.rank + q) % a.world;
+    long long b0, b1;
+    chunk_block_range(a, p, b0, b1);
+    const float* src = a.bufs[p];
+    for (long long e = b0 + 4 * threadIdx.x; e < b1; e += 4 * blockDim.x)
+      *reinterpret_cast<float4*>(dst + e) = __ldcv(reinterpret_cast<const float4*>(src + e));
+  }
+}
+
 // Stand-alone cross-rank barrier on a signal pad (one block): every rank
 // announces the next epoch in every peer's pad and waits (bounded) for all
 // peers' announcements.  Orders the peer reductions of a preceding kernel
@@ -187,6 +251,58 @@ void fused_allreduce_mean(at::Tensor& buf, const at::Tensor& buf_ptrs, const at:
   a.scale = scale == 0.0 ? 1.f / static_cast<float>(world) : static_cast<float>(scale);
   a.err = (err.has_value() && err->defined()) ? err->data_ptr<int>() : nullptr;
   fused_allreduce_kernel<<<static_cast<unsigned>(blocks), kArThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+static ArArgs chunked_args(const at::Tensor& buf, const at::Tensor& buf_ptrs, const at::Tensor& pad_ptrs,
+                           int64_t rank, int64_t blocks, const c10::optional<at::Tensor>& err, const char* what) {
+  TORCH_CHECK(buf.is_cuda() && buf.scalar_type() == at::kFloat && buf.is_contiguous(), what,
+              ": fp32 CUDA buffer expected");
+  TORCH_CHECK(buf_ptrs.scalar_type() == at::kLong && pad_ptrs.scalar_type() == at::kLong && !buf_ptrs.is_cuda() &&
+                  !pad_ptrs.is_cuda(),
+              what, ": pointer tables must be int64 CPU tensors");
+  const int64_t world = buf_ptrs.numel();
+  TORCH_CHECK(world >= 1 && world <= kArMaxRanks && pad_ptrs.numel() == world && rank >= 0 && rank < world, what,
+              ": 1..8 ranks supported");
+  TORCH_CHECK(blocks >= 1 && blocks <= 1024, what, ": blocks out of range");
+  TORCH_CHECK(buf.numel() % (4 * world) == 0, what, ": the buffer must hold a multiple of 4 * world elements");
+  ArArgs a;
+  memset(&a, 0, sizeof(a));
+  for (int64_t p = 0; p < world; ++p) {
+    a.bufs[p] = reinterpret_cast<float*>(buf_ptrs.data_ptr<int64_t>()[p]);
+    a.pads[p] = reinterpret_cast<uint32_t*>(pad_ptrs.data_ptr<int64_t>()[p]);
+  }
+  TORCH_CHECK(a.bufs[rank] == buf.data_ptr<float>(), what, ": buffer is not this rank's symmetric allocation");
+  for (int64_t p = 0; p < world; ++p)
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(a.bufs[p]) % 16 == 0, what, ": peer buffers must be 16-byte aligned");
+  a.n = buf.numel();
+  a.world = static_cast<int>(world);
+  a.rank = static_cast<int>(rank);
+  a.blocks = static_cast<int>(blocks);
+  a.err = (err.has_value() && err->defined()) ? err->data_ptr<int>() : nullptr;
+  return a;
+}
+
+// In place: chunk `rank` of this rank's buffer becomes scale * (sum over the
+// ranks of their chunk `rank`); the other chunks are left as they are.
+// scale 0 selects 1/world.  pad_ptrs: signal pads of >= 2 * 8 * blocks words.
+void fused_reduce_scatter(at::Tensor& buf, const at::Tensor& buf_ptrs, const at::Tensor& pad_ptrs, int64_t rank,
+                          int64_t blocks, const c10::optional<at::Tensor>& err, double scale) {
+  ArArgs a = chunked_args(buf, buf_ptrs, pad_ptrs, rank, blocks, err, "fused_reduce_scatter");
+  a.scale = scale == 0.0 ? 1.f / static_cast<float>(a.world) : static_cast<float>(scale);
+  c10::cuda::CUDAGuard guard(buf.device());
+  fused_reduce_scatter_kernel<<<static_cast<unsigned>(blocks), kArThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// In place: chunk p of this rank's buffer is replaced by chunk p of rank p's
+// buffer, for every p != rank.
+void fused_all_gather(at::Tensor& buf, const at::Tensor& buf_ptrs, const at::Tensor& pad_ptrs, int64_t rank,
+                      int64_t blocks, const c10::optional<at::Tensor>& err) {
+  ArArgs a = chunked_args(buf, buf_ptrs, pad_ptrs, rank, blocks, err, "fused_all_gather");
+  a.scale = 1.f;
+  c10::cuda::CUDAGuard guard(buf.device());
+  fused_all_gather_kernel<<<static_cast<unsigned>(blocks), kArThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -248,10 +364,14 @@ at::Tensor slot_sum(const at::Tensor& slots, int64_t W, int64_t rows, int64_t ld
 TORCH_LIBRARY_FRAGMENT(tgcm, m) {
   m.def("slot_sum(Tensor slots, int W, int rows, int ld, int L, Tensor? valid=None) -> Tensor");
   m.def("fused_allreduce_mean(Tensor(a!) buf, Tensor buf_ptrs, Tensor pad_ptrs, int rank, int blocks, Tensor? err, float scale=0.0) -> ()");
+  m.def("fused_reduce_scatter(Tensor(a!) buf, Tensor buf_ptrs, Tensor pad_ptrs, int rank, int blocks, Tensor? err, float scale=0.0) -> ()");
+  m.def("fused_all_gather(Tensor(a!) buf, Tensor buf_ptrs, Tensor pad_ptrs, int rank, int blocks, Tensor? err) -> ()");
   m.def("peer_barrier(Tensor pad_ptrs, int rank, Tensor? err, int device) -> ()", &tgcm::peer_barrier);
 }
 
 TORCH_LIBRARY_IMPL(tgcm, CUDA, m) {
   m.impl("fused_allreduce_mean", &tgcm::fused_allreduce_mean);
   m.impl("slot_sum", &tgcm::slot_sum);
+  m.impl("fused_reduce_scatter", &tgcm::fused_reduce_scatter);
+  m.impl("fused_all_gather", &tgcm::fused_all_gather);
 }

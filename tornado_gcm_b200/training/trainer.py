@@ -223,12 +223,25 @@ class GCMTrainer:
         """``data_parallel``: replicated weights, gradients reduced over the ranks after
         backward — averaged (data parallelism: each rank's loss is a full loss of its own
         samples) or summed with ``grad_average=False`` (a model sharded over the ranks:
-        each rank's loss is its share of one global loss)."""
+        each rank's loss is its share of one global loss).  ``data_parallel="sharded"``:
+        data parallelism with the averaged gradients and the AdamW state split over the
+        ranks (:class:`~tornado_gcm_b200.parallel.sharded_optim.ShardedAdamW`: reduce-scatter,
+        clip by the global norm, AdamW on the own chunk, all-gather of the weights)."""
         self.gcm = gcm
         params = [p for p in gcm.parameters() if p.requires_grad]
         self.dp = None
+        self.zero_opt = None
         dev = params[0].device
-        if data_parallel:
+        if data_parallel == "sharded":
+            from tornado_gcm_b200.parallel.sharded_optim import ShardedAdamW
+
+            if not grad_average:
+                raise ValueError("the sharded optimizer averages gradients (data parallelism)")
+            self.zero_opt = ShardedAdamW(params, lr=lr, weight_decay=weight_decay, betas=betas, eps=eps,
+                                         max_grad_norm=max_grad_norm, capturable=graph and dev.type == "cuda")
+            self.zero_opt.zero_grad()
+            self._flat = self.zero_opt.flat_grad
+        elif data_parallel:
             from tornado_gcm_b200.parallel.ddp import GradientAllReducer
 
             self.dp = GradientAllReducer(params, average=grad_average)
@@ -247,8 +260,11 @@ class GCMTrainer:
         # the column networks add their weight/bias gradients straight into .grad
         self.fused_grad_accumulation = dev.type == "cuda"
         self.device = dev
-        self.optimizer = torch.optim.AdamW(params, lr=lr, weight_decay=weight_decay, betas=betas, eps=eps,
-                                           fused=dev.type == "cuda", capturable=graph and dev.type == "cuda")
+        if self.zero_opt is not None:
+            self.optimizer = self.zero_opt.optimizer
+        else:
+            self.optimizer = torch.optim.AdamW(params, lr=lr, weight_decay=weight_decay, betas=betas, eps=eps,
+                                               fused=dev.type == "cuda", capturable=graph and dev.type == "cuda")
         self.params = params
         self.max_grad_norm = max_grad_norm
         self.ema = _Ema(gcm, ema_num_steps)
@@ -288,10 +304,13 @@ class GCMTrainer:
             loss.backward()
         finally:
             linear_ops.set_fused_grad_accumulation(prev)
-        if self.dp is not None:
-            self.dp.reduce()
-        torch.nn.utils.clip_grad_norm_(self.params, self.max_grad_norm, foreach=True)
-        self.optimizer.step()
+        if self.zero_opt is not None:
+            self.zero_opt.step()
+        else:
+            if self.dp is not None:
+                self.dp.reduce()
+            torch.nn.utils.clip_grad_norm_(self.params, self.max_grad_norm, foreach=True)
+            self.optimizer.step()
         self.ema.update()
         return loss.detach()
 
@@ -303,6 +322,15 @@ class GCMTrainer:
     def _zero(self):
         self._flat.zero_()
         self._attach()
+        if self.zero_opt is not None:
+            self.zero_opt.attach()
+
+    @property
+    def grad_reducer(self) -> str:
+        """Which collective reduces the gradients (recorded in benchmark lines)."""
+        if self.zero_opt is not None:
+            return "sharded optimizer: " + self.zero_opt.backend
+        return self.dp.backend if self.dp is not None else "none (one rank)"
 
     def train_step(self, data0: dict, targets: list, forcings: dict) -> torch.Tensor:
         """One optimizer step; returns the loss as a 0-d device tensor."""
