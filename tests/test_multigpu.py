@@ -189,6 +189,12 @@ def _worker_gathered_linear(rank, world, port, q):
             res[f"rel_{O}"] = float((out - ref).norm() / ref.norm())
             base = lin.baseline_forward(x.to(dev), out_dtype=torch.float32).cpu()
             res[f"base_{O}"] = float((out - base).abs().max())
+            # the pulled-weight path (large token counts) gives the same result
+            pulled = lin.pull_forward(x.to(dev), out_dtype=torch.float32).cpu()
+            res[f"pull_{O}"] = float((pulled - base).abs().max())
+            xl = torch.randn(-(-lin.pull_min_work // lin.Kp) + 17, K, device=dev)
+            res[f"dispatch_{O}"] = float((lin(xl, out_dtype=torch.float32) -
+                                          lin.baseline_forward(xl, out_dtype=torch.float32)).abs().max())
         torch.cuda.synchronize(dev)
         res["flag"] = _ext.check_error_flag(dev)
         dist.barrier()
@@ -216,6 +222,8 @@ def test_gathered_linear_two_gpus():
         assert isinstance(res, dict), res
         assert res["rel_384"] < 1e-2 and res["rel_193"] < 1e-2
         assert res["base_384"] < 1e-3 and res["base_193"] < 1e-3
+        assert res["pull_384"] < 1e-3 and res["pull_193"] < 1e-3
+        assert res["dispatch_384"] < 1e-3 and res["dispatch_193"] < 1e-3
         assert res["flag"] == 0
 
 

@@ -27,6 +27,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
 
+#include <algorithm>
 #include <cstdint>
 
 namespace tgcm {
@@ -194,6 +195,25 @@ __global__ void __launch_bounds__(kArThreads) fused_all_gather_kernel(ArArgs a) 
   }
 }
 
+// Pull copy of static peer buffers: dst[p * bytes + i] = src_p[i] for every
+// rank p (its own buffer included), 16-byte plain loads over NVLink.  Used
+// for weight shards that do not change after set-up, so no barrier is needed.
+struct PullArgs {
+  const uint4* src[kArMaxRanks];
+  uint4* dst;
+  long long vecs;  // 16-byte vectors per source
+  int world;
+};
+
+__global__ void __launch_bounds__(256) pull_peer_buffers_kernel(PullArgs a) {
+  const long long total = a.vecs * a.world;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int p = static_cast<int>(i / a.vecs);
+    a.dst[i] = a.src[p][i - p * a.vecs];
+  }
+}
+
 // Stand-alone cross-rank barrier on a signal pad (one block): every rank
 // announces the next epoch in every peer's pad and waits (bounded) for all
 // peers' announcements.  Orders the peer reductions of a preceding kernel
@@ -306,6 +326,33 @@ void fused_all_gather(at::Tensor& buf, const at::Tensor& buf_ptrs, const at::Ten
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// dst (CUDA, contiguous, >= world * bytes_per_src bytes): the concatenation of the
+// first bytes_per_src bytes of every peer buffer in src_ptrs (int64 CPU tensor).
+void pull_peer_buffers(at::Tensor& dst, const at::Tensor& src_ptrs, int64_t bytes_per_src) {
+  TORCH_CHECK(dst.is_cuda() && dst.is_contiguous(), "pull_peer_buffers: contiguous CUDA destination expected");
+  TORCH_CHECK(src_ptrs.scalar_type() == at::kLong && !src_ptrs.is_cuda(), "src_ptrs must be an int64 CPU tensor");
+  const int64_t world = src_ptrs.numel();
+  TORCH_CHECK(world >= 1 && world <= kArMaxRanks, "1..8 sources supported");
+  TORCH_CHECK(bytes_per_src > 0 && bytes_per_src % 16 == 0, "bytes_per_src must be a positive multiple of 16");
+  TORCH_CHECK(dst.numel() * dst.element_size() >= world * bytes_per_src, "destination too small");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(dst.data_ptr()) % 16 == 0, "destination must be 16-byte aligned");
+  PullArgs a;
+  memset(&a, 0, sizeof(a));
+  for (int64_t p = 0; p < world; ++p) {
+    const int64_t v = src_ptrs.data_ptr<int64_t>()[p];
+    TORCH_CHECK(v % 16 == 0, "source buffers must be 16-byte aligned");
+    a.src[p] = reinterpret_cast<const uint4*>(v);
+  }
+  a.dst = reinterpret_cast<uint4*>(dst.data_ptr());
+  a.vecs = bytes_per_src / 16;
+  a.world = static_cast<int>(world);
+  c10::cuda::CUDAGuard guard(dst.device());
+  const long long total = a.vecs * world;
+  const unsigned blocks = static_cast<unsigned>(std::min<long long>((total + 255) / 256, 148LL * 4));
+  pull_peer_buffers_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 namespace {
 
 // out[i, l] = sum_w slots[w][i, l] for l < L (slots: W blocks of rows x ld floats);
@@ -366,6 +413,7 @@ TORCH_LIBRARY_FRAGMENT(tgcm, m) {
   m.def("fused_allreduce_mean(Tensor(a!) buf, Tensor buf_ptrs, Tensor pad_ptrs, int rank, int blocks, Tensor? err, float scale=0.0) -> ()");
   m.def("fused_reduce_scatter(Tensor(a!) buf, Tensor buf_ptrs, Tensor pad_ptrs, int rank, int blocks, Tensor? err, float scale=0.0) -> ()");
   m.def("fused_all_gather(Tensor(a!) buf, Tensor buf_ptrs, Tensor pad_ptrs, int rank, int blocks, Tensor? err) -> ()");
+  m.def("pull_peer_buffers(Tensor(a!) dst, Tensor src_ptrs, int bytes_per_src) -> ()");
   m.def("peer_barrier(Tensor pad_ptrs, int rank, Tensor? err, int device) -> ()", &tgcm::peer_barrier);
 }
 
@@ -374,4 +422,5 @@ TORCH_LIBRARY_IMPL(tgcm, CUDA, m) {
   m.impl("slot_sum", &tgcm::slot_sum);
   m.impl("fused_reduce_scatter", &tgcm::fused_reduce_scatter);
   m.impl("fused_all_gather", &tgcm::fused_all_gather);
+  m.impl("pull_peer_buffers", &tgcm::pull_peer_buffers);
 }

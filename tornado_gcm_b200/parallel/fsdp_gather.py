@@ -35,6 +35,12 @@ from tornado_gcm_b200.ops import _ext
 from tornado_gcm_b200.ops.linear import ACT_CODES as _ACT
 
 
+# Crossover between reading the shards inside the GEMM and pulling them first, in
+# GEMM rows x padded input width (2 x B200: the in-GEMM read wins at 8192 x 384,
+# the pulled weight from 16384 x 384 and from 8192 x 768 on).
+PULL_MIN_WORK = 16384 * 384
+
+
 def _pad8(k: int) -> int:
     return (k + 7) // 8 * 8
 
@@ -78,6 +84,8 @@ class GatheredLinear:
         self._handle = h
         self.w_ptrs = torch.tensor([int(p) for p in h.buffer_ptrs], dtype=torch.int64)
         self.bias = None if bias is None else bias.detach().float().contiguous().to(dev)
+        # GEMM size (rows x Kp) from which the weight is pulled locally before the GEMM (see __call__)
+        self.pull_min_work = int(os.environ.get("TGCM_GATHER_PULL_MIN_WORK", str(PULL_MIN_WORK)))
         torch.cuda.synchronize(dev)
         dist.barrier(group=self.group)
 
@@ -91,14 +99,40 @@ class GatheredLinear:
         return self.local_weight()[: r1 - r0, : self.in_features]
 
     def __call__(self, x: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
-        ops = _ext.require("fused all-gather linear")
+        """Dispatch on the GEMM's size: below ``pull_min_work`` (token rows x padded input
+        width) the GEMM reads the shards in place (:meth:`fused_forward`); from it on the
+        weight is pulled into this GPU's memory first (:meth:`pull_forward`), so that the
+        128-row tiles of the ordinary kernel apply."""
+        rows = x.numel() // x.shape[-1]
+        if rows * self.Kp >= self.pull_min_work:
+            return self.pull_forward(x, out_dtype)
+        return self.fused_forward(x, out_dtype)
+
+    def _rows_in(self, x: torch.Tensor) -> torch.Tensor:
         x = x.to(torch.bfloat16)
         if x.shape[-1] != self.Kp:
             x = torch.nn.functional.pad(x, (0, self.Kp - x.shape[-1]))
-        x2 = x.reshape(-1, self.Kp).contiguous()
+        return x.reshape(-1, self.Kp).contiguous()
+
+    def fused_forward(self, x: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+        """The GEMM's producer warp loads every weight block from the rank that owns it."""
+        ops = _ext.require("fused all-gather linear")
+        x2 = self._rows_in(x)
         out = torch.empty(x2.shape[0], self.O, dtype=out_dtype, device=x2.device)
         ops.linear_fwd_gathered(x2, self.w_ptrs, self.rows, self.O, self.bias, self.act, out, None,
                                 _ext.error_flag(x2.device))
+        return out.reshape(x.shape[:-1] + (self.O,))
+
+    def pull_forward(self, x: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+        """One copy kernel pulls every shard over NVLink (16-byte peer loads) into a transient
+        local buffer, then the ordinary tcgen05 linear kernel runs: for large token counts the
+        weight is reused by so many tiles that reading it once and locally wins."""
+        ops = _ext.require("pulled all-gather linear")
+        full = torch.empty(self.world * self.rows, self.Kp, dtype=torch.bfloat16, device=self.shard.device)
+        ops.pull_peer_buffers(full, self.w_ptrs, self.rows * self.Kp * 2)
+        x2 = self._rows_in(x)
+        out = torch.empty(x2.shape[0], self.O, dtype=out_dtype, device=x2.device)
+        ops.linear_fwd(x2, full[: self.O], self.bias, self.act, out, None, _ext.error_flag(x2.device))
         return out.reshape(x.shape[:-1] + (self.O,))
 
     def baseline_forward(self, x: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
@@ -167,7 +201,7 @@ def _time(fn, iters: int, warmup: int) -> float:
 
 def main(argv=None) -> None:  # pragma: no cover - needs several GPUs
     ap = argparse.ArgumentParser(description="fused all-gather linear vs NCCL all-gather + linear")
-    ap.add_argument("--tokens", type=int, nargs="+", default=[8192, 32768])
+    ap.add_argument("--tokens", type=int, nargs="+", default=[8192, 16384, 32768])
     ap.add_argument("--width", type=int, nargs="+", default=[384, 768])
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
@@ -183,15 +217,21 @@ def main(argv=None) -> None:  # pragma: no cover - needs several GPUs
             lin = GatheredLinear(w, b, "gelu_tanh")
             for T in args.tokens:
                 x = torch.randn(T, width, device="cuda").to(torch.bfloat16)
-                fused = _time(lambda: lin(x), args.iters, args.warmup)
+                fused = _time(lambda: lin.fused_forward(x), args.iters, args.warmup)
+                pull = _time(lambda: lin.pull_forward(x), args.iters, args.warmup)
+                auto = _time(lambda: lin(x), args.iters, args.warmup)
                 base = _time(lambda: lin.baseline_forward(x), args.iters, args.warmup)
                 flops = 2.0 * T * width * width
                 wbytes = 2.0 * width * width * (lin.world - 1) / lin.world
-                err = float((lin(x).float() - lin.baseline_forward(x).float()).abs().max())
+                ref = lin.baseline_forward(x).float()
+                err = float((lin.fused_forward(x).float() - ref).abs().max())
+                err_pull = float((lin.pull_forward(x).float() - ref).abs().max())
                 if dist.get_rank() == 0:
                     print(json.dumps({"tokens": T, "width": width, "gpus": lin.world, "fused_ms": fused,
-                                      "nccl_gather_ms": base, "fused_tflops": flops / fused / 1e9,
-                                      "remote_weight_bytes": wbytes, "max_abs_diff": err}), flush=True)
+                                      "pull_ms": pull, "dispatch_ms": auto, "nccl_gather_ms": base,
+                                      "dispatch_path": "pull" if T * lin.Kp >= lin.pull_min_work else "fused",
+                                      "dispatch_tflops": flops / auto / 1e9, "remote_weight_bytes": wbytes,
+                                      "max_abs_diff": err, "max_abs_diff_pull": err_pull}), flush=True)
     finally:
         dist.barrier()
         dist.destroy_process_group()
