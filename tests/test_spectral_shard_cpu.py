@@ -147,3 +147,43 @@ def test_sharded_model_loss_and_gradients_match_full_model(world):
         assert n_grads > 10
         assert abs(l_shd - l_ref) <= 1e-5 * abs(l_ref)
         assert worst < 1e-4
+
+
+def _worker_dtensor_entry(rank, world, port, q):
+    """The reference's DTensor entry point with the latitude layout runs the sharded step."""
+    try:
+        _init(rank, world, port)
+        from tornado_gcm_b200.distributed.dtensor_sharding import maybe_enable_dtensor_sharding
+        from tornado_gcm_b200.models.builders import build_hybrid_gcm
+
+        def make():
+            gcm, data = build_hybrid_gcm("5.6deg", "cpu", seed=0)
+            gcm.model.packed_on_cpu = True
+            gcm.physics_steps_per_output = 2
+            return gcm, data
+
+        ref, data = make()
+        enc = ref.encoder
+        norm = lambda d: {k: (v - getattr(enc, f"mean_{k}")) / getattr(enc, f"std_{k}") for k, v in d.items()}
+        x0, tg, forc = norm(data.sample(2, 0)), [norm(data.sample(2, 1))], data.forcings(2)
+        l_ref = float(ref.loss(x0, tg, forc).detach())
+
+        class Cfg:
+            dtensor_aware = True
+            dtensor_state_layout = "spatial_lat"
+
+        shd, _ = make()
+        out = maybe_enable_dtensor_sharding(shd, Cfg())
+        sc = out.scatter_fields
+        loss = out.loss(sc(x0), [sc(t) for t in tg], sc(forc)).detach().clone()
+        dist.all_reduce(loss)
+        q.put((rank, l_ref, float(loss), out._dtensor_runtime_mode, out.shard.world))
+        dist.destroy_process_group()
+    except Exception:  # pragma: no cover - reported to the parent
+        q.put((rank, traceback.format_exc()))
+
+
+def test_dtensor_latitude_layout_runs_the_sharded_step():
+    for _, l_ref, l_shd, mode, w in _spawn(_worker_dtensor_entry, 2):
+        assert mode == "model_sharded" and w == 2
+        assert abs(l_shd - l_ref) <= 1e-5 * abs(l_ref)

@@ -377,6 +377,41 @@ class SpectralShardingContext:
 
 # ─────────────────────────── model hook ─────────────────────────────
 
+# State layouts that run the model step itself sharded (modal rows by zonal
+# wavenumber, nodal columns by latitude block) instead of sharding the state
+# between steps and gathering it before each one.
+MODEL_SHARDED_LAYOUTS = ("spatial_lat", "wavenumber_latitude")
+
+
+def _is_hybrid_gcm(model) -> bool:
+    return all(hasattr(model, a) for a in ("model", "encoder", "decoder", "loss"))
+
+
+def _shard_hybrid_model(model: nn.Module, config: Any) -> nn.Module:
+    """Latitude layout on a hybrid GCM: the whole step runs sharded over the ranks.
+
+    The reference shards the state by latitude and gathers it back before every
+    step (its spectral context is never used by the step,
+    ``distributed/dtensor_sharding.py:779-846``, ``training/trainer.py:184-206``).
+    Here the layout selects :func:`~tornado_gcm_b200.parallel.spectral_shard.shard_hybrid_gcm`:
+    every spectral field keeps the rows of this rank's wavenumbers, every nodal
+    field this rank's latitude block, and the transforms move data between the
+    two layouts (fused peer-memory epilogues on NVLink, ``torch.distributed``
+    collectives elsewhere).  ``model.scatter_fields`` cuts a batch of nodal
+    fields down to this rank's block; train it with
+    ``GCMTrainer(data_parallel=True, grad_average=False)``.
+    """
+    from tornado_gcm_b200.parallel import spectral_shard as ss
+
+    dev = next(model.parameters()).device
+    engine = getattr(config, "dtensor_transform_engine", None) or ("auto" if dev.type == "cuda" else "collective")
+    ss.shard_hybrid_gcm(model, None, engine)
+    ctx = model.shard
+    model._dtensor_runtime_mode = "model_sharded"
+    model._dtensor_mesh = None
+    model.scatter_fields = lambda fields: ss.scatter_fields(fields, ctx)
+    return model
+
 
 def maybe_enable_dtensor_sharding(model: nn.Module, config: Any, coords: Any = None) -> nn.Module:
     """Bind a mesh and state shard/gather helpers to ``model`` when ``config.dtensor_aware``.
@@ -388,6 +423,9 @@ def maybe_enable_dtensor_sharding(model: nn.Module, config: Any, coords: Any = N
     """
     if not getattr(config, "dtensor_aware", False):
         return model
+    state_layout = getattr(config, "dtensor_state_layout", "level") or "level"
+    if state_layout in MODEL_SHARDED_LAYOUTS and _is_hybrid_gcm(model):
+        return _shard_hybrid_model(model, config)
     backend = dist.get_backend() if dist.is_available() and dist.is_initialized() else ""
     if backend == "nccl":
         device = "cuda"
@@ -403,7 +441,6 @@ def maybe_enable_dtensor_sharding(model: nn.Module, config: Any, coords: Any = N
             coords = getattr(owner, "coords", None)
             if coords is not None:
                 break
-    state_layout = getattr(config, "dtensor_state_layout", "level") or "level"
     param_layout = getattr(config, "dtensor_param_layout", "replicate") or "replicate"
     state_spec = layout_to_sharding_spec(state_layout, mesh.ndim)
     param_spec = layout_to_sharding_spec(param_layout, mesh.ndim)
