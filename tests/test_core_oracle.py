@@ -152,3 +152,16 @@ def test_sil3_step_matches(ref, rng):
     step = ti.imex_rk_sil3(eq, 0.01)
     rstep = ref.time_integration.imex_rk_sil3(req.as_imex_ode(), 0.01)
     _assert_state_close(step(st), rstep(rst), rtol=1e-8, atol=1e-10)
+
+
+def test_compiled_sil3_tableau_liveness():
+    """The compiled SIL3 program: stage weights, implicit weights and which tendencies are evaluated."""
+    from tornado_gcm_b200.core import time_integration as ti
+
+    dt = 0.5
+    plans, final = ti.compile_imex_tableau(ti.SIL3_TABLEAU, dt)
+    assert [p.eta for p in plans] == pytest.approx([0.0, dt / 6, dt / 3, dt / 4])
+    assert plans[0].keep == {"F", "G"} and plans[1].keep == {"F"} and plans[2].keep == {"F", "G"}
+    assert plans[3].keep == {"G"}                      # b_ex[3] = 0: F of the last stage is never needed
+    assert plans[2].terms == ((dt / 6, "F", 0), (dt / 3, "G", 0), (dt / 2, "F", 1))
+    assert [(k, j) for _, k, j in final] == [("F", 0), ("G", 0), ("F", 1), ("F", 2), ("G", 2), ("G", 3)]

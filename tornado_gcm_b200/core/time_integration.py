@@ -187,39 +187,82 @@ SIL3_TABLEAU = ImExButcherTableau(
 )
 
 
-def imex_runge_kutta(tableau: ImExButcherTableau, equation: ImplicitExplicitODE, time_step: float,
-                     step_hook: Optional[Callable[[int, Any], None]] = None) -> TimeStepFn:
-    """Generic IMEX-RK: y_i = (I - dt a_im[i,i] G)^{-1}(y0 + dt Σ_j<i a_ex F_j + a_im G_j)."""
-    dt = time_step
+@dataclasses.dataclass(frozen=True)
+class _StagePlan:
+    """One stage of a compiled IMEX-RK tableau.
+
+    ``terms``: the (weight, kind, index) products added to y0 to form the stage's
+    right-hand side, kind ``"F"`` (explicit tendency of stage index) or ``"G"``
+    (implicit tendency); ``eta``: the implicit weight of the stage's solve;
+    ``keep``: which of this stage's tendencies a later stage or the final
+    combination reads (the others are never evaluated).
+    """
+
+    terms: tuple
+    eta: float
+    keep: frozenset
+
+
+def compile_imex_tableau(tableau: ImExButcherTableau, dt: float) -> tuple:
+    """(stage plans, final terms) of ``tableau`` at step ``dt``.
+
+    The tableau is turned into a small program once: row ``i - 1`` of ``a_ex`` /
+    ``a_im`` gives stage i's right-hand side (zero weights dropped), the diagonal
+    entry ``a_im[i - 1][i]`` its implicit weight, and a liveness pass from the
+    last combination backwards marks the tendencies that are read at all.
+    """
     a_ex, a_im, b_ex, b_im = tableau.a_ex, tableau.a_im, tableau.b_ex, tableau.b_im
     n = len(b_ex)
 
+    def products(row_ex, row_im, width):
+        out = []
+        for j in range(width):
+            if j < len(row_ex) and row_ex[j]:
+                out.append((dt * row_ex[j], "F", j))
+            if j < len(row_im) and row_im[j]:
+                out.append((dt * row_im[j], "G", j))
+        return tuple(out)
+
+    rhs = [()] + [products(a_ex[i - 1], a_im[i - 1], i) for i in range(1, n)]
+    etas = [0.0] + [dt * a_im[i - 1][i] for i in range(1, n)]
+    final = products(b_ex, b_im, n)
+    live = {(k, j) for _, k, j in final}
+    plans = [None] * n
+    for i in range(n - 1, -1, -1):
+        plans[i] = _StagePlan(rhs[i], etas[i], frozenset(k for k in ("F", "G") if (k, i) in live))
+        live |= {(k, j) for _, k, j in rhs[i]}
+    return tuple(plans), final
+
+
+def imex_runge_kutta(tableau: ImExButcherTableau, equation: ImplicitExplicitODE, time_step: float,
+                     step_hook: Optional[Callable[[int, Any], None]] = None) -> TimeStepFn:
+    """Generic IMEX-RK: y_i = (I - dt a_im[i,i] G)^{-1}(y0 + dt Σ_j<i a_ex F_j + a_im G_j).
+
+    Stage 0 is y0 itself; the step returns y0 + dt Σ_j (b_ex F_j + b_im G_j).
+    Tendencies that no later combination reads are not evaluated.
+    """
+    plans, final = compile_imex_tableau(tableau, time_step)
+    tendency = {"F": equation.explicit_terms, "G": equation.implicit_terms}
+
+    def combine(y0, terms, tend):
+        y = y0
+        for w, kind, j in terms:
+            y = tree_axpy(y, w, tend[kind, j])
+        return y
+
     def step_fn(y0):
-        f = [None] * n
-        g = [None] * n
-        f[0] = equation.explicit_terms(y0)
-        g[0] = equation.implicit_terms(y0)
-        for i in range(1, n):
-            y_star = y0
-            for j in range(i):
-                if a_ex[i - 1][j]:
-                    y_star = tree_axpy(y_star, dt * a_ex[i - 1][j], f[j])
-                if a_im[i - 1][j]:
-                    y_star = tree_axpy(y_star, dt * a_im[i - 1][j], g[j])
-            y_i = equation.implicit_inverse(y_star, dt * a_im[i - 1][i])
-            if step_hook is not None:
-                step_hook(i, y_i)
-            if b_ex[i] or any(a_ex[r][i] for r in range(i, n - 1)):
-                f[i] = equation.explicit_terms(y_i)
-            if b_im[i] or any(a_im[r][i] for r in range(i, n - 1)):
-                g[i] = equation.implicit_terms(y_i)
-        out = y0
-        for j in range(n):
-            if b_ex[j] and f[j] is not None:
-                out = tree_axpy(out, dt * b_ex[j], f[j])
-            if b_im[j] and g[j] is not None:
-                out = tree_axpy(out, dt * b_im[j], g[j])
-        return out
+        tend = {}
+        for i, plan in enumerate(plans):
+            if i == 0:
+                y_i = y0
+            else:
+                y_i = equation.implicit_inverse(combine(y0, plan.terms, tend), plan.eta)
+                if step_hook is not None:
+                    step_hook(i, y_i)
+            for kind in ("F", "G"):
+                if kind in plan.keep:
+                    tend[kind, i] = tendency[kind](y_i)
+        return combine(y0, final, tend)
     return step_fn
 
 
