@@ -46,20 +46,10 @@ class PrecisionPolicy:
     audit_every_n_steps: int = 100
 
     def compute_dtype(self, zone: PrecisionZone) -> torch.dtype:
-        return {
-            PrecisionZone.Z0_NUMERICAL_FOUNDATION: self.z0_dtype,
-            PrecisionZone.Z1_DYNAMICS_CORE: self.z1_compute_dtype,
-            PrecisionZone.Z2_CONSERVATION_FIXER: self.z2_compute_dtype,
-            PrecisionZone.Z3_NEURAL_NETWORK: self.z3_compute_dtype,
-        }[zone]
+        return getattr(self, _ZONE_FIELDS[zone][0])
 
     def storage_dtype(self, zone: PrecisionZone) -> torch.dtype:
-        return {
-            PrecisionZone.Z0_NUMERICAL_FOUNDATION: self.z0_dtype,
-            PrecisionZone.Z1_DYNAMICS_CORE: self.z1_storage_dtype,
-            PrecisionZone.Z2_CONSERVATION_FIXER: self.z2_storage_dtype,
-            PrecisionZone.Z3_NEURAL_NETWORK: self.z3_param_dtype,
-        }[zone]
+        return getattr(self, _ZONE_FIELDS[zone][1])
 
     def sht_precision(self, total_wavenumbers: int) -> str:
         """Transform precision for a grid with ``total_wavenumbers`` (honours the threshold)."""
@@ -81,17 +71,10 @@ class PrecisionPolicy:
 
     @classmethod
     def for_training_phase(cls, phase: int, base: Optional["PrecisionPolicy"] = None) -> "PrecisionPolicy":
-        base = base or cls()
-        if phase == 1:
-            return dataclasses.replace(base, z3_compute_dtype=torch.bfloat16, z1_use_tf32=True,
-                                       z2_compute_dtype=torch.float32)
-        if phase == 2:
-            return dataclasses.replace(base, z3_compute_dtype=torch.bfloat16, z1_use_tf32=True,
-                                       z2_compute_dtype=torch.float64)
-        if phase == 3:
-            return dataclasses.replace(base, z3_compute_dtype=torch.float32, z3_param_dtype=torch.float32,
-                                       z1_use_tf32=True, z2_compute_dtype=torch.float64)
-        raise ValueError(f"Unknown training phase: {phase}")
+        """Phase 1 aggressive (FP32 fixer), 2 standard PZHA, 3 FP32 network fine-tune."""
+        if phase not in _PHASE_OVERRIDES:
+            raise ValueError(f"Unknown training phase: {phase}")
+        return dataclasses.replace(base or cls(), **_PHASE_OVERRIDES[phase])
 
     @classmethod
     def pzha_b200(cls) -> "PrecisionPolicy":
@@ -117,21 +100,41 @@ class PolicyEngine:
         return {z: (self._policy.compute_dtype(z), self._policy.storage_dtype(z)) for z in PrecisionZone}
 
     def get_module_zone_map(self, model: torch.nn.Module) -> dict:
-        z3 = {"nn", "mlp", "transformer", "encoder", "decoder", "learned", "embed", "tower", "parameterization"}
-        z2 = {"fixer", "conservation", "energy", "mass"}
-        z0 = {"sht", "spectral", "legendre", "basis", "fourier", "sigma"}
-        out = {}
-        for name, _ in model.named_modules():
+        """Zone of every named submodule: the first rule of ``_MODULE_ZONE_RULES`` whose
+        keyword occurs in the lower-cased name, else the dynamics core (Z1)."""
+        def zone_of(name: str) -> PrecisionZone:
             low = name.lower()
-            if any(k in low for k in z3):
-                out[name] = PrecisionZone.Z3_NEURAL_NETWORK
-            elif any(k in low for k in z2):
-                out[name] = PrecisionZone.Z2_CONSERVATION_FIXER
-            elif any(k in low for k in z0):
-                out[name] = PrecisionZone.Z0_NUMERICAL_FOUNDATION
-            else:
-                out[name] = PrecisionZone.Z1_DYNAMICS_CORE
-        return out
+            for zone, words in _MODULE_ZONE_RULES:
+                if any(w in low for w in words):
+                    return zone
+            return PrecisionZone.Z1_DYNAMICS_CORE
+
+        return {name: zone_of(name) for name, _ in model.named_modules()}
+
+
+# (compute field, storage field) of each zone
+_ZONE_FIELDS = {
+    PrecisionZone.Z0_NUMERICAL_FOUNDATION: ("z0_dtype", "z0_dtype"),
+    PrecisionZone.Z1_DYNAMICS_CORE: ("z1_compute_dtype", "z1_storage_dtype"),
+    PrecisionZone.Z2_CONSERVATION_FIXER: ("z2_compute_dtype", "z2_storage_dtype"),
+    PrecisionZone.Z3_NEURAL_NETWORK: ("z3_compute_dtype", "z3_param_dtype"),
+}
+
+# the documented variable-precision training phases, as overrides of a base policy
+_PHASE_OVERRIDES = {
+    1: {"z3_compute_dtype": torch.bfloat16, "z1_use_tf32": True, "z2_compute_dtype": torch.float32},
+    2: {"z3_compute_dtype": torch.bfloat16, "z1_use_tf32": True, "z2_compute_dtype": torch.float64},
+    3: {"z3_compute_dtype": torch.float32, "z3_param_dtype": torch.float32, "z1_use_tf32": True,
+        "z2_compute_dtype": torch.float64},
+}
+
+# module-name keywords per zone, tried in this order (networks before fixers before bases)
+_MODULE_ZONE_RULES = (
+    (PrecisionZone.Z3_NEURAL_NETWORK,
+     ("nn", "mlp", "transformer", "encoder", "decoder", "learned", "embed", "tower", "parameterization")),
+    (PrecisionZone.Z2_CONSERVATION_FIXER, ("fixer", "conservation", "energy", "mass")),
+    (PrecisionZone.Z0_NUMERICAL_FOUNDATION, ("sht", "spectral", "legendre", "basis", "fourier", "sigma")),
+)
 
 
 DEFAULT_POLICY = PrecisionPolicy()
