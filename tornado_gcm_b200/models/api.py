@@ -41,23 +41,27 @@ State = primitive_equations.State
 ForcingFn = Callable[[dict, float], dict]
 
 
+_EPD_MEMORY_FIELDS = frozenset(("vorticity", "divergence", "temperature_variation", "log_surface_pressure"))
+
+
 def _physics_memory_ok_for_epd(memory, state: State) -> bool:
+    """Whether ``memory`` supplies every ``memory_*`` feature the physics network was built with.
+
+    A :class:`State` (or any object that is not a dict) is used as it is.  A dict
+    qualifies when it holds the four core spectral fields and, for a state with
+    tracers, a tracer dict covering all of them; an empty or partial dict (a
+    forcing-only blob, say) would narrow the packed feature vector below the
+    trained width, so the caller falls back to the current state.
+    """
     if memory is None:
         return False
-    if isinstance(memory, State):
+    if not isinstance(memory, dict):
         return True
-    if isinstance(memory, dict):
-        if not memory:
-            return False
-        req = ("vorticity", "divergence", "temperature_variation", "log_surface_pressure")
-        if not all(k in memory for k in req):
-            return False
-        if state.tracers:
-            mt = memory.get("tracers")
-            if not isinstance(mt, dict) or set(state.tracers) - set(mt):
-                return False
-        return True
-    return True
+    if not _EPD_MEMORY_FIELDS.issubset(memory):
+        return False
+    wanted = set(state.tracers or ())
+    have = memory.get("tracers")
+    return not wanted or (isinstance(have, dict) and wanted.issubset(have))
 
 
 @dataclasses.dataclass
