@@ -412,7 +412,7 @@ def run_b200(args, rank, world):
                 "seq_len_meaning": "6-h rollout steps per example (backprop through the whole rollout)",
                 "parallelism": (f"lat{world} (modal rows by zonal wavenumber, nodal columns by latitude block; "
                                 f"transposes fused into the Legendre GEMMs)") if lat else (
-                    f"dp{world} (gradients and AdamW state sharded)" if args.parallel == "sharded" else f"dp{world}"),
+                    f"dp{world} (gradients and AdamW state sharded)" if dp_mode == "sharded" else f"dp{world}"),
                 "zones": "Z1 TF32 tcgen05 transforms, Z3 BF16 tcgen05 towers, Z2 FP64-accumulated fixer",
                 "grad_reducer": trainer.grad_reducer,
                 "cuda_graph": trainer.use_graph,
