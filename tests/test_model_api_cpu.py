@@ -218,3 +218,17 @@ def test_checkpointed_outer_steps_give_the_same_gradients():
     for a, b, c in zip(g0, g1, g2):
         torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-7)
         torch.testing.assert_close(a, c, rtol=1e-5, atol=1e-7)
+
+
+def test_physics_memory_check_needs_every_core_field_and_tracer():
+    from tornado_gcm_b200.models.api import _physics_memory_ok_for_epd as ok
+
+    class _S:
+        def __init__(self, tracers):
+            self.tracers = tracers
+
+    core = {k: 0 for k in ("vorticity", "divergence", "temperature_variation", "log_surface_pressure")}
+    assert not ok(None, _S({})) and not ok({}, _S({})) and not ok({"vorticity": 0}, _S({}))
+    assert ok(core, _S({})) and ok(object(), _S({}))
+    assert not ok(core, _S({"q": 0})) and not ok({**core, "tracers": [0]}, _S({"q": 0}))
+    assert ok({**core, "tracers": {"q": 0, "c": 0}}, _S({"q": 0}))

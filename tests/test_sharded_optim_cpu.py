@@ -131,3 +131,26 @@ def test_sharded_optimizer_single_rank_is_adamw_with_clipping():
         opt.step()
         for p, s in zip(a.parameters(), b.parameters()):
             torch.testing.assert_close(p, s, atol=1e-6, rtol=1e-6)
+
+
+def test_sharded_optimizer_state_round_trip():
+    """The optimizer shard saves and loads its moments; a shard of another layout is refused."""
+    from tornado_gcm_b200.parallel.sharded_optim import ShardedAdamW
+
+    torch.manual_seed(2)
+    m = _Toy()
+    opt = ShardedAdamW(list(m.parameters()), lr=1e-2)
+    opt.zero_grad()
+    m.loss(*_batch(0, 0)).backward()
+    opt.step()
+    sd = opt.state_dict()
+    assert sd["world"] == 1 and sd["chunk"] == opt.chunk and sd["numel"] == opt.numel
+    m2 = _Toy()
+    opt2 = ShardedAdamW(list(m2.parameters()), lr=1e-2)
+    opt2.load_state_dict(sd)
+    a = opt.optimizer.state[opt.shard]["exp_avg"]
+    b = opt2.optimizer.state[opt2.shard]["exp_avg"]
+    torch.testing.assert_close(a, b)
+    bad = dict(sd, chunk=sd["chunk"] + 4)
+    with pytest.raises(ValueError):
+        opt2.load_state_dict(bad)
