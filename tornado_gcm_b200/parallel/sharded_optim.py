@@ -149,6 +149,8 @@ class ShardedAdamW:
         self.params = [p for p in params if p.requires_grad]
         if not self.params:
             raise ValueError("no trainable parameters")
+        if any(p.dtype != torch.float32 for p in self.params):
+            raise ValueError("the sharded optimizer keeps fp32 master weights: pass fp32 parameters")
         dev = self.params[0].device
         self.device = dev
         self.group = group or (dist.group.WORLD if dist.is_initialized() else None)
