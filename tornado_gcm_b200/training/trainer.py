@@ -219,14 +219,18 @@ class GCMTrainer:
 
     def __init__(self, gcm: nn.Module, lr: float = 1e-4, weight_decay: float = 0.0, max_grad_norm: float = 1.0,
                  ema_num_steps: int = 1999, graph: bool = False, betas=(0.9, 0.95), eps: float = 1e-6,
-                 data_parallel: bool = False, grad_average: bool = True):
+                 data_parallel: bool = False, grad_average: bool = True, check_errors_every: int = 0):
         """``data_parallel``: replicated weights, gradients reduced over the ranks after
         backward — averaged (data parallelism: each rank's loss is a full loss of its own
         samples) or summed with ``grad_average=False`` (a model sharded over the ranks:
         each rank's loss is its share of one global loss).  ``data_parallel="sharded"``:
         data parallelism with the averaged gradients and the AdamW state split over the
         ranks (:class:`~tornado_gcm_b200.parallel.sharded_optim.ShardedAdamW`: reduce-scatter,
-        clip by the global norm, AdamW on the own chunk, all-gather of the weights)."""
+        clip by the global norm, AdamW on the own chunk, all-gather of the weights).
+        ``check_errors_every``: every that many steps, read the device error flag that the
+        kernels set when a bounded wait expires or a table index is out of range, and raise
+        (one host synchronisation; 0 leaves the check to the caller, see
+        :meth:`check_device_errors`)."""
         self.gcm = gcm
         params = [p for p in gcm.parameters() if p.requires_grad]
         self.dp = None
@@ -273,6 +277,7 @@ class GCMTrainer:
         self._static = None
         self._static_loss = None
         self.step_count = 0
+        self.check_errors_every = int(check_errors_every)
         # host-side liveness check and fault injection between steps (see parallel/elastic.py)
         self.heartbeat = None
         self._fault_spec = os.environ.get("TGCM_FAULT_INJECT") or None
@@ -339,14 +344,23 @@ class GCMTrainer:
         if not self.use_graph:
             self._zero()
             loss = self._step_body(data0, targets, forcings)
-            self.step_count += 1
-            return loss
-        if self._graph is None:
-            self._capture(data0, targets, forcings)
-        self._copy_in(data0, targets, forcings)
-        self._graph.replay()
+        else:
+            if self._graph is None:
+                self._capture(data0, targets, forcings)
+            self._copy_in(data0, targets, forcings)
+            self._graph.replay()
+            loss = self._static_loss
         self.step_count += 1
-        return self._static_loss
+        if self.check_errors_every > 0 and self.step_count % self.check_errors_every == 0:
+            self.check_device_errors()
+        return loss
+
+    def check_device_errors(self) -> None:
+        """Raise if a kernel of this device recorded an error (expired bounded wait, bad index)."""
+        if self.device.type == "cuda":
+            from tornado_gcm_b200.ops import _ext
+
+            _ext.check_error_flag(self.device)
 
     # ── CUDA graph machinery ─────────────────────────────────────────
     def _copy_in(self, data0, targets, forcings):
