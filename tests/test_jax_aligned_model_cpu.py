@@ -156,3 +156,13 @@ def test_aligned_model_steps_from_checkpoint(checkpoint):
     for t in (tend.vorticity, tend.temperature_variation, nxt.vorticity, nxt.log_surface_pressure):
         assert torch.isfinite(t).all()
     assert float(tend.vorticity.abs().max()) > 0.0
+
+
+def test_reference_named_builders(checkpoint):
+    path, _ = checkpoint
+    comps, report = jcl.build_and_load_jax_model(path)
+    assert not comps.training and not report["missing"]
+    model, comps2, coords, config, report2 = jcl.build_jax_aligned_experiment_model(path)
+    assert config["physics_features"] == 2365 and not report2["missing"]
+    for a, b in zip(comps.parameters(), comps2.parameters()):
+        torch.testing.assert_close(a, b)

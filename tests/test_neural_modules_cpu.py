@@ -342,3 +342,25 @@ def test_stochastic_physics_step(grid):
     s1, r1 = step(st, randomness=r0)
     torch.testing.assert_close(s1.vorticity, st.vorticity)
     assert r1.prng_step == 3
+
+
+def test_reference_diagnostics_api():
+    from tornado_gcm_b200.core.primitive_equations import State
+    from tornado_gcm_b200.neural import diagnostics as d
+    from tornado_gcm_b200.utils.typing import ModelState
+
+    def mk(q, t):
+        z = torch.zeros(4, 5, 6)
+        return State(vorticity=z + 1, divergence=z, temperature_variation=z + t,
+                     log_surface_pressure=torch.zeros(1, 5, 6), tracers={"specific_humidity": torch.full((4, 5, 6), q)})
+
+    traj = [mk(1.0, 2.0), mk(0.5, 2.0), mk(0.75, 3.0)]
+    assert d.extract_energies(traj, mk(1.0, 2.0)).shape[0] == 4 and d.extract_masses(traj, mk(1.0, 2.0)).shape[0] == 4
+    p, e = d.extract_precipitation_evaporation(traj)
+    torch.testing.assert_close(p, torch.tensor([0.0, 2.0, 0.0], dtype=torch.float64))   # column q 4 -> 2 -> 3
+    torch.testing.assert_close(e, torch.tensor([0.0, 0.0, -1.0], dtype=torch.float64))
+    assert float(d.precipitation_rate_diagnostic(traj[1], traj[0])) == 2.0
+    assert float(d.heating_rate_diagnostic(traj[2], traj[1])) == 4.0                     # 4 levels x (+1)
+    out = d.CombinedStepDiagnostics()(ModelState(state=traj[2], memory=traj[1]))
+    assert set(out) == {"P_minus_E_rate", "heating_rate", "total_energy", "dry_air_mass"}
+    assert float(out["P_minus_E_rate"]) == -1.0

@@ -16,19 +16,18 @@ from tornado_gcm_b200.parallel.ddp import (  # noqa: F401
     all_reduce_metrics,
     build_distributed_sampler,
     cleanup_distributed,
+    get_distributed_sampler,
     get_local_rank,
     get_rank,
     get_world_size,
     is_distributed,
     is_main_process,
     register_fp32_spectral_grad_hooks,
+    register_spectral_grad_hooks,
     setup_distributed,
     wrap_ddp,
     wrap_fsdp,
 )
-
-register_spectral_grad_hooks = register_fp32_spectral_grad_hooks
-get_distributed_sampler = build_distributed_sampler
 
 __all__ = [
     "DDPConfig", "FSDPConfig", "GradientAllReducer", "setup_distributed", "cleanup_distributed", "wrap_ddp",

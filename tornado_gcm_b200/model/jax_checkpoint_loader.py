@@ -407,3 +407,20 @@ def build_jax_aligned_model(checkpoint: str | Path | dict | None = None, device:
     config = {"resolution": "2.8", "n_levels": N_SIGMA_LAYERS, "dt_hours": 1.0, "grid": "TL63",
               "latent_size": LATENT_SIZE, "num_blocks": NUM_BLOCKS, "physics_features": PHYSICS_EPD_INPUT}
     return model, comps, coords, config, report
+
+
+def build_jax_aligned_experiment_model(checkpoint_path: str | Path | None = None, device: str | torch.device = "cpu"):
+    """Reference-named entry point (``model/jax_checkpoint_loader.py:885``): the runnable
+    2.8° NeuralGCM of :func:`build_jax_aligned_model`, weights loaded with the strict map.
+    Returns ``(model, components, coords, config, report)``."""
+    return build_jax_aligned_model(checkpoint_path, device=device, strict=True)
+
+
+def build_and_load_jax_model(checkpoint_path: str | Path, device: str | torch.device = "cpu"):
+    """The neural components alone with the checkpoint's weights (reference
+    ``model/jax_checkpoint_loader.py:861``): ``(components in eval mode, load report)``.
+    Leaves without a target are reported rather than refused, as in the reference."""
+    comps = build_jax_neural_components()
+    flat = read_jax_checkpoint(checkpoint_path)
+    report = load_jax_weights(comps, {k: v for k, v in flat.items() if k.startswith("params/")}, strict=False)
+    return comps.to(device).eval(), report

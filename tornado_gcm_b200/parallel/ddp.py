@@ -167,6 +167,21 @@ def register_fp32_spectral_grad_hooks(model: nn.Module, keywords: Sequence[str] 
     return handles
 
 
+def register_spectral_grad_hooks(model: nn.Module, spectral_param_patterns: Sequence[str] = ("dynamics",)) -> list:
+    """Reference-named variant of :func:`register_fp32_spectral_grad_hooks`: parameters whose
+    name matches one of the regular expressions get their gradients in fp32."""
+    import re
+
+    rx = [re.compile(p) for p in spectral_param_patterns]
+    return [p.register_hook(lambda g: g.float() if g is not None and g.dtype != torch.float32 else g)
+            for name, p in model.named_parameters() if any(r.search(name) for r in rx)]
+
+
+def get_distributed_sampler(dataset, shuffle: bool = True, seed: int = 42):
+    """Reference-named sampler helper: a DistributedSampler with more than one rank, else None."""
+    return build_distributed_sampler(dataset, shuffle=shuffle, seed=seed)
+
+
 def build_distributed_sampler(dataset, shuffle: bool = True, seed: int = 0, drop_last: bool = False):
     from torch.utils.data.distributed import DistributedSampler
 

@@ -15,7 +15,7 @@ from __future__ import annotations
 
 import dataclasses
 import math
-from typing import Iterator, Mapping
+from typing import Iterator, Mapping, Protocol, runtime_checkable
 
 import numpy as np
 
@@ -213,6 +213,15 @@ def parse_units(units_str: str) -> Unit:
     return units.parse_expression(units_str)
 
 
+@runtime_checkable
+class ScaleProtocol(Protocol):
+    """What a non-dimensionalisation scale offers (:class:`Scale` implements it)."""
+
+    def nondimensionalize(self, quantity: "Quantity") -> float: ...
+
+    def dimensionalize(self, value: float, unit: "Unit") -> "Quantity": ...
+
+
 class Scale(Mapping):
     """Reference quantity per base dimension (reference: ``scales.py:82-147``)."""
 
@@ -262,6 +271,23 @@ NEURALGCM_V1_SCALE = Scale(RADIUS, 1 / 2 / OMEGA, 1.0 * units.kg, 1.0 * units.K)
 ATMOSPHERIC_SCALE = Scale(RADIUS, 1 / 2 / OMEGA, MASS_OF_DRY_ATMOSPHERE, 1.0 * units.K)
 SI_SCALE = Scale(1.0 * units.m, 1.0 * units.s, 1.0 * units.kg, 1.0 * units.K)
 DEFAULT_SCALE = NEURALGCM_V1_SCALE
+
+
+@runtime_checkable
+class SimUnitsProtocol(Protocol):
+    """What a set of non-dimensional physical constants offers (:class:`SimUnits` implements it)."""
+
+    radius: float
+    angular_velocity: float
+    gravity_acceleration: float
+    ideal_gas_constant: float
+    water_vapor_gas_constant: float
+    water_vapor_isobaric_heat_capacity: float
+    kappa: float
+
+    def nondimensionalize(self, quantity: "Quantity") -> float: ...
+
+    def dimensionalize(self, value: float, unit: "Unit") -> "Quantity": ...
 
 
 @dataclasses.dataclass(frozen=True)
@@ -347,7 +373,7 @@ def seconds_per_time_unit(scale: Scale = DEFAULT_SCALE) -> float:
 
 
 __all__ = [
-    "Unit", "Quantity", "units", "Scale", "SimUnits", "NEURALGCM_V1_SCALE",
+    "Unit", "Quantity", "units", "Scale", "ScaleProtocol", "SimUnits", "SimUnitsProtocol", "NEURALGCM_V1_SCALE",
     "ATMOSPHERIC_SCALE", "SI_SCALE", "DEFAULT_SCALE", "RADIUS", "OMEGA",
     "ANGULAR_VELOCITY", "GRAVITY_ACCELERATION", "ISOBARIC_HEAT_CAPACITY",
     "WATER_VAPOR_CP", "KAPPA", "IDEAL_GAS_CONSTANT", "IDEAL_GAS_CONSTANT_H20",
