@@ -343,6 +343,28 @@ def _prefix(x: torch.Tensor) -> torch.Tensor:
     return torch.cumsum(x, dim=-3)
 
 
+def _adiabatic_heating(temp, q, ugl, f_exp, f_full, c: ColumnConstants) -> torch.Tensor:
+    """κ T ω/p per column (Durran's energy-conserving σ discretisation): the reference
+    profile with the explicit σ flux ``f_exp`` plus the (moist-weighted) anomaly with the
+    full flux ``f_full``; ``f_*`` are the downward prefix sums of flux × Δσ."""
+    like = temp
+    dsig = _vec(c.dsigma, like, (-1, 1, 1))
+    alpha = _vec(c.alpha, like, (-1, 1, 1))
+    t_ref = _vec(c.t_ref, like, (-1, 1, 1))
+
+    def t_omega(tf, fcum):
+        af = alpha * fcum
+        af_prev = torch.cat([torch.zeros_like(af[..., :1, :, :]), af[..., :-1, :, :]], dim=-3)
+        return tf * (ugl - (af + af_prev) / dsig)
+
+    if q is not None:
+        denom = 1.0 + (c.cpv_ratio - 1.0) * q
+        var_in = temp * ((1.0 + (c.rv_ratio - 1.0) * q) / denom) + t_ref * (((c.rv_ratio - c.cpv_ratio) * q) / denom)
+    else:
+        var_in = temp
+    return c.kappa * (t_omega(t_ref, f_exp) + t_omega(var_in, f_full))
+
+
 def nodal_explicit_tendencies(inp: Mapping[str, Any], c: ColumnConstants, humidity_key: Optional[str],
                               cloud_keys: tuple = ()) -> dict:
     """Nonlinear explicit tendencies per column.
@@ -402,19 +424,7 @@ def nodal_explicit_tendencies(inp: Mapping[str, Any], c: ColumnConstants, humidi
     if c.vertical_advection:
         t_vert = _vadv(sd_full, temp, inv_dc) + _vadv(sd_exp, t_ref.expand_as(temp), inv_dc)
 
-    def t_omega(tf, fcum):
-        af = alpha * fcum
-        af_prev = torch.cat([torch.zeros_like(af[..., :1, :, :]), af[..., :-1, :, :]], dim=-3)
-        return tf * (ugl - (af + af_prev) / dsig)
-
-    mean_part = t_omega(t_ref, f_exp)
-    if humidity:
-        denom = 1.0 + (c.cpv_ratio - 1.0) * q
-        var_in = temp * ((1.0 + (c.rv_ratio - 1.0) * q) / denom) + t_ref * (((c.rv_ratio - c.cpv_ratio) * q) / denom)
-    else:
-        var_in = temp
-    var_part = t_omega(var_in, f_full)
-    out["temp"] = temp * div + t_vert + c.kappa * (mean_part + var_part)
+    out["temp"] = temp * div + t_vert + _adiabatic_heating(temp, q if humidity else None, ugl, f_exp, f_full, c)
     out["temp_u"] = u * temp * sec2
     out["temp_v"] = v * temp * sec2
     out["lnps"] = -(ugl * dsig).sum(dim=-3, keepdim=True)
@@ -626,6 +636,109 @@ class PrimitiveEquationsSigma(time_integration.ImplicitExplicitODE):
         inp = self.nodal_inputs(state, grid)
         out = nodal_explicit_tendencies(inp, self.column_constants, self.humidity_key, self.cloud_keys or ())
         return self.modal_outputs(out, state, grid)
+
+    # ── the explicit tendency term by term (reference ``core/primitive_equations.py:590-947``) ──
+    # Each method takes the nodal DiagnosticState of ``compute_diagnostic_state``; together they
+    # add up to ``explicit_terms`` (which evaluates all of them in one pass per column).
+    def _nodal_consts(self, like: torch.Tensor):
+        c = self.column_constants
+        return (_vec(c.sec2, like, (1, -1)), _vec(c.coriolis, like, (1, -1)), _vec(c.dsigma, like, (-1, 1, 1)),
+                _vec(c.t_ref, like, (-1, 1, 1)), _vec(c.inv_dcenter, like, (-1, 1, 1)))
+
+    def _aux_humidity(self, aux: DiagnosticState):
+        if self.humidity_key is None:
+            return None
+        return self._tracer_or_zero(aux.tracers, self.humidity_key, aux.temperature_variation)
+
+    def curl_and_div_tendencies(self, aux_state: DiagnosticState) -> tuple:
+        """(dζ/dt, dδ/dt) of the flux (ζ+f) k×v + σ̇ ∂v/∂σ + R T' ∇ln p_s (moist-weighted)."""
+        u, v = aux_state.cos_lat_u
+        sec2, f, _, _, inv_dc = self._nodal_consts(u)
+        adj = torch.ones_like(aux_state.temperature_variation)
+        q = self._aux_humidity(aux_state)
+        if q is not None:
+            adj = 1.0 + (self.column_constants.rv_ratio - 1.0) * q
+            for k in self.cloud_keys or ():
+                adj = adj - self._tracer_or_zero(aux_state.tracers, k, q)
+        rt = self.R * aux_state.temperature_variation * adj
+        gx, gy = aux_state.cos_lat_grad_log_sp
+        tv = aux_state.vorticity + f
+        au = av = torch.zeros_like(u)
+        if self.include_vertical_advection and aux_state.sigma_dot_full.shape[-3] > 0:
+            au = -_vadv(aux_state.sigma_dot_full, u, inv_dc)
+            av = -_vadv(aux_state.sigma_dot_full, v, inv_dc)
+        fu = self.grid.to_modal(-v * tv * sec2 + (au + rt * gx) * sec2)
+        fv = self.grid.to_modal(u * tv * sec2 + (av + rt * gy) * sec2)
+        return -self.grid.curl_cos_lat((fu, fv), clip=False), -self.grid.div_cos_lat((fu, fv), clip=False)
+
+    def kinetic_energy_tendency(self, aux_state: DiagnosticState) -> torch.Tensor:
+        """-∇²(½|v|²), modal."""
+        u, v = aux_state.cos_lat_u
+        sec2 = self._nodal_consts(u)[0]
+        return -self.grid.laplacian(self.grid.to_modal(0.5 * (u * u + v * v) * sec2))
+
+    def horizontal_scalar_advection(self, scalar_nodal: torch.Tensor, aux_state: DiagnosticState) -> tuple:
+        """(nodal s δ, modal -∇·(v s)): the two parts of -v·∇s = s δ - ∇·(v s)."""
+        u, v = aux_state.cos_lat_u
+        sec2 = self._nodal_consts(u)[0]
+        fu = self.grid.to_modal(u * scalar_nodal * sec2)
+        fv = self.grid.to_modal(v * scalar_nodal * sec2)
+        return scalar_nodal * aux_state.divergence, -self.grid.div_cos_lat((fu, fv), clip=False)
+
+    def nodal_temperature_vertical_tendency(self, aux_state: DiagnosticState) -> torch.Tensor:
+        """Vertical advection of T' by the full σ̇ and of the reference profile by the explicit σ̇."""
+        temp = aux_state.temperature_variation
+        if not self.include_vertical_advection:
+            return torch.zeros_like(temp)
+        _, _, _, t_ref, inv_dc = self._nodal_consts(temp)
+        return (_vadv(aux_state.sigma_dot_full, temp, inv_dc)
+                + _vadv(aux_state.sigma_dot_explicit, t_ref.expand_as(temp), inv_dc))
+
+    def nodal_temperature_adiabatic_tendency(self, aux_state: DiagnosticState) -> torch.Tensor:
+        """κ T ω/p (moist-weighted anomaly part when humidity is carried)."""
+        temp = aux_state.temperature_variation
+        dsig = self._nodal_consts(temp)[2]
+        ugl = aux_state.u_dot_grad_log_sp
+        f_exp = _prefix(ugl * dsig)
+        f_full = _prefix((aux_state.divergence + ugl) * dsig)
+        return _adiabatic_heating(temp, self._aux_humidity(aux_state), ugl, f_exp, f_full, self.column_constants)
+
+    def nodal_log_pressure_tendency(self, aux_state: DiagnosticState) -> torch.Tensor:
+        """-Σ_k (v·∇ln p_s) Δσ_k (the divergence part is implicit)."""
+        dsig = self._nodal_consts(aux_state.u_dot_grad_log_sp)[2]
+        return -(aux_state.u_dot_grad_log_sp * dsig).sum(dim=-3, keepdim=True)
+
+    def _humidity_gradients(self, state: State, like: torch.Tensor):
+        q_m = self._tracer_or_zero(state.tracers, self.humidity_key, state.temperature_variation)
+        qx, qy = self.grid.cos_lat_grad(q_m, clip=False)
+        return self.grid.to_nodal(qx).to(like.dtype), self.grid.to_nodal(qy).to(like.dtype)
+
+    def divergence_tendency_due_to_humidity(self, state: State, aux_state: DiagnosticState) -> torch.Tensor:
+        """Virtual-temperature corrections of the pressure-gradient force and the geopotential
+        in the divergence equation (zero for a dry model)."""
+        q = self._aux_humidity(aux_state)
+        if q is None:
+            return torch.zeros_like(state.divergence)
+        sec2, _, _, t_ref, _ = self._nodal_consts(q)
+        r_diff = self.R * (self.column_constants.rv_ratio - 1.0)
+        qx, qy = self._humidity_gradients(state, q)
+        gx, gy = aux_state.cos_lat_grad_log_sp
+        lap = self.grid.to_nodal(self.grid.laplacian(state.log_surface_pressure)).to(q.dtype)
+        hum_div = r_diff * t_ref * sec2 * (qx * gx + qy * gy) + q * lap * t_ref * r_diff
+        tdiff = q * (aux_state.temperature_variation + t_ref) * (self.column_constants.rv_ratio - 1.0)
+        geo = get_geopotential_diff_sigma(self.grid.to_modal(tdiff), self.vertical, self.R)
+        return -self.grid.laplacian(geo) - self.grid.to_modal(hum_div)
+
+    def vorticity_tendency_due_to_humidity(self, state: State, aux_state: DiagnosticState) -> torch.Tensor:
+        """Curl of the moist pressure-gradient correction (zero for a dry model)."""
+        q = self._aux_humidity(aux_state)
+        if q is None:
+            return torch.zeros_like(state.vorticity)
+        sec2, _, _, t_ref, _ = self._nodal_consts(q)
+        r_diff = self.R * (self.column_constants.rv_ratio - 1.0)
+        qx, qy = self._humidity_gradients(state, q)
+        gx, gy = aux_state.cos_lat_grad_log_sp
+        return self.grid.to_modal(r_diff * t_ref * sec2 * (gx * qy - gy * qx))
 
     # ── implicit terms ────────────────────────────────────────────────
     def implicit_terms(self, state: State) -> State:
