@@ -232,3 +232,23 @@ def test_physics_memory_check_needs_every_core_field_and_tracer():
     assert ok(core, _S({})) and ok(object(), _S({}))
     assert not ok(core, _S({"q": 0})) and not ok({**core, "tracers": [0]}, _S({"q": 0}))
     assert ok({**core, "tracers": {"q": 0, "c": 0}}, _S({"q": 0}))
+
+
+def test_sda_trainer_backward_precision_hooks():
+    from tornado_gcm_b200.precision.sda import SDAConfig
+    from tornado_gcm_b200.training.sda_trainer import SDATrainer
+
+    gcm, _, _ = _small()
+    cfg = SDAConfig()
+    cfg.training.rollout_steps = 1
+    cfg.training.batch_size = 1
+    tr = SDATrainer(gcm, cfg, total_steps=1)
+    tr.configure_backward_precision(("decoder",))
+    n = len(tr._backward_hooks)
+    assert n > 0
+    hist = tr.fit(log_every=1)
+    assert np.isfinite(hist[-1]["loss"])
+    tr.configure_backward_precision(("decoder",))      # re-configuring replaces, not stacks
+    assert len(tr._backward_hooks) == n
+    tr.remove_backward_hooks()
+    assert not tr._backward_hooks

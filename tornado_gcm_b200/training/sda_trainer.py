@@ -13,7 +13,7 @@ from __future__ import annotations
 
 import logging
 import pathlib
-from typing import Callable, Iterator, Optional
+from typing import Callable, Iterator, Optional, Sequence
 
 import torch
 import torch.nn as nn
@@ -44,6 +44,7 @@ class SDATrainer:
         self._rollout_steps = int(tr.rollout_steps)
         self._data = data
         self.history: list[dict] = []
+        self._backward_hooks: list = []
 
     def _make_trainer(self) -> GCMTrainer:
         tr = self.sda_config.training
@@ -145,6 +146,35 @@ class SDATrainer:
 
     def get_ema_state_dict(self) -> dict:
         return self._trainer.ema.state_dict()
+
+    # ── per-layer backward precision (reference ``training/sda_trainer.py:184-226``) ──
+    def configure_backward_precision(self, final_layer_keywords: Sequence[str] = ("output_layer", "head", "final"),
+                                     high_precision_dtype: torch.dtype = torch.float32) -> None:
+        """Hand the gradients that the final network layers pass back to their inputs over in
+        ``high_precision_dtype``: a full backward hook on every module whose name contains one of
+        the keywords.  Autograd delivers each gradient in its input's dtype, so the widening
+        reaches inputs held in that dtype (fp32 activations or master copies); BF16 inputs keep
+        BF16 gradients.  A captured training step picks the hooks up at its next capture."""
+        self.remove_backward_hooks()
+        words = tuple(k.lower() for k in final_layer_keywords)
+
+        def widen(module, grad_input, grad_output):
+            return tuple(g.to(high_precision_dtype) if isinstance(g, torch.Tensor) and g.is_floating_point() else g
+                         for g in grad_input)
+
+        for name, module in self.gcm.named_modules():
+            if name and any(w in name.lower() for w in words):
+                self._backward_hooks.append(module.register_full_backward_hook(widen))
+        if self._backward_hooks:
+            self._trainer.release_graph()
+
+    def remove_backward_hooks(self) -> None:
+        """Remove the hooks of :meth:`configure_backward_precision`."""
+        for h in self._backward_hooks:
+            h.remove()
+        if self._backward_hooks:
+            self._trainer.release_graph()
+        self._backward_hooks.clear()
 
     # ── checkpoints ──
     def save_checkpoint(self, path) -> None:

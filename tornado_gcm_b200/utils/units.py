@@ -285,9 +285,31 @@ class SimUnitsProtocol(Protocol):
     water_vapor_isobaric_heat_capacity: float
     kappa: float
 
+    @property
+    def R(self) -> float: ...
+
+    @property
+    def R_vapor(self) -> float: ...
+
+    @property
+    def g(self) -> float: ...
+
+    @property
+    def Cp(self) -> float: ...
+
+    @property
+    def Cp_vapor(self) -> float: ...
+
     def nondimensionalize(self, quantity: "Quantity") -> float: ...
 
+    def nondimensionalize_timedelta64(self, timedelta: np.timedelta64) -> float: ...
+
     def dimensionalize(self, value: float, unit: "Unit") -> "Quantity": ...
+
+    def dimensionalize_timedelta64(self, value: float) -> np.timedelta64: ...
+
+    @classmethod
+    def from_si(cls, **kwargs) -> "SimUnitsProtocol": ...
 
 
 @dataclasses.dataclass(frozen=True)
