@@ -22,6 +22,20 @@ def _free_port() -> int:
     return port
 
 
+def _free_port_pair() -> int:
+    """A port p with p and p + 1 both free (the recovery test re-forms its group on p + 1)."""
+    for _ in range(200):
+        p = _free_port()
+        try:
+            with socket.socket() as a, socket.socket() as b:
+                a.bind(("127.0.0.1", p))
+                b.bind(("127.0.0.1", p + 1))
+            return p
+        except OSError:
+            continue
+    raise RuntimeError("no pair of adjacent free ports")
+
+
 def _init(rank, world, port, timeout_s=30.0):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -146,7 +160,7 @@ def test_rank_failure_detected_and_survivors_resume(tmp_path):
     world = 3
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
+    port = _free_port_pair()
     procs = [ctx.Process(target=_worker_elastic, args=(r, world, port, str(tmp_path), q)) for r in range(world)]
     for p in procs:
         p.start()
