@@ -252,3 +252,21 @@ def test_sda_trainer_backward_precision_hooks():
     assert len(tr._backward_hooks) == n
     tr.remove_backward_hooks()
     assert not tr._backward_hooks
+
+
+def test_inference_and_vectorized_wrappers_follow_the_reference_contract():
+    from tornado_gcm_b200.models.api import InferenceModel, VectorizedModel
+
+    gcm, data, norm = _small()
+    gcm.eval()
+    m = gcm.model
+    forc = data.forcings(1)
+    with torch.no_grad():
+        s0 = gcm.encoder(norm(data.sample(1, 0)), forc)
+        inf = InferenceModel(m, post_process_fn=lambda s: s.vorticity.norm())
+        traj = inf(s0, 2, 1, forcings=forc)
+        assert len(traj) == 2 and all(torch.isfinite(t) for t in traj)
+        # assimilation without an encoder on the bare model: a model-space state, blended
+        half = InferenceModel(m).assimilate(s0 * 2.0, state=s0, alpha=0.5)
+        torch.testing.assert_close(half.vorticity, s0.vorticity * 1.5)
+        assert VectorizedModel(m, use_vmap=False).mode == "loop" and VectorizedModel(m).mode == "batch"

@@ -507,31 +507,51 @@ class NeuralGCMModel(nn.Module):
 
 
 class InferenceModel(nn.Module):
-    """Encode → rollout → decode wrapper (reference ``model/api.py:1005-1133``)."""
+    """Assimilate → rollout → observe wrapper (reference ``model/api.py:1005-1133``).
 
-    def __init__(self, model: NeuralGCMModel):
+    ``forward`` rolls a model-space state (or :class:`ModelState`) forward and returns
+    the trajectory through ``post_process_fn``; :meth:`assimilate` maps raw inputs into
+    model space (optionally blended into an existing state); :meth:`observe` decodes.
+    """
+
+    def __init__(self, model: NeuralGCMModel, post_process_fn: Callable | None = None):
         super().__init__()
         self.model = model
+        self.post_process_fn = post_process_fn
 
-    def assimilate(self, inputs, forcings=None):
-        return self.model.encode(inputs, forcings)
+    def assimilate(self, inputs, forcings=None, state: State | None = None, alpha: float = 1.0,
+                   return_model_state: bool = False):
+        """Encode ``inputs`` (or take them as a model-space :class:`State` when the model has no
+        encoder); with ``state``, return ``(1 - alpha) state + alpha encoded``."""
+        if self.model.encoder is not None:
+            encoded = self.model.encode(inputs, forcings)
+        elif isinstance(inputs, State):
+            encoded = inputs
+        else:
+            raise ValueError("the model has no encoder: pass a model-space State as inputs")
+        out = encoded if (state is None or alpha >= 1.0) else state * (1.0 - alpha) + encoded * alpha
+        return self.model.initialize_model_state(out) if return_model_state else out
 
     def observe(self, state, forcings=None):
-        return self.model.decode(state, forcings)
+        """Decoded fields of ``state``; the state itself when the model has no decoder."""
+        return self.model.decode(state, forcings) if self.model.decoder is not None else state
 
     @torch.no_grad()
-    def forward(self, inputs, outer_steps: int, inner_steps: int | None = None, forcings=None,
-                decode: bool = True):
-        state = self.assimilate(inputs, forcings) if self.model.encoder is not None else inputs
-        post = (lambda s: self.observe(s, forcings)) if (decode and self.model.decoder is not None) else None
-        return self.model.forward(state, outer_steps, inner_steps, forcings=forcings, post_process_fn=post)
+    def forward(self, initial_state, outer_steps: int, inner_steps: int | None = None, forcings=None) -> list:
+        self.model.eval()
+        _, traj = self.model.forward(initial_state, outer_steps, inner_steps, forcings=forcings,
+                                     post_process_fn=self.post_process_fn)
+        return traj
 
 
 class VectorizedModel(nn.Module):
     """Ensemble wrapper: members as a leading batch dimension (or a loop)."""
 
-    def __init__(self, model: NeuralGCMModel, mode: str = "batch"):
+    def __init__(self, model: NeuralGCMModel, mode: str | None = None, use_vmap: bool = True):
+        """``mode``: ``batch`` (members as the leading dimension of every kernel) or ``loop``
+        (one member at a time); without it ``use_vmap`` (the reference's switch) picks batch."""
         super().__init__()
+        mode = mode if mode is not None else ("batch" if use_vmap else "loop")
         if mode not in ("batch", "loop", "vmap"):
             raise ValueError(f"unknown mode {mode}")
         self.model = model
@@ -548,10 +568,10 @@ class VectorizedModel(nn.Module):
                         None if states.sim_time is None else states.sim_time + self.model.config.dt)
         return stacked
 
-    def forward(self, states: State, outer_steps: int, inner_steps: int | None = None, forcings=None,
+    def forward(self, initial_states: State, outer_steps: int, inner_steps: int | None = None, forcings=None,
                 post_process_fn=None):
         inner_steps = self.model.config.inner_steps if inner_steps is None else inner_steps
-        cur, traj = states, []
+        cur, traj = initial_states, []
         for _ in range(outer_steps):
             for _ in range(inner_steps):
                 cur = self.step(cur, forcings)
