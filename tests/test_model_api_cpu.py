@@ -270,3 +270,37 @@ def test_inference_and_vectorized_wrappers_follow_the_reference_contract():
         half = InferenceModel(m).assimilate(s0 * 2.0, state=s0, alpha=0.5)
         torch.testing.assert_close(half.vorticity, s0.vorticity * 1.5)
         assert VectorizedModel(m, use_vmap=False).mode == "loop" and VectorizedModel(m).mode == "batch"
+
+
+def test_atmosphere_and_pressure_level_facades():
+    import numpy as np
+
+    from tornado_gcm_b200.core import coordinate_systems as cs, sigma_coordinates as sc, spherical_harmonic as sh
+    from tornado_gcm_b200.core import primitive_equations_states as pes
+    from tornado_gcm_b200.model.atmosphere import AtmosphereConfig, AtmosphericModel
+    from tornado_gcm_b200.model.legacy import SHORT_TO_LONG, PressureLevelModel
+    from tornado_gcm_b200.utils.units import SimUnits
+
+    # dycore-only facade: two outer steps from an isothermal state at rest stay at rest
+    coords = cs.CoordinateSystem(sh.Grid.T21(), sc.SigmaCoordinates.equidistant(4))
+    units = SimUnits.from_si()
+    cfg = AtmosphereConfig(coords=coords, physics_specs=units, dt=0.01, dycore_substeps=1,
+                           reference_temperature=np.full(4, 288.0), orography=torch.zeros(coords.horizontal.modal_shape))
+    atm = AtmosphericModel(cfg)
+    init_fn, _ = pes.isothermal_rest_atmosphere(coords, units, tref=288.0)
+    s0 = init_fn()
+    s0.tracers = {"specific_humidity": torch.zeros_like(s0.temperature_variation)}
+    final, traj = atm(s0, 2, forcings={})
+    assert len(traj) == 2 and torch.isfinite(final.vorticity).all()
+    half = atm.assimilate(None, state=s0, alpha=1.0) if atm.encoder is not None else s0
+    assert half is s0
+
+    # pressure-level wrapper on the hybrid model, with the reference's keyword names
+    gcm, data, _ = _small()
+    gcm.eval()
+    plm = PressureLevelModel(atmosphere_model=gcm)
+    raw = {SHORT_TO_LONG.get(k, k): v for k, v in data.sample(1, 0).items()}
+    with torch.no_grad():
+        out = plm.predict(raw, forcings=data.forcings(1), outer_steps=1)
+    assert len(out) == 1 and set(out[0]) <= set(plm.output_variables) and out[0]
+    assert all(torch.isfinite(v).all() for v in out[0].values())

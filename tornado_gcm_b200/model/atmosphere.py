@@ -79,11 +79,12 @@ class AtmosphericModel(nn.Module):
     def core(self) -> NeuralGCMModel:
         return self._core
 
-    def encode(self, inputs, forcings=None):
-        return self._core.encode(inputs, forcings)
+    def encode(self, inputs, forcing=None, forcings=None):
+        """``forcing`` is the reference's keyword; ``forcings`` is accepted as well."""
+        return self._core.encode(inputs, forcing if forcing is not None else forcings)
 
-    def decode(self, state, forcings=None):
-        return self._core.decode(state, forcings)
+    def decode(self, state, forcing=None, forcings=None):
+        return self._core.decode(state, forcing if forcing is not None else forcings)
 
     def step(self, state, forcings=None):
         return self._core.step(state, forcings)
@@ -95,11 +96,14 @@ class AtmosphericModel(nn.Module):
         return self._core.initialize_model_state(state, **kwargs)
 
     def forward(self, initial_state, outer_steps: int, inner_steps: Optional[int] = None, forcings=None,
-                post_process_fn=None):
-        return self._core(initial_state, outer_steps, inner_steps, forcings=forcings, post_process_fn=post_process_fn)
+                post_process_fn=None, checkpoint_outer_steps: bool = False):
+        return self._core(initial_state, outer_steps, inner_steps, forcings=forcings, post_process_fn=post_process_fn,
+                          checkpoint_outer_steps=checkpoint_outer_steps)
 
-    def assimilate(self, inputs, forcings=None):
-        return self.encode(inputs, forcings)
+    def assimilate(self, inputs, forcings=None, state=None, alpha: float = 1.0):
+        """Encoded ``inputs``; with ``state``, blended as ``(1 - alpha) state + alpha encoded``."""
+        encoded = self.encode(inputs, forcings=forcings)
+        return encoded if (state is None or alpha >= 1.0) else state * (1.0 - alpha) + encoded * alpha
 
-    def observe(self, state, forcings=None):
-        return self.decode(state, forcings)
+    def observe(self, state, forcing=None, forcings=None):
+        return self.decode(state, forcing if forcing is not None else forcings)

@@ -35,8 +35,13 @@ class PressureLevelConfig:
 class PressureLevelModel(nn.Module):
     """``gcm`` is a :class:`~tornado_gcm_b200.models.builders.HybridGCM`."""
 
-    def __init__(self, gcm: nn.Module, config: Optional[PressureLevelConfig] = None):
+    def __init__(self, gcm: Optional[nn.Module] = None, config: Optional[PressureLevelConfig] = None,
+                 atmosphere_model: Optional[nn.Module] = None):
+        """``atmosphere_model`` is the reference's name for the wrapped model."""
         super().__init__()
+        gcm = gcm if gcm is not None else atmosphere_model
+        if gcm is None:
+            raise ValueError("PressureLevelModel needs the model to wrap")
         self.gcm = gcm
         self.config = config or PressureLevelConfig()
 
@@ -76,7 +81,10 @@ class PressureLevelModel(nn.Module):
         return state
 
     @torch.no_grad()
-    def predict(self, inputs: dict, forcings: Optional[dict] = None, steps: int = 1) -> list:
+    def predict(self, inputs: dict, forcings: Optional[dict] = None, steps: int = 1,
+                outer_steps: Optional[int] = None) -> list:
+        """Decoded outputs after each of ``steps`` (the reference: ``outer_steps``) 6-h steps."""
+        steps = outer_steps if outer_steps is not None else steps
         state = self.encode(inputs, forcings)
         out = []
         for _ in range(steps):
