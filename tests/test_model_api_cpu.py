@@ -304,3 +304,21 @@ def test_atmosphere_and_pressure_level_facades():
         out = plm.predict(raw, forcings=data.forcings(1), outer_steps=1)
     assert len(out) == 1 and set(out[0]) <= set(plm.output_variables) and out[0]
     assert all(torch.isfinite(v).all() for v in out[0].values())
+
+
+def test_host_offload_rollout_gradients_match_plain_rollout():
+    from tornado_gcm_b200.training.trainer import HostOffloadCheckpoint
+
+    w = torch.nn.Parameter(torch.tensor([0.9, 1.1]))
+    step = lambda s: torch.tanh(s * w) + 0.1  # noqa: E731
+    x0 = torch.tensor([0.3, -0.2])
+    final, traj = HostOffloadCheckpoint(max_offloaded=3).rollout(step, x0, 6, segment_length=2)
+    assert len(traj) == 6
+    (g1,) = torch.autograd.grad(sum(t.sum() for t in traj), [w])
+    s, ref = x0, []
+    for _ in range(6):
+        s = step(s)
+        ref.append(s)
+    (g2,) = torch.autograd.grad(sum(t.sum() for t in ref), [w])
+    torch.testing.assert_close(g1, g2)
+    torch.testing.assert_close(final, s)

@@ -218,15 +218,15 @@ def shard_tensor_from_local(local_tensor: torch.Tensor, spec: DTensorShardingSpe
     return DTensor.from_local(local_tensor, device_mesh=mesh, placements=spec.placements, run_check=False, **kw)
 
 
-def gather_tensor(t):
+def gather_tensor(dtensor):
     """Full tensor of a DTensor (all-gather when sharded); plain tensors pass through."""
-    return t.full_tensor() if _is_dtensor(t) else t
+    return dtensor.full_tensor() if _is_dtensor(dtensor) else dtensor
 
 
-def redistribute_tensor(t, target_spec: DTensorShardingSpec, mesh=None):
-    if not _is_dtensor(t):
-        return t
-    return t.redistribute(device_mesh=mesh or t.device_mesh, placements=target_spec.placements)
+def redistribute_tensor(dtensor, target_spec: DTensorShardingSpec, mesh=None):
+    if not _is_dtensor(dtensor):
+        return dtensor
+    return dtensor.redistribute(device_mesh=mesh or dtensor.device_mesh, placements=target_spec.placements)
 
 
 # ─────────────────────── state dicts and states ─────────────────────
@@ -346,9 +346,9 @@ class SpectralShardingContext:
     def _replicated(self):
         return DTensorShardingSpec.replicate(self.mesh.ndim)
 
-    def to_modal(self, grid, nodal):
+    def to_modal(self, grid, nodal_dt):
         """Nodal (DTensor or local) → modal DTensor (level-sharded or replicated)."""
-        local = nodal.to_local() if _is_dtensor(nodal) else nodal
+        local = nodal_dt.to_local() if _is_dtensor(nodal_dt) else nodal_dt
         if self._dim is None:
             return grid.to_modal(local)
         if self._dim == 0:
@@ -356,17 +356,17 @@ class SpectralShardingContext:
         if self._dim == local.ndim - 1:     # latitude: partial sums + all-reduce
             modal = self._lat_sht(grid).to_modal(local)
         else:                               # longitude: gather the rows first
-            modal = grid.to_modal(gather_tensor(nodal))
+            modal = grid.to_modal(gather_tensor(nodal_dt))
         return shard_tensor_from_local(modal, self._replicated(), self.mesh)
 
-    def to_nodal(self, grid, modal):
+    def to_nodal(self, grid, modal_dt):
         """Modal → nodal DTensor with this context's spec."""
         if self._dim is None:
-            return grid.to_nodal(modal.to_local() if _is_dtensor(modal) else modal)
+            return grid.to_nodal(modal_dt.to_local() if _is_dtensor(modal_dt) else modal_dt)
         if self._dim == 0:
-            local = modal.to_local() if _is_dtensor(modal) else modal
+            local = modal_dt.to_local() if _is_dtensor(modal_dt) else modal_dt
             return shard_tensor_from_local(grid.to_nodal(local), self.spec, self.mesh)
-        full = gather_tensor(modal)
+        full = gather_tensor(modal_dt)
         sh = grid.spherical_harmonics
         shape = tuple(full.shape[:-2]) + (sh.longitude_nodes, sh.latitude_nodes)
         if self._dim == full.ndim - 1:      # each rank evaluates its own latitude rows

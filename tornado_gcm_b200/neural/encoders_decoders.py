@@ -55,26 +55,26 @@ class WeatherbenchToPrimitiveEncoder(nn.Module):
         else:
             self._orography = None
 
-    def weatherbench_to_primitive(self, wb: Dict[str, torch.Tensor]) -> pe.State:
-        """``wb``: ``u_component_of_wind``, ``v_component_of_wind``, ``temperature``,
+    def weatherbench_to_primitive(self, wb_dict: Dict[str, torch.Tensor]) -> pe.State:
+        """``wb_dict``: ``u_component_of_wind``, ``v_component_of_wind``, ``temperature``,
         ``geopotential`` (``(n_pressure, lon, lat)``), optional ``specific_humidity``
         and other tracers on the same levels, optional ``geopotential_at_surface``."""
         grid, vertical = self.coords.horizontal, self.coords.vertical
         g = self.physics_specs.g
-        t = wb["temperature"]
-        geo = wb["geopotential"]
-        if "geopotential_at_surface" in wb:
-            zs = wb["geopotential_at_surface"] / g
+        t = wb_dict["temperature"]
+        geo = wb_dict["geopotential"]
+        if "geopotential_at_surface" in wb_dict:
+            zs = wb_dict["geopotential_at_surface"] / g
         elif self._orography is not None:
             zs = self._orography.to(t.device, t.dtype)
         else:
             zs = torch.zeros_like(geo[..., -1:, :, :])
         ps = vi.get_surface_pressure(self.input_pressure, geo, zs, g)             # (…, 1, lon, lat)
-        names = {"u": wb["u_component_of_wind"], "v": wb["v_component_of_wind"], "t": t}
-        tracer_keys = [k for k, v in wb.items() if k.startswith("specific_") and torch.is_tensor(v)
+        names = {"u": wb_dict["u_component_of_wind"], "v": wb_dict["v_component_of_wind"], "t": t}
+        tracer_keys = [k for k, v in wb_dict.items() if k.startswith("specific_") and torch.is_tensor(v)
                        and v.shape[-3:] == t.shape[-3:]]
         for k in tracer_keys:
-            names[k] = wb[k]
+            names[k] = wb_dict[k]
         on_sigma = vi.interp_pressure_to_sigma(names, self.input_pressure, vertical, ps)
         cos = torch.as_tensor(grid.cos_lat, dtype=t.dtype, device=t.device)
         t_ref = torch.as_tensor(self.ref_temps, dtype=t.dtype, device=t.device).reshape(-1, 1, 1)
@@ -85,8 +85,8 @@ class WeatherbenchToPrimitiveEncoder(nn.Module):
         div = grid.div_cos_lat((modal["u"], modal["v"]))
         return pe.State(vor, div, modal["t"], modal["lnps"], {k: modal[k] for k in tracer_keys})
 
-    def forward(self, wb: Dict[str, torch.Tensor]) -> pe.State:
-        return self.weatherbench_to_primitive(wb)
+    def forward(self, wb_dict: Dict[str, torch.Tensor]) -> pe.State:
+        return self.weatherbench_to_primitive(wb_dict)
 
 
 class LearnedWeatherbenchToPrimitiveEncoder(WeatherbenchToPrimitiveEncoder):
@@ -103,8 +103,8 @@ class LearnedWeatherbenchToPrimitiveEncoder(WeatherbenchToPrimitiveEncoder):
         self.correction_transform = correction_transform
         self.prediction_mask = prediction_mask or {}
 
-    def forward(self, wb: Dict[str, torch.Tensor], forcing: Optional[Dict[str, torch.Tensor]] = None) -> pe.State:
-        st = self.weatherbench_to_primitive(wb)
+    def forward(self, wb_dict: Dict[str, torch.Tensor], forcing: Optional[Dict[str, torch.Tensor]] = None) -> pe.State:
+        st = self.weatherbench_to_primitive(wb_dict)
         corr = self.correction_net(self.features_fn(_state_dict(st), forcing=forcing))
         if self.correction_transform is not None:
             corr = self.correction_transform(corr)

@@ -60,17 +60,17 @@ def get_reference_temperature(model_levels, p_surf_ref: float = P_SURF_REF) -> n
     return np.interp(np.log(p), np.log(REF_PRESSURE), REF_TEMPERATURE)
 
 
-def temperature_linearize(state: Dict, ref_temperatures, abs_key: str = TEMPERATURE_KEY,
+def temperature_linearize(state_dict: Dict, ref_temperatures, abs_key: str = TEMPERATURE_KEY,
                           del_key: str = TEMPERATURE_VAR_KEY) -> Dict:
-    out = dict(state)
+    out = dict(state_dict)
     if abs_key in out:
         out[del_key] = field_utils.extract_1d_field_perturbation(out.pop(abs_key), ref_temperatures, axis=-3)
     return out
 
 
-def temperature_delinearize(state: Dict, ref_temperatures, abs_key: str = TEMPERATURE_KEY,
+def temperature_delinearize(state_dict: Dict, ref_temperatures, abs_key: str = TEMPERATURE_KEY,
                             del_key: str = TEMPERATURE_VAR_KEY) -> Dict:
-    out = dict(state)
+    out = dict(state_dict)
     if del_key in out:
         out[abs_key] = field_utils.reconstruct_1d_field_from_ref_values(out.pop(del_key), ref_temperatures, axis=-3)
     return out

@@ -36,10 +36,10 @@ class SparseSpectralTransform:
             self._dev[key] = d
         return d
 
-    def inverse_legendre(self, c: MixedPrecisionSparse) -> torch.Tensor:
-        lo, hi = self._on(c.device)
-        y = torch.einsum("mjl,...ml->...mj", lo, c.low_block().double())
-        y = y + torch.einsum("mjl,...ml->...mj", hi, c.high_block().float()).double()
+    def inverse_legendre(self, sparse_coeff: MixedPrecisionSparse) -> torch.Tensor:
+        lo, hi = self._on(sparse_coeff.device)
+        y = torch.einsum("mjl,...ml->...mj", lo, sparse_coeff.low_block().double())
+        y = y + torch.einsum("mjl,...ml->...mj", hi, sparse_coeff.high_block().float()).double()
         return y.float()
 
     def forward_legendre(self, x: torch.Tensor) -> MixedPrecisionSparse:
@@ -48,8 +48,8 @@ class SparseSpectralTransform:
         high = torch.einsum("mjl,...mj->...ml", hi, x.float())
         return MixedPrecisionSparse.from_blocks(low, high, self.config.high_order_dtype)
 
-    def inverse_transform(self, c: MixedPrecisionSparse) -> torch.Tensor:
-        mid = self.inverse_legendre(c)
+    def inverse_transform(self, sparse_coeff: MixedPrecisionSparse) -> torch.Tensor:
+        mid = self.inverse_legendre(sparse_coeff)
         if self.fourier_basis is None:
             return mid
         return torch.einsum("im,...mj->...ij", self.fourier_basis.to(mid.device, mid.dtype), mid)

@@ -590,12 +590,23 @@ class HostOffloadCheckpoint:
             return host.to(dev, non_blocking=True)
         return p
 
-    def rollout(self, step_fn: Callable, state, total_steps: int, segment: int = 8):
-        traj = []
-        with torch.autograd.graph.saved_tensors_hooks(self._pack, self._unpack):
-            for _ in range(total_steps):
+    def rollout(self, step_fn: Callable, initial_state, total_steps: int, segment_length: int = 4):
+        """``(final state, trajectory)`` of ``total_steps`` calls of ``step_fn``.
+
+        The tensors that autograd saves during the first steps go to pinned host memory
+        and come back when backward reaches them; the last ``segment_length`` steps, which
+        backward needs first, keep theirs on the device.  At most ``max_offloaded`` steps
+        are offloaded (the following ones stay on the device)."""
+        self._offloaded.clear()
+        n_off = min(max(total_steps - segment_length, 0), self.max_offloaded)
+        traj, state = [], initial_state
+        for i in range(total_steps):
+            if i < n_off:
+                with torch.autograd.graph.saved_tensors_hooks(self._pack, self._unpack):
+                    state = step_fn(state)
+            else:
                 state = step_fn(state)
-                traj.append(state)
+            traj.append(state)
         return state, traj
 
     def clear(self):

@@ -351,8 +351,8 @@ class SimUnits:
     def dimensionalize(self, value, unit: Unit) -> Quantity:
         return self.scale.dimensionalize(value, unit)
 
-    def nondimensionalize_timedelta64(self, td: np.timedelta64) -> float:
-        seconds = td / np.timedelta64(1, "s")
+    def nondimensionalize_timedelta64(self, timedelta: np.timedelta64) -> float:
+        seconds = timedelta / np.timedelta64(1, "s")
         return self.scale.nondimensionalize(float(seconds) * units.s)
 
     def dimensionalize_timedelta64(self, value: float) -> np.timedelta64:
