@@ -364,3 +364,24 @@ def test_reference_diagnostics_api():
     out = d.CombinedStepDiagnostics()(ModelState(state=traj[2], memory=traj[1]))
     assert set(out) == {"P_minus_E_rate", "heating_rate", "total_energy", "dry_air_mass"}
     assert float(out["P_minus_E_rate"]) == -1.0
+
+
+def test_conv_layers_accept_the_reference_vocabulary():
+    from tornado_gcm_b200.neural.standard_layers import CnnLevel, ConvLonLat
+    from tornado_gcm_b200.neural.towers import Conv2DTower, VerticalConvTower
+
+    torch.manual_seed(0)
+    t = VerticalConvTower(input_channels=3, output_channels=2, hidden_channels=[4, 4], kernel_size=3,
+                          checkpoint_tower=True)
+    x = torch.randn(3, 8, 5, 4, requires_grad=True)
+    y = t(x)
+    assert y.shape == (2, 8, 5, 4)
+    y.sum().backward()
+    assert x.grad is not None and all(p.grad is not None for p in t.parameters())
+    c2 = Conv2DTower(input_channels=3, output_channels=2, num_hidden_units=5, num_hidden_layers=3, use_bias=False)
+    assert len(c2.layers) == 4 and c2.layers[0].conv.bias is None
+    assert c2(torch.randn(3, 6, 4)).shape == (2, 6, 4)
+    assert ConvLonLat(input_channels=2, output_channels=3).conv.out_channels == 3
+    cnn = CnnLevel(2, 3, channels=[4], kernel_sizes=[3, 5], dilations=[1, 2])
+    assert cnn.layers[1].conv.kernel_size == (5,) and cnn.layers[1].conv.dilation == (2,)
+    assert cnn(torch.randn(7, 2, 16)).shape == (7, 3, 16)

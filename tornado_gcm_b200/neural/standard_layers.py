@@ -129,9 +129,10 @@ class ConvLevel(nn.Module):
     """1-D convolution along the level axis with 'same' padding."""
 
     def __init__(self, input_size: int, output_size: int, kernel_size: int = 3, use_bias: bool = True,
-                 padding: str = "same"):
+                 padding: str = "same", stride: int = 1, dilation: int = 1):
         super().__init__()
-        self.conv = nn.Conv1d(input_size, output_size, kernel_size, padding=padding, bias=use_bias)
+        self.conv = nn.Conv1d(input_size, output_size, kernel_size, stride=stride, padding=padding,
+                              dilation=dilation, bias=use_bias)
         lecun_normal_(self.conv.weight)
         if self.conv.bias is not None:
             nn.init.zeros_(self.conv.bias)
@@ -144,10 +145,19 @@ class CnnLevel(nn.Module):
     """Stack of ConvLevel layers with activations."""
 
     def __init__(self, input_size: int, output_size: int, *, channels: Sequence[int] = (), kernel_size: int = 3,
-                 activation: Callable = F.relu, activate_final: bool = False, use_bias: bool = True):
+                 activation: Callable = F.relu, activate_final: bool = False, use_bias: bool = True,
+                 kernel_sizes=None, strides=1, dilations=1):
+        """``kernel_sizes`` / ``strides`` / ``dilations``: one value for every layer or one per
+        layer (the reference's names; ``kernel_sizes`` overrides ``kernel_size``)."""
         super().__init__()
         sizes = (input_size,) + tuple(channels) + (output_size,)
-        self.layers = nn.ModuleList(ConvLevel(a, b, kernel_size, use_bias) for a, b in zip(sizes[:-1], sizes[1:]))
+        n = len(sizes) - 1
+        per = lambda v: list(v) if isinstance(v, (list, tuple)) else [v] * n  # noqa: E731
+        ks, st, dl = per(kernel_size if kernel_sizes is None else kernel_sizes), per(strides), per(dilations)
+        if not (len(ks) == len(st) == len(dl) == n):
+            raise ValueError(f"per-layer settings must have {n} entries")
+        self.layers = nn.ModuleList(ConvLevel(a, b, ks[i], use_bias, stride=st[i], dilation=dl[i])
+                                    for i, (a, b) in enumerate(zip(sizes[:-1], sizes[1:])))
         self.activation = activation
         self.activate_final = activate_final
 
@@ -211,9 +221,15 @@ class Sequential(nn.Module):
 class ConvLonLat(nn.Module):
     """2-D conv on (lon, lat): circular padding in lon, zero padding in lat."""
 
-    def __init__(self, input_size: int, output_size: int, kernel_size: tuple[int, int] = (3, 3),
-                 dilation: int = 1, use_bias: bool = True):
+    def __init__(self, input_size: int | None = None, output_size: int | None = None,
+                 kernel_size: tuple[int, int] = (3, 3), dilation: int = 1, use_bias: bool = True,
+                 input_channels: int | None = None, output_channels: int | None = None):
+        """``input_channels`` / ``output_channels`` are the reference's names for the sizes."""
         super().__init__()
+        input_size = input_size if input_size is not None else input_channels
+        output_size = output_size if output_size is not None else output_channels
+        if input_size is None or output_size is None:
+            raise ValueError("ConvLonLat needs input and output channel counts")
         self.kernel_size = tuple(kernel_size)
         self.dilation = dilation
         self.conv = nn.Conv2d(input_size, output_size, self.kernel_size, dilation=dilation, bias=use_bias)

@@ -80,16 +80,34 @@ class VerticalConvTower(nn.Module):
     Input ``(..., channels, levels, lon, lat)`` → ``(..., out_channels, levels, lon, lat)``.
     """
 
-    def __init__(self, input_size: int, output_size: int, *, channels: Sequence[int] = (64, 64, 64, 64),
-                 kernel_size: int = 5, activation: Callable = F.relu, activate_final: bool = False,
-                 use_bias: bool = True):
+    def __init__(self, input_size: int | None = None, output_size: int | None = None,
+                 channels: Sequence[int] = (64, 64, 64, 64), kernel_size: int = 5, activation: Callable = F.relu,
+                 activate_final: bool = False, use_bias: bool = True, *, input_channels: int | None = None,
+                 output_channels: int | None = None, hidden_channels: Sequence[int] | None = None,
+                 checkpoint_tower: bool = False):
+        """The reference's names are accepted: ``input_channels``, ``output_channels``,
+        ``hidden_channels``; ``checkpoint_tower`` recomputes the tower in backward instead of
+        keeping its activations."""
         super().__init__()
+        input_size = input_size if input_size is not None else input_channels
+        output_size = output_size if output_size is not None else output_channels
+        if input_size is None or output_size is None:
+            raise ValueError("VerticalConvTower needs input and output channel counts")
+        channels = tuple(hidden_channels) if hidden_channels is not None else tuple(channels)
+        self.checkpoint_tower = checkpoint_tower
         sizes = (input_size,) + tuple(channels) + (output_size,)
         self.layers = nn.ModuleList(ConvLevel(a, b, kernel_size, use_bias) for a, b in zip(sizes[:-1], sizes[1:]))
         self.activation = activation
         self.activate_final = activate_final
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.checkpoint_tower and self.training and torch.is_grad_enabled():
+            from torch.utils.checkpoint import checkpoint
+
+            return checkpoint(self._forward, x, use_reentrant=False)
+        return self._forward(x)
+
+    def _forward(self, x: torch.Tensor) -> torch.Tensor:
         if x.is_cuda:
             from tornado_gcm_b200.ops import levelconv
 
@@ -111,12 +129,22 @@ class VerticalConvTower(nn.Module):
 class Conv2DTower(nn.Module):
     """Stack of ConvLonLat layers on ``(..., channels, lon, lat)``."""
 
-    def __init__(self, input_size: int, output_size: int, *, channels: Sequence[int] = (32, 32),
-                 kernel_size: tuple[int, int] = (3, 3), activation: Callable = F.relu,
-                 activate_final: bool = False):
+    def __init__(self, input_size: int | None = None, output_size: int | None = None, *,
+                 channels: Sequence[int] | None = None, kernel_size: tuple[int, int] = (3, 3),
+                 activation: Callable = F.relu, activate_final: bool = False, use_bias: bool = True,
+                 input_channels: int | None = None, output_channels: int | None = None,
+                 num_hidden_units: int = 32, num_hidden_layers: int = 2):
+        """Hidden widths: ``channels``, else ``num_hidden_layers`` layers of ``num_hidden_units``
+        (the reference's parameters); ``input_channels`` / ``output_channels`` name the sizes."""
         super().__init__()
+        input_size = input_size if input_size is not None else input_channels
+        output_size = output_size if output_size is not None else output_channels
+        if input_size is None or output_size is None:
+            raise ValueError("Conv2DTower needs input and output channel counts")
+        channels = tuple(channels) if channels is not None else (num_hidden_units,) * num_hidden_layers
         sizes = (input_size,) + tuple(channels) + (output_size,)
-        self.layers = nn.ModuleList(ConvLonLat(a, b, kernel_size) for a, b in zip(sizes[:-1], sizes[1:]))
+        self.layers = nn.ModuleList(ConvLonLat(a, b, kernel_size, use_bias=use_bias)
+                                    for a, b in zip(sizes[:-1], sizes[1:]))
         self.activation = activation
         self.activate_final = activate_final
 
