@@ -322,3 +322,26 @@ def test_host_offload_rollout_gradients_match_plain_rollout():
     (g2,) = torch.autograd.grad(sum(t.sum() for t in ref), [w])
     torch.testing.assert_close(g1, g2)
     torch.testing.assert_close(final, s)
+
+
+def test_sda_trainer_reference_keywords():
+    from tornado_gcm_b200.precision.sda import SDAConfig
+    from tornado_gcm_b200.training.sda_trainer import SDATrainer
+
+    gcm, _, _ = _small()
+    cfg = SDAConfig()
+    cfg.training.rollout_steps = 1
+    cfg.training.batch_size = 1
+    opt = torch.optim.AdamW(gcm.parameters(), lr=3e-4, weight_decay=0.01)
+    calls = []
+
+    def loss_fn(predictions, targets):
+        calls.append(len(predictions))
+        return {"total": sum(((p["t"] - t["t"]) ** 2).mean() for p, t in zip(predictions, targets))}
+
+    tr = SDATrainer(gcm, cfg, optimizer=opt, loss_fn=loss_fn, max_grad_norm=0.5, ema_num_steps=99)
+    assert tr._trainer.optimizer.param_groups[0]["lr"] == 3e-4 and tr._trainer.max_grad_norm == 0.5
+    seen = []
+    hist = tr.fit(total_steps=2, callbacks=[lambda i, out: seen.append(i)], log_interval=1)
+    assert len(hist) == 2 and seen == [0, 1] and calls and np.isfinite(hist[-1]["loss"])
+    gcm.loss_fn = None

@@ -99,6 +99,9 @@ class HybridGCM(nn.Module):
         # a model sharded over W ranks (parallel.spectral_shard.shard_hybrid_gcm) sees 1/W of
         # every field: its local mean squared error counts 1/W towards the global loss
         self.loss_scale = 1.0
+        # optional trajectory loss ``fn(predictions=[...], targets=[...]) -> tensor or {"total": tensor}``
+        # in place of the per-field MSE (the reference trainer's ``loss_fn`` protocol)
+        self.loss_fn = None
         self.shard = None
 
     def normalize_forcings(self, forcings: dict) -> dict:
@@ -148,6 +151,9 @@ class HybridGCM(nn.Module):
 
     def loss(self, data0: dict, targets: list, forcings: dict) -> torch.Tensor:
         _, preds = self.rollout(data0, forcings, len(targets))
+        if self.loss_fn is not None:
+            out = self.loss_fn(predictions=preds, targets=list(targets))
+            return (out["total"] if isinstance(out, dict) else out) * self.loss_scale
         total = 0.0
         for pred, tgt in zip(preds, targets):
             total = total + sum(((pred[k] - tgt[k]) ** 2).mean() for k in DATA_FIELDS) / len(DATA_FIELDS)

@@ -27,9 +27,30 @@ logger = logging.getLogger(__name__)
 class SDATrainer:
     def __init__(self, model: nn.Module, sda_config: Optional[SDAConfig] = None, total_steps: Optional[int] = None,
                  batch_size: Optional[int] = None, data=None, graph: Optional[bool] = None,
-                 data_parallel: bool = False):
+                 data_parallel: bool = False, *, optimizer: Optional[torch.optim.Optimizer] = None,
+                 loss_fn: Optional[Callable] = None, max_grad_norm: Optional[float] = None,
+                 ema_num_steps: Optional[int] = None):
+        """The reference's keywords are accepted: ``optimizer`` supplies the AdamW
+        hyperparameters (learning rate, weight decay, betas, eps of its first parameter
+        group; the step itself runs on the fused AdamW of the captured training step),
+        ``loss_fn(predictions=..., targets=...)`` replaces the per-field MSE of the model,
+        ``max_grad_norm`` / ``ema_num_steps`` override the configuration."""
         self.sda_config = sda_config or SDAConfig()
         tr = self.sda_config.training
+        if optimizer is not None:
+            g = optimizer.param_groups[0]
+            tr.learning_rate = float(g.get("lr", tr.learning_rate))
+            tr.weight_decay = float(g.get("weight_decay", tr.weight_decay))
+            self._betas = tuple(g.get("betas", (0.9, 0.95)))
+            self._eps = float(g.get("eps", 1e-6))
+        else:
+            self._betas, self._eps = (0.9, 0.95), 1e-6
+        if max_grad_norm is not None:
+            tr.max_grad_norm = float(max_grad_norm)
+        if ema_num_steps is not None:
+            tr.ema_num_steps = int(ema_num_steps)
+        if loss_fn is not None:
+            model.loss_fn = loss_fn
         self.total_steps = int(total_steps if total_steps is not None else tr.total_steps)
         self.batch_size = int(batch_size if batch_size is not None else tr.batch_size)
         self.gcm = model
@@ -49,7 +70,8 @@ class SDATrainer:
     def _make_trainer(self) -> GCMTrainer:
         tr = self.sda_config.training
         return GCMTrainer(self.gcm, lr=tr.learning_rate, weight_decay=tr.weight_decay, max_grad_norm=tr.max_grad_norm,
-                          ema_num_steps=tr.ema_num_steps, graph=self._graph, data_parallel=self._data_parallel)
+                          ema_num_steps=tr.ema_num_steps, graph=self._graph, data_parallel=self._data_parallel,
+                          betas=self._betas, eps=self._eps)
 
     # ── properties of the reference API ──
     @property
@@ -105,11 +127,12 @@ class SDATrainer:
                 self.gcm.model.set_transform_precision(prec)
                 self._trainer.release_graph()
 
-    def train_step(self, batch=None) -> dict:
+    def train_step(self, batch=None, rollout_steps: Optional[int] = None) -> dict:
+        """One step; ``rollout_steps`` overrides the scheduler's rollout length for this step."""
         if batch is None:
             batch = next(self._it) if hasattr(self, "_it") else next(self._new_iter())
         x0, targets, forcings = batch
-        targets = list(targets)[: self._rollout_steps]
+        targets = list(targets)[: (self._rollout_steps if rollout_steps is None else int(rollout_steps))]
         loss = self._trainer.train_step(x0, targets, forcings)
         interval = max(int(self.sda_config.scheduler.check_interval), 1)
         if (self.step_count % interval) == 0:  # one host read per scheduler check, not per step
@@ -123,17 +146,27 @@ class SDATrainer:
         return self._it
 
     def fit(self, num_steps: Optional[int] = None, log_every: int = 100,
-            callback: Optional[Callable[[int, dict], None]] = None) -> list[dict]:
-        n = self.total_steps if num_steps is None else int(num_steps)
-        it = self._new_iter()
+            callback: Optional[Callable[[int, dict], None]] = None, *, data_iter=None,
+            total_steps: Optional[int] = None, callbacks: Optional[Sequence[Callable]] = None,
+            log_interval: Optional[int] = None) -> list[dict]:
+        """Train ``num_steps`` (the reference: ``total_steps``) steps on the configured data or on
+        ``data_iter``; ``callback`` / every entry of ``callbacks`` is called as ``fn(step, out)``."""
+        n = self.total_steps if (num_steps is None and total_steps is None) else int(
+            num_steps if num_steps is not None else total_steps)
+        log_every = log_interval if log_interval is not None else log_every
+        fns = ([callback] if callback is not None else []) + list(callbacks or [])
+        if data_iter is not None:
+            self._it = it = iter(data_iter)
+        else:
+            it = self._new_iter()
         for i in range(n):
             out = self.train_step(next(it))
             if (i + 1) % max(log_every, 1) == 0 or i == n - 1:
                 rec = {"step": self.step_count, "loss": float(out["loss"]), "rollout_steps": out["rollout_steps"]}
                 self.history.append(rec)
                 logger.info("step %d loss %.5g rollout %d", rec["step"], rec["loss"], rec["rollout_steps"])
-            if callback is not None:
-                callback(i, out)
+            for fn in fns:
+                fn(i, out)
         return self.history
 
     train = fit
