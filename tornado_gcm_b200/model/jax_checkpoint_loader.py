@@ -64,18 +64,23 @@ def _gelu_tanh(x: torch.Tensor) -> torch.Tensor:
 
 
 def build_epd_tower(input_size: int, output_size: int, latent_size: int = LATENT_SIZE, num_blocks: int = NUM_BLOCKS,
-                    process_hidden: int = 3, decode_hidden: int = 0) -> Epd:
-    """The checkpoint's EPD: encode = one biased linear, ``num_blocks`` residual
-    process MLPs of ``process_hidden + 1`` biased linears, decode = bias-free MLP
-    with ``decode_hidden`` hidden layers; GELU (tanh form) between layers."""
+                    process_hidden: int = 3, decode_hidden: int = 0, *, process_n_hidden: Optional[int] = None,
+                    decode_n_hidden: Optional[int] = None, encode_bias: bool = True,
+                    decode_bias: bool = False) -> Epd:
+    """The checkpoint's EPD: encode = one linear (biased by default), ``num_blocks`` residual
+    process MLPs of ``process_hidden + 1`` biased linears, decode = MLP (bias-free by
+    default) with ``decode_hidden`` hidden layers; GELU (tanh form) between layers.
+    ``process_n_hidden`` / ``decode_n_hidden`` are the reference's names of the two counts."""
+    process_hidden = process_hidden if process_n_hidden is None else process_n_hidden
+    decode_hidden = decode_hidden if decode_n_hidden is None else decode_n_hidden
     mlp = lambda i, o, hidden, bias: Mlp(i, o, intermediate_sizes=(latent_size,) * hidden, activation=_gelu_tanh,
                                          activate_final=False, use_bias=bias)
-    return Epd(mlp(input_size, latent_size, 0, True), mlp(latent_size, output_size, decode_hidden, False),
+    return Epd(mlp(input_size, latent_size, 0, encode_bias), mlp(latent_size, output_size, decode_hidden, decode_bias),
                [mlp(latent_size, latent_size, process_hidden, True) for _ in range(num_blocks)])
 
 
-def build_surface_epd(input_size: int) -> Epd:
-    return build_epd_tower(input_size, SURFACE_LATENT, latent_size=SURFACE_LATENT, num_blocks=1, decode_hidden=1)
+def build_surface_epd(input_size: int, output_size: int = SURFACE_LATENT) -> Epd:
+    return build_epd_tower(input_size, output_size, latent_size=SURFACE_LATENT, num_blocks=1, decode_hidden=1)
 
 
 def build_volume_conv_tower() -> VerticalConvTower:
@@ -224,8 +229,17 @@ def _convert(value: np.ndarray, kind: str, target: torch.Tensor) -> torch.Tensor
     return t.to(target.dtype)
 
 
-def load_jax_weights(module: nn.Module, jax_params: dict, strict: bool = False) -> dict:
-    """Copy mapped leaves into ``module``; returns a report of what was (not) loaded."""
+def load_jax_weights(model: nn.Module, checkpoint_path, strict: bool = False) -> dict:
+    """Copy mapped leaves into ``model``; returns a report of what was (not) loaded.
+
+    ``checkpoint_path``: a pickled Haiku checkpoint (read with :func:`read_jax_checkpoint`,
+    its ``params/`` leaves used) or an already flattened ``{path: array}`` dict."""
+    if isinstance(checkpoint_path, (str, Path)):
+        flat = read_jax_checkpoint(checkpoint_path)
+        jax_params = {k: v for k, v in flat.items() if k.startswith("params/")}
+    else:
+        jax_params = checkpoint_path
+    module = model
     mapping = build_weight_mapping(jax_params)
     sd = module.state_dict()
     loaded, skipped = [], []

@@ -90,21 +90,28 @@ def is_main_process() -> bool:
     return get_rank() == 0
 
 
-def setup_distributed(backend: Optional[str] = None, timeout_s: float = 600.0) -> tuple[int, int, int]:
-    """Initialise from torchrun env vars (RANK, WORLD_SIZE, LOCAL_RANK, MASTER_*)."""
+def setup_distributed(backend: Optional[str] = None, init_method: Optional[str] = None,
+                      world_size: Optional[int] = None, rank: Optional[int] = None,
+                      timeout_s: float = 600.0) -> tuple[int, int, int]:
+    """Initialise the default process group; returns ``(rank, world, local rank)``.
+
+    ``world_size`` / ``rank`` default to the launcher's WORLD_SIZE / RANK; ``init_method``
+    defaults to ``env://`` (MASTER_ADDR / MASTER_PORT, 127.0.0.1:29500 when unset)."""
     if is_distributed():
         return get_rank(), get_world_size(), get_local_rank()
-    world = int(os.environ.get("WORLD_SIZE", "1"))
+    world = int(world_size if world_size is not None else os.environ.get("WORLD_SIZE", "1"))
     if world <= 1:
         return 0, 1, 0
-    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-    os.environ.setdefault("MASTER_PORT", "29500")
+    rank = int(rank if rank is not None else os.environ.get("RANK", "0"))
+    if init_method is None or init_method.startswith("env://"):
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29500")
     if backend is None:
         backend = "nccl" if torch.cuda.is_available() else "gloo"
     local = get_local_rank()
     if backend == "nccl":
         torch.cuda.set_device(local)
-    dist.init_process_group(backend=backend, init_method="env://",
+    dist.init_process_group(backend=backend, init_method=init_method or "env://", world_size=world, rank=rank,
                             timeout=datetime.timedelta(seconds=timeout_s))
     return dist.get_rank(), dist.get_world_size(), local
 
@@ -114,13 +121,17 @@ def cleanup_distributed() -> None:
         dist.destroy_process_group()
 
 
-def wrap_ddp(model: nn.Module, config: DDPConfig | None = None, device_ids=None) -> nn.Module:
-    """torch DDP with the reference's settings (baseline path)."""
+def wrap_ddp(model: nn.Module, config: DDPConfig | None = None, device_id: Optional[int] = None,
+             device_ids=None) -> nn.Module:
+    """torch DDP with the reference's settings (baseline path); ``device_id`` (the reference's
+    argument) or ``device_ids`` pick the GPU, else the current device."""
     config = config or DDPConfig()
     if not is_distributed():
         return model
     from torch.nn.parallel import DistributedDataParallel as DDP
 
+    if device_ids is None and device_id is not None:
+        device_ids = [device_id]
     if device_ids is None and torch.cuda.is_available() and next(model.parameters()).is_cuda:
         device_ids = [torch.cuda.current_device()]
     wrapped = DDP(model, device_ids=device_ids, find_unused_parameters=config.find_unused_parameters,

@@ -43,8 +43,11 @@ def register_state_pytree() -> None:
     _PYTREE_REGISTERED = True
 
 
-def configure_matmul_precision(allow_tf32: bool = True, deterministic: bool = False) -> None:
-    """TF32 switches for PyTorch's own matmuls/convolutions (the sm_100a kernels choose per zone)."""
+def configure_matmul_precision(allow_tf32: bool = True, allow_fp16_accumulation: bool = False,
+                               deterministic: bool = False) -> None:
+    """TF32 and reduced-precision-reduction switches for PyTorch's own matmuls and convolutions
+    (the sm_100a kernels choose their precision per zone)."""
+    torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = allow_fp16_accumulation
     torch.backends.cuda.matmul.allow_tf32 = allow_tf32
     torch.backends.cudnn.allow_tf32 = allow_tf32
     torch.set_float32_matmul_precision("high" if allow_tf32 else "highest")

@@ -89,14 +89,17 @@ def has_sm100() -> bool:
     return torch.cuda.is_available() and _ext.available()
 
 
-def sht_legendre_inverse(basis, x: torch.Tensor, backend: Optional[str] = None) -> torch.Tensor:
-    """``backend``: ``"sm100"``, ``"torch"`` or ``None`` (sm100 for CUDA tensors)."""
-    if backend == "sm100" or (backend is None and x.is_cuda and _ext.available()):
+def sht_legendre_inverse(basis, x: torch.Tensor, use_fp64: bool = False, backend: Optional[str] = None) -> torch.Tensor:
+    """``backend``: ``"sm100"`` (the TF32 tensor-core kernel), ``"torch"`` or ``None`` (sm100 for
+    CUDA tensors).  ``use_fp64`` asks for FP64 accumulation and selects the FP64 einsum (the
+    reference's ``use_fp64`` switch; it defaults on there, where the default kernel is FP64)."""
+    if not use_fp64 and (backend == "sm100" or (backend is None and x.is_cuda and _ext.available())):
         return sht_legendre_inverse_sm100(basis, x)
-    return sht_legendre_inverse_torch(basis, x)
+    return sht_legendre_inverse_torch(basis, x)  # FP64 accumulation
 
 
-def sht_legendre_forward(basis, x: torch.Tensor, backend: Optional[str] = None) -> torch.Tensor:
-    if backend == "sm100" or (backend is None and x.is_cuda and _ext.available()):
+def sht_legendre_forward(basis, x: torch.Tensor, use_fp64: bool = False, backend: Optional[str] = None) -> torch.Tensor:
+    """Analysis counterpart of :func:`sht_legendre_inverse` (same switches)."""
+    if not use_fp64 and (backend == "sm100" or (backend is None and x.is_cuda and _ext.available())):
         return sht_legendre_forward_sm100(basis, x)
-    return sht_legendre_forward_torch(basis, x)
+    return sht_legendre_forward_torch(basis, x)  # FP64 accumulation
