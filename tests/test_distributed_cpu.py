@@ -37,9 +37,15 @@ def _free_port_pair() -> int:
 
 
 def _init(rank, world, port, timeout_s=30.0):
+    """Gloo group whose collectives time out after ``timeout_s``.  The ranks first meet on the
+    store with a generous limit (spawned ranks can take many seconds to import torch on a busy
+    machine), so that a short collective timeout does not also cut the rendezvous short."""
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world,
+    store = dist.TCPStore("127.0.0.1", port, world, rank == 0, timeout=datetime.timedelta(seconds=120))
+    store.set(f"up{rank}", "1")
+    store.wait([f"up{r}" for r in range(world)])
+    dist.init_process_group("gloo", store=store, rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=timeout_s))
 
 

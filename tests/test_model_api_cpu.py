@@ -66,7 +66,7 @@ def test_jax_checkpoint_roundtrip(tmp_path):
         pickle.dump(nested, fh)
     flat = jl.load_jax_checkpoint(path)
     target = jl.JaxNeuralComponents()
-    rep = jl.load_jax_weights(target, flat)
+    rep = jl.load_jax_weights(target, flat, strict=False)
     assert not rep["skipped"] and not rep["unmatched"]
     mapping = jl.build_weight_mapping(flat)
     sd = target.state_dict()

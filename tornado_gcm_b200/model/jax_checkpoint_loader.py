@@ -229,7 +229,7 @@ def _convert(value: np.ndarray, kind: str, target: torch.Tensor) -> torch.Tensor
     return t.to(target.dtype)
 
 
-def load_jax_weights(model: nn.Module, checkpoint_path, strict: bool = False) -> dict:
+def load_jax_weights(model: nn.Module, checkpoint_path, strict: bool = True) -> dict:
     """Copy mapped leaves into ``model``; returns a report of what was (not) loaded.
 
     ``checkpoint_path``: a pickled Haiku checkpoint (read with :func:`read_jax_checkpoint`,
@@ -283,7 +283,7 @@ def load_jax_hybrid(flat: dict, device: str | torch.device = "cpu", resolution: 
     from tornado_gcm_b200.models.builders import build_hybrid_gcm
 
     comps = JaxNeuralComponents()
-    report = load_jax_weights(comps, flat)
+    report = load_jax_weights(comps, flat, strict=False)
     gcm, _ = build_hybrid_gcm(resolution, device)
     pairs = [(comps.physics_epd, gcm.model.parameterization.tower), (comps.encoder_epd[0], gcm.encoder.net),
              (comps.decoder_epd, gcm.decoder.net)]

@@ -145,7 +145,7 @@ class CnnLevel(nn.Module):
     """Stack of ConvLevel layers with activations."""
 
     def __init__(self, input_size: int, output_size: int, *, channels: Sequence[int] = (), kernel_size: int = 3,
-                 activation: Callable = F.relu, activate_final: bool = False, use_bias: bool = True,
+                 activation: Callable = F.gelu, activate_final: bool = False, use_bias: bool = True,
                  kernel_sizes=None, strides=1, dilations=1):
         """``kernel_sizes`` / ``strides`` / ``dilations``: one value for every layer or one per
         layer (the reference's names; ``kernel_sizes`` overrides ``kernel_size``)."""

@@ -81,7 +81,7 @@ class VerticalConvTower(nn.Module):
     """
 
     def __init__(self, input_size: int | None = None, output_size: int | None = None,
-                 channels: Sequence[int] = (64, 64, 64, 64), kernel_size: int = 5, activation: Callable = F.relu,
+                 channels: Sequence[int] = (64, 64, 64, 64), kernel_size: int = 3, activation: Callable = F.relu,
                  activate_final: bool = False, use_bias: bool = True, *, input_channels: int | None = None,
                  output_channels: int | None = None, hidden_channels: Sequence[int] | None = None,
                  checkpoint_tower: bool = False):

@@ -206,7 +206,7 @@ class PhysicsConstrainedLoss(nn.Module):
     """Prediction loss + λ_E energy + λ_M mass + λ_H hydrology (after warmup)."""
 
     def __init__(self, prediction_loss: Optional[nn.Module] = None, lambda_e: float = 1e-3, lambda_m: float = 1e-3,
-                 lambda_h: float = 1e-3, warmup_steps: int = 0):
+                 lambda_h: float = 1e-3, warmup_steps: int = 1000):
         super().__init__()
         self.prediction_loss = prediction_loss or TrajectoryMSE()
         self.lambda_e, self.lambda_m, self.lambda_h = lambda_e, lambda_m, lambda_h
