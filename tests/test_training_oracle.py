@@ -151,3 +151,29 @@ def test_vertical_interpolation_and_soft_clip_match(ref):
     a = vi.get_surface_pressure(pc, geo, oro, units.g if hasattr(units, "g") else 9.80616)
     b = rvi.get_surface_pressure(rpc, geo, oro, units.g if hasattr(units, "g") else 9.80616)
     torch.testing.assert_close(a, b, rtol=1e-12, atol=1e-10)
+
+
+def test_feature_transforms_match(ref):
+    from tornado_gcm_b200.neural import transforms as ours
+
+    rt = ref.import_module("tornado_gcm.neural.transforms")
+    g = torch.Generator().manual_seed(9)
+    x = {"a": torch.randn(4, 6, 5, generator=g, dtype=torch.float64) * 3,
+         "b": torch.randn(1, 6, 5, generator=g, dtype=torch.float64)}
+    shifts, scales = {"a": 0.5, "b": -1.0}, {"a": 2.0, "b": 0.25}
+
+    def same(a, b, what):
+        assert set(a) == set(b), what
+        for k in a:
+            torch.testing.assert_close(a[k].double(), b[k].double(), rtol=1e-6, atol=1e-9, msg=f"{what}.{k}")
+
+    for name in ("ShiftAndNormalize", "InverseShiftAndNormalize"):
+        for gs in (None, 3.0):
+            same(getattr(ours, name)(shifts, scales, gs)(x), getattr(rt, name)(shifts, scales, gs)(x), name)
+    same(ours.InverseLevelScale(["a"], [1.0, 2.0, 4.0, 8.0])(x), rt.InverseLevelScale(["a"], [1.0, 2.0, 4.0, 8.0])(x),
+         "InverseLevelScale")
+    same(ours.HardClip(-1.0, 2.0)(x), rt.HardClip(-1.0, 2.0)(x), "HardClip")
+    ls = {"a": torch.tensor([1.0, 0.5, 2.0, 4.0], dtype=torch.float64)}
+    tt_a = ours.TendencyTransform(ls, clip_min={"a": -2.0}, clip_max={"b": 0.5})
+    tt_b = rt.TendencyTransform(ls, clip_min={"a": -2.0}, clip_max={"b": 0.5})
+    same(tt_a(x), tt_b(x), "TendencyTransform")
