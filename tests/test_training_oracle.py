@@ -177,3 +177,34 @@ def test_feature_transforms_match(ref):
     tt_a = ours.TendencyTransform(ls, clip_min={"a": -2.0}, clip_max={"b": 0.5})
     tt_b = rt.TendencyTransform(ls, clip_min={"a": -2.0}, clip_max={"b": 0.5})
     same(tt_a(x), tt_b(x), "TendencyTransform")
+
+
+def test_physics_features_match(ref):
+    """Radiation (solar geometry), pressure, latitude and velocity/prognostic features."""
+    from tornado_gcm_b200.core import spherical_harmonic as sh
+    from tornado_gcm_b200.neural import features as ours
+
+    rfe = ref.import_module("tornado_gcm.neural.features")
+    g = sh.Grid.T21(precision="highest")
+    rg = ref.spherical_harmonic.Grid.T21()
+    gen = torch.Generator().manual_seed(4)
+    mask = torch.as_tensor(g.mask)
+    m = lambda n: torch.randn(n, *g.modal_shape, generator=gen, dtype=torch.float64) * mask * 1e-2  # noqa: E731
+    inputs = {"vorticity": m(3), "divergence": m(3), "temperature_variation": m(3),
+              "log_surface_pressure": m(1),
+              "sim_time": torch.tensor(1234.5, dtype=torch.float64)}
+
+    def same(a, b, what, tol=1e-5):
+        assert set(a) == set(b), (what, sorted(a), sorted(b))
+        for k in a:
+            x, y = torch.as_tensor(a[k]).double(), torch.as_tensor(b[k]).double()
+            torch.testing.assert_close(x, y, rtol=tol, atol=tol * (float(y.abs().max()) + 1e-30), msg=f"{what}.{k}")
+
+    for t in (0.0, 1234.5):
+        inp = dict(inputs, sim_time=torch.tensor(t, dtype=torch.float64))
+        same(ours.RadiationFeatures(g, 738000.0, 1.0)(inp), rfe.RadiationFeatures(rg, 738000.0, 1.0)(inp),
+             "radiation")
+    same(ours.LatitudeFeatures(g)(inputs), rfe.LatitudeFeatures(rg)(inputs), "latitude")
+    sig = [0.1, 0.5, 0.9]
+    same(ours.PressureFeatures(g, sig)(inputs), rfe.PressureFeatures(rg, sig)(inputs), "pressure")
+    same(ours.VelocityAndPrognostics(g)(inputs), rfe.VelocityAndPrognostics(rg)(inputs), "velocity", tol=1e-4)
