@@ -208,3 +208,26 @@ def test_physics_features_match(ref):
     sig = [0.1, 0.5, 0.9]
     same(ours.PressureFeatures(g, sig)(inputs), rfe.PressureFeatures(rg, sig)(inputs), "pressure")
     same(ours.VelocityAndPrognostics(g)(inputs), rfe.VelocityAndPrognostics(rg)(inputs), "velocity", tol=1e-4)
+
+
+def test_storage_files_interchange_with_the_reference(ref, tmp_path):
+    """Files written by either side read back on the other (exact and lossy BF16 records)."""
+    from tornado_gcm_b200.precision.sda import StorageConfig as OurCfg
+    from tornado_gcm_b200.precision.storage import SDAStorageManager as Ours
+
+    rsda = ref.import_module("tornado_gcm.precision.sda")
+    rman = ref.import_module("tornado_gcm.precision.storage.manager")
+    g = torch.Generator().manual_seed(2)
+    vars_ = {"temperature": torch.randn(3, 8, 4, generator=g), "u": torch.randn(3, 8, 4, generator=g)}
+    ours = Ours(OurCfg(mode="mixed", critical_variables=["temperature"], non_critical_variables=["u"],
+                       compressor="none"))
+    theirs = rman.SDAStorageManager(rsda.StorageConfig(mode="exact", critical_variables=["temperature", "u"],
+                                                       compressor="none"))
+    ours.write(vars_, str(tmp_path / "a"), step=3)
+    back = theirs.read(str(tmp_path / "a"), step=3)
+    torch.testing.assert_close(back["temperature"], vars_["temperature"])
+    torch.testing.assert_close(back["u"], vars_["u"].to(torch.bfloat16).float())
+    theirs.write(vars_, str(tmp_path / "b"))
+    back = ours.read(str(tmp_path / "b"))
+    for k in vars_:
+        torch.testing.assert_close(back[k], vars_[k])

@@ -145,9 +145,13 @@ class LossyCodec:
                 logger.warning("LossyCodec: max relative error %.3e exceeds bound %.3e",
                                self.last_max_rel_error, self._error_bound)
         raw, dname = _to_host_bytes(q)
+        if q.dtype == torch.bfloat16:
+            dname = "int16"  # BF16 bit patterns under the record name the reference's files use
         return _EncodedTensor(_compress(raw, self._compressor, self._level), tuple(tensor.shape), dname,
                               str(tensor.dtype), self._compressor)
 
     def decode(self, encoded: _EncodedTensor, restore_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
         t = _from_bytes(_decompress(encoded.data, encoded.compressor), encoded.dtype_name, encoded.shape)
+        if encoded.dtype_name == "int16" and self._target_dtype == torch.bfloat16:
+            t = t.view(torch.bfloat16)
         return t.to(restore_dtype) if restore_dtype is not None else t
