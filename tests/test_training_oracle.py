@@ -231,3 +231,32 @@ def test_storage_files_interchange_with_the_reference(ref, tmp_path):
     back = ours.read(str(tmp_path / "b"))
     for k in vars_:
         torch.testing.assert_close(back[k], vars_[k])
+
+
+def test_training_checkpoints_interchange_with_the_reference(ref, tmp_path):
+    """A reference checkpoint (model, optimizer, training state, EMA) loads here and back."""
+    from tornado_gcm_b200.training import checkpointing as ours
+
+    rck = ref.import_module("tornado_gcm.training.checkpointing")
+    torch.manual_seed(0)
+    net = torch.nn.Sequential(torch.nn.Linear(4, 6), torch.nn.GELU(), torch.nn.Linear(6, 2))
+    opt = torch.optim.AdamW(net.parameters(), lr=1e-3)
+    net(torch.randn(3, 4)).sum().backward()
+    opt.step()
+    ema = {n: p.detach().clone() * 0.5 for n, p in net.named_parameters()}
+    rck.save_checkpoint(tmp_path / "r.pt", net, opt, rck.TrainingState(step=7, phase=2, best_val_loss=0.25), ema)
+    net2 = torch.nn.Sequential(torch.nn.Linear(4, 6), torch.nn.GELU(), torch.nn.Linear(6, 2))
+    opt2 = torch.optim.AdamW(net2.parameters(), lr=1e-3)
+    st = ours.load_checkpoint(tmp_path / "r.pt", net2, opt2)
+    assert (st.step, st.phase, st.best_val_loss) == (7, 2, 0.25)
+    for a, b in zip(net.parameters(), net2.parameters()):
+        torch.testing.assert_close(a, b)
+    assert opt2.state_dict()["state"][0]["step"] == opt.state_dict()["state"][0]["step"]
+    for k, v in ours.load_ema(tmp_path / "r.pt").items():
+        torch.testing.assert_close(v, ema[k])
+    ours.save_checkpoint(tmp_path / "o.pt", net2, opt2, ours.TrainingState(step=8, phase=3), ema)
+    net3 = torch.nn.Sequential(torch.nn.Linear(4, 6), torch.nn.GELU(), torch.nn.Linear(6, 2))
+    st3 = rck.load_checkpoint(tmp_path / "o.pt", net3)
+    assert st3.step == 8 and st3.phase == 3
+    for a, b in zip(net.parameters(), net3.parameters()):
+        torch.testing.assert_close(a, b)
