@@ -260,3 +260,25 @@ def test_training_checkpoints_interchange_with_the_reference(ref, tmp_path):
     assert st3.step == 8 and st3.phase == 3
     for a, b in zip(net.parameters(), net3.parameters()):
         torch.testing.assert_close(a, b)
+
+
+def test_reference_sda_configs_load_alike(ref):
+    """Every SDA YAML of the reference parses here into the same policy, profiler, scheduler,
+    accelerator, storage and sparse settings as in the reference."""
+    import glob
+    import os
+
+    from tornado_gcm_b200.precision.sda import SDAConfig
+
+    rsda = ref.import_module("tornado_gcm.precision.sda")
+    root = os.path.dirname(os.path.dirname(ref.import_module("tornado_gcm.precision.sda").__file__))
+    files = sorted(glob.glob(os.path.join(root, "configs", "*.yaml")))
+    assert files
+    for path in files:
+        a, b = SDAConfig.from_yaml(path).to_dict(), rsda.SDAConfig.from_yaml(path).to_dict()
+        for section in ("policy", "profiler", "scheduler", "accelerator", "storage", "sparse"):
+            if section not in b:
+                continue
+            for k, v in b[section].items():
+                if k in a.get(section, {}):
+                    assert str(a[section][k]) == str(v), (os.path.basename(path), section, k, a[section][k], v)
