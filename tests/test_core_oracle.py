@@ -223,3 +223,27 @@ def test_test_case_initial_states_match(ref):
     for f in ("vorticity", "divergence"):
         close(getattr(pa, f), getattr(pb, f), f)
     close(pes.gaussian_scalar(coords), rpes.gaussian_scalar(rcoords), "gaussian")
+
+
+def test_hybrid_coordinates_match(ref, rng):
+    from tornado_gcm_b200.core import hybrid_coordinates as hc
+
+    rhc = ref.import_module("tornado_gcm.core.hybrid_coordinates")
+    a = hc.HybridCoordinates.analytic_levels(12)
+    b = rhc.HybridCoordinates.analytic_levels(12)
+    for name in ("a_boundaries", "b_boundaries", "pressure_thickness", "sigma_thickness", "a_centers", "b_centers",
+                 "center_to_center"):
+        np.testing.assert_allclose(getattr(a, name), getattr(b, name), rtol=1e-12, atol=1e-12, err_msg=name)
+    np.testing.assert_allclose(a.get_eta(950.0), b.get_eta(950.0), rtol=1e-12)
+    np.testing.assert_allclose(a.get_sigma_centers(980.0), b.get_sigma_centers(980.0), rtol=1e-12)
+    ps = torch.as_tensor(900.0 + 100.0 * rng.random((1, 5, 4)))
+    for name in ("pressure_boundaries", "pressure_centers", "layer_thickness"):
+        torch.testing.assert_close(getattr(a, name)(ps), getattr(b, name)(ps), msg=name)
+    x = torch.as_tensor(rng.standard_normal((12, 5, 4)))
+    w = torch.as_tensor(rng.standard_normal((11, 5, 4)))
+    for down in (True, False):
+        torch.testing.assert_close(hc.cumulative_integral_over_pressure(x, ps, a, downward=down),
+                                   rhc.cumulative_integral_over_pressure(x, ps, b, downward=down))
+    torch.testing.assert_close(hc.integral_over_pressure(x, ps, a), rhc.integral_over_pressure(x, ps, b))
+    torch.testing.assert_close(hc.centered_difference(x, a), rhc.centered_difference(x, b))
+    torch.testing.assert_close(hc.centered_vertical_advection(w, x, a), rhc.centered_vertical_advection(w, x, b))
