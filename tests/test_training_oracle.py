@@ -282,3 +282,25 @@ def test_reference_sda_configs_load_alike(ref):
             for k, v in b[section].items():
                 if k in a.get(section, {}):
                     assert str(a[section][k]) == str(v), (os.path.basename(path), section, k, a[section][k], v)
+
+
+def test_random_field_spectrum_matches_the_reference_shape(ref):
+    """Same AR(1) coefficient and the same spectral shape exp(-κ l(l+1)/2); the normalisation
+    differs by design (here: the nodal area-mean variance equals ``variance``)."""
+    import numpy as np
+
+    from tornado_gcm_b200.core import spherical_harmonic as sh
+    from tornado_gcm_b200.neural.stochastic import GaussianRandomField
+
+    rst = ref.import_module("tornado_gcm.neural.stochastic")
+    g, rg = sh.Grid.T21(), ref.spherical_harmonic.Grid.T21()
+    a = GaussianRandomField(g, correlation_time=3.0, correlation_length=0.2, variance=2.0)
+    b = rst.GaussianRandomField(rg, correlation_time=3.0, correlation_length=0.2, variance=2.0)
+    assert a._phi == pytest.approx(b._phi, rel=1e-15)
+    ratio = (a._sigma[0] / b._sigma_n).numpy()
+    np.testing.assert_allclose(ratio, ratio[0], rtol=1e-5)
+    gen = torch.Generator().manual_seed(0)
+    draws = torch.stack([g.to_nodal(a.sample_modal((), gen).double()) for _ in range(400)])
+    w = torch.as_tensor(g.spherical_harmonics.basis.w, dtype=torch.float64)
+    area_var = float((draws ** 2).mean(0).mean(0) @ w / w.sum())
+    assert area_var == pytest.approx(2.0, rel=0.1)
