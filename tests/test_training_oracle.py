@@ -304,3 +304,27 @@ def test_random_field_spectrum_matches_the_reference_shape(ref):
     w = torch.as_tensor(g.spherical_harmonics.basis.w, dtype=torch.float64)
     area_var = float((draws ** 2).mean(0).mean(0) @ w / w.sum())
     assert area_var == pytest.approx(2.0, rel=0.1)
+
+
+def test_data_windows_and_forecast_starts_match(ref):
+    import numpy as np
+
+    from tornado_gcm_b200.training import data_loading as dl, evaluation as ev
+
+    rdl = ref.import_module("tornado_gcm.training.data_loading")
+    rev = ref.import_module("tornado_gcm.training.evaluation")
+    t = np.concatenate([np.arange(0, 40), np.arange(43, 60), np.arange(70, 75), np.arange(90, 120)]) * 6.0
+    assert dl.find_contiguous_segments(t) == rdl.find_contiguous_segments(t)
+    for w, r in ((8, 0.05), (12, 0.2), (20, 0.05)):
+        a = dl.gap_tolerant_sampling(t, w, r)
+        b = rdl.gap_tolerant_sampling(t, w, r)
+        key = lambda x: (x.start_idx, x.length, x.weight) if hasattr(x, "start_idx") else tuple(vars(x).values())  # noqa: E731
+        assert a and [key(x) for x in a] == [key(x) for x in b], (w, r)
+    first, last = np.datetime64("2020-01-01T00"), np.datetime64("2020-12-31T00")
+    for alt in (True, False):
+        np.testing.assert_array_equal(ev.get_forecast_starts_equispaced(10, first, last, alt),
+                                      rev.get_forecast_starts_equispaced(10, first, last, alt))
+    cands = np.arange(np.datetime64("2020-01-01T00"), np.datetime64("2020-03-01T00"), np.timedelta64(6, "h"))
+    for bal in (True, False):
+        np.testing.assert_array_equal(ev.get_forecast_starts_balanced(12, cands, bal),
+                                      rev.get_forecast_starts_balanced(12, cands, bal))
