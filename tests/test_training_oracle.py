@@ -328,3 +328,31 @@ def test_data_windows_and_forecast_starts_match(ref):
     for bal in (True, False):
         np.testing.assert_array_equal(ev.get_forecast_starts_balanced(12, cands, bal),
                                       rev.get_forecast_starts_balanced(12, cands, bal))
+
+
+def test_data_pipeline_helpers_match(ref):
+    import numpy as np
+
+    from tornado_gcm_b200.training import data_pipeline as dp
+
+    rdp = ref.import_module("tornado_gcm.training.data_pipeline")
+    t0 = np.datetime64("2020-01-01T00")
+    times = t0 + np.arange(0, 96, 6).astype("timedelta64[h]")
+    for scale in (1.0, 6.0):
+        s_a = dp.datetime64_to_sim_time(times, t0, scale)
+        np.testing.assert_array_equal(s_a, rdp.datetime64_to_sim_time(times, t0, scale))
+        np.testing.assert_array_equal(dp.sim_time_to_datetime64(s_a, t0, scale),
+                                      rdp.sim_time_to_datetime64(s_a, t0, scale))
+    src_lon, src_lat = np.linspace(0, 357.5, 144), np.linspace(-90, 90, 73)
+    tgt_lon, tgt_lat = np.linspace(0, 354.375, 64), np.linspace(-87.2, 87.2, 32)
+    field = np.random.default_rng(1).standard_normal((3, 144, 73))
+    a = dp.BilinearRegridder(src_lon, src_lat, tgt_lon, tgt_lat)
+    b = rdp.BilinearRegridder(src_lon, src_lat, tgt_lon, tgt_lat)
+    np.testing.assert_allclose(np.asarray(a(field)), np.asarray(b(field)), rtol=1e-10, atol=1e-12)
+    lon, lat = np.linspace(0, 350, 36), np.linspace(-85, 85, 18)
+    holes = np.random.default_rng(2).standard_normal((36, 18))
+    holes[5:9, 3:6] = np.nan
+    fa, fb = dp.NearestNaNFiller(lon, lat), rdp.NearestNaNFiller(lon, lat)
+    ca, cb = fa.fill(holes), fb.fill(holes)
+    assert not np.isnan(ca).any()
+    np.testing.assert_allclose(np.asarray(ca), np.asarray(cb))
