@@ -356,3 +356,36 @@ def test_data_pipeline_helpers_match(ref):
     ca, cb = fa.fill(holes), fb.fill(holes)
     assert not np.isnan(ca).any()
     np.testing.assert_allclose(np.asarray(ca), np.asarray(cb))
+
+
+def test_verification_metrics_match(ref):
+    """RMSE, ACC (with and without climatology) and bias per variable and lead time, on
+    dict and State trajectories."""
+    from tornado_gcm_b200.core import primitive_equations as pe
+    from tornado_gcm_b200.training import evaluation as ev
+
+    rev = ref.import_module("tornado_gcm.training.evaluation")
+    rpe = ref.import_module("tornado_gcm.core.primitive_equations")
+    g = torch.Generator().manual_seed(8)
+    r = lambda *s: torch.randn(*s, generator=g, dtype=torch.float64)  # noqa: E731
+    preds = [{"t": r(3, 6, 5), "z": r(1, 6, 5)} for _ in range(3)]
+    tgts = [{"t": r(3, 6, 5), "z": r(1, 6, 5)} for _ in range(3)]
+    clim = {"t": r(3, 6, 5), "z": r(1, 6, 5)}
+
+    def same(a, b, what):
+        assert set(a) == set(b), what
+        for k in a:
+            assert a[k] == pytest.approx(b[k], rel=1e-6, abs=1e-9), (what, k)  # fp32 metric tables here
+
+    same(ev.compute_rmse(preds, tgts), rev.compute_rmse(preds, tgts), "rmse")
+    same(ev.compute_bias(preds, tgts), rev.compute_bias(preds, tgts), "bias")
+    same(ev.compute_anomaly_correlation(preds, tgts), rev.compute_anomaly_correlation(preds, tgts), "acc")
+    same(ev.compute_anomaly_correlation(preds, tgts, clim), rev.compute_anomaly_correlation(preds, tgts, clim),
+         "acc-clim")
+    same(ev.compute_rmse(preds, tgts, ["t"]), rev.compute_rmse(preds, tgts, ["t"]), "rmse-filter")
+    gen_state = torch.Generator().manual_seed(11)
+    rr = lambda *s: torch.randn(*s, generator=gen_state, dtype=torch.float64)  # noqa: E731
+    raw = [(rr(2, 4, 3), rr(2, 4, 3), rr(2, 4, 3), rr(1, 4, 3)) for _ in range(4)]
+    ours_s = [pe.State(*x, {}) for x in raw]
+    ref_s = [rpe.State(*x, {}) for x in raw]
+    same(ev.compute_rmse(ours_s[:2], ours_s[2:]), rev.compute_rmse(ref_s[:2], ref_s[2:]), "rmse-state")
