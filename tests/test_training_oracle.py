@@ -389,3 +389,34 @@ def test_verification_metrics_match(ref):
     ours_s = [pe.State(*x, {}) for x in raw]
     ref_s = [rpe.State(*x, {}) for x in raw]
     same(ev.compute_rmse(ours_s[:2], ours_s[2:]), rev.compute_rmse(ref_s[:2], ref_s[2:]), "rmse-state")
+
+
+def test_precision_monitor_and_zone_casts_match(ref):
+    from tornado_gcm_b200.precision import monitor as mon, zone_cast as zc
+    from tornado_gcm_b200.precision.policy import PrecisionPolicy, PrecisionZone
+
+    rmon = ref.import_module("tornado_gcm.precision.monitor")
+    rzc = ref.import_module("tornado_gcm.precision.zone_cast")
+    rpol = ref.import_module("tornado_gcm.precision.policy")
+    g = torch.Generator().manual_seed(6)
+    x = torch.randn(4, 8, 5, generator=g, dtype=torch.float64) * 10
+    x[0, 0, 0] = float("nan")
+    a, b = mon.PrecisionMonitor(), rmon.PrecisionMonitor()
+    for m in (a, b):
+        m.audit_zone_transfer("Z1_to_Z3", x, x.to(torch.bfloat16))
+        m.step()
+        m.audit_conservation(torch.tensor(1.0), torch.tensor(1.0 + 3e-7), torch.tensor(2.0), torch.tensor(2.0 - 1e-6))
+    sa, sb = a.summary(), b.summary()
+    assert set(sb) <= set(sa)
+    for k in sb:
+        assert sa[k] == pytest.approx(sb[k], rel=1e-5, abs=1e-12, nan_ok=True), k
+    ops = (torch.randn(3, 4, generator=g), torch.randn(4, 5, generator=g, dtype=torch.float64))
+    torch.testing.assert_close(zc.einsum_highest("ij,jk->ik", *ops), rzc.einsum_highest("ij,jk->ik", *ops))
+    y = torch.randn(6, generator=g)
+    for src, dst in ((PrecisionZone.Z1_DYNAMICS_CORE, PrecisionZone.Z3_NEURAL_NETWORK),
+                     (PrecisionZone.Z3_NEURAL_NETWORK, PrecisionZone.Z2_CONSERVATION_FIXER)):
+        rs, rd = getattr(rpol.PrecisionZone, src.name), getattr(rpol.PrecisionZone, dst.name)
+        oa = zc.zone_cast(y, src, dst, PrecisionPolicy())
+        ob = rzc.zone_cast(y, rs, rd, rpol.PrecisionPolicy())
+        assert oa.dtype == ob.dtype
+        torch.testing.assert_close(oa, ob)
