@@ -25,7 +25,7 @@ Structure is different and batch-first:
 from __future__ import annotations
 
 import dataclasses
-from typing import Any, Callable, Mapping, Optional
+from typing import Any, Mapping, Optional
 
 import numpy as np
 import torch

@@ -31,7 +31,7 @@ import torch.nn as nn
 from tornado_gcm_b200.core import primitive_equations as pe
 from tornado_gcm_b200.core import spherical_harmonic
 from tornado_gcm_b200.core import vertical_interpolation as vi
-from tornado_gcm_b200.neural.transforms import batched_to_modal, batched_to_nodal
+from tornado_gcm_b200.neural.transforms import batched_to_modal
 from tornado_gcm_b200.utils.typing import KeyWithCosLatFactor
 
 

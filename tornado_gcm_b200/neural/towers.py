@@ -11,7 +11,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from tornado_gcm_b200.neural.standard_layers import ConvLevel, ConvLonLat, lecun_normal_
+from tornado_gcm_b200.neural.standard_layers import ConvLevel, ConvLonLat
 
 
 def _net_dtype(net: nn.Module, x: torch.Tensor) -> torch.Tensor:

@@ -9,8 +9,6 @@ run on cuBLAS.
 
 from __future__ import annotations
 
-from typing import Optional
-
 import torch
 
 from tornado_gcm_b200.precision.sda import SparseConfig

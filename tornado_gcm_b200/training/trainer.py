@@ -19,14 +19,14 @@ import dataclasses
 import logging
 import os
 import math
-from typing import Any, Callable, Optional, Sequence
+from typing import Any, Callable, Sequence
 
 import torch
 import torch.nn as nn
 import torch.utils.checkpoint as checkpoint_util
 
 from tornado_gcm_b200.core.primitive_equations import State
-from tornado_gcm_b200.precision.policy import PrecisionPolicy, PrecisionZone
+from tornado_gcm_b200.precision.policy import PrecisionPolicy
 
 logger = logging.getLogger(__name__)
 

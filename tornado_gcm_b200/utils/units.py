@@ -14,7 +14,6 @@ rotation rate, g, dry-air Cp and kappa, vapour R and Cp).
 from __future__ import annotations
 
 import dataclasses
-import math
 from typing import Iterator, Mapping, Protocol, runtime_checkable
 
 import numpy as np
