@@ -154,3 +154,57 @@ def test_sharded_optimizer_state_round_trip():
     bad = dict(sd, chunk=sd["chunk"] + 4)
     with pytest.raises(ValueError):
         opt2.load_state_dict(bad)
+
+
+def _worker_full_state(rank, world, port, q):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+        from tornado_gcm_b200.parallel.sharded_optim import ShardedAdamW
+
+        torch.manual_seed(0)
+        m_sh, m_rep = _Toy(), _Toy()
+        m_rep.load_state_dict(m_sh.state_dict())
+        opt = ShardedAdamW(list(m_sh.parameters()), lr=1e-2, weight_decay=0.01, max_grad_norm=None)
+        for step in range(2):
+            opt.zero_grad()
+            m_sh.loss(*_batch(0, step)).backward()    # same data on every rank: the mean is that gradient
+            opt.step()
+        full = opt.full_state_dict()
+        # a replicated AdamW resumes from the gathered state and matches one more sharded step
+        with torch.no_grad():
+            for a, b in zip(m_rep.parameters(), m_sh.parameters()):
+                a.copy_(b)
+        ref_opt = torch.optim.AdamW(m_rep.parameters(), lr=1e-2, weight_decay=0.01, betas=(0.9, 0.95), eps=1e-6)
+        ref_opt.load_state_dict(full)
+        for o, model in ((opt, m_sh), (ref_opt, m_rep)):
+            o.zero_grad()
+            model.loss(*_batch(0, 2)).backward()
+            o.step()
+        err = max(float((a - b).abs().max()) for a, b in zip(m_rep.parameters(), m_sh.parameters()))
+        # and the sharded optimizer takes the full state back
+        opt2 = ShardedAdamW(list(_Toy().parameters()), lr=1e-2)
+        opt2.load_full_state_dict(full)
+        mom = opt2.optimizer.state[opt2.shard]["exp_avg"]
+        q.put((rank, err, len(full["state"]), int(mom.numel() == opt2.chunk)))
+        dist.destroy_process_group()
+    except Exception:  # pragma: no cover
+        q.put((rank, traceback.format_exc()))
+
+
+def test_sharded_optimizer_full_state_round_trip():
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker_full_state, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=180) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for r in res:
+        assert not isinstance(r[1], str), r[1]
+        _, err, n, ok = r
+        assert err < 1e-6 and n == 5 and ok       # five parameters in the toy model

@@ -242,6 +242,54 @@ class ShardedAdamW:
         self.comm.all_gather_params()
         return total
 
+    def _gather_flat(self, chunk: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return chunk.detach().clone()
+        parts = [torch.empty_like(chunk) for _ in range(self.world)]
+        dist.all_gather(parts, chunk.detach().contiguous(), group=self.group)
+        return torch.cat(parts)
+
+    def full_state_dict(self) -> dict:
+        """The optimizer state as a ``torch.optim.AdamW`` over the model's parameters would
+        hold it (moments shaped like each parameter, in parameter order), gathered from
+        every rank.  Collective: every rank calls it; every rank gets the result."""
+        st = self.optimizer.state.get(self.shard, {})
+        if "exp_avg" not in st:
+            return {"state": {}, "param_groups": self._full_groups()}
+        m1, m2 = self._gather_flat(st["exp_avg"]), self._gather_flat(st["exp_avg_sq"])
+        step = st["step"].detach().clone() if torch.is_tensor(st["step"]) else torch.tensor(float(st["step"]))
+        state, off = {}, 0
+        for i, p in enumerate(self.params):
+            k = p.numel()
+            state[i] = {"step": step.clone(), "exp_avg": m1[off:off + k].view_as(p).clone(),
+                        "exp_avg_sq": m2[off:off + k].view_as(p).clone()}
+            off += k
+        return {"state": state, "param_groups": self._full_groups()}
+
+    def _full_groups(self) -> list:
+        g = {k: v for k, v in self.optimizer.param_groups[0].items() if k != "params"}
+        g["params"] = list(range(len(self.params)))
+        return [g]
+
+    def load_full_state_dict(self, sd: dict) -> None:
+        """Take this rank's chunk of a full (replicated-layout) AdamW state dict."""
+        if not sd.get("state"):
+            return
+        flat1 = torch.zeros(self.numel_padded, dtype=torch.float32, device=self.device)
+        flat2 = torch.zeros_like(flat1)
+        off = 0
+        for i, p in enumerate(self.params):
+            k = p.numel()
+            flat1[off:off + k] = sd["state"][i]["exp_avg"].reshape(-1).to(flat1)
+            flat2[off:off + k] = sd["state"][i]["exp_avg_sq"].reshape(-1).to(flat2)
+            off += k
+        c0 = self.rank * self.chunk
+        step = sd["state"][0]["step"]
+        own = {"step": torch.as_tensor(step, dtype=torch.float32).clone(),
+               "exp_avg": flat1[c0:c0 + self.chunk].clone(), "exp_avg_sq": flat2[c0:c0 + self.chunk].clone()}
+        groups = [dict(sd["param_groups"][0], params=[0])]
+        self.optimizer.load_state_dict({"state": {0: own}, "param_groups": groups})
+
     def state_dict(self) -> dict:
         """This rank's optimizer state (its chunk's moments) with the layout needed to merge shards."""
         return {"optimizer": self.optimizer.state_dict(), "rank": self.rank, "world": self.world,
