@@ -420,3 +420,29 @@ def test_precision_monitor_and_zone_casts_match(ref):
         ob = rzc.zone_cast(y, rs, rd, rpol.PrecisionPolicy())
         assert oa.dtype == ob.dtype
         torch.testing.assert_close(oa, ob)
+
+
+def test_multi_adam_groups_and_gradient_cuts_match(ref):
+    from tornado_gcm_b200.training import optimization as ours
+
+    ro = ref.import_module("tornado_gcm.training.optimization")
+    torch.manual_seed(0)
+    model = torch.nn.ModuleDict({"encoder": torch.nn.Linear(3, 4), "physics_net": torch.nn.Linear(4, 4),
+                                 "decoder": torch.nn.Linear(4, 2)})
+    keys, lrs = ("encoder", "REGEX_^phys"), (1e-3, 3e-4)
+    a = ours.multi_adam(model, keys, lrs, default_learning_rate=5e-5, weight_decay=0.1)
+    b = ro.multi_adam(model, keys, lrs, default_learning_rate=5e-5, weight_decay=0.1)
+    ga = sorted((g["lr"], g.get("weight_decay"), tuple(sorted(id(p) for p in g["params"]))) for g in a.param_groups)
+    gb = sorted((g["lr"], g.get("weight_decay"), tuple(sorted(id(p) for p in g["params"]))) for g in b.param_groups)
+    assert ga == gb
+    with pytest.raises(Exception):
+        ours.multi_adam(model, ("nothing",), (1e-3,))
+    w = torch.nn.Parameter(torch.tensor(1.3))
+    step = lambda s: s * w + 0.1  # noqa: E731
+    x0 = torch.tensor(0.5)
+    ta = ours.StopGradientTrajectory([2]).rollout(step, x0, 4)
+    tb = ro.StopGradientTrajectory([2]).rollout(step, x0, 4)
+    ga_, = torch.autograd.grad(sum(ta), [w])
+    gb_, = torch.autograd.grad(sum(tb), [w])
+    torch.testing.assert_close(ga_, gb_)
+    torch.testing.assert_close(torch.stack(list(ta)), torch.stack(list(tb)))
