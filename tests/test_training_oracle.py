@@ -446,3 +446,29 @@ def test_multi_adam_groups_and_gradient_cuts_match(ref):
     gb_, = torch.autograd.grad(sum(tb), [w])
     torch.testing.assert_close(ga_, gb_)
     torch.testing.assert_close(torch.stack(list(ta)), torch.stack(list(tb)))
+
+
+def test_network_state_dicts_interchange_with_the_reference(ref):
+    """Reference layers' weights load into this framework's layers with strict key matching and
+    give the same outputs (the towers of a reference checkpoint keep working here)."""
+    import torch.nn.functional as F
+
+    from tornado_gcm_b200.neural import standard_layers as ours
+    from tornado_gcm_b200.neural import towers as our_towers
+
+    rsl = ref.import_module("tornado_gcm.neural.standard_layers")
+    rtw = ref.import_module("tornado_gcm.neural.towers")
+    torch.manual_seed(3)
+    pairs = [
+        (rsl.Mlp(7, 3, intermediate_sizes=[5, 6], activation=F.gelu),
+         ours.Mlp(7, 3, intermediate_sizes=[5, 6], activation=F.gelu), (4, 7)),
+        (rsl.ConvLevel(3, 5, kernel_size=3), ours.ConvLevel(3, 5, kernel_size=3), (2, 3, 8)),
+        (rsl.ConvLonLat(3, 4, (3, 3)), ours.ConvLonLat(3, 4, (3, 3)), (3, 8, 6)),
+        (rtw.VerticalConvTower(3, 2, [4, 4], kernel_size=3), our_towers.VerticalConvTower(3, 2, [4, 4], kernel_size=3),
+         (3, 8, 5, 4)),
+    ]
+    for theirs, mine, shape in pairs:
+        mine.load_state_dict(theirs.state_dict(), strict=True)
+        x = torch.randn(*shape)
+        with torch.no_grad():
+            torch.testing.assert_close(mine(x), theirs(x), msg=type(mine).__name__)
