@@ -472,3 +472,51 @@ def test_network_state_dicts_interchange_with_the_reference(ref):
         x = torch.randn(*shape)
         with torch.no_grad():
             torch.testing.assert_close(mine(x), theirs(x), msg=type(mine).__name__)
+
+
+def test_modal_div_curl_parameterization_matches(ref):
+    """The modal parameterization of the reference benchmark arm: reference weights in this
+    framework's module, same tendencies (forcings appended, div/curl back to modal)."""
+    import torch.nn.functional as F
+
+    from tornado_gcm_b200.core import primitive_equations as pe, spherical_harmonic as sh
+    from tornado_gcm_b200.neural.parameterizations import ModalNeuralDivCurlParameterization
+    from tornado_gcm_b200.neural.standard_layers import Mlp
+    from tornado_gcm_b200.neural.towers import ForwardTower
+
+    rsl = ref.import_module("tornado_gcm.neural.standard_layers")
+    rtw = ref.import_module("tornado_gcm.neural.towers")
+    rpa = ref.import_module("tornado_gcm.neural.parameterizations")
+    rpe = ref.import_module("tornado_gcm.core.primitive_equations")
+    n = 3
+    g, rg = sh.Grid.T21(precision="highest"), _ref_grid_fp64_like(ref)
+    c_in, c_out = 3 * n + 1 + 2, 3 * n + 1
+    torch.manual_seed(0)
+    rnet = rtw.ForwardTower(rsl.Mlp(c_in, c_out, intermediate_sizes=[16], activation=F.gelu))
+    net = ForwardTower(Mlp(c_in, c_out, intermediate_sizes=[16], activation=F.gelu))
+    net.load_state_dict(rnet.state_dict(), strict=True)
+    a = ModalNeuralDivCurlParameterization(g, net, n, fwd_dtype=torch.float32)
+    b = rpa.ModalNeuralDivCurlParameterization(rg, rnet, n, fwd_dtype=torch.float32)
+    gen = torch.Generator().manual_seed(1)
+    mask = torch.as_tensor(g.mask)
+    m = lambda k: (torch.randn(k, *g.modal_shape, generator=gen) * mask * 1e-2).double()  # noqa: E731
+    vals = (m(n), m(n), m(n), m(1))
+    forc = {"sst": torch.rand(*g.nodal_shape, generator=gen).double(), "ice": torch.rand(1, *g.nodal_shape,
+                                                                                         generator=gen).double()}
+    with torch.no_grad():
+        ta = a(pe.State(*vals, {}), forcings=forc)
+        tb = b(rpe.State(*vals, {}), forcings=forc)
+    for f in ("vorticity", "divergence", "temperature_variation", "log_surface_pressure"):
+        x, y = getattr(ta, f).double(), getattr(tb, f).double()
+        assert float(y.abs().max()) > 0, f
+        torch.testing.assert_close(x, y, rtol=1e-4, atol=1e-4 * float(y.abs().max()), msg=f)
+
+
+def _ref_grid_fp64_like(ref):
+    rg = ref.spherical_harmonic.Grid.T21()
+    rsh = ref.spherical_harmonic.RealSphericalHarmonics(
+        longitude_wavenumbers=rg.longitude_wavenumbers, total_wavenumbers=rg.total_wavenumbers,
+        longitude_nodes=rg.longitude_nodes, latitude_nodes=rg.latitude_nodes,
+        latitude_spacing=rg.latitude_spacing, einsum_fn=ref.spherical_harmonic.einsum_highest)
+    rg.__dict__["spherical_harmonics"] = rsh
+    return rg
