@@ -59,14 +59,24 @@ def main(verbose: bool = False) -> None:
 @click.option("--batch-size", "-b", default=None, type=int, help="Per-device batch (default: config).")
 @click.option("--device", "-d", default="cuda", show_default=True)
 @click.option("--use-sda/--no-sda", default=True, show_default=True, help="Drive phases with the SDA scheduler.")
+@click.option("--parallel", type=click.Choice(["dp", "sharded"]), default="dp", show_default=True,
+              help="Under torchrun: dp = replicated weights and optimizer, gradients averaged; sharded = "
+                   "gradients and AdamW state split over the ranks.")
 def train(config: str, checkpoint: Optional[str], jax_weights: Optional[str], steps: Optional[int],
-          batch_size: Optional[int], device: str, use_sda: bool) -> None:
-    """Train the hybrid model (synthetic reanalysis-shaped data unless the config names a source)."""
+          batch_size: Optional[int], device: str, use_sda: bool, parallel: str) -> None:
+    """Train the hybrid model (synthetic reanalysis-shaped data unless the config names a source).
+
+    Launched by torchrun with several processes, every rank trains on its own batches and the
+    gradients are combined as ``--parallel`` says; rank 0 reports and writes the checkpoint."""
     from tornado_gcm_b200.models.builders import build_hybrid_gcm
+    from tornado_gcm_b200.parallel.ddp import get_rank, setup_distributed
     from tornado_gcm_b200.precision.sda import SDAConfig
     from tornado_gcm_b200.training.sda_trainer import SDATrainer
 
     cfg = SDAConfig.from_yaml(_config_path(config))
+    rank, world, local = setup_distributed()
+    if world > 1 and device == "cuda":
+        device = f"cuda:{local}"
     dev = _device(device)
     if jax_weights:
         from tornado_gcm_b200.model.jax_checkpoint_loader import load_jax_checkpoint
@@ -77,12 +87,13 @@ def train(config: str, checkpoint: Optional[str], jax_weights: Optional[str], st
     if not use_sda:
         cfg.scheduler.mode = "milestone"
         cfg.scheduler.check_interval = 10 ** 9
-    trainer = SDATrainer(gcm, cfg, total_steps=steps, batch_size=batch_size)
+    dp = ("sharded" if parallel == "sharded" else True) if world > 1 else False
+    trainer = SDATrainer(gcm, cfg, total_steps=steps, batch_size=batch_size, data_parallel=dp)
     if checkpoint and pathlib.Path(checkpoint).exists():
         logger.info("resuming from %s", checkpoint)
         trainer.load_checkpoint(checkpoint)
     hist = trainer.train(log_every=max(1, trainer.total_steps // 20))
-    if hist:
+    if hist and get_rank() == 0:
         click.echo(f"final loss {hist[-1]['loss']:.6g} after {hist[-1]['step']} steps")
     if checkpoint:
         trainer.save_checkpoint(checkpoint)

@@ -99,8 +99,10 @@ class SDATrainer:
     def _synthetic_batches(self) -> Iterator:
         from tornado_gcm_b200.training.synthetic import SyntheticReanalysis
 
+        from tornado_gcm_b200.parallel.ddp import get_rank
+
         grid = self.gcm.model.config.coords.horizontal
-        src = SyntheticReanalysis(grid, seed=0)
+        src = SyntheticReanalysis(grid, seed=get_rank())  # every rank draws its own samples
         enc = self.gcm.encoder
         norm = lambda d: {k: (v.to(self.device) - getattr(enc, f"mean_{k}")) / getattr(enc, f"std_{k}")
                           for k, v in d.items()}
@@ -211,10 +213,16 @@ class SDATrainer:
 
     # ── checkpoints ──
     def save_checkpoint(self, path) -> None:
+        """One checkpoint file (written by rank 0).  With the sharded optimizer the moments are
+        gathered into the replicated AdamW layout first, a collective every rank takes part in."""
+        from tornado_gcm_b200.parallel.ddp import get_rank
         from tornado_gcm_b200.training.checkpointing import _atomic_save
 
-        _atomic_save({"model_state_dict": self.gcm.state_dict(),
-                      "optimizer_state_dict": self._trainer.optimizer.state_dict(),
+        zo = self._trainer.zero_opt
+        opt_sd = zo.full_state_dict() if zo is not None else self._trainer.optimizer.state_dict()
+        if get_rank() != 0:
+            return
+        _atomic_save({"model_state_dict": self.gcm.state_dict(), "optimizer_state_dict": opt_sd,
                       "ema": self.get_ema_state_dict(), "step": self.step_count,
                       "rollout_steps": self._rollout_steps}, pathlib.Path(path))
 
@@ -222,7 +230,10 @@ class SDATrainer:
         ck = torch.load(path, map_location=self.device, weights_only=False)
         self.gcm.load_state_dict(ck["model_state_dict"])
         self._trainer.release_graph()
-        self._trainer.optimizer.load_state_dict(ck["optimizer_state_dict"])
+        if self._trainer.zero_opt is not None:
+            self._trainer.zero_opt.load_full_state_dict(ck["optimizer_state_dict"])
+        else:
+            self._trainer.optimizer.load_state_dict(ck["optimizer_state_dict"])
         for name, shadow in zip(self._trainer.ema.names, self._trainer.ema.shadow):
             if name in ck.get("ema", {}):
                 shadow.copy_(ck["ema"][name])
