@@ -97,7 +97,8 @@ def train(config: str, checkpoint: Optional[str], jax_weights: Optional[str], st
         click.echo(f"final loss {hist[-1]['loss']:.6g} after {hist[-1]['step']} steps")
     if checkpoint:
         trainer.save_checkpoint(checkpoint)
-        logger.info("saved %s", checkpoint)
+        if get_rank() == 0:
+            logger.info("saved %s", checkpoint)
 
 
 @main.command()
