@@ -247,3 +247,21 @@ def test_hybrid_coordinates_match(ref, rng):
     torch.testing.assert_close(hc.integral_over_pressure(x, ps, a), rhc.integral_over_pressure(x, ps, b))
     torch.testing.assert_close(hc.centered_difference(x, a), rhc.centered_difference(x, b))
     torch.testing.assert_close(hc.centered_vertical_advection(w, x, a), rhc.centered_vertical_advection(w, x, b))
+
+
+def test_nested_scan_utilities_match(ref):
+    from tornado_gcm_b200.core import scan_utils as su
+
+    rsu = ref.import_module("tornado_gcm.core.scan_utils")
+    for freqs, dt, total in (({"atmos": 6, "ocean": 24}, 1, None), ({"a": 2, "b": 6, "c": 12}, 1, 48),
+                             ({"fast": 1.0, "slow": 4.0}, 0.5, 16)):
+        assert su.compute_nested_steps(freqs, dt, total) == rsu.compute_nested_steps(freqs, dt, total)
+        assert [tuple(g) if isinstance(g, (list, tuple)) else g for g in su.frequency_groups(freqs, dt)] == \
+            [tuple(g) if isinstance(g, (list, tuple)) else g for g in rsu.frequency_groups(freqs, dt)]
+    forcings = [{"x": torch.tensor(float(i))} for i in range(24)]
+    freqs = {"atmos": 6, "ocean": 24}
+    step = lambda s, f: s + (0.0 if f is None else float(f["x"]) if isinstance(f, dict) and "x" in f else 1.0)  # noqa: E731
+    a_final, a_traj = su.nested_rollout(step, torch.tensor(0.0), forcings, freqs, collect_every=1)
+    b_final, b_traj = rsu.nested_rollout(step, torch.tensor(0.0), forcings, freqs, collect_every=1)
+    torch.testing.assert_close(a_final, b_final)
+    assert len(a_traj) == len(b_traj)
