@@ -265,3 +265,22 @@ def test_nested_scan_utilities_match(ref):
     b_final, b_traj = rsu.nested_rollout(step, torch.tensor(0.0), forcings, freqs, collect_every=1)
     torch.testing.assert_close(a_final, b_final)
     assert len(a_traj) == len(b_traj)
+
+
+def test_spectral_resampling_matches(ref, rng):
+    """Spectral down/up-sampling and interpolation between truncations, on modal fields and dicts."""
+    rcs = ref.coordinate_systems
+    s, rs = sc.SigmaCoordinates.equidistant(4), ref.sigma_coordinates.SigmaCoordinates.equidistant(4)
+    hi, lo = cs.CoordinateSystem(sh.Grid.T42(), s), cs.CoordinateSystem(sh.Grid.T21(), s)
+    rhi, rlo = rcs.CoordinateSystem(ref.spherical_harmonic.Grid.T42(), rs), \
+        rcs.CoordinateSystem(ref.spherical_harmonic.Grid.T21(), rs)
+    x_hi = {"v": _band_limited_modal(hi.horizontal, 4, rng)}
+    x_lo = {"v": _band_limited_modal(lo.horizontal, 4, rng)}
+    pairs = [(cs.get_spectral_downsample_fn(hi, lo), rcs.get_spectral_downsample_fn(rhi, rlo), x_hi),
+             (cs.get_spectral_upsample_fn(lo, hi), rcs.get_spectral_upsample_fn(rlo, rhi), x_lo),
+             (cs.get_spectral_interpolate_fn(hi, lo), rcs.get_spectral_interpolate_fn(rhi, rlo), x_hi),
+             (cs.get_spectral_interpolate_fn(lo, hi), rcs.get_spectral_interpolate_fn(rlo, rhi), x_lo)]
+    for ours_fn, ref_fn, x in pairs:
+        a, b = ours_fn(x), ref_fn(x)
+        assert a["v"].shape == b["v"].shape
+        torch.testing.assert_close(a["v"], b["v"])
