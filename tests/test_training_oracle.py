@@ -520,3 +520,24 @@ def _ref_grid_fp64_like(ref):
         latitude_spacing=rg.latitude_spacing, einsum_fn=ref.spherical_harmonic.einsum_highest)
     rg.__dict__["spherical_harmonics"] = rsh
     return rg
+
+
+def test_field_utilities_match(ref):
+    from tornado_gcm_b200.neural import field_utils as fu
+
+    rfu = ref.import_module("tornado_gcm.neural.field_utils")
+    g = torch.Generator().manual_seed(21)
+    x = torch.randn(2, 5, 6, 4, generator=g, dtype=torch.float64)
+    refv = torch.linspace(200.0, 290.0, 5, dtype=torch.float64)
+    w = torch.rand(5, generator=g, dtype=torch.float64)
+    cases = [
+        ("reconstruct_1d_field_from_ref_values", (x, refv)),
+        ("extract_1d_field_perturbation", (x, refv)),
+        ("slice_along_axis", (x, 1, 3)),
+        ("pad_along_axis", (x, 1, 2)),
+        ("weighted_vertical_mean", (x, w)),
+        ("repeat_surface_to_volume", (x[:, :1], 4)),
+        ("vertical_flip", (x,)),
+    ]
+    for name, args in cases:
+        torch.testing.assert_close(getattr(fu, name)(*args), getattr(rfu, name)(*args), msg=name)
