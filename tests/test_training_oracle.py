@@ -541,3 +541,27 @@ def test_field_utilities_match(ref):
     ]
     for name, args in cases:
         torch.testing.assert_close(getattr(fu, name)(*args), getattr(rfu, name)(*args), msg=name)
+
+
+def test_stream_norm_and_modal_filter_modules_match(ref):
+    from tornado_gcm_b200.core import spherical_harmonic as sh
+    from tornado_gcm_b200.neural.normalizations import StreamNorm
+    from tornado_gcm_b200.neural.spatial_filters import ComposedFilter, ExponentialModalFilter, \
+        HorizontalDiffusionFilter
+
+    rn = ref.import_module("tornado_gcm.neural.normalizations")
+    rsf = ref.import_module("tornado_gcm.neural.spatial_filters")
+    g = torch.Generator().manual_seed(13)
+    a, b = StreamNorm(6, momentum=0.1), rn.StreamNorm(6, momentum=0.1)
+    for _ in range(3):
+        x = torch.randn(5, 4, 6, generator=g) * 2 + 1
+        torch.testing.assert_close(a(x), b(x))
+    a.eval(), b.eval()
+    x = torch.randn(3, 6, generator=g)
+    torch.testing.assert_close(a(x), b(x))
+    torch.testing.assert_close(a.running_var, b.running_var)
+    grid, rgrid = sh.Grid.T21(), ref.spherical_harmonic.Grid.T21()
+    m = torch.randn(2, *grid.modal_shape, generator=g)
+    fa = ComposedFilter(ExponentialModalFilter(grid, 8.0, 6, 0.3), HorizontalDiffusionFilter(grid, 0.02, 2))
+    fb = rsf.ComposedFilter(rsf.ExponentialModalFilter(rgrid, 8.0, 6, 0.3), rsf.HorizontalDiffusionFilter(rgrid, 0.02, 2))
+    torch.testing.assert_close(fa(m), fb(m))
